@@ -1,0 +1,939 @@
+"""CPU oracle for the rollout hot path -- TEST INFRASTRUCTURE ONLY.
+
+This module restates, in numpy, the reference algorithms that the B200 kernels
+replace.  It exists to check the CUDA path (tests/, __graft_entry__.smoke())
+and to time the CPU baseline leg of bench.py; the product never imports it.
+
+Parity pin: every function here is checked against golden vectors produced by
+running the reference implementation itself (tests/golden/make_golden.py,
+which imports the reference from its source tree and feeds it the same random
+draws) and against the reference's committed known-answer files
+(deploy/ref_state.json, deploy/sweep_states.json).
+
+Formulation: the reference propagates fronts by shifting whole planes one cell
+at a time.  Here each target cell instead looks back k cells along a ray
+(`_behind`) and keeps an "open path" mask, which yields the same coverage /
+danger values.  All float32 arithmetic follows the reference's operation
+order so that positions, rewards and danger compare bit-exactly; the policy
+forward is computed in float64 as the accuracy reference for the fp16/fp32
+GPU path.
+
+Layouts are the reference's env-major ones: planes (N, H, W), per-player
+(N, P), positions (N, P, 2).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+F32 = np.float32
+EPS = F32(1e-4)                 # sim/move.py:33
+DIRS4 = ((-1, 0), (1, 0), (0, -1), (0, 1))   # up, down, left, right
+MOVE_IDLE = 4
+
+
+# ----------------------------------------------------------------- helpers
+
+def _behind(x: np.ndarray, dr: int, dc: int, k: int, fill) -> np.ndarray:
+    """out[..., i, j] = x[..., i - k*dr, j - k*dc]; `fill` outside the grid.
+
+    The value of the cell k steps *behind* (i, j) for a ray travelling in
+    direction (dr, dc).
+    """
+    out = np.full_like(x, fill)
+    h, w = x.shape[-2], x.shape[-1]
+    sr, sc = dr * k, dc * k
+    i0, i1 = max(0, sr), min(h, h + sr)
+    j0, j1 = max(0, sc), min(w, w + sc)
+    if i0 < i1 and j0 < j1:
+        out[..., i0:i1, j0:j1] = x[..., i0 - sr:i1 - sr, j0 - sc:j1 - sc]
+    return out
+
+
+def blast_map(bomb_blast: np.ndarray, default_blast: int) -> np.ndarray:
+    """Per-cell blast length; 0 falls back to cfg.blast (sim/torch_sim.py:727-730)."""
+    return np.where(bomb_blast > 0, bomb_blast.astype(np.int64), default_blast)
+
+
+def fuse_weight(fuse: np.ndarray, fuse_max: int) -> np.ndarray:
+    """Danger weight of a bomb: clamp(1 - (f-1)/FUSE, 0)^2 (sim/blast.py:218-220)."""
+    raw = F32(1.0) - (fuse.astype(F32) - F32(1.0)) / F32(fuse_max)
+    raw = np.maximum(raw, F32(0.0))
+    return np.where(fuse > 0, raw * raw, F32(0.0)).astype(F32)
+
+
+# ------------------------------------------------------------ fire / chains
+
+def fire_cover(sources, wall, solid, blast, brick, max_b: int) -> np.ndarray:
+    """Cross-shaped flame coverage from `sources` (sim/blast.py:43-98).
+
+    A cell c is covered when it is a firing source, or when some firing
+    source s = c - k*d (k <= blast(s)) sees it along direction d with every
+    cell strictly between them non-wall and non-solid, and c is not a wall.
+    Solid cells (live bombs, bricks) are covered but stop the ray.
+
+    `max_b` is the reference's blast-tier bound: a source whose blast
+    exceeds it emits no rays (only its own cell burns), exactly like the
+    tier loop `for b in 1..b_max` of sim/blast.py:90-97.
+    """
+    seed = sources & ~wall & ~brick
+    cov = seed.copy()
+    clear = ~wall & ~solid
+    emit = seed & (blast <= max_b)
+    for dr, dc in DIRS4:
+        open_path = np.ones_like(seed)
+        for k in range(1, max_b + 1):
+            src = _behind(emit & (blast >= k), dr, dc, k, False)
+            cov |= open_path & src & ~wall
+            open_path &= _behind(clear, dr, dc, k, False)
+    return cov
+
+
+def resolve_explosions(fuse, owner, wall, blast, brick, rounds: int, tier_cap=None):
+    """(covered, triggered) after the initial blast plus `rounds` chain rounds.
+
+    sim/blast.py:101-155 with the fixed round count used on the rollout path
+    (min(max_chain-1, chain_cap_rounds), sim/torch_sim.py:809-833).
+    `tier_cap`: blast tiers considered (None = all present).
+    """
+    triggered = (fuse == 0) & (owner >= 0)
+    live = fuse > 0
+    solid = live | brick
+    max_b = (int(blast.max()) if blast.size else 0) if tier_cap is None else int(tier_cap)
+    covered = fire_cover(triggered, wall, solid, blast, brick, max_b)
+    for _ in range(rounds):
+        newly = live & covered & ~triggered
+        if not newly.any():
+            break
+        covered = covered | fire_cover(newly, wall, solid, blast, brick, max_b)
+        triggered = triggered | newly
+    return covered, triggered
+
+
+def danger_map(fuse, wall, blast, brick, fuse_max: int, rounds_a: int) -> np.ndarray:
+    """Chain-corrected danger map (sim/blast.py:158-317).
+
+    Stage A (rounds_a rounds): a bomb that a front bomb's flame reaches takes
+    the front's weight if larger, and joins the next front.  Stage B: every
+    non-wall cell takes the max weight over the bombs whose flame reaches it.
+    """
+    bombed = fuse > 0
+    w = fuse_weight(fuse, fuse_max)
+    solid = bombed | brick
+    clear = ~wall & ~solid
+    max_b = int(blast.max()) if blast.size else 0
+
+    def reach_max(values):
+        best = np.zeros(values.shape, dtype=F32)
+        for dr, dc in DIRS4:
+            open_path = np.ones(values.shape, dtype=bool)
+            for k in range(1, max_b + 1):
+                v = _behind(np.where(bombed & (blast >= k), values, F32(0.0)),
+                            dr, dc, k, F32(0.0))
+                best = np.maximum(best, np.where(open_path & ~wall, v, F32(0.0)))
+                open_path &= _behind(clear, dr, dc, k, False)
+        return best
+
+    if rounds_a > 0:
+        cur = w.copy()
+        front = np.where(bombed, w, F32(0.0))
+        for _ in range(rounds_a):
+            spread = np.where(bombed, reach_max(front), F32(0.0))
+            newly = (spread > cur) & bombed
+            cur = np.maximum(cur, spread)
+            front = np.where(newly, spread, F32(0.0))
+            if not newly.any():
+                break
+        weight = cur
+    else:
+        weight = w
+    seed = np.where(wall, F32(0.0), weight)
+    return np.maximum(seed, reach_max(weight)).astype(F32)
+
+
+# ------------------------------------------------------------- movement
+
+def _impassable_pair(blocked_flat, r0, c0, r1, c1, y, x, rad, h, w):
+    """Either of two cells blocks this player (sim/move.py:154-181)."""
+    oob = ((r0 < 0) | (r0 >= h) | (c0 < 0) | (c0 >= w)
+           | (r1 < 0) | (r1 >= h) | (c1 < 0) | (c1 >= w))
+    i0 = np.clip(r0, 0, h - 1) * w + np.clip(c0, 0, w - 1)
+    i1 = np.clip(r1, 0, h - 1) * w + np.clip(c1, 0, w - 1)
+    s0 = np.take_along_axis(blocked_flat, i0, axis=1)
+    s1 = np.take_along_axis(blocked_flat, i1, axis=1)
+    ra = np.floor(y - rad).astype(np.int64)
+    rb = np.floor(y + rad).astype(np.int64)
+    ca = np.floor(x - rad).astype(np.int64)
+    cb = np.floor(x + rad).astype(np.int64)
+    in0 = (r0 >= ra) & (r0 <= rb) & (c0 >= ca) & (c0 <= cb)
+    in1 = (r1 >= ra) & (r1 <= rb) & (c1 >= ca) & (c1 <= cb)
+    return oob | (s0 & ~in0) | (s1 & ~in1)
+
+
+def resolve_axis(coord, delta, other, y, x, blocked_flat, rad, h, w, vertical):
+    """Slide along one axis and stop flush against the first blocking cell.
+
+    (N, K) arrays; sim/move.py:184-231.  Every float op keeps the reference's
+    order so the stop positions agree to the bit.
+    """
+    rad = F32(rad)
+    sgn = np.sign(delta).astype(F32)
+    old_lead = np.floor((coord - delta) + sgn * rad).astype(np.int64)
+    new_lead = np.floor(coord + sgn * rad).astype(np.int64)
+    lo = np.minimum(old_lead, new_lead)
+    hi = np.maximum(old_lead, new_lead)
+    span0 = np.floor(other - rad).astype(np.int64)
+    span1 = np.floor(other + rad).astype(np.int64)
+
+    def hit(lead):
+        if vertical:
+            return _impassable_pair(blocked_flat, lead, span0, lead, span1,
+                                    y, x, rad, h, w)
+        return _impassable_pair(blocked_flat, span0, lead, span1, lead,
+                                y, x, rad, h, w)
+
+    hit_lo, hit_hi = hit(lo), hit(hi)
+    pos_dir = sgn > 0
+    first_lead = np.where(pos_dir, hi, lo)
+    second_lead = np.where(pos_dir, lo, hi)
+    first_hit = np.where(pos_dir, hit_hi, hit_lo)
+    second_hit = np.where(pos_dir, hit_lo, hit_hi)
+    has = first_hit | second_hit
+    first = np.where(first_hit, first_lead, np.where(second_hit, second_lead, 0))
+    ff = first.astype(F32)
+    stop = np.where(pos_dir, (ff - rad) - EPS, ((ff + F32(1.0)) + rad) + EPS)
+    return np.where(has, stop, coord).astype(F32)
+
+
+def step_table(step_len: float) -> np.ndarray:
+    dirs = ((-1.0, 0.0), (1.0, 0.0), (0.0, -1.0), (0.0, 1.0))
+    return np.array([[dy * step_len, dx * step_len] for dy, dx in dirs]
+                    + [[0.0, 0.0]], dtype=F32)
+
+
+def move_players(cfg, pos, move, alive, blocked, spd):
+    """New positions after one tick of AABB sliding (sim/move.py:234-279)."""
+    n, p, _ = pos.shape
+    h, w, rad = cfg.height, cfg.width, cfg.radius
+    bflat = blocked.reshape(n, -1)
+    delta = step_table(cfg.step_len)[np.clip(move, 0, 4)] * spd[..., None]
+    moving = alive & (move != MOVE_IDLE)
+    delta = np.where(moving[..., None], delta, F32(0.0)).astype(F32)
+    dy, dx = delta[..., 0], delta[..., 1]
+    y, x = pos[..., 0], pos[..., 1]
+    ny = resolve_axis(y + dy, dy, x, y, x, bflat, rad, h, w, True)
+    nx = resolve_axis(x + dx, dx, y, y, x, bflat, rad, h, w, False)
+    out = np.empty_like(pos)
+    out[..., 0] = np.clip(np.where(dy != 0, ny, y), F32(rad), F32(h - rad))
+    out[..., 1] = np.clip(np.where(dx != 0, nx, x), F32(rad), F32(w - rad))
+    return out
+
+
+def center_flat(pos, w, h, clamp=True):
+    cell = np.floor(pos).astype(np.int64)
+    flat = cell[..., 0] * w + cell[..., 1]
+    return np.clip(flat, 0, h * w - 1) if clamp else flat
+
+
+# ---------------------------------------------------------- obs and masks
+
+def live_counts(owner, fuse, p):
+    """(N, P) live bomb count per player."""
+    n = owner.shape[0]
+    live = fuse > 0
+    return np.stack([((owner == i) & live).reshape(n, -1).sum(1)
+                     for i in range(p)], axis=1)
+
+
+def encode_obs(cfg, st, danger) -> np.ndarray:
+    """Shared (N, C, H, W) float32 observation (sim/obs.py:48-136)."""
+    n, p = st["alive"].shape
+    h, w = cfg.height, cfg.width
+    obs = np.zeros((n, cfg.n_channels, h, w), dtype=F32)
+    fuse, owner, pos, alive = st["fuse"], st["owner"], st["pos"], st["alive"]
+    fuse_norm = fuse.astype(F32) / F32(cfg.fuse)
+    for i in range(p):
+        obs[:, i] = _splat(pos[:, i], alive[:, i], h, w)
+        obs[:, p + i] = np.where((owner == i) & (fuse > 0), fuse_norm, F32(0.0))
+    obs[:, 2 * p] = (st["wall"] | st["brick"]).astype(F32)
+    obs[:, 2 * p + 1] = danger
+    obs[:, 2 * p + 2] = (st["t"].astype(F32) / F32(cfg.max_steps))[:, None, None]
+    if not cfg.obs_extra_enabled:
+        return obs
+    obs[:, 2 * p + 3] = st["crate"].astype(F32)
+    flat = center_flat(pos, w, h, clamp=False)
+    rows = np.arange(n)
+    for i in range(p):
+        ch = obs[:, 2 * p + 4 + i].reshape(n, -1)
+        ch[rows, flat[:, i]] = ((st["invuln"][:, i] > 0) & alive[:, i]).astype(F32)
+    caps = st["bombs_cap"]
+    cap = np.maximum(caps.astype(F32), F32(1.0))
+    avail = np.maximum((caps - live_counts(owner, fuse, p)).astype(F32), F32(0.0))
+    base = 3 * p + 4
+    for i in range(p):
+        a = alive[:, i].astype(F32)
+        obs[:, base + i].reshape(n, -1)[rows, flat[:, i]] = (avail[:, i] / cap[:, i]) * a
+        obs[:, base + p + i].reshape(n, -1)[rows, flat[:, i]] = \
+            (cap[:, i] / F32(cfg.growth_bombs_max)) * a
+    return obs
+
+
+def _splat(pos_me, gate, h, w):
+    """Bilinear splat of one player position, mass 1 (sim/obs.py:25-45)."""
+    n = pos_me.shape[0]
+    fy = np.clip(pos_me[:, 0] - F32(0.5), F32(0.0), F32(h - 1.0))
+    fx = np.clip(pos_me[:, 1] - F32(0.5), F32(0.0), F32(w - 1.0))
+    y0 = np.clip(np.floor(fy).astype(np.int64), 0, h - 1)
+    x0 = np.clip(np.floor(fx).astype(np.int64), 0, w - 1)
+    y1 = np.clip(y0 + 1, 0, h - 1)
+    x1 = np.clip(x0 + 1, 0, w - 1)
+    wy = np.clip(fy - y0.astype(F32), F32(0.0), F32(1.0))
+    wx = np.clip(fx - x0.astype(F32), F32(0.0), F32(1.0))
+    g = gate.astype(F32)
+    out = np.zeros((n, h * w), dtype=F32)
+    rows = np.arange(n)
+    for yy, wyy in ((y0, F32(1.0) - wy), (y1, wy)):
+        for xx, wxx in ((x0, F32(1.0) - wx), (x1, wx)):
+            np.add.at(out, (rows, yy * w + xx), (wyy * wxx) * g)
+    return out.reshape(n, h, w)
+
+
+def legal_mask(cfg, st):
+    """(move_mask (N,P,5), bomb_mask (N,P,2)) (sim/obs.py:139-229)."""
+    n, p = st["alive"].shape
+    h, w, rad = cfg.height, cfg.width, cfg.radius
+    fuse, alive, pos = st["fuse"], st["alive"], st["pos"]
+    blocked = (st["wall"] | (fuse > 0) | st["brick"]).reshape(n, -1)
+    step = F32(cfg.step_len)
+    y, x = pos[..., 0], pos[..., 1]
+    mm = np.ones((n, p, 5), dtype=bool)
+    for d, (sgn, vertical) in enumerate(((-1, True), (1, True), (-1, False), (1, False))):
+        dv = np.full_like(y, step) if sgn > 0 else np.full_like(y, -step)
+        if vertical:
+            ny = resolve_axis(y + dv, dv, x, y, x, blocked, rad, h, w, True)
+            moved = np.abs(ny - y) > F32(2e-4)
+        else:
+            nx = resolve_axis(x + dv, dv, y, y, x, blocked, rad, h, w, False)
+            moved = np.abs(nx - x) > F32(2e-4)
+        mm[..., d] = moved
+    mm = (mm & alive[..., None]) | ~alive[..., None]
+    flat = center_flat(pos, w, h, clamp=False)
+    ff = fuse.reshape(n, -1)
+    bb = (fuse > 0) | st["brick"]
+    bbf = bb.reshape(n, -1)
+    live = live_counts(st["owner"], fuse, p)
+    rows = np.arange(n)
+    bm = np.ones((n, p, 2), dtype=bool)
+    for i in range(p):
+        under = ff[rows, flat[:, i]] > 0
+        under_b = bbf[rows, flat[:, i]]
+        ok = ~under & ~under_b & (live[:, i] < st["bombs_cap"][:, i]) & alive[:, i]
+        bm[:, i, 1] = ok | ~alive[:, i]
+    return mm, bm
+
+
+# ------------------------------------------------------------------ step
+
+def _rounds_resolve(cfg):
+    return min(cfg.max_chain - 1, cfg.chain_cap_rounds)
+
+
+def _rounds_danger(cfg):
+    return min(cfg.max_chain, cfg.chain_cap_rounds) if cfg.max_chain > 1 else 0
+
+
+def place_bombs(cfg, st, bomb, alive0):
+    """Sequential per-player placement (sim/torch_sim.py:1357-1402)."""
+    n, p = alive0.shape
+    h, w = cfg.height, cfg.width
+    fuse = st["fuse"].reshape(n, -1)
+    owner = st["owner"].reshape(n, -1)
+    bblast = st["bomb_blast"].reshape(n, -1)
+    brick = st["brick"].reshape(n, -1)
+    flat = center_flat(st["pos"], w, h)
+    rows = np.arange(n)
+    placed = np.zeros((n, p), dtype=bool)
+    for me in range(p):
+        idx = flat[:, me]
+        live = ((owner == me) & (fuse > 0)).sum(1)
+        cur = fuse[rows, idx]
+        ok = (alive0[:, me] & (bomb[:, me] == 1) & (cur <= 0)
+              & ~brick[rows, idx] & (live < st["bombs_cap"][:, me]))
+        placed[:, me] = ok
+        fuse[rows[ok], idx[ok]] = cfg.fuse
+        owner[rows[ok], idx[ok]] = me
+        bblast[rows[ok], idx[ok]] = st["blast_cap"][ok, me].astype(np.int16)
+    return placed
+
+
+def place_predict_reward(cfg, st, placed, alive0):
+    """Immediate placement bonus: cover + chain (+ dist) (sim/torch_sim.py:1263-1355)."""
+    n, p = alive0.shape
+    h, w = cfg.height, cfg.width
+    if not (cfg.place_cover_reward or cfg.place_chain_reward or cfg.place_dist_reward):
+        return np.zeros((n, p), dtype=F32)
+    fuse, owner = st["fuse"], st["owner"]
+    live = fuse > 0
+    bm = blast_map(st["bomb_blast"], cfg.blast)
+    frac = np.clip(fuse.astype(F32) / F32(cfg.fuse), F32(0.0), F32(1.0))
+    weight = F32(cfg.chain_time_factor) + F32(1.0 - cfg.chain_time_factor) * (F32(1.0) - frac)
+    flat = center_flat(st["pos"], w, h)
+    rows = np.arange(n)
+    placed_map = np.zeros((n, h * w), dtype=bool)
+    for me in range(p):                       # later players overwrite earlier
+        placed_map[rows, flat[:, me]] = placed[:, me]
+    placed_map = placed_map.reshape(n, h, w)
+    cover = np.zeros((n, p), dtype=F32)
+    dist_pts = np.zeros((n, p), dtype=F32)
+    chain = np.zeros((n, p), dtype=F32)
+    cooldown_ok = st["since_bomb"] >= cfg.place_dist_cooldown
+    cell_f = np.floor(st["pos"]).astype(F32)
+    max_b = int(bm.max())
+    for me in range(p):
+        seed = np.zeros((n, h * w), dtype=bool)
+        seed[rows, flat[:, me]] = placed[:, me]
+        cov = fire_cover(seed.reshape(n, h, w), st["wall"], live | st["brick"],
+                         bm, st["brick"], max_b)
+        cflat = cov.reshape(n, -1)
+        for o in range(p):
+            if o == me:
+                continue
+            under = cflat[rows, flat[:, o]]
+            cover[:, me] += (under & alive0[:, o]).astype(F32)
+            if cfg.place_dist_reward > 0:
+                d = np.sqrt(((cell_f[:, me] - cell_f[:, o]) ** 2).sum(-1)).astype(F32)
+                ok = placed[:, me] & ~under & (d < cfg.place_dist_radius) \
+                    & cooldown_ok[:, me] & alive0[:, o]
+                gain = np.maximum(F32(1.0) - d / F32(cfg.place_dist_radius), F32(0.0))
+                dist_pts[:, me] += (ok * gain).astype(F32)
+        chained = cov & live & (owner >= 0) & ~placed_map
+        chain[:, me] = np.where(chained, weight, F32(0.0)).reshape(n, -1).sum(1, dtype=F32)
+    bonus = (F32(cfg.place_cover_reward) * cover + F32(cfg.place_dist_reward) * dist_pts
+             + F32(cfg.place_chain_reward) * chain)
+    return (bonus * alive0.astype(F32)).astype(F32)
+
+
+def step(cfg, st, actions, rb_hit, rb_grow, explore_coef=1.0):
+    """One tick, in place on `st` (sim/torch_sim.py:895-1261), no auto-reset.
+
+    rb_hit / rb_grow: (N, P) float32 uniforms for crate pickup (the
+    reference's `_rand_buf` layout).  Returns (reward (N,P) f32, done (N,),
+    info dict with covered/triggered/died/winner/n_alive).
+    """
+    n, p = st["alive"].shape
+    h, w = cfg.height, cfg.width
+    rows = np.arange(n)
+    alive0 = st["alive"].copy()
+    a0f = alive0.astype(F32)
+    hp_before = st["hp"].astype(np.int32)
+    move, bomb = actions[..., 0], actions[..., 1]
+    coef = F32(explore_coef)
+
+    st["fuse"][...] = np.where(st["fuse"] > 0, st["fuse"] - 1, st["fuse"])
+    placed = place_bombs(cfg, st, bomb, alive0)
+    place_bonus = place_predict_reward(cfg, st, placed, alive0)
+    st["since_bomb"] += 1
+    st["since_bomb"][placed] = 0
+
+    blocked = st["wall"] | st["brick"] | (st["fuse"] > 0)
+    st["pos"][...] = move_players(cfg, st["pos"], move, alive0, blocked, st["spd_g"])
+
+    bmap = blast_map(st["bomb_blast"], cfg.blast)
+    # The reference compiles resolve once, on the first step, with that step's
+    # hint max(bomb_blast.max(), cfg.blast) bound into the closure
+    # (sim/torch_sim.py:818-832): later steps keep those blast tiers.
+    if int(st.get("resolve_tiers", -1)) < 0:
+        st["resolve_tiers"] = np.int64(max(int(st["bomb_blast"].max()), int(cfg.blast)))
+    covered, triggered = resolve_explosions(st["fuse"], st["owner"], st["wall"], bmap,
+                                            st["brick"], _rounds_resolve(cfg),
+                                            tier_cap=int(st["resolve_tiers"]))
+    chain_bonus = np.zeros((n, p), dtype=F32)
+    if cfg.chain_blast_bonus > 0 and cfg.max_chain > 1:
+        nat = (triggered & (st["fuse"] == 0)).reshape(n, -1)
+        own = st["owner"].reshape(n, -1)
+        chained = (triggered.reshape(n, -1) & ~nat)
+        for pl in range(p):
+            fired = np.minimum((nat & (own == pl)).sum(1), 1)
+            cross = (chained & (own != pl)).sum(1)
+            chain_bonus[:, pl] = F32(cfg.chain_blast_bonus) * (cross * fired).astype(F32)
+    if cfg.map_mode == "corridor":
+        st["crate"] |= st["brick"] & covered
+    st["brick"] &= ~covered
+
+    flat = center_flat(st["pos"], w, h)
+    hit = alive0 & covered.reshape(n, -1)[rows[:, None], flat]
+    hit_eff = hit & (st["invuln"] <= 0)
+    hp_new = np.maximum(st["hp"].astype(np.int32) - hit_eff.astype(np.int32), 0)
+    died = hit_eff & (hp_new == 0)
+    st["hp"][...] = hp_new.astype(np.uint8)
+    st["alive"][...] = alive0 & ~died
+    st["invuln"][...] = np.maximum(st["invuln"] - 1, 0)
+    st["invuln"][hit_eff] = cfg.invuln_ticks
+
+    st["fuse"][triggered] = 0
+    st["owner"][triggered] = -1
+    st["bomb_blast"][triggered] = 0
+    st["t"] += 1
+    n_alive = st["alive"].sum(1)
+    done = (n_alive <= 1) | (st["t"] >= cfg.max_steps)
+
+    dmg = np.maximum(hp_before - st["hp"].astype(np.int32), 0).astype(F32)
+    dealt = dmg.sum(1, keepdims=True, dtype=F32) - dmg
+    hr = F32(cfg.hit_reward)
+    reward = (((-F32(cfg.step_penalty)) * a0f + hr * dealt) - hr * dmg
+              + (coef * place_bonus) * a0f)
+
+    if cfg.hit_attr_penalty > 0:
+        hit_any = (dmg > 0) & alive0
+        pen = cfg.hit_attr_penalty
+        nb = np.maximum(st["bombs_cap"] - pen, st["lo_bombs"])
+        nz = np.maximum(st["blast_cap"] - pen, st["lo_blast"])
+        ns = np.maximum(st["spd_g"] - F32(pen * cfg.growth_speed_step), st["lo_spd"])
+        lost = (((st["bombs_cap"] - nb) + (st["blast_cap"] - nz)).astype(F32)
+                + np.round((st["spd_g"] - ns) / F32(cfg.growth_speed_step))).astype(np.int64)
+        st["bombs_cap"][...] = np.where(hit_any, nb, st["bombs_cap"])
+        st["blast_cap"][...] = np.where(hit_any, nz, st["blast_cap"])
+        st["spd_g"][...] = np.where(hit_any, ns, st["spd_g"])
+        st["pending_lost"] += lost * hit_any
+    reward = reward + (coef * chain_bonus) * a0f
+
+    if cfg.map_mode == "corridor":
+        flat = center_flat(st["pos"], w, h)
+        stood = st["crate"].reshape(n, -1)[rows[:, None], flat]
+        reward = reward + (F32(cfg.brick_reward) * stood.astype(F32)) * a0f
+        rec = st["recycle"].reshape(n, -1)[rows[:, None], flat]
+        prob = np.where(rec, F32(cfg.recycle_crate_prob), st["crate_prob"][:, None])
+        hits = stood & (rb_hit < prob) & alive0
+        _grow(cfg, st, hits.astype(np.int64) * alive0, rb_grow)
+        st["crate"].reshape(n, -1)[rows[:, None], flat] = False
+        st["recycle"].reshape(n, -1)[rows[:, None], flat] = False
+
+    danger = danger_map(st["fuse"], st["wall"], blast_map(st["bomb_blast"], cfg.blast),
+                        st["brick"], cfg.fuse, _rounds_danger(cfg))
+    flat = center_flat(st["pos"], w, h)
+    standing = danger.reshape(n, -1)[rows[:, None], flat]
+    reward = reward - (F32(explore_coef * cfg.danger_penalty) * standing) * a0f
+
+    if cfg.combo_reward > 0:
+        hit_this = dmg > 0
+        for me in range(p):
+            dm = dealt[:, me]
+            c = st["combo"][:, me].copy()
+            gap = np.maximum(st["t"] - st["last_hit"][:, me], 0).astype(F32)
+            factor = np.power(F32(cfg.combo_gap_factor), gap).astype(F32)
+            inc = (dm > 0).astype(np.int64)
+            now = (c + inc) * inc
+            pts = ((now.astype(F32) * F32(cfg.combo_reward)) * factor) * np.minimum(dm, F32(1.0))
+            reward[:, me] = reward[:, me] + pts * a0f[:, me]
+            st["combo"][:, me] = np.where(inc > 0, now, c)
+            st["last_hit"][:, me] = np.where(inc > 0, st["t"], st["last_hit"][:, me])
+            st["combo"][:, me] = np.where(hit_this[:, me], 0, st["combo"][:, me])
+
+    alive = st["alive"]
+    death_done = done & (n_alive == 1)
+    winner = death_done[:, None] & alive & (n_alive == 1)[:, None]
+    loser = death_done[:, None] & ~alive & (n_alive == 1)[:, None]
+    hpf = st["hp"].astype(F32)
+    all_alive = done & (n_alive == p)
+    if not cfg.win_hp_scaled:
+        reward = reward + F32(cfg.win_bonus) * (winner.astype(F32) - loser.astype(F32))
+        if cfg.timeout_draw:
+            tot = hpf.sum(1, dtype=F32)
+            for me in range(p):
+                opp = (tot - hpf[:, me]) / F32(p - 1)
+                diff = hpf[:, me] - opp
+                reward[:, me] = reward[:, me] + ((F32(cfg.win_bonus / cfg.max_hp) * diff)
+                                                 * all_alive.astype(F32)) * coef
+    else:
+        scale = coef if cfg.timeout_draw else F32(1.0)
+        tot = hpf.sum(1, dtype=F32)
+        for me in range(p):
+            diff = hpf[:, me] - (tot - hpf[:, me]) / F32(p - 1)
+            base = F32(cfg.win_bonus / cfg.max_hp) * diff
+            reward[:, me] = reward[:, me] + (base * death_done.astype(F32)
+                                             + (base * all_alive.astype(F32)) * scale)
+    info = {"n_alive": n_alive, "blast": covered, "trig": triggered,
+            "died": died, "winner": winner}
+    return reward.astype(F32), done, info
+
+
+def _grow(cfg, st, hits, rb):
+    """Crate-driven growth of bombs/blast/speed (sim/torch_sim.py:862-893)."""
+    attr = np.floor(rb * F32(3.0)).astype(np.int64)
+    if cfg.crate_speed_only:
+        attr = np.where(st["hazard"][:, None], 2, attr)
+    st["bombs_cap"][...] = np.minimum(st["bombs_cap"] + (attr == 0) * hits,
+                                      cfg.growth_bombs_max)
+    st["blast_cap"][...] = np.minimum(st["blast_cap"] + (attr == 1) * hits,
+                                      cfg.growth_blast_max)
+    add = ((attr == 2) * hits).astype(F32) * F32(cfg.growth_speed_step)
+    st["spd_g"][...] = np.minimum(st["spd_g"] + add, F32(cfg.growth_speed_max))
+
+
+def observe(cfg, st):
+    """danger + obs (fp32) for the current state (sim/torch_sim.py:605-627)."""
+    dng = danger_map(st["fuse"], st["wall"], blast_map(st["bomb_blast"], cfg.blast),
+                     st["brick"], cfg.fuse, _rounds_danger(cfg))
+    return encode_obs(cfg, st, dng), dng
+
+
+# ------------------------------------------------------------------- bots
+
+def sample_legal(mask, u):
+    """Inverse-CDF sample over legal entries (sim/bots.py:36-46); u: (N,) f32."""
+    cs = np.cumsum(mask.astype(F32), axis=-1, dtype=F32)
+    s = np.maximum(cs[:, -1:], F32(1e-6))
+    return ((u[:, None].astype(F32) * s) > cs).sum(-1).astype(np.int64)
+
+
+def random_attack(alive_me, mm, bm, u_move, u_bomb, bomb_rate):
+    """Uniform legal move, bomb with probability bomb_rate (sim/bots.py:49-58)."""
+    move = sample_legal(mm, u_move)
+    bomb = ((u_bomb < F32(bomb_rate)) & bm[:, 1]).astype(np.int64)
+    move = np.where(alive_me, move, MOVE_IDLE)
+    bomb = np.where(alive_me, bomb, 0)
+    return np.stack([move, bomb], axis=-1)
+
+
+def _cells(pos, pid, h, w):
+    r = np.clip(np.floor(pos[:, pid, 0]).astype(np.int64), 0, h - 1)
+    c = np.clip(np.floor(pos[:, pid, 1]).astype(np.int64), 0, w - 1)
+    return r, c
+
+
+def _candidates(r, c, h, w):
+    rows = np.stack([np.clip(r - 1, 0, h - 1), np.clip(r + 1, 0, h - 1), r, r, r], 1)
+    cols = np.stack([c, c, np.clip(c - 1, 0, w - 1), np.clip(c + 1, 0, w - 1), c], 1)
+    return rows, cols
+
+
+def greedy_attack(cfg, st, danger_obs, mm, bm, pid, noise):
+    """Chebyshev approach with a hard danger filter (sim/bots.py:95-176).
+
+    danger_obs: (N, H, W) float32 read from the fp16 observation; noise (N,5).
+    """
+    n, p = st["alive"].shape
+    h, w = cfg.height, cfg.width
+    pos = st["pos"]
+    dflat = danger_obs.reshape(n, -1)
+    blocked = (st["wall"] | st["brick"]).reshape(n, -1)
+    r, c = _cells(pos, pid, h, w)
+    rows = np.arange(n)
+    own = dflat[rows, r * w + c]
+    cr, cc = _candidates(r, c, h, w)
+    cflat = cr * w + cc
+    dng = np.take_along_axis(dflat, cflat, 1)
+    blk = np.take_along_axis(blocked, cflat, 1)
+    dist = np.full((n, 5), F32(1e9), dtype=F32)
+    for o in range(p):
+        if o == pid:
+            continue
+        ro, co = _cells(pos, o, h, w)
+        d = np.maximum(np.abs(cr - ro[:, None]), np.abs(cc - co[:, None])).astype(F32)
+        d = np.where(st["alive"][:, o][:, None], d, F32(1e9))
+        dist = np.minimum(dist, d)
+    inf = F32(np.inf)
+    nz = F32(0.05) * noise.astype(F32)
+    best = np.zeros(n, dtype=np.int64)
+    best_s = np.full(n, inf, dtype=F32)
+    esc_s = np.full(n, inf, dtype=F32)
+    esc_d = np.zeros(n, dtype=np.int64)
+    for d in range(5):
+        legal = mm[:, d] & ~blk[:, d]
+        s = np.where(legal, (dist[:, d] + F32(2.0) * dng[:, d]) + nz[:, d], inf)
+        better = s < best_s
+        best_s = np.where(better, s, best_s)
+        best = np.where(better, d, best)
+        e = np.where(legal, dng[:, d], inf)
+        eb = e < esc_s
+        esc_s = np.where(eb, e, esc_s)
+        esc_d = np.where(eb, d, esc_d)
+    use_safe = (best_s < inf) & (dng[rows, best] < F32(0.35))
+    move = np.where(use_safe, best, esc_d)
+    place = (bm[:, 1] & (dist[:, MOVE_IDLE] < st["blast_cap"][:, pid].astype(F32))
+             & (own < F32(0.2))).astype(np.int64)
+    dead = ~st["alive"][:, pid]
+    return np.stack([np.where(dead, MOVE_IDLE, move), np.where(dead, 0, place)], -1)
+
+
+def dijkstra_field(sources, danger, blocked, lam=2.0):
+    """Multi-source shortest-path cost field, exact fixed point (sim/bots.py:179-238).
+
+    cost(c) = 1 + lam*danger(c) (inf when blocked); dist = min over paths of
+    the left-to-right float32 sum of entered-cell costs.  The reference's
+    Jacobi passes stop at the same fixed point, which any convergent
+    relaxation order reaches.
+    """
+    n = sources.shape[0]
+    h, w = sources.shape[-2:]
+    cost = F32(1.0) + F32(lam) * danger.astype(F32)
+    cost = np.where(blocked, F32(np.inf), cost).astype(F32)
+    dist = np.where(sources, F32(0.0), F32(np.inf)).astype(F32)
+    for _ in range(h * w + 1):
+        best = np.full_like(dist, F32(np.inf))
+        best[:, 1:, :] = np.minimum(best[:, 1:, :], dist[:, :-1, :])
+        best[:, :-1, :] = np.minimum(best[:, :-1, :], dist[:, 1:, :])
+        best[:, :, 1:] = np.minimum(best[:, :, 1:], dist[:, :, :-1])
+        best[:, :, :-1] = np.minimum(best[:, :, :-1], dist[:, :, 1:])
+        new = np.minimum(dist, best + cost)
+        if np.array_equal(new, dist):
+            break
+        dist = new
+    return dist.reshape(n, h * w)
+
+
+class ModeTicker:
+    """astar approach/flee mode switcher with fed draws (sim/bots.py:241-264)."""
+
+    def __init__(self, mode0, timer0):
+        self.mode = np.asarray(mode0, dtype=np.int64).copy()
+        self.timer = np.asarray(timer0, dtype=np.int64).copy()
+        self.tick = 0
+
+    def advance(self, new_mode, new_timer):
+        self.tick += 1
+        self.timer -= 1
+        if self.tick % 16 == 0:
+            sw = self.timer <= 0
+            self.mode = np.where(sw, new_mode, self.mode)
+            self.timer = np.where(sw, new_timer, self.timer)
+        return self.mode
+
+
+def astar_attack(cfg, st, danger_obs, mm, bm, pid, noise, mode=None, cap_max=None,
+                 return_fields=False):
+    """Danger-aware path-field bot (sim/bots.py:267-508), eat_crates off.
+
+    cap_max: batch max of blast_cap[:, pid] (the reference's chain scan
+    length, sim/bots.py:484); computed here when None.
+    """
+    n, p = st["alive"].shape
+    h, w = cfg.height, cfg.width
+    pos, fuse = st["pos"], st["fuse"]
+    rows = np.arange(n)
+    dflat = danger_obs.reshape(n, -1).astype(F32)
+    r, c = _cells(pos, pid, h, w)
+    own = dflat[rows, r * w + c]
+    threat = (st["owner"] == pid) & (fuse > 0)
+    for _ in range(int(cfg.growth_blast_max)):
+        nb = threat.copy()
+        nb[:, 1:, :] |= threat[:, :-1, :]
+        nb[:, :-1, :] |= threat[:, 1:, :]
+        nb[:, :, 1:] |= threat[:, :, :-1]
+        nb[:, :, :-1] |= threat[:, :, 1:]
+        threat = nb
+    block_all = st["wall"] | st["brick"] | (fuse > 0)
+    dng2 = danger_obs.astype(F32)
+    v_safe = dijkstra_field(dng2 < F32(0.35), dng2, block_all)
+    opp_src = np.zeros((n, h * w), dtype=bool)
+    for o in range(p):
+        if o == pid:
+            continue
+        ro, co = _cells(pos, o, h, w)
+        opp_src[rows, ro * w + co] = st["alive"][:, o]
+    v_opp = dijkstra_field(opp_src.reshape(n, h, w), dng2, block_all)
+
+    cr, cc = _candidates(r, c, h, w)
+    cflat = cr * w + cc
+    vopp = np.take_along_axis(v_opp, cflat, 1)
+    vsafe = np.take_along_axis(v_safe, cflat, 1)
+    dng = np.take_along_axis(dflat, cflat, 1)
+    thr = np.take_along_axis(threat.reshape(n, -1), cflat, 1).astype(F32)
+    blk = np.take_along_axis((st["wall"] | st["brick"]).reshape(n, -1), cflat, 1)
+    legal = mm & ~blk
+    inf = F32(np.inf)
+    nz = F32(0.05) * noise.astype(F32)
+    two = F32(2.0)
+
+    app = ((vopp + two * dng) + two * thr) + nz
+    app = np.where(dng >= F32(0.5), inf, app)
+    app = np.where(legal, app, inf)
+    app_ok = np.isfinite(app.min(1))
+    use_esc = (own >= F32(0.35)) | ~app_ok
+    esc = (vsafe * F32(100.0) + two * thr) + nz
+    idle_col = np.arange(5) == 4
+    esc = np.where(use_esc[:, None] & idle_col[None], inf, esc)
+    esc = np.where(legal, esc, inf)
+    score = np.where(use_esc[:, None], esc, app)
+    if mode is not None:
+        vf = np.minimum(vopp, F32(1e3))
+        flee = ((-vf + two * dng) + two * thr) + nz
+        flee = np.where(dng >= F32(0.5), inf, flee)
+        flee = np.where(legal, flee, inf)
+        flee = np.where(use_esc[:, None], esc, flee)
+        score = np.where((mode == 1)[:, None], flee, score)
+    move = np.argmin(score, 1).astype(np.int64)
+    any_legal = legal.any(1)
+    no_path = ~np.isfinite(score).any(1)
+    dl = np.where(legal, dng, inf)
+    dmv = np.where(~idle_col[None], dl, inf)
+    fb = np.where(np.isfinite(dmv.min(1)), np.argmin(dmv, 1), np.argmin(dl, 1))
+    move = np.where(no_path & any_legal, fb, move)
+
+    cap = st["blast_cap"][:, pid].astype(np.int64)
+    big = 10 ** 9
+    dr_o = np.full(n, big, dtype=np.int64)
+    dc_o = np.full(n, big, dtype=np.int64)
+    for o in range(p):
+        if o == pid:
+            continue
+        ro, co = _cells(pos, o, h, w)
+        dr_o = np.where(st["alive"][:, o], np.abs(r - ro), dr_o)
+        dc_o = np.where(st["alive"][:, o], np.abs(c - co), dc_o)
+    aligned = ((dr_o == 0) & (dc_o <= cap)) | ((dc_o == 0) & (dr_o <= cap))
+    manh = np.minimum(dr_o + dc_o, 10 ** 8)
+    near = manh <= np.maximum(cap + 1, 1)
+    chain = np.zeros(n, dtype=bool)
+    kmax = int(cap.max()) if cap_max is None else int(cap_max)
+    for k in range(1, kmax + 1):
+        for dr, dc in DIRS4:
+            rr, cc2 = r + dr * k, c + dc * k
+            inb = (rr >= 0) & (rr < h) & (cc2 >= 0) & (cc2 < w)
+            f = fuse[rows, np.clip(rr, 0, h - 1), np.clip(cc2, 0, w - 1)]
+            chain |= inb & (f > 0) & (f <= 10)
+    can = bm[:, 1]
+    can_escape = (legal & (dng < F32(0.35)) & ~(thr > 0)).any(1)
+    place = (can & (aligned | near | chain) & (own < F32(0.2)) & can_escape)
+    if mode is not None:
+        flee_place = can & (aligned | near) & (own < F32(0.2)) & can_escape
+        place = np.where(mode == 1, flee_place, place)
+    dead = ~st["alive"][:, pid]
+    out = np.stack([np.where(dead, MOVE_IDLE, move),
+                    np.where(dead, 0, place.astype(np.int64))], -1)
+    if return_fields:
+        return out, v_safe, v_opp
+    return out
+
+
+# ----------------------------------------------------------------- policy
+
+def _ln(x, g, b, eps=1e-5):
+    m = x.mean(-1, keepdims=True)
+    v = ((x - m) ** 2).mean(-1, keepdims=True)
+    return (x - m) / np.sqrt(v + eps) * g + b
+
+
+def inv_cols(cfg_c, h, w, p, pid):
+    """Column gather that folds the seat's view permutation into W0 (train/model.py:127-138)."""
+    base = 2 * p + 3
+    perm = [pid, p + pid] + [i for i in range(p) if i != pid] \
+        + [p + i for i in range(p) if i != pid] + [2 * p, 2 * p + 1, 2 * p + 2] \
+        + list(range(base, cfg_c))
+    inv = np.argsort(np.asarray(perm))
+    hw = h * w
+    return np.concatenate([np.arange(hw) + int(inv[k]) * hw for k in range(cfg_c)])
+
+
+def mlp_forward(params, obs, pid, p):
+    """float64 MLP forward -> (move_logits, bomb_logits, value) (train/model.py:191-196).
+
+    params: dict of numpy arrays keyed like ActorCritic's state_dict.
+    """
+    n, c, h, w = obs.shape
+    x = obs.reshape(n, -1).astype(np.float64)
+    W0 = params["shared.0.weight"].astype(np.float64)[:, inv_cols(c, h, w, p, pid)]
+    z = x @ W0.T + params["shared.0.bias"]
+    z = np.maximum(_ln(z, params["shared.1.weight"], params["shared.1.bias"]), 0)
+    z = z @ params["shared.3.weight"].T.astype(np.float64) + params["shared.3.bias"]
+    z = np.maximum(_ln(z, params["shared.4.weight"], params["shared.4.bias"]), 0)
+
+    def head(name):
+        a = np.maximum(z @ params[f"{name}.0.weight"].T.astype(np.float64)
+                       + params[f"{name}.0.bias"], 0)
+        return a @ params[f"{name}.2.weight"].T.astype(np.float64) + params[f"{name}.2.bias"]
+
+    return head("move_head"), head("bomb_head"), head("critic")[:, 0]
+
+
+def masked_sample(logits, mask, u):
+    """Inverse-CDF draw from the masked categorical (train/model.py:216-245).
+
+    Masked logits take float32's lowest finite value; a = #{k : u*S > cs_k}
+    where cs is the running sum of exp(z - max z).  Returns (action, logp).
+    """
+    z = np.where(mask, logits, np.finfo(np.float32).min).astype(np.float64)
+    m = z.max(-1, keepdims=True)
+    e = np.exp(z - m)
+    cs = np.cumsum(e, -1)
+    s = cs[:, -1:]
+    a = np.minimum(((u[:, None] * s) > cs).sum(-1), z.shape[-1] - 1)
+    logp = np.take_along_axis(z, a[:, None], 1)[:, 0] - m[:, 0] - np.log(s[:, 0])
+    return a.astype(np.int64), logp
+
+
+def mlp_act(params, obs, mm, bm, pid, p, u_move, u_bomb):
+    ml, bl, v = mlp_forward(params, obs, pid, p)
+    am, lm = masked_sample(ml, mm, u_move.astype(np.float64))
+    ab, lb = masked_sample(bl, bm, u_bomb.astype(np.float64))
+    return np.stack([am, ab], -1), lm + lb, v, ml, bl
+
+
+# ------------------------------------------------------------------ state
+
+STATE_KEYS = ("wall", "brick", "crate", "recycle", "fuse", "owner", "bomb_blast",
+              "pos", "alive", "hp", "since_bomb", "t", "bombs_cap", "blast_cap",
+              "spd_g", "invuln", "pending_lost", "combo", "last_hit", "lo_bombs",
+              "lo_blast", "lo_spd", "crate_prob", "hazard")
+
+
+def copy_state(st):
+    return {k: np.array(v, copy=True) for k, v in st.items()}
+
+
+# --------------------------------------------------------- crate recycling
+
+def recycle_exclusion(cfg):
+    """Flat cells where recycled crates never land (sim/torch_sim.py:465-533):
+    the 4-neighbourhoods of the open / mode / ring spawns plus the open
+    map's central cross band."""
+    h, w = cfg.height, cfg.width
+    near = lambda r, c: {(r, c)} | {(r + dr, c + dc) for dr, dc in DIRS4
+                                    if 0 <= r + dr < h and 0 <= c + dc < w}
+    row = (h - 1) / 2.0 + 0.5
+    open_sp = [(int(row), int((w - 1) * (i + 1) / (cfg.n_players + 1) + 0.5))
+               for i in range(cfg.n_players)]
+    open_excl = set()
+    for r, c in open_sp:
+        open_excl |= near(r, c)
+    cy, cx = (h - 1) // 2, (w - 1) // 2
+    cross = {(r, c) for c in range(w) for r in (cy - 1, cy)} \
+        | {(r, c) for r in range(h) for c in (cx - 1, cx)}
+    cross -= open_excl
+    excl = set(open_excl)
+    for r, c in list(cfg.spawn_cells()) + list(cfg.ring_spawn_cells()):
+        excl |= near(r, c)
+    excl |= cross
+    return np.array(sorted(r * w + c for r, c in excl), dtype=np.int64)
+
+
+def flush_recycle(cfg, st, gen):
+    """Drop one crate per lost attribute layer on random free cells.
+
+    sim/torch_sim.py:549-596; `gen` is a torch CPU generator in the same
+    state as the reference's `sim.gen` (randperm draws, player-major, env
+    order).
+    """
+    import torch
+    n, p = st["pending_lost"].shape
+    hw = cfg.height * cfg.width
+    if st["pending_lost"].sum() <= 0:
+        return
+    excl = recycle_exclusion(cfg)
+    for pl in range(p):
+        lost = st["pending_lost"][:, pl]
+        idx = np.flatnonzero(lost > 0)
+        if idx.size == 0:
+            continue
+        avail = (~st["wall"][idx] & ~st["brick"][idx]).reshape(-1, hw).copy()
+        avail[:, excl] = False
+        crate = st["crate"].reshape(n, -1)
+        rec = st["recycle"].reshape(n, -1)
+        for i, e in enumerate(idx):
+            cells = np.flatnonzero(avail[i])
+            if cells.size == 0:
+                continue
+            k = min(int(lost[e]), cells.size)
+            perm = torch.randperm(cells.size, generator=gen)[:k].numpy()
+            crate[e, cells[perm]] = True
+            rec[e, cells[perm]] = True
+    st["pending_lost"][...] = 0

@@ -1,0 +1,437 @@
+#!/usr/bin/env python3
+"""Generate golden vectors by running the reference implementation itself.
+
+Run in a container that holds the reference source tree (it is imported, not
+copied):
+
+    python tests/golden/make_golden.py --ref /path/to/qqt-gpu-sim
+
+Two import shims are applied before the reference loads: `triton` is blocked
+so movement uses the eager torch path, and the missing `sim.dev.synchronize`
+that `train/ppo.py` imports is provided.  Every random draw the rollout makes
+(bot samplers and noise, mode-ticker integers, crate-pickup uniforms, learner
+sampling uniforms) is fed from a recorded numpy stream, so the oracle and the
+CUDA engine can replay the same trajectory.
+
+Outputs (compressed npz, all env-major like the reference tensors):
+  kat_states.npz   the reference's own known-answer states
+                   (deploy/ref_state.json, deploy/sweep_states.json) with
+                   their danger / obs / masks / covered / triggered
+  traj_cfg1.npz    open border map, random bots p=0.05, 256 ticks
+  traj_cfg2.npz    pillar corridor, MLP learner vs astar, 128 ticks
+  traj_cfg4.npz    pillar corridor, self-play MLP (both seats), 64 ticks
+  traj_cfg5.npz    pillar corridor, CNN learner vs greedy, 48 ticks
+  stress_cfg3.npz  bomb stress: one idle step, danger/obs/masks, V fields
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+from functools import partial
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(REPO, "qqt-gpu-sim_b200"))
+
+from qqt_b200 import scenarios  # noqa: E402
+from qqt_b200.policy_init import init_params  # noqa: E402
+
+
+def load_reference(ref_root):
+    sys.modules["triton"] = None
+    sys.path.insert(0, ref_root)
+    import torch  # noqa: F401
+    import sim.dev
+    sim.dev.synchronize = lambda *a, **k: None
+    import sim.bots as rbots
+    import sim.torch_sim as rts
+    from sim.blast import danger_map, resolve_explosions
+    from sim.config import SimConfig
+    from sim.obs import encode_obs, legal_mask
+    from train.model import ActorCritic
+    return dict(bots=rbots, ts=rts, SimConfig=SimConfig, danger_map=danger_map,
+                resolve=resolve_explosions, encode_obs=encode_obs,
+                legal_mask=legal_mask, ActorCritic=ActorCritic)
+
+
+class FedTorch:
+    """Stand-in for the `torch` module inside sim/bots.py: rand/randint come
+    from a numpy stream and are recorded in call order."""
+
+    def __init__(self, real, rng):
+        self._real = real
+        self._rng = rng
+        self.log = []
+
+    def rand(self, *size, device=None, **kw):
+        shape = size[0] if len(size) == 1 and isinstance(size[0], tuple) else size
+        v = self._rng.random(shape).astype(np.float32)
+        self.log.append(("rand", v))
+        return self._real.from_numpy(v)
+
+    def randint(self, low, high, size, device=None, **kw):
+        v = self._rng.integers(low, high, size=size).astype(np.int64)
+        self.log.append(("randint", v))
+        return self._real.from_numpy(v)
+
+    def __getattr__(self, name):
+        return getattr(self._real, name)
+
+
+def state_np(sim):
+    import torch
+    out = {}
+    names = {"wall": "wall", "brick": "brick", "crate": "crate",
+             "recycle": "_recycle_crate", "fuse": "fuse", "owner": "owner",
+             "bomb_blast": "bomb_blast", "pos": "pos", "alive": "alive",
+             "hp": "hp", "since_bomb": "since_bomb", "t": "t",
+             "bombs_cap": "bombs_cap", "blast_cap": "blast_cap", "spd_g": "spd_g",
+             "invuln": "invuln", "pending_lost": "_pending_lost", "combo": "_combo",
+             "last_hit": "_last_hit", "lo_bombs": "_lo_bombs", "lo_blast": "_lo_blast",
+             "lo_spd": "_lo_spd", "crate_prob": "crate_prob", "hazard": "_hazard"}
+    for k, attr in names.items():
+        v = getattr(sim, attr)
+        assert isinstance(v, torch.Tensor)
+        out[k] = v.detach().cpu().numpy().copy()
+    return out
+
+
+def set_state(sim, st):
+    import torch
+    names = {"wall": "wall", "brick": "brick", "crate": "crate",
+             "recycle": "_recycle_crate", "fuse": "fuse", "owner": "owner",
+             "bomb_blast": "bomb_blast", "pos": "pos"}
+    for k, attr in names.items():
+        if k in st:
+            getattr(sim, attr).copy_(torch.from_numpy(np.asarray(st[k])))
+
+
+def load_params(model, params):
+    import torch
+    sd = model.state_dict()
+    for k in sd:
+        sd[k] = torch.from_numpy(params[k])
+    model.load_state_dict(sd)
+
+
+def masked_sample_np(logits, mask, u):
+    z = np.where(mask, logits.astype(np.float64), np.finfo(np.float32).min)
+    m = z.max(-1, keepdims=True)
+    e = np.exp(z - m)
+    cs = np.cumsum(e, -1)
+    s = cs[:, -1:]
+    a = np.minimum(((u[:, None] * s) > cs).sum(-1), z.shape[-1] - 1)
+    logp = np.take_along_axis(z, a[:, None], 1)[:, 0] - m[:, 0] - np.log(s[:, 0])
+    return a.astype(np.int64), logp
+
+
+def rollout(R, cfg, n, ticks, seed, template, learner_arch, opp_kind, rng_seed,
+            obs_every=4, bomb_rate=0.05):
+    import torch
+    torch.set_num_threads(4)
+    ts, rbots = R["ts"], R["bots"]
+    rng = np.random.default_rng(rng_seed)
+    fed = FedTorch(torch, rng)
+    rbots.torch = fed
+    h, w, p = cfg.height, cfg.width, cfg.n_players
+    border = scenarios.border_walls(h, w)
+    orig_open = ts.make_open_obstacles
+    if template == "open_border":
+        ts.make_open_obstacles = lambda c, count, gen, dev: \
+            torch.from_numpy(np.broadcast_to(border, (count, h, w)).copy())
+    try:
+        sim = ts.BatchedSim(cfg, n, device="cpu", seed=seed)
+        if template == "corridor":
+            wall, brick = scenarios.pillar_corridor(n, h, w, seed=seed)
+            set_state(sim, {"wall": wall, "brick": brick})
+            sp = np.array(scenarios.corner_spawns(cfg), dtype=np.float32)
+            sim.pos.copy_(torch.from_numpy(np.broadcast_to(sp, (n, p, 2)).copy()))
+        init = state_np(sim)
+        models = {}
+        seats = []
+        if learner_arch is not None:
+            m = R["ActorCritic"](cfg.obs_shape, arch=learner_arch)
+            params = init_params(cfg.obs_shape, arch=learner_arch, seed=seed)
+            load_params(m, params)
+            m.eval()
+            models[0] = m
+            seats.append(("net", 0))
+        else:
+            seats.append(("bot", 0))
+        if opp_kind == "self":
+            models[1] = models[0]
+            seats.append(("net", 1))
+        else:
+            seats.append(("bot", 1))
+        bots = {}
+        for kind, pid in seats:
+            if kind == "bot":
+                kname = opp_kind if pid == 1 else "random"
+                if kname == "random":
+                    bots[pid] = rbots.BotWrapper(
+                        sim, partial(rbots.random_attack, bomb_rate=bomb_rate), "random")
+                else:
+                    bots[pid] = rbots.make_bot(sim, kname)
+        rec = {k: [] for k in ("mm", "bm", "actions", "reward", "done", "winner",
+                               "rb_hit", "rb_grow", "u_net", "logits_m", "logits_b",
+                               "value", "logp", "draws_kind", "state", "n_alive")}
+        obs_ticks, obs_rec, dng_rec = [], [], []
+        reset_rec, flush_rec = [], []
+        fields_rec = []
+        bot_draws = []
+        for t in range(ticks):
+            obs = sim.observe()
+            mm, bm = sim.legal_mask()
+            if t % obs_every == 0:
+                obs_ticks.append(t)
+                obs_rec.append(obs.numpy().copy())
+                dng_rec.append(sim._dng_cache.numpy().copy() if sim._dng_cache is not None
+                               else np.zeros((n, h, w), np.float32))
+            acts = torch.zeros((n, p, 2), dtype=torch.long)
+            u_net = np.zeros((n, p, 2), dtype=np.float64)
+            lm = np.zeros((n, p, 5), np.float32)
+            lb = np.zeros((n, p, 2), np.float32)
+            val = np.zeros((n, p), np.float32)
+            lp = np.zeros((n, p), np.float64)
+            tick_draws = {}
+            for kind, pid in seats:
+                if kind == "net":
+                    with torch.no_grad():
+                        ml, bl, v = models[pid](obs, pid)
+                    u = rng.random((n, 2))
+                    u_net[:, pid] = u
+                    am, l1 = masked_sample_np(ml.numpy(), mm[:, pid].numpy(), u[:, 0])
+                    ab, l2 = masked_sample_np(bl.numpy(), bm[:, pid].numpy(), u[:, 1])
+                    acts[:, pid, 0] = torch.from_numpy(am)
+                    acts[:, pid, 1] = torch.from_numpy(ab)
+                    lm[:, pid], lb[:, pid], val[:, pid] = ml.numpy(), bl.numpy(), v.numpy()
+                    lp[:, pid] = l1 + l2
+                else:
+                    fed.log.clear()
+                    a = bots[pid].act(obs, mm[:, pid], bm[:, pid], pid)
+                    acts[:, pid] = a
+                    tick_draws[pid] = list(fed.log)
+            bot_draws.append(tick_draws)
+            if opp_kind == "astar" and t % 8 == 0:
+                dng = obs.float()[:, 2 * p + 1]
+                blk = sim.wall | sim.brick | (sim.fuse > 0)
+                vs = rbots._dijkstra_field(sim, dng < 0.35, dng, blocked=blk)
+                src = torch.zeros(n, h, w, dtype=torch.bool)
+                r0 = sim.pos[:, 0, 0].floor().long().clamp(0, h - 1)
+                c0 = sim.pos[:, 0, 1].floor().long().clamp(0, w - 1)
+                src.view(n, -1)[torch.arange(n), r0 * w + c0] = sim.alive[:, 0]
+                vo = rbots._dijkstra_field(sim, src, dng, blocked=blk)
+                fields_rec.append((t, vs.numpy().copy(), vo.numpy().copy()))
+            rb = rng.random((2, n, p)).astype(np.float32)
+            buf = np.zeros(n * (2 * p + 1), dtype=np.float32)
+            buf[: n * p] = rb[0].reshape(-1)
+            buf[n * p: 2 * n * p] = rb[1].reshape(-1)
+            sim._rand_buf = torch.from_numpy(buf)
+            r, d, info = sim.step(acts, auto_reset=False)
+            rec["mm"].append(mm.numpy().copy())
+            rec["bm"].append(bm.numpy().copy())
+            rec["actions"].append(acts.numpy().copy())
+            rec["reward"].append(r.numpy().copy())
+            rec["done"].append(d.numpy().copy())
+            rec["winner"].append(info["winner"].numpy().copy())
+            rec["n_alive"].append(info["n_alive"].numpy().copy())
+            rec["rb_hit"].append(rb[0])
+            rec["rb_grow"].append(rb[1])
+            rec["u_net"].append(u_net)
+            rec["logits_m"].append(lm)
+            rec["logits_b"].append(lb)
+            rec["value"].append(val)
+            rec["logp"].append(lp)
+            rec["state"].append(state_np(sim))
+            if bool(d.any()):
+                sim.reset_(d)
+                reset_rec.append((t, state_np(sim)))
+            if t % 16 == 15:
+                gstate = sim.gen.get_state().numpy().copy()
+                sim.flush_recycle()
+                flush_rec.append((t, gstate, state_np(sim)))
+    finally:
+        ts.make_open_obstacles = orig_open
+        rbots.torch = torch
+    out = {"init_" + k: v for k, v in init.items()}
+    for k in ("mm", "bm", "actions", "reward", "done", "winner", "rb_hit", "rb_grow",
+              "u_net", "logits_m", "logits_b", "value", "logp", "n_alive"):
+        out[k] = np.stack(rec[k])
+    skeys = [k for k in rec["state"][0] if k != "wall"]
+    for k in skeys:
+        out["st_" + k] = np.stack([s[k] for s in rec["state"]])
+    out["obs_ticks"] = np.array(obs_ticks)
+    out["obs"] = np.stack(obs_rec)
+    out["danger"] = np.stack(dng_rec)
+    out["reset_ticks"] = np.array([t for t, _ in reset_rec], dtype=np.int64)
+    for i, (t, s) in enumerate(reset_rec):
+        for k in skeys:
+            out[f"reset{i}_{k}"] = s[k]
+    out["flush_ticks"] = np.array([t for t, _, _ in flush_rec], dtype=np.int64)
+    for i, (t, g, s) in enumerate(flush_rec):
+        out[f"flush{i}_gen"] = g
+        for k in ("crate", "recycle", "pending_lost"):
+            out[f"flush{i}_{k}"] = s[k]
+    if fields_rec:
+        out["field_ticks"] = np.array([t for t, _, _ in fields_rec])
+        out["vsafe"] = np.stack([a for _, a, _ in fields_rec])
+        out["vopp"] = np.stack([b for _, _, b in fields_rec])
+    # bot draws per tick and seat, flattened in call order
+    for pid in (0, 1):
+        kinds = []
+        for t, td in enumerate(bot_draws):
+            for j, (kind, v) in enumerate(td.get(pid, [])):
+                out[f"draw_p{pid}_t{t}_{j}"] = v
+                kinds.append((t, j, kind))
+        if kinds:
+            out[f"draw_p{pid}_index"] = np.array([[t, j, 0 if k == "rand" else 1]
+                                                  for t, j, k in kinds], dtype=np.int64)
+    return out
+
+
+def kat_states(R, ref_root):
+    import torch
+    cfg = R["SimConfig"](height=13, width=13, n_players=2, map_mode="corridor",
+                         speed=3.0, max_steps=1800, obs_extra_enabled=True, obs_fp16=False)
+    with open(os.path.join(ref_root, "deploy", "ref_state.json")) as f:
+        states = [json.load(f)]
+    with open(os.path.join(ref_root, "deploy", "sweep_states.json")) as f:
+        states += json.load(f)["states"]
+    h, w = 13, 13
+    keys = ("wall", "brick", "fuse", "owner", "bomb_blast", "crate")
+    dt = {"wall": bool, "brick": bool, "crate": bool, "fuse": np.int16,
+          "owner": np.int8, "bomb_blast": np.int16}
+    out = {k: [] for k in keys + ("pos", "alive", "t", "invuln", "bombs_cap",
+                                 "blast_cap", "danger", "obs", "mm", "bm",
+                                 "covered", "triggered")}
+    for s in states:
+        st = s["state"]
+        for k in keys:
+            out[k].append(np.array(st[k], dtype=dt[k]).reshape(h, w))
+        out["pos"].append(np.array(st["pos"], np.float32).reshape(2, 2))
+        out["alive"].append(np.array(st["alive"], bool))
+        out["t"].append(st["t"])
+        out["invuln"].append(np.array(st["invuln"], np.int64))
+        out["bombs_cap"].append(np.array(st["bombs_cap"], np.int64))
+        out["blast_cap"].append(np.array(st["blast_cap"], np.int64))
+        # recompute with the reference and check it against the stored answer
+        T = {k: torch.from_numpy(out[k][-1][None]) for k in keys}
+        bmap = torch.where(T["bomb_blast"] > 0, T["bomb_blast"].long(), cfg.blast)
+        dng = R["danger_map"](T["fuse"], T["wall"], bmap, cfg.fuse, T["brick"], cfg.max_chain)
+        pos = torch.from_numpy(out["pos"][-1][None])
+        alive = torch.from_numpy(out["alive"][-1][None])
+        tt = torch.tensor([st["t"]])
+        inv = torch.from_numpy(out["invuln"][-1][None])
+        bp = torch.from_numpy(out["bombs_cap"][-1][None])
+        obs = R["encode_obs"](cfg, T["wall"], T["fuse"], T["owner"], pos, alive, tt,
+                              T["brick"], T["bomb_blast"], T["crate"], inv, bp,
+                              danger_precomputed=dng)
+        mm, bm = R["legal_mask"](cfg, T["wall"], T["fuse"], T["owner"], pos, alive,
+                                 T["brick"], bp)
+        cov, trig = R["resolve"](T["fuse"], T["owner"], T["wall"], bmap, cfg.max_chain,
+                                 T["brick"])
+        assert np.array_equal(np.array(s["danger"], np.float32), dng[0].numpy().reshape(-1))
+        assert np.array_equal(np.array(s["obs"], np.float32), obs[0].numpy().reshape(-1))
+        assert np.array_equal(np.array(s["mm"], bool), mm[0].numpy())
+        assert np.array_equal(np.array(s["covered"], bool), cov[0].numpy().reshape(-1))
+        out["danger"].append(dng[0].numpy())
+        out["obs"].append(obs[0].numpy())
+        out["mm"].append(mm[0].numpy())
+        out["bm"].append(bm[0].numpy())
+        out["covered"].append(cov[0].numpy())
+        out["triggered"].append(trig[0].numpy())
+    return {k: np.stack([np.asarray(x) for x in v]) for k, v in out.items()}
+
+
+def stress(R, cfg, n, seed):
+    import torch
+    ts, rbots = R["ts"], R["bots"]
+    h, w, p = cfg.height, cfg.width, cfg.n_players
+    border = scenarios.border_walls(h, w)
+    orig_open = ts.make_open_obstacles
+    ts.make_open_obstacles = lambda c, count, gen, dev: \
+        torch.from_numpy(np.broadcast_to(border, (count, h, w)).copy())
+    rng = np.random.default_rng(seed + 100)
+    fed = FedTorch(torch, rng)
+    rbots.torch = fed
+    try:
+        sim = ts.BatchedSim(cfg, n, device="cpu", seed=seed)
+        fuse, owner, blast = scenarios.bomb_stress(n, cfg, seed)
+        set_state(sim, {"fuse": fuse, "owner": owner, "bomb_blast": blast})
+        sp = np.array(scenarios.open_spawns(cfg), dtype=np.float32)
+        sim.pos.copy_(torch.from_numpy(np.broadcast_to(sp, (n, p, 2)).copy()))
+        init = state_np(sim)
+        acts = torch.zeros((n, p, 2), dtype=torch.long)
+        acts[..., 0] = 4
+        rb = rng.random((2, n, p)).astype(np.float32)
+        buf = np.zeros(n * (2 * p + 1), dtype=np.float32)
+        buf[: n * p] = rb[0].reshape(-1)
+        buf[n * p: 2 * n * p] = rb[1].reshape(-1)
+        sim._rand_buf = torch.from_numpy(buf)
+        r, d, info = sim.step(acts, auto_reset=False)
+        after = state_np(sim)
+        obs = sim.observe()
+        mm, bm = sim.legal_mask()
+        dng = obs.float()[:, 2 * p + 1]
+        blk = sim.wall | sim.brick | (sim.fuse > 0)
+        out = {"init_" + k: v for k, v in init.items()}
+        out.update({"after_" + k: v for k, v in after.items()})
+        out.update(reward=r.numpy(), done=d.numpy(), covered=info["blast"].numpy(),
+                   triggered=info["trig"].numpy(), obs=obs.numpy(), mm=mm.numpy(),
+                   bm=bm.numpy(), rb_hit=rb[0], rb_grow=rb[1],
+                   danger=sim._dng_cache.numpy())
+        for pid in range(p):
+            vs = rbots._dijkstra_field(sim, dng < 0.35, dng, blocked=blk)
+            src = torch.zeros(n, h, w, dtype=torch.bool)
+            o = 1 - pid
+            ro = sim.pos[:, o, 0].floor().long().clamp(0, h - 1)
+            co = sim.pos[:, o, 1].floor().long().clamp(0, w - 1)
+            src.view(n, -1)[torch.arange(n), ro * w + co] = sim.alive[:, o]
+            vo = rbots._dijkstra_field(sim, src, dng, blocked=blk)
+            out[f"vsafe{pid}"] = vs.numpy()
+            out[f"vopp{pid}"] = vo.numpy()
+            fed.log.clear()
+            a = rbots.astar_attack(sim, obs, mm[:, pid], bm[:, pid], pid)
+            out[f"astar_act{pid}"] = a.numpy()
+            out[f"astar_noise{pid}"] = fed.log[0][1]
+    finally:
+        ts.make_open_obstacles = orig_open
+        rbots.torch = torch
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default=os.environ.get("QQT_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--only", default="")
+    args = ap.parse_args()
+    R = load_reference(args.ref)
+    SC = R["SimConfig"]
+    jobs = {
+        "kat_states": lambda: kat_states(R, args.ref),
+        "traj_cfg1": lambda: rollout(R, SC(**scenarios.CFG1), 16, 256, 0, "open_border",
+                                     None, "random", rng_seed=10, obs_every=8),
+        "traj_cfg2": lambda: rollout(R, SC(**scenarios.CFG2), 24, 128, 1, "corridor",
+                                     "mlp", "astar", rng_seed=11, obs_every=4),
+        "traj_cfg4": lambda: rollout(R, SC(**scenarios.CFG2), 12, 64, 4, "corridor",
+                                     "mlp", "self", rng_seed=14, obs_every=8),
+        "traj_cfg5": lambda: rollout(R, SC(**scenarios.CFG2), 8, 48, 3, "corridor",
+                                     "cnn", "greedy", rng_seed=13, obs_every=8),
+        "stress_cfg3": lambda: stress(R, SC(**scenarios.CFG1), 48, 5),
+    }
+    for name, fn in jobs.items():
+        if args.only and name not in args.only.split(","):
+            continue
+        out = fn()
+        path = os.path.join(HERE, name + ".npz")
+        np.savez_compressed(path, **out)
+        print(f"{name}: {os.path.getsize(path) / 1e6:.2f} MB")
+
+
+if __name__ == "__main__":
+    main()
