@@ -1,0 +1,247 @@
+/*
+ * qqt_b200.h -- C ABI of the B200 rollout engine (libqqt_b200.so).
+ *
+ * Drop-in boundary for the reference's batched simulator path: each entry
+ * point replaces one reference call (cited per function).  The reference is
+ * Python, so its natural binding is ctypes; INTEGRATION.md shows the stub.
+ *
+ * Conventions
+ *   - All pointers are device pointers owned by the caller.  The library
+ *     never allocates or frees device memory and keeps no pointer across
+ *     calls (the MLP weight pack is a caller-owned buffer too).
+ *   - Every call is stream-ordered on `stream` and does not synchronise the
+ *     host, so a whole rollout tick can be captured into one CUDA graph.
+ *   - Return value: QQT_OK (0) or a QQT_E_* code for argument errors and
+ *     launch failures.  Conditions detected inside kernels (out-of-range
+ *     positions, relaxation not converged) are OR-ed into a device error
+ *     word that qqt_get_error() reads and clears.
+ *
+ * Layout (N envs, C = H*W cells, P players; env index innermost):
+ *   plane   [C][N]       wall/brick/crate/recycle (uint8 0/1), fuse (int16),
+ *                        owner (int8), bomb_blast (int16)
+ *   player  [P][N]       alive/hp (uint8), since_bomb (int32),
+ *                        bombs_cap/blast_cap/invuln/pending_lost/combo/
+ *                        last_hit/lo_bombs/lo_blast (int64),
+ *                        spd_g/lo_spd (float)
+ *   pos     [P][2][N]    float (row, col) of each player's centre
+ *   env     [N]          t (int64), crate_prob (float), hazard (uint8)
+ *   obs     [N][obs_stride] fp16 (or fp32), channel-major (C_obs, H, W) per
+ *                        env, rows padded to obs_stride elements (16 bytes
+ *                        multiple) with zeros
+ *   masks   move [N][P][5], bomb [N][P][2] uint8
+ *   actions [N][P][2] int64 (move, bomb)
+ */
+#ifndef QQT_B200_H
+#define QQT_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* qqt_stream_t;   /* == cudaStream_t */
+
+enum {
+  QQT_OK = 0,
+  QQT_E_ARG = 1,         /* null pointer, bad size or unsupported config     */
+  QQT_E_ALIGN = 2,       /* pointer or stride misaligned                     */
+  QQT_E_LIMIT = 3,       /* N, H, W or P above the compiled limits            */
+  QQT_E_LAUNCH = 4,      /* CUDA launch error                                 */
+  QQT_E_DEVICE = 5       /* unsupported device (needs sm_100)                 */
+};
+
+/* device error word bits (qqt_get_error) */
+enum {
+  QQT_DEV_POS_RANGE = 1u << 0,   /* a centre cell fell outside the grid     */
+  QQT_DEV_NOT_CONVERGED = 1u << 1, /* path-field relaxation hit its cap     */
+  QQT_DEV_BAD_ACTION = 1u << 2,  /* action index outside its head's range   */
+  QQT_DEV_TIMEOUT = 1u << 3      /* a bounded mbarrier wait expired         */
+};
+
+/* Scalar configuration.  Float fields hold the float32 values the reference
+ * multiplies by (products of Python doubles are formed in double, then
+ * rounded once), so results match bit for bit.  Mirrors sim/config.py:102-603
+ * plus the derived quantities the kernels need. */
+typedef struct QqtCfg {
+  int32_t n_envs, height, width, n_players;
+  int32_t fuse, blast, max_steps, invuln_ticks, max_hp;
+  int32_t resolve_rounds;   /* min(max_chain-1, chain_cap_rounds)             */
+  int32_t danger_rounds;    /* min(max_chain, chain_cap_rounds), 0 if max_chain<=1 */
+  int32_t corridor;         /* map_mode == "corridor": crates and growth      */
+  int32_t hit_attr_penalty, growth_bombs_max, growth_blast_max;
+  int32_t place_dist_cooldown, crate_speed_only, timeout_draw, win_hp_scaled;
+  int32_t combo_on, obs_extra, obs_channels, obs_stride, obs_fp32;
+  float radius, step_len, move_eps2;   /* move_eps2 = 2e-4                    */
+  float step_penalty, hit_reward, brick_reward, danger_penalty; /* coef*dp   */
+  float explore_coef, place_cover_reward, place_chain_reward, place_dist_reward;
+  float place_dist_radius, chain_time_factor, chain_time_rest; /* 1-cf       */
+  float growth_speed_step, growth_speed_max, pen_speed; /* pen*step         */
+  float recycle_crate_prob, combo_reward, combo_gap_factor, win_bonus;
+  float win_bonus_per_hp, chain_blast_bonus, obs_growth_bombs_max;
+  float fuse_f, max_steps_f, h_minus_rad, w_minus_rad;
+} QqtCfg;
+
+typedef struct QqtState {
+  uint8_t *wall, *brick, *crate, *recycle;
+  int16_t *fuse;
+  int8_t *owner;
+  int16_t *bomb_blast;
+  float *pos;
+  uint8_t *alive, *hp;
+  int32_t *since_bomb;
+  int64_t *t;
+  int64_t *bombs_cap, *blast_cap;
+  float *spd_g;
+  int64_t *invuln, *pending_lost, *combo, *last_hit, *lo_bombs, *lo_blast;
+  float *lo_spd, *crate_prob;
+  uint8_t *hazard;
+} QqtState;
+
+/* Per-env reset template used by the device-side auto-reset (the
+ * benchmark configurations reset every env to its own template map; see
+ * qqt_step).  Planes [C][N]; caps [P][N]; spawn [P][2][N]. */
+typedef struct QqtTemplate {
+  const uint8_t *wall, *brick, *crate;
+  const float *spawn;
+  const int64_t *bombs_cap, *blast_cap;
+  const float *spd;
+  const float *crate_prob;
+  uint64_t seed;            /* spawn-swap draws: hash(seed, env, episode)     */
+  int32_t swap_spawns;      /* 1: swap P0/P1 spawns with probability 1/2     */
+  int32_t since_bomb0;      /* place_dist_cooldown                            */
+  int64_t *episode;         /* [N] per-env reset counter (in/out)             */
+} QqtTemplate;
+
+/* Optional outputs of a step (any may be NULL). */
+typedef struct QqtStepOut {
+  float *reward;            /* [N][P]                                         */
+  uint8_t *done;            /* [N]                                            */
+  uint8_t *died, *winner;   /* [N][P]                                         */
+  int64_t *n_alive;         /* [N]                                            */
+  uint8_t *covered, *triggered; /* [C][N]                                     */
+  uint8_t *reset_mask;      /* [N] envs reset by the device auto-reset        */
+} QqtStepOut;
+
+/* One tick of the environment, fused: fuse countdown, sequential bomb
+ * placement, placement bonus, AABB sliding, chain explosion, bricks to
+ * crates, damage, clearing, rewards (step/hit/place/attribute penalty/crate
+ * pickup and growth/danger standing/combo/terminal) and done.
+ * Replaces BatchedSim.step (sim/torch_sim.py:895-1261).
+ *   actions   [N][P][2] int64
+ *   rb_hit, rb_grow  [N][P] float uniforms for crate pickup (the reference's
+ *             `_rand_buf` halves, sim/torch_sim.py:1129-1138); may be NULL
+ *             when cfg->corridor == 0
+ *   tiers     device int32: the blast tiers the chain resolver considers.
+ *             The reference fixes them on its first step
+ *             (sim/torch_sim.py:818-832); with first_step != 0 the call
+ *             records max(bomb_blast.max() after placement, blast) into
+ *             *tiers (two launches: placement, then the rest), later calls
+ *             read it.
+ *   scratch   device buffer of qqt_step_scratch_bytes(cfg) bytes
+ *   tmpl      NULL: no reset (the caller resets on the host);
+ *             otherwise done envs are reset on the device to their template.
+ */
+int qqt_step(const QqtCfg *cfg, const QqtState *st, const int64_t *actions,
+             const float *rb_hit, const float *rb_grow, int32_t *tiers,
+             int32_t first_step, const QqtStepOut *out, const QqtTemplate *tmpl,
+             void *scratch, qqt_stream_t stream);
+uint64_t qqt_step_scratch_bytes(const QqtCfg *cfg);
+
+/* Danger map + shared observation + legal masks for the current state.
+ * Replaces BatchedSim.observe (sim/torch_sim.py:605-627, encode_obs
+ * sim/obs.py:48-136, danger_map sim/blast.py:158-317) and
+ * BatchedSim.legal_mask (sim/torch_sim.py:636-645, sim/obs.py:170-229).
+ *   obs     [N][obs_stride] fp16 (fp32 when cfg->obs_fp32); may be NULL
+ *   danger  [N][C] float32 danger map; may be NULL
+ *   mm, bm  [N][P][5], [N][P][2]; may be NULL */
+int qqt_observe(const QqtCfg *cfg, const QqtState *st, void *obs, float *danger,
+                uint8_t *mm, uint8_t *bm, qqt_stream_t stream);
+
+/* Legal masks only (sim/obs.py:170-229). */
+int qqt_legal_mask(const QqtCfg *cfg, const QqtState *st, uint8_t *mm, uint8_t *bm,
+                   qqt_stream_t stream);
+
+/* Bot entry points act for one seat.  Masks and actions are that seat's
+ * rows: row e of the move mask starts at mm + e*mm_stride (5 entries), of
+ * the bomb mask at bm + e*bm_stride (2 entries), of the action at
+ * act + e*act_stride (move, bomb).  A slice mm[:, pid] of an [N][P][5] mask
+ * is passed as (pointer to its first row, stride P*5). */
+
+/* astar bot: own-bomb threat, the two shortest-path fields V_safe / V_opp
+ * with cell cost 1 + 2*danger, candidate scoring, fallback and bomb
+ * decision.  Replaces astar_attack + _mode_ticker (sim/bots.py:179-508,
+ * 241-264).
+ *   obs        [N][obs_stride] fp16 observation (danger channel is read)
+ *   noise      [N][5] uniforms (the bot's torch.rand(n, 5))
+ *   mode, timer [N] int64 mode-ticker state (NULL: always approach)
+ *   tick16     1 when this call is a multiple-of-16 ticker call
+ *   new_mode, new_timer [N] int64 draws used when a timer has expired on
+ *              such a call (may be NULL when tick16 == 0)
+ *   vsafe, vopp [N][C] float fields (may be NULL)
+ *   scratch    >= 4 bytes of device memory (batch max of blast_cap[pid]) */
+int qqt_astar_act(const QqtCfg *cfg, const QqtState *st, const void *obs,
+                  const uint8_t *mm, int32_t mm_stride, const uint8_t *bm,
+                  int32_t bm_stride, int32_t pid, const float *noise, int64_t *mode,
+                  int64_t *timer, int32_t tick16, const int64_t *new_mode,
+                  const int64_t *new_timer, int64_t *act, int32_t act_stride,
+                  float *vsafe, float *vopp, void *scratch, qqt_stream_t stream);
+
+/* random bot (sim/bots.py:36-58): uniform legal move from u_move [N]
+ * (inverse CDF over legal entries), bomb when u_bomb [N] < bomb_rate and
+ * the bomb mask allows it. */
+int qqt_random_act(const QqtCfg *cfg, const QqtState *st, const uint8_t *mm,
+                   int32_t mm_stride, const uint8_t *bm, int32_t bm_stride, int32_t pid,
+                   const float *u_move, const float *u_bomb, float bomb_rate,
+                   int64_t *act, int32_t act_stride, qqt_stream_t stream);
+
+/* greedy bot (sim/bots.py:95-176); noise [N][5] uniforms. */
+int qqt_greedy_act(const QqtCfg *cfg, const QqtState *st, const void *obs,
+                   const uint8_t *mm, int32_t mm_stride, const uint8_t *bm,
+                   int32_t bm_stride, int32_t pid, const float *noise, int64_t *act,
+                   int32_t act_stride, qqt_stream_t stream);
+
+/* MLP policy (train/model.py:121-153, 167-245).  For each listed seat:
+ * Linear(K -> 128) on the tensor cores (tcgen05 kind::f16, TMA-staged
+ * operands, fp16 obs x the hi+lo fp16 halves of the seat-permuted fp32
+ * weights, fp32 accumulation in TMEM; the seat's view permutation is folded
+ * into the packed weights' column gather), then LN, ReLU, Linear(128,128),
+ * LN, ReLU, the move/bomb/critic heads, masking with float32's lowest value
+ * and inverse-CDF sampling a = #{k : u*S > cs_k} over exp(z - max z).
+ *   pack    weights packed by qqt_mlp_pack (256-byte aligned)
+ *   obs     [N][obs_stride] fp16, obs_stride % 8 == 0, 16-byte aligned; the
+ *           first k_in = C*H*W entries of each row are the observation
+ *   mm, bm  [N][P][5], [N][P][2] masks of all seats
+ *   n_seats 1 or 2 (must equal the pack's); pids[n_seats] host array
+ *   u       [n_seats][N][2] uniforms (move, bomb)
+ *   act     [N][P][2]: writes the listed seats; logp, value [n_seats][N];
+ *   logits  [n_seats][N][8] (5 move, 2 bomb, value) or NULL
+ *   work    device buffer of qqt_mlp_work_bytes(N, n_seats) bytes */
+int qqt_mlp_act(const void *pack, const void *obs, int32_t n_envs, int32_t obs_stride,
+                int32_t k_in, int32_t n_players, const uint8_t *mm, const uint8_t *bm,
+                int32_t n_seats, const int32_t *pids, const float *u, int64_t *act,
+                float *logp, float *value, float *logits, void *work, qqt_stream_t stream);
+uint64_t qqt_mlp_work_bytes(int32_t n_envs, int32_t n_seats);
+
+/* Pack the fp32 parameters of one ActorCritic(mlp) for qqt_mlp_act.
+ * params: 20 device pointers in the order of qqt_mlp_param_names()
+ * (the reference state_dict keys); pids[n_seats] (host) selects the view
+ * permutations; pack: device buffer of qqt_mlp_pack_bytes() bytes, 256-byte
+ * aligned.  Re-run after every optimizer step. */
+int qqt_mlp_pack(const float *const *params, int32_t k_in, int32_t n_players,
+                 int32_t channels, int32_t hw, int32_t n_seats, const int32_t *pids,
+                 void *pack, qqt_stream_t stream);
+uint64_t qqt_mlp_pack_bytes(int32_t k_in, int32_t n_seats);
+const char *qqt_mlp_param_names(void);
+
+/* Device error word: returns the accumulated QQT_DEV_* bits and clears
+ * them (synchronises the device). */
+int qqt_get_error(uint32_t *code_out);
+
+/* Library version string. */
+const char *qqt_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QQT_B200_H */

@@ -1,0 +1,637 @@
+// MLP policy: first layer on the 5th-generation tensor cores, the rest fused
+// into one row-parallel kernel (train/model.py:121-153, 167-245).
+//
+// k_mlp_gemm  (one CTA per 128 envs, 192 threads)
+//   warp 0     allocates TMEM, then lane 0 streams K tiles with TMA:
+//              A = obs tile [128 rows x 64 k] fp16, B = packed W0 (hi and lo
+//              fp16 halves of the seat-permuted fp32 weights) [NT x 64]
+//   warp 1     lane 0 issues tcgen05.mma kind::f16, M=128, N=NT, K=16, two
+//              per K step (A*Bhi + A*Blo) into one fp32 TMEM accumulator;
+//              obs values are exact in fp16 and the hi/lo split keeps W's
+//              float32 precision
+//   warps 2-5  wait for the accumulator, tcgen05.ld their 32 TMEM lanes, add
+//              the bias and store the pre-activations [N][NT] fp32
+// k_mlp_heads (4 lanes per row)
+//   LN -> ReLU -> Linear(128,128) -> LN -> ReLU -> move/bomb/critic heads,
+//   masking with float32's lowest value, inverse-CDF sampling, log-prob.
+//
+// Every mbarrier wait is bounded; on expiry the CTA raises QQT_DEV_TIMEOUT,
+// drains the copies it issued (bounded), frees its TMEM and returns.
+
+#include <cuda.h>
+
+#include "qqt_common.cuh"
+
+namespace qqt {
+
+constexpr int kBM = 128;          // env rows per CTA
+constexpr int kBK = 64;           // K elements per stage (128 bytes of fp16)
+constexpr uint32_t kWaitLimit = 1u << 22;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait; false (and the timeout flag) when the limit expires.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  flag_error(QQT_DEV_TIMEOUT);
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// K-major operand tile with 128-byte swizzle: 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
+  const uint64_t addr = smem_u32(tile);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3FFFull;          // start address
+  d |= (uint64_t)1 << 16;                // leading byte offset (16 B, unused for SW128 K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;      // stride byte offset: next 8-row group
+  d |= (uint64_t)1 << 46;                // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                // 128-byte swizzle
+  return d;
+}
+
+// kind::f16 instruction descriptor: fp16 A/B, fp32 D, both K-major.
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int NT>
+struct GemmCfg {
+  static constexpr int kStages = NT == 128 ? 4 : 2;
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = NT * kBK * 2;          // one of hi / lo
+  static constexpr int kStageBytes = kABytes + 2 * kBBytes;
+  static constexpr int kSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <int NT>
+__global__ void __launch_bounds__(192, 1)
+k_mlp_gemm(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+           int n_rows, int k_tiles, const float* __restrict__ bias, float* __restrict__ out) {
+  using G = GemmCfg<NT>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = (uint64_t*)(smem + G::kStages * G::kStageBytes);
+  uint64_t* empty = full + G::kStages;
+  uint64_t* accb = empty + G::kStages;
+  uint32_t* tmem_slot = (uint32_t*)(accb + 1);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  const int warp = warp_id(), lane = lane_id();
+  const int m0 = blockIdx.x * kBM;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < G::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accb, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(NT));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer
+    int issued_until = 0;
+    for (int kt = 0; kt < k_tiles; ++kt) {
+      const int s = kt % G::kStages;
+      if (kt >= G::kStages) {
+        if (!mbar_wait(&empty[s], ((kt / G::kStages) - 1) & 1)) {
+          *abort_flag = 1;
+          break;
+        }
+      }
+      if (*abort_flag) break;
+      uint8_t* st = smem + s * G::kStageBytes;
+      mbar_expect_tx(&full[s], G::kStageBytes);
+      tma_load_2d(&tm_a, &full[s], st, kt * kBK, m0);
+      tma_load_2d(&tm_b, &full[s], st + G::kABytes, kt * kBK, 0);
+      tma_load_2d(&tm_b, &full[s], st + G::kABytes + G::kBBytes, kt * kBK, NT);
+      issued_until = kt + 1;
+    }
+    // drain: every issued stage must land before the CTA may exit
+    for (int kt = max(0, issued_until - G::kStages); kt < issued_until; ++kt)
+      mbar_wait(&full[kt % G::kStages], (kt / G::kStages) & 1);
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer
+    const uint32_t idesc = idesc_f16(kBM, NT);
+    bool ok = true;
+    for (int kt = 0; kt < k_tiles && ok; ++kt) {
+      const int s = kt % G::kStages;
+      if (!mbar_wait(&full[s], (kt / G::kStages) & 1) || *abort_flag) {
+        *abort_flag = 1;
+        ok = false;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      uint8_t* st = smem + s * G::kStageBytes;
+      const uint64_t da = sw128_desc(st);
+      const uint64_t dh = sw128_desc(st + G::kABytes);
+      const uint64_t dl = sw128_desc(st + G::kABytes + G::kBBytes);
+#pragma unroll
+      for (int kk = 0; kk < kBK / 16; ++kk) {
+        const uint64_t off = (uint64_t)((kk * 32) >> 4);   // 32 bytes per K=16 step
+        umma_f16(tmem, da + off, dh + off, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+        umma_f16(tmem, da + off, dl + off, idesc, 1u);
+      }
+      umma_commit(&empty[s]);
+    }
+    umma_commit(accb);   // fires once every issued MMA has completed
+  } else if (warp >= 2) {
+    // ---------------- epilogue: TMEM -> registers -> global
+    const int q = warp & 3;                       // TMEM lane quadrant of this warp
+    const bool got = mbar_wait(accb, 0);
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    if (got && !*abort_flag) {
+      const int row = m0 + q * 32 + lane;
+      for (int c0 = 0; c0 < NT; c0 += 32) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + c0, v);
+        if (row < n_rows) {
+          float4* dst = reinterpret_cast<float4*>(out + (size_t)row * NT + c0);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            dst[i] = make_float4(__fadd_rn(v[4 * i], bias[c0 + 4 * i]),
+                                 __fadd_rn(v[4 * i + 1], bias[c0 + 4 * i + 1]),
+                                 __fadd_rn(v[4 * i + 2], bias[c0 + 4 * i + 2]),
+                                 __fadd_rn(v[4 * i + 3], bias[c0 + 4 * i + 3]));
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(NT));
+  }
+}
+
+// ------------------------------------------------------------ pack layout
+
+// Pack (bytes): [B fp16: 2 x NT x KP] [f32 params]
+struct MlpPack {
+  int kp, nt, n_seats;
+  size_t b_off, f_off;
+};
+
+// f32 parameter block offsets (floats)
+enum {
+  F_B0 = 0,                       // [NT] first-layer bias per seat column
+  F_LN1G = F_B0 + 256, F_LN1B = F_LN1G + 128,
+  F_W1 = F_LN1B + 128,            // [128][128]
+  F_B1 = F_W1 + 128 * 128,
+  F_LN2G = F_B1 + 128, F_LN2B = F_LN2G + 128,
+  F_HW0 = F_LN2B + 128,           // [3][64][128] move, bomb, critic hidden
+  F_HB0 = F_HW0 + 3 * 64 * 128,   // [3][64]
+  F_HW2 = F_HB0 + 3 * 64,         // [8][64] rows: 5 move, 2 bomb, 1 value
+  F_HB2 = F_HW2 + 8 * 64,         // [8]
+  F_TOTAL = F_HB2 + 8
+};
+
+__host__ __device__ inline MlpPack mlp_pack_layout(int k_in, int n_seats) {
+  MlpPack p;
+  p.kp = (k_in + kBK - 1) / kBK * kBK;
+  p.nt = 128 * n_seats;
+  p.n_seats = n_seats;
+  p.b_off = 0;
+  p.f_off = ((size_t)2 * p.nt * p.kp * 2 + 255) / 256 * 256;
+  return p;
+}
+
+// One thread per packed weight element: column gather by the seat's view
+// permutation, then the fp16 hi / lo split.
+struct SeatChannels {
+  int32_t src[2][64];   // W0 column block used by stored channel c of seat s
+};
+
+__global__ void k_mlp_pack_w0(const float* __restrict__ w0, int k_in, int kp, int hw, int channels,
+                              SeatChannels sc, int nt, __half* __restrict__ b) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const size_t total = (size_t)nt * kp;
+  if (i >= total) return;
+  const int row = (int)(i / kp), k = (int)(i % kp);
+  float wv = 0.f;
+  if (k < k_in) {
+    const int seat = row / 128, r = row % 128;
+    const int ch = k / hw, cell = k - ch * hw;
+    const int src = sc.src[seat][ch] * hw + cell;
+    wv = w0[(size_t)r * k_in + src];
+  }
+  const __half hi = __float2half_rn(wv);
+  const __half lo = __float2half_rn(__fsub_rn(wv, __half2float(hi)));
+  b[(size_t)row * kp + k] = hi;
+  b[(size_t)nt * kp + (size_t)row * kp + k] = lo;
+}
+
+struct HeadParams {
+  const float *b0, *ln1g, *ln1b, *w1, *b1, *ln2g, *ln2b;
+  const float *mw0, *mb0, *mw2, *mb2, *bw0, *bb0, *bw2, *bb2, *cw0, *cb0, *cw2, *cb2;
+};
+
+__global__ void k_mlp_pack_rest(HeadParams hp, int n_seats, float* __restrict__ f) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < 128 * n_seats) f[F_B0 + i] = hp.b0[i % 128];
+  if (i < 128) {
+    f[F_LN1G + i] = hp.ln1g[i];
+    f[F_LN1B + i] = hp.ln1b[i];
+    f[F_B1 + i] = hp.b1[i];
+    f[F_LN2G + i] = hp.ln2g[i];
+    f[F_LN2B + i] = hp.ln2b[i];
+  }
+  if (i < 128 * 128) f[F_W1 + i] = hp.w1[i];
+  if (i < 64 * 128) {
+    f[F_HW0 + i] = hp.mw0[i];
+    f[F_HW0 + 64 * 128 + i] = hp.bw0[i];
+    f[F_HW0 + 2 * 64 * 128 + i] = hp.cw0[i];
+  }
+  if (i < 64) {
+    f[F_HB0 + i] = hp.mb0[i];
+    f[F_HB0 + 64 + i] = hp.bb0[i];
+    f[F_HB0 + 128 + i] = hp.cb0[i];
+  }
+  if (i < 8 * 64) {
+    const int r = i / 64, c = i % 64;
+    float v;
+    if (r < 5) v = hp.mw2[r * 64 + c];
+    else if (r < 7) v = hp.bw2[(r - 5) * 64 + c];
+    else v = hp.cw2[c];
+    f[F_HW2 + i] = v;
+  }
+  if (i < 8) f[F_HB2 + i] = i < 5 ? hp.mb2[i] : (i < 7 ? hp.bb2[i - 5] : hp.cb2[0]);
+}
+
+// ---------------------------------------------------------------- heads
+
+// LayerNorm over 128 values spread as 32 per lane over a 4-lane group.
+__device__ __forceinline__ void ln_relu_32(float* x, const float* g, const float* b, int part) {
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) s += x[i];
+  s += __shfl_xor_sync(QQT_FULL, s, 1);
+  s += __shfl_xor_sync(QQT_FULL, s, 2);
+  const float mean = s * (1.f / 128.f);
+  float v = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float d = x[i] - mean;
+    v = fmaf(d, d, v);
+  }
+  v += __shfl_xor_sync(QQT_FULL, v, 1);
+  v += __shfl_xor_sync(QQT_FULL, v, 2);
+  const float rstd = rsqrtf(v * (1.f / 128.f) + 1e-5f);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int k = part * 32 + i;
+    x[i] = fmaxf(fmaf((x[i] - mean) * rstd, __ldg(g + k), __ldg(b + k)), 0.f);
+  }
+}
+
+// 4 lanes per env row; lane part p holds features [32p, 32p+32).
+__global__ void __launch_bounds__(128)
+k_mlp_heads(const float* __restrict__ pre, int nt, int seat, int pid, int n_rows, int P,
+            const float* __restrict__ f, const uint8_t* __restrict__ mm,
+            const uint8_t* __restrict__ bm, const float* __restrict__ u, int64_t* __restrict__ act,
+            float* __restrict__ logp_out, float* __restrict__ value_out,
+            float* __restrict__ logits_out) {
+  __shared__ float xs[32][129];
+  const int lane = lane_id(), part = lane & 3;
+  const int lrow = threadIdx.x >> 2;                    // row within block (0..31)
+  const int row = blockIdx.x * 32 + lrow;
+  const bool valid = row < n_rows;
+  float x[32];
+  const float* src = pre + (size_t)(valid ? row : 0) * nt + seat * 128 + part * 32;
+#pragma unroll
+  for (int i = 0; i < 32; i += 4) {
+    const float4 t = *reinterpret_cast<const float4*>(src + i);
+    x[i] = t.x;
+    x[i + 1] = t.y;
+    x[i + 2] = t.z;
+    x[i + 3] = t.w;
+  }
+  ln_relu_32(x, f + F_LN1G, f + F_LN1B, part);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) xs[lrow][part * 32 + i] = x[i];
+  __syncwarp();
+  // layer 2: this lane computes outputs [32p, 32p+32) from the full row
+  float y[32];
+  const float* w1 = f + F_W1;
+  for (int j = 0; j < 32; ++j) {
+    const int o = part * 32 + j;
+    float acc = __ldg(f + F_B1 + o);
+    const float* wr = w1 + o * 128;
+#pragma unroll 8
+    for (int k = 0; k < 128; k += 4) {
+      const float4 wv = __ldg(reinterpret_cast<const float4*>(wr + k));
+      acc = fmaf(wv.x, xs[lrow][k], acc);
+      acc = fmaf(wv.y, xs[lrow][k + 1], acc);
+      acc = fmaf(wv.z, xs[lrow][k + 2], acc);
+      acc = fmaf(wv.w, xs[lrow][k + 3], acc);
+    }
+    y[j] = acc;
+  }
+  ln_relu_32(y, f + F_LN2G, f + F_LN2B, part);
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 32; ++i) xs[lrow][part * 32 + i] = y[i];
+  __syncwarp();
+  // heads: 192 hidden units (3 heads x 64), 48 per lane; final layers summed
+  float outp[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int j = 0; j < 48; ++j) {
+    const int hu = part * 48 + j;            // 0..191
+    const int head = hu / 64, hi = hu % 64;
+    const float* wr = f + F_HW0 + (size_t)hu * 128;
+    float acc = __ldg(f + F_HB0 + hu);
+#pragma unroll 8
+    for (int k = 0; k < 128; k += 4) {
+      const float4 wv = __ldg(reinterpret_cast<const float4*>(wr + k));
+      acc = fmaf(wv.x, xs[lrow][k], acc);
+      acc = fmaf(wv.y, xs[lrow][k + 1], acc);
+      acc = fmaf(wv.z, xs[lrow][k + 2], acc);
+      acc = fmaf(wv.w, xs[lrow][k + 3], acc);
+    }
+    acc = fmaxf(acc, 0.f);
+    const float* w2 = f + F_HW2;
+    if (head == 0) {
+#pragma unroll
+      for (int o = 0; o < 5; ++o) outp[o] = fmaf(__ldg(w2 + o * 64 + hi), acc, outp[o]);
+    } else if (head == 1) {
+#pragma unroll
+      for (int o = 5; o < 7; ++o) outp[o] = fmaf(__ldg(w2 + o * 64 + hi), acc, outp[o]);
+    } else {
+      outp[7] = fmaf(__ldg(w2 + 7 * 64 + hi), acc, outp[7]);
+    }
+  }
+#pragma unroll
+  for (int o = 0; o < 8; ++o) {
+    outp[o] += __shfl_xor_sync(QQT_FULL, outp[o], 1);
+    outp[o] += __shfl_xor_sync(QQT_FULL, outp[o], 2);
+  }
+  if (!valid || part != 0) return;
+  float z[8];
+#pragma unroll
+  for (int o = 0; o < 8; ++o) z[o] = outp[o] + __ldg(f + F_HB2 + o);
+  if (logits_out) {
+    float* lo = logits_out + ((size_t)seat * n_rows + row) * 8;
+#pragma unroll
+    for (int o = 0; o < 8; ++o) lo[o] = z[o];
+  }
+  const float lowest = -3.402823466e38f;
+  const uint8_t* mrow = mm + ((size_t)row * P + pid) * 5;
+  const uint8_t* brow = bm + ((size_t)row * P + pid) * 2;
+  // move head
+  float zm[5], zb[2];
+  float mx = lowest;
+  for (int k = 0; k < 5; ++k) {
+    zm[k] = mrow[k] ? z[k] : lowest;
+    mx = fmaxf(mx, zm[k]);
+  }
+  float cs[5], acc = 0.f;
+  for (int k = 0; k < 5; ++k) {
+    acc += expf(zm[k] - mx);
+    cs[k] = acc;
+  }
+  const float um = u[((size_t)seat * n_rows + row) * 2] * acc;
+  int am = 0;
+  for (int k = 0; k < 5; ++k) am += um > cs[k];
+  am = min(am, 4);
+  const float lpm = zm[am] - mx - logf(acc);
+  float mb = lowest;
+  for (int k = 0; k < 2; ++k) {
+    zb[k] = brow[k] ? z[5 + k] : lowest;
+    mb = fmaxf(mb, zb[k]);
+  }
+  const float e0 = expf(zb[0] - mb), s2 = e0 + expf(zb[1] - mb);
+  const float ub = u[((size_t)seat * n_rows + row) * 2 + 1] * s2;
+  const int ab = ub > e0 ? 1 : 0;
+  const float lpb = zb[ab] - mb - logf(s2);
+  act[((size_t)row * P + pid) * 2] = am;
+  act[((size_t)row * P + pid) * 2 + 1] = ab;
+  if (logp_out) logp_out[(size_t)seat * n_rows + row] = lpm + lpb;
+  if (value_out) value_out[(size_t)seat * n_rows + row] = z[7];
+}
+
+}  // namespace qqt
+
+using namespace qqt;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)p;
+  }
+  return fn;
+}
+
+// 2-D fp16 K-major tensor map: inner dim K (elements), outer dim rows.
+static bool make_map(CUtensorMap* m, const void* base, uint64_t k, uint64_t rows,
+                     uint64_t row_bytes, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {k, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static const char* kParamNames =
+    "shared.0.weight shared.0.bias shared.1.weight shared.1.bias shared.3.weight shared.3.bias "
+    "shared.4.weight shared.4.bias move_head.0.weight move_head.0.bias move_head.2.weight "
+    "move_head.2.bias bomb_head.0.weight bomb_head.0.bias bomb_head.2.weight bomb_head.2.bias "
+    "critic.0.weight critic.0.bias critic.2.weight critic.2.bias";
+
+extern "C" const char* qqt_mlp_param_names(void) { return kParamNames; }
+
+extern "C" uint64_t qqt_mlp_pack_bytes(int32_t k_in, int32_t n_seats) {
+  if (k_in <= 0 || n_seats < 1 || n_seats > 2) return 0;
+  const MlpPack L = mlp_pack_layout(k_in, n_seats);
+  return L.f_off + (uint64_t)F_TOTAL * 4;
+}
+
+extern "C" int qqt_mlp_pack(const float* const* params, int32_t k_in, int32_t n_players,
+                            int32_t channels, int32_t hw, int32_t n_seats, const int32_t* pids,
+                            void* pack, qqt_stream_t stream) {
+  if (!params || !pack || !pids || n_seats < 1 || n_seats > 2) return QQT_E_ARG;
+  if (k_in != channels * hw) return QQT_E_ARG;
+  if (n_players < 2 || n_players > QQT_MAX_P || channels > 64) return QQT_E_ARG;
+  for (int i = 0; i < 20; ++i)
+    if (!params[i]) return QQT_E_ARG;
+  const MlpPack L = mlp_pack_layout(k_in, n_seats);
+  // source channel of each stored channel for each seat: inverse of the view permutation
+  SeatChannels sc;
+  memset(&sc, 0, sizeof(sc));
+  const int base = 2 * n_players + 3;
+  for (int s = 0; s < n_seats; ++s) {
+    const int me = pids[s];
+    if (me < 0 || me >= n_players) return QQT_E_ARG;
+    int perm[64], j = 0;
+    perm[j++] = me;
+    perm[j++] = n_players + me;
+    for (int i = 0; i < n_players; ++i)
+      if (i != me) perm[j++] = i;
+    for (int i = 0; i < n_players; ++i)
+      if (i != me) perm[j++] = n_players + i;
+    perm[j++] = 2 * n_players;
+    perm[j++] = 2 * n_players + 1;
+    perm[j++] = 2 * n_players + 2;
+    for (int c = base; c < channels; ++c) perm[j++] = c;
+    // view channel v reads stored channel perm[v]; W0's column block v pairs with
+    // view channel v, so stored channel perm[v] takes W0 block v
+    for (int v = 0; v < channels; ++v) sc.src[s][perm[v]] = v;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  uint8_t* pk = (uint8_t*)pack;
+  const size_t total = (size_t)L.nt * L.kp;
+  k_mlp_pack_w0<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
+      params[0], k_in, L.kp, hw, channels, sc, L.nt, (__half*)(pk + L.b_off));
+  HeadParams hp;
+  hp.b0 = params[1];
+  hp.ln1g = params[2];
+  hp.ln1b = params[3];
+  hp.w1 = params[4];
+  hp.b1 = params[5];
+  hp.ln2g = params[6];
+  hp.ln2b = params[7];
+  hp.mw0 = params[8];
+  hp.mb0 = params[9];
+  hp.mw2 = params[10];
+  hp.mb2 = params[11];
+  hp.bw0 = params[12];
+  hp.bb0 = params[13];
+  hp.bw2 = params[14];
+  hp.bb2 = params[15];
+  hp.cw0 = params[16];
+  hp.cb0 = params[17];
+  hp.cw2 = params[18];
+  hp.cb2 = params[19];
+  k_mlp_pack_rest<<<(128 * 128 + 255) / 256, 256, 0, st>>>(hp, n_seats, (float*)(pk + L.f_off));
+  return launch_status();
+}
+
+extern "C" uint64_t qqt_mlp_work_bytes(int32_t n_envs, int32_t n_seats) {
+  return (uint64_t)n_envs * 128 * n_seats * 4;
+}
+
+extern "C" int qqt_mlp_act(const void* pack, const void* obs, int32_t n_envs, int32_t obs_stride,
+                           int32_t k_in, int32_t n_players, const uint8_t* mm, const uint8_t* bm,
+                           int32_t n_seats, const int32_t* pids, const float* u, int64_t* act,
+                           float* logp, float* value, float* logits, void* work,
+                           qqt_stream_t stream) {
+  if (!pack || !obs || !mm || !bm || !pids || !u || !act || !work) return QQT_E_ARG;
+  if (n_envs <= 0 || n_seats < 1 || n_seats > 2 || n_players < 2 || n_players > QQT_MAX_P)
+    return QQT_E_ARG;
+  if (obs_stride % 8 || obs_stride < k_in || ((uintptr_t)obs & 15) || ((uintptr_t)pack & 255))
+    return QQT_E_ALIGN;
+  const MlpPack L = mlp_pack_layout(k_in, n_seats);
+  const uint8_t* pk = (const uint8_t*)pack;
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, obs, (uint64_t)obs_stride, (uint64_t)n_envs, (uint64_t)obs_stride * 2, kBM))
+    return QQT_E_ARG;
+  if (!make_map(&mb, pk + L.b_off, (uint64_t)L.kp, (uint64_t)2 * L.nt, (uint64_t)L.kp * 2,
+                (uint32_t)L.nt))
+    return QQT_E_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  float* pre = (float*)work;
+  const float* fpar = (const float*)(pk + L.f_off);
+  const int k_tiles = L.kp / kBK;
+  const int grid = (n_envs + kBM - 1) / kBM;
+  if (L.nt == 128) {
+    cudaFuncSetAttribute(k_mlp_gemm<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         GemmCfg<128>::kSmem);
+    k_mlp_gemm<128><<<grid, 192, GemmCfg<128>::kSmem, st>>>(ma, mb, n_envs, k_tiles, fpar + F_B0, pre);
+  } else {
+    cudaFuncSetAttribute(k_mlp_gemm<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         GemmCfg<256>::kSmem);
+    k_mlp_gemm<256><<<grid, 192, GemmCfg<256>::kSmem, st>>>(ma, mb, n_envs, k_tiles, fpar + F_B0, pre);
+  }
+  for (int s = 0; s < n_seats; ++s) {
+    k_mlp_heads<<<(n_envs + 31) / 32, 128, 0, st>>>(pre, L.nt, s, pids[s], n_envs, n_players, fpar,
+                                                      mm, bm, u, act, logp, value, logits);
+  }
+  return launch_status();
+}

@@ -1,0 +1,5 @@
+// Unity build of libqqt_b200.so: one translation unit so the device error
+// word and helpers are shared without relocatable device code.
+#include "sim_observe.cu"
+#include "sim_step.cu"
+#include "policy_mlp.cu"

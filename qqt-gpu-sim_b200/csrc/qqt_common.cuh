@@ -1,0 +1,380 @@
+// Shared device code of the B200 rollout engine.
+//
+// Work decomposition: one thread block owns a tile of QQT_TILE_E consecutive
+// envs.  The block stages the tile's planes from the SoA global layout
+// ([cell][env], env innermost, so consecutive threads read consecutive envs)
+// into shared memory transposed to [env][cell], then each warp simulates one
+// env at a time with its 32 lanes spread over cells / bombs / players.  With
+// per-env contiguous planes, lanes walking consecutive cells hit distinct
+// banks.
+//
+// Float arithmetic on the parity path uses the _rn intrinsics in the exact
+// operation order of the reference (the library is also built with
+// -fmad=false), so positions, rewards and danger match the reference bit for
+// bit.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/qqt_b200.h"
+
+#define QQT_MAX_H 21
+#define QQT_MAX_W 21
+#define QQT_MAX_CELLS (QQT_MAX_H * QQT_MAX_W)
+#define QQT_MAX_P 4
+#define QQT_TILE_E 32
+#define QQT_NWARP 8
+#define QQT_FULL 0xffffffffu
+
+namespace qqt {
+
+__device__ unsigned int g_error = 0;   // device error word (qqt_get_error)
+
+__device__ __forceinline__ void flag_error(unsigned bits) { atomicOr(&g_error, bits); }
+
+__device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
+__device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
+
+__device__ __forceinline__ int warp_sum(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(QQT_FULL, v, o);
+  return v;
+}
+__device__ __forceinline__ int warp_max(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(QQT_FULL, v, o));
+  return v;
+}
+
+// Cells c in [0, n) with pred(c), ascending, written to list; returns count.
+template <class F>
+__device__ __forceinline__ int warp_compact(int n, uint16_t* list, F pred) {
+  const int lane = lane_id();
+  int count = 0;
+  for (int base = 0; base < n; base += 32) {
+    const int c = base + lane;
+    const bool p = c < n && pred(c);
+    const unsigned m = __ballot_sync(QQT_FULL, p);
+    if (p) list[count + __popc(m & ((1u << lane) - 1u))] = (uint16_t)c;
+    count += __popc(m);
+  }
+  __syncwarp();
+  return count;
+}
+
+// ------------------------------------------------------------ tile staging
+
+// Per-env planes of one block tile, [env slot][cell].
+struct Tile {
+  uint8_t *wall, *brick, *crate, *recycle;
+  int8_t* owner;
+  int16_t *fuse, *blast;
+  int cells;
+};
+
+__host__ __device__ inline size_t tile_bytes(int cells) {
+  // 4 u8 planes + owner + 2 i16 planes, each E * cells, 16-byte aligned
+  const size_t u8 = ((size_t)QQT_TILE_E * cells + 15) & ~(size_t)15;
+  const size_t i16 = ((size_t)QQT_TILE_E * cells * 2 + 15) & ~(size_t)15;
+  return 5 * u8 + 2 * i16;
+}
+
+__device__ inline Tile carve_tile(uint8_t* base, int cells) {
+  Tile t;
+  const size_t u8 = ((size_t)QQT_TILE_E * cells + 15) & ~(size_t)15;
+  const size_t i16 = ((size_t)QQT_TILE_E * cells * 2 + 15) & ~(size_t)15;
+  t.wall = base;
+  t.brick = base + u8;
+  t.crate = base + 2 * u8;
+  t.recycle = base + 3 * u8;
+  t.owner = (int8_t*)(base + 4 * u8);
+  t.fuse = (int16_t*)(base + 5 * u8);
+  t.blast = (int16_t*)(base + 5 * u8 + i16);
+  t.cells = cells;
+  return t;
+}
+
+enum : unsigned {
+  PL_WALL = 1, PL_BRICK = 2, PL_CRATE = 4, PL_RECYCLE = 8,
+  PL_OWNER = 16, PL_FUSE = 32, PL_BLAST = 64, PL_ALL = 127
+};
+
+// Global [cell][N] -> shared [slot][cell] for envs e0 .. e0+E-1 (block-wide).
+__device__ inline void load_tile(const Tile& t, const QqtState& st, int n, int e0,
+                                 unsigned planes) {
+  const int cells = t.cells;
+  const int total = cells * QQT_TILE_E;
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const int c = i / QQT_TILE_E;
+    const int s = i - c * QQT_TILE_E;
+    const int e = e0 + s;
+    const int so = s * cells + c;
+    if (e < n) {
+      const size_t g = (size_t)c * n + e;
+      if (planes & PL_WALL) t.wall[so] = st.wall[g];
+      if (planes & PL_BRICK) t.brick[so] = st.brick[g];
+      if (planes & PL_CRATE) t.crate[so] = st.crate[g];
+      if (planes & PL_RECYCLE) t.recycle[so] = st.recycle[g];
+      if (planes & PL_OWNER) t.owner[so] = st.owner[g];
+      if (planes & PL_FUSE) t.fuse[so] = st.fuse[g];
+      if (planes & PL_BLAST) t.blast[so] = st.bomb_blast[g];
+    }
+  }
+}
+
+__device__ inline void store_tile(const Tile& t, const QqtState& st, int n, int e0,
+                                  unsigned planes) {
+  const int cells = t.cells;
+  const int total = cells * QQT_TILE_E;
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const int c = i / QQT_TILE_E;
+    const int s = i - c * QQT_TILE_E;
+    const int e = e0 + s;
+    const int so = s * cells + c;
+    if (e < n) {
+      const size_t g = (size_t)c * n + e;
+      if (planes & PL_WALL) st.wall[g] = t.wall[so];
+      if (planes & PL_BRICK) st.brick[g] = t.brick[so];
+      if (planes & PL_CRATE) st.crate[g] = t.crate[so];
+      if (planes & PL_RECYCLE) st.recycle[g] = t.recycle[so];
+      if (planes & PL_OWNER) st.owner[g] = t.owner[so];
+      if (planes & PL_FUSE) st.fuse[g] = t.fuse[so];
+      if (planes & PL_BLAST) st.bomb_blast[g] = t.blast[so];
+    }
+  }
+}
+
+// One env's view into the tile.
+struct Env {
+  uint8_t *wall, *brick, *crate, *recycle;
+  int8_t* owner;
+  int16_t *fuse, *blast;
+  int h, w, cells;
+};
+
+__device__ inline Env env_view(const Tile& t, int slot, int h, int w) {
+  const int o = slot * t.cells;
+  Env v;
+  v.wall = t.wall + o;
+  v.brick = t.brick + o;
+  v.crate = t.crate + o;
+  v.recycle = t.recycle + o;
+  v.owner = t.owner + o;
+  v.fuse = t.fuse + o;
+  v.blast = t.blast + o;
+  v.h = h;
+  v.w = w;
+  v.cells = t.cells;
+  return v;
+}
+
+__device__ __forceinline__ int blast_of(const Env& v, int c, int default_blast) {
+  const int b = v.blast[c];
+  return b > 0 ? b : default_blast;
+}
+
+__constant__ const int kDR[4] = {-1, 1, 0, 0};
+__constant__ const int kDC[4] = {0, 0, -1, 1};
+
+// ------------------------------------------------------------- fire rays
+
+// Flame of one source: its own cell (unless wall/brick) plus, when its blast
+// is within the tier bound, up to `blast` cells per direction; walls stop
+// the ray uncovered, solid cells (live bombs, bricks) are covered then stop
+// it (sim/blast.py:43-98).  `cov` is a byte map; concurrent writers only
+// store 1.
+__device__ inline void emit_flame(const Env& v, int src, int blast, int tier_cap,
+                                  volatile uint8_t* cov) {
+  if (v.wall[src] || v.brick[src]) return;
+  cov[src] = 1;
+  if (blast > tier_cap) return;
+  const int r0 = src / v.w, c0 = src - r0 * v.w;
+  for (int d = 0; d < 4; ++d) {
+    int r = r0, c = c0;
+    for (int k = 1; k <= blast; ++k) {
+      r += kDR[d];
+      c += kDC[d];
+      if (r < 0 || r >= v.h || c < 0 || c >= v.w) break;
+      const int q = r * v.w + c;
+      if (v.wall[q]) break;
+      cov[q] = 1;
+      if (v.fuse[q] > 0 || v.brick[q]) break;
+    }
+  }
+}
+
+// ------------------------------------------------------------- danger map
+
+// Bomb weight clamp(1 - (f-1)/FUSE, 0)^2 in float32 (sim/blast.py:218-220).
+__device__ __forceinline__ float fuse_weight(int f, float fuse_f) {
+  if (f <= 0) return 0.f;
+  float raw = __fsub_rn(1.f, __fdiv_rn(__fsub_rn((float)f, 1.f), fuse_f));
+  raw = fmaxf(raw, 0.f);
+  return __fmul_rn(raw, raw);
+}
+
+// Largest weight `val` over the bombs whose flame reaches cell c (the nearest
+// bomb along each direction, within its blast, through clear cells), or 0.
+// Solid = bomb (fuse > 0) or brick; walls stop silently.
+__device__ inline float reach_max(const Env& v, int c, const float* val, int default_blast,
+                                  int max_b) {
+  const int r0 = c / v.w, c0 = c - r0 * v.w;
+  float best = 0.f;
+  for (int d = 0; d < 4; ++d) {
+    int r = r0, cc = c0;
+    for (int k = 1; k <= max_b; ++k) {
+      r -= kDR[d];
+      cc -= kDC[d];
+      if (r < 0 || r >= v.h || cc < 0 || cc >= v.w) break;
+      const int q = r * v.w + cc;
+      if (v.wall[q]) break;
+      if (v.fuse[q] > 0) {
+        if (k <= blast_of(v, q, default_blast)) best = fmaxf(best, val[q]);
+        break;
+      }
+      if (v.brick[q]) break;
+    }
+  }
+  return best;
+}
+
+// Per-warp scratch for the danger map, indexed by cell.
+struct DangerScratch {
+  float* cur;     // chain-corrected bomb weights
+  float* front;   // front value (0 = not in front)
+  float* spread;
+  uint16_t* bombs;
+};
+
+// Stage A (chain correction among bombs, sim/blast.py:251-289).  Fills
+// s.cur[c] for every bomb cell (0 elsewhere).  Returns the bomb count.
+__device__ inline int danger_stage_a(const Env& v, const DangerScratch& s, float fuse_f,
+                                     int default_blast, int rounds, int* max_b_out) {
+  const int lane = lane_id();
+  const int nb = warp_compact(v.cells, s.bombs, [&](int c) { return v.fuse[c] > 0; });
+  int mb = 0;
+  for (int c = lane; c < v.cells; c += 32) {
+    const float w = fuse_weight(v.fuse[c], fuse_f);
+    s.cur[c] = w;
+    s.front[c] = w;
+    if (v.fuse[c] > 0) mb = max(mb, blast_of(v, c, default_blast));
+  }
+  mb = warp_max(mb);
+  *max_b_out = mb;
+  __syncwarp();
+  for (int r = 0; r < rounds && nb > 0; ++r) {
+    for (int i = lane; i < nb; i += 32) {
+      const int c = s.bombs[i];
+      s.spread[c] = reach_max(v, c, s.front, default_blast, mb);
+    }
+    __syncwarp();
+    // each bomb is updated by one lane and reads only its own entries here
+    bool any_new = false;
+    for (int i = lane; i < nb; i += 32) {
+      const int c = s.bombs[i];
+      const float sp = s.spread[c];
+      const bool nw = sp > s.cur[c];
+      s.cur[c] = fmaxf(s.cur[c], sp);
+      s.front[c] = nw ? sp : 0.f;   // newly raised bombs form the next front
+      any_new |= nw;
+    }
+    __syncwarp();
+    if (!__any_sync(QQT_FULL, any_new)) break;
+  }
+  return nb;
+}
+
+// Stage B value at one cell (sim/blast.py:291-317): walls 0, else the max of
+// the cell's own bomb weight and every reaching bomb's corrected weight.
+__device__ __forceinline__ float danger_at(const Env& v, const DangerScratch& s, int c,
+                                           int default_blast, int max_b) {
+  if (v.wall[c]) return 0.f;
+  const float own = v.fuse[c] > 0 ? s.cur[c] : 0.f;
+  return fmaxf(own, reach_max(v, c, s.cur, default_blast, max_b));
+}
+
+// ------------------------------------------------------------ movement
+
+// Either of two cells blocks a player whose box currently spans
+// rows [ra, rb] x cols [ca, cb] (sim/move.py:72-95).
+__device__ __forceinline__ bool impassable_pair(const Env& v, int r0, int c0, int r1, int c1,
+                                                int ra, int rb, int ca, int cb) {
+  const int h = v.h, w = v.w;
+  if (r0 < 0 || r0 >= h || c0 < 0 || c0 >= w || r1 < 0 || r1 >= h || c1 < 0 || c1 >= w)
+    return true;
+  const int q0 = r0 * w + c0, q1 = r1 * w + c1;
+  const bool s0 = v.wall[q0] || v.brick[q0] || v.fuse[q0] > 0;
+  const bool s1 = v.wall[q1] || v.brick[q1] || v.fuse[q1] > 0;
+  const bool in0 = r0 >= ra && r0 <= rb && c0 >= ca && c0 <= cb;
+  const bool in1 = r1 >= ra && r1 <= rb && c1 >= ca && c1 <= cb;
+  return (s0 && !in0) || (s1 && !in1);
+}
+
+// Slide along one axis; stop flush against the first blocking cell
+// (sim/move.py:98-151).  Same float operation order as the reference.
+__device__ inline float resolve_axis(const Env& v, float coord, float delta, float other,
+                                     float y, float x, float rad, bool vertical) {
+  const float sgn = delta > 0.f ? 1.f : (delta < 0.f ? -1.f : 0.f);
+  const float sr = __fmul_rn(sgn, rad);
+  const int old_lead = (int)floorf(__fadd_rn(__fsub_rn(coord, delta), sr));
+  const int new_lead = (int)floorf(__fadd_rn(coord, sr));
+  const int lo = min(old_lead, new_lead), hi = max(old_lead, new_lead);
+  const int span0 = (int)floorf(__fsub_rn(other, rad));
+  const int span1 = (int)floorf(__fadd_rn(other, rad));
+  const int ra = (int)floorf(__fsub_rn(y, rad)), rb = (int)floorf(__fadd_rn(y, rad));
+  const int ca = (int)floorf(__fsub_rn(x, rad)), cb = (int)floorf(__fadd_rn(x, rad));
+  bool hit_lo, hit_hi;
+  if (vertical) {
+    hit_lo = impassable_pair(v, lo, span0, lo, span1, ra, rb, ca, cb);
+    hit_hi = impassable_pair(v, hi, span0, hi, span1, ra, rb, ca, cb);
+  } else {
+    hit_lo = impassable_pair(v, span0, lo, span1, lo, ra, rb, ca, cb);
+    hit_hi = impassable_pair(v, span0, hi, span1, hi, ra, rb, ca, cb);
+  }
+  const bool pos = sgn > 0.f;
+  const int first_lead = pos ? hi : lo, second_lead = pos ? lo : hi;
+  const bool first_hit = pos ? hit_hi : hit_lo, second_hit = pos ? hit_lo : hit_hi;
+  if (!(first_hit || second_hit)) return coord;
+  const float f = (float)(first_hit ? first_lead : second_lead);
+  const float eps = 1e-4f;
+  return pos ? __fsub_rn(__fsub_rn(f, rad), eps)
+             : __fadd_rn(__fadd_rn(__fadd_rn(f, 1.f), rad), eps);
+}
+
+// Centre cell of a position, clamped to the grid (sim/move.py:282-288 plus
+// the reference's defensive clamp); out-of-grid positions raise a flag.
+__device__ __forceinline__ int center_cell(float y, float x, int h, int w) {
+  const int r = (int)floorf(y), c = (int)floorf(x);
+  int flat = r * w + c;
+  if (r < 0 || r >= h || c < 0 || c >= w) {
+    flag_error(QQT_DEV_POS_RANGE);
+    flat = min(max(flat, 0), h * w - 1);
+  }
+  return flat;
+}
+
+// Deterministic uniform in [0, 1) from a 64-bit key (splitmix64 finaliser).
+__host__ __device__ __forceinline__ float hash_uniform(uint64_t x) {
+  x += 0x9E3779B97F4A7C15ull;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  x ^= x >> 31;
+  return (float)(x >> 40) * (1.0f / 16777216.0f);
+}
+
+}  // namespace qqt
+
+static inline int check_cfg(const QqtCfg* cfg) {
+  if (!cfg) return QQT_E_ARG;
+  if (cfg->n_envs <= 0 || cfg->height <= 0 || cfg->width <= 0) return QQT_E_ARG;
+  if (cfg->height > QQT_MAX_H || cfg->width > QQT_MAX_W || cfg->n_players < 2 ||
+      cfg->n_players > QQT_MAX_P)
+    return QQT_E_LIMIT;
+  return QQT_OK;
+}
+
+static inline int launch_status() {
+  return cudaGetLastError() == cudaSuccess ? QQT_OK : QQT_E_LAUNCH;
+}

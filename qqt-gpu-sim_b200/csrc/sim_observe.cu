@@ -1,0 +1,638 @@
+// Danger map + shared fp16 observation + legal masks, and the rule bots.
+//
+// k_observe: one block per tile of 32 envs, one warp per env at a time.
+//   danger: stage A (chain correction among bombs, gather over the nearest
+//   bomb per direction) then stage B per cell; observation rows are written
+//   straight from registers in 16-byte chunks (lane j writes chunk j of the
+//   env's padded row), so every store is a coalesced 128-bit store.
+// k_astar: warp per env; the two path fields share one warp (row / column
+//   sweeps to a fixed point, exactly the reference's Bellman-Ford limit).
+
+#include "qqt_common.cuh"
+
+namespace qqt {
+
+
+// One seat's masks and action rows: row e at base + e * stride.
+struct SeatIO {
+  const uint8_t* mm;
+  const uint8_t* bm;
+  int64_t* act;
+  int mm_stride, bm_stride, act_stride;
+};
+
+struct PInfo {
+  float y, x, sw[4];
+  int sc[4];
+  int flat, alive, live;
+  float inv, avail, capv;
+  int64_t bombs_cap;
+};
+
+__host__ __device__ inline size_t observe_warp_bytes(int cells) {
+  // cur, front, spread, dng (float) + bombs (u16) + PInfo[4]
+  return ((size_t)cells * 16 + (size_t)cells * 2 + 15) / 16 * 16 + 4 * sizeof(PInfo) + 64;
+}
+
+template <bool F32OUT>
+__global__ void __launch_bounds__(QQT_NWARP * 32)
+k_observe(QqtCfg cfg, QqtState st, void* obs, float* danger_out, uint8_t* mm, uint8_t* bm) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int h = cfg.height, w = cfg.width, C = h * w, N = cfg.n_envs, P = cfg.n_players;
+  const int e0 = blockIdx.x * QQT_TILE_E;
+  Tile tile = carve_tile(smem, C);
+  load_tile(tile, st, N, e0, PL_WALL | PL_BRICK | PL_CRATE | PL_OWNER | PL_FUSE | PL_BLAST);
+  __syncthreads();
+  uint8_t* wb = smem + tile_bytes(C) + (size_t)warp_id() * observe_warp_bytes(C);
+  DangerScratch ds;
+  ds.cur = (float*)wb;
+  ds.front = ds.cur + C;
+  ds.spread = ds.front + C;
+  float* dng = ds.spread + C;
+  ds.bombs = (uint16_t*)(dng + C);
+  PInfo* pi = (PInfo*)(wb + ((size_t)C * 16 + (size_t)C * 2 + 15) / 16 * 16);
+  const int lane = lane_id();
+
+  for (int s = warp_id(); s < QQT_TILE_E; s += QQT_NWARP) {
+    const int e = e0 + s;
+    if (e >= N) break;
+    const Env v = env_view(tile, s, h, w);
+    int max_b = 0;
+    danger_stage_a(v, ds, cfg.fuse_f, cfg.blast, cfg.danger_rounds, &max_b);
+    for (int c = lane; c < C; c += 32) {
+      const float d = danger_at(v, ds, c, cfg.blast, max_b);
+      dng[c] = d;
+      if (danger_out) danger_out[(size_t)e * C + c] = d;
+    }
+    // live bombs per player
+    int cnt[QQT_MAX_P] = {0, 0, 0, 0};
+    for (int c = lane; c < C; c += 32) {
+      const int o = v.owner[c];
+      if (v.fuse[c] > 0 && o >= 0 && o < P) cnt[o]++;
+    }
+    int live[QQT_MAX_P];
+#pragma unroll
+    for (int p = 0; p < QQT_MAX_P; ++p) live[p] = warp_sum(cnt[p]);
+    if (lane < P) {
+      const int p = lane;
+      PInfo q;
+      q.y = st.pos[((size_t)p * 2 + 0) * N + e];
+      q.x = st.pos[((size_t)p * 2 + 1) * N + e];
+      q.alive = st.alive[(size_t)p * N + e] != 0;
+      q.live = live[p];
+      const float g = q.alive ? 1.f : 0.f;
+      const float fy = fminf(fmaxf(__fsub_rn(q.y, 0.5f), 0.f), (float)(h - 1));
+      const float fx = fminf(fmaxf(__fsub_rn(q.x, 0.5f), 0.f), (float)(w - 1));
+      const int y0 = min(max((int)floorf(fy), 0), h - 1), x0 = min(max((int)floorf(fx), 0), w - 1);
+      const int y1 = min(y0 + 1, h - 1), x1 = min(x0 + 1, w - 1);
+      const float wy = fminf(fmaxf(__fsub_rn(fy, (float)y0), 0.f), 1.f);
+      const float wx = fminf(fmaxf(__fsub_rn(fx, (float)x0), 0.f), 1.f);
+      const float wys[2] = {__fsub_rn(1.f, wy), wy}, wxs[2] = {__fsub_rn(1.f, wx), wx};
+      const int ys[2] = {y0, y1}, xs[2] = {x0, x1};
+#pragma unroll
+      for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+          q.sc[a * 2 + b] = ys[a] * w + xs[b];
+          q.sw[a * 2 + b] = __fmul_rn(__fmul_rn(wys[a], wxs[b]), g);
+        }
+      q.flat = center_cell(q.y, q.x, h, w);
+      const int64_t inv = st.invuln[(size_t)p * N + e];
+      q.inv = (inv > 0 && q.alive) ? 1.f : 0.f;
+      q.bombs_cap = st.bombs_cap[(size_t)p * N + e];
+      const float cap = fmaxf((float)q.bombs_cap, 1.f);
+      const float avail = fmaxf((float)(q.bombs_cap - (int64_t)q.live), 0.f);
+      q.avail = __fmul_rn(__fdiv_rn(avail, cap), g);
+      q.capv = __fmul_rn(__fdiv_rn(cap, cfg.obs_growth_bombs_max), g);
+      pi[p] = q;
+    }
+    __syncwarp();
+
+    if (obs) {
+      const float tv = __fdiv_rn((float)st.t[e], cfg.max_steps_f);
+      const int epc = F32OUT ? 4 : 8;
+      const int nchunk = cfg.obs_stride / epc;
+      const int ch_used = cfg.obs_channels;
+      for (int j = lane; j < nchunk; j += 32) {
+        float vals[8];
+        int i = j * epc;
+        int ch = i / C, cell = i - ch * C;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if (k >= epc) break;
+          float val = 0.f;
+          if (ch < ch_used) {
+            if (ch < P) {
+              const PInfo& q = pi[ch];
+#pragma unroll
+              for (int m = 0; m < 4; ++m)
+                if (q.sc[m] == cell) val = __fadd_rn(val, q.sw[m]);
+            } else if (ch < 2 * P) {
+              const int f = v.fuse[cell];
+              if (f > 0 && v.owner[cell] == ch - P) val = __fdiv_rn((float)f, cfg.fuse_f);
+            } else if (ch == 2 * P) {
+              val = (v.wall[cell] | v.brick[cell]) ? 1.f : 0.f;
+            } else if (ch == 2 * P + 1) {
+              val = dng[cell];
+            } else if (ch == 2 * P + 2) {
+              val = tv;
+            } else if (ch == 2 * P + 3) {
+              val = v.crate[cell] ? 1.f : 0.f;
+            } else if (ch < 3 * P + 4) {
+              const PInfo& q = pi[ch - (2 * P + 4)];
+              if (q.flat == cell) val = q.inv;
+            } else if (ch < 4 * P + 4) {
+              const PInfo& q = pi[ch - (3 * P + 4)];
+              if (q.flat == cell) val = q.avail;
+            } else {
+              const PInfo& q = pi[ch - (4 * P + 4)];
+              if (q.flat == cell) val = q.capv;
+            }
+          }
+          vals[k] = val;
+          if (++cell == C) {
+            cell = 0;
+            ++ch;
+          }
+        }
+        if (F32OUT) {
+          float4 out4 = make_float4(vals[0], vals[1], vals[2], vals[3]);
+          reinterpret_cast<float4*>((float*)obs + (size_t)e * cfg.obs_stride)[j] = out4;
+        } else {
+          uint4 out4;
+          __half2 hh[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            hh[k] = __halves2half2(__float2half_rn(vals[2 * k]), __float2half_rn(vals[2 * k + 1]));
+          memcpy(&out4, hh, 16);
+          reinterpret_cast<uint4*>((__half*)obs + (size_t)e * cfg.obs_stride)[j] = out4;
+        }
+      }
+    }
+
+    if (mm) {
+      if (lane < 4 * P) {
+        const int p = lane >> 2, d = lane & 3;
+        const PInfo& q = pi[p];
+        const float dv = (d & 1) ? cfg.step_len : -cfg.step_len;
+        bool moved;
+        if (d < 2) {
+          const float ny = resolve_axis(v, __fadd_rn(q.y, dv), dv, q.x, q.y, q.x, cfg.radius, true);
+          moved = fabsf(__fsub_rn(ny, q.y)) > cfg.move_eps2;
+        } else {
+          const float nx = resolve_axis(v, __fadd_rn(q.x, dv), dv, q.y, q.y, q.x, cfg.radius, false);
+          moved = fabsf(__fsub_rn(nx, q.x)) > cfg.move_eps2;
+        }
+        mm[((size_t)e * P + p) * 5 + d] = q.alive ? (moved ? 1 : 0) : 1;
+      } else if (lane < 5 * P) {
+        mm[((size_t)e * P + (lane - 4 * P)) * 5 + 4] = 1;
+      }
+    }
+    if (bm && lane < P) {
+      const PInfo& q = pi[lane];
+      const bool under = v.fuse[q.flat] > 0;
+      const bool under_b = under || v.brick[q.flat];
+      const bool ok = !under && !under_b && (int64_t)q.live < q.bombs_cap;
+      bm[((size_t)e * P + lane) * 2 + 0] = 1;
+      bm[((size_t)e * P + lane) * 2 + 1] = q.alive ? (ok ? 1 : 0) : 1;
+    }
+    __syncwarp();
+  }
+}
+
+// ------------------------------------------------------------------ astar
+
+__host__ __device__ inline size_t astar_warp_bytes(int cells) {
+  return ((size_t)cells * (4 * 4 + 1 + 2) + 15) / 16 * 16 + 64;
+}
+
+// Two multi-source path fields to their common fixed point: row sweeps
+// (left->right, right->left) then column sweeps, repeated until no value
+// changes.  Values only decrease and every value is a path sum, so any
+// sweep order ends at the reference's Jacobi fixed point.
+__device__ inline bool relax_two(volatile float* d0, volatile float* d1, const float* cost,
+                                 int h, int w, int max_iter) {
+  const int lane = lane_id();
+  const float INF = __int_as_float(0x7f800000);
+  for (int it = 0; it < max_iter; ++it) {
+    bool changed = false;
+    for (int task = lane; task < 2 * h; task += 32) {
+      volatile float* d = task < h ? d0 : d1;
+      const int r = task < h ? task : task - h;
+      for (int k = 0; k < 2 * w; ++k) {
+        const int cc = k < w ? k : 2 * w - 1 - k;
+        const int c = r * w + cc;
+        const float cst = cost[c];
+        if (cst == INF) continue;
+        float m = INF;
+        if (r > 0) m = fminf(m, d[c - w]);
+        if (r < h - 1) m = fminf(m, d[c + w]);
+        if (cc > 0) m = fminf(m, d[c - 1]);
+        if (cc < w - 1) m = fminf(m, d[c + 1]);
+        const float nd = __fadd_rn(m, cst);
+        if (nd < d[c]) {
+          d[c] = nd;
+          changed = true;
+        }
+      }
+    }
+    __syncwarp();
+    for (int task = lane; task < 2 * w; task += 32) {
+      volatile float* d = task < w ? d0 : d1;
+      const int cc = task < w ? task : task - w;
+      for (int k = 0; k < 2 * h; ++k) {
+        const int r = k < h ? k : 2 * h - 1 - k;
+        const int c = r * w + cc;
+        const float cst = cost[c];
+        if (cst == INF) continue;
+        float m = INF;
+        if (r > 0) m = fminf(m, d[c - w]);
+        if (r < h - 1) m = fminf(m, d[c + w]);
+        if (cc > 0) m = fminf(m, d[c - 1]);
+        if (cc < w - 1) m = fminf(m, d[c + 1]);
+        const float nd = __fadd_rn(m, cst);
+        if (nd < d[c]) {
+          d[c] = nd;
+          changed = true;
+        }
+      }
+    }
+    __syncwarp();
+    if (!__any_sync(QQT_FULL, changed)) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ int argmin5(const float* s) {
+  int best = 0;
+  for (int k = 1; k < 5; ++k)
+    if (s[k] < s[best]) best = k;
+  return best;
+}
+
+__global__ void __launch_bounds__(QQT_NWARP * 32)
+k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const float* noise,
+        int64_t* mode_arr, int64_t* timer_arr, int tick16, const int64_t* new_mode,
+        const int64_t* new_timer, float* vsafe_out, float* vopp_out, const int* cap_max_ptr) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int h = cfg.height, w = cfg.width, C = h * w, N = cfg.n_envs, P = cfg.n_players;
+  const int e0 = blockIdx.x * QQT_TILE_E;
+  const float INF = __int_as_float(0x7f800000);
+  Tile tile = carve_tile(smem, C);
+  load_tile(tile, st, N, e0, PL_WALL | PL_BRICK | PL_OWNER | PL_FUSE);
+  __syncthreads();
+  uint8_t* wb = smem + tile_bytes(C) + (size_t)warp_id() * astar_warp_bytes(C);
+  float* d16 = (float*)wb;
+  float* cost = d16 + C;
+  float* vs = cost + C;
+  float* vo = vs + C;
+  uint8_t* threat = (uint8_t*)(vo + C);
+  uint16_t* own = (uint16_t*)(threat + ((C + 1) & ~1));
+  const int lane = lane_id();
+  const int cap_max = *cap_max_ptr;
+  const int G = cfg.growth_blast_max;
+  const int dch = 2 * P + 1;
+
+  for (int s = warp_id(); s < QQT_TILE_E; s += QQT_NWARP) {
+    const int e = e0 + s;
+    if (e >= N) break;
+    const Env v = env_view(tile, s, h, w);
+    const __half* orow = obs + (size_t)e * cfg.obs_stride + (size_t)dch * C;
+    for (int c = lane; c < C; c += 32) {
+      const float d = __half2float(orow[c]);
+      d16[c] = d;
+      const bool blk = v.wall[c] || v.brick[c] || v.fuse[c] > 0;
+      cost[c] = blk ? INF : __fadd_rn(1.f, __fmul_rn(2.f, d));
+      vs[c] = d < 0.35f ? 0.f : INF;
+      vo[c] = INF;
+    }
+    const int nown = warp_compact(C, own, [&](int c) { return v.owner[c] == pid && v.fuse[c] > 0; });
+    for (int c = lane; c < C; c += 32) {
+      const int r = c / w, cc = c - r * w;
+      uint8_t t = 0;
+      for (int i = 0; i < nown && !t; ++i) {
+        const int b = own[i], br = b / w, bc = b - br * w;
+        if (abs(br - r) + abs(bc - cc) <= G) t = 1;
+      }
+      threat[c] = t;
+    }
+    __syncwarp();
+    if (lane == 0) {
+      for (int o = 0; o < P; ++o) {
+        if (o == pid || !st.alive[(size_t)o * N + e]) continue;
+        const int ro = min(max((int)floorf(st.pos[((size_t)o * 2) * N + e]), 0), h - 1);
+        const int co = min(max((int)floorf(st.pos[((size_t)o * 2 + 1) * N + e]), 0), w - 1);
+        vo[ro * w + co] = 0.f;
+      }
+    }
+    __syncwarp();
+    if (!relax_two(vs, vo, cost, h, w, C + 1) && lane == 0) flag_error(QQT_DEV_NOT_CONVERGED);
+    if (vsafe_out)
+      for (int c = lane; c < C; c += 32) vsafe_out[(size_t)e * C + c] = vs[c];
+    if (vopp_out)
+      for (int c = lane; c < C; c += 32) vopp_out[(size_t)e * C + c] = vo[c];
+
+    if (lane == 0) {
+      int mode = 0;
+      bool has_mode = mode_arr != nullptr;
+      if (has_mode) {
+        int64_t tm = timer_arr[e] - 1;
+        int64_t md = mode_arr[e];
+        if (tick16 && tm <= 0) {
+          md = new_mode[e];
+          tm = new_timer[e];
+        }
+        timer_arr[e] = tm;
+        mode_arr[e] = md;
+        mode = (int)md;
+      }
+      const float py = st.pos[((size_t)pid * 2) * N + e], px = st.pos[((size_t)pid * 2 + 1) * N + e];
+      const int r = min(max((int)floorf(py), 0), h - 1), c = min(max((int)floorf(px), 0), w - 1);
+      const float own_dng = d16[r * w + c];
+      const int cr[5] = {max(r - 1, 0), min(r + 1, h - 1), r, r, r};
+      const int ccs[5] = {c, c, max(c - 1, 0), min(c + 1, w - 1), c};
+      float vopp_c[5], vsafe_c[5], dng_c[5], thr_c[5], nz[5];
+      bool legal[5];
+      const uint8_t* mrow = io.mm + (size_t)e * io.mm_stride;
+      for (int k = 0; k < 5; ++k) {
+        const int q = cr[k] * w + ccs[k];
+        vopp_c[k] = vo[q];
+        vsafe_c[k] = vs[q];
+        dng_c[k] = d16[q];
+        thr_c[k] = threat[q] ? 1.f : 0.f;
+        legal[k] = mrow[k] && !(v.wall[q] || v.brick[q]);
+        nz[k] = __fmul_rn(0.05f, noise[(size_t)e * 5 + k]);
+      }
+      float app[5], esc[5], score[5];
+      bool app_ok = false;
+      for (int k = 0; k < 5; ++k) {
+        float a = __fadd_rn(__fadd_rn(__fadd_rn(vopp_c[k], __fmul_rn(2.f, dng_c[k])),
+                                      __fmul_rn(2.f, thr_c[k])), nz[k]);
+        if (dng_c[k] >= 0.5f || !legal[k]) a = INF;
+        app[k] = a;
+        app_ok |= a < INF;
+      }
+      const bool use_esc = own_dng >= 0.35f || !app_ok;
+      for (int k = 0; k < 5; ++k) {
+        float x = __fadd_rn(__fadd_rn(__fmul_rn(vsafe_c[k], 100.f), __fmul_rn(2.f, thr_c[k])), nz[k]);
+        if ((use_esc && k == 4) || !legal[k]) x = INF;
+        esc[k] = x;
+        score[k] = use_esc ? esc[k] : app[k];
+      }
+      if (has_mode && mode == 1) {
+        for (int k = 0; k < 5; ++k) {
+          float f = __fadd_rn(__fadd_rn(__fadd_rn(-fminf(vopp_c[k], 1e3f), __fmul_rn(2.f, dng_c[k])),
+                                        __fmul_rn(2.f, thr_c[k])), nz[k]);
+          if (dng_c[k] >= 0.5f || !legal[k]) f = INF;
+          score[k] = use_esc ? esc[k] : f;
+        }
+      }
+      int move = argmin5(score);
+      bool any_legal = false, finite = false;
+      float dl[5], dmv[5];
+      for (int k = 0; k < 5; ++k) {
+        any_legal |= legal[k];
+        finite |= score[k] < INF;
+        dl[k] = legal[k] ? dng_c[k] : INF;
+        dmv[k] = k < 4 ? dl[k] : INF;
+      }
+      if (!finite && any_legal) {
+        const int fm = argmin5(dmv);
+        move = dmv[fm] < INF ? fm : argmin5(dl);
+      }
+      const int64_t cap = st.blast_cap[(size_t)pid * N + e];
+      long long dr_o = 1000000000LL, dc_o = 1000000000LL;
+      for (int o = 0; o < P; ++o) {
+        if (o == pid || !st.alive[(size_t)o * N + e]) continue;
+        const int ro = min(max((int)floorf(st.pos[((size_t)o * 2) * N + e]), 0), h - 1);
+        const int co = min(max((int)floorf(st.pos[((size_t)o * 2 + 1) * N + e]), 0), w - 1);
+        dr_o = llabs((long long)(r - ro));
+        dc_o = llabs((long long)(c - co));
+      }
+      const bool aligned = (dr_o == 0 && dc_o <= cap) || (dc_o == 0 && dr_o <= cap);
+      const long long manh = min(dr_o + dc_o, 100000000LL);
+      const bool near = manh <= max((long long)cap + 1, 1LL);
+      bool chain = false;
+      for (int k = 1; k <= cap_max && !chain; ++k)
+        for (int d = 0; d < 4; ++d) {
+          const int rr = r + kDR[d] * k, c2 = c + kDC[d] * k;
+          if (rr < 0 || rr >= h || c2 < 0 || c2 >= w) continue;
+          const int f = v.fuse[rr * w + c2];
+          if (f > 0 && f <= 10) chain = true;
+        }
+      const bool can = io.bm[(size_t)e * io.bm_stride + 1] != 0;
+      bool can_escape = false;
+      for (int k = 0; k < 5; ++k) can_escape |= legal[k] && dng_c[k] < 0.35f && thr_c[k] == 0.f;
+      bool place = can && (aligned || near || chain) && own_dng < 0.2f && can_escape;
+      if (has_mode && mode == 1) place = can && (aligned || near) && own_dng < 0.2f && can_escape;
+      const bool alive = st.alive[(size_t)pid * N + e] != 0;
+      io.act[(size_t)e * io.act_stride + 0] = alive ? move : 4;
+      io.act[(size_t)e * io.act_stride + 1] = alive ? (place ? 1 : 0) : 0;
+    }
+    __syncwarp();
+  }
+}
+
+__global__ void k_cap_max(const int64_t* blast_cap, int n, int* out) {
+  int m = 0;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    m = max(m, (int)blast_cap[i]);
+  m = warp_max(m);
+  if (lane_id() == 0) atomicMax(out, m);
+}
+
+// ---------------------------------------------------------- random / greedy
+
+__device__ __forceinline__ int sample_legal(const uint8_t* mask, int k, float u) {
+  float cs[5];
+  float acc = 0.f;
+  for (int i = 0; i < k; ++i) {
+    acc = __fadd_rn(acc, mask[i] ? 1.f : 0.f);
+    cs[i] = acc;
+  }
+  const float us = __fmul_rn(u, fmaxf(cs[k - 1], 1e-6f));
+  int a = 0;
+  for (int i = 0; i < k; ++i) a += us > cs[i];
+  return a;
+}
+
+__global__ void k_random(int n, const uint8_t* alive, SeatIO io, int pid, const float* u_move,
+                         const float* u_bomb, float rate) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= n) return;
+  const bool al = alive[(size_t)pid * n + e] != 0;
+  const int move = sample_legal(io.mm + (size_t)e * io.mm_stride, 5, u_move[e]);
+  const bool bomb = u_bomb[e] < rate && io.bm[(size_t)e * io.bm_stride + 1];
+  io.act[(size_t)e * io.act_stride + 0] = al ? move : 4;
+  io.act[(size_t)e * io.act_stride + 1] = (al && bomb) ? 1 : 0;
+}
+
+__global__ void k_greedy(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid,
+                         const float* noise) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  const int N = cfg.n_envs, P = cfg.n_players, h = cfg.height, w = cfg.width, C = h * w;
+  if (e >= N) return;
+  const float INF = __int_as_float(0x7f800000);
+  const __half* drow = obs + (size_t)e * cfg.obs_stride + (size_t)(2 * P + 1) * C;
+  const int r = min(max((int)floorf(st.pos[((size_t)pid * 2) * N + e]), 0), h - 1);
+  const int c = min(max((int)floorf(st.pos[((size_t)pid * 2 + 1) * N + e]), 0), w - 1);
+  const float own = __half2float(drow[r * w + c]);
+  const int cr[5] = {max(r - 1, 0), min(r + 1, h - 1), r, r, r};
+  const int ccs[5] = {c, c, max(c - 1, 0), min(c + 1, w - 1), c};
+  float dist[5], dng[5];
+  bool blk[5];
+  for (int k = 0; k < 5; ++k) {
+    const int q = cr[k] * w + ccs[k];
+    dng[k] = __half2float(drow[q]);
+    blk[k] = st.wall[(size_t)q * N + e] || st.brick[(size_t)q * N + e];
+    dist[k] = 1e9f;
+  }
+  for (int o = 0; o < P; ++o) {
+    if (o == pid) continue;
+    const int ro = min(max((int)floorf(st.pos[((size_t)o * 2) * N + e]), 0), h - 1);
+    const int co = min(max((int)floorf(st.pos[((size_t)o * 2 + 1) * N + e]), 0), w - 1);
+    const bool al = st.alive[(size_t)o * N + e] != 0;
+    for (int k = 0; k < 5; ++k) {
+      const float d = al ? (float)max(abs(cr[k] - ro), abs(ccs[k] - co)) : 1e9f;
+      dist[k] = fminf(dist[k], d);
+    }
+  }
+  const uint8_t* mrow = io.mm + (size_t)e * io.mm_stride;
+  int best = 0, esc_d = 0;
+  float best_s = INF, esc_s = INF;
+  for (int k = 0; k < 5; ++k) {
+    const bool legal = mrow[k] && !blk[k];
+    const float nz = __fmul_rn(0.05f, noise[(size_t)e * 5 + k]);
+    const float sc = legal ? __fadd_rn(__fadd_rn(dist[k], __fmul_rn(2.f, dng[k])), nz) : INF;
+    if (sc < best_s) {
+      best_s = sc;
+      best = k;
+    }
+    const float es = legal ? dng[k] : INF;
+    if (es < esc_s) {
+      esc_s = es;
+      esc_d = k;
+    }
+  }
+  const bool use_safe = best_s < INF && dng[best] < 0.35f;
+  const int move = use_safe ? best : esc_d;
+  const bool place = io.bm[(size_t)e * io.bm_stride + 1] &&
+                     dist[4] < (float)st.blast_cap[(size_t)pid * N + e] && own < 0.2f;
+  const bool al = st.alive[(size_t)pid * N + e] != 0;
+  io.act[(size_t)e * io.act_stride + 0] = al ? move : 4;
+  io.act[(size_t)e * io.act_stride + 1] = (al && place) ? 1 : 0;
+}
+
+}  // namespace qqt
+
+using namespace qqt;
+
+extern "C" int qqt_observe(const QqtCfg* cfg, const QqtState* st, void* obs, float* danger,
+                           uint8_t* mm, uint8_t* bm, qqt_stream_t stream) {
+  int rc = check_cfg(cfg);
+  if (rc) return rc;
+  if (!st) return QQT_E_ARG;
+  const int C = cfg->height * cfg->width;
+  if (obs) {
+    const int epc = cfg->obs_fp32 ? 4 : 8;
+    if (cfg->obs_stride % epc || cfg->obs_stride < cfg->obs_channels * C) return QQT_E_ALIGN;
+    if (((uintptr_t)obs) & 15) return QQT_E_ALIGN;
+  }
+  const size_t sm = tile_bytes(C) + QQT_NWARP * observe_warp_bytes(C);
+  const int blocks = (cfg->n_envs + QQT_TILE_E - 1) / QQT_TILE_E;
+  if (cfg->obs_fp32) {
+    cudaFuncSetAttribute(k_observe<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    k_observe<true><<<blocks, QQT_NWARP * 32, sm, (cudaStream_t)stream>>>(*cfg, *st, obs, danger, mm, bm);
+  } else {
+    cudaFuncSetAttribute(k_observe<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    k_observe<false><<<blocks, QQT_NWARP * 32, sm, (cudaStream_t)stream>>>(*cfg, *st, obs, danger, mm, bm);
+  }
+  return launch_status();
+}
+
+extern "C" int qqt_legal_mask(const QqtCfg* cfg, const QqtState* st, uint8_t* mm, uint8_t* bm,
+                              qqt_stream_t stream) {
+  if (!mm || !bm) return QQT_E_ARG;
+  return qqt_observe(cfg, st, nullptr, nullptr, mm, bm, stream);
+}
+
+static int seat_io(const uint8_t* mm, int32_t mm_stride, const uint8_t* bm, int32_t bm_stride,
+                   int64_t* act, int32_t act_stride, SeatIO* io) {
+  if (!mm || !bm || !act || mm_stride < 5 || bm_stride < 2 || act_stride < 2) return QQT_E_ARG;
+  io->mm = mm;
+  io->bm = bm;
+  io->act = act;
+  io->mm_stride = mm_stride;
+  io->bm_stride = bm_stride;
+  io->act_stride = act_stride;
+  return QQT_OK;
+}
+
+extern "C" int qqt_astar_act(const QqtCfg* cfg, const QqtState* st, const void* obs,
+                             const uint8_t* mm, int32_t mm_stride, const uint8_t* bm,
+                             int32_t bm_stride, int32_t pid, const float* noise, int64_t* mode,
+                             int64_t* timer, int32_t tick16, const int64_t* new_mode,
+                             const int64_t* new_timer, int64_t* act, int32_t act_stride,
+                             float* vsafe, float* vopp, void* scratch, qqt_stream_t stream) {
+  int rc = check_cfg(cfg);
+  if (rc) return rc;
+  SeatIO io;
+  if ((rc = seat_io(mm, mm_stride, bm, bm_stride, act, act_stride, &io))) return rc;
+  if (!st || !obs || !noise || !scratch) return QQT_E_ARG;
+  if (pid < 0 || pid >= cfg->n_players || cfg->obs_fp32) return QQT_E_ARG;
+  if ((mode == nullptr) != (timer == nullptr)) return QQT_E_ARG;
+  if (mode && tick16 && (!new_mode || !new_timer)) return QQT_E_ARG;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int N = cfg->n_envs, C = cfg->height * cfg->width;
+  int* capmax = (int*)scratch;
+  cudaMemsetAsync(capmax, 0, sizeof(int), s);
+  k_cap_max<<<min((N + 255) / 256, 148), 256, 0, s>>>(st->blast_cap + (size_t)pid * N, N, capmax);
+  const size_t sm = tile_bytes(C) + QQT_NWARP * astar_warp_bytes(C);
+  cudaFuncSetAttribute(k_astar, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  k_astar<<<(N + QQT_TILE_E - 1) / QQT_TILE_E, QQT_NWARP * 32, sm, s>>>(
+      *cfg, *st, (const __half*)obs, io, pid, noise, mode, timer, tick16, new_mode, new_timer,
+      vsafe, vopp, capmax);
+  return launch_status();
+}
+
+extern "C" int qqt_random_act(const QqtCfg* cfg, const QqtState* st, const uint8_t* mm,
+                              int32_t mm_stride, const uint8_t* bm, int32_t bm_stride, int32_t pid,
+                              const float* u_move, const float* u_bomb, float bomb_rate,
+                              int64_t* act, int32_t act_stride, qqt_stream_t stream) {
+  int rc = check_cfg(cfg);
+  if (rc) return rc;
+  SeatIO io;
+  if ((rc = seat_io(mm, mm_stride, bm, bm_stride, act, act_stride, &io))) return rc;
+  if (!st || !u_move || !u_bomb || pid < 0 || pid >= cfg->n_players) return QQT_E_ARG;
+  const int N = cfg->n_envs;
+  k_random<<<(N + 127) / 128, 128, 0, (cudaStream_t)stream>>>(N, st->alive, io, pid, u_move, u_bomb,
+                                                                bomb_rate);
+  return launch_status();
+}
+
+extern "C" int qqt_greedy_act(const QqtCfg* cfg, const QqtState* st, const void* obs,
+                              const uint8_t* mm, int32_t mm_stride, const uint8_t* bm,
+                              int32_t bm_stride, int32_t pid, const float* noise, int64_t* act,
+                              int32_t act_stride, qqt_stream_t stream) {
+  int rc = check_cfg(cfg);
+  if (rc) return rc;
+  SeatIO io;
+  if ((rc = seat_io(mm, mm_stride, bm, bm_stride, act, act_stride, &io))) return rc;
+  if (!st || !obs || !noise || pid < 0 || pid >= cfg->n_players || cfg->obs_fp32)
+    return QQT_E_ARG;
+  const int N = cfg->n_envs;
+  k_greedy<<<(N + 127) / 128, 128, 0, (cudaStream_t)stream>>>(*cfg, *st, (const __half*)obs, io, pid,
+                                                                noise);
+  return launch_status();
+}
+
+extern "C" int qqt_get_error(uint32_t* code_out) {
+  unsigned v = 0;
+  if (cudaMemcpyFromSymbol(&v, qqt::g_error, sizeof(v)) != cudaSuccess) return QQT_E_LAUNCH;
+  const unsigned z = 0;
+  if (cudaMemcpyToSymbol(qqt::g_error, &z, sizeof(z)) != cudaSuccess) return QQT_E_LAUNCH;
+  if (code_out) *code_out = v;
+  return QQT_OK;
+}
+
+extern "C" const char* qqt_version(void) { return "qqt_b200 0.1 sm_100a"; }

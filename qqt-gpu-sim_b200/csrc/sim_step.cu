@@ -1,0 +1,601 @@
+// One environment tick, fused into a single kernel (replaces
+// BatchedSim.step, sim/torch_sim.py:895-1261).
+//
+// Block = tile of 32 envs staged in shared memory; warp = one env at a time.
+// Order inside an env follows the reference exactly:
+//   fuse countdown -> sequential placement -> placement bonus -> since_bomb
+//   -> AABB sliding -> chain explosion (initial + fixed rounds) -> bricks to
+//   crates -> damage / invulnerability -> clearing -> t, done -> rewards
+//   (step, hit, placement, attribute penalty, chain bonus, crate pickup and
+//   growth, danger standing, combo, terminal) -> optional device reset.
+// Lanes < P own one player each; lanes stride over cells / bombs otherwise.
+
+#include "qqt_common.cuh"
+
+namespace qqt {
+
+struct PlayerState {
+  float y, x, spd, lo_spd;
+  int alive0, hp, move, bomb, flat0, placed;
+  int32_t since;
+  int64_t bombs_cap, blast_cap, invuln, pending, combo, last_hit, lo_b, lo_z;
+};
+
+struct PShared {
+  int flat0, alive0, bomb, placed;
+  int64_t bombs_cap, blast_cap;
+};
+
+// Per-warp scratch layout (byte offsets, 16-byte aligned sections).
+struct StepLayout {
+  size_t cov, trig, list, cur, bombs, ps, total;
+};
+
+__host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
+
+__host__ __device__ inline StepLayout step_layout(int cells) {
+  StepLayout L;
+  L.cov = 0;
+  L.trig = align16(L.cov + cells);
+  L.list = align16(L.trig + cells);
+  L.cur = align16(L.list + (size_t)cells * 2);
+  L.bombs = align16(L.cur + (size_t)cells * 12);   // cur, front, spread
+  L.ps = align16(L.bombs + (size_t)cells * 2);
+  L.total = align16(L.ps + QQT_MAX_P * sizeof(PShared));
+  return L;
+}
+
+__host__ __device__ inline size_t step_warp_bytes(int cells) { return step_layout(cells).total; }
+
+enum { PHASE_FULL = 0, PHASE_PLACE = 1, PHASE_AFTER_PLACE = 2 };
+
+struct StepParams {
+  QqtCfg cfg;
+  QqtState st;
+  const int64_t* actions;
+  const float* rb_hit;
+  const float* rb_grow;
+  int* tiers;
+  QqtStepOut out;
+  QqtTemplate tmpl;
+  int has_tmpl;
+  int phase;
+  uint8_t* placed_buf;   // [P][N]
+};
+
+__device__ __forceinline__ bool placed_map_at(const PShared* ps, int P, int cell) {
+  bool v = false;
+  for (int i = 0; i < P; ++i)
+    if (ps[i].flat0 == cell) v = ps[i].placed != 0;   // later players overwrite
+  return v;
+}
+
+__global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const QqtCfg& cfg = a.cfg;
+  const QqtState& st = a.st;
+  const int h = cfg.height, w = cfg.width, C = h * w, N = cfg.n_envs, P = cfg.n_players;
+  const int e0 = blockIdx.x * QQT_TILE_E;
+  const int lane = lane_id();
+  Tile tile = carve_tile(smem, C);
+  load_tile(tile, st, N, e0, PL_ALL);
+  __syncthreads();
+  const StepLayout L = step_layout(C);
+  uint8_t* wb = smem + tile_bytes(C) + (size_t)warp_id() * L.total;
+  uint8_t* cov = wb + L.cov;
+  uint8_t* trig = wb + L.trig;
+  uint16_t* list = (uint16_t*)(wb + L.list);
+  DangerScratch ds;
+  ds.cur = (float*)(wb + L.cur);
+  ds.front = ds.cur + C;
+  ds.spread = ds.front + C;
+  ds.bombs = (uint16_t*)(wb + L.bombs);
+  PShared* ps = (PShared*)(wb + L.ps);
+  const int tiers = a.phase == PHASE_PLACE ? 0 : *a.tiers;
+  const float INF = __int_as_float(0x7f800000);
+
+  for (int s = warp_id(); s < QQT_TILE_E; s += QQT_NWARP) {
+    const int e = e0 + s;
+    if (e >= N) break;
+    const Env v = env_view(tile, s, h, w);
+    PlayerState me;
+    const int p = lane;
+    if (p < P) {
+      const size_t i = (size_t)p * N + e;
+      me.y = st.pos[((size_t)p * 2) * N + e];
+      me.x = st.pos[((size_t)p * 2 + 1) * N + e];
+      me.spd = st.spd_g[i];
+      me.lo_spd = st.lo_spd[i];
+      me.alive0 = st.alive[i] != 0;
+      me.hp = st.hp[i];
+      me.since = st.since_bomb[i];
+      me.bombs_cap = st.bombs_cap[i];
+      me.blast_cap = st.blast_cap[i];
+      me.invuln = st.invuln[i];
+      me.pending = st.pending_lost[i];
+      me.combo = st.combo[i];
+      me.last_hit = st.last_hit[i];
+      me.lo_b = st.lo_bombs[i];
+      me.lo_z = st.lo_blast[i];
+      const int64_t mv = a.actions[((size_t)e * P + p) * 2];
+      const int64_t bo = a.actions[((size_t)e * P + p) * 2 + 1];
+      me.move = (int)max(min(mv, (int64_t)1 << 20), -((int64_t)1 << 20));
+      me.bomb = bo == 1 ? 1 : 0;
+      me.flat0 = center_cell(me.y, me.x, h, w);
+      me.placed = 0;
+    }
+
+    // ---- 1-2. countdown and sequential placement
+    if (a.phase != PHASE_AFTER_PLACE) {
+      for (int c = lane; c < C; c += 32) {
+        const int16_t f = v.fuse[c];
+        if (f > 0) v.fuse[c] = f - 1;
+      }
+      __syncwarp();
+      int cnt[QQT_MAX_P] = {0, 0, 0, 0};
+      for (int c = lane; c < C; c += 32) {
+        const int o = v.owner[c];
+        if (v.fuse[c] > 0 && o >= 0 && o < P) cnt[o]++;
+      }
+      int live[QQT_MAX_P];
+#pragma unroll
+      for (int q = 0; q < QQT_MAX_P; ++q) live[q] = warp_sum(cnt[q]);
+      if (p < P) {
+        ps[p].flat0 = me.flat0;
+        ps[p].alive0 = me.alive0;
+        ps[p].bomb = me.bomb;
+        ps[p].bombs_cap = me.bombs_cap;
+        ps[p].blast_cap = me.blast_cap;
+      }
+      __syncwarp();
+      if (lane == 0) {
+        for (int q = 0; q < P; ++q) {
+          const int idx = ps[q].flat0;
+          const bool ok = ps[q].alive0 && ps[q].bomb && v.fuse[idx] <= 0 && !v.brick[idx] &&
+                          (int64_t)live[q] < ps[q].bombs_cap;
+          ps[q].placed = ok;
+          if (ok) {
+            v.fuse[idx] = (int16_t)cfg.fuse;
+            v.owner[idx] = (int8_t)q;
+            v.blast[idx] = (int16_t)ps[q].blast_cap;
+          }
+        }
+      }
+      __syncwarp();
+      if (p < P) me.placed = ps[p].placed;
+      if (a.phase == PHASE_PLACE) {
+        if (p < P) a.placed_buf[(size_t)p * N + e] = (uint8_t)me.placed;
+        int mb = cfg.blast;
+        for (int c = lane; c < C; c += 32) mb = max(mb, (int)v.blast[c]);
+        mb = warp_max(mb);
+        if (lane == 0) atomicMax(a.tiers, mb);
+        continue;
+      }
+    } else {
+      if (p < P) {
+        me.placed = a.placed_buf[(size_t)p * N + e];
+        ps[p].flat0 = me.flat0;
+        ps[p].alive0 = me.alive0;
+        ps[p].bomb = me.bomb;
+        ps[p].bombs_cap = me.bombs_cap;
+        ps[p].blast_cap = me.blast_cap;
+        ps[p].placed = me.placed;
+      }
+      __syncwarp();
+    }
+    const float a0f = (p < P && me.alive0) ? 1.f : 0.f;
+
+    // ---- 3. placement bonus (sim/torch_sim.py:1263-1355)
+    float bonus = 0.f;
+    if (p < P) {
+      float cover = 0.f, chain = 0.f, dist = 0.f;
+      if (me.placed) {
+        const int s0 = me.flat0;
+        const int b = blast_of(v, s0, cfg.blast);
+        const int r0 = s0 / w, c0 = s0 - r0 * w;
+        for (int d = -1; d < 4; ++d) {
+          int r = r0, cc = c0;
+          for (int k = (d < 0 ? 0 : 1); k <= (d < 0 ? 0 : b); ++k) {
+            if (d >= 0) {
+              r += kDR[d];
+              cc += kDC[d];
+              if (r < 0 || r >= h || cc < 0 || cc >= w) break;
+            }
+            const int q = r * w + cc;
+            if (d >= 0 && v.wall[q]) break;
+            for (int o = 0; o < P; ++o)
+              if (o != p && ps[o].flat0 == q && ps[o].alive0) cover = __fadd_rn(cover, 1.f);
+            const int fq = v.fuse[q];
+            if (fq > 0 && v.owner[q] >= 0 && !placed_map_at(ps, P, q)) {
+              const float frac = fminf(fmaxf(__fdiv_rn((float)fq, cfg.fuse_f), 0.f), 1.f);
+              chain = __fadd_rn(chain, __fadd_rn(cfg.chain_time_factor,
+                                                 __fmul_rn(cfg.chain_time_rest, __fsub_rn(1.f, frac))));
+            }
+            if (d >= 0 && (fq > 0 || v.brick[q])) break;
+          }
+        }
+        if (cfg.place_dist_reward != 0.f && me.since >= cfg.place_dist_cooldown) {
+          const float ry = (float)(s0 / w), rx = (float)(s0 % w);
+          for (int o = 0; o < P; ++o) {
+            if (o == p || !ps[o].alive0) continue;
+            const int fo = ps[o].flat0;
+            // opponent under the predicted flame earns cover, not distance
+            bool under = fo == s0;
+            const int orow = fo / w, ocol = fo % w;
+            if (!under && (orow == r0 || ocol == c0)) {
+              const int d = orow == r0 ? (ocol > c0 ? 3 : 2) : (orow > r0 ? 1 : 0);
+              const int dist_cells = abs(orow - r0) + abs(ocol - c0);
+              int r = r0, cc = c0;
+              for (int k = 1; k <= b && k <= dist_cells; ++k) {
+                r += kDR[d];
+                cc += kDC[d];
+                const int q = r * w + cc;
+                if (v.wall[q]) break;
+                if (k == dist_cells) under = true;
+                if (v.fuse[q] > 0 || v.brick[q]) break;
+              }
+            }
+            const float dy = __fsub_rn(ry, (float)orow), dx = __fsub_rn(rx, (float)ocol);
+            const float dd = sqrtf(__fadd_rn(__fmul_rn(dy, dy), __fmul_rn(dx, dx)));
+            if (!under && dd < cfg.place_dist_radius) {
+              const float gain = fmaxf(__fsub_rn(1.f, __fdiv_rn(dd, cfg.place_dist_radius)), 0.f);
+              dist = __fadd_rn(dist, gain);
+            }
+          }
+        }
+      }
+      bonus = __fmul_rn(__fadd_rn(__fadd_rn(__fmul_rn(cfg.place_cover_reward, cover),
+                                            __fmul_rn(cfg.place_dist_reward, dist)),
+                                  __fmul_rn(cfg.place_chain_reward, chain)),
+                        a0f);
+      // ---- 4. passivity counter
+      me.since = me.placed ? 0 : me.since + 1;
+      // ---- 5. movement (sim/move.py:234-279)
+      const int mv = min(max(me.move, 0), 4);
+      float ty = 0.f, tx = 0.f;
+      if (mv == 0) ty = -cfg.step_len;
+      if (mv == 1) ty = cfg.step_len;
+      if (mv == 2) tx = -cfg.step_len;
+      if (mv == 3) tx = cfg.step_len;
+      const bool moving = me.alive0 && me.move != 4;
+      const float dy = moving ? __fmul_rn(ty, me.spd) : 0.f;
+      const float dx = moving ? __fmul_rn(tx, me.spd) : 0.f;
+      const float ny = resolve_axis(v, __fadd_rn(me.y, dy), dy, me.x, me.y, me.x, cfg.radius, true);
+      const float nx = resolve_axis(v, __fadd_rn(me.x, dx), dx, me.y, me.y, me.x, cfg.radius, false);
+      const float oy = dy != 0.f ? ny : me.y;
+      const float ox = dx != 0.f ? nx : me.x;
+      me.y = fminf(fmaxf(oy, cfg.radius), cfg.h_minus_rad);
+      me.x = fminf(fmaxf(ox, cfg.radius), cfg.w_minus_rad);
+    }
+
+    // ---- 6. chain explosion (sim/blast.py:101-155)
+    for (int c = lane; c < C; c += 32) {
+      cov[c] = 0;
+      trig[c] = (v.fuse[c] == 0 && v.owner[c] >= 0) ? 1 : 0;
+    }
+    __syncwarp();
+    {
+      int ns = warp_compact(C, list, [&](int c) { return trig[c] != 0; });
+      for (int i = lane; i < ns; i += 32) {
+        const int c = list[i];
+        emit_flame(v, c, blast_of(v, c, cfg.blast), tiers, cov);
+      }
+      __syncwarp();
+      for (int r = 0; r < cfg.resolve_rounds; ++r) {
+        ns = warp_compact(C, list, [&](int c) { return v.fuse[c] > 0 && cov[c] && !trig[c]; });
+        if (ns == 0) break;
+        for (int i = lane; i < ns; i += 32) trig[list[i]] = 1;
+        __syncwarp();
+        for (int i = lane; i < ns; i += 32) {
+          const int c = list[i];
+          emit_flame(v, c, blast_of(v, c, cfg.blast), tiers, cov);
+        }
+        __syncwarp();
+      }
+    }
+
+    // ---- 7. chain bonus (off by default) needs owners before clearing
+    float chain_bonus = 0.f;
+    if (cfg.chain_blast_bonus != 0.f) {
+      int fired[QQT_MAX_P] = {0, 0, 0, 0}, cross[QQT_MAX_P] = {0, 0, 0, 0};
+      for (int c = lane; c < C; c += 32) {
+        if (!trig[c]) continue;
+        const int o = v.owner[c];
+        const bool nat = v.fuse[c] == 0;
+        for (int q = 0; q < P; ++q) {
+          if (nat && o == q) fired[q] = 1;
+          if (!nat && o != q) cross[q]++;
+        }
+      }
+      for (int q = 0; q < QQT_MAX_P; ++q) {
+        const int f = warp_max(fired[q]);
+        const int x = warp_sum(cross[q]);
+        if (q == p) chain_bonus = __fmul_rn(cfg.chain_blast_bonus, (float)(x * f));
+      }
+    }
+
+    // ---- 8. bricks burnt: crates on corridor maps
+    for (int c = lane; c < C; c += 32) {
+      if (cov[c]) {
+        if (cfg.corridor && v.brick[c]) v.crate[c] = 1;
+        v.brick[c] = 0;
+      }
+    }
+
+    // ---- 9. damage and invulnerability
+    int flat1 = 0, hp_new = 0, alive = 0, died = 0;
+    if (p < P) {
+      flat1 = center_cell(me.y, me.x, h, w);
+      const bool hit = me.alive0 && cov[flat1];
+      const bool hit_eff = hit && me.invuln <= 0;
+      hp_new = max(me.hp - (hit_eff ? 1 : 0), 0);
+      died = hit_eff && hp_new == 0;
+      alive = me.alive0 && !died;
+      me.invuln = me.invuln - 1 > 0 ? me.invuln - 1 : 0;
+      if (hit_eff) me.invuln = cfg.invuln_ticks;
+    }
+    __syncwarp();
+    // ---- 10. clear exploded bombs
+    for (int c = lane; c < C; c += 32) {
+      if (trig[c]) {
+        v.fuse[c] = 0;
+        v.owner[c] = -1;
+        v.blast[c] = 0;
+      }
+    }
+    // ---- 11. t and done
+    const int64_t t1 = st.t[e] + 1;
+    const unsigned amask = __ballot_sync(QQT_FULL, p < P && alive);
+    const int n_alive = __popc(amask);
+    const bool done = n_alive <= 1 || t1 >= cfg.max_steps;
+
+    // ---- 12. rewards
+    const float dmg = (p < P) ? (float)max(me.hp - hp_new, 0) : 0.f;
+    float tot_dmg = 0.f, tot_hp = 0.f;
+    for (int q = 0; q < P; ++q) {
+      tot_dmg = __fadd_rn(tot_dmg, __shfl_sync(QQT_FULL, dmg, q));
+      tot_hp = __fadd_rn(tot_hp, __shfl_sync(QQT_FULL, (float)hp_new, q));
+    }
+    const float dealt = __fsub_rn(tot_dmg, dmg);
+    const float coef = cfg.explore_coef;
+    float reward = 0.f;
+    int stood = 0;
+    if (p < P) {
+      reward = __fadd_rn(__fsub_rn(__fadd_rn(__fmul_rn(-cfg.step_penalty, a0f),
+                                             __fmul_rn(cfg.hit_reward, dealt)),
+                                   __fmul_rn(cfg.hit_reward, dmg)),
+                         __fmul_rn(__fmul_rn(coef, bonus), a0f));
+      if (cfg.hit_attr_penalty > 0) {
+        const bool hit_any = dmg > 0.f && me.alive0;
+        const int64_t pen = cfg.hit_attr_penalty;
+        const int64_t nb = max(me.bombs_cap - pen, me.lo_b);
+        const int64_t nz = max(me.blast_cap - pen, me.lo_z);
+        const float nsp = fmaxf(__fsub_rn(me.spd, cfg.pen_speed), me.lo_spd);
+        const float lostf = __fadd_rn((float)((me.bombs_cap - nb) + (me.blast_cap - nz)),
+                                      rintf(__fdiv_rn(__fsub_rn(me.spd, nsp), cfg.growth_speed_step)));
+        if (hit_any) {
+          me.bombs_cap = nb;
+          me.blast_cap = nz;
+          me.spd = nsp;
+          me.pending += (int64_t)lostf;
+        }
+      }
+      reward = __fadd_rn(reward, __fmul_rn(__fmul_rn(coef, chain_bonus), a0f));
+      if (cfg.corridor) {
+        stood = v.crate[flat1] != 0;
+        reward = __fadd_rn(reward, __fmul_rn(__fmul_rn(cfg.brick_reward, stood ? 1.f : 0.f), a0f));
+        const bool rec = v.recycle[flat1] != 0;
+        const float prob = rec ? cfg.recycle_crate_prob : st.crate_prob[e];
+        const size_t ri = (size_t)e * P + p;
+        const bool hits = stood && a.rb_hit[ri] < prob && me.alive0;
+        int attr = (int)floorf(__fmul_rn(a.rb_grow[ri], 3.f));
+        if (cfg.crate_speed_only && st.hazard[e]) attr = 2;
+        const int64_t add_b = (hits && attr == 0) ? 1 : 0;
+        const int64_t add_z = (hits && attr == 1) ? 1 : 0;
+        const float add_s = (hits && attr == 2) ? 1.f : 0.f;
+        me.bombs_cap = min(me.bombs_cap + add_b, (int64_t)cfg.growth_bombs_max);
+        me.blast_cap = min(me.blast_cap + add_z, (int64_t)cfg.growth_blast_max);
+        me.spd = fminf(__fadd_rn(me.spd, __fmul_rn(add_s, cfg.growth_speed_step)), cfg.growth_speed_max);
+      }
+    }
+    __syncwarp();
+    if (cfg.corridor && p < P) {
+      v.crate[flat1] = 0;
+      v.recycle[flat1] = 0;
+    }
+    __syncwarp();
+    // danger standing penalty on the post-step state (sim/torch_sim.py:1163-1182)
+    {
+      int max_b = 0;
+      danger_stage_a(v, ds, cfg.fuse_f, cfg.blast, cfg.danger_rounds, &max_b);
+      if (p < P) {
+        const float standing = danger_at(v, ds, flat1, cfg.blast, max_b);
+        reward = __fsub_rn(reward, __fmul_rn(__fmul_rn(cfg.danger_penalty, standing), a0f));
+      }
+    }
+    const bool death_done = done && n_alive == 1;
+    const bool all_alive = done && n_alive == P;
+    int winner = 0;
+    if (p < P) {
+      if (cfg.combo_on) {
+        const int64_t c = me.combo;
+        int64_t gap = t1 - me.last_hit;
+        if (gap < 0) gap = 0;
+        const float factor = powf(cfg.combo_gap_factor, (float)gap);
+        const int64_t inc = dealt > 0.f ? 1 : 0;
+        const int64_t now = (c + inc) * inc;
+        const float pts = __fmul_rn(__fmul_rn(__fmul_rn((float)now, cfg.combo_reward), factor),
+                                    fminf(dealt, 1.f));
+        reward = __fadd_rn(reward, __fmul_rn(pts, a0f));
+        if (inc) {
+          me.combo = now;
+          me.last_hit = t1;
+        }
+        if (dmg > 0.f) me.combo = 0;
+      }
+      winner = death_done && alive && n_alive == 1;
+      const int loser = death_done && !alive && n_alive == 1;
+      const float hpf = (float)hp_new;
+      const float diff = __fsub_rn(hpf, __fdiv_rn(__fsub_rn(tot_hp, hpf), (float)(P - 1)));
+      const float aa = all_alive ? 1.f : 0.f;
+      if (!cfg.win_hp_scaled) {
+        reward = __fadd_rn(reward, __fmul_rn(cfg.win_bonus,
+                                             __fsub_rn(winner ? 1.f : 0.f, loser ? 1.f : 0.f)));
+        if (cfg.timeout_draw)
+          reward = __fadd_rn(reward, __fmul_rn(__fmul_rn(__fmul_rn(cfg.win_bonus_per_hp, diff), aa), coef));
+      } else {
+        const float base = __fmul_rn(cfg.win_bonus_per_hp, diff);
+        const float scale = cfg.timeout_draw ? coef : 1.f;
+        reward = __fadd_rn(reward, __fadd_rn(__fmul_rn(base, death_done ? 1.f : 0.f),
+                                             __fmul_rn(__fmul_rn(base, aa), scale)));
+      }
+    }
+
+    // ---- outputs
+    if (p < P) {
+      const size_t ri = (size_t)e * P + p;
+      if (a.out.reward) a.out.reward[ri] = reward;
+      if (a.out.died) a.out.died[ri] = (uint8_t)died;
+      if (a.out.winner) a.out.winner[ri] = (uint8_t)winner;
+    }
+    if (lane == 0) {
+      if (a.out.done) a.out.done[e] = done;
+      if (a.out.n_alive) a.out.n_alive[e] = n_alive;
+      if (a.out.reset_mask) a.out.reset_mask[e] = (done && a.has_tmpl) ? 1 : 0;
+    }
+    if (a.out.covered || a.out.triggered) {
+      for (int c = lane; c < C; c += 32) {
+        if (a.out.covered) a.out.covered[(size_t)c * N + e] = cov[c];
+        if (a.out.triggered) a.out.triggered[(size_t)c * N + e] = trig[c];
+      }
+    }
+
+    // ---- device reset to the env's template (no host round trip)
+    int64_t t_out = t1;
+    if (done && a.has_tmpl) {
+      const QqtTemplate& tp = a.tmpl;
+      for (int c = lane; c < C; c += 32) {
+        const size_t g = (size_t)c * N + e;
+        v.wall[c] = tp.wall[g];
+        v.brick[c] = tp.brick[g];
+        v.crate[c] = tp.crate ? tp.crate[g] : 0;
+        v.recycle[c] = 0;
+        v.fuse[c] = 0;
+        v.owner[c] = -1;
+        v.blast[c] = 0;
+      }
+      const int64_t epi = tp.episode[e];
+      const bool swap = tp.swap_spawns &&
+                        hash_uniform(tp.seed ^ ((uint64_t)e << 32) ^ (uint64_t)epi) < 0.5f;
+      if (p < P) {
+        const int src = (swap && p < 2) ? 1 - p : p;
+        const size_t i = (size_t)p * N + e;
+        me.y = tp.spawn[((size_t)src * 2) * N + e];
+        me.x = tp.spawn[((size_t)src * 2 + 1) * N + e];
+        alive = 1;
+        hp_new = cfg.max_hp;
+        me.since = tp.since_bomb0;
+        me.invuln = 0;
+        me.pending = 0;
+        me.combo = 0;
+        me.last_hit = -1000000000LL;
+        me.bombs_cap = tp.bombs_cap[i];
+        me.blast_cap = tp.blast_cap[i];
+        me.spd = tp.spd[i];
+        me.lo_b = me.bombs_cap;
+        me.lo_z = me.blast_cap;
+        me.lo_spd = me.spd;
+      }
+      if (lane == 0) {
+        tp.episode[e] = epi + 1;
+        st.crate_prob[e] = tp.crate_prob[e];
+        st.hazard[e] = 0;
+      }
+      t_out = 0;
+    }
+    if (p < P) {
+      const size_t i = (size_t)p * N + e;
+      st.pos[((size_t)p * 2) * N + e] = me.y;
+      st.pos[((size_t)p * 2 + 1) * N + e] = me.x;
+      st.alive[i] = (uint8_t)alive;
+      st.hp[i] = (uint8_t)hp_new;
+      st.since_bomb[i] = me.since;
+      st.bombs_cap[i] = me.bombs_cap;
+      st.blast_cap[i] = me.blast_cap;
+      st.spd_g[i] = me.spd;
+      st.invuln[i] = me.invuln;
+      st.pending_lost[i] = me.pending;
+      st.combo[i] = me.combo;
+      st.last_hit[i] = me.last_hit;
+      if (done && a.has_tmpl) {
+        st.lo_bombs[i] = me.lo_b;
+        st.lo_blast[i] = me.lo_z;
+        st.lo_spd[i] = me.lo_spd;
+      }
+    }
+    if (lane == 0) st.t[e] = t_out;
+    __syncwarp();
+  }
+  __syncthreads();
+  const unsigned planes = a.phase == PHASE_PLACE ? (PL_FUSE | PL_OWNER | PL_BLAST)
+                                                  : (a.has_tmpl ? PL_ALL : (PL_ALL & ~PL_WALL));
+  store_tile(tile, st, N, e0, planes);
+}
+
+}  // namespace qqt
+
+using namespace qqt;
+
+extern "C" uint64_t qqt_step_scratch_bytes(const QqtCfg* cfg) {
+  if (!cfg) return 0;
+  return ((uint64_t)cfg->n_players * cfg->n_envs + 255) / 256 * 256;
+}
+
+extern "C" int qqt_step(const QqtCfg* cfg, const QqtState* st, const int64_t* actions,
+                        const float* rb_hit, const float* rb_grow, int32_t* tiers,
+                        int32_t first_step, const QqtStepOut* out, const QqtTemplate* tmpl,
+                        void* scratch, qqt_stream_t stream) {
+  int rc = check_cfg(cfg);
+  if (rc) return rc;
+  if (!st || !actions || !tiers || !scratch) return QQT_E_ARG;
+  if (cfg->corridor && (!rb_hit || !rb_grow)) return QQT_E_ARG;
+  if (tmpl && (!tmpl->wall || !tmpl->brick || !tmpl->spawn || !tmpl->bombs_cap ||
+               !tmpl->blast_cap || !tmpl->spd || !tmpl->crate_prob || !tmpl->episode))
+    return QQT_E_ARG;
+  StepParams p;
+  p.cfg = *cfg;
+  p.st = *st;
+  p.actions = actions;
+  p.rb_hit = rb_hit;
+  p.rb_grow = rb_grow;
+  p.tiers = tiers;
+  if (out) {
+    p.out = *out;
+  } else {
+    memset(&p.out, 0, sizeof(p.out));
+  }
+  if (tmpl) {
+    p.tmpl = *tmpl;
+    p.has_tmpl = 1;
+  } else {
+    memset(&p.tmpl, 0, sizeof(p.tmpl));
+    p.has_tmpl = 0;
+  }
+  p.placed_buf = (uint8_t*)scratch;
+  const int C = cfg->height * cfg->width;
+  const size_t sm = tile_bytes(C) + QQT_NWARP * step_warp_bytes(C);
+  cudaFuncSetAttribute(k_step, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  const int blocks = (cfg->n_envs + QQT_TILE_E - 1) / QQT_TILE_E;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (first_step) {
+    cudaMemsetAsync(tiers, 0xff, sizeof(int32_t), s);   // -1
+    p.phase = PHASE_PLACE;
+    k_step<<<blocks, QQT_NWARP * 32, sm, s>>>(p);
+    p.phase = PHASE_AFTER_PLACE;
+    k_step<<<blocks, QQT_NWARP * 32, sm, s>>>(p);
+  } else {
+    p.phase = PHASE_FULL;
+    k_step<<<blocks, QQT_NWARP * 32, sm, s>>>(p);
+  }
+  return launch_status();
+}

@@ -1,0 +1,594 @@
+"""B200Sim: the reference `BatchedSim` API on the B200 kernels.
+
+State lives on the device in structure-of-arrays layout with the env index
+innermost: planes are [H*W][N], per-player arrays [P][N], positions
+[P][2][N].  The public attributes (`sim.fuse`, `sim.pos`, ...) are strided
+torch views with the reference's shapes ((N,H,W), (N,P), (N,P,2)), so bots,
+tests and callers that index or poke them work unchanged and without copies;
+assigning to an attribute copies into the device buffer.
+
+Per tick the engine runs three library calls (observe, one step, plus the
+policy and bot calls made by the caller); nothing in `observe`, `legal_mask`
+or a template-reset `step` synchronises the host, so a tick can be captured
+into a CUDA graph.  Reference call sites: sim/torch_sim.py:53-1466.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _capi as capi
+from . import mapgen
+from .config import SimConfig
+
+_PLANES = {"wall": torch.bool, "brick": torch.bool, "crate": torch.bool,
+           "_recycle_crate": torch.bool, "fuse": torch.int16, "owner": torch.int8,
+           "bomb_blast": torch.int16}
+_PLAYER = {"alive": torch.bool, "hp": torch.uint8, "since_bomb": torch.int32,
+           "bombs_cap": torch.int64, "blast_cap": torch.int64, "spd_g": torch.float32,
+           "invuln": torch.int64, "_pending_lost": torch.int64, "_combo": torch.int64,
+           "_last_hit": torch.int64, "_lo_bombs": torch.int64, "_lo_blast": torch.int64,
+           "_lo_spd": torch.float32}
+_ENV = {"t": torch.int64, "crate_prob": torch.float32, "_hazard": torch.bool,
+        "_is_open": torch.bool, "_map_kind": torch.int64, "_opp_boost": torch.int64}
+# ctypes QqtState field -> attribute name
+_CSTATE = {"wall": "wall", "brick": "brick", "crate": "crate", "recycle": "_recycle_crate",
+           "fuse": "fuse", "owner": "owner", "bomb_blast": "bomb_blast", "pos": "pos",
+           "alive": "alive", "hp": "hp", "since_bomb": "since_bomb", "t": "t",
+           "bombs_cap": "bombs_cap", "blast_cap": "blast_cap", "spd_g": "spd_g",
+           "invuln": "invuln", "pending_lost": "_pending_lost", "combo": "_combo",
+           "last_hit": "_last_hit", "lo_bombs": "_lo_bombs", "lo_blast": "_lo_blast",
+           "lo_spd": "_lo_spd", "crate_prob": "crate_prob", "hazard": "_hazard"}
+
+
+def _round_up(x: int, m: int) -> int:
+    return (x + m - 1) // m * m
+
+
+def make_ccfg(cfg: SimConfig, n_envs: int, explore_coef: float = 1.0,
+              obs_stride: int | None = None) -> capi.QqtCfg:
+    """Scalar config for the kernels; float fields are the float32 values the
+    reference multiplies by (double products rounded once)."""
+    c = capi.QqtCfg()
+    hw = cfg.height * cfg.width
+    fp32 = not cfg.obs_fp16
+    stride = obs_stride or _round_up(cfg.n_channels * hw, 4 if fp32 else 8)
+    ints = dict(n_envs=n_envs, height=cfg.height, width=cfg.width, n_players=cfg.n_players,
+                fuse=cfg.fuse, blast=cfg.blast, max_steps=cfg.max_steps,
+                invuln_ticks=cfg.invuln_ticks, max_hp=cfg.max_hp,
+                resolve_rounds=min(cfg.max_chain - 1, cfg.chain_cap_rounds),
+                danger_rounds=(min(cfg.max_chain, cfg.chain_cap_rounds)
+                               if cfg.max_chain > 1 else 0),
+                corridor=int(cfg.map_mode == "corridor"),
+                hit_attr_penalty=cfg.hit_attr_penalty, growth_bombs_max=cfg.growth_bombs_max,
+                growth_blast_max=cfg.growth_blast_max,
+                place_dist_cooldown=cfg.place_dist_cooldown,
+                crate_speed_only=int(cfg.crate_speed_only), timeout_draw=int(cfg.timeout_draw),
+                win_hp_scaled=int(cfg.win_hp_scaled), combo_on=int(cfg.combo_reward > 0),
+                obs_extra=int(cfg.obs_extra_enabled), obs_channels=cfg.n_channels,
+                obs_stride=stride, obs_fp32=int(fp32))
+    floats = dict(radius=cfg.radius, step_len=cfg.step_len, move_eps2=2e-4,
+                  step_penalty=cfg.step_penalty, hit_reward=cfg.hit_reward,
+                  brick_reward=cfg.brick_reward,
+                  danger_penalty=explore_coef * cfg.danger_penalty,
+                  explore_coef=explore_coef, place_cover_reward=cfg.place_cover_reward,
+                  place_chain_reward=cfg.place_chain_reward,
+                  place_dist_reward=cfg.place_dist_reward,
+                  place_dist_radius=cfg.place_dist_radius,
+                  chain_time_factor=cfg.chain_time_factor,
+                  chain_time_rest=1.0 - cfg.chain_time_factor,
+                  growth_speed_step=cfg.growth_speed_step,
+                  growth_speed_max=cfg.growth_speed_max,
+                  pen_speed=cfg.hit_attr_penalty * cfg.growth_speed_step,
+                  recycle_crate_prob=cfg.recycle_crate_prob, combo_reward=cfg.combo_reward,
+                  combo_gap_factor=cfg.combo_gap_factor, win_bonus=cfg.win_bonus,
+                  win_bonus_per_hp=cfg.win_bonus / cfg.max_hp,
+                  chain_blast_bonus=(cfg.chain_blast_bonus if cfg.max_chain > 1 else 0.0),
+                  obs_growth_bombs_max=float(cfg.growth_bombs_max), fuse_f=float(cfg.fuse),
+                  max_steps_f=float(cfg.max_steps), h_minus_rad=cfg.height - cfg.radius,
+                  w_minus_rad=cfg.width - cfg.radius)
+    for k, v in ints.items():
+        setattr(c, k, int(v))
+    for k, v in floats.items():
+        setattr(c, k, float(v))
+    return c
+
+
+class B200Sim:
+    """Drop-in for `sim.torch_sim.BatchedSim` backed by libqqt_b200.so."""
+
+    def __init__(self, cfg: SimConfig, num_envs: int, device: str | torch.device = "cuda",
+                 seed: int = 0, template: dict | None = None) -> None:
+        self.cfg = cfg
+        self.num_envs = n = int(num_envs)
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise RuntimeError("B200Sim runs on a CUDA device only (no CPU fallback)")
+        capi.lib()
+        self.gen = torch.Generator(device="cpu").manual_seed(seed)
+        h, w, p = cfg.height, cfg.width, cfg.n_players
+        hw = h * w
+        d = self.device
+        self._buf = {}
+        for k, dt in _PLANES.items():
+            self._buf[k] = torch.zeros((hw, n), dtype=dt, device=d)
+        self._buf["owner"].fill_(-1)
+        for k, dt in _PLAYER.items():
+            self._buf[k] = torch.zeros((p, n), dtype=dt, device=d)
+        self._buf["pos"] = torch.zeros((p, 2, n), dtype=torch.float32, device=d)
+        for k, dt in _ENV.items():
+            self._buf[k] = torch.zeros((n,), dtype=dt, device=d)
+        self._buf["alive"].fill_(True)
+        self._buf["hp"].fill_(cfg.max_hp)
+        self._buf["_last_hit"].fill_(-10 ** 9)
+        self._buf["crate_prob"].fill_(cfg.growth_crate_prob)
+        self._buf["_lo_bombs"].fill_(cfg.growth_bombs_start)
+        self._buf["_lo_blast"].fill_(cfg.growth_blast_start)
+        self._buf["_lo_spd"].fill_(cfg.growth_speed_start)
+        self._buf["spd_g"].fill_(1.0)
+        self._explore_coef = 1.0
+        self.speed_mult = None
+        self._rand_buf: torch.Tensor | None = None
+        self._ccfg = make_ccfg(cfg, n, 1.0)
+        self.obs_stride = int(self._ccfg.obs_stride)
+        obs_dt = torch.float16 if cfg.obs_fp16 else torch.float32
+        self._obs = torch.zeros((n, self.obs_stride), dtype=obs_dt, device=d)
+        self._danger = torch.zeros((n, hw), dtype=torch.float32, device=d)
+        self._mm = torch.ones((n, p, 5), dtype=torch.bool, device=d)
+        self._bm = torch.ones((n, p, 2), dtype=torch.bool, device=d)
+        self._reward = torch.zeros((n, p), dtype=torch.float32, device=d)
+        self._done = torch.zeros((n,), dtype=torch.bool, device=d)
+        self._died = torch.zeros((n, p), dtype=torch.bool, device=d)
+        self._winner = torch.zeros((n, p), dtype=torch.bool, device=d)
+        self._n_alive = torch.zeros((n,), dtype=torch.int64, device=d)
+        self._covered = torch.zeros((hw, n), dtype=torch.bool, device=d)
+        self._triggered = torch.zeros((hw, n), dtype=torch.bool, device=d)
+        self._reset_mask = torch.zeros((n,), dtype=torch.bool, device=d)
+        self._tiers = torch.full((1,), -1, dtype=torch.int32, device=d)
+        self._first_step = True
+        nb = int(capi.lib().qqt_step_scratch_bytes(ctypes.byref(self._ccfg)))
+        self._step_scratch = torch.zeros((max(nb, 256),), dtype=torch.uint8, device=d)
+        self._tmpl = None
+        self._cstate = self._make_cstate()
+        self._cout = self._make_cout()
+        if template is not None:
+            self.set_template(template, apply=True)
+        else:
+            self.reset_all()
+
+    # ------------------------------------------------------------ views
+    def _view(self, key):
+        b = self._buf[key]
+        n, cfg = self.num_envs, self.cfg
+        if key in _PLANES:
+            return b.t().view(n, cfg.height, cfg.width)
+        if key in _PLAYER:
+            return b.t()
+        if key == "pos":
+            return b.permute(2, 0, 1)
+        return b
+
+    def _make_cstate(self):
+        s = capi.QqtState()
+        for f, key in _CSTATE.items():
+            setattr(s, f, self._buf[key].data_ptr())
+        return s
+
+    def _make_cout(self):
+        o = capi.QqtStepOut()
+        o.reward = self._reward.data_ptr()
+        o.done = self._done.data_ptr()
+        o.died = self._died.data_ptr()
+        o.winner = self._winner.data_ptr()
+        o.n_alive = self._n_alive.data_ptr()
+        o.covered = self._covered.data_ptr()
+        o.triggered = self._triggered.data_ptr()
+        o.reset_mask = self._reset_mask.data_ptr()
+        return o
+
+    def _stream(self):
+        return capi.stream_ptr(self.device)
+
+    # ----------------------------------------------------- templates / reset
+    def set_template(self, template: dict, apply: bool = True, seed: int = 0,
+                     swap_spawns: bool = False) -> None:
+        """Install per-env reset templates and switch auto-reset to the device.
+
+        template: numpy/torch arrays, env-major like the reference:
+          wall, brick (N,H,W) bool; optional crate (N,H,W); spawn (N,P,2);
+          bombs_cap, blast_cap (N,P) int; spd (N,P) float; crate_prob (N,).
+        Done envs are then reset inside the step kernel to their template,
+        with no host round trip (the benchmark configurations' reset rule).
+        """
+        n, p, hw = self.num_envs, self.cfg.n_players, self.cfg.n_cells
+        d = self.device
+        T = lambda a, dt: torch.as_tensor(np.asarray(a)).to(d, dt)  # noqa: E731
+        tm = {
+            "wall": T(template["wall"], torch.bool).reshape(n, hw).t().contiguous(),
+            "brick": T(template["brick"], torch.bool).reshape(n, hw).t().contiguous(),
+            "crate": T(template.get("crate", np.zeros((n, hw), bool)), torch.bool)
+            .reshape(n, hw).t().contiguous(),
+            "spawn": T(template["spawn"], torch.float32).permute(1, 2, 0).contiguous(),
+            "bombs_cap": T(template["bombs_cap"], torch.int64).t().contiguous(),
+            "blast_cap": T(template["blast_cap"], torch.int64).t().contiguous(),
+            "spd": T(template["spd"], torch.float32).t().contiguous(),
+            "crate_prob": T(template["crate_prob"], torch.float32).contiguous(),
+            "episode": torch.zeros((n,), dtype=torch.int64, device=d),
+        }
+        self._tmpl_buf = tm
+        c = capi.QqtTemplate()
+        for k in ("wall", "brick", "crate", "spawn", "bombs_cap", "blast_cap", "spd",
+                  "crate_prob", "episode"):
+            setattr(c, k, tm[k].data_ptr())
+        c.seed = int(seed) & ((1 << 64) - 1)
+        c.swap_spawns = int(swap_spawns)
+        c.since_bomb0 = int(self.cfg.place_dist_cooldown)
+        self._tmpl = c
+        if apply:
+            self._apply_template(torch.ones(n, dtype=torch.bool, device=d))
+
+    def _apply_template(self, mask: torch.Tensor) -> None:
+        tm, b = self._tmpl_buf, self._buf
+        idx = mask.nonzero(as_tuple=True)[0]
+        if idx.numel() == 0:
+            return
+        for k in ("wall", "brick"):
+            b[k][:, idx] = tm[k][:, idx]
+        b["crate"][:, idx] = tm["crate"][:, idx]
+        b["_recycle_crate"][:, idx] = False
+        b["fuse"][:, idx] = 0
+        b["owner"][:, idx] = -1
+        b["bomb_blast"][:, idx] = 0
+        b["pos"][:, :, idx] = tm["spawn"][:, :, idx]
+        b["bombs_cap"][:, idx] = tm["bombs_cap"][:, idx]
+        b["blast_cap"][:, idx] = tm["blast_cap"][:, idx]
+        b["spd_g"][:, idx] = tm["spd"][:, idx]
+        b["_lo_bombs"][:, idx] = tm["bombs_cap"][:, idx]
+        b["_lo_blast"][:, idx] = tm["blast_cap"][:, idx]
+        b["_lo_spd"][:, idx] = tm["spd"][:, idx]
+        b["crate_prob"][idx] = tm["crate_prob"][idx]
+        self._reset_common(idx)
+
+    def _reset_common(self, idx) -> None:
+        b, cfg = self._buf, self.cfg
+        b["_recycle_crate"][:, idx] = False
+        b["_pending_lost"][:, idx] = 0
+        b["_combo"][:, idx] = 0
+        b["_last_hit"][:, idx] = -10 ** 9
+        b["fuse"][:, idx] = 0
+        b["owner"][:, idx] = -1
+        b["bomb_blast"][:, idx] = 0
+        b["alive"][:, idx] = True
+        b["hp"][:, idx] = cfg.max_hp
+        b["since_bomb"][:, idx] = cfg.place_dist_cooldown
+        b["invuln"][:, idx] = 0
+        b["t"][idx] = 0
+
+    def reset_all(self) -> None:
+        self.reset_(torch.ones((self.num_envs,), dtype=torch.bool, device=self.device))
+
+    def _opp_start(self, idx, b0, z0, s0):
+        """Seat-1 start attributes by opponent boost tier (sim/torch_sim.py:433-453)."""
+        cfg = self.cfg
+        bo = self._buf["_opp_boost"][idx].cpu()
+        m = cfg.opp_hist_mult
+        b = torch.where(bo == 2, torch.full_like(b0, cfg.opp_growth_bombs),
+                        torch.where(bo == 1, (b0 * m).round().clamp(max=cfg.growth_bombs_max), b0))
+        z = torch.where(bo == 2, torch.full_like(z0, cfg.opp_growth_blast),
+                        torch.where(bo == 1, (z0 * m).round().clamp(max=cfg.growth_blast_max), z0))
+        s = torch.where(bo == 2, torch.full_like(s0, cfg.opp_growth_speed),
+                        torch.where(bo == 1, (s0 * m).clamp(max=cfg.growth_speed_max), s0))
+        return b.long(), z.long(), s
+
+    def reset_(self, mask: torch.Tensor) -> None:
+        """Reset the masked envs on the host generator (sim/torch_sim.py:178-420).
+
+        With a device template installed, envs reset to their template
+        instead (the benchmark configurations)."""
+        if self._tmpl is not None:
+            self._apply_template(mask.to(self.device))
+            return
+        cfg, b, d = self.cfg, self._buf, self.device
+        idx_cpu = mask.detach().to("cpu").nonzero(as_tuple=True)[0]
+        count = int(idx_cpu.numel())
+        if count == 0:
+            return
+        idx = idx_cpu.to(d)
+        hw, p, gen = cfg.n_cells, cfg.n_players, self.gen
+        b["_is_open"][idx] = False
+        put = lambda key, rows, val: b[key].__setitem__((slice(None), rows), val)  # noqa: E731
+        if cfg.map_mode != "corridor":
+            wall = mapgen.open_obstacles(cfg, count, gen)
+            put("wall", idx, wall.reshape(count, hw).t().to(d))
+            put("brick", idx, False)
+            b0 = torch.full((count,), float(cfg.max_bombs))
+            z0 = torch.full((count,), float(cfg.blast))
+            s0 = torch.full((count,), 1.0)
+            ob, oz, os_ = self._opp_start(idx, b0, z0, s0)
+            caps = [(cfg.max_bombs, cfg.blast, 1.0), (ob, oz, os_)]
+            self._set_caps(idx, caps)
+            b["_map_kind"][idx] = 1
+            pos = torch.tensor(cfg.spawn_pos(), dtype=torch.float32)
+            pos = pos.unsqueeze(0).expand(count, -1, -1).clone()
+            sw = torch.rand(count, generator=gen) < 0.5
+        else:
+            r = torch.rand(count, generator=gen)
+            pf = cfg.pure_open_fraction
+            is_pure = r < pf
+            is_open = ~is_pure & (r < pf + cfg.open_fraction)
+            is_ring = ~(is_pure | is_open) & (r < pf + cfg.open_fraction + cfg.ring_fraction)
+            is_corr = ~(is_pure | is_open | is_ring)
+            wall = torch.zeros((count, cfg.height, cfg.width), dtype=torch.bool)
+            brick = torch.zeros_like(wall)
+            bcap = torch.zeros((count, p), dtype=torch.long)
+            zcap = torch.zeros((count, p), dtype=torch.long)
+            scap = torch.zeros((count, p), dtype=torch.float32)
+            cprob = torch.zeros((count,), dtype=torch.float32)
+            kind = torch.zeros((count,), dtype=torch.long)
+            opn = is_pure | is_open
+            if opn.any():
+                no = int(opn.sum())
+                wa = mapgen.open_obstacles(cfg, no, gen)
+                wa[is_pure[opn]] = False
+                wall[opn] = wa
+                self._fill_caps(bcap, zcap, scap, opn, idx, cfg.open_growth_bombs,
+                                cfg.open_growth_blast, cfg.open_growth_speed)
+                cprob[opn] = 1.0
+                kind[opn] = 1
+            if is_ring.any():
+                nr = int(is_ring.sum())
+                wall[is_ring] = mapgen.ring_walls(cfg, nr)
+                brick[is_ring] = mapgen.ring_bricks(cfg, nr, gen)
+                self._fill_caps(bcap, zcap, scap, is_ring, idx, cfg.growth_bombs_start,
+                                cfg.growth_blast_start, cfg.growth_speed_start)
+                cprob[is_ring] = cfg.ring_crate_prob
+                kind[is_ring] = 2
+            if is_corr.any():
+                nc = int(is_corr.sum())
+                tr = (torch.randint(0, cfg.top_wall_rows + 1, (nc,), generator=gen)
+                      if cfg.random_wall_rows else None)
+                wall[is_corr] = mapgen.walls(cfg, nc, gen, top_rows=tr)
+                brick[is_corr] = mapgen.bricks(cfg, nc, gen, top_rows=tr)
+                self._fill_caps(bcap, zcap, scap, is_corr, idx, cfg.growth_bombs_start,
+                                cfg.growth_blast_start, cfg.growth_speed_start)
+                cprob[is_corr] = cfg.growth_crate_prob
+            put("wall", idx, wall.reshape(count, hw).t().to(d))
+            put("brick", idx, brick.reshape(count, hw).t().to(d))
+            b["bombs_cap"][:, idx] = bcap.t().to(d)
+            b["blast_cap"][:, idx] = zcap.t().to(d)
+            b["spd_g"][:, idx] = scap.t().to(d)
+            b["_lo_bombs"][:, idx] = bcap.t().to(d)
+            b["_lo_blast"][:, idx] = zcap.t().to(d)
+            b["_lo_spd"][:, idx] = scap.t().to(d)
+            b["crate_prob"][idx] = cprob.to(d)
+            b["_map_kind"][idx] = kind.to(d)
+            b["_is_open"][idx] = opn.to(d)
+            pos = torch.zeros((count, p, 2), dtype=torch.float32)
+            if opn.any():
+                pos[opn] = torch.tensor(mapgen.open_spawns(cfg), dtype=torch.float32)
+            if is_ring.any():
+                pos[is_ring] = torch.tensor(cfg.ring_spawns(), dtype=torch.float32)
+            if is_corr.any():
+                pos[is_corr] = torch.tensor(cfg.spawn_pos(), dtype=torch.float32)
+            sw = torch.rand(count, generator=gen) < 0.5
+        if bool(sw.any()):
+            tmp = pos[sw, 0].clone()
+            pos[sw, 0] = pos[sw, 1]
+            pos[sw, 1] = tmp
+        b["pos"][:, :, idx] = pos.permute(1, 2, 0).to(d)
+        b["crate"][:, idx] = False
+        self._reset_common(idx)
+        if cfg.open_crate_cross and cfg.map_mode == "corridor":
+            open_idx = idx[b["_is_open"][idx]]
+            if open_idx.numel():
+                cells = torch.tensor([r * cfg.width + c for r, c in mapgen.open_cross_cells(cfg)],
+                                     dtype=torch.long, device=d)
+                b["crate"][cells.unsqueeze(1), open_idx.unsqueeze(0)] = True
+        if cfg.hazard_fraction > 0:
+            hz = torch.rand(count, generator=gen) < cfg.hazard_fraction
+            b["_hazard"][idx] = hz.to(d)
+            hz_idx = idx[hz.to(d)]
+            if hz_idx.numel():
+                b["bombs_cap"][:, hz_idx] = 0
+        else:
+            b["_hazard"][idx] = False
+
+    def _set_caps(self, idx, caps):
+        b, d = self._buf, self.device
+        for pl, (bb, zz, ss) in enumerate(caps[:2]):
+            for key, v in (("bombs_cap", bb), ("blast_cap", zz), ("spd_g", ss)):
+                val = v.to(d) if isinstance(v, torch.Tensor) else v
+                b[key][pl, idx] = val
+                lo = {"bombs_cap": "_lo_bombs", "blast_cap": "_lo_blast", "spd_g": "_lo_spd"}[key]
+                b[lo][pl, idx] = val
+
+    def _fill_caps(self, bcap, zcap, scap, sel, idx, b_start, z_start, s_start):
+        k = int(sel.sum())
+        b0 = torch.full((k,), float(b_start))
+        z0 = torch.full((k,), float(z_start))
+        s0 = torch.full((k,), float(s_start))
+        ob, oz, os_ = self._opp_start(idx[sel.to(idx.device)], b0, z0, s0)
+        bcap[sel, 0], zcap[sel, 0], scap[sel, 0] = b_start, z_start, s_start
+        bcap[sel, 1], zcap[sel, 1], scap[sel, 1] = ob, oz, os_
+
+    def set_opp_boost(self, v: int) -> None:
+        self._buf["_opp_boost"].fill_(int(v))
+
+    def set_explore_coef(self, v: float) -> None:
+        self._explore_coef = float(v)
+        self._ccfg = make_ccfg(self.cfg, self.num_envs, self._explore_coef, self.obs_stride)
+
+    # -------------------------------------------------------------- tick
+    def observe(self) -> torch.Tensor:
+        """(N, C, H, W) shared observation (fp16 by default); a view of a
+        persistent, row-padded buffer (sim/torch_sim.py:605-627)."""
+        capi.check(capi.lib().qqt_observe(ctypes.byref(self._ccfg), ctypes.byref(self._cstate),
+                                          self._obs.data_ptr(), self._danger.data_ptr(), None,
+                                          None, self._stream()), "qqt_observe")
+        return self.obs_view()
+
+    def obs_view(self) -> torch.Tensor:
+        cfg = self.cfg
+        c = cfg.n_channels * cfg.n_cells
+        return self._obs[:, :c].view(self.num_envs, cfg.n_channels, cfg.height, cfg.width)
+
+    def observe_and_mask(self):
+        """observe() and legal_mask() in one launch."""
+        capi.check(capi.lib().qqt_observe(ctypes.byref(self._ccfg), ctypes.byref(self._cstate),
+                                          self._obs.data_ptr(), self._danger.data_ptr(),
+                                          self._mm.data_ptr(), self._bm.data_ptr(),
+                                          self._stream()), "qqt_observe")
+        return self.obs_view(), self._mm, self._bm
+
+    def danger(self) -> torch.Tensor:
+        """(N, H, W) float32 danger map computed by the last observe()."""
+        return self._danger.view(self.num_envs, self.cfg.height, self.cfg.width)
+
+    def legal_mask(self):
+        """(move_mask (N,P,5) bool, bomb_mask (N,P,2) bool) (sim/obs.py:170-229)."""
+        capi.check(capi.lib().qqt_legal_mask(ctypes.byref(self._ccfg),
+                                             ctypes.byref(self._cstate), self._mm.data_ptr(),
+                                             self._bm.data_ptr(), self._stream()),
+                   "qqt_legal_mask")
+        return self._mm, self._bm
+
+    def _crate_draws(self):
+        n, p = self.num_envs, self.cfg.n_players
+        if self._rand_buf is not None:
+            rb = self._rand_buf
+            return (rb[: n * p].view(n, p).contiguous(),
+                    rb[n * p: 2 * n * p].view(n, p).contiguous())
+        r = torch.rand(n * p * 2, device=self.device).view(p, 2, n)
+        return r[:, 0, :].t().contiguous(), r[:, 1, :].t().contiguous()
+
+    def step(self, actions: torch.Tensor, auto_reset: bool = True, crate_draws=None):
+        """One tick (sim/torch_sim.py:895-1261) -> (reward (N,P), done (N,), info).
+
+        With a template installed, done envs reset on the device inside the
+        same kernel; otherwise auto_reset resets them on the host generator.
+        `crate_draws`: optional (rb_hit, rb_grow) (N,P) float tensors.
+        """
+        acts = actions.to(self.device, torch.int64).contiguous()
+        rb_hit = rb_grow = None
+        if self.cfg.map_mode == "corridor":
+            rb_hit, rb_grow = crate_draws if crate_draws is not None else self._crate_draws()
+            rb_hit = rb_hit.to(self.device, torch.float32).contiguous()
+            rb_grow = rb_grow.to(self.device, torch.float32).contiguous()
+        dev_reset = auto_reset and self._tmpl is not None
+        rc = capi.lib().qqt_step(ctypes.byref(self._ccfg), ctypes.byref(self._cstate),
+                                 acts.data_ptr(), capi.ptr(rb_hit), capi.ptr(rb_grow),
+                                 self._tiers.data_ptr(), int(self._first_step),
+                                 ctypes.byref(self._cout),
+                                 ctypes.byref(self._tmpl) if dev_reset else None,
+                                 self._step_scratch.data_ptr(), self._stream())
+        capi.check(rc, "qqt_step")
+        self._first_step = False
+        n, h, w = self.num_envs, self.cfg.height, self.cfg.width
+        info = {"n_alive": self._n_alive, "died": self._died, "winner": self._winner,
+                "blast": self._covered.t().view(n, h, w),
+                "trig": self._triggered.t().view(n, h, w)}
+        if auto_reset and not dev_reset:
+            if bool(self._done.any()):
+                info = {k: v.clone() for k, v in info.items()}
+                self.reset_(self._done.clone())
+        return self._reward, self._done, info
+
+    # ------------------------------------------------------------ recycle
+    def flush_recycle(self) -> None:
+        """Drop one crate per lost attribute layer on random free cells, host
+        generator draws in the reference's order (sim/torch_sim.py:549-596)."""
+        cfg = self.cfg
+        lost = self._buf["_pending_lost"]
+        if not bool((lost.sum() > 0).item()):
+            return
+        n, p, hw = self.num_envs, cfg.n_players, cfg.n_cells
+        excl = torch.tensor(_recycle_exclusion(cfg), dtype=torch.long)
+        lost_cpu = lost.cpu()
+        for pl in range(p):
+            lp = lost_cpu[pl]
+            idx = (lp > 0).nonzero(as_tuple=True)[0]
+            if idx.numel() == 0:
+                continue
+            idx_d = idx.to(self.device)
+            avail = (~self._buf["wall"][:, idx_d] & ~self._buf["brick"][:, idx_d]).t().cpu()
+            avail[:, excl] = False
+            rows, cols = [], []
+            for i, e in enumerate(idx.tolist()):
+                cells = avail[i].nonzero(as_tuple=True)[0]
+                if cells.numel() == 0:
+                    continue
+                k = min(int(lp[e]), int(cells.numel()))
+                pick = cells[torch.randperm(cells.numel(), generator=self.gen)[:k]]
+                rows.append(pick)
+                cols.append(torch.full_like(pick, e))
+            if rows:
+                r = torch.cat(rows).to(self.device)
+                c = torch.cat(cols).to(self.device)
+                self._buf["crate"][r, c] = True
+                self._buf["_recycle_crate"][r, c] = True
+        lost.zero_()
+
+    # --------------------------------------------------------- snapshots
+    def state_dict(self) -> dict:
+        keys = ("wall", "brick", "crate", "fuse", "owner", "bomb_blast", "pos", "alive", "hp",
+                "since_bomb", "t")
+        return {k: getattr(self, k).clone() for k in keys}
+
+    def load_state_dict(self, snap: dict) -> None:
+        for key, val in snap.items():
+            getattr(self, key).copy_(val)
+
+    def load_numpy_state(self, st: dict) -> None:
+        """Write an env-major numpy state (oracle/golden key names) into the
+        device buffers."""
+        names = {"recycle": "_recycle_crate", "pending_lost": "_pending_lost",
+                 "combo": "_combo", "last_hit": "_last_hit", "lo_bombs": "_lo_bombs",
+                 "lo_blast": "_lo_blast", "lo_spd": "_lo_spd", "hazard": "_hazard"}
+        for k, v in st.items():
+            key = names.get(k, k)
+            if key not in self._buf:
+                continue
+            self._view(key).copy_(torch.as_tensor(np.asarray(v)).to(self.device))
+
+    def numpy_state(self) -> dict:
+        names = {"_recycle_crate": "recycle", "_pending_lost": "pending_lost",
+                 "_combo": "combo", "_last_hit": "last_hit", "_lo_bombs": "lo_bombs",
+                 "_lo_blast": "lo_blast", "_lo_spd": "lo_spd", "_hazard": "hazard"}
+        out = {}
+        for key in list(_PLANES) + list(_PLAYER) + ["pos", "t", "crate_prob", "_hazard"]:
+            out[names.get(key, key)] = self._view(key).cpu().numpy().copy()
+        return out
+
+
+def _make_prop(key):
+    def get(self):
+        return self._view(key)
+
+    def set_(self, value):
+        self._view(key).copy_(torch.as_tensor(value).to(self.device))
+
+    return property(get, set_)
+
+
+for _k in list(_PLANES) + list(_PLAYER) + ["pos"] + list(_ENV):
+    setattr(B200Sim, _k, _make_prop(_k))
+
+
+def _recycle_exclusion(cfg) -> list[int]:
+    """Cells that never receive recycled crates: the 4-neighbourhoods of the
+    open, mode and ring spawns plus the open cross band (sim/torch_sim.py:508-533)."""
+    h, w = cfg.height, cfg.width
+    excl = set()
+    spawn_sets = [[(int(y), int(x)) for y, x in mapgen.open_spawns(cfg)],
+                  list(cfg.spawn_cells()), list(cfg.ring_spawn_cells())]
+    for spawns in spawn_sets:
+        for r, c in spawns:
+            excl.add((r, c))
+            for dr, dc in mapgen.DIRS4:
+                if 0 <= r + dr < h and 0 <= c + dc < w:
+                    excl.add((r + dr, c + dc))
+    excl |= set(mapgen.open_cross_cells(cfg))
+    return sorted(r * w + c for r, c in excl)

@@ -1,0 +1,178 @@
+"""GPU parity: the CUDA engine (through the C ABI) against the reference's
+golden trajectories and the CPU oracle.
+
+Bar: integer / boolean state, masks and bot actions bit-exact; positions,
+danger and fp16 observations bit-exact (the kernels keep the reference's
+float32 operation order); rewards within 1e-6 absolute (the reference sums
+the placement chain bonus over cells in a different order); path fields
+bit-exact.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import goldens as G
+
+pytestmark = pytest.mark.gpu
+
+if torch.cuda.is_available():
+    from qqt_b200 import scenarios
+    from qqt_b200.bots import AstarBot, GreedyBot, RandomBot
+    from qqt_b200.config import SimConfig
+    from qqt_b200.sim import B200Sim
+    from qqt_b200 import _capi
+
+
+@pytest.fixture(autouse=True)
+def _need_gpu():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    yield
+    torch.cuda.synchronize()
+    assert _capi.device_error() == 0, "device error word set"
+
+
+def _np(t):
+    return t.detach().cpu().numpy()
+
+
+def _sim_from_state(cfg, st):
+    n = st["alive"].shape[0]
+    sim = B200Sim(cfg, n, device="cuda", seed=0)
+    sim.load_numpy_state(st)
+    return sim
+
+
+def test_kat_states_observe_masks():
+    g = G.load("kat_states")
+    cfg = SimConfig(height=13, width=13, n_players=2, map_mode="corridor", speed=3.0,
+                    max_steps=1800, obs_extra_enabled=True, obs_fp16=False)
+    n = g["wall"].shape[0]
+    st = {k: g[k] for k in ("wall", "brick", "fuse", "owner", "bomb_blast", "crate", "pos",
+                            "alive", "invuln", "bombs_cap", "blast_cap")}
+    st["t"] = g["t"].astype(np.int64)
+    st["recycle"] = np.zeros_like(st["wall"])
+    sim = _sim_from_state(cfg, st)
+    obs, mm, bm = sim.observe_and_mask()
+    assert np.array_equal(_np(sim.danger()), g["danger"])
+    assert np.array_equal(_np(obs), g["obs"])
+    assert np.array_equal(_np(mm), g["mm"]) and np.array_equal(_np(bm), g["bm"])
+
+
+def _replay(name, cfg, learner, opp, bomb_rate=0.05, field_check=False):
+    g = G.load(name)
+    st = G.init_state(g)
+    wall = st["wall"]
+    n, p = st["alive"].shape
+    sim = _sim_from_state(cfg, st)
+    T = g["reward"].shape[0]
+    obs_ticks = list(g["obs_ticks"])
+    reset_ticks = list(g["reset_ticks"])
+    flush_ticks = list(g["flush_ticks"])
+    field_ticks = list(g["field_ticks"]) if "field_ticks" in g else []
+    bots = {}
+    for pid in (0, 1):
+        is_net = (pid == 0 and learner is not None) or (pid == 1 and opp == "self")
+        if is_net:
+            continue
+        kind = "random" if (pid == 0 or opp == "random") else opp
+        bots[pid] = {"random": lambda: RandomBot(sim, bomb_rate), "greedy": lambda: GreedyBot(sim),
+                     "astar": lambda: AstarBot(sim, mode=True)}[kind]()
+        if kind == "astar":
+            bots[pid].keep_fields = field_check
+    for t in range(T):
+        obs, mm, bm = sim.observe_and_mask()
+        assert np.array_equal(_np(mm), g["mm"][t]), f"{name} t={t}: move mask"
+        assert np.array_equal(_np(bm), g["bm"][t]), f"{name} t={t}: bomb mask"
+        if t in obs_ticks:
+            assert np.array_equal(_np(obs), g["obs"][obs_ticks.index(t)]), f"{name} t={t}: obs"
+        for pid, bot in bots.items():
+            draws = G.bot_draws(g, pid, t)
+            if isinstance(bot, RandomBot):
+                bot.feed(u_move=draws[0][1][:, 0], u_bomb=draws[1][1])
+            elif isinstance(bot, GreedyBot):
+                bot.feed(noise=draws[0][1])
+            else:
+                ints = [v for k, v in draws if k == "randint"]
+                noise = [v for k, v in draws if k == "rand"][0]
+                feed = {"noise": noise}
+                if bot.mode is None:
+                    feed["mode0"], feed["timer0"] = ints[0], ints[1]
+                    ints = ints[2:]
+                if ints:
+                    feed["new_mode"], feed["new_timer"] = ints[0], ints[1]
+                elif (bot.calls + 1) % 16 == 0:
+                    feed["new_mode"] = np.zeros(n, np.int64)
+                    feed["new_timer"] = np.zeros(n, np.int64)
+                bot.feed(**feed)
+            a = bot.act(obs, mm[:, pid], bm[:, pid], pid)
+            assert np.array_equal(_np(a), g["actions"][t][:, pid]), f"{name} t={t}: bot {pid}"
+            if field_check and t in field_ticks and pid == 1:
+                i = field_ticks.index(t)
+                assert np.array_equal(_np(bot.vsafe), g["vsafe"][i]), f"{name} t={t}: V_safe"
+                assert np.array_equal(_np(bot.vopp), g["vopp"][i]), f"{name} t={t}: V_opp"
+        acts = torch.from_numpy(g["actions"][t]).cuda()
+        rb = (torch.from_numpy(g["rb_hit"][t]).cuda(), torch.from_numpy(g["rb_grow"][t]).cuda())
+        r, d, info = sim.step(acts, auto_reset=False, crate_draws=rb)
+        assert np.array_equal(_np(d), g["done"][t]), f"{name} t={t}: done"
+        assert np.array_equal(_np(info["winner"]), g["winner"][t]), f"{name} t={t}: winner"
+        err = np.abs(_np(r) - g["reward"][t]).max()
+        assert err <= 1e-6, f"{name} t={t}: reward err {err}"
+        got = sim.numpy_state()
+        got["wall"] = got["wall"]
+        bad = G.compare_state(G.state_at(g, t, wall), got)
+        assert not bad, f"{name} t={t}: state differs in {bad}"
+        if t in reset_ticks:
+            rs = G.reset_state(g, reset_ticks.index(t), wall)
+            sim.load_numpy_state(rs)
+        if t in flush_ticks:
+            i = flush_ticks.index(t)
+            sim.gen.set_state(torch.from_numpy(g[f"flush{i}_gen"]))
+            sim.flush_recycle()
+            got = sim.numpy_state()
+            for k in ("crate", "recycle", "pending_lost"):
+                assert np.array_equal(got[k], g[f"flush{i}_{k}"]), f"{name} t={t}: flush {k}"
+
+
+def test_traj_cfg1_random_bots_gpu():
+    _replay("traj_cfg1", SimConfig(**scenarios.CFG1), None, "random")
+
+
+def test_traj_cfg2_astar_gpu():
+    _replay("traj_cfg2", SimConfig(**scenarios.CFG2), "mlp", "astar", field_check=True)
+
+
+def test_traj_cfg5_greedy_gpu():
+    _replay("traj_cfg5", SimConfig(**scenarios.CFG2), "cnn", "greedy")
+
+
+def test_stress_cfg3_gpu():
+    g = G.load("stress_cfg3")
+    cfg = SimConfig(**scenarios.CFG1)
+    st = G.init_state(g)
+    n, p = st["alive"].shape
+    sim = _sim_from_state(cfg, st)
+    acts = torch.zeros((n, p, 2), dtype=torch.int64, device="cuda")
+    acts[..., 0] = 4
+    r, d, info = sim.step(acts, auto_reset=False,
+                          crate_draws=(torch.from_numpy(g["rb_hit"]).cuda(),
+                                       torch.from_numpy(g["rb_grow"]).cuda()))
+    assert np.array_equal(_np(info["blast"]), g["covered"])
+    assert np.array_equal(_np(info["trig"]), g["triggered"])
+    assert np.abs(_np(r) - g["reward"]).max() <= 1e-6
+    assert not G.compare_state(G.init_state(g, "after_"), sim.numpy_state())
+    obs, mm, bm = sim.observe_and_mask()
+    assert np.array_equal(_np(sim.danger()), g["danger"])
+    assert np.array_equal(_np(obs), g["obs"])
+    assert np.array_equal(_np(mm), g["mm"]) and np.array_equal(_np(bm), g["bm"])
+    for pid in range(p):
+        bot = AstarBot(sim, mode=False)
+        bot.keep_fields = True
+        bot.feed(noise=g[f"astar_noise{pid}"])
+        a = bot.act(obs, mm[:, pid], bm[:, pid], pid)
+        assert np.array_equal(_np(bot.vsafe), g[f"vsafe{pid}"])
+        assert np.array_equal(_np(bot.vopp), g[f"vopp{pid}"])
+        assert np.array_equal(_np(a), g[f"astar_act{pid}"])
