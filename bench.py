@@ -1,0 +1,463 @@
+#!/usr/bin/env python3
+"""Rollout throughput benchmark (BASELINE.json metric, configuration 2).
+
+One "step" = one 128-tick rollout of N=5632 envs on the pillar-corridor map:
+observe -> masks -> MLP learner (seat 0) -> astar opponent (seat 1) -> step
+(device auto-reset) -> crate recycling every 16 ticks, captured as one CUDA
+graph.  value = envs * ticks * ranks / max-over-ranks device time.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Multi-GPU (weak scaling, no data-path collective): launched with
+torch.distributed.run, each rank runs its own 5632-env shard.
+--impl reference times the CPU restatement of the reference algorithm
+(oracle/, the reference itself is Python and cannot be shipped) on the
+host's cores for the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [ROOT, os.path.join(ROOT, "qqt-gpu-sim_b200")]
+
+METRIC = "rollout env-steps/sec (sim+obs+policy+sample) at 1/2/4/8 B200 vs ref CPU"
+UNIT = "env-steps/s"
+N_ENVS = 5632      # overridden by --envs for profiling cases
+TICKS = 128
+WORKLOAD = ("cfg2: 13x13 pillar corridor (bricks p=0.7), P=2, N=5632 envs per GPU, "
+            "random-init MLP learner seat 0 (view_perm) vs astar seat 1, 128-tick rollout")
+
+# Algorithmic bytes per env per launch (reference dtypes, compulsory traffic),
+# per kernel; see DESIGN.md "Roofline accounting".
+ALG_BYTES = {
+    "step": 169 * (1 + 1 + 1 + 1 + 2 + 1 + 2) * 2 - 169 + 280 + 32 + 8 + 1,
+    "observe": 169 * (1 + 1 + 1 + 1 + 2 + 2) + 56 + 2368 * 2 + 14,
+    "astar": 169 * (1 + 1 + 1 + 2) + 169 * 2 + 10 + 20 + 16,
+    "mlp_gemm": 2368 * 2 + 128 * 4,
+    "mlp_heads": 128 * 4 + 10 + 8 + 16 + 8,
+}
+MLP_FLOPS = 2 * 2366 * 128
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            m = json.load(f)
+        return float(m["hbm_gbs"]), float(m["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples every 200 ms while running."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def __enter__(self):
+        def run():
+            while not self._stop.is_set():
+                try:
+                    out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits"], capture_output=True,
+                                         text=True, timeout=5).stdout.strip()
+                    if out:
+                        self.rows.append([x.strip() for x in out.split(",")])
+                except Exception:
+                    pass
+                self._stop.wait(0.2)
+        self._t = threading.Thread(target=run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4)
+                          if len(r) > 5 + i and r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.rows)}
+
+
+def _template(cfg, n, seed):
+    import numpy as np
+    from qqt_b200 import scenarios
+    p = cfg.n_players
+    wall, brick = scenarios.pillar_corridor(n, cfg.height, cfg.width, seed=seed)
+    spawn = np.broadcast_to(np.array(scenarios.corner_spawns(cfg), np.float32), (n, p, 2)).copy()
+    return {"wall": wall, "brick": brick, "spawn": spawn,
+            "bombs_cap": np.full((n, p), cfg.growth_bombs_start, np.int64),
+            "blast_cap": np.full((n, p), cfg.growth_blast_start, np.int64),
+            "spd": np.full((n, p), cfg.growth_speed_start, np.float32),
+            "crate_prob": np.full((n,), cfg.growth_crate_prob, np.float32)}
+
+
+# --------------------------------------------------------------- CPU legs
+
+def _oracle_rollout_worker(args):
+    """Run the oracle tick protocol on a shard (spawned process)."""
+    n, ticks, seed = args
+    import numpy as np
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(1)
+    except Exception:
+        pass
+    from oracle import qqt_oracle as O
+    from qqt_b200 import scenarios
+    from qqt_b200.config import SimConfig
+    from qqt_b200.policy_init import init_params
+    cfg = SimConfig(**scenarios.CFG2)
+    p = cfg.n_players
+    t = _template(cfg, n, seed)
+    st = {"wall": t["wall"], "brick": t["brick"], "crate": np.zeros_like(t["wall"]),
+          "recycle": np.zeros_like(t["wall"]),
+          "fuse": np.zeros(t["wall"].shape, np.int16), "owner": np.full(t["wall"].shape, -1, np.int8),
+          "bomb_blast": np.zeros(t["wall"].shape, np.int16), "pos": t["spawn"].copy(),
+          "alive": np.ones((n, p), bool), "hp": np.full((n, p), cfg.max_hp, np.uint8),
+          "since_bomb": np.full((n, p), cfg.place_dist_cooldown, np.int32),
+          "t": np.zeros(n, np.int64), "bombs_cap": t["bombs_cap"].copy(),
+          "blast_cap": t["blast_cap"].copy(), "spd_g": t["spd"].copy(),
+          "invuln": np.zeros((n, p), np.int64), "pending_lost": np.zeros((n, p), np.int64),
+          "combo": np.zeros((n, p), np.int64), "last_hit": np.full((n, p), -10 ** 9, np.int64),
+          "lo_bombs": t["bombs_cap"].copy(), "lo_blast": t["blast_cap"].copy(),
+          "lo_spd": t["spd"].copy(), "crate_prob": t["crate_prob"].copy(),
+          "hazard": np.zeros(n, bool)}
+    params = init_params(cfg.obs_shape, "mlp", seed=1)
+    rng = np.random.default_rng(seed)
+    ticker = O.ModeTicker(rng.integers(0, 2, n), rng.integers(60, 240, n))
+    t0 = time.perf_counter()
+    for _ in range(ticks):
+        obs, _ = O.observe(cfg, st)
+        obs16 = obs.astype(np.float16)
+        mm, bm = O.legal_mask(cfg, st)
+        u = rng.random((n, 2))
+        a0, _, _, _, _ = O.mlp_act(params, obs16.astype(np.float32), mm[:, 0], bm[:, 0], 0, p,
+                                   u[:, 0], u[:, 1])
+        mode = ticker.advance(rng.integers(0, 2, n), rng.integers(60, 240, n))
+        a1 = O.astar_attack(cfg, st, obs16[:, 2 * p + 1].astype(np.float32), mm[:, 1], bm[:, 1], 1,
+                            rng.random((n, 5)).astype(np.float32), mode=mode)
+        acts = np.stack([a0, a1], 1)
+        rb = rng.random((2, n, p)).astype(np.float32)
+        O.step(cfg, st, acts, rb[0], rb[1])
+    return n * ticks, time.perf_counter() - t0
+
+
+def cpu_leg(n_envs, ticks, procs, seed=0):
+    """Bounded oracle sample on `procs` processes (spawned: no GPU state)."""
+    import multiprocessing as mp
+    per = max(1, n_envs // procs)
+    if procs == 1:
+        steps, dt = _oracle_rollout_worker((per, ticks, seed))
+        return steps / dt, steps, dt
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(procs) as pool:
+        res = pool.map(_oracle_rollout_worker, [(per, ticks, seed + i) for i in range(procs)])
+    # workers run concurrently; each times its own loop (process start-up excluded)
+    dt = max(r[1] for r in res)
+    steps = sum(r[0] for r in res)
+    return steps / dt, steps, dt
+
+
+# ------------------------------------------------------------ GPU leg
+
+def build_engine(device, rank):
+    import torch
+    from qqt_b200 import scenarios
+    from qqt_b200.bots import AstarBot
+    from qqt_b200.config import SimConfig
+    from qqt_b200.policy import B200Policy
+    from qqt_b200.policy_init import init_params
+    from qqt_b200.rollout import Rollout
+    from qqt_b200.sim import B200Sim
+    cfg = SimConfig(**scenarios.CFG2)
+    sim = B200Sim(cfg, N_ENVS, device=device, seed=1 + rank,
+                  template=_template(cfg, N_ENVS, 1 + rank))
+    sim.set_template(_template(cfg, N_ENVS, 1 + rank), apply=False, seed=1 + rank,
+                     swap_spawns=False)
+    pol = B200Policy(init_params(cfg.obs_shape, "mlp", seed=1), cfg.obs_shape, 2, seats=(0,),
+                     device=device)
+    bot = AstarBot(sim, mode=True)
+    ro = Rollout(sim, pol, bot, T=TICKS)
+    gen = torch.Generator(device=device).manual_seed(1234 + rank)
+    return ro, gen
+
+
+def instrumented_kernel_times(ro):
+    """One eager rollout with CUDA events around every library call:
+    per-kernel launches and mean device duration (ms)."""
+    import torch
+    sim, buf, dr = ro.sim, ro.buf, ro.draws
+    times = {k: [] for k in ("observe", "mlp", "astar", "step", "flush")}
+
+    def timed(name, fn):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        times[name].append((a, b))
+
+    bot = ro.opponent
+    for t in range(ro.T):
+        holder = {}
+        timed("observe", lambda: holder.update(zip(("obs", "mm", "bm"), sim.observe_and_mask(
+            buf.obs_rows[t], buf.mm[t], buf.bm[t], danger=False))))
+        obs, mm, bm = holder["obs"], holder["mm"], holder["bm"]
+        acts = buf.act[t]
+        timed("mlp", lambda: ro.learner.act_seats(obs, [mm[:, 0]], [bm[:, 0]], dr.u_net[t],
+                                                   [acts[:, 0]], buf.logp[t], buf.val[t]))
+        feed = {"noise": dr.noise[t]}
+        if (bot.calls + 1) % 16 == 0:
+            feed["new_mode"], feed["new_timer"] = dr.tick_mode[0], dr.tick_timer[0]
+        bot.feed(**feed)
+        timed("astar", lambda: bot.act(obs, mm[:, 1], bm[:, 1], 1, out=acts[:, 1]))
+        timed("step", lambda: sim.step(acts, auto_reset=True,
+                                       crate_draws=(dr.crate[t, 0], dr.crate[t, 1]),
+                                       reward_out=buf.rew[t], done_out=buf.done[t]))
+        if t % 16 == 15:
+            timed("flush", lambda: sim.flush_recycle())
+    torch.cuda.synchronize()
+    return {k: (len(v), sum(a.elapsed_time(b) for a, b in v) / max(1, len(v))) for k, v in times.items()}
+
+
+def gpu_bench(args):
+    import numpy as np
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = f"cuda:{local}"
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device(device))
+    ro, gen = build_engine(device, rank)
+    sim, buf, dr = ro.sim, ro.buf, ro.draws
+    # first tick eagerly (one-time set-up: resolve tiers, ticker state)
+    dr.generate(gen)
+    ro.tick(0)
+    ro.collect()                     # finish a full eager rollout for a warm state
+    kt = instrumented_kernel_times(ro)
+    ro.capture()
+    pool = [RolloutDrawsPool.make(dr, gen) for _ in range(min(args.steps + args.warmup, 4))]
+    l2 = torch.empty((64 << 20,), dtype=torch.float32, device=device)   # 256 MB > L2
+
+    def one_step(i, ev):
+        a, b = ev
+        a.record()
+        RolloutDrawsPool.load(dr, pool[i % len(pool)])
+        ro.replay()
+        b.record()
+
+    for i in range(args.warmup):
+        one_step(i, (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)))
+        l2.zero_()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            one_step(i, evs[i])
+            l2.zero_()                      # flush L2 between timed steps (not timed)
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in evs)
+    t_max = torch.tensor([ms], device=device)
+    if dist:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    ms = float(t_max.item())
+    value = N_ENVS * TICKS * world * args.steps / (ms / 1e3)
+
+    # ---- e2e: public API with host-fed draws and a host read of the rewards
+    host_draws = [t.detach().cpu().pin_memory() for t in dr.tensors()]
+    h2d = sum(t.numel() * t.element_size() for t in host_draws)
+    rew_host = torch.empty((TICKS, N_ENVS), dtype=torch.float32).pin_memory()
+    d2h = rew_host.numel() * 4
+    e_evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+             for _ in range(args.steps)]
+    for i in range(args.steps):
+        a, b = e_evs[i]
+        a.record()
+        for dst, src in zip(dr.tensors(), host_draws):
+            dst.copy_(src, non_blocking=True)
+        ro.replay()
+        rew_host.copy_(buf.rew[:, :, 0], non_blocking=True)
+        b.record()
+        b.synchronize()
+        l2.zero_()
+    e_ms = sum(a.elapsed_time(b) for a, b in e_evs)
+    t_e = torch.tensor([e_ms], device=device)
+    if dist:
+        dist.all_reduce(t_e, op=dist.ReduceOp.MAX)
+    e_value = N_ENVS * TICKS * world * args.steps / (float(t_e.item()) / 1e3)
+    ro.graph = None
+    torch.cuda.synchronize()
+
+    out = None
+    if rank == 0:
+        hbm, tflops, src = _peaks()
+        per = {}
+        for k, (launches, mean_ms) in kt.items():
+            if launches == 0:
+                continue
+            if k == "mlp":
+                name, byt = "mlp", ALG_BYTES["mlp_gemm"] + ALG_BYTES["mlp_heads"]
+            else:
+                name, byt = k, ALG_BYTES.get(k, 169 * 8)
+            per[name] = {"launches_per_rollout": launches, "mean_ms": round(mean_ms, 5),
+                         "share": None, "alg_bytes_per_launch": byt * N_ENVS}
+        tot = sum(v["launches_per_rollout"] * v["mean_ms"] for v in per.values())
+        for v in per.values():
+            v["share"] = round(v["launches_per_rollout"] * v["mean_ms"] / tot, 4)
+        dom = max((k for k in per if k != "flush"), key=lambda k: per[k]["share"])
+        d = per[dom]
+        achieved = d["alg_bytes_per_launch"] / (d["mean_ms"] / 1e3) / 1e9
+        traffic = _ncu_traffic(dom)
+        cores = args.cpu_procs
+        cpu_v, cpu_steps, cpu_dt = cpu_leg(args.cpu_envs, args.cpu_ticks, cores)
+        out = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 sim, fp16xfp16->f32 GEMM",
+            "data": "synthetic (seeded template maps, random-init policy, device RNG draws)",
+            "config": {"workload": WORKLOAD, "envs_per_gpu": N_ENVS, "ticks": TICKS,
+                       "parallelism": f"env shards x{world}, no rollout collective",
+                       "l2": "flushed (256 MB write) between timed steps; each step also "
+                             "writes a 3.4 GB observation buffer",
+                       "cuda_graph": True},
+            "e2e": {"value": round(e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": (TICKS * 6 + TICKS // 16) * args.steps,
+            "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1),
+                         "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                         "peak_source": src, "traffic": traffic,
+                         "per_kernel": per},
+            "cpu_baseline": {"value": round(cpu_v, 1), "unit": UNIT, "cores": cores,
+                             "kind": "port",
+                             "sample": f"oracle (numpy restatement), {args.cpu_envs} envs x "
+                                       f"{args.cpu_ticks} ticks of the same workload"},
+            "clocks": clk.summary(),
+        }
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
+
+
+def _ncu_traffic(kernel):
+    """DRAM bytes per launch from the committed ncu summary, if present."""
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(kernel)
+    except Exception:
+        return None
+
+
+class RolloutDrawsPool:
+    @staticmethod
+    def make(dr, gen):
+        import torch
+        ts = [torch.empty_like(t) for t in dr.tensors()]
+        for t in ts[:3]:
+            t.uniform_(generator=gen)
+        ts[3].random_(0, 2, generator=gen)
+        ts[4].random_(60, 240, generator=gen)
+        return ts
+
+    @staticmethod
+    def load(dr, ts):
+        for dst, src in zip(dr.tensors(), ts):
+            dst.copy_(src, non_blocking=True)
+
+
+def reference_arm(args):
+    """Time the CPU restatement of the reference on the host's cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    procs = args.cpu_procs_ref or max(1, len(os.sched_getaffinity(0)))
+    vals = []
+    for _ in range(args.warmup):
+        cpu_leg(procs * 8, 2, procs)
+    for i in range(args.steps):
+        v, steps, dt = cpu_leg(procs * 32, args.ref_ticks, procs, seed=i)
+        vals.append((steps, dt))
+    steps = sum(s for s, _ in vals)
+    dt = sum(d for _, d in vals)
+    value = steps / dt
+    return {"impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": UNIT,
+            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 sim, f64 policy (numpy)", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "sample_envs": procs * 32,
+                       "sample_ticks": args.ref_ticks},
+            "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": procs,
+                             "kind": "port",
+                             "sample": f"oracle restatement of the reference path, "
+                                       f"{procs} processes x 32 envs x {args.ref_ticks} ticks "
+                                       f"per step"},
+            "e2e": {"value": round(value, 1), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-envs", type=int, default=256)
+    ap.add_argument("--cpu-ticks", type=int, default=8)
+    ap.add_argument("--cpu-procs", type=int, default=1)
+    ap.add_argument("--cpu-procs-ref", type=int, default=0)
+    ap.add_argument("--ref-ticks", type=int, default=4)
+    ap.add_argument("--envs", type=int, default=5632, help="envs per GPU (profiling cases)")
+    ap.add_argument("--ticks", type=int, default=128, help="ticks per rollout (multiple of 16)")
+    args = ap.parse_args()
+    global N_ENVS, TICKS
+    N_ENVS, TICKS = args.envs, args.ticks
+    if TICKS % 16:
+        raise SystemExit("--ticks must be a multiple of 16")
+    out = reference_arm(args) if args.impl == "reference" else gpu_bench(args)
+    if out is not None:
+        print(json.dumps(out))
+
+
+if __name__ == "__main__":
+    main()

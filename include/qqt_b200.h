@@ -148,6 +148,17 @@ int qqt_step(const QqtCfg *cfg, const QqtState *st, const int64_t *actions,
              void *scratch, qqt_stream_t stream);
 uint64_t qqt_step_scratch_bytes(const QqtCfg *cfg);
 
+/* Crate recycling on the device: for every player with pending lost
+ * attribute layers, drop min(lost, free cells) crates on distinct free cells
+ * (no wall, no brick, not in the exclusion set) chosen uniformly at random,
+ * mark them recycled and clear the pending count.  Same rule as
+ * BatchedSim.flush_recycle (sim/torch_sim.py:549-596), drawn from a
+ * counter-based RNG keyed by (seed, counter, env, player) instead of the
+ * host generator, so it needs no host round trip.
+ *   excl_bits  host array of ceil(C/32) words, bit c = excluded cell c */
+int qqt_flush_recycle(const QqtCfg *cfg, const QqtState *st, const uint32_t *excl_bits,
+                      uint64_t seed, uint64_t counter, qqt_stream_t stream);
+
 /* Danger map + shared observation + legal masks for the current state.
  * Replaces BatchedSim.observe (sim/torch_sim.py:605-627, encode_obs
  * sim/obs.py:48-136, danger_map sim/blast.py:158-317) and
@@ -211,16 +222,21 @@ int qqt_greedy_act(const QqtCfg *cfg, const QqtState *st, const void *obs,
  *   pack    weights packed by qqt_mlp_pack (256-byte aligned)
  *   obs     [N][obs_stride] fp16, obs_stride % 8 == 0, 16-byte aligned; the
  *           first k_in = C*H*W entries of each row are the observation
- *   mm, bm  [N][P][5], [N][P][2] masks of all seats
- *   n_seats 1 or 2 (must equal the pack's); pids[n_seats] host array
+ *   n_seats 1 or 2, the seats the pack was built for, in its order
+ *   mm, bm  host arrays of n_seats device pointers: seat s's move-mask row e
+ *           is at mm[s] + e*mm_stride (5 entries), bomb-mask row at
+ *           bm[s] + e*bm_stride (2 entries)
  *   u       [n_seats][N][2] uniforms (move, bomb)
- *   act     [N][P][2]: writes the listed seats; logp, value [n_seats][N];
- *   logits  [n_seats][N][8] (5 move, 2 bomb, value) or NULL
+ *   act     host array of n_seats device pointers; row e of seat s at
+ *           act[s] + e*act_stride (move, bomb int64)
+ *   logp, value [n_seats][N] (may be NULL); logits [n_seats][N][8]
+ *           (5 move, 2 bomb, value) or NULL
  *   work    device buffer of qqt_mlp_work_bytes(N, n_seats) bytes */
 int qqt_mlp_act(const void *pack, const void *obs, int32_t n_envs, int32_t obs_stride,
-                int32_t k_in, int32_t n_players, const uint8_t *mm, const uint8_t *bm,
-                int32_t n_seats, const int32_t *pids, const float *u, int64_t *act,
-                float *logp, float *value, float *logits, void *work, qqt_stream_t stream);
+                int32_t k_in, int32_t n_seats, const uint8_t *const *mm, int32_t mm_stride,
+                const uint8_t *const *bm, int32_t bm_stride, const float *u,
+                int64_t *const *act, int32_t act_stride, float *logp, float *value,
+                float *logits, void *work, qqt_stream_t stream);
 uint64_t qqt_mlp_work_bytes(int32_t n_envs, int32_t n_seats);
 
 /* Pack the fp32 parameters of one ActorCritic(mlp) for qqt_mlp_act.

@@ -362,11 +362,11 @@ __device__ __forceinline__ void ln_relu_32(float* x, const float* g, const float
 
 // 4 lanes per env row; lane part p holds features [32p, 32p+32).
 __global__ void __launch_bounds__(128)
-k_mlp_heads(const float* __restrict__ pre, int nt, int seat, int pid, int n_rows, int P,
-            const float* __restrict__ f, const uint8_t* __restrict__ mm,
-            const uint8_t* __restrict__ bm, const float* __restrict__ u, int64_t* __restrict__ act,
-            float* __restrict__ logp_out, float* __restrict__ value_out,
-            float* __restrict__ logits_out) {
+k_mlp_heads(const float* __restrict__ pre, int nt, int seat, int n_rows,
+            const float* __restrict__ f, const uint8_t* __restrict__ mm, int mm_stride,
+            const uint8_t* __restrict__ bm, int bm_stride, const float* __restrict__ u,
+            int64_t* __restrict__ act, int act_stride, float* __restrict__ logp_out,
+            float* __restrict__ value_out, float* __restrict__ logits_out) {
   __shared__ float xs[32][129];
   const int lane = lane_id(), part = lane & 3;
   const int lrow = threadIdx.x >> 2;                    // row within block (0..31)
@@ -450,8 +450,8 @@ k_mlp_heads(const float* __restrict__ pre, int nt, int seat, int pid, int n_rows
     for (int o = 0; o < 8; ++o) lo[o] = z[o];
   }
   const float lowest = -3.402823466e38f;
-  const uint8_t* mrow = mm + ((size_t)row * P + pid) * 5;
-  const uint8_t* brow = bm + ((size_t)row * P + pid) * 2;
+  const uint8_t* mrow = mm + (size_t)row * mm_stride;
+  const uint8_t* brow = bm + (size_t)row * bm_stride;
   // move head
   float zm[5], zb[2];
   float mx = lowest;
@@ -478,8 +478,8 @@ k_mlp_heads(const float* __restrict__ pre, int nt, int seat, int pid, int n_rows
   const float ub = u[((size_t)seat * n_rows + row) * 2 + 1] * s2;
   const int ab = ub > e0 ? 1 : 0;
   const float lpb = zb[ab] - mb - logf(s2);
-  act[((size_t)row * P + pid) * 2] = am;
-  act[((size_t)row * P + pid) * 2 + 1] = ab;
+  act[(size_t)row * act_stride] = am;
+  act[(size_t)row * act_stride + 1] = ab;
   if (logp_out) logp_out[(size_t)seat * n_rows + row] = lpm + lpb;
   if (value_out) value_out[(size_t)seat * n_rows + row] = z[7];
 }
@@ -598,13 +598,16 @@ extern "C" uint64_t qqt_mlp_work_bytes(int32_t n_envs, int32_t n_seats) {
 }
 
 extern "C" int qqt_mlp_act(const void* pack, const void* obs, int32_t n_envs, int32_t obs_stride,
-                           int32_t k_in, int32_t n_players, const uint8_t* mm, const uint8_t* bm,
-                           int32_t n_seats, const int32_t* pids, const float* u, int64_t* act,
-                           float* logp, float* value, float* logits, void* work,
-                           qqt_stream_t stream) {
-  if (!pack || !obs || !mm || !bm || !pids || !u || !act || !work) return QQT_E_ARG;
-  if (n_envs <= 0 || n_seats < 1 || n_seats > 2 || n_players < 2 || n_players > QQT_MAX_P)
+                           int32_t k_in, int32_t n_seats, const uint8_t* const* mm,
+                           int32_t mm_stride, const uint8_t* const* bm, int32_t bm_stride,
+                           const float* u, int64_t* const* act, int32_t act_stride, float* logp,
+                           float* value, float* logits, void* work, qqt_stream_t stream) {
+  if (!pack || !obs || !mm || !bm || !u || !act || !work) return QQT_E_ARG;
+  if (n_envs <= 0 || n_seats < 1 || n_seats > 2 || mm_stride < 5 || bm_stride < 2 ||
+      act_stride < 2)
     return QQT_E_ARG;
+  for (int s = 0; s < n_seats; ++s)
+    if (!mm[s] || !bm[s] || !act[s]) return QQT_E_ARG;
   if (obs_stride % 8 || obs_stride < k_in || ((uintptr_t)obs & 15) || ((uintptr_t)pack & 255))
     return QQT_E_ALIGN;
   const MlpPack L = mlp_pack_layout(k_in, n_seats);
@@ -630,8 +633,9 @@ extern "C" int qqt_mlp_act(const void* pack, const void* obs, int32_t n_envs, in
     k_mlp_gemm<256><<<grid, 192, GemmCfg<256>::kSmem, st>>>(ma, mb, n_envs, k_tiles, fpar + F_B0, pre);
   }
   for (int s = 0; s < n_seats; ++s) {
-    k_mlp_heads<<<(n_envs + 31) / 32, 128, 0, st>>>(pre, L.nt, s, pids[s], n_envs, n_players, fpar,
-                                                      mm, bm, u, act, logp, value, logits);
+    k_mlp_heads<<<(n_envs + 31) / 32, 128, 0, st>>>(pre, L.nt, s, n_envs, fpar, mm[s], mm_stride,
+                                                      bm[s], bm_stride, u, act[s], act_stride, logp,
+                                                      value, logits);
   }
   return launch_status();
 }

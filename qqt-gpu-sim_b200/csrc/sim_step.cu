@@ -542,9 +542,65 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
   store_tile(tile, st, N, e0, planes);
 }
 
+// Crate recycling on the device (sim/torch_sim.py:549-596 semantics with a
+// counter-based RNG): for each player with lost layers, pick
+// min(lost, available) distinct cells uniformly among free cells outside the
+// exclusion set by selection sampling, mark them crate + recycled, clear the
+// pending count.  One thread per env; planes read in SoA order (coalesced).
+struct ExclBits {
+  uint32_t w[(QQT_MAX_CELLS + 31) / 32];
+};
+
+__global__ void k_flush_recycle(QqtCfg cfg, QqtState st, ExclBits ex, uint64_t seed,
+                                uint64_t counter) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  const int N = cfg.n_envs, P = cfg.n_players, C = cfg.height * cfg.width;
+  if (e >= N) return;
+  for (int p = 0; p < P; ++p) {
+    const int64_t lost = st.pending_lost[(size_t)p * N + e];
+    if (lost <= 0) continue;
+    int avail = 0;
+    for (int c = 0; c < C; ++c) {
+      const size_t g = (size_t)c * N + e;
+      avail += !st.wall[g] && !st.brick[g] && !((ex.w[c >> 5] >> (c & 31)) & 1u);
+    }
+    int need = (int)min((int64_t)avail, lost);
+    int left = avail;
+    uint64_t key = seed ^ (counter * 0x9E3779B97F4A7C15ull) ^ ((uint64_t)e << 20) ^
+                   ((uint64_t)p << 52) ^ ((uint64_t)st.t[e] * 0xD1B54A32D192ED03ull);
+    for (int c = 0; c < C && need > 0; ++c) {
+      const size_t g = (size_t)c * N + e;
+      if (st.wall[g] || st.brick[g] || ((ex.w[c >> 5] >> (c & 31)) & 1u)) continue;
+      // select with probability need / left (Knuth's algorithm S)
+      const float u = hash_uniform(key + (uint64_t)c);
+      if (u * (float)left < (float)need) {
+        st.crate[g] = 1;
+        st.recycle[g] = 1;
+        --need;
+      }
+      --left;
+    }
+    st.pending_lost[(size_t)p * N + e] = 0;
+  }
+}
+
 }  // namespace qqt
 
 using namespace qqt;
+
+extern "C" int qqt_flush_recycle(const QqtCfg* cfg, const QqtState* st, const uint32_t* excl_bits,
+                                 uint64_t seed, uint64_t counter, qqt_stream_t stream) {
+  int rc = check_cfg(cfg);
+  if (rc) return rc;
+  if (!st || !excl_bits) return QQT_E_ARG;
+  ExclBits ex;
+  const int C = cfg->height * cfg->width;
+  memset(&ex, 0, sizeof(ex));
+  for (int i = 0; i < (C + 31) / 32; ++i) ex.w[i] = excl_bits[i];
+  const int N = cfg->n_envs;
+  k_flush_recycle<<<(N + 127) / 128, 128, 0, (cudaStream_t)stream>>>(*cfg, *st, ex, seed, counter);
+  return launch_status();
+}
 
 extern "C" uint64_t qqt_step_scratch_bytes(const QqtCfg* cfg) {
   if (!cfg) return 0;

@@ -81,15 +81,16 @@ def lib():
                                        c_p, c_p, c_f32, c_p, c_i32, c_p]),
             "qqt_greedy_act": (c_i32, [P(QqtCfg), P(QqtState), c_p, c_p, c_i32, c_p, c_i32,
                                        c_i32, c_p, c_p, c_i32, c_p]),
+            "qqt_flush_recycle": (c_i32, [P(QqtCfg), P(QqtState), c_p, c_u64, c_u64, c_p]),
             "qqt_get_error": (c_i32, [P(ctypes.c_uint32)]),
             "qqt_version": (ctypes.c_char_p, []),
         }
         optional = {
-            "qqt_mlp_act": (c_i32, [c_p, c_p, c_i32, c_i32, c_i32, c_p, c_p, c_i32, c_p,
-                                    c_p, c_p, c_p, c_p, c_p, c_p]),
-            "qqt_mlp_pack": (c_i32, [c_p, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_p,
-                                     c_p, c_p]),
+            "qqt_mlp_act": (c_i32, [c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_p, c_i32, c_p,
+                                    c_i32, c_p, c_p, c_i32, c_p, c_p, c_p, c_p, c_p]),
+            "qqt_mlp_pack": (c_i32, [c_p, c_i32, c_i32, c_i32, c_i32, c_i32, c_p, c_p, c_p]),
             "qqt_mlp_pack_bytes": (c_u64, [c_i32, c_i32]),
+            "qqt_mlp_work_bytes": (c_u64, [c_i32, c_i32]),
             "qqt_mlp_param_names": (ctypes.c_char_p, []),
         }
         for name, (res, args) in list(sig.items()) + list(optional.items()):

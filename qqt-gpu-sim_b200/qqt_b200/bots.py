@@ -46,11 +46,14 @@ class _Bot:
             return torch.rand(shape, device=self.sim.device)
         return torch.randint(lo, hi, shape, device=self.sim.device)
 
-    def _io(self, mmask, bmask):
+    def _io(self, mmask, bmask, out=None):
         mm, mp, ms = _rows(_as_u8(mmask), 5)
         bm, bp, bs = _rows(_as_u8(bmask), 2)
-        act = torch.empty((self.sim.num_envs, 2), dtype=torch.int64, device=self.sim.device)
-        return (mm, bm), mp, ms, bp, bs, act
+        if out is None:
+            out = torch.empty((self.sim.num_envs, 2), dtype=torch.int64, device=self.sim.device)
+        elif out.dtype != torch.int64 or out.stride(1) != 1:
+            raise ValueError("out must be an int64 (N, 2) view with unit inner stride")
+        return (mm, bm), mp, ms, bp, bs, out
 
     def __repr__(self):
         return f"B200Bot({self.name})"
@@ -63,16 +66,17 @@ class RandomBot(_Bot):
         super().__init__(sim, "random")
         self.bomb_rate = bomb_rate
 
-    def act(self, obs, mmask, bmask, pid: int):
+    def act(self, obs, mmask, bmask, pid: int, out=None):
         n = self.sim.num_envs
-        keep, mp, ms, bp, bs, act = self._io(mmask, bmask)
+        keep, mp, ms, bp, bs, act = self._io(mmask, bmask, out)
         u_move = self._take("u_move", (n,))
         u_bomb = self._take("u_bomb", (n,))
         self._fed = None
         s = self.sim
         rc = capi.lib().qqt_random_act(ctypes.byref(s._ccfg), ctypes.byref(s._cstate), mp, ms,
                                        bp, bs, pid, u_move.data_ptr(), u_bomb.data_ptr(),
-                                       float(self.bomb_rate), act.data_ptr(), 2, s._stream())
+                                       float(self.bomb_rate), act.data_ptr(), act.stride(0),
+                                       s._stream())
         capi.check(rc, "qqt_random_act")
         return act
 
@@ -83,16 +87,16 @@ class GreedyBot(_Bot):
     def __init__(self, sim):
         super().__init__(sim, "greedy")
 
-    def act(self, obs, mmask, bmask, pid: int):
+    def act(self, obs, mmask, bmask, pid: int, out=None):
         n = self.sim.num_envs
-        keep, mp, ms, bp, bs, act = self._io(mmask, bmask)
+        keep, mp, ms, bp, bs, act = self._io(mmask, bmask, out)
         noise = self._take("noise", (n, 5))
         self._fed = None
         s = self.sim
         o = _obs_ptr(s, obs)
         rc = capi.lib().qqt_greedy_act(ctypes.byref(s._ccfg), ctypes.byref(s._cstate), o, mp, ms,
-                                       bp, bs, pid, noise.data_ptr(), act.data_ptr(), 2,
-                                       s._stream())
+                                       bp, bs, pid, noise.data_ptr(), act.data_ptr(),
+                                       act.stride(0), s._stream())
         capi.check(rc, "qqt_greedy_act")
         return act
 
@@ -111,10 +115,10 @@ class AstarBot(_Bot):
         self.vopp = None
         self.keep_fields = False
 
-    def act(self, obs, mmask, bmask, pid: int):
+    def act(self, obs, mmask, bmask, pid: int, out=None):
         s = self.sim
         n, hw = s.num_envs, s.cfg.n_cells
-        keep, mp, ms, bp, bs, act = self._io(mmask, bmask)
+        keep, mp, ms, bp, bs, act = self._io(mmask, bmask, out)
         mode_p = timer_p = nm_p = nt_p = None
         tick16 = 0
         if self.use_mode:
@@ -140,7 +144,7 @@ class AstarBot(_Bot):
         o = _obs_ptr(s, obs)
         rc = capi.lib().qqt_astar_act(ctypes.byref(s._ccfg), ctypes.byref(s._cstate), o, mp, ms,
                                       bp, bs, pid, noise.data_ptr(), mode_p, timer_p, tick16,
-                                      nm_p, nt_p, act.data_ptr(), 2, vs, vo,
+                                      nm_p, nt_p, act.data_ptr(), act.stride(0), vs, vo,
                                       self._scratch.data_ptr(), s._stream())
         capi.check(rc, "qqt_astar_act")
         return act
@@ -178,8 +182,10 @@ class IdleBot(_Bot):
     def __init__(self, sim):
         super().__init__(sim, "idle")
 
-    def act(self, obs, mmask, bmask, pid: int):
+    def act(self, obs, mmask, bmask, pid: int, out=None):
         n = self.sim.num_envs
-        out = torch.zeros((n, 2), dtype=torch.int64, device=self.sim.device)
+        if out is None:
+            out = torch.zeros((n, 2), dtype=torch.int64, device=self.sim.device)
         out[:, 0] = 4
+        out[:, 1] = 0
         return out

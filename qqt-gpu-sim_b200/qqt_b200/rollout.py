@@ -1,0 +1,154 @@
+"""Rollout collection on the device: the B200 counterpart of
+SelfPlayRunner.collect (train/ppo.py:197-314).
+
+Tick protocol (ppo.py:213-271): observe -> legal masks -> learner act ->
+opponent act -> step(auto_reset) -> crate recycling every 16 ticks.  Every
+kernel writes straight into its row of a device-resident rollout buffer
+(observation rows, masks, actions, log-probs, values, rewards, done flags),
+so a tick moves no data besides what the kernels themselves read and write,
+and the whole T-tick rollout can be captured into one CUDA graph.
+
+Random draws for a rollout (learner sampling uniforms, bot noise, the astar
+mode-ticker integers, crate-pickup uniforms) are inputs in `RolloutDraws`;
+`RolloutDraws.generate` fills them on the device.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from .bots import AstarBot, GreedyBot, RandomBot
+from .policy import B200Policy
+
+
+class DeviceRolloutBuffer:
+    """(T, N, ...) buffers; obs rows keep the engine's padded stride."""
+
+    def __init__(self, T, n, p, n_seats, obs_stride, obs_shape, device):
+        d = torch.device(device)
+        self.T, self.n, self.p = T, n, p
+        self.obs_shape = obs_shape
+        self.obs_rows = torch.zeros((T, n, obs_stride), dtype=torch.float16, device=d)
+        self.mm = torch.ones((T, n, p, 5), dtype=torch.bool, device=d)
+        self.bm = torch.ones((T, n, p, 2), dtype=torch.bool, device=d)
+        self.act = torch.zeros((T, n, p, 2), dtype=torch.int64, device=d)
+        self.logp = torch.zeros((T, n_seats, n), dtype=torch.float32, device=d)
+        self.val = torch.zeros((T, n_seats, n), dtype=torch.float32, device=d)
+        self.rew = torch.zeros((T, n, p), dtype=torch.float32, device=d)
+        self.done = torch.zeros((T, n), dtype=torch.bool, device=d)
+
+    def obs(self, t):
+        c, h, w = self.obs_shape
+        return self.obs_rows[t, :, : c * h * w].view(self.n, c, h, w)
+
+
+@dataclass
+class RolloutDraws:
+    u_net: torch.Tensor        # (T, S, N, 2)
+    noise: torch.Tensor        # (T, N, 5)   opponent bot noise / random-bot uniforms
+    crate: torch.Tensor        # (T, 2, N, P) crate-pickup uniforms (hit, grow)
+    tick_mode: torch.Tensor    # (T // 16 + 1, N) astar ticker new modes
+    tick_timer: torch.Tensor   # (T // 16 + 1, N) astar ticker new timers
+
+    @staticmethod
+    def empty(T, n, p, n_seats, device):
+        d = torch.device(device)
+        k = T // 16 + 1
+        return RolloutDraws(torch.zeros((T, n_seats, n, 2), device=d),
+                            torch.zeros((T, n, 5), device=d),
+                            torch.zeros((T, 2, n, p), device=d),
+                            torch.zeros((k, n), dtype=torch.int64, device=d),
+                            torch.zeros((k, n), dtype=torch.int64, device=d))
+
+    def generate(self, gen: torch.Generator | None = None) -> None:
+        for t in (self.u_net, self.noise, self.crate):
+            t.uniform_(generator=gen)
+        self.tick_mode.random_(0, 2, generator=gen)
+        self.tick_timer.random_(60, 240, generator=gen)
+
+    def tensors(self):
+        return [self.u_net, self.noise, self.crate, self.tick_mode, self.tick_timer]
+
+
+class Rollout:
+    """T-tick collection of `sim` with a B200Policy learner and an opponent.
+
+    learner: B200Policy whose seats are the learning/network seats (one seat
+    vs a bot, or both seats for self-play); opponent: a bot from
+    qqt_b200.bots for the remaining seat, or None for self-play.
+    """
+
+    def __init__(self, sim, learner: B200Policy, opponent=None, T: int = 128,
+                 flush_every: int = 16):
+        self.sim, self.learner, self.opponent = sim, learner, opponent
+        self.T = T
+        self.flush_every = flush_every
+        cfg = sim.cfg
+        self.p = cfg.n_players
+        self.seats = learner.seats
+        self.opp_seat = next(i for i in range(self.p) if i not in self.seats) \
+            if opponent is not None else None
+        self.buf = DeviceRolloutBuffer(T, sim.num_envs, self.p, len(self.seats),
+                                       sim.obs_stride, cfg.obs_shape, sim.device)
+        self.draws = RolloutDraws.empty(T, sim.num_envs, self.p, len(self.seats), sim.device)
+        self.graph = None
+
+    def tick(self, t: int) -> None:
+        sim, buf, dr = self.sim, self.buf, self.draws
+        obs, mm, bm = sim.observe_and_mask(buf.obs_rows[t], buf.mm[t], buf.bm[t], danger=False)
+        acts = buf.act[t]
+        self.learner.act_seats(obs, [mm[:, s] for s in self.seats], [bm[:, s] for s in self.seats],
+                               dr.u_net[t], [acts[:, s] for s in self.seats], buf.logp[t],
+                               buf.val[t])
+        if self.opponent is not None:
+            o = self.opp_seat
+            bot = self.opponent
+            if isinstance(bot, AstarBot):
+                feed = {"noise": dr.noise[t]}
+                if bot.use_mode and (bot.calls + 1) % 16 == 0:
+                    k = (bot.calls + 1) // 16
+                    feed["new_mode"] = dr.tick_mode[k % dr.tick_mode.shape[0]]
+                    feed["new_timer"] = dr.tick_timer[k % dr.tick_timer.shape[0]]
+                bot.feed(**feed)
+            elif isinstance(bot, GreedyBot):
+                bot.feed(noise=dr.noise[t])
+            elif isinstance(bot, RandomBot):
+                bot.feed(u_move=dr.noise[t, :, 0], u_bomb=dr.noise[t, :, 1])
+            bot.act(obs, mm[:, o], bm[:, o], o, out=acts[:, o])
+        sim.step(acts, auto_reset=True, crate_draws=(dr.crate[t, 0], dr.crate[t, 1]),
+                 reward_out=buf.rew[t], done_out=buf.done[t])
+        if self.flush_every and t % self.flush_every == self.flush_every - 1:
+            sim.flush_recycle()
+
+    def collect(self) -> DeviceRolloutBuffer:
+        """Run T ticks eagerly (kernel launches only; no host synchronisation
+        when the sim resets on the device)."""
+        for t in range(self.T):
+            self.tick(t)
+        return self.buf
+
+    def capture(self) -> None:
+        """Capture one full T-tick rollout into a CUDA graph (call after at
+        least one eager tick so first-step set-up is done)."""
+        if isinstance(self.opponent, AstarBot) and self.opponent.mode is None:
+            raise RuntimeError("run one eager tick before capture (ticker init)")
+        s = torch.cuda.Stream(self.sim.device)
+        s.wait_stream(torch.cuda.current_stream(self.sim.device))
+        g = torch.cuda.CUDAGraph()
+        calls0 = self.opponent.calls if isinstance(self.opponent, AstarBot) else 0
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                self.collect()
+        torch.cuda.current_stream(self.sim.device).wait_stream(s)
+        if isinstance(self.opponent, AstarBot):
+            self.opponent.calls = calls0   # capture did not run the ticks
+        self.graph = g
+
+    def replay(self) -> DeviceRolloutBuffer:
+        """Replay the captured rollout (T ticks)."""
+        self.graph.replay()
+        if isinstance(self.opponent, AstarBot):
+            self.opponent.calls += self.T
+        return self.buf

@@ -109,6 +109,7 @@ class B200Sim:
             raise RuntimeError("B200Sim runs on a CUDA device only (no CPU fallback)")
         capi.lib()
         self.gen = torch.Generator(device="cpu").manual_seed(seed)
+        self._flush_seed = (int(seed) * 0x2545F4914F6CDD1D + 0x1234567) & ((1 << 64) - 1)
         h, w, p = cfg.height, cfg.width, cfg.n_players
         hw = h * w
         d = self.device
@@ -435,13 +436,22 @@ class B200Sim:
         c = cfg.n_channels * cfg.n_cells
         return self._obs[:, :c].view(self.num_envs, cfg.n_channels, cfg.height, cfg.width)
 
-    def observe_and_mask(self):
-        """observe() and legal_mask() in one launch."""
+    def observe_and_mask(self, obs_out=None, mm_out=None, bm_out=None, danger=True):
+        """observe() and legal_mask() in one launch.
+
+        obs_out (N, obs_stride) / mm_out (N,P,5) / bm_out (N,P,2): optional
+        contiguous slots (rollout-buffer rows) written directly."""
+        ob = self._obs if obs_out is None else obs_out
+        mm = self._mm if mm_out is None else mm_out
+        bm = self._bm if bm_out is None else bm_out
         capi.check(capi.lib().qqt_observe(ctypes.byref(self._ccfg), ctypes.byref(self._cstate),
-                                          self._obs.data_ptr(), self._danger.data_ptr(),
-                                          self._mm.data_ptr(), self._bm.data_ptr(),
-                                          self._stream()), "qqt_observe")
-        return self.obs_view(), self._mm, self._bm
+                                          ob.data_ptr(), self._danger.data_ptr() if danger else None,
+                                          mm.data_ptr(), bm.data_ptr(), self._stream()),
+                   "qqt_observe")
+        cfg = self.cfg
+        c = cfg.n_channels * cfg.n_cells
+        view = ob[:, :c].view(self.num_envs, cfg.n_channels, cfg.height, cfg.width)
+        return view, mm, bm
 
     def danger(self) -> torch.Tensor:
         """(N, H, W) float32 danger map computed by the last observe()."""
@@ -464,14 +474,30 @@ class B200Sim:
         r = torch.rand(n * p * 2, device=self.device).view(p, 2, n)
         return r[:, 0, :].t().contiguous(), r[:, 1, :].t().contiguous()
 
-    def step(self, actions: torch.Tensor, auto_reset: bool = True, crate_draws=None):
+    def step(self, actions: torch.Tensor, auto_reset: bool = True, crate_draws=None,
+             reward_out: torch.Tensor | None = None, done_out: torch.Tensor | None = None):
         """One tick (sim/torch_sim.py:895-1261) -> (reward (N,P), done (N,), info).
 
         With a template installed, done envs reset on the device inside the
         same kernel; otherwise auto_reset resets them on the host generator.
         `crate_draws`: optional (rb_hit, rb_grow) (N,P) float tensors.
+        `reward_out` (N,P) float32 / `done_out` (N,) bool: contiguous slots
+        (e.g. rollout-buffer rows) written directly instead of the engine's
+        own buffers.
         """
-        acts = actions.to(self.device, torch.int64).contiguous()
+        acts = actions
+        if acts.device != self.device or acts.dtype != torch.int64 or not acts.is_contiguous():
+            acts = acts.to(self.device, torch.int64).contiguous()
+        cout = self._cout
+        reward, done = self._reward, self._done
+        if reward_out is not None or done_out is not None:
+            cout = capi.QqtStepOut.from_buffer_copy(self._cout)
+            if reward_out is not None:
+                cout.reward = reward_out.data_ptr()
+                reward = reward_out
+            if done_out is not None:
+                cout.done = done_out.data_ptr()
+                done = done_out
         rb_hit = rb_grow = None
         if self.cfg.map_mode == "corridor":
             rb_hit, rb_grow = crate_draws if crate_draws is not None else self._crate_draws()
@@ -481,7 +507,7 @@ class B200Sim:
         rc = capi.lib().qqt_step(ctypes.byref(self._ccfg), ctypes.byref(self._cstate),
                                  acts.data_ptr(), capi.ptr(rb_hit), capi.ptr(rb_grow),
                                  self._tiers.data_ptr(), int(self._first_step),
-                                 ctypes.byref(self._cout),
+                                 ctypes.byref(cout),
                                  ctypes.byref(self._tmpl) if dev_reset else None,
                                  self._step_scratch.data_ptr(), self._stream())
         capi.check(rc, "qqt_step")
@@ -491,15 +517,30 @@ class B200Sim:
                 "blast": self._covered.t().view(n, h, w),
                 "trig": self._triggered.t().view(n, h, w)}
         if auto_reset and not dev_reset:
-            if bool(self._done.any()):
+            if bool(done.any()):
                 info = {k: v.clone() for k, v in info.items()}
-                self.reset_(self._done.clone())
-        return self._reward, self._done, info
+                self.reset_(done.clone())
+        return reward, done, info
 
     # ------------------------------------------------------------ recycle
-    def flush_recycle(self) -> None:
-        """Drop one crate per lost attribute layer on random free cells, host
-        generator draws in the reference's order (sim/torch_sim.py:549-596)."""
+    def flush_recycle(self, on_device: bool | None = None) -> None:
+        """Drop one crate per lost attribute layer on random free cells
+        (sim/torch_sim.py:549-596).
+
+        on_device=False (default without a template): host generator draws in
+        the reference's order, bit-compatible with the reference; True
+        (default with a template): one kernel, counter-based draws, no host
+        round trip."""
+        if on_device is None:
+            on_device = self._tmpl is not None
+        if on_device:
+            self._flush_count = getattr(self, "_flush_count", 0) + 1
+            words = (ctypes.c_uint32 * 14)(*self._excl_words())
+            rc = capi.lib().qqt_flush_recycle(ctypes.byref(self._ccfg), ctypes.byref(self._cstate),
+                                              words, int(self._flush_seed), self._flush_count,
+                                              self._stream())
+            capi.check(rc, "qqt_flush_recycle")
+            return
         cfg = self.cfg
         lost = self._buf["_pending_lost"]
         if not bool((lost.sum() > 0).item()):
@@ -530,6 +571,15 @@ class B200Sim:
                 self._buf["crate"][r, c] = True
                 self._buf["_recycle_crate"][r, c] = True
         lost.zero_()
+
+    def _excl_words(self):
+        w = getattr(self, "_excl_cache", None)
+        if w is None:
+            w = [0] * 14
+            for c in _recycle_exclusion(self.cfg):
+                w[c >> 5] |= 1 << (c & 31)
+            self._excl_cache = w
+        return w
 
     # --------------------------------------------------------- snapshots
     def state_dict(self) -> dict:

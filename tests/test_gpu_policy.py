@@ -1,0 +1,113 @@
+"""GPU parity of the MLP policy (tcgen05 first layer + fused heads).
+
+Contract: logits and values within 2e-3 relative to the largest reference
+magnitude of that output; sampled actions equal the oracle's inverse-CDF
+draw except where the uniform lands within float32 rounding of a CDF
+boundary (counted, must be 0 on these seeds).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import goldens as G
+
+pytestmark = pytest.mark.gpu
+REL_TOL = 2e-3
+
+if torch.cuda.is_available():
+    from oracle import qqt_oracle as O
+    from qqt_b200 import scenarios
+    from qqt_b200.config import SimConfig
+    from qqt_b200.policy import B200Policy
+    from qqt_b200.policy_init import init_params
+    from qqt_b200 import _capi
+
+
+@pytest.fixture(autouse=True)
+def _need_gpu():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    yield
+    torch.cuda.synchronize()
+    assert _capi.device_error() == 0, "device error word set"
+
+
+def _padded(obs16: np.ndarray) -> torch.Tensor:
+    n = obs16.shape[0]
+    k = obs16[0].size
+    stride = (k + 7) // 8 * 8
+    buf = torch.zeros((n, stride), dtype=torch.float16, device="cuda")
+    buf[:, :k] = torch.from_numpy(obs16.reshape(n, -1)).cuda()
+    return buf[:, :k].view(obs16.shape)
+
+
+def _rel(a, b):
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-12))
+
+
+def test_mlp_logits_vs_reference_goldens():
+    g = G.load("traj_cfg2")
+    cfg = SimConfig(**scenarios.CFG2)
+    params = init_params(cfg.obs_shape, "mlp", seed=1)
+    pol = B200Policy(params, cfg.obs_shape, 2, seats=(0,))
+    for i, t in enumerate(g["obs_ticks"][:8]):
+        obs = _padded(g["obs"][i])
+        mm = torch.from_numpy(g["mm"][t]).cuda()
+        bm = torch.from_numpy(g["bm"][t]).cuda()
+        u = torch.from_numpy(g["u_net"][t][:, 0].astype(np.float32)).cuda().view(1, -1, 2)
+        logits, acts, logp = pol.forward_logits(obs, mm, bm, u)
+        lg = logits[0].cpu().numpy()
+        assert _rel(lg[:, :5], g["logits_m"][t][:, 0]) <= REL_TOL
+        assert _rel(lg[:, 5:7], g["logits_b"][t][:, 0]) <= REL_TOL
+        assert _rel(lg[:, 7], g["value"][t][:, 0]) <= REL_TOL
+        assert np.array_equal(acts[0].cpu().numpy(), g["actions"][t][:, 0])
+        assert np.abs(logp[0].cpu().numpy() - g["logp"][t][:, 0]).max() <= 1e-4
+
+
+@pytest.mark.parametrize("seats", [(0,), (1,), (0, 1)])
+def test_mlp_full_size_vs_oracle(seats):
+    cfg = SimConfig(**scenarios.CFG2)
+    n, p = 5632, 2
+    rng = np.random.default_rng(7)
+    c, h, w = cfg.obs_shape
+    obs16 = (rng.random((n, c, h, w)) * (rng.random((n, c, h, w)) < 0.3)).astype(np.float16)
+    mm = rng.random((n, p, 5)) < 0.8
+    mm[..., 4] = True
+    bm = rng.random((n, p, 2)) < 0.7
+    bm[..., 0] = True
+    params = init_params(cfg.obs_shape, "mlp", seed=3)
+    pol = B200Policy(params, cfg.obs_shape, p, seats=seats)
+    u = rng.random((len(seats), n, 2)).astype(np.float32)
+    logits, acts, logp = pol.forward_logits(_padded(obs16), torch.from_numpy(mm).cuda(),
+                                            torch.from_numpy(bm).cuda(), torch.from_numpy(u).cuda())
+    lg = logits.cpu().numpy()
+    for s, pid in enumerate(seats):
+        ml, bl, v = O.mlp_forward(params, obs16.astype(np.float32), pid, p)
+        assert _rel(lg[s, :, :5], ml) <= REL_TOL, _rel(lg[s, :, :5], ml)
+        assert _rel(lg[s, :, 5:7], bl) <= REL_TOL
+        assert _rel(lg[s, :, 7], v) <= REL_TOL
+        a, lp, _, _, _ = O.mlp_act(params, obs16.astype(np.float32), mm[:, pid], bm[:, pid], pid,
+                                   p, u[s, :, 0], u[s, :, 1])
+        mismatch = int((acts[s].cpu().numpy() != a).any(-1).sum())
+        assert mismatch == 0, f"{mismatch} sampled actions differ"
+        assert np.abs(logp[s].cpu().numpy() - lp).max() <= 1e-3
+
+
+def test_mlp_ragged_tail_and_small_batch():
+    cfg = SimConfig(**scenarios.CFG2)
+    p = 2
+    params = init_params(cfg.obs_shape, "mlp", seed=5)
+    pol = B200Policy(params, cfg.obs_shape, p, seats=(0,))
+    rng = np.random.default_rng(11)
+    for n in (1, 37, 129, 300):
+        obs16 = rng.random((n,) + cfg.obs_shape).astype(np.float16)
+        mm = np.ones((n, p, 5), bool)
+        bm = np.ones((n, p, 2), bool)
+        logits, _, _ = pol.forward_logits(_padded(obs16), torch.from_numpy(mm).cuda(),
+                                          torch.from_numpy(bm).cuda())
+        ml, _, v = O.mlp_forward(params, obs16.astype(np.float32), 0, p)
+        assert _rel(logits[0, :, :5].cpu().numpy(), ml) <= REL_TOL
+        assert _rel(logits[0, :, 7].cpu().numpy(), v) <= REL_TOL
