@@ -148,6 +148,7 @@ int qqt_step(const QqtCfg *cfg, const QqtState *st, const int64_t *actions,
              void *scratch, qqt_stream_t stream);
 uint64_t qqt_step_scratch_bytes(const QqtCfg *cfg);
 
+
 /* Crate recycling on the device: for every player with pending lost
  * attribute layers, drop min(lost, free cells) crates on distinct free cells
  * (no wall, no brick, not in the exclusion set) chosen uniformly at random,
@@ -249,6 +250,15 @@ int qqt_mlp_pack(const float *const *params, int32_t k_in, int32_t n_players,
                  void *pack, qqt_stream_t stream);
 uint64_t qqt_mlp_pack_bytes(int32_t k_in, int32_t n_seats);
 const char *qqt_mlp_param_names(void);
+
+/* Generalised advantage estimation over a rollout buffer
+ * (train/ppo.py:101-110): rew [T] rows of rew_stride floats (row t, env e
+ * at rew[t*rew_stride + e]), done [T][N] uint8, val rows of val_stride,
+ * last_val [N]; writes adv, ret [T][N] float32.  Same float32 operation
+ * order as the reference loop. */
+int qqt_gae(const float *rew, int32_t rew_stride, const uint8_t *done, const float *val,
+            int32_t val_stride, const float *last_val, int32_t T, int32_t N, double gamma,
+            double lam, float *adv, float *ret, qqt_stream_t stream);
 
 /* Device error word: returns the accumulated QQT_DEV_* bits and clears
  * them (synchronises the device). */

@@ -252,11 +252,11 @@ struct MlpPack {
 enum {
   F_B0 = 0,                       // [NT] first-layer bias per seat column
   F_LN1G = F_B0 + 256, F_LN1B = F_LN1G + 128,
-  F_W1 = F_LN1B + 128,            // [128][128]
+  F_W1 = F_LN1B + 128,            // [128 in][128 out] (transposed)
   F_B1 = F_W1 + 128 * 128,
   F_LN2G = F_B1 + 128, F_LN2B = F_LN2G + 128,
-  F_HW0 = F_LN2B + 128,           // [3][64][128] move, bomb, critic hidden
-  F_HB0 = F_HW0 + 3 * 64 * 128,   // [3][64]
+  F_HW0 = F_LN2B + 128,           // [128 in][192 hidden] (transposed; move, bomb, critic)
+  F_HB0 = F_HW0 + 3 * 64 * 128,   // [192]
   F_HW2 = F_HB0 + 3 * 64,         // [8][64] rows: 5 move, 2 bomb, 1 value
   F_HB2 = F_HW2 + 8 * 64,         // [8]
   F_TOTAL = F_HB2 + 8
@@ -312,11 +312,15 @@ __global__ void k_mlp_pack_rest(HeadParams hp, int n_seats, float* __restrict__ 
     f[F_LN2G + i] = hp.ln2g[i];
     f[F_LN2B + i] = hp.ln2b[i];
   }
-  if (i < 128 * 128) f[F_W1 + i] = hp.w1[i];
+  if (i < 128 * 128) {
+    const int o = i / 128, k = i % 128;                 // w1 is [out][in]
+    f[F_W1 + k * 128 + o] = hp.w1[i];
+  }
   if (i < 64 * 128) {
-    f[F_HW0 + i] = hp.mw0[i];
-    f[F_HW0 + 64 * 128 + i] = hp.bw0[i];
-    f[F_HW0 + 2 * 64 * 128 + i] = hp.cw0[i];
+    const int o = i / 128, k = i % 128;                 // head weights [64][128]
+    f[F_HW0 + k * 192 + o] = hp.mw0[i];
+    f[F_HW0 + k * 192 + 64 + o] = hp.bw0[i];
+    f[F_HW0 + k * 192 + 128 + o] = hp.cw0[i];
   }
   if (i < 64) {
     f[F_HB0 + i] = hp.mb0[i];
@@ -336,8 +340,8 @@ __global__ void k_mlp_pack_rest(HeadParams hp, int n_seats, float* __restrict__ 
 
 // ---------------------------------------------------------------- heads
 
-// LayerNorm over 128 values spread as 32 per lane over a 4-lane group.
-__device__ __forceinline__ void ln_relu_32(float* x, const float* g, const float* b, int part) {
+// LayerNorm + ReLU over one row held as 32 features per lane by 4 lanes.
+__device__ __forceinline__ void ln_relu_4x32(float* x, const float* g, const float* b, int part) {
   float s = 0.f;
 #pragma unroll
   for (int i = 0; i < 32; ++i) s += x[i];
@@ -360,90 +364,148 @@ __device__ __forceinline__ void ln_relu_32(float* x, const float* g, const float
   }
 }
 
-// 4 lanes per env row; lane part p holds features [32p, 32p+32).
+constexpr int kHR = 32;   // env rows per heads block
+constexpr int kXS = 132;  // padded activation row (16-byte aligned, bank-skewed)
+
+// acc[r][j] += sum_k x[4rg+r][k] * W[k][o0 + j] for k in [0,128): float4
+// activations from shared memory, float4 weights (contiguous outputs).
+template <int NO, int LD>
+__device__ __forceinline__ void tile_matmul(float (*acc)[12], const float (*xs)[kXS], int rg,
+                                            const float* __restrict__ wt, int o0) {
+#pragma unroll 2
+  for (int k = 0; k < 128; k += 4) {
+    float4 a[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) a[r] = *reinterpret_cast<const float4*>(&xs[4 * rg + r][k]);
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      float wv[NO];
+#pragma unroll
+      for (int j = 0; j < NO; j += 4) {
+        const float4 q = __ldg(reinterpret_cast<const float4*>(wt + (k + kk) * LD + o0 + j));
+        wv[j] = q.x;
+        wv[j + 1] = q.y;
+        wv[j + 2] = q.z;
+        wv[j + 3] = q.w;
+      }
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const float av = kk == 0 ? a[r].x : kk == 1 ? a[r].y : kk == 2 ? a[r].z : a[r].w;
+#pragma unroll
+        for (int j = 0; j < NO; ++j) acc[r][j] = fmaf(wv[j], av, acc[r][j]);
+      }
+    }
+  }
+}
+
+// Register-blocked tail of the MLP: a block of 128 threads owns 32 rows.
+// Row-wise steps (LayerNorm) use 4 threads per row; in the two matrix steps
+// thread t owns rows 4*(t/16)..+3 and a contiguous run of outputs (8 of the
+// 128 layer-2 outputs, 12 of the 192 head units), so per 4 k-steps it issues
+// 4 shared float4 loads and 2-3 float4 weight loads for 128-192 FMAs.
 __global__ void __launch_bounds__(128)
 k_mlp_heads(const float* __restrict__ pre, int nt, int seat, int n_rows,
             const float* __restrict__ f, const uint8_t* __restrict__ mm, int mm_stride,
             const uint8_t* __restrict__ bm, int bm_stride, const float* __restrict__ u,
             int64_t* __restrict__ act, int act_stride, float* __restrict__ logp_out,
             float* __restrict__ value_out, float* __restrict__ logits_out) {
-  __shared__ float xs[32][129];
-  const int lane = lane_id(), part = lane & 3;
-  const int lrow = threadIdx.x >> 2;                    // row within block (0..31)
-  const int row = blockIdx.x * 32 + lrow;
-  const bool valid = row < n_rows;
-  float x[32];
-  const float* src = pre + (size_t)(valid ? row : 0) * nt + seat * 128 + part * 32;
+  __shared__ __align__(16) float xs[kHR][kXS];
+  const int t = threadIdx.x, lane = lane_id();
+  const int row0 = blockIdx.x * kHR;
+  // ---- LN1 (4 threads per row)
+  {
+    const int r = t >> 2, part = t & 3;
+    const int row = min(row0 + r, n_rows - 1);
+    const float* src = pre + (size_t)row * nt + seat * 128 + part * 32;
+    float x[32];
 #pragma unroll
-  for (int i = 0; i < 32; i += 4) {
-    const float4 t = *reinterpret_cast<const float4*>(src + i);
-    x[i] = t.x;
-    x[i + 1] = t.y;
-    x[i + 2] = t.z;
-    x[i + 3] = t.w;
-  }
-  ln_relu_32(x, f + F_LN1G, f + F_LN1B, part);
-#pragma unroll
-  for (int i = 0; i < 32; ++i) xs[lrow][part * 32 + i] = x[i];
-  __syncwarp();
-  // layer 2: this lane computes outputs [32p, 32p+32) from the full row
-  float y[32];
-  const float* w1 = f + F_W1;
-  for (int j = 0; j < 32; ++j) {
-    const int o = part * 32 + j;
-    float acc = __ldg(f + F_B1 + o);
-    const float* wr = w1 + o * 128;
-#pragma unroll 8
-    for (int k = 0; k < 128; k += 4) {
-      const float4 wv = __ldg(reinterpret_cast<const float4*>(wr + k));
-      acc = fmaf(wv.x, xs[lrow][k], acc);
-      acc = fmaf(wv.y, xs[lrow][k + 1], acc);
-      acc = fmaf(wv.z, xs[lrow][k + 2], acc);
-      acc = fmaf(wv.w, xs[lrow][k + 3], acc);
+    for (int i = 0; i < 32; i += 4) {
+      const float4 q = *reinterpret_cast<const float4*>(src + i);
+      x[i] = q.x;
+      x[i + 1] = q.y;
+      x[i + 2] = q.z;
+      x[i + 3] = q.w;
     }
-    y[j] = acc;
-  }
-  ln_relu_32(y, f + F_LN2G, f + F_LN2B, part);
-  __syncwarp();
+    ln_relu_4x32(x, f + F_LN1G, f + F_LN1B, part);
 #pragma unroll
-  for (int i = 0; i < 32; ++i) xs[lrow][part * 32 + i] = y[i];
-  __syncwarp();
-  // heads: 192 hidden units (3 heads x 64), 48 per lane; final layers summed
-  float outp[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int j = 0; j < 48; ++j) {
-    const int hu = part * 48 + j;            // 0..191
-    const int head = hu / 64, hi = hu % 64;
-    const float* wr = f + F_HW0 + (size_t)hu * 128;
-    float acc = __ldg(f + F_HB0 + hu);
-#pragma unroll 8
-    for (int k = 0; k < 128; k += 4) {
-      const float4 wv = __ldg(reinterpret_cast<const float4*>(wr + k));
-      acc = fmaf(wv.x, xs[lrow][k], acc);
-      acc = fmaf(wv.y, xs[lrow][k + 1], acc);
-      acc = fmaf(wv.z, xs[lrow][k + 2], acc);
-      acc = fmaf(wv.w, xs[lrow][k + 3], acc);
+    for (int i = 0; i < 32; ++i) xs[r][part * 32 + i] = x[i];
+  }
+  __syncthreads();
+  const int rg = t >> 4, og = t & 15;
+  float acc[4][12];
+  // ---- layer 2: outputs 8*og .. 8*og+7
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float bj = __ldg(f + F_B1 + 8 * og + j);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) acc[r][j] = bj;
+  }
+  tile_matmul<8, 128>(acc, xs, rg, f + F_W1, 8 * og);
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) xs[4 * rg + r][8 * og + j] = acc[r][j];
+  __syncthreads();
+  // ---- LN2 (4 threads per row)
+  {
+    const int r = t >> 2, part = t & 3;
+    float x[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) x[i] = xs[r][part * 32 + i];
+    ln_relu_4x32(x, f + F_LN2G, f + F_LN2B, part);
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) xs[r][part * 32 + i] = x[i];
+  }
+  __syncthreads();
+  // ---- heads hidden layer: units 12*og .. 12*og+11 (0..63 move, 64..127
+  //      bomb, 128..191 critic)
+#pragma unroll
+  for (int j = 0; j < 12; ++j) {
+    const float bj = __ldg(f + F_HB0 + 12 * og + j);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) acc[r][j] = bj;
+  }
+  tile_matmul<12, 192>(acc, xs, rg, f + F_HW0, 12 * og);
+  // ---- output layers: partial sums over this thread's units, then a
+  //      16-lane reduction inside the row group
+  const float* w2 = f + F_HW2;
+  float outp[4][8];
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int o = 0; o < 8; ++o) outp[r][o] = 0.f;
+#pragma unroll
+  for (int j = 0; j < 12; ++j) {
+    const int hu = 12 * og + j, head = hu >> 6, hi = hu & 63;
+    const int o_lo = head == 0 ? 0 : (head == 1 ? 5 : 7);
+    const int o_hi = head == 0 ? 5 : (head == 1 ? 7 : 8);
+#pragma unroll
+    for (int o = 0; o < 8; ++o) {
+      if (o < o_lo || o >= o_hi) continue;
+      const float wv = __ldg(w2 + o * 64 + hi);
+#pragma unroll
+      for (int r = 0; r < 4; ++r) outp[r][o] = fmaf(wv, fmaxf(acc[r][j], 0.f), outp[r][o]);
     }
-    acc = fmaxf(acc, 0.f);
-    const float* w2 = f + F_HW2;
-    if (head == 0) {
-#pragma unroll
-      for (int o = 0; o < 5; ++o) outp[o] = fmaf(__ldg(w2 + o * 64 + hi), acc, outp[o]);
-    } else if (head == 1) {
-#pragma unroll
-      for (int o = 5; o < 7; ++o) outp[o] = fmaf(__ldg(w2 + o * 64 + hi), acc, outp[o]);
-    } else {
-      outp[7] = fmaf(__ldg(w2 + 7 * 64 + hi), acc, outp[7]);
-    }
   }
 #pragma unroll
-  for (int o = 0; o < 8; ++o) {
-    outp[o] += __shfl_xor_sync(QQT_FULL, outp[o], 1);
-    outp[o] += __shfl_xor_sync(QQT_FULL, outp[o], 2);
-  }
-  if (!valid || part != 0) return;
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int o = 0; o < 8; ++o)
+#pragma unroll
+      for (int m = 1; m < 16; m <<= 1) outp[r][o] += __shfl_xor_sync(QQT_FULL, outp[r][o], m);
+  // ---- masking, sampling, log-prob: thread og < 4 of each row group takes row og
   float z[8];
 #pragma unroll
-  for (int o = 0; o < 8; ++o) z[o] = outp[o] + __ldg(f + F_HB2 + o);
+  for (int r = 0; r < 4; ++r)
+    if ((lane & 15) == r)
+#pragma unroll
+      for (int o = 0; o < 8; ++o) z[o] = outp[r][o];
+  const int row = row0 + 4 * rg + og;
+  if (og >= 4 || row >= n_rows) return;
+#pragma unroll
+  for (int o = 0; o < 8; ++o) z[o] += __ldg(f + F_HB2 + o);
   if (logits_out) {
     float* lo = logits_out + ((size_t)seat * n_rows + row) * 8;
 #pragma unroll
@@ -452,32 +514,34 @@ k_mlp_heads(const float* __restrict__ pre, int nt, int seat, int n_rows,
   const float lowest = -3.402823466e38f;
   const uint8_t* mrow = mm + (size_t)row * mm_stride;
   const uint8_t* brow = bm + (size_t)row * bm_stride;
-  // move head
-  float zm[5], zb[2];
+  float zm[5], cs[5];
   float mx = lowest;
+#pragma unroll
   for (int k = 0; k < 5; ++k) {
     zm[k] = mrow[k] ? z[k] : lowest;
     mx = fmaxf(mx, zm[k]);
   }
-  float cs[5], acc = 0.f;
+  float tot = 0.f;
+#pragma unroll
   for (int k = 0; k < 5; ++k) {
-    acc += expf(zm[k] - mx);
-    cs[k] = acc;
+    tot += expf(zm[k] - mx);
+    cs[k] = tot;
   }
-  const float um = u[((size_t)seat * n_rows + row) * 2] * acc;
+  const float um = u[((size_t)seat * n_rows + row) * 2] * tot;
   int am = 0;
+#pragma unroll
   for (int k = 0; k < 5; ++k) am += um > cs[k];
   am = min(am, 4);
-  const float lpm = zm[am] - mx - logf(acc);
-  float mb = lowest;
-  for (int k = 0; k < 2; ++k) {
-    zb[k] = brow[k] ? z[5 + k] : lowest;
-    mb = fmaxf(mb, zb[k]);
-  }
-  const float e0 = expf(zb[0] - mb), s2 = e0 + expf(zb[1] - mb);
+  float zam = zm[0];
+#pragma unroll
+  for (int k = 1; k < 5; ++k) zam = am == k ? zm[k] : zam;
+  const float lpm = zam - mx - logf(tot);
+  const float zb0 = brow[0] ? z[5] : lowest, zb1 = brow[1] ? z[6] : lowest;
+  const float mb = fmaxf(zb0, zb1);
+  const float e0 = expf(zb0 - mb), s2 = e0 + expf(zb1 - mb);
   const float ub = u[((size_t)seat * n_rows + row) * 2 + 1] * s2;
   const int ab = ub > e0 ? 1 : 0;
-  const float lpb = zb[ab] - mb - logf(s2);
+  const float lpb = (ab ? zb1 : zb0) - mb - logf(s2);
   act[(size_t)row * act_stride] = am;
   act[(size_t)row * act_stride + 1] = ab;
   if (logp_out) logp_out[(size_t)seat * n_rows + row] = lpm + lpb;
@@ -633,7 +697,7 @@ extern "C" int qqt_mlp_act(const void* pack, const void* obs, int32_t n_envs, in
     k_mlp_gemm<256><<<grid, 192, GemmCfg<256>::kSmem, st>>>(ma, mb, n_envs, k_tiles, fpar + F_B0, pre);
   }
   for (int s = 0; s < n_seats; ++s) {
-    k_mlp_heads<<<(n_envs + 31) / 32, 128, 0, st>>>(pre, L.nt, s, n_envs, fpar, mm[s], mm_stride,
+    k_mlp_heads<<<(n_envs + kHR - 1) / kHR, 128, 0, st>>>(pre, L.nt, s, n_envs, fpar, mm[s], mm_stride,
                                                       bm[s], bm_stride, u, act[s], act_stride, logp,
                                                       value, logits);
   }

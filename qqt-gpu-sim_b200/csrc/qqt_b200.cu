@@ -3,3 +3,4 @@
 #include "sim_observe.cu"
 #include "sim_step.cu"
 #include "policy_mlp.cu"
+#include "train_gae.cu"

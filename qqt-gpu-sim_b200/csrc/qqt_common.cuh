@@ -24,7 +24,7 @@
 #define QQT_MAX_W 21
 #define QQT_MAX_CELLS (QQT_MAX_H * QQT_MAX_W)
 #define QQT_MAX_P 4
-#define QQT_TILE_E 32
+#define QQT_TILE_E 8
 #define QQT_NWARP 8
 #define QQT_FULL 0xffffffffu
 

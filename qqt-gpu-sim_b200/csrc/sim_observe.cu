@@ -8,6 +8,8 @@
 // k_astar: warp per env; the two path fields share one warp (row / column
 //   sweeps to a fixed point, exactly the reference's Bellman-Ford limit).
 
+#include <type_traits>
+
 #include "qqt_common.cuh"
 
 namespace qqt {
@@ -29,29 +31,65 @@ struct PInfo {
   int64_t bombs_cap;
 };
 
-__host__ __device__ inline size_t observe_warp_bytes(int cells) {
-  // cur, front, spread, dng (float) + bombs (u16) + PInfo[4]
-  return ((size_t)cells * 16 + (size_t)cells * 2 + 15) / 16 * 16 + 4 * sizeof(PInfo) + 64;
+// Per-warp scratch of k_observe: stage-A weights and bomb list, then one
+// observation row staged in shared memory (the stage-A front/spread arrays
+// are dead by then and share its space), then the per-player values.
+struct ObsLayout {
+  size_t cur, bombs, row, pinfo, total;
+};
+
+__host__ __device__ inline size_t a16(size_t x) { return (x + 15) & ~(size_t)15; }
+
+__host__ __device__ inline ObsLayout obs_layout(int cells, int stride, int elem_bytes) {
+  ObsLayout L;
+  L.cur = 0;
+  L.bombs = a16((size_t)cells * 4);
+  L.row = a16(L.bombs + (size_t)cells * 2);
+  const size_t row_bytes = (size_t)stride * elem_bytes;
+  const size_t ab = (size_t)cells * 8;                  // front + spread
+  L.pinfo = a16(L.row + (row_bytes > ab ? row_bytes : ab));
+  L.total = a16(L.pinfo + QQT_MAX_P * sizeof(PInfo));
+  return L;
 }
+
+template <class T>
+__device__ __forceinline__ T to_obs(float v);
+template <>
+__device__ __forceinline__ float to_obs<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half to_obs<__half>(float v) { return __float2half_rn(v); }
+
+// Fuse tables (bit-identical to computing the IEEE division / weight per cell).
+struct FuseTables {
+  float weight[32], norm[32];
+};
 
 template <bool F32OUT>
 __global__ void __launch_bounds__(QQT_NWARP * 32)
 k_observe(QqtCfg cfg, QqtState st, void* obs, float* danger_out, uint8_t* mm, uint8_t* bm) {
+  using T = typename std::conditional<F32OUT, float, __half>::type;
   extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ FuseTables ft;
   const int h = cfg.height, w = cfg.width, C = h * w, N = cfg.n_envs, P = cfg.n_players;
   const int e0 = blockIdx.x * QQT_TILE_E;
+  if (threadIdx.x < 32) {
+    ft.weight[threadIdx.x] = fuse_weight(threadIdx.x, cfg.fuse_f);
+    ft.norm[threadIdx.x] = __fdiv_rn((float)threadIdx.x, cfg.fuse_f);
+  }
   Tile tile = carve_tile(smem, C);
   load_tile(tile, st, N, e0, PL_WALL | PL_BRICK | PL_CRATE | PL_OWNER | PL_FUSE | PL_BLAST);
   __syncthreads();
-  uint8_t* wb = smem + tile_bytes(C) + (size_t)warp_id() * observe_warp_bytes(C);
+  const ObsLayout L = obs_layout(C, cfg.obs_stride, (int)sizeof(T));
+  uint8_t* wb = smem + tile_bytes(C) + (size_t)warp_id() * L.total;
   DangerScratch ds;
-  ds.cur = (float*)wb;
-  ds.front = ds.cur + C;
+  ds.cur = (float*)(wb + L.cur);
+  ds.bombs = (uint16_t*)(wb + L.bombs);
+  ds.front = (float*)(wb + L.row);
   ds.spread = ds.front + C;
-  float* dng = ds.spread + C;
-  ds.bombs = (uint16_t*)(dng + C);
-  PInfo* pi = (PInfo*)(wb + ((size_t)C * 16 + (size_t)C * 2 + 15) / 16 * 16);
+  T* row = (T*)(wb + L.row);
+  PInfo* pi = (PInfo*)(wb + L.pinfo);
   const int lane = lane_id();
+  const int nch = cfg.obs_channels;
 
   for (int s = warp_id(); s < QQT_TILE_E; s += QQT_NWARP) {
     const int e = e0 + s;
@@ -59,12 +97,6 @@ k_observe(QqtCfg cfg, QqtState st, void* obs, float* danger_out, uint8_t* mm, ui
     const Env v = env_view(tile, s, h, w);
     int max_b = 0;
     danger_stage_a(v, ds, cfg.fuse_f, cfg.blast, cfg.danger_rounds, &max_b);
-    for (int c = lane; c < C; c += 32) {
-      const float d = danger_at(v, ds, c, cfg.blast, max_b);
-      dng[c] = d;
-      if (danger_out) danger_out[(size_t)e * C + c] = d;
-    }
-    // live bombs per player
     int cnt[QQT_MAX_P] = {0, 0, 0, 0};
     for (int c = lane; c < C; c += 32) {
       const int o = v.owner[c];
@@ -90,11 +122,11 @@ k_observe(QqtCfg cfg, QqtState st, void* obs, float* danger_out, uint8_t* mm, ui
       const float wys[2] = {__fsub_rn(1.f, wy), wy}, wxs[2] = {__fsub_rn(1.f, wx), wx};
       const int ys[2] = {y0, y1}, xs[2] = {x0, x1};
 #pragma unroll
-      for (int a = 0; a < 2; ++a)
+      for (int a2 = 0; a2 < 2; ++a2)
 #pragma unroll
-        for (int b = 0; b < 2; ++b) {
-          q.sc[a * 2 + b] = ys[a] * w + xs[b];
-          q.sw[a * 2 + b] = __fmul_rn(__fmul_rn(wys[a], wxs[b]), g);
+        for (int b2 = 0; b2 < 2; ++b2) {
+          q.sc[a2 * 2 + b2] = ys[a2] * w + xs[b2];
+          q.sw[a2 * 2 + b2] = __fmul_rn(__fmul_rn(wys[a2], wxs[b2]), g);
         }
       q.flat = center_cell(q.y, q.x, h, w);
       const int64_t inv = st.invuln[(size_t)p * N + e];
@@ -106,68 +138,48 @@ k_observe(QqtCfg cfg, QqtState st, void* obs, float* danger_out, uint8_t* mm, ui
       q.capv = __fmul_rn(__fdiv_rn(cap, cfg.obs_growth_bombs_max), g);
       pi[p] = q;
     }
-    __syncwarp();
+    __syncwarp();   // stage A done (front/spread dead), PInfo visible
 
-    if (obs) {
-      const float tv = __fdiv_rn((float)st.t[e], cfg.max_steps_f);
-      const int epc = F32OUT ? 4 : 8;
-      const int nchunk = cfg.obs_stride / epc;
-      const int ch_used = cfg.obs_channels;
-      for (int j = lane; j < nchunk; j += 32) {
-        float vals[8];
-        int i = j * epc;
-        int ch = i / C, cell = i - ch * C;
+    const float tv = __fdiv_rn((float)st.t[e], cfg.max_steps_f);
+    if (obs || danger_out) {
+      for (int c = lane; c < C; c += 32) {
+        const float d = danger_at(v, ds, c, cfg.blast, max_b);
+        if (danger_out) danger_out[(size_t)e * C + c] = d;
+        if (!obs) continue;
+        const int f = v.fuse[c], o = v.owner[c];
+        const float fn = f > 0 ? (f < 32 ? ft.norm[f] : __fdiv_rn((float)f, cfg.fuse_f)) : 0.f;
+        for (int p = 0; p < P; ++p) {
+          const PInfo& q = pi[p];
+          float sv = 0.f;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          if (k >= epc) break;
-          float val = 0.f;
-          if (ch < ch_used) {
-            if (ch < P) {
-              const PInfo& q = pi[ch];
-#pragma unroll
-              for (int m = 0; m < 4; ++m)
-                if (q.sc[m] == cell) val = __fadd_rn(val, q.sw[m]);
-            } else if (ch < 2 * P) {
-              const int f = v.fuse[cell];
-              if (f > 0 && v.owner[cell] == ch - P) val = __fdiv_rn((float)f, cfg.fuse_f);
-            } else if (ch == 2 * P) {
-              val = (v.wall[cell] | v.brick[cell]) ? 1.f : 0.f;
-            } else if (ch == 2 * P + 1) {
-              val = dng[cell];
-            } else if (ch == 2 * P + 2) {
-              val = tv;
-            } else if (ch == 2 * P + 3) {
-              val = v.crate[cell] ? 1.f : 0.f;
-            } else if (ch < 3 * P + 4) {
-              const PInfo& q = pi[ch - (2 * P + 4)];
-              if (q.flat == cell) val = q.inv;
-            } else if (ch < 4 * P + 4) {
-              const PInfo& q = pi[ch - (3 * P + 4)];
-              if (q.flat == cell) val = q.avail;
-            } else {
-              const PInfo& q = pi[ch - (4 * P + 4)];
-              if (q.flat == cell) val = q.capv;
-            }
-          }
-          vals[k] = val;
-          if (++cell == C) {
-            cell = 0;
-            ++ch;
-          }
+          for (int m = 0; m < 4; ++m)
+            if (q.sc[m] == c) sv = __fadd_rn(sv, q.sw[m]);
+          row[p * C + c] = to_obs<T>(sv);
+          row[(P + p) * C + c] = to_obs<T>((o == p && f > 0) ? fn : 0.f);
         }
-        if (F32OUT) {
-          float4 out4 = make_float4(vals[0], vals[1], vals[2], vals[3]);
-          reinterpret_cast<float4*>((float*)obs + (size_t)e * cfg.obs_stride)[j] = out4;
-        } else {
-          uint4 out4;
-          __half2 hh[4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            hh[k] = __halves2half2(__float2half_rn(vals[2 * k]), __float2half_rn(vals[2 * k + 1]));
-          memcpy(&out4, hh, 16);
-          reinterpret_cast<uint4*>((__half*)obs + (size_t)e * cfg.obs_stride)[j] = out4;
+        row[2 * P * C + c] = to_obs<T>((v.wall[c] | v.brick[c]) ? 1.f : 0.f);
+        row[(2 * P + 1) * C + c] = to_obs<T>(d);
+        row[(2 * P + 2) * C + c] = to_obs<T>(tv);
+        if (nch > 2 * P + 3) {
+          row[(2 * P + 3) * C + c] = to_obs<T>(v.crate[c] ? 1.f : 0.f);
+          for (int ch = 2 * P + 4; ch < nch; ++ch) row[ch * C + c] = to_obs<T>(0.f);
         }
       }
+    }
+    if (obs) {
+      for (int i = nch * C + lane; i < cfg.obs_stride; i += 32) row[i] = to_obs<T>(0.f);
+      __syncwarp();
+      if (lane < P && nch > 2 * P + 3) {
+        const PInfo& q = pi[lane];
+        row[(2 * P + 4 + lane) * C + q.flat] = to_obs<T>(q.inv);
+        row[(3 * P + 4 + lane) * C + q.flat] = to_obs<T>(q.avail);
+        row[(4 * P + 4 + lane) * C + q.flat] = to_obs<T>(q.capv);
+      }
+      __syncwarp();
+      const int nchunk = cfg.obs_stride * (int)sizeof(T) / 16;
+      const uint4* src = reinterpret_cast<const uint4*>(row);
+      uint4* dst = reinterpret_cast<uint4*>((uint8_t*)obs + (size_t)e * cfg.obs_stride * sizeof(T));
+      for (int j = lane; j < nchunk; j += 32) dst[j] = src[j];
     }
 
     if (mm) {
@@ -538,7 +550,8 @@ extern "C" int qqt_observe(const QqtCfg* cfg, const QqtState* st, void* obs, flo
     if (cfg->obs_stride % epc || cfg->obs_stride < cfg->obs_channels * C) return QQT_E_ALIGN;
     if (((uintptr_t)obs) & 15) return QQT_E_ALIGN;
   }
-  const size_t sm = tile_bytes(C) + QQT_NWARP * observe_warp_bytes(C);
+  const size_t sm = tile_bytes(C) +
+                   QQT_NWARP * obs_layout(C, cfg->obs_stride, cfg->obs_fp32 ? 4 : 2).total;
   const int blocks = (cfg->n_envs + QQT_TILE_E - 1) / QQT_TILE_E;
   if (cfg->obs_fp32) {
     cudaFuncSetAttribute(k_observe<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);

@@ -545,42 +545,72 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
 // Crate recycling on the device (sim/torch_sim.py:549-596 semantics with a
 // counter-based RNG): for each player with lost layers, pick
 // min(lost, available) distinct cells uniformly among free cells outside the
-// exclusion set by selection sampling, mark them crate + recycled, clear the
-// pending count.  One thread per env; planes read in SoA order (coalesced).
+// exclusion set -- every free cell draws a random key and the k smallest
+// keys win -- mark them crate + recycled, clear the pending count.
+// One warp per env, lanes over cells.
 struct ExclBits {
   uint32_t w[(QQT_MAX_CELLS + 31) / 32];
 };
 
 __global__ void k_flush_recycle(QqtCfg cfg, QqtState st, ExclBits ex, uint64_t seed,
                                 uint64_t counter) {
-  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  const int e = blockIdx.x * (blockDim.x >> 5) + warp_id();
   const int N = cfg.n_envs, P = cfg.n_players, C = cfg.height * cfg.width;
+  const int lane = lane_id();
   if (e >= N) return;
   for (int p = 0; p < P; ++p) {
     const int64_t lost = st.pending_lost[(size_t)p * N + e];
     if (lost <= 0) continue;
-    int avail = 0;
-    for (int c = 0; c < C; ++c) {
-      const size_t g = (size_t)c * N + e;
-      avail += !st.wall[g] && !st.brick[g] && !((ex.w[c >> 5] >> (c & 31)) & 1u);
+    const uint64_t key = seed ^ (counter * 0x9E3779B97F4A7C15ull) ^ ((uint64_t)e << 20) ^
+                         ((uint64_t)p << 52) ^ ((uint64_t)st.t[e] * 0xD1B54A32D192ED03ull);
+    // per-lane keys for its cells (up to 14 cells per lane for 21x21)
+    float kv[(QQT_MAX_CELLS + 31) / 32];
+    int nav = 0;
+#pragma unroll
+    for (int i = 0; i < (QQT_MAX_CELLS + 31) / 32; ++i) {
+      const int c = lane + 32 * i;
+      float k = 2.f;                                    // 2 = not available
+      if (c < C) {
+        const size_t g = (size_t)c * N + e;
+        if (!st.wall[g] && !st.brick[g] && !((ex.w[c >> 5] >> (c & 31)) & 1u)) {
+          k = hash_uniform(key + (uint64_t)c);
+          ++nav;
+        }
+      }
+      kv[i] = k;
     }
-    int need = (int)min((int64_t)avail, lost);
-    int left = avail;
-    uint64_t key = seed ^ (counter * 0x9E3779B97F4A7C15ull) ^ ((uint64_t)e << 20) ^
-                   ((uint64_t)p << 52) ^ ((uint64_t)st.t[e] * 0xD1B54A32D192ED03ull);
-    for (int c = 0; c < C && need > 0; ++c) {
-      const size_t g = (size_t)c * N + e;
-      if (st.wall[g] || st.brick[g] || ((ex.w[c >> 5] >> (c & 31)) & 1u)) continue;
-      // select with probability need / left (Knuth's algorithm S)
-      const float u = hash_uniform(key + (uint64_t)c);
-      if (u * (float)left < (float)need) {
+    nav = warp_sum(nav);
+    const int need = (int)min((int64_t)nav, lost);
+    for (int r = 0; r < need; ++r) {
+      float best = 2.f;
+      int bc = 0x7fffffff;
+#pragma unroll
+      for (int i = 0; i < (QQT_MAX_CELLS + 31) / 32; ++i)
+        if (kv[i] < best) {
+          best = kv[i];
+          bc = lane + 32 * i;
+        }
+      // warp argmin (ties -> lower cell)
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(QQT_FULL, best, o);
+        const int oc = __shfl_xor_sync(QQT_FULL, bc, o);
+        if (ob < best || (ob == best && oc < bc)) {
+          best = ob;
+          bc = oc;
+        }
+      }
+      if ((bc & 31) == lane) {
+        const size_t g = (size_t)bc * N + e;
         st.crate[g] = 1;
         st.recycle[g] = 1;
-        --need;
+#pragma unroll
+        for (int i = 0; i < (QQT_MAX_CELLS + 31) / 32; ++i)
+          if (lane + 32 * i == bc) kv[i] = 2.f;
       }
-      --left;
+      __syncwarp();
     }
-    st.pending_lost[(size_t)p * N + e] = 0;
+    if (lane == 0) st.pending_lost[(size_t)p * N + e] = 0;
   }
 }
 
@@ -598,7 +628,7 @@ extern "C" int qqt_flush_recycle(const QqtCfg* cfg, const QqtState* st, const ui
   memset(&ex, 0, sizeof(ex));
   for (int i = 0; i < (C + 31) / 32; ++i) ex.w[i] = excl_bits[i];
   const int N = cfg->n_envs;
-  k_flush_recycle<<<(N + 127) / 128, 128, 0, (cudaStream_t)stream>>>(*cfg, *st, ex, seed, counter);
+  k_flush_recycle<<<(N + 7) / 8, 256, 0, (cudaStream_t)stream>>>(*cfg, *st, ex, seed, counter);
   return launch_status();
 }
 
@@ -655,3 +685,4 @@ extern "C" int qqt_step(const QqtCfg* cfg, const QqtState* st, const int64_t* ac
   }
   return launch_status();
 }
+

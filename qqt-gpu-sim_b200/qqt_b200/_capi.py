@@ -82,6 +82,8 @@ def lib():
             "qqt_greedy_act": (c_i32, [P(QqtCfg), P(QqtState), c_p, c_p, c_i32, c_p, c_i32,
                                        c_i32, c_p, c_p, c_i32, c_p]),
             "qqt_flush_recycle": (c_i32, [P(QqtCfg), P(QqtState), c_p, c_u64, c_u64, c_p]),
+            "qqt_gae": (c_i32, [c_p, c_i32, c_p, c_p, c_i32, c_p, c_i32, c_i32, ctypes.c_double,
+                                ctypes.c_double, c_p, c_p, c_p]),
             "qqt_get_error": (c_i32, [P(ctypes.c_uint32)]),
             "qqt_version": (ctypes.c_char_p, []),
         }

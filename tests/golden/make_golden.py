@@ -405,6 +405,99 @@ def stress(R, cfg, n, seed):
     return out
 
 
+RESET_CFGS = {
+    "open_default": dict(),
+    "open_obstacles": dict(open_obstacle_max=6, height=11, width=11),
+    "corridor_default": dict(map_mode="corridor", speed=3.0, max_steps=1800),
+    "corridor_dense": dict(map_mode="corridor", wall_density=0.45, random_wall_rows=False),
+    "corridor_mixed": dict(map_mode="corridor", open_fraction=0.3, ring_fraction=0.3,
+                           pure_open_fraction=0.1, wall_density=0.25, open_obstacle_max=3),
+    "pillars_open": dict(wall_density=0.6, height=11, width=11),
+}
+
+
+def reset_modes(R):
+    """Initial states of BatchedSim(cfg, 24, seed=999) plus a second reset_ of
+    every other env, for several map modes (host generator parity)."""
+    import torch
+    out = {}
+    for name, kw in RESET_CFGS.items():
+        cfg = R["SimConfig"](**kw)
+        sim = R["ts"].BatchedSim(cfg, 24, device="cpu", seed=999)
+        for k, v in state_np(sim).items():
+            out[f"{name}__init__{k}"] = v
+        mask = torch.zeros(24, dtype=torch.bool)
+        mask[::2] = True
+        sim.reset_(mask)
+        for k, v in state_np(sim).items():
+            out[f"{name}__again__{k}"] = v
+    return out
+
+
+def ppo_golden(R):
+    """compute_gae + one ppo_update (2 epochs x 2 minibatches) of the
+    reference on a seeded 8-tick, 24-env buffer, minibatch permutations
+    recorded."""
+    import torch
+    import train.ppo as rppo
+    cfg = R["SimConfig"](**scenarios.CFG2)
+    T, n = 8, 24
+    rng = np.random.default_rng(21)
+    shp = (T, n) + tuple(cfg.obs_shape)
+    obs = (rng.random(shp) * (rng.random(shp) < 0.3)).astype(np.float16)
+    mm = rng.random((T, n, 5)) < 0.8
+    mm[..., 4] = True
+    bm = rng.random((T, n, 2)) < 0.7
+    bm[..., 0] = True
+    model = R["ActorCritic"](cfg.obs_shape, arch="mlp")
+    load_params(model, init_params(cfg.obs_shape, "mlp", seed=9))
+    buf = rppo.RolloutBuffer(T, n, cfg.obs_shape, "cpu", obs_dtype=torch.float16, arch="mlp")
+    with torch.no_grad():
+        for t in range(T):
+            o = torch.from_numpy(obs[t])
+            ml, bl, v = model(o, 0)
+            u = rng.random((n, 2))
+            am, l1 = masked_sample_np(ml.numpy(), mm[t], u[:, 0])
+            ab, l2 = masked_sample_np(bl.numpy(), bm[t], u[:, 1])
+            buf.add(o, torch.from_numpy(mm[t]), torch.from_numpy(bm[t]),
+                    torch.from_numpy(np.stack([am, ab], -1)),
+                    torch.from_numpy((l1 + l2).astype(np.float32)), v,
+                    torch.from_numpy(rng.normal(0, 0.5, n).astype(np.float32)),
+                    torch.from_numpy((rng.random(n) < 0.05).astype(np.float32)),
+                    torch.from_numpy(rng.random(n) < 0.1))
+    last_val = torch.from_numpy(rng.normal(0, 0.3, n).astype(np.float32))
+    adv, ret = rppo.compute_gae(buf, last_val, 0.995, 0.95)
+    pcfg = rppo.PPOConfig(epochs=2, minibatches=2, lr=1e-4)
+    opt = torch.optim.Adam(model.parameters(), lr=1e-4, eps=1e-5)
+    perms = []
+    real = rppo.torch
+
+    class PermTorch:
+        def randperm(self, k, device=None, **kw):
+            p = torch.from_numpy(rng.permutation(k).astype(np.int64))
+            perms.append(p.numpy().copy())
+            return p
+
+        def __getattr__(self, name):
+            return getattr(real, name)
+
+    rppo.torch = PermTorch()
+    try:
+        stats = rppo.ppo_update(model, opt, buf, last_val, pcfg, entropy_coef=0.03)
+    finally:
+        rppo.torch = real
+    out = {"obs": obs, "mm": mm, "bm": bm, "act": buf.act.numpy(), "logp": buf.logp.numpy(),
+           "val": buf.val.numpy(), "rew": buf.rew.numpy(), "done": buf.done.numpy(),
+           "dmg": buf.dmg.numpy(), "last_val": last_val.numpy(), "adv": adv.numpy(),
+           "ret": ret.numpy(), "n_perms": np.array(len(perms)),
+           "stats": np.array([stats[k] for k in ("pg", "vf", "ent", "kl", "clipfrac")])}
+    for i, p in enumerate(perms):
+        out[f"perm{i}"] = p
+    for k, v in model.state_dict().items():
+        out["param__" + k] = v.numpy().copy()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("QQT_REFERENCE_ROOT", "/root/reference"))
@@ -423,6 +516,8 @@ def main():
         "traj_cfg5": lambda: rollout(R, SC(**scenarios.CFG2), 8, 48, 3, "corridor",
                                      "cnn", "greedy", rng_seed=13, obs_every=8),
         "stress_cfg3": lambda: stress(R, SC(**scenarios.CFG1), 48, 5),
+        "reset_modes": lambda: reset_modes(R),
+        "ppo_update": lambda: ppo_golden(R),
     }
     for name, fn in jobs.items():
         if args.only and name not in args.only.split(","):
