@@ -148,6 +148,23 @@ int qqt_step(const QqtCfg *cfg, const QqtState *st, const int64_t *actions,
              void *scratch, qqt_stream_t stream);
 uint64_t qqt_step_scratch_bytes(const QqtCfg *cfg);
 
+/* qqt_step for callers that cannot allocate device memory (for example code
+ * running inside another runtime's stream capture, or an embedding that only
+ * hands this library pre-placed buffers).  No counterpart in the reference:
+ * it exists only for such callers.  Same arguments and results as qqt_step
+ * minus `scratch`: the scratch lives in a static device array of
+ * QQT_STEP_NOALLOC_MAX = 262144 bytes, so n_envs * n_players must not exceed
+ * it (else QQT_E_LIMIT).  The array is held by every GPU that loads the
+ * library until the process exits.  The first call on a device looks up the
+ * array's device address with that device current; make that first call
+ * before any stream capture.  All calls share the one array (the placement
+ * flags of the first-step pass are written before they are read, so nothing
+ * needs clearing): calls that overlap on the GPU race with each other.
+ * Allocates nothing. */
+int qqt_step_noalloc(const QqtCfg *cfg, const QqtState *st, const int64_t *actions,
+                     const float *rb_hit, const float *rb_grow, int32_t *tiers,
+                     int32_t first_step, const QqtStepOut *out, const QqtTemplate *tmpl,
+                     qqt_stream_t stream);
 
 /* Crate recycling on the device: for every player with pending lost
  * attribute layers, drop min(lost, free cells) crates on distinct free cells

@@ -686,3 +686,44 @@ extern "C" int qqt_step(const QqtCfg* cfg, const QqtState* st, const int64_t* ac
   return launch_status();
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free step.  Some callers cannot call cudaMalloc at all: code that
+// runs inside another runtime's stream capture, an embedding that hands this
+// library a fixed device budget, or a host without a device allocator hook.
+// qqt_step_noalloc gives them the same step as qqt_step with its scratch (the
+// per-player placement flags of the first-step pass) in a fixed static device
+// array instead of a caller buffer.  The array is QQT_STEP_NOALLOC_MAX bytes
+// (n_envs * n_players must fit); every GPU that loads the library holds it
+// until exit.
+#include <mutex>
+
+#define QQT_STEP_NOALLOC_MAX (256 * 1024)
+static __device__ __align__(256) uint8_t g_step_noalloc_scratch[QQT_STEP_NOALLOC_MAX];
+
+// Device address of the static array, looked up once per device with that
+// device current (in host code the array's name is only a host-side stand-in).
+static void* step_noalloc_ptr() {
+  static std::mutex mu;
+  static void* addr[128] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_step_noalloc_scratch) != cudaSuccess) return nullptr;
+    addr[dev] = p;
+  }
+  return addr[dev];
+}
+
+extern "C" int qqt_step_noalloc(const QqtCfg* cfg, const QqtState* st, const int64_t* actions,
+                                const float* rb_hit, const float* rb_grow, int32_t* tiers,
+                                int32_t first_step, const QqtStepOut* out,
+                                const QqtTemplate* tmpl, qqt_stream_t stream) {
+  int rc = check_cfg(cfg);
+  if (rc) return rc;
+  if ((uint64_t)cfg->n_envs * (uint64_t)cfg->n_players > QQT_STEP_NOALLOC_MAX) return QQT_E_LIMIT;
+  void* scratch = step_noalloc_ptr();
+  if (!scratch) return QQT_E_LAUNCH;
+  return qqt_step(cfg, st, actions, rb_hit, rb_grow, tiers, first_step, out, tmpl, scratch, stream);
+}
