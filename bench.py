@@ -185,7 +185,7 @@ def cpu_leg(n_envs, ticks, procs, seed=0):
 
 # ------------------------------------------------------------ GPU leg
 
-def build_engine(device, rank):
+def build_engine(device, rank, slots=None):
     import torch
     from qqt_b200 import scenarios
     from qqt_b200.bots import AstarBot
@@ -202,7 +202,7 @@ def build_engine(device, rank):
     pol = B200Policy(init_params(cfg.obs_shape, "mlp", seed=1), cfg.obs_shape, 2, seats=(0,),
                      device=device)
     bot = AstarBot(sim, mode=True)
-    ro = Rollout(sim, pol, bot, T=TICKS)
+    ro = Rollout(sim, pol, bot, T=TICKS, slots=slots)
     gen = torch.Generator(device=device).manual_seed(1234 + rank)
     return ro, gen
 
@@ -225,12 +225,13 @@ def instrumented_kernel_times(ro):
     bot = ro.opponent
     for t in range(ro.T):
         holder = {}
+        b = t % ro.slots
         timed("observe", lambda: holder.update(zip(("obs", "mm", "bm"), sim.observe_and_mask(
-            buf.obs_rows[t], buf.mm[t], buf.bm[t], danger=False))))
+            buf.obs_rows[b], buf.mm[b], buf.bm[b], danger=False))))
         obs, mm, bm = holder["obs"], holder["mm"], holder["bm"]
-        acts = buf.act[t]
+        acts = buf.act[b]
         timed("mlp", lambda: ro.learner.act_seats(obs, [mm[:, 0]], [bm[:, 0]], dr.u_net[t],
-                                                   [acts[:, 0]], buf.logp[t], buf.val[t]))
+                                                   [acts[:, 0]], buf.logp[b], buf.val[b]))
         feed = {"noise": dr.noise[t]}
         if (bot.calls + 1) % 16 == 0:
             feed["new_mode"], feed["new_timer"] = dr.tick_mode[0], dr.tick_timer[0]
@@ -238,7 +239,8 @@ def instrumented_kernel_times(ro):
         timed("astar", lambda: bot.act(obs, mm[:, 1], bm[:, 1], 1, out=acts[:, 1]))
         timed("step", lambda: sim.step(acts, auto_reset=True,
                                        crate_draws=(dr.crate[t, 0], dr.crate[t, 1]),
-                                       reward_out=buf.rew[t], done_out=buf.done[t]))
+                                       reward_out=buf.rew[b], done_out=buf.done[b],
+                                       info_planes=False))
         if t % 16 == 15:
             timed("flush", lambda: sim.flush_recycle())
     torch.cuda.synchronize()
@@ -259,7 +261,7 @@ def gpu_bench(args):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device(device))
-    ro, gen = build_engine(device, rank)
+    ro, gen = build_engine(device, rank, args.slots)
     sim, buf, dr = ro.sim, ro.buf, ro.draws
     # first tick eagerly (one-time set-up: resolve tiers, ticker state)
     dr.generate(gen)
@@ -304,7 +306,7 @@ def gpu_bench(args):
     # ---- e2e: public API with host-fed draws and a host read of the rewards
     host_draws = [t.detach().cpu().pin_memory() for t in dr.tensors()]
     h2d = sum(t.numel() * t.element_size() for t in host_draws)
-    rew_host = torch.empty((TICKS, N_ENVS), dtype=torch.float32).pin_memory()
+    rew_host = torch.empty((buf.rew.shape[0], N_ENVS), dtype=torch.float32).pin_memory()
     d2h = rew_host.numel() * 4
     e_evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
              for _ in range(args.steps)]
@@ -314,7 +316,7 @@ def gpu_bench(args):
         for dst, src in zip(dr.tensors(), host_draws):
             dst.copy_(src, non_blocking=True)
         ro.replay()
-        rew_host.copy_(buf.rew[:, :, 0], non_blocking=True)
+        rew_host[: buf.rew.shape[0]].copy_(buf.rew[:, :, 0], non_blocking=True)
         b.record()
         b.synchronize()
         l2.zero_()
@@ -449,6 +451,8 @@ def main():
     ap.add_argument("--ref-ticks", type=int, default=4)
     ap.add_argument("--envs", type=int, default=5632, help="envs per GPU (profiling cases)")
     ap.add_argument("--ticks", type=int, default=128, help="ticks per rollout (multiple of 16)")
+    ap.add_argument("--slots", type=int, default=0,
+                    help="rollout-buffer slots (0 = one per tick; fewer = ring, profiling only)")
     args = ap.parse_args()
     global N_ENVS, TICKS
     N_ENVS, TICKS = args.envs, args.ticks

@@ -268,6 +268,28 @@ int qqt_mlp_pack(const float *const *params, int32_t k_in, int32_t n_players,
 uint64_t qqt_mlp_pack_bytes(int32_t k_in, int32_t n_seats);
 const char *qqt_mlp_param_names(void);
 
+/* CNN policy (train/model.py:77-101, 187-196): conv0 3x3 (C -> 16, the
+ * seat's view permutation folded into its input channels) -> LN[16,H,W] ->
+ * ReLU -> conv 16->32 -> LN -> ReLU -> conv 32->64 -> LN -> ReLU -> conv 1x1
+ * 64->8 -> LN -> ReLU -> Linear(8HW->128), then the same tail as the MLP
+ * (LN, ReLU, 128x128, LN, ReLU, heads, masking, inverse-CDF sampling).
+ * Arguments as qqt_mlp_act; channels must be 14 (P = 2 layout);
+ * work = qqt_cnn_work_bytes(N, n_seats). */
+int qqt_cnn_act(const void *pack, const void *obs, int32_t n_envs, int32_t obs_stride,
+                int32_t height, int32_t width, int32_t channels, int32_t n_seats,
+                const uint8_t *const *mm, int32_t mm_stride, const uint8_t *const *bm,
+                int32_t bm_stride, const float *u, int64_t *const *act, int32_t act_stride,
+                float *logp, float *value, float *logits, void *work, qqt_stream_t stream);
+uint64_t qqt_cnn_work_bytes(int32_t n_envs, int32_t n_seats);
+
+/* Pack the fp32 parameters of one ActorCritic(cnn): params = 36 device
+ * pointers in the order of qqt_cnn_param_names() (reference state_dict
+ * keys); pids[n_seats] host array; pack = qqt_cnn_pack_bytes() bytes. */
+int qqt_cnn_pack(const float *const *params, int32_t n_players, int32_t channels, int32_t hw,
+                 int32_t n_seats, const int32_t *pids, void *pack, qqt_stream_t stream);
+uint64_t qqt_cnn_pack_bytes(int32_t channels, int32_t hw, int32_t n_seats);
+const char *qqt_cnn_param_names(void);
+
 /* Generalised advantage estimation over a rollout buffer
  * (train/ppo.py:101-110): rew [T] rows of rew_stride floats (row t, env e
  * at rew[t*rew_stride + e]), done [T][N] uint8, val rows of val_stride,

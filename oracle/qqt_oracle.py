@@ -845,6 +845,40 @@ def mlp_forward(params, obs, pid, p):
     return head("move_head"), head("bomb_head"), head("critic")[:, 0]
 
 
+def cnn_forward(params, obs, pid, p):
+    """float64 CNN forward -> (move_logits, bomb_logits, value) (train/model.py:77-101, 187-196).
+
+    Uses torch's float64 convolutions on the CPU as the accuracy reference.
+    """
+    import torch
+    import torch.nn.functional as F
+    T = lambda k: torch.from_numpy(np.asarray(params[k], dtype=np.float64))  # noqa: E731
+    n, c, h, w = obs.shape
+    base = 2 * p + 3
+    perm = [pid, p + pid] + [i for i in range(p) if i != pid] \
+        + [p + i for i in range(p) if i != pid] + [2 * p, 2 * p + 1, 2 * p + 2] + list(range(base, c))
+    inv = torch.from_numpy(np.argsort(np.asarray(perm)))
+    x = torch.from_numpy(obs.astype(np.float64))
+    x = F.conv2d(x, T("conv0.weight")[:, inv], T("conv0.bias"), padding=1)
+    for ln, conv, pad in (("conv.0", "conv.2", 1), ("conv.3", "conv.5", 1), ("conv.6", "conv.8", 0)):
+        g = T(ln + ".weight")
+        x = torch.relu(F.layer_norm(x, tuple(g.shape), g, T(ln + ".bias"), 1e-5))
+        x = F.conv2d(x, T(conv + ".weight"), T(conv + ".bias"), padding=pad)
+    g = T("conv.9.weight")
+    x = torch.relu(F.layer_norm(x, tuple(g.shape), g, T("conv.9.bias"), 1e-5)).reshape(n, -1)
+    z = x.numpy() @ np.asarray(params["shared.0.weight"], np.float64).T + params["shared.0.bias"]
+    z = np.maximum(_ln(z, params["shared.1.weight"], params["shared.1.bias"]), 0)
+    z = z @ np.asarray(params["shared.3.weight"], np.float64).T + params["shared.3.bias"]
+    z = np.maximum(_ln(z, params["shared.4.weight"], params["shared.4.bias"]), 0)
+
+    def head(name):
+        a = np.maximum(z @ np.asarray(params[f"{name}.0.weight"], np.float64).T
+                       + params[f"{name}.0.bias"], 0)
+        return a @ np.asarray(params[f"{name}.2.weight"], np.float64).T + params[f"{name}.2.bias"]
+
+    return head("move_head"), head("bomb_head"), head("critic")[:, 0]
+
+
 def masked_sample(logits, mask, u):
     """Inverse-CDF draw from the masked categorical (train/model.py:216-245).
 

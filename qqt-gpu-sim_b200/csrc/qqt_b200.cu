@@ -3,4 +3,5 @@
 #include "sim_observe.cu"
 #include "sim_step.cu"
 #include "policy_mlp.cu"
+#include "policy_cnn.cu"
 #include "train_gae.cu"

@@ -96,6 +96,13 @@ def lib():
             "qqt_mlp_pack_bytes": (c_u64, [c_i32, c_i32]),
             "qqt_mlp_work_bytes": (c_u64, [c_i32, c_i32]),
             "qqt_mlp_param_names": (ctypes.c_char_p, []),
+            "qqt_cnn_act": (c_i32, [c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_p,
+                                    c_i32, c_p, c_i32, c_p, c_p, c_i32, c_p, c_p, c_p, c_p,
+                                    c_p]),
+            "qqt_cnn_pack": (c_i32, [c_p, c_i32, c_i32, c_i32, c_i32, c_p, c_p, c_p]),
+            "qqt_cnn_pack_bytes": (c_u64, [c_i32, c_i32, c_i32]),
+            "qqt_cnn_work_bytes": (c_u64, [c_i32, c_i32]),
+            "qqt_cnn_param_names": (ctypes.c_char_p, []),
         }
         for name, (res, args) in list(sig.items()) + list(optional.items()):
             if name in optional and not hasattr(L, name):

@@ -23,6 +23,11 @@ PARAM_NAMES = ("shared.0.weight shared.0.bias shared.1.weight shared.1.bias shar
                "critic.0.bias critic.2.weight critic.2.bias").split()
 
 
+CNN_PARAM_NAMES = ("conv0.weight conv0.bias conv.0.weight conv.0.bias conv.2.weight conv.2.bias "
+                   "conv.3.weight conv.3.bias conv.5.weight conv.5.bias conv.6.weight conv.6.bias "
+                   "conv.8.weight conv.8.bias conv.9.weight conv.9.bias").split() + PARAM_NAMES
+
+
 def _rows(t: torch.Tensor, width: int):
     if t.dtype == torch.bool:
         t = t.view(torch.uint8)
@@ -32,14 +37,20 @@ def _rows(t: torch.Tensor, width: int):
 
 
 class B200Policy:
-    """MLP actor-critic for one or two seats sharing one observation.
+    """Actor-critic (arch "mlp" or "cnn") for one or two seats sharing one
+    observation.
 
     params: name -> tensor/ndarray (reference state_dict keys).
-    seats: the pids this pack serves; two seats run as one N=256 GEMM.
+    seats: the pids this pack serves; for the MLP two seats run as one
+    N=256 tensor-core GEMM.
     """
 
     def __init__(self, params: dict, obs_shape, n_players: int = 2, seats=(0,),
-                 device="cuda") -> None:
+                 device="cuda", arch: str = "mlp") -> None:
+        if arch not in ("mlp", "cnn"):
+            raise ValueError(f"unsupported arch {arch}")
+        self.arch = arch
+        self.names = PARAM_NAMES if arch == "mlp" else CNN_PARAM_NAMES
         self.device = torch.device(device)
         self.obs_shape = tuple(obs_shape)
         c, h, w = self.obs_shape
@@ -50,31 +61,39 @@ class B200Policy:
             raise ValueError("one or two seats per pack")
         self.params = {k: torch.as_tensor(np.asarray(params[k]) if not torch.is_tensor(params[k])
                                           else params[k]).to(self.device, torch.float32)
-                       .contiguous() for k in PARAM_NAMES}
+                       .contiguous() for k in self.names}
         L = capi.lib()
-        nbytes = int(L.qqt_mlp_pack_bytes(self.k_in, len(self.seats)))
+        if arch == "mlp":
+            nbytes = int(L.qqt_mlp_pack_bytes(self.k_in, len(self.seats)))
+        else:
+            nbytes = int(L.qqt_cnn_pack_bytes(c, h * w, len(self.seats)))
         self.pack = torch.zeros((nbytes,), dtype=torch.uint8, device=self.device)
         self._work = {}
         self.repack()
 
     def repack(self) -> None:
         L = capi.lib()
-        ptrs = (ctypes.c_void_p * 20)(*[self.params[k].data_ptr() for k in PARAM_NAMES])
+        ptrs = (ctypes.c_void_p * len(self.names))(*[self.params[k].data_ptr() for k in self.names])
         pids = (ctypes.c_int32 * 2)(*(list(self.seats) + [0] * (2 - len(self.seats))))
         c, h, w = self.obs_shape
-        rc = L.qqt_mlp_pack(ptrs, self.k_in, self.n_players, c, h * w, len(self.seats), pids,
-                            self.pack.data_ptr(), capi.stream_ptr(self.device))
-        capi.check(rc, "qqt_mlp_pack")
+        if self.arch == "mlp":
+            rc = L.qqt_mlp_pack(ptrs, self.k_in, self.n_players, c, h * w, len(self.seats), pids,
+                                self.pack.data_ptr(), capi.stream_ptr(self.device))
+        else:
+            rc = L.qqt_cnn_pack(ptrs, self.n_players, c, h * w, len(self.seats), pids,
+                                self.pack.data_ptr(), capi.stream_ptr(self.device))
+        capi.check(rc, "qqt_%s_pack" % self.arch)
 
     def load_state_dict(self, sd: dict) -> None:
-        for k in PARAM_NAMES:
+        for k in self.names:
             self.params[k].copy_(torch.as_tensor(sd[k]))
         self.repack()
 
     def _work_buf(self, n):
         buf = self._work.get(n)
         if buf is None:
-            nb = int(capi.lib().qqt_mlp_work_bytes(n, len(self.seats)))
+            fn = capi.lib().qqt_mlp_work_bytes if self.arch == "mlp" else capi.lib().qqt_cnn_work_bytes
+            nb = int(fn(n, len(self.seats)))
             buf = torch.empty((nb // 4,), dtype=torch.float32, device=self.device)
             self._work[n] = buf
         return buf
@@ -118,12 +137,20 @@ class B200Policy:
         mp = (ctypes.c_void_p * 2)(*([m.data_ptr() for m in mms] + [0] * (2 - S)))
         bp = (ctypes.c_void_p * 2)(*([b.data_ptr() for b in bms] + [0] * (2 - S)))
         ap = (ctypes.c_void_p * 2)(*([a.data_ptr() for a in acts] + [0] * (2 - S)))
-        rc = capi.lib().qqt_mlp_act(self.pack.data_ptr(), ob.data_ptr(), n, stride, self.k_in, S,
-                                    mp, mms[0].stride(0), bp, bms[0].stride(0), uu.data_ptr(), ap,
-                                    acts[0].stride(0), capi.ptr(logp), capi.ptr(value),
-                                    capi.ptr(logits), self._work_buf(n).data_ptr(),
-                                    capi.stream_ptr(self.device))
-        capi.check(rc, "qqt_mlp_act")
+        if self.arch == "mlp":
+            rc = capi.lib().qqt_mlp_act(self.pack.data_ptr(), ob.data_ptr(), n, stride, self.k_in,
+                                        S, mp, mms[0].stride(0), bp, bms[0].stride(0),
+                                        uu.data_ptr(), ap, acts[0].stride(0), capi.ptr(logp),
+                                        capi.ptr(value), capi.ptr(logits),
+                                        self._work_buf(n).data_ptr(), capi.stream_ptr(self.device))
+        else:
+            c, h, w = self.obs_shape
+            rc = capi.lib().qqt_cnn_act(self.pack.data_ptr(), ob.data_ptr(), n, stride, h, w, c, S,
+                                        mp, mms[0].stride(0), bp, bms[0].stride(0),
+                                        uu.data_ptr(), ap, acts[0].stride(0), capi.ptr(logp),
+                                        capi.ptr(value), capi.ptr(logits),
+                                        self._work_buf(n).data_ptr(), capi.stream_ptr(self.device))
+        capi.check(rc, "qqt_%s_act" % self.arch)
 
     def act(self, obs, move_mask, bomb_mask, pid: int = 0, u=None):
         """ActorCritic.act: (actions (B,2), logp (B,), value (B,)) for seat pid."""

@@ -81,7 +81,7 @@ class Rollout:
     """
 
     def __init__(self, sim, learner: B200Policy, opponent=None, T: int = 128,
-                 flush_every: int = 16):
+                 flush_every: int = 16, slots: int | None = None):
         self.sim, self.learner, self.opponent = sim, learner, opponent
         self.T = T
         self.flush_every = flush_every
@@ -90,18 +90,34 @@ class Rollout:
         self.seats = learner.seats
         self.opp_seat = next(i for i in range(self.p) if i not in self.seats) \
             if opponent is not None else None
-        self.buf = DeviceRolloutBuffer(T, sim.num_envs, self.p, len(self.seats),
+        # `slots` < T keeps only the last `slots` ticks (a ring), e.g. for
+        # profiling large env counts without a full T-tick buffer
+        self.slots = slots or T
+        self.buf = DeviceRolloutBuffer(self.slots, sim.num_envs, self.p, len(self.seats),
                                        sim.obs_stride, cfg.obs_shape, sim.device)
+        # the learner and the opponent both read only this tick's observation
+        # and masks: they run as two concurrent branches (policy on a side
+        # stream) that join before the step
+        self.side = torch.cuda.Stream(sim.device) if opponent is not None else None
         self.draws = RolloutDraws.empty(T, sim.num_envs, self.p, len(self.seats), sim.device)
         self.graph = None
 
     def tick(self, t: int) -> None:
         sim, buf, dr = self.sim, self.buf, self.draws
-        obs, mm, bm = sim.observe_and_mask(buf.obs_rows[t], buf.mm[t], buf.bm[t], danger=False)
-        acts = buf.act[t]
-        self.learner.act_seats(obs, [mm[:, s] for s in self.seats], [bm[:, s] for s in self.seats],
-                               dr.u_net[t], [acts[:, s] for s in self.seats], buf.logp[t],
-                               buf.val[t])
+        b = t % self.slots
+        obs, mm, bm = sim.observe_and_mask(buf.obs_rows[b], buf.mm[b], buf.bm[b], danger=False)
+        acts = buf.act[b]
+        main = torch.cuda.current_stream(sim.device)
+        if self.side is not None:
+            self.side.wait_stream(main)
+            with torch.cuda.stream(self.side):
+                self.learner.act_seats(obs, [mm[:, s] for s in self.seats],
+                                       [bm[:, s] for s in self.seats], dr.u_net[t],
+                                       [acts[:, s] for s in self.seats], buf.logp[b], buf.val[b])
+        else:
+            self.learner.act_seats(obs, [mm[:, s] for s in self.seats], [bm[:, s] for s in self.seats],
+                                   dr.u_net[t], [acts[:, s] for s in self.seats], buf.logp[b],
+                                   buf.val[b])
         if self.opponent is not None:
             o = self.opp_seat
             bot = self.opponent
@@ -117,8 +133,9 @@ class Rollout:
             elif isinstance(bot, RandomBot):
                 bot.feed(u_move=dr.noise[t, :, 0], u_bomb=dr.noise[t, :, 1])
             bot.act(obs, mm[:, o], bm[:, o], o, out=acts[:, o])
+            main.wait_stream(self.side)
         sim.step(acts, auto_reset=True, crate_draws=(dr.crate[t, 0], dr.crate[t, 1]),
-                 reward_out=buf.rew[t], done_out=buf.done[t])
+                 reward_out=buf.rew[b], done_out=buf.done[b], info_planes=False)
         if self.flush_every and t % self.flush_every == self.flush_every - 1:
             sim.flush_recycle()
 

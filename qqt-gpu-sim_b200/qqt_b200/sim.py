@@ -475,7 +475,8 @@ class B200Sim:
         return r[:, 0, :].t().contiguous(), r[:, 1, :].t().contiguous()
 
     def step(self, actions: torch.Tensor, auto_reset: bool = True, crate_draws=None,
-             reward_out: torch.Tensor | None = None, done_out: torch.Tensor | None = None):
+             reward_out: torch.Tensor | None = None, done_out: torch.Tensor | None = None,
+             info_planes: bool = True):
         """One tick (sim/torch_sim.py:895-1261) -> (reward (N,P), done (N,), info).
 
         With a template installed, done envs reset on the device inside the
@@ -483,15 +484,19 @@ class B200Sim:
         `crate_draws`: optional (rb_hit, rb_grow) (N,P) float tensors.
         `reward_out` (N,P) float32 / `done_out` (N,) bool: contiguous slots
         (e.g. rollout-buffer rows) written directly instead of the engine's
-        own buffers.
+        own buffers.  info_planes=False skips writing info["blast"] /
+        info["trig"] (the flame and exploded-bomb planes).
         """
         acts = actions
         if acts.device != self.device or acts.dtype != torch.int64 or not acts.is_contiguous():
             acts = acts.to(self.device, torch.int64).contiguous()
         cout = self._cout
         reward, done = self._reward, self._done
-        if reward_out is not None or done_out is not None:
+        if reward_out is not None or done_out is not None or not info_planes:
             cout = capi.QqtStepOut.from_buffer_copy(self._cout)
+            if not info_planes:
+                cout.covered = None
+                cout.triggered = None
             if reward_out is not None:
                 cout.reward = reward_out.data_ptr()
                 reward = reward_out

@@ -111,3 +111,42 @@ def test_mlp_ragged_tail_and_small_batch():
         ml, _, v = O.mlp_forward(params, obs16.astype(np.float32), 0, p)
         assert _rel(logits[0, :, :5].cpu().numpy(), ml) <= REL_TOL
         assert _rel(logits[0, :, 7].cpu().numpy(), v) <= REL_TOL
+
+
+def test_cnn_logits_vs_reference_goldens():
+    g = G.load("traj_cfg5")
+    cfg = SimConfig(**scenarios.CFG2)
+    params = init_params(cfg.obs_shape, "cnn", seed=3)
+    pol = B200Policy(params, cfg.obs_shape, 2, seats=(0,), arch="cnn")
+    for i, t in enumerate(g["obs_ticks"]):
+        obs = _padded(g["obs"][i])
+        mm = torch.from_numpy(g["mm"][t]).cuda()
+        bm = torch.from_numpy(g["bm"][t]).cuda()
+        u = torch.from_numpy(g["u_net"][t][:, 0].astype(np.float32)).cuda().view(1, -1, 2)
+        logits, acts, logp = pol.forward_logits(obs, mm, bm, u)
+        lg = logits[0].cpu().numpy()
+        assert _rel(lg[:, :5], g["logits_m"][t][:, 0]) <= REL_TOL
+        assert _rel(lg[:, 5:7], g["logits_b"][t][:, 0]) <= REL_TOL
+        assert _rel(lg[:, 7], g["value"][t][:, 0]) <= REL_TOL
+        assert np.array_equal(acts[0].cpu().numpy(), g["actions"][t][:, 0])
+
+
+@pytest.mark.parametrize("seats", [(0,), (0, 1)])
+def test_cnn_vs_oracle(seats):
+    cfg = SimConfig(**scenarios.CFG2)
+    n, p = 300, 2
+    rng = np.random.default_rng(17)
+    shp = (n,) + tuple(cfg.obs_shape)
+    obs16 = (rng.random(shp) * (rng.random(shp) < 0.3)).astype(np.float16)
+    mm = np.ones((n, p, 5), bool)
+    bm = np.ones((n, p, 2), bool)
+    params = init_params(cfg.obs_shape, "cnn", seed=4)
+    pol = B200Policy(params, cfg.obs_shape, p, seats=seats, arch="cnn")
+    logits, _, _ = pol.forward_logits(_padded(obs16), torch.from_numpy(mm).cuda(),
+                                      torch.from_numpy(bm).cuda())
+    lg = logits.cpu().numpy()
+    for s, pid in enumerate(seats):
+        ml, bl, v = O.cnn_forward(params, obs16.astype(np.float32), pid, p)
+        assert _rel(lg[s, :, :5], ml) <= REL_TOL
+        assert _rel(lg[s, :, 5:7], bl) <= REL_TOL
+        assert _rel(lg[s, :, 7], v) <= REL_TOL
