@@ -260,7 +260,9 @@ extern "C" int qqt_cnn_pack(const float* const* params_dev, int32_t n_players, i
   k_cnn_pack<<<(unsigned)((n_items + 255) / 256), 256, 0, st>>>(cp, channels, hw, n_seats, sc, pk);
   // shared tail (LN, 128x128, LN, heads) in the MLP pack's float layout
   HeadParams hp;
-  const float* const* q = params_dev + 17;   // q[1] = shared.0.bias, q[2] = shared.1.weight, ...
+  // q[] uses the MLP's parameter order: q[0] = shared.0.weight (index 16),
+  // q[1] = shared.0.bias, q[2] = shared.1.weight, ..., q[19] = critic.2.bias (35)
+  const float* const* q = params_dev + 16;
   hp.b0 = q[1];
   hp.ln1g = q[2];
   hp.ln1b = q[3];
