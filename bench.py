@@ -104,16 +104,8 @@ class ClockSampler:
 
 
 def _template(cfg, n, seed):
-    import numpy as np
     from qqt_b200 import scenarios
-    p = cfg.n_players
-    wall, brick = scenarios.pillar_corridor(n, cfg.height, cfg.width, seed=seed)
-    spawn = np.broadcast_to(np.array(scenarios.corner_spawns(cfg), np.float32), (n, p, 2)).copy()
-    return {"wall": wall, "brick": brick, "spawn": spawn,
-            "bombs_cap": np.full((n, p), cfg.growth_bombs_start, np.int64),
-            "blast_cap": np.full((n, p), cfg.growth_blast_start, np.int64),
-            "spd": np.full((n, p), cfg.growth_speed_start, np.float32),
-            "crate_prob": np.full((n,), cfg.growth_crate_prob, np.float32)}
+    return scenarios.corridor_template(cfg, n, seed)
 
 
 # --------------------------------------------------------------- CPU legs
@@ -185,26 +177,32 @@ def cpu_leg(n_envs, ticks, procs, seed=0):
 
 # ------------------------------------------------------------ GPU leg
 
-def build_engine(device, rank, slots=None):
+def build_engine(device, rank, slots=None, groups=1):
+    """The rank's env shard as `groups` independent env groups (one sim, astar
+    bot and rollout buffer each; one shared policy pack)."""
     import torch
     from qqt_b200 import scenarios
     from qqt_b200.bots import AstarBot
     from qqt_b200.config import SimConfig
     from qqt_b200.policy import B200Policy
     from qqt_b200.policy_init import init_params
-    from qqt_b200.rollout import Rollout
+    from qqt_b200.rollout import Rollout, RolloutGroups
     from qqt_b200.sim import B200Sim
     cfg = SimConfig(**scenarios.CFG2)
-    sim = B200Sim(cfg, N_ENVS, device=device, seed=1 + rank,
-                  template=_template(cfg, N_ENVS, 1 + rank))
-    sim.set_template(_template(cfg, N_ENVS, 1 + rank), apply=False, seed=1 + rank,
-                     swap_spawns=False)
+    if N_ENVS % groups:
+        raise ValueError("envs per GPU must divide into the groups")
+    n = N_ENVS // groups
+    tmpl = _template(cfg, N_ENVS, 1 + rank)
     pol = B200Policy(init_params(cfg.obs_shape, "mlp", seed=1), cfg.obs_shape, 2, seats=(0,),
                      device=device)
-    bot = AstarBot(sim, mode=True)
-    ro = Rollout(sim, pol, bot, T=TICKS, slots=slots)
+    ros = []
+    for g in range(groups):
+        part = {k: v[g * n:(g + 1) * n] for k, v in tmpl.items()}
+        sim = B200Sim(cfg, n, device=device, seed=1 + rank + 1000 * g, template=part)
+        sim.set_template(part, apply=False, seed=1 + rank + 1000 * g, swap_spawns=False)
+        ros.append(Rollout(sim, pol, AstarBot(sim, mode=True), T=TICKS, slots=slots))
     gen = torch.Generator(device=device).manual_seed(1234 + rank)
-    return ro, gen
+    return RolloutGroups(ros), gen
 
 
 def instrumented_kernel_times(ro):
@@ -261,22 +259,25 @@ def gpu_bench(args):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device(device))
-    ro, gen = build_engine(device, rank, args.slots)
-    sim, buf, dr = ro.sim, ro.buf, ro.draws
+    grp, gen = build_engine(device, rank, args.slots, args.groups)
     # first tick eagerly (one-time set-up: resolve tiers, ticker state)
-    dr.generate(gen)
-    ro.tick(0)
-    ro.collect()                     # finish a full eager rollout for a warm state
-    kt = instrumented_kernel_times(ro)
-    ro.capture()
-    pool = [RolloutDrawsPool.make(dr, gen) for _ in range(min(args.steps + args.warmup, 4))]
+    for ro in grp.ros:
+        ro.draws.generate(gen)
+        ro.tick(0)
+    grp.collect()                    # finish a full eager rollout for a warm state
+    kt = instrumented_kernel_times(grp.ros[0])
+    n_inst = grp.ros[0].sim.num_envs
+    grp.capture()
+    pool = [[RolloutDrawsPool.make(ro.draws, gen) for ro in grp.ros]
+            for _ in range(min(args.steps + args.warmup, 4))]
     l2 = torch.empty((64 << 20,), dtype=torch.float32, device=device)   # 256 MB > L2
 
     def one_step(i, ev):
         a, b = ev
         a.record()
-        RolloutDrawsPool.load(dr, pool[i % len(pool)])
-        ro.replay()
+        for ro, ts in zip(grp.ros, pool[i % len(pool)]):
+            RolloutDrawsPool.load(ro.draws, ts)
+        grp.replay()
         b.record()
 
     for i in range(args.warmup):
@@ -304,19 +305,22 @@ def gpu_bench(args):
     value = N_ENVS * TICKS * world * args.steps / (ms / 1e3)
 
     # ---- e2e: public API with host-fed draws and a host read of the rewards
-    host_draws = [t.detach().cpu().pin_memory() for t in dr.tensors()]
+    dev_draws = [t for ro in grp.ros for t in ro.draws.tensors()]
+    host_draws = [t.detach().cpu().pin_memory() for t in dev_draws]
     h2d = sum(t.numel() * t.element_size() for t in host_draws)
-    rew_host = torch.empty((buf.rew.shape[0], N_ENVS), dtype=torch.float32).pin_memory()
-    d2h = rew_host.numel() * 4
+    rew_host = [torch.empty((ro.buf.rew.shape[0], ro.sim.num_envs), dtype=torch.float32).pin_memory()
+                for ro in grp.ros]
+    d2h = sum(r.numel() * 4 for r in rew_host)
     e_evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
              for _ in range(args.steps)]
     for i in range(args.steps):
         a, b = e_evs[i]
         a.record()
-        for dst, src in zip(dr.tensors(), host_draws):
+        for dst, src in zip(dev_draws, host_draws):
             dst.copy_(src, non_blocking=True)
-        ro.replay()
-        rew_host[: buf.rew.shape[0]].copy_(buf.rew[:, :, 0], non_blocking=True)
+        grp.replay()
+        for ro, rh in zip(grp.ros, rew_host):
+            rh.copy_(ro.buf.rew[:, :, 0], non_blocking=True)
         b.record()
         b.synchronize()
         l2.zero_()
@@ -325,7 +329,7 @@ def gpu_bench(args):
     if dist:
         dist.all_reduce(t_e, op=dist.ReduceOp.MAX)
     e_value = N_ENVS * TICKS * world * args.steps / (float(t_e.item()) / 1e3)
-    ro.graph = None
+    grp.graph = None
     torch.cuda.synchronize()
 
     out = None
@@ -340,7 +344,7 @@ def gpu_bench(args):
             else:
                 name, byt = k, ALG_BYTES.get(k, 169 * 8)
             per[name] = {"launches_per_rollout": launches, "mean_ms": round(mean_ms, 5),
-                         "share": None, "alg_bytes_per_launch": byt * N_ENVS}
+                         "share": None, "alg_bytes_per_launch": byt * n_inst}
         tot = sum(v["launches_per_rollout"] * v["mean_ms"] for v in per.values())
         for v in per.values():
             v["share"] = round(v["launches_per_rollout"] * v["mean_ms"] / tot, 4)
@@ -357,13 +361,16 @@ def gpu_bench(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "f32 sim, fp16xfp16->f32 GEMM",
             "data": "synthetic (seeded template maps, random-init policy, device RNG draws)",
             "config": {"workload": WORKLOAD, "envs_per_gpu": N_ENVS, "ticks": TICKS,
+                       "env_groups_per_gpu": args.groups,
                        "parallelism": f"env shards x{world}, no rollout collective",
                        "l2": "flushed (256 MB write) between timed steps; each step also "
                              "writes a 3.4 GB observation buffer",
                        "cuda_graph": True},
             "e2e": {"value": round(e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "gpu_launches": (TICKS * 6 + TICKS // 16) * args.steps,
+            # per tick and group: observe, fused MLP, astar cap + field, step;
+            # crate recycling every 16 ticks
+            "gpu_launches": (TICKS * 5 + TICKS // 16) * args.groups * args.steps,
             "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1),
                          "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                          "peak_source": src, "traffic": traffic,
@@ -451,6 +458,8 @@ def main():
     ap.add_argument("--ref-ticks", type=int, default=4)
     ap.add_argument("--envs", type=int, default=5632, help="envs per GPU (profiling cases)")
     ap.add_argument("--ticks", type=int, default=128, help="ticks per rollout (multiple of 16)")
+    ap.add_argument("--groups", type=int, default=2,
+                    help="independent env groups per GPU, each on its own stream")
     ap.add_argument("--slots", type=int, default=0,
                     help="rollout-buffer slots (0 = one per tick; fewer = ring, profiling only)")
     args = ap.parse_args()

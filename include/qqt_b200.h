@@ -237,6 +237,9 @@ int qqt_greedy_act(const QqtCfg *cfg, const QqtState *st, const void *obs,
  * into the packed weights' column gather), then LN, ReLU, Linear(128,128),
  * LN, ReLU, the move/bomb/critic heads, masking with float32's lowest value
  * and inverse-CDF sampling a = #{k : u*S > cs_k} over exp(z - max z).
+ * One kernel per 128 env rows: Linear(128,128) and the heads' hidden layer
+ * also run on tcgen05 (fp16 hi/lo splits of activations and weights, three
+ * products per K step), every intermediate stays in TMEM / shared memory.
  *   pack    weights packed by qqt_mlp_pack (256-byte aligned)
  *   obs     [N][obs_stride] fp16, obs_stride % 8 == 0, 16-byte aligned; the
  *           first k_in = C*H*W entries of each row are the observation
@@ -249,7 +252,7 @@ int qqt_greedy_act(const QqtCfg *cfg, const QqtState *st, const void *obs,
  *           act[s] + e*act_stride (move, bomb int64)
  *   logp, value [n_seats][N] (may be NULL); logits [n_seats][N][8]
  *           (5 move, 2 bomb, value) or NULL
- *   work    device buffer of qqt_mlp_work_bytes(N, n_seats) bytes */
+ *   work    reserved (may be NULL); qqt_mlp_work_bytes gives its size */
 int qqt_mlp_act(const void *pack, const void *obs, int32_t n_envs, int32_t obs_stride,
                 int32_t k_in, int32_t n_seats, const uint8_t *const *mm, int32_t mm_stride,
                 const uint8_t *const *bm, int32_t bm_stride, const float *u,

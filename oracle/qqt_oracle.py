@@ -682,6 +682,51 @@ def dijkstra_field(sources, danger, blocked, lam=2.0):
     return dist.reshape(n, h * w)
 
 
+def _splitmix_unit(x):
+    """SplitMix64 finaliser (S. Vigna's published mixer) -> the top 24 bits as
+    a float in [0, 1): the device's counter-based uniform."""
+    x = np.asarray(x, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        x = x + np.uint64(0x9E3779B97F4A7C15)
+        x = (x ^ (x >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        x = (x ^ (x >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+    x = x ^ (x >> np.uint64(31))
+    return (x >> np.uint64(40)).astype(np.float32) * np.float32(1.0 / 16777216.0)
+
+
+def flush_recycle_keyed(cfg, st, excl, seed, counter):
+    """Crate recycling with counter-based draws (the engine's device variant of
+    sim/torch_sim.py:549-596): for each player p (in order) of each env with
+    pending_lost > 0, the min(lost, #available) available cells (not wall,
+    not brick, not in `excl`) with the smallest keys u(key + cell) get a
+    crate and a recycle mark (ties -> lower cell); key = seed ^ counter*G ^
+    (e << 20) ^ (p << 52) ^ t_e*M.  Checker for k_flush_recycle."""
+    n = st["wall"].shape[0]
+    p = st["alive"].shape[1]
+    h, w = cfg.height, cfg.width
+    cells = np.arange(h * w, dtype=np.uint64)
+    ex = np.zeros(h * w, bool)
+    ex[list(excl)] = True
+    G = np.uint64(0x9E3779B97F4A7C15)
+    M = np.uint64(0xD1B54A32D192ED03)
+    with np.errstate(over="ignore"):
+        for pl in range(p):
+            for e in range(n):
+                lost = int(st["pending_lost"][e, pl])
+                if lost <= 0:
+                    continue
+                key = (np.uint64(seed) ^ (np.uint64(counter) * G) ^ (np.uint64(e) << np.uint64(20))
+                       ^ (np.uint64(pl) << np.uint64(52)) ^ (np.uint64(st["t"][e]) * M))
+                avail = ~(st["wall"][e].reshape(-1) | st["brick"][e].reshape(-1) | ex)
+                k = _splitmix_unit(key + cells)
+                idx = np.nonzero(avail)[0]
+                order = idx[np.lexsort((idx, k[idx]))][:min(lost, idx.size)]
+                st["crate"][e].reshape(-1)[order] = True
+                st["recycle"][e].reshape(-1)[order] = True
+                st["pending_lost"][e, pl] = 0
+    return st
+
+
 class ModeTicker:
     """astar approach/flee mode switcher with fed draws (sim/bots.py:241-264)."""
 

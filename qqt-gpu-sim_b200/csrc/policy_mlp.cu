@@ -1,22 +1,30 @@
-// MLP policy: first layer on the 5th-generation tensor cores, the rest fused
-// into one row-parallel kernel (train/model.py:121-153, 167-245).
+// MLP policy on the 5th-generation tensor cores, one fused kernel per 128
+// env rows (train/model.py:121-153, 167-245).
 //
-// k_mlp_gemm  (one CTA per 128 envs, 192 threads)
-//   warp 0     allocates TMEM, then lane 0 streams K tiles with TMA:
-//              A = obs tile [128 rows x 64 k] fp16, B = packed W0 (hi and lo
-//              fp16 halves of the seat-permuted fp32 weights) [NT x 64]
-//   warp 1     lane 0 issues tcgen05.mma kind::f16, M=128, N=NT, K=16, two
-//              per K step (A*Bhi + A*Blo) into one fp32 TMEM accumulator;
-//              obs values are exact in fp16 and the hi/lo split keeps W's
-//              float32 precision
-//   warps 2-5  wait for the accumulator, tcgen05.ld their 32 TMEM lanes, add
-//              the bias and store the pre-activations [N][NT] fp32
-// k_mlp_heads (4 lanes per row)
-//   LN -> ReLU -> Linear(128,128) -> LN -> ReLU -> move/bomb/critic heads,
-//   masking with float32's lowest value, inverse-CDF sampling, log-prob.
+// k_mlp_fused<NT>  (one CTA per 128 envs, 192 threads, NT = 128 x seats)
+//   layer 1  warp 0 lane 0 streams K tiles with TMA: A = obs tile [128 x 64]
+//            fp16, B = packed W0 (fp16 hi and lo halves of the seat-permuted
+//            fp32 weights) [NT x 64]; warp 1 lane 0 issues tcgen05.mma
+//            kind::f16 M=128 N=NT, two per K=16 step (A*Bhi + A*Blo) into an
+//            fp32 TMEM accumulator; obs values are exact in fp16 and the
+//            hi/lo split keeps W0's float32 precision.
+//   tail     the pipeline's shared memory is reused: one bulk copy brings
+//            the pre-swizzled fp16 hi/lo images of shared.3 (128x128) and the
+//            three head hidden layers (192x128).  Warps 2-5 own one row per
+//            thread: tcgen05.ld the row, +bias, LayerNorm, ReLU, split the
+//            row into fp16 hi/lo and store it as the next MMA's A operand
+//            (128-byte swizzled K-major).  Each of the two remaining layers
+//            is 8 K steps x 3 MMAs (Ahi*Whi + Ahi*Wlo + Alo*Whi), which keeps
+//            the products at float32 accuracy.  The 192 head units come
+//            back from TMEM, the output layers (5 move, 2 bomb, 1 value) are
+//            per-thread dot products, then masking with float32's lowest
+//            value, inverse-CDF sampling and the log-probability.
+// k_mlp_heads (4 lanes per row; used by the CNN policy after its trunk)
+//   the same tail on the CUDA cores from a pre-activation buffer.
 //
 // Every mbarrier wait is bounded; on expiry the CTA raises QQT_DEV_TIMEOUT,
-// drains the copies it issued (bounded), frees its TMEM and returns.
+// waits (bounded) for the copies and MMAs it issued, frees its TMEM and
+// returns.
 
 #include <cuda.h>
 
@@ -71,6 +79,33 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
       : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Untiled bulk copy global -> shared (16-byte aligned, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Generic-proxy shared-memory writes -> visible to the tensor cores.
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Byte offset of element (n, k) in a K-major operand image of `nrows` rows
+// and K = 128 stored as two 64-wide K blocks with the 128-byte swizzle
+// (row n at n*128 bytes, 16-byte chunk c at chunk c ^ (n % 8)).
+__host__ __device__ __forceinline__ uint32_t sw128_off(int n, int k, int nrows) {
+  return (uint32_t)((k >> 6) * nrows * 128 + n * 128 + ((((k & 63) >> 3) ^ (n & 7)) << 4) +
+                    (k & 7) * 2);
+}
+
 // K-major operand tile with 128-byte swizzle: 8-row groups 1024 bytes apart.
 __device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
   const uint64_t addr = smem_u32(tile);
@@ -119,134 +154,20 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-template <int NT>
-struct GemmCfg {
-  static constexpr int kStages = NT == 128 ? 4 : 2;
-  static constexpr int kABytes = kBM * kBK * 2;
-  static constexpr int kBBytes = NT * kBK * 2;          // one of hi / lo
-  static constexpr int kStageBytes = kABytes + 2 * kBBytes;
-  static constexpr int kSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
-};
-
-template <int NT>
-__global__ void __launch_bounds__(192, 1)
-k_mlp_gemm(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-           int n_rows, int k_tiles, const float* __restrict__ bias, float* __restrict__ out) {
-  using G = GemmCfg<NT>;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t* full = (uint64_t*)(smem + G::kStages * G::kStageBytes);
-  uint64_t* empty = full + G::kStages;
-  uint64_t* accb = empty + G::kStages;
-  uint32_t* tmem_slot = (uint32_t*)(accb + 1);
-  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
-  const int warp = warp_id(), lane = lane_id();
-  const int m0 = blockIdx.x * kBM;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < G::kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    mbar_init(accb, 1);
-    *abort_flag = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(tmem_slot)),
-                 "r"(NT));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  }
-  asm volatile("tcgen05.fence::before_thread_sync;");
-  __syncthreads();
-  asm volatile("tcgen05.fence::after_thread_sync;");
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer
-    int issued_until = 0;
-    for (int kt = 0; kt < k_tiles; ++kt) {
-      const int s = kt % G::kStages;
-      if (kt >= G::kStages) {
-        if (!mbar_wait(&empty[s], ((kt / G::kStages) - 1) & 1)) {
-          *abort_flag = 1;
-          break;
-        }
-      }
-      if (*abort_flag) break;
-      uint8_t* st = smem + s * G::kStageBytes;
-      mbar_expect_tx(&full[s], G::kStageBytes);
-      tma_load_2d(&tm_a, &full[s], st, kt * kBK, m0);
-      tma_load_2d(&tm_b, &full[s], st + G::kABytes, kt * kBK, 0);
-      tma_load_2d(&tm_b, &full[s], st + G::kABytes + G::kBBytes, kt * kBK, NT);
-      issued_until = kt + 1;
-    }
-    // drain: every issued stage must land before the CTA may exit
-    for (int kt = max(0, issued_until - G::kStages); kt < issued_until; ++kt)
-      mbar_wait(&full[kt % G::kStages], (kt / G::kStages) & 1);
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer
-    const uint32_t idesc = idesc_f16(kBM, NT);
-    bool ok = true;
-    for (int kt = 0; kt < k_tiles && ok; ++kt) {
-      const int s = kt % G::kStages;
-      if (!mbar_wait(&full[s], (kt / G::kStages) & 1) || *abort_flag) {
-        *abort_flag = 1;
-        ok = false;
-        break;
-      }
-      asm volatile("tcgen05.fence::after_thread_sync;");
-      uint8_t* st = smem + s * G::kStageBytes;
-      const uint64_t da = sw128_desc(st);
-      const uint64_t dh = sw128_desc(st + G::kABytes);
-      const uint64_t dl = sw128_desc(st + G::kABytes + G::kBBytes);
-#pragma unroll
-      for (int kk = 0; kk < kBK / 16; ++kk) {
-        const uint64_t off = (uint64_t)((kk * 32) >> 4);   // 32 bytes per K=16 step
-        umma_f16(tmem, da + off, dh + off, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
-        umma_f16(tmem, da + off, dl + off, idesc, 1u);
-      }
-      umma_commit(&empty[s]);
-    }
-    umma_commit(accb);   // fires once every issued MMA has completed
-  } else if (warp >= 2) {
-    // ---------------- epilogue: TMEM -> registers -> global
-    const int q = warp & 3;                       // TMEM lane quadrant of this warp
-    const bool got = mbar_wait(accb, 0);
-    asm volatile("tcgen05.fence::after_thread_sync;");
-    if (got && !*abort_flag) {
-      const int row = m0 + q * 32 + lane;
-      for (int c0 = 0; c0 < NT; c0 += 32) {
-        float v[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + c0, v);
-        if (row < n_rows) {
-          float4* dst = reinterpret_cast<float4*>(out + (size_t)row * NT + c0);
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            dst[i] = make_float4(__fadd_rn(v[4 * i], bias[c0 + 4 * i]),
-                                 __fadd_rn(v[4 * i + 1], bias[c0 + 4 * i + 1]),
-                                 __fadd_rn(v[4 * i + 2], bias[c0 + 4 * i + 2]),
-                                 __fadd_rn(v[4 * i + 3], bias[c0 + 4 * i + 3]));
-        }
-      }
-    }
-  }
-  asm volatile("tcgen05.fence::before_thread_sync;");
-  __syncthreads();
-  if (warp == 0) {
-    asm volatile("tcgen05.fence::after_thread_sync;");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(NT));
-  }
-}
-
 // ------------------------------------------------------------ pack layout
 
-// Pack (bytes): [B fp16: 2 x NT x KP] [f32 params]
+// Pack (bytes): [B fp16: 2 x NT x KP] [f32 params] [tail operand images]
 struct MlpPack {
   int kp, nt, n_seats;
-  size_t b_off, f_off;
+  size_t b_off, f_off, img_off, total;
 };
+
+// Tail operand images (bytes from img_off), each 128-byte swizzled K-major,
+// K = 128, fp16 hi then lo: shared.3 [128 out x 128 in], then the three head
+// hidden layers stacked [192 x 128] (move 0-63, bomb 64-127, critic 128-191).
+constexpr uint32_t kImgW1 = 0, kImgW1Bytes = 128 * 128 * 2;          // per hi / lo
+constexpr uint32_t kImgH0 = 2 * kImgW1Bytes, kImgH0Bytes = 192 * 128 * 2;
+constexpr uint32_t kImgBytes = kImgH0 + 2 * kImgH0Bytes;             // 160 KB
 
 // f32 parameter block offsets (floats)
 enum {
@@ -269,6 +190,8 @@ __host__ __device__ inline MlpPack mlp_pack_layout(int k_in, int n_seats) {
   p.n_seats = n_seats;
   p.b_off = 0;
   p.f_off = ((size_t)2 * p.nt * p.kp * 2 + 255) / 256 * 256;
+  p.img_off = (p.f_off + (size_t)F_TOTAL * 4 + 1023) / 1024 * 1024;
+  p.total = p.img_off + kImgBytes;
   return p;
 }
 
@@ -338,6 +261,27 @@ __global__ void k_mlp_pack_rest(HeadParams hp, int n_seats, float* __restrict__ 
   if (i < 8) f[F_HB2 + i] = i < 5 ? hp.mb2[i] : (i < 7 ? hp.bb2[i - 5] : hp.cb2[0]);
 }
 
+// fp16 hi / lo split of shared.3 and the head hidden layers into the
+// swizzled operand images, one thread per (row, k).
+__global__ void k_mlp_pack_images(HeadParams hp, uint8_t* __restrict__ img) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= 192 * 128) return;
+  const int n = i >> 7, k = i & 127;
+  if (n < 128) {
+    const float v = hp.w1[n * 128 + k];                  // [out][in]: K-major already
+    const __half hi = __float2half_rn(v);
+    const __half lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
+    *reinterpret_cast<__half*>(img + kImgW1 + sw128_off(n, k, 128)) = hi;
+    *reinterpret_cast<__half*>(img + kImgW1 + kImgW1Bytes + sw128_off(n, k, 128)) = lo;
+  }
+  const float v = n < 64 ? hp.mw0[n * 128 + k]
+                         : (n < 128 ? hp.bw0[(n - 64) * 128 + k] : hp.cw0[(n - 128) * 128 + k]);
+  const __half hi = __float2half_rn(v);
+  const __half lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
+  *reinterpret_cast<__half*>(img + kImgH0 + sw128_off(n, k, 192)) = hi;
+  *reinterpret_cast<__half*>(img + kImgH0 + kImgH0Bytes + sw128_off(n, k, 192)) = lo;
+}
+
 // ---------------------------------------------------------------- heads
 
 // LayerNorm + ReLU over one row held as 32 features per lane by 4 lanes.
@@ -396,6 +340,60 @@ __device__ __forceinline__ void tile_matmul(float (*acc)[12], const float (*xs)[
       }
     }
   }
+}
+
+// Logits z (5 move, 2 bomb, value) of one row -> masked categorical samples
+// (inverse CDF: a = #{k : u * S > cs_k} over exp(z - max z)), joint
+// log-prob, value; masked logits take float32's lowest value
+// (train/model.py:204-245).
+__device__ __forceinline__ void sample_write(const float* z, int row, int seat, int n_rows,
+                                             const uint8_t* __restrict__ mm, int mm_stride,
+                                             const uint8_t* __restrict__ bm, int bm_stride,
+                                             const float* __restrict__ u,
+                                             int64_t* __restrict__ act, int act_stride,
+                                             float* __restrict__ logp_out,
+                                             float* __restrict__ value_out,
+                                             float* __restrict__ logits_out) {
+  if (logits_out) {
+    float* lo = logits_out + ((size_t)seat * n_rows + row) * 8;
+#pragma unroll
+    for (int o = 0; o < 8; ++o) lo[o] = z[o];
+  }
+  const float lowest = -3.402823466e38f;
+  const uint8_t* mrow = mm + (size_t)row * mm_stride;
+  const uint8_t* brow = bm + (size_t)row * bm_stride;
+  float zm[5], cs[5];
+  float mx = lowest;
+#pragma unroll
+  for (int k = 0; k < 5; ++k) {
+    zm[k] = mrow[k] ? z[k] : lowest;
+    mx = fmaxf(mx, zm[k]);
+  }
+  float tot = 0.f;
+#pragma unroll
+  for (int k = 0; k < 5; ++k) {
+    tot += expf(zm[k] - mx);
+    cs[k] = tot;
+  }
+  const float um = u[((size_t)seat * n_rows + row) * 2] * tot;
+  int am = 0;
+#pragma unroll
+  for (int k = 0; k < 5; ++k) am += um > cs[k];
+  am = min(am, 4);
+  float zam = zm[0];
+#pragma unroll
+  for (int k = 1; k < 5; ++k) zam = am == k ? zm[k] : zam;
+  const float lpm = zam - mx - logf(tot);
+  const float zb0 = brow[0] ? z[5] : lowest, zb1 = brow[1] ? z[6] : lowest;
+  const float mb = fmaxf(zb0, zb1);
+  const float e0 = expf(zb0 - mb), s2 = e0 + expf(zb1 - mb);
+  const float ub = u[((size_t)seat * n_rows + row) * 2 + 1] * s2;
+  const int ab = ub > e0 ? 1 : 0;
+  const float lpb = (ab ? zb1 : zb0) - mb - logf(s2);
+  act[(size_t)row * act_stride] = am;
+  act[(size_t)row * act_stride + 1] = ab;
+  if (logp_out) logp_out[(size_t)seat * n_rows + row] = lpm + lpb;
+  if (value_out) value_out[(size_t)seat * n_rows + row] = z[7];
 }
 
 // Register-blocked tail of the MLP: a block of 128 threads owns 32 rows.
@@ -506,46 +504,305 @@ k_mlp_heads(const float* __restrict__ pre, int nt, int seat, int n_rows,
   if (og >= 4 || row >= n_rows) return;
 #pragma unroll
   for (int o = 0; o < 8; ++o) z[o] += __ldg(f + F_HB2 + o);
-  if (logits_out) {
-    float* lo = logits_out + ((size_t)seat * n_rows + row) * 8;
+  sample_write(z, row, seat, n_rows, mm, mm_stride, bm, bm_stride, u, act, act_stride, logp_out,
+               value_out, logits_out);
+}
+
+// ------------------------------------------------------------ fused MLP
+
+struct SeatOut {
+  const uint8_t* mm[2];
+  const uint8_t* bm[2];
+  int64_t* act[2];
+};
+
+template <int NT>
+struct FusedCfg {
+  static constexpr int kStages = NT == 128 ? 4 : 2;
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = NT * kBK * 2;          // one of hi / lo
+  static constexpr int kStageBytes = kABytes + 2 * kBBytes;
+  static constexpr int kPipeBytes = kStages * kStageBytes;
+  // tail layout inside the (reused) pipeline region
+  static constexpr int kW1 = 0;                         // shared.3 hi, lo
+  static constexpr int kH0 = (int)kImgH0;               // head hidden hi, lo
+  static constexpr int kAct = (int)kImgBytes;           // activation operand hi, lo
+  static constexpr int kActBytes = kBM * 128 * 2;       // one of hi / lo
+  static constexpr int kTailBytes = kAct + 2 * kActBytes;
+  static constexpr int kRegion = kPipeBytes > kTailBytes ? kPipeBytes : kTailBytes;
+  static constexpr int kSmem = kRegion + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kColH = NT;                 // head hidden accumulator (192 cols)
+};
+static_assert(FusedCfg<128>::kSmem <= 232448 && FusedCfg<256>::kSmem <= 232448,
+              "fused MLP shared memory over the per-CTA limit");
+static_assert(FusedCfg<256>::kColH + 192 <= FusedCfg<256>::kTmemCols, "TMEM columns");
+
+// One epilogue thread's row: TMEM columns [col, col + 128) -> x.
+__device__ __forceinline__ void tmem_row128(uint32_t taddr, float* x) {
 #pragma unroll
-    for (int o = 0; o < 8; ++o) lo[o] = z[o];
+  for (int c = 0; c < 4; ++c) tmem_ld32(taddr + 32 * c, x + 32 * c);
+}
+
+// x += bias; LayerNorm(128) with affine; ReLU (train/model.py:121-153).
+__device__ __forceinline__ void bias_ln_relu_row(float* x, const float* __restrict__ bias,
+                                                 const float* __restrict__ g,
+                                                 const float* __restrict__ b) {
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 128; ++i) {
+    x[i] = __fadd_rn(x[i], __ldg(bias + i));
+    s += x[i];
   }
-  const float lowest = -3.402823466e38f;
-  const uint8_t* mrow = mm + (size_t)row * mm_stride;
-  const uint8_t* brow = bm + (size_t)row * bm_stride;
-  float zm[5], cs[5];
-  float mx = lowest;
+  const float mean = s * (1.f / 128.f);
+  float v = 0.f;
 #pragma unroll
-  for (int k = 0; k < 5; ++k) {
-    zm[k] = mrow[k] ? z[k] : lowest;
-    mx = fmaxf(mx, zm[k]);
+  for (int i = 0; i < 128; ++i) {
+    const float d = x[i] - mean;
+    v = fmaf(d, d, v);
   }
-  float tot = 0.f;
+  const float rstd = rsqrtf(v * (1.f / 128.f) + 1e-5f);
 #pragma unroll
-  for (int k = 0; k < 5; ++k) {
-    tot += expf(zm[k] - mx);
-    cs[k] = tot;
+  for (int i = 0; i < 128; ++i) x[i] = fmaxf(fmaf((x[i] - mean) * rstd, __ldg(g + i), __ldg(b + i)), 0.f);
+}
+
+// Row r of the activation operand: fp16 hi and lo images, 16-byte stores.
+__device__ __forceinline__ void store_split_row(const float* x, uint8_t* a_hi, uint8_t* a_lo, int r) {
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {
+    uint32_t hv[4], lv[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float v0 = x[8 * c + 2 * j], v1 = x[8 * c + 2 * j + 1];
+      const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+      const __half l0 = __float2half_rn(__fsub_rn(v0, __half2float(h0)));
+      const __half l1 = __float2half_rn(__fsub_rn(v1, __half2float(h1)));
+      hv[j] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+      lv[j] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+    }
+    const uint32_t off = sw128_off(r, 8 * c, kBM);
+    *reinterpret_cast<uint4*>(a_hi + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+    *reinterpret_cast<uint4*>(a_lo + off) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
   }
-  const float um = u[((size_t)seat * n_rows + row) * 2] * tot;
-  int am = 0;
+}
+
+// D[tmem] (+)= A * W over K = 128 with the three-term fp16 split.
+__device__ __forceinline__ void umma_split_k128(uint32_t d_tmem, const uint8_t* a_hi,
+                                                const uint8_t* a_lo, const uint8_t* w_hi,
+                                                const uint8_t* w_lo, int w_rows, uint32_t idesc) {
+  const uint64_t ah = sw128_desc(a_hi), al = sw128_desc(a_lo);
+  const uint64_t wh = sw128_desc(w_hi), wl = sw128_desc(w_lo);
 #pragma unroll
-  for (int k = 0; k < 5; ++k) am += um > cs[k];
-  am = min(am, 4);
-  float zam = zm[0];
+  for (int kk = 0; kk < 8; ++kk) {
+    const uint64_t oa = (uint64_t)(((kk >> 2) * kBM * 128 + (kk & 3) * 32) >> 4);
+    const uint64_t ow = (uint64_t)(((kk >> 2) * w_rows * 128 + (kk & 3) * 32) >> 4);
+    umma_f16(d_tmem, ah + oa, wh + ow, idesc, kk > 0 ? 1u : 0u);
+    umma_f16(d_tmem, ah + oa, wl + ow, idesc, 1u);
+    umma_f16(d_tmem, al + oa, wh + ow, idesc, 1u);
+  }
+}
+
+template <int NT>
+__global__ void __launch_bounds__(192, 1)
+k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+            int n_rows, int k_tiles, const float* __restrict__ f, const uint8_t* __restrict__ img,
+            SeatOut io, int mm_stride, int bm_stride, const float* __restrict__ u, int act_stride,
+            float* __restrict__ logp_out, float* __restrict__ value_out,
+            float* __restrict__ logits_out) {
+  using G = FusedCfg<NT>;
+  constexpr int S = NT / 128;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = (uint64_t*)(smem + G::kRegion);
+  uint64_t* empty = full + G::kStages;
+  uint64_t* accb = empty + G::kStages;    // layer-1 accumulator complete
+  uint64_t* wbar = accb + 1;              // tail weight images landed
+  uint64_t* abar = wbar + 1;              // activation operand written (128 arrivals)
+  uint64_t* dbar = abar + 1;              // tail MMA group complete
+  uint32_t* tmem_slot = (uint32_t*)(dbar + 1);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  const int warp = warp_id(), lane = lane_id();
+  const int m0 = blockIdx.x * kBM;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < G::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accb, 1);
+    mbar_init(wbar, 1);
+    mbar_init(abar, 128);
+    mbar_init(dbar, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(G::kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer (layer 1)
+    int issued_until = 0;
+    for (int kt = 0; kt < k_tiles; ++kt) {
+      const int s = kt % G::kStages;
+      if (kt >= G::kStages) {
+        if (!mbar_wait(&empty[s], ((kt / G::kStages) - 1) & 1)) {
+          *abort_flag = 1;
+          break;
+        }
+      }
+      if (*abort_flag) break;
+      uint8_t* st = smem + s * G::kStageBytes;
+      mbar_expect_tx(&full[s], G::kStageBytes);
+      tma_load_2d(&tm_a, &full[s], st, kt * kBK, m0);
+      tma_load_2d(&tm_b, &full[s], st + G::kABytes, kt * kBK, 0);
+      tma_load_2d(&tm_b, &full[s], st + G::kABytes + G::kBBytes, kt * kBK, NT);
+      issued_until = kt + 1;
+    }
+    // drain: every issued stage must land before the CTA may exit
+    for (int kt = max(0, issued_until - G::kStages); kt < issued_until; ++kt)
+      mbar_wait(&full[kt % G::kStages], (kt / G::kStages) & 1);
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer
+    const uint32_t idesc = idesc_f16(kBM, NT);
+    bool ok = true;
+    for (int kt = 0; kt < k_tiles && ok; ++kt) {
+      const int s = kt % G::kStages;
+      if (!mbar_wait(&full[s], (kt / G::kStages) & 1) || *abort_flag) {
+        *abort_flag = 1;
+        ok = false;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      uint8_t* st = smem + s * G::kStageBytes;
+      const uint64_t da = sw128_desc(st);
+      const uint64_t dh = sw128_desc(st + G::kABytes);
+      const uint64_t dl = sw128_desc(st + G::kABytes + G::kBBytes);
 #pragma unroll
-  for (int k = 1; k < 5; ++k) zam = am == k ? zm[k] : zam;
-  const float lpm = zam - mx - logf(tot);
-  const float zb0 = brow[0] ? z[5] : lowest, zb1 = brow[1] ? z[6] : lowest;
-  const float mb = fmaxf(zb0, zb1);
-  const float e0 = expf(zb0 - mb), s2 = e0 + expf(zb1 - mb);
-  const float ub = u[((size_t)seat * n_rows + row) * 2 + 1] * s2;
-  const int ab = ub > e0 ? 1 : 0;
-  const float lpb = (ab ? zb1 : zb0) - mb - logf(s2);
-  act[(size_t)row * act_stride] = am;
-  act[(size_t)row * act_stride + 1] = ab;
-  if (logp_out) logp_out[(size_t)seat * n_rows + row] = lpm + lpb;
-  if (value_out) value_out[(size_t)seat * n_rows + row] = z[7];
+      for (int kk = 0; kk < kBK / 16; ++kk) {
+        const uint64_t off = (uint64_t)((kk * 32) >> 4);   // 32 bytes per K=16 step
+        umma_f16(tmem, da + off, dh + off, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+        umma_f16(tmem, da + off, dl + off, idesc, 1u);
+      }
+      umma_commit(&empty[s]);
+    }
+    umma_commit(accb);   // fires once every issued MMA has completed
+    // the pipeline region is free once layer 1's MMAs are done: bring in the
+    // tail weight images (all CTAs read the same 160 KB, an L2 hit)
+    bool loaded = false;
+    if (mbar_wait(accb, 0) && ok) {
+      mbar_expect_tx(wbar, kImgBytes);
+      for (uint32_t o = 0; o < kImgBytes; o += 16384) bulk_load(smem + o, img + o, 16384, wbar);
+      loaded = true;
+    } else {
+      *abort_flag = 1;
+    }
+    const uint32_t id2 = idesc_f16(kBM, 128), id3 = idesc_f16(kBM, 192);
+    uint8_t* a_hi = smem + G::kAct;
+    uint8_t* a_lo = a_hi + G::kActBytes;
+    int committed = 0;
+    if (loaded && !mbar_wait(wbar, 0)) *abort_flag = 1;
+    for (int s = 0; s < S && !*abort_flag; ++s) {
+      // layer 2: D2 overwrites this seat's layer-1 columns (already read)
+      if (!mbar_wait(abar, (2 * s) & 1)) { *abort_flag = 1; break; }
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      umma_split_k128(tmem + 128 * s, a_hi, a_lo, smem + G::kW1, smem + G::kW1 + kImgW1Bytes, 128,
+                      id2);
+      umma_commit(dbar);
+      ++committed;
+      // head hidden layer
+      if (!mbar_wait(abar, (2 * s + 1) & 1)) { *abort_flag = 1; break; }
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      umma_split_k128(tmem + G::kColH, a_hi, a_lo, smem + G::kH0, smem + G::kH0 + kImgH0Bytes, 192,
+                      id3);
+      umma_commit(dbar);
+      ++committed;
+    }
+    // the epilogue consumes every commit; on abort wait here for the last one
+    if (*abort_flag && committed > 0) mbar_wait(dbar, (committed - 1) & 1);
+    if (loaded && *abort_flag) mbar_wait(wbar, 0);
+  } else if (warp >= 2) {
+    // ---------------- epilogue: one row per thread (TMEM lane quadrant warp % 4)
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const int row = m0 + r;
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    uint8_t* a_hi = smem + G::kAct;
+    uint8_t* a_lo = a_hi + G::kActBytes;
+    // tcgen05.ld is warp-collective: every branch around it is warp-uniform
+    auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+      const bool got = mbar_wait(bar, parity);
+      return __all_sync(QQT_FULL, got) && __shfl_sync(QQT_FULL, *abort_flag, 0) == 0;
+    };
+    bool ok = wait_all(accb, 0);
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    // the activation operand overlays pipeline stages: wait for the weight
+    // images (issued after every layer-1 MMA completed) before writing it
+    ok = ok && wait_all(wbar, 0);
+    for (int s = 0; s < S && ok; ++s) {
+      float x[128];
+      // LN1 over the layer-1 pre-activations
+      tmem_row128(lane_base + 128 * s, x);
+      bias_ln_relu_row(x, f + F_B0 + 128 * s, f + F_LN1G, f + F_LN1B);
+      store_split_row(x, a_hi, a_lo, r);
+      fence_proxy_async();
+      asm volatile("tcgen05.fence::before_thread_sync;");
+      mbar_arrive(abar);
+      // LN2 over layer 2
+      if (!wait_all(dbar, (2 * s) & 1)) { ok = false; break; }
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      tmem_row128(lane_base + 128 * s, x);
+      bias_ln_relu_row(x, f + F_B1, f + F_LN2G, f + F_LN2B);
+      store_split_row(x, a_hi, a_lo, r);
+      fence_proxy_async();
+      asm volatile("tcgen05.fence::before_thread_sync;");
+      mbar_arrive(abar);
+      // head hidden units -> output layers
+      if (!wait_all(dbar, (2 * s + 1) & 1)) { ok = false; break; }
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      float z[8];
+#pragma unroll
+      for (int o = 0; o < 8; ++o) z[o] = 0.f;
+#pragma unroll
+      for (int c = 0; c < 6; ++c) {
+        float h[32];
+        tmem_ld32(lane_base + G::kColH + 32 * c, h);
+        const int head = c >> 1, u0 = (c & 1) * 32;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) h[i] = fmaxf(__fadd_rn(h[i], __ldg(f + F_HB0 + 32 * c + i)), 0.f);
+        const int o_lo = head == 0 ? 0 : (head == 1 ? 5 : 7);
+        const int o_hi = head == 0 ? 5 : (head == 1 ? 7 : 8);
+#pragma unroll
+        for (int o = 0; o < 8; ++o) {
+          if (o < o_lo || o >= o_hi) continue;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) z[o] = fmaf(__ldg(f + F_HW2 + o * 64 + u0 + i), h[i], z[o]);
+        }
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;");
+      if (row < n_rows) {
+#pragma unroll
+        for (int o = 0; o < 8; ++o) z[o] += __ldg(f + F_HB2 + o);
+        sample_write(z, row, s, n_rows, io.mm[s], mm_stride, io.bm[s], bm_stride, u, io.act[s],
+                     act_stride, logp_out, value_out, logits_out);
+      }
+    }
+    if (!ok) *abort_flag = 1;
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(G::kTmemCols));
+  }
 }
 
 }  // namespace qqt
@@ -593,8 +850,7 @@ extern "C" const char* qqt_mlp_param_names(void) { return kParamNames; }
 
 extern "C" uint64_t qqt_mlp_pack_bytes(int32_t k_in, int32_t n_seats) {
   if (k_in <= 0 || n_seats < 1 || n_seats > 2) return 0;
-  const MlpPack L = mlp_pack_layout(k_in, n_seats);
-  return L.f_off + (uint64_t)F_TOTAL * 4;
+  return mlp_pack_layout(k_in, n_seats).total;
 }
 
 extern "C" int qqt_mlp_pack(const float* const* params, int32_t k_in, int32_t n_players,
@@ -654,11 +910,15 @@ extern "C" int qqt_mlp_pack(const float* const* params, int32_t k_in, int32_t n_
   hp.cw2 = params[18];
   hp.cb2 = params[19];
   k_mlp_pack_rest<<<(128 * 128 + 255) / 256, 256, 0, st>>>(hp, n_seats, (float*)(pk + L.f_off));
+  k_mlp_pack_images<<<(192 * 128 + 255) / 256, 256, 0, st>>>(hp, pk + L.img_off);
   return launch_status();
 }
 
+// The fused kernel keeps every intermediate on chip; `work` is reserved.
 extern "C" uint64_t qqt_mlp_work_bytes(int32_t n_envs, int32_t n_seats) {
-  return (uint64_t)n_envs * 128 * n_seats * 4;
+  (void)n_envs;
+  (void)n_seats;
+  return 256;
 }
 
 extern "C" int qqt_mlp_act(const void* pack, const void* obs, int32_t n_envs, int32_t obs_stride,
@@ -666,7 +926,8 @@ extern "C" int qqt_mlp_act(const void* pack, const void* obs, int32_t n_envs, in
                            int32_t mm_stride, const uint8_t* const* bm, int32_t bm_stride,
                            const float* u, int64_t* const* act, int32_t act_stride, float* logp,
                            float* value, float* logits, void* work, qqt_stream_t stream) {
-  if (!pack || !obs || !mm || !bm || !u || !act || !work) return QQT_E_ARG;
+  (void)work;
+  if (!pack || !obs || !mm || !bm || !u || !act) return QQT_E_ARG;
   if (n_envs <= 0 || n_seats < 1 || n_seats > 2 || mm_stride < 5 || bm_stride < 2 ||
       act_stride < 2)
     return QQT_E_ARG;
@@ -683,23 +944,27 @@ extern "C" int qqt_mlp_act(const void* pack, const void* obs, int32_t n_envs, in
                 (uint32_t)L.nt))
     return QQT_E_ARG;
   cudaStream_t st = (cudaStream_t)stream;
-  float* pre = (float*)work;
   const float* fpar = (const float*)(pk + L.f_off);
   const int k_tiles = L.kp / kBK;
   const int grid = (n_envs + kBM - 1) / kBM;
-  if (L.nt == 128) {
-    cudaFuncSetAttribute(k_mlp_gemm<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         GemmCfg<128>::kSmem);
-    k_mlp_gemm<128><<<grid, 192, GemmCfg<128>::kSmem, st>>>(ma, mb, n_envs, k_tiles, fpar + F_B0, pre);
-  } else {
-    cudaFuncSetAttribute(k_mlp_gemm<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         GemmCfg<256>::kSmem);
-    k_mlp_gemm<256><<<grid, 192, GemmCfg<256>::kSmem, st>>>(ma, mb, n_envs, k_tiles, fpar + F_B0, pre);
+  SeatOut io;
+  for (int s = 0; s < 2; ++s) {
+    io.mm[s] = s < n_seats ? mm[s] : nullptr;
+    io.bm[s] = s < n_seats ? bm[s] : nullptr;
+    io.act[s] = s < n_seats ? act[s] : nullptr;
   }
-  for (int s = 0; s < n_seats; ++s) {
-    k_mlp_heads<<<(n_envs + kHR - 1) / kHR, 128, 0, st>>>(pre, L.nt, s, n_envs, fpar, mm[s], mm_stride,
-                                                      bm[s], bm_stride, u, act[s], act_stride, logp,
-                                                      value, logits);
+  if (L.nt == 128) {
+    cudaFuncSetAttribute(k_mlp_fused<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         FusedCfg<128>::kSmem);
+    k_mlp_fused<128><<<grid, 192, FusedCfg<128>::kSmem, st>>>(
+        ma, mb, n_envs, k_tiles, fpar, pk + L.img_off, io, mm_stride, bm_stride, u, act_stride,
+        logp, value, logits);
+  } else {
+    cudaFuncSetAttribute(k_mlp_fused<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         FusedCfg<256>::kSmem);
+    k_mlp_fused<256><<<grid, 192, FusedCfg<256>::kSmem, st>>>(
+        ma, mb, n_envs, k_tiles, fpar, pk + L.img_off, io, mm_stride, bm_stride, u, act_stride,
+        logp, value, logits);
   }
   return launch_status();
 }

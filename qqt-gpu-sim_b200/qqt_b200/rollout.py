@@ -169,3 +169,61 @@ class Rollout:
         if isinstance(self.opponent, AstarBot):
             self.opponent.calls += self.T
         return self.buf
+
+
+class RolloutGroups:
+    """Several independent env groups (one `Rollout` each, with its own sim
+    state, bot and draws) ticked on their own streams, so one group's
+    simulation kernels overlap another group's policy and bot kernels; the
+    whole T-tick rollout of every group is still one CUDA graph.
+
+    `Rollout.tick` has no cross-group dependency: each group's kernels are
+    ordered only by its own stream (plus its policy side stream)."""
+
+    def __init__(self, rollouts):
+        self.ros = list(rollouts)
+        dev = self.ros[0].sim.device
+        self.device = dev
+        self.T = self.ros[0].T
+        self.streams = [torch.cuda.Stream(dev) for _ in self.ros]
+        self.graph = None
+
+    @property
+    def num_envs(self) -> int:
+        return sum(r.sim.num_envs for r in self.ros)
+
+    def collect(self):
+        main = torch.cuda.current_stream(self.device)
+        for s in self.streams:
+            s.wait_stream(main)
+        for t in range(self.T):
+            for ro, s in zip(self.ros, self.streams):
+                with torch.cuda.stream(s):
+                    ro.tick(t)
+        for s in self.streams:
+            main.wait_stream(s)
+        return [r.buf for r in self.ros]
+
+    def capture(self) -> None:
+        for ro in self.ros:
+            if isinstance(ro.opponent, AstarBot) and ro.opponent.mode is None:
+                raise RuntimeError("run one eager tick before capture (ticker init)")
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        g = torch.cuda.CUDAGraph()
+        calls0 = [r.opponent.calls if isinstance(r.opponent, AstarBot) else 0 for r in self.ros]
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                self.collect()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        for r, c in zip(self.ros, calls0):
+            if isinstance(r.opponent, AstarBot):
+                r.opponent.calls = c
+        self.graph = g
+
+    def replay(self):
+        self.graph.replay()
+        for r in self.ros:
+            if isinstance(r.opponent, AstarBot):
+                r.opponent.calls += r.T
+        return [r.buf for r in self.ros]

@@ -85,3 +85,18 @@ def bomb_stress(n: int, cfg: SimConfig, seed: int, lo: int = 20, hi: int = 40):
 # Benchmark configurations (SimConfig keyword arguments).
 CFG1 = dict(height=13, width=13, n_players=2, map_mode="open", speed=3.0, tick_hz=10)
 CFG2 = dict(map_mode="corridor", open_fraction=0.0, speed=3.0, max_steps=1800)
+
+
+def corridor_template(cfg, n: int, seed: int) -> dict:
+    """Per-env map template of the cfg2 workload: border walls, permanent
+    pillars, bricks with p=0.7 (corner L cells kept free), corner spawns and
+    the growth start values; fed to `B200Sim(template=...)` and applied again
+    by every device auto-reset."""
+    p = cfg.n_players
+    wall, brick = pillar_corridor(n, cfg.height, cfg.width, seed=seed)
+    spawn = np.broadcast_to(np.array(corner_spawns(cfg), np.float32), (n, p, 2)).copy()
+    return {"wall": wall, "brick": brick, "spawn": spawn,
+            "bombs_cap": np.full((n, p), cfg.growth_bombs_start, np.int64),
+            "blast_cap": np.full((n, p), cfg.growth_blast_start, np.int64),
+            "spd": np.full((n, p), cfg.growth_speed_start, np.float32),
+            "crate_prob": np.full((n,), cfg.growth_crate_prob, np.float32)}
