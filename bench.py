@@ -1,18 +1,25 @@
 #!/usr/bin/env python3
-"""Rollout throughput benchmark (BASELINE.json metric, configuration 2).
+"""Rollout throughput benchmark (BASELINE.json metric).
 
-One "step" = one 128-tick rollout of N=5632 envs on the pillar-corridor map:
-observe -> masks -> MLP learner (seat 0) -> astar opponent (seat 1) -> step
-(device auto-reset) -> crate recycling every 16 ticks, captured as one CUDA
-graph.  value = envs * ticks * ranks / max-over-ranks device time.
+One "step" = one 128-tick rollout of one GPU's env shard: observe -> masks ->
+learner act -> opponent act -> step (device auto-reset) -> crate recycling
+every 16 ticks, captured as one CUDA graph.  value = envs * ticks * ranks /
+max-over-ranks device time.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--config cfg2|cfg4|cfg5]
 
-Multi-GPU (weak scaling, no data-path collective): launched with
-torch.distributed.run, each rank runs its own 5632-env shard.
---impl reference times the CPU restatement of the reference algorithm
-(oracle/, the reference itself is Python and cannot be shipped) on the
-host's cores for the same workload.
+--config selects the workload (default cfg2, the headline): cfg2 = N=5632,
+MLP learner seat 0 vs astar seat 1; cfg4 = N=65536, self-play (one MLP for
+both seats, one N=256 GEMM), plus one PPO update on the seat-0 buffer timed
+separately; cfg5 = N=5632, CNN learner vs greedy.
+
+Multi-GPU (weak scaling, no data-path collective in the rollout): launched
+with torch.distributed.run, each rank runs its own shard; cfg4's PPO update
+all-reduces gradients and advantage statistics over NCCL.  --impl reference
+times the CPU restatement of the reference algorithm (oracle/, the reference
+itself is Python and cannot be shipped) on the host's cores for the same
+workload.
 """
 
 from __future__ import annotations
@@ -31,21 +38,36 @@ sys.path[:0] = [ROOT, os.path.join(ROOT, "qqt-gpu-sim_b200")]
 
 METRIC = "rollout env-steps/sec (sim+obs+policy+sample) at 1/2/4/8 B200 vs ref CPU"
 UNIT = "env-steps/s"
-N_ENVS = 5632      # overridden by --envs for profiling cases
-TICKS = 128
-WORKLOAD = ("cfg2: 13x13 pillar corridor (bricks p=0.7), P=2, N=5632 envs per GPU, "
-            "random-init MLP learner seat 0 (view_perm) vs astar seat 1, 128-tick rollout")
 
-# Algorithmic bytes per env per launch (reference dtypes, compulsory traffic),
-# per kernel; see DESIGN.md "Roofline accounting".
+CONFIGS = {
+    "cfg2": dict(envs=5632, learner="mlp", seats=(0,), opponent="astar", ppo=False, cpu=(256, 8),
+                 workload="cfg2: 13x13 pillar corridor (bricks p=0.7), P=2, N=5632 envs per "
+                          "GPU, random-init MLP learner seat 0 (view_perm) vs astar seat 1, "
+                          "128-tick rollout"),
+    "cfg4": dict(envs=65536, learner="mlp", seats=(0, 1), opponent=None, ppo=True, cpu=(256, 8),
+                 workload="cfg4: cfg2 map, N=65536 envs per GPU, self-play (one random-init "
+                          "MLP for both seats, one N=256 GEMM), 128-tick rollout; PPO update "
+                          "(4 epochs x 8 minibatches, seat-0 buffer) timed separately"),
+    "cfg5": dict(envs=5632, learner="cnn", seats=(0,), opponent="greedy", ppo=False, cpu=(16, 2),
+                 workload="cfg5: cfg2 map, N=5632 envs per GPU, random-init CNN learner seat 0 "
+                          "vs greedy seat 1, 128-tick rollout"),
+}
+CFG = CONFIGS["cfg2"]
+N_ENVS = 5632      # from the config; --envs overrides for profiling cases
+TICKS = 128
+
+# Algorithmic bytes per env per launch (reference dtypes, compulsory traffic).
+OBS_ROW = 2368 * 2
 ALG_BYTES = {
     "step": 169 * (1 + 1 + 1 + 1 + 2 + 1 + 2) * 2 - 169 + 280 + 32 + 8 + 1,
-    "observe": 169 * (1 + 1 + 1 + 1 + 2 + 2) + 56 + 2368 * 2 + 14,
+    "observe": 169 * (1 + 1 + 1 + 1 + 2 + 2) + 56 + OBS_ROW + 14,
     "astar": 169 * (1 + 1 + 1 + 2) + 169 * 2 + 10 + 20 + 16,
-    "mlp_gemm": 2368 * 2 + 128 * 4,
-    "mlp_heads": 128 * 4 + 10 + 8 + 16 + 8,
+    "greedy": 169 * (1 + 1 + 1 + 2) + 169 * 2 + 10 + 20 + 16,
+    "policy": OBS_ROW,           # + per seat: masks, uniforms, actions, log-prob, value
+    "flush": 169 * 8 + 16,
 }
-MLP_FLOPS = 2 * 2366 * 128
+POLICY_PER_SEAT = 5 + 2 + 8 + 16 + 4 + 4
+MLP_FLOPS = 2 * (2366 * 128 + 128 * 128 + 3 * 128 * 64 + 64 * 8)
 
 
 def _peaks():
@@ -58,7 +80,7 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle samples every 200 ms while running."""
+    """nvidia-smi clock / throttle samples every 50 ms while running."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -81,7 +103,7 @@ class ClockSampler:
                         self.rows.append([x.strip() for x in out.split(",")])
                 except Exception:
                     pass
-                self._stop.wait(0.2)
+                self._stop.wait(0.05)
         self._t = threading.Thread(target=run, daemon=True)
         self._t.start()
         return self
@@ -111,8 +133,8 @@ def _template(cfg, n, seed):
 # --------------------------------------------------------------- CPU legs
 
 def _oracle_rollout_worker(args):
-    """Run the oracle tick protocol on a shard (spawned process)."""
-    n, ticks, seed = args
+    """Run the oracle tick protocol of a config on a shard (spawned process)."""
+    n, ticks, seed, conf = args
     import numpy as np
     try:
         from threadpoolctl import threadpool_limits
@@ -123,6 +145,7 @@ def _oracle_rollout_worker(args):
     from qqt_b200 import scenarios
     from qqt_b200.config import SimConfig
     from qqt_b200.policy_init import init_params
+    c = CONFIGS[conf]
     cfg = SimConfig(**scenarios.CFG2)
     p = cfg.n_players
     t = _template(cfg, n, seed)
@@ -139,36 +162,52 @@ def _oracle_rollout_worker(args):
           "lo_bombs": t["bombs_cap"].copy(), "lo_blast": t["blast_cap"].copy(),
           "lo_spd": t["spd"].copy(), "crate_prob": t["crate_prob"].copy(),
           "hazard": np.zeros(n, bool)}
-    params = init_params(cfg.obs_shape, "mlp", seed=1)
+    params = init_params(cfg.obs_shape, c["learner"], seed=1)
     rng = np.random.default_rng(seed)
     ticker = O.ModeTicker(rng.integers(0, 2, n), rng.integers(60, 240, n))
+    dch = 2 * p + 1
+
+    def learner(obs32, mm, bm, pid):
+        u = rng.random((n, 2))
+        if c["learner"] == "mlp":
+            return O.mlp_act(params, obs32, mm[:, pid], bm[:, pid], pid, p, u[:, 0], u[:, 1])[0]
+        ml, bl, _ = O.cnn_forward(params, obs32, pid, p)
+        am, _ = O.masked_sample(ml, mm[:, pid], u[:, 0])
+        ab, _ = O.masked_sample(bl, bm[:, pid], u[:, 1])
+        return np.stack([am, ab], -1)
+
     t0 = time.perf_counter()
     for _ in range(ticks):
         obs, _ = O.observe(cfg, st)
-        obs16 = obs.astype(np.float16)
+        obs32 = obs.astype(np.float16).astype(np.float32)
         mm, bm = O.legal_mask(cfg, st)
-        u = rng.random((n, 2))
-        a0, _, _, _, _ = O.mlp_act(params, obs16.astype(np.float32), mm[:, 0], bm[:, 0], 0, p,
-                                   u[:, 0], u[:, 1])
-        mode = ticker.advance(rng.integers(0, 2, n), rng.integers(60, 240, n))
-        a1 = O.astar_attack(cfg, st, obs16[:, 2 * p + 1].astype(np.float32), mm[:, 1], bm[:, 1], 1,
-                            rng.random((n, 5)).astype(np.float32), mode=mode)
+        a0 = learner(obs32, mm, bm, 0)
+        if c["opponent"] == "astar":
+            mode = ticker.advance(rng.integers(0, 2, n), rng.integers(60, 240, n))
+            a1 = O.astar_attack(cfg, st, obs32[:, dch], mm[:, 1], bm[:, 1], 1,
+                                rng.random((n, 5)).astype(np.float32), mode=mode)
+        elif c["opponent"] == "greedy":
+            a1 = O.greedy_attack(cfg, st, obs32[:, dch], mm[:, 1], bm[:, 1], 1,
+                                 rng.random((n, 5)).astype(np.float32))
+        else:
+            a1 = learner(obs32, mm, bm, 1)
         acts = np.stack([a0, a1], 1)
         rb = rng.random((2, n, p)).astype(np.float32)
         O.step(cfg, st, acts, rb[0], rb[1])
     return n * ticks, time.perf_counter() - t0
 
 
-def cpu_leg(n_envs, ticks, procs, seed=0):
+def cpu_leg(n_envs, ticks, procs, seed=0, conf="cfg2"):
     """Bounded oracle sample on `procs` processes (spawned: no GPU state)."""
     import multiprocessing as mp
     per = max(1, n_envs // procs)
     if procs == 1:
-        steps, dt = _oracle_rollout_worker((per, ticks, seed))
+        steps, dt = _oracle_rollout_worker((per, ticks, seed, conf))
         return steps / dt, steps, dt
     ctx = mp.get_context("spawn")
     with ctx.Pool(procs) as pool:
-        res = pool.map(_oracle_rollout_worker, [(per, ticks, seed + i) for i in range(procs)])
+        res = pool.map(_oracle_rollout_worker,
+                       [(per, ticks, seed + i, conf) for i in range(procs)])
     # workers run concurrently; each times its own loop (process start-up excluded)
     dt = max(r[1] for r in res)
     steps = sum(r[0] for r in res)
@@ -178,11 +217,11 @@ def cpu_leg(n_envs, ticks, procs, seed=0):
 # ------------------------------------------------------------ GPU leg
 
 def build_engine(device, rank, slots=None, groups=1):
-    """The rank's env shard as `groups` independent env groups (one sim, astar
-    bot and rollout buffer each; one shared policy pack)."""
+    """The rank's env shard as `groups` independent env groups (one sim, bot
+    and rollout buffer each; one shared policy pack)."""
     import torch
     from qqt_b200 import scenarios
-    from qqt_b200.bots import AstarBot
+    from qqt_b200.bots import make_bot
     from qqt_b200.config import SimConfig
     from qqt_b200.policy import B200Policy
     from qqt_b200.policy_init import init_params
@@ -193,24 +232,26 @@ def build_engine(device, rank, slots=None, groups=1):
         raise ValueError("envs per GPU must divide into the groups")
     n = N_ENVS // groups
     tmpl = _template(cfg, N_ENVS, 1 + rank)
-    pol = B200Policy(init_params(cfg.obs_shape, "mlp", seed=1), cfg.obs_shape, 2, seats=(0,),
-                     device=device)
+    pol = B200Policy(init_params(cfg.obs_shape, CFG["learner"], seed=1), cfg.obs_shape, 2,
+                     seats=CFG["seats"], device=device, arch=CFG["learner"])
     ros = []
     for g in range(groups):
         part = {k: v[g * n:(g + 1) * n] for k, v in tmpl.items()}
         sim = B200Sim(cfg, n, device=device, seed=1 + rank + 1000 * g, template=part)
         sim.set_template(part, apply=False, seed=1 + rank + 1000 * g, swap_spawns=False)
-        ros.append(Rollout(sim, pol, AstarBot(sim, mode=True), T=TICKS, slots=slots))
+        bot = make_bot(sim, CFG["opponent"], mode=True) if CFG["opponent"] else None
+        ros.append(Rollout(sim, pol, bot, T=TICKS, slots=slots))
     gen = torch.Generator(device=device).manual_seed(1234 + rank)
     return RolloutGroups(ros), gen
 
 
 def instrumented_kernel_times(ro):
     """One eager rollout with CUDA events around every library call:
-    per-kernel launches and mean device duration (ms)."""
+    per-call launches and mean device duration (ms)."""
     import torch
     sim, buf, dr = ro.sim, ro.buf, ro.draws
-    times = {k: [] for k in ("observe", "mlp", "astar", "step", "flush")}
+    bot_name = CFG["opponent"] or "bot"
+    times = {k: [] for k in ("observe", "policy", bot_name, "step", "flush")}
 
     def timed(name, fn):
         a = torch.cuda.Event(enable_timing=True)
@@ -220,7 +261,7 @@ def instrumented_kernel_times(ro):
         b.record()
         times[name].append((a, b))
 
-    bot = ro.opponent
+    bot, seats = ro.opponent, ro.seats
     for t in range(ro.T):
         holder = {}
         b = t % ro.slots
@@ -228,25 +269,76 @@ def instrumented_kernel_times(ro):
             buf.obs_rows[b], buf.mm[b], buf.bm[b], danger=False))))
         obs, mm, bm = holder["obs"], holder["mm"], holder["bm"]
         acts = buf.act[b]
-        timed("mlp", lambda: ro.learner.act_seats(obs, [mm[:, 0]], [bm[:, 0]], dr.u_net[t],
-                                                   [acts[:, 0]], buf.logp[b], buf.val[b]))
-        feed = {"noise": dr.noise[t]}
-        if (bot.calls + 1) % 16 == 0:
-            feed["new_mode"], feed["new_timer"] = dr.tick_mode[0], dr.tick_timer[0]
-        bot.feed(**feed)
-        timed("astar", lambda: bot.act(obs, mm[:, 1], bm[:, 1], 1, out=acts[:, 1]))
+        timed("policy", lambda: ro.learner.act_seats(
+            obs, [mm[:, s] for s in seats], [bm[:, s] for s in seats], dr.u_net[t],
+            [acts[:, s] for s in seats], buf.logp[b], buf.val[b]))
+        if bot is not None:
+            o = ro.opp_seat
+            ro.feed_opponent(t)
+            timed(bot_name, lambda: bot.act(obs, mm[:, o], bm[:, o], o, out=acts[:, o]))
         timed("step", lambda: sim.step(acts, auto_reset=True,
                                        crate_draws=(dr.crate[t, 0], dr.crate[t, 1]),
                                        reward_out=buf.rew[b], done_out=buf.done[b],
-                                       info_planes=False))
+                                       hit_out=buf.dmg[b], info_planes=False))
         if t % 16 == 15:
             timed("flush", lambda: sim.flush_recycle())
     torch.cuda.synchronize()
-    return {k: (len(v), sum(a.elapsed_time(b) for a, b in v) / max(1, len(v))) for k, v in times.items()}
+    return {k: (len(v), sum(a.elapsed_time(b) for a, b in v) / max(1, len(v)))
+            for k, v in times.items()}
+
+
+def _launches_per_tick():
+    """Kernels per tick of one env group: observe, policy (fused MLP: 1;
+    CNN: trunk + heads per seat), bot (astar: cap + field; greedy: 1), step."""
+    pol = 1 if CFG["learner"] == "mlp" else 1 + len(CFG["seats"])
+    bot = {"astar": 2, "greedy": 1, None: 0}[CFG["opponent"]]
+    return 1 + pol + bot + 1
+
+
+def ppo_leg(grp, device):
+    """cfg4: one PPO update (4 epochs x 8 minibatches) on the seat-0 rollout
+    buffer, after a bootstrap value for the state the rollout ended in;
+    device time by CUDA events."""
+    import torch
+    from qqt_b200.ppo import MLPActorCritic, PPOConfig, ppo_update
+    ro = grp.ros[0]
+    sim, buf, pol = ro.sim, ro.buf, ro.learner
+    cfg = PPOConfig(epochs=4, minibatches=8, lr=1e-4, entropy_coef=0.03, entropy_final=0.03)
+    model = MLPActorCritic(sim.cfg.obs_shape, 2).to(device)
+    model.load_state_dict({k: v.clone() for k, v in pol.params.items()}, strict=False)
+    opt = torch.optim.Adam(model.parameters(), lr=cfg.lr, eps=1e-5)
+    n = sim.num_envs
+    rows = torch.zeros((n, sim.obs_stride), dtype=torch.float16, device=device)
+    mm = torch.ones((n, 2, 5), dtype=torch.bool, device=device)
+    bm = torch.ones((n, 2, 2), dtype=torch.bool, device=device)
+    acts = torch.zeros((n, 2, 2), dtype=torch.int64, device=device)
+    last = torch.zeros((len(ro.seats), n), dtype=torch.float32, device=device)
+    u = torch.rand((len(ro.seats), n, 2), device=device)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record()
+    obs, mmv, bmv = sim.observe_and_mask(rows, mm, bm, danger=False)
+    pol.act_seats(obs, [mmv[:, s] for s in ro.seats], [bmv[:, s] for s in ro.seats], u,
+                  [acts[:, s] for s in ro.seats], None, last)
+    data = {"obs": buf.obs_rows, "mm": buf.mm[:, :, 0], "bm": buf.bm[:, :, 0],
+            "act": buf.act[:, :, 0], "logp": buf.logp[:, 0], "val": buf.val[:, 0],
+            "rew": buf.rew[:, :, 0], "done": buf.done, "dmg": buf.dmg[:, :, 0]}
+    stats = ppo_update(model, opt, data, last[0], cfg, cfg.entropy_coef, pid=0)
+    pol.load_state_dict({k: p.detach() for k, p in model.state_dict().items()
+                         if k in pol.params})
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    samples = buf.done.numel()
+    return {"ms": round(ms, 2), "samples": samples,
+            "samples_per_s": round(samples / (ms / 1e3), 1),
+            "minibatches": cfg.epochs * cfg.minibatches,
+            "includes": "bootstrap value, GAE kernel, advantage stats, 32 x (forward, "
+                        "backward, gradient all-reduce, clip, Adam), policy repack",
+            "losses": {k: round(v, 5) for k, v in stats.items()}}
 
 
 def gpu_bench(args):
-    import numpy as np
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -259,7 +351,8 @@ def gpu_bench(args):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device(device))
-    grp, gen = build_engine(device, rank, args.slots, args.groups)
+    groups = 1 if CFG["ppo"] else args.groups
+    grp, gen = build_engine(device, rank, args.slots, groups)
     # first tick eagerly (one-time set-up: resolve tiers, ticker state)
     for ro in grp.ros:
         ro.draws.generate(gen)
@@ -332,45 +425,53 @@ def gpu_bench(args):
     grp.graph = None
     torch.cuda.synchronize()
 
+    ppo = None
+    if CFG["ppo"]:
+        ppo = ppo_leg(grp, device)
+        t_p = torch.tensor([ppo["ms"]], device=device)
+        if dist:
+            dist.all_reduce(t_p, op=dist.ReduceOp.MAX)
+        ppo["ms"] = round(float(t_p.item()), 2)
+        ppo["samples_per_s"] = round(ppo["samples"] * world / (ppo["ms"] / 1e3), 1)
+
     out = None
     if rank == 0:
         hbm, tflops, src = _peaks()
         per = {}
+        n_seats = len(CFG["seats"])
         for k, (launches, mean_ms) in kt.items():
             if launches == 0:
                 continue
-            if k == "mlp":
-                name, byt = "mlp", ALG_BYTES["mlp_gemm"] + ALG_BYTES["mlp_heads"]
-            else:
-                name, byt = k, ALG_BYTES.get(k, 169 * 8)
-            per[name] = {"launches_per_rollout": launches, "mean_ms": round(mean_ms, 5),
-                         "share": None, "alg_bytes_per_launch": byt * n_inst}
+            byt = ALG_BYTES["policy"] + n_seats * POLICY_PER_SEAT if k == "policy" else \
+                ALG_BYTES.get(k, 169 * 8)
+            per[k] = {"launches_per_rollout": launches, "mean_ms": round(mean_ms, 5),
+                      "share": None, "alg_bytes_per_launch": byt * n_inst}
         tot = sum(v["launches_per_rollout"] * v["mean_ms"] for v in per.values())
         for v in per.values():
             v["share"] = round(v["launches_per_rollout"] * v["mean_ms"] / tot, 4)
         dom = max((k for k in per if k != "flush"), key=lambda k: per[k]["share"])
         d = per[dom]
         achieved = d["alg_bytes_per_launch"] / (d["mean_ms"] / 1e3) / 1e9
-        traffic = _ncu_traffic(dom)
+        traffic = _ncu_traffic(dom) if args.config == "cfg2" else None
         cores = args.cpu_procs
-        cpu_v, cpu_steps, cpu_dt = cpu_leg(args.cpu_envs, args.cpu_ticks, cores)
+        cpu_v, cpu_steps, cpu_dt = cpu_leg(args.cpu_envs, args.cpu_ticks, cores, conf=args.config)
         out = {
             "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32 sim, fp16xfp16->f32 GEMM",
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 sim, fp16xfp16->f32 tensor-core policy",
             "data": "synthetic (seeded template maps, random-init policy, device RNG draws)",
-            "config": {"workload": WORKLOAD, "envs_per_gpu": N_ENVS, "ticks": TICKS,
-                       "env_groups_per_gpu": args.groups,
+            "config": {"workload": CFG["workload"], "envs_per_gpu": N_ENVS, "ticks": TICKS,
+                       "env_groups_per_gpu": groups,
                        "parallelism": f"env shards x{world}, no rollout collective",
                        "l2": "flushed (256 MB write) between timed steps; each step also "
-                             "writes a 3.4 GB observation buffer",
+                             "writes its T x N observation buffer (> L2)",
                        "cuda_graph": True},
             "e2e": {"value": round(e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            # per tick and group: observe, fused MLP, astar cap + field, step;
-            # crate recycling every 16 ticks
-            "gpu_launches": (TICKS * 5 + TICKS // 16) * args.groups * args.steps,
+            # per tick and group: observe, policy, bot, step; recycling every 16 ticks
+            "gpu_launches": (TICKS * _launches_per_tick() + TICKS // 16) * groups * args.steps,
             "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1),
                          "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                          "peak_source": src, "traffic": traffic,
@@ -381,6 +482,8 @@ def gpu_bench(args):
                                        f"{args.cpu_ticks} ticks of the same workload"},
             "clocks": clk.summary(),
         }
+        if ppo is not None:
+            out["ppo_update"] = ppo
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -422,9 +525,9 @@ def reference_arm(args):
     procs = args.cpu_procs_ref or max(1, len(os.sched_getaffinity(0)))
     vals = []
     for _ in range(args.warmup):
-        cpu_leg(procs * 8, 2, procs)
+        cpu_leg(procs * 8, 2, procs, conf=args.config)
     for i in range(args.steps):
-        v, steps, dt = cpu_leg(procs * 32, args.ref_ticks, procs, seed=i)
+        v, steps, dt = cpu_leg(procs * 32, args.ref_ticks, procs, seed=i, conf=args.config)
         vals.append((steps, dt))
     steps = sum(s for s, _ in vals)
     dt = sum(d for _, d in vals)
@@ -434,7 +537,7 @@ def reference_arm(args):
             "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 2),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32 sim, f64 policy (numpy)", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "sample_envs": procs * 32,
+            "config": {"workload": CFG["workload"], "sample_envs": procs * 32,
                        "sample_ticks": args.ref_ticks},
             "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": procs,
                              "kind": "port",
@@ -451,20 +554,24 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--cpu-envs", type=int, default=256)
-    ap.add_argument("--cpu-ticks", type=int, default=8)
+    ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
+    ap.add_argument("--cpu-envs", type=int, default=0, help="CPU sample envs (0: per config)")
+    ap.add_argument("--cpu-ticks", type=int, default=0, help="CPU sample ticks (0: per config)")
     ap.add_argument("--cpu-procs", type=int, default=1)
     ap.add_argument("--cpu-procs-ref", type=int, default=0)
     ap.add_argument("--ref-ticks", type=int, default=4)
-    ap.add_argument("--envs", type=int, default=5632, help="envs per GPU (profiling cases)")
+    ap.add_argument("--envs", type=int, default=0, help="envs per GPU (profiling cases)")
     ap.add_argument("--ticks", type=int, default=128, help="ticks per rollout (multiple of 16)")
     ap.add_argument("--groups", type=int, default=2,
                     help="independent env groups per GPU, each on its own stream")
     ap.add_argument("--slots", type=int, default=0,
                     help="rollout-buffer slots (0 = one per tick; fewer = ring, profiling only)")
     args = ap.parse_args()
-    global N_ENVS, TICKS
-    N_ENVS, TICKS = args.envs, args.ticks
+    global CFG, N_ENVS, TICKS
+    CFG = CONFIGS[args.config]
+    N_ENVS, TICKS = args.envs or CFG["envs"], args.ticks
+    args.cpu_envs = args.cpu_envs or CFG["cpu"][0]
+    args.cpu_ticks = args.cpu_ticks or CFG["cpu"][1]
     if TICKS % 16:
         raise SystemExit("--ticks must be a multiple of 16")
     out = reference_arm(args) if args.impl == "reference" else gpu_bench(args)

@@ -121,6 +121,10 @@ typedef struct QqtStepOut {
   int64_t *n_alive;         /* [N]                                            */
   uint8_t *covered, *triggered; /* [C][N]                                     */
   uint8_t *reset_mask;      /* [N] envs reset by the device auto-reset        */
+  uint8_t *hit;             /* [N][P] lost hp this tick in an env that did not
+                               end: the rollout's damage flag, (hp before the
+                               step - hp after the auto-reset step) > 0
+                               (train/ppo.py:247-251); may be NULL           */
 } QqtStepOut;
 
 /* One tick of the environment, fused: fuse countdown, sequential bomb

@@ -323,13 +323,14 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
     }
 
     // ---- 9. damage and invulnerability
-    int flat1 = 0, hp_new = 0, alive = 0, died = 0;
+    int flat1 = 0, hp_new = 0, alive = 0, died = 0, lost_hp = 0;
     if (p < P) {
       flat1 = center_cell(me.y, me.x, h, w);
       const bool hit = me.alive0 && cov[flat1];
       const bool hit_eff = hit && me.invuln <= 0;
       hp_new = max(me.hp - (hit_eff ? 1 : 0), 0);
       died = hit_eff && hp_new == 0;
+      lost_hp = hp_new < me.hp;
       alive = me.alive0 && !died;
       me.invuln = me.invuln - 1 > 0 ? me.invuln - 1 : 0;
       if (hit_eff) me.invuln = cfg.invuln_ticks;
@@ -456,6 +457,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
       const size_t ri = (size_t)e * P + p;
       if (a.out.reward) a.out.reward[ri] = reward;
       if (a.out.died) a.out.died[ri] = (uint8_t)died;
+      if (a.out.hit) a.out.hit[ri] = (uint8_t)(lost_hp && !done);
       if (a.out.winner) a.out.winner[ri] = (uint8_t)winner;
     }
     if (lane == 0) {

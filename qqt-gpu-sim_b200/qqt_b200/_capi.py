@@ -51,7 +51,8 @@ class QqtTemplate(ctypes.Structure):
 
 class QqtStepOut(ctypes.Structure):
     _fields_ = [("reward", c_p), ("done", c_p), ("died", c_p), ("winner", c_p),
-                ("n_alive", c_p), ("covered", c_p), ("triggered", c_p), ("reset_mask", c_p)]
+                ("n_alive", c_p), ("covered", c_p), ("triggered", c_p), ("reset_mask", c_p),
+                ("hit", c_p)]
 
 
 _lib = None

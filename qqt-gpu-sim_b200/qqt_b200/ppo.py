@@ -58,6 +58,7 @@ class MLPActorCritic(nn.Module):
         super().__init__()
         c, h, w = obs_shape
         self.obs_shape = tuple(obs_shape)
+        self.k_in = c * h * w
         self.n_players = n_players
         self.shared = nn.Sequential(nn.Linear(c * h * w, 128), nn.LayerNorm(128), nn.ReLU(),
                                     nn.Linear(128, 128), nn.LayerNorm(128), nn.ReLU())
@@ -70,7 +71,8 @@ class MLPActorCritic(nn.Module):
 
     def forward(self, obs: torch.Tensor, pid: int = 0):
         n = obs.shape[0]
-        x = obs.reshape(n, -1).to(self.shared[0].weight.dtype)
+        # (N, C, H, W) or the engine's row-padded (N, stride >= C*H*W) rows
+        x = obs.reshape(n, -1)[:, : self.k_in].to(self.shared[0].weight.dtype)
         w0 = self.shared[0].weight[:, getattr(self, f"inv_cols_{pid}")]
         x = F.linear(x, w0, self.shared[0].bias)
         x = self.shared[1:](x)
@@ -167,7 +169,8 @@ def ppo_update(model: MLPActorCritic, opt, data: dict, last_val, cfg: PPOConfig,
             pool = torch.cat([base, rare_idx.repeat(over - 1)])
     mb = max(1, total // cfg.minibatches)
     perm_fn = perm_fn or (lambda k: torch.randperm(k, device=dev))
-    out = {"pg": 0.0, "vf": 0.0, "ent": 0.0, "kl": 0.0, "clipfrac": 0.0}
+    # statistics stay on the device; one host read at the end
+    out = {k: torch.zeros((), device=dev) for k in ("pg", "vf", "ent", "kl", "clipfrac")}
     updates = 0
     params = [p for p in model.parameters()]
     for _ in range(cfg.epochs):
@@ -197,10 +200,10 @@ def ppo_update(model: MLPActorCritic, opt, data: dict, last_val, cfg: PPOConfig,
             torch.nn.utils.clip_grad_norm_(params, cfg.max_grad_norm)
             opt.step()
             with torch.no_grad():
-                out["pg"] += float(pg)
-                out["vf"] += float(vf)
-                out["ent"] += float(ent_m)
-                out["kl"] += float((old_logp[sel] - logp).mean())
-                out["clipfrac"] += float(((ratio - 1).abs() > cfg.clip_eps).float().mean())
+                out["pg"] += pg.detach()
+                out["vf"] += vf.detach()
+                out["ent"] += ent_m.detach()
+                out["kl"] += (old_logp[sel] - logp).mean().detach()
+                out["clipfrac"] += ((ratio - 1).abs() > cfg.clip_eps).float().mean()
             updates += 1
-    return {k: v / max(1, updates) for k, v in out.items()}
+    return {k: float(v) / max(1, updates) for k, v in out.items()}

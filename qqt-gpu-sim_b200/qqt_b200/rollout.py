@@ -38,6 +38,7 @@ class DeviceRolloutBuffer:
         self.val = torch.zeros((T, n_seats, n), dtype=torch.float32, device=d)
         self.rew = torch.zeros((T, n, p), dtype=torch.float32, device=d)
         self.done = torch.zeros((T, n), dtype=torch.bool, device=d)
+        self.dmg = torch.zeros((T, n, p), dtype=torch.bool, device=d)   # hp lost, env not ended
 
     def obs(self, t):
         c, h, w = self.obs_shape
@@ -121,23 +122,30 @@ class Rollout:
         if self.opponent is not None:
             o = self.opp_seat
             bot = self.opponent
-            if isinstance(bot, AstarBot):
-                feed = {"noise": dr.noise[t]}
-                if bot.use_mode and (bot.calls + 1) % 16 == 0:
-                    k = (bot.calls + 1) // 16
-                    feed["new_mode"] = dr.tick_mode[k % dr.tick_mode.shape[0]]
-                    feed["new_timer"] = dr.tick_timer[k % dr.tick_timer.shape[0]]
-                bot.feed(**feed)
-            elif isinstance(bot, GreedyBot):
-                bot.feed(noise=dr.noise[t])
-            elif isinstance(bot, RandomBot):
-                bot.feed(u_move=dr.noise[t, :, 0], u_bomb=dr.noise[t, :, 1])
+            self.feed_opponent(t)
             bot.act(obs, mm[:, o], bm[:, o], o, out=acts[:, o])
             main.wait_stream(self.side)
         sim.step(acts, auto_reset=True, crate_draws=(dr.crate[t, 0], dr.crate[t, 1]),
-                 reward_out=buf.rew[b], done_out=buf.done[b], info_planes=False)
+                 reward_out=buf.rew[b], done_out=buf.done[b], hit_out=buf.dmg[b],
+                 info_planes=False)
         if self.flush_every and t % self.flush_every == self.flush_every - 1:
             sim.flush_recycle()
+
+    def feed_opponent(self, t: int) -> None:
+        """Hand the opponent bot its draws for tick t (noise; the astar mode
+        ticker's new modes/timers every 16th call)."""
+        bot, dr = self.opponent, self.draws
+        if isinstance(bot, AstarBot):
+            feed = {"noise": dr.noise[t]}
+            if bot.use_mode and (bot.calls + 1) % 16 == 0:
+                k = (bot.calls + 1) // 16
+                feed["new_mode"] = dr.tick_mode[k % dr.tick_mode.shape[0]]
+                feed["new_timer"] = dr.tick_timer[k % dr.tick_timer.shape[0]]
+            bot.feed(**feed)
+        elif isinstance(bot, GreedyBot):
+            bot.feed(noise=dr.noise[t])
+        elif isinstance(bot, RandomBot):
+            bot.feed(u_move=dr.noise[t, :, 0], u_bomb=dr.noise[t, :, 1])
 
     def collect(self) -> DeviceRolloutBuffer:
         """Run T ticks eagerly (kernel launches only; no host synchronisation

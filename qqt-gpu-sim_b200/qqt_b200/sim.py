@@ -144,6 +144,7 @@ class B200Sim:
         self._done = torch.zeros((n,), dtype=torch.bool, device=d)
         self._died = torch.zeros((n, p), dtype=torch.bool, device=d)
         self._winner = torch.zeros((n, p), dtype=torch.bool, device=d)
+        self._hit = torch.zeros((n, p), dtype=torch.bool, device=d)
         self._n_alive = torch.zeros((n,), dtype=torch.int64, device=d)
         self._covered = torch.zeros((hw, n), dtype=torch.bool, device=d)
         self._triggered = torch.zeros((hw, n), dtype=torch.bool, device=d)
@@ -188,6 +189,7 @@ class B200Sim:
         o.covered = self._covered.data_ptr()
         o.triggered = self._triggered.data_ptr()
         o.reset_mask = self._reset_mask.data_ptr()
+        o.hit = self._hit.data_ptr()
         return o
 
     def _stream(self):
@@ -475,6 +477,7 @@ class B200Sim:
         return r[:, 0, :].t().contiguous(), r[:, 1, :].t().contiguous()
 
     def step(self, actions: torch.Tensor, auto_reset: bool = True, crate_draws=None,
+             hit_out: torch.Tensor | None = None,
              reward_out: torch.Tensor | None = None, done_out: torch.Tensor | None = None,
              info_planes: bool = True):
         """One tick (sim/torch_sim.py:895-1261) -> (reward (N,P), done (N,), info).
@@ -492,8 +495,14 @@ class B200Sim:
             acts = acts.to(self.device, torch.int64).contiguous()
         cout = self._cout
         reward, done = self._reward, self._done
-        if reward_out is not None or done_out is not None or not info_planes:
+        hit = self._hit
+        if reward_out is not None or done_out is not None or hit_out is not None or not info_planes:
             cout = capi.QqtStepOut.from_buffer_copy(self._cout)
+            if hit_out is not None:
+                if hit_out.dtype != torch.bool or not hit_out.is_contiguous():
+                    raise ValueError("hit_out must be a contiguous bool (N, P) slot")
+                cout.hit = hit_out.data_ptr()
+                hit = hit_out
             if not info_planes:
                 cout.covered = None
                 cout.triggered = None
@@ -518,7 +527,7 @@ class B200Sim:
         capi.check(rc, "qqt_step")
         self._first_step = False
         n, h, w = self.num_envs, self.cfg.height, self.cfg.width
-        info = {"n_alive": self._n_alive, "died": self._died, "winner": self._winner,
+        info = {"n_alive": self._n_alive, "died": self._died, "winner": self._winner, "hit": hit,
                 "blast": self._covered.t().view(n, h, w),
                 "trig": self._triggered.t().view(n, h, w)}
         if auto_reset and not dev_reset:

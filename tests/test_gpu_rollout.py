@@ -76,7 +76,7 @@ def _restore(sim, bot, snap):
 def _buffers(ro):
     b = ro.buf
     return {k: getattr(b, k).clone() for k in ("obs_rows", "mm", "bm", "act", "logp", "val",
-                                                "rew", "done")}
+                                                "rew", "done", "dmg")}
 
 
 def test_rollout_ticks_vs_oracle():
@@ -112,7 +112,10 @@ def test_rollout_ticks_vs_oracle():
         assert np.array_equal(acts[:, 1], a1), f"t={t} astar actions"
         assert np.abs(ro.buf.logp[t, 0].cpu().numpy() - lp0).max() <= 1e-3
         assert np.abs(ro.buf.val[t, 0].cpu().numpy() - v0).max() <= 2e-3 * max(np.abs(v0).max(), 1e-3)
+        hp0 = st["hp"].astype(np.int32)
         rew, done, _ = O.step(cfg, st, acts, dr["crate"][t, 0], dr["crate"][t, 1])
+        dmg = ((hp0 - st["hp"].astype(np.int32)) > 0) & ~done[:, None]
+        assert np.array_equal(ro.buf.dmg[t].cpu().numpy(), dmg), f"t={t} damage flags"
         assert not done.any(), "no episode ends inside this rollout (resets not exercised here)"
         assert np.array_equal(ro.buf.rew[t].cpu().numpy(), rew), f"t={t} reward"
         assert np.array_equal(ro.buf.done[t].cpu().numpy(), done), f"t={t} done"
