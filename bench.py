@@ -48,6 +48,11 @@ CONFIGS = {
                  workload="cfg4: cfg2 map, N=65536 envs per GPU, self-play (one random-init "
                           "MLP for both seats, one N=256 GEMM), 128-tick rollout; PPO update "
                           "(4 epochs x 8 minibatches, seat-0 buffer) timed separately"),
+    "cfg3": dict(envs=16384, learner=None, seats=(), opponent=None, ppo=False, cpu=(64, 1),
+                 workload="cfg3: chain/danger stress, 13x13 border-wall map, N=16384 envs per GPU, "
+                          "20-40 bombs per env (fuse U{1..30}, blast U{1..5}); one step = step "
+                          "(IDLE, no reset) + danger map + obs + masks + astar V_safe/V_opp and "
+                          "actions for both players, from the same stress state every step"),
     "cfg5": dict(envs=5632, learner="cnn", seats=(0,), opponent="greedy", ppo=False, cpu=(16, 2),
                  workload="cfg5: cfg2 map, N=5632 envs per GPU, random-init CNN learner seat 0 "
                           "vs greedy seat 1, 128-tick rollout"),
@@ -490,6 +495,167 @@ def gpu_bench(args):
     return out
 
 
+# ------------------------------------------------------------ cfg3 stress
+
+def _stress_state(cfg, n, seed):
+    """Env-major numpy state of the cfg3 stress case."""
+    import numpy as np
+    from qqt_b200 import scenarios
+    p = cfg.n_players
+    fuse, owner, blast = scenarios.bomb_stress(n, cfg, seed)
+    wall = np.broadcast_to(scenarios.border_walls(cfg.height, cfg.width), fuse.shape).copy()
+    spawn = np.array(scenarios.open_spawns(cfg), np.float32)
+    return {"wall": wall, "brick": np.zeros_like(wall), "crate": np.zeros_like(wall),
+            "recycle": np.zeros_like(wall), "fuse": fuse, "owner": owner, "bomb_blast": blast,
+            "pos": np.broadcast_to(spawn, (n, p, 2)).copy(), "alive": np.ones((n, p), bool),
+            "hp": np.full((n, p), cfg.max_hp, np.uint8), "invuln": np.zeros((n, p), np.int64),
+            "t": np.full(n, 40, np.int64)}
+
+
+def _stress_oracle_worker(args):
+    n, seed = args
+    import numpy as np
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(1)
+    except Exception:
+        pass
+    from oracle import qqt_oracle as O
+    from qqt_b200 import scenarios
+    from qqt_b200.config import SimConfig
+    cfg = SimConfig(**scenarios.CFG1)
+    p = cfg.n_players
+    st = _stress_state(cfg, n, seed)
+    full = {"since_bomb": np.full((n, p), cfg.place_dist_cooldown, np.int32),
+            "bombs_cap": np.full((n, p), cfg.growth_bombs_start, np.int64),
+            "blast_cap": np.full((n, p), cfg.growth_blast_start, np.int64),
+            "spd_g": np.full((n, p), cfg.growth_speed_start, np.float32),
+            "pending_lost": np.zeros((n, p), np.int64), "combo": np.zeros((n, p), np.int64),
+            "last_hit": np.full((n, p), -10 ** 9, np.int64),
+            "lo_bombs": np.full((n, p), cfg.growth_bombs_start, np.int64),
+            "lo_blast": np.full((n, p), cfg.growth_blast_start, np.int64),
+            "lo_spd": np.full((n, p), cfg.growth_speed_start, np.float32),
+            "crate_prob": np.full(n, cfg.growth_crate_prob, np.float32),
+            "hazard": np.zeros(n, bool)}
+    st.update(full)
+    rng = np.random.default_rng(seed)
+    acts = np.zeros((n, p, 2), np.int64)
+    acts[..., 0] = 4
+    t0 = time.perf_counter()
+    rb = rng.random((2, n, p)).astype(np.float32)
+    O.step(cfg, st, acts, rb[0], rb[1])
+    obs, _ = O.observe(cfg, st)
+    obs32 = obs.astype(np.float16).astype(np.float32)
+    mm, bm = O.legal_mask(cfg, st)
+    for pid in range(p):
+        O.astar_attack(cfg, st, obs32[:, 2 * p + 1], mm[:, pid], bm[:, pid], pid,
+                       rng.random((n, 5)).astype(np.float32), return_fields=True)
+    return n, time.perf_counter() - t0
+
+
+def stress_bench(args):
+    """cfg3: device time of step + danger/obs/masks + both players' astar
+    fields and actions, restarted from the stress state every step."""
+    import torch
+    from qqt_b200 import scenarios
+    from qqt_b200.bots import AstarBot
+    from qqt_b200.config import SimConfig
+    from qqt_b200.sim import B200Sim
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = f"cuda:{local}"
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device(device))
+    cfg = SimConfig(**scenarios.CFG1)
+    n, p = N_ENVS, cfg.n_players
+    sim = B200Sim(cfg, n, device=device, seed=7 + rank)
+    sim.load_numpy_state(_stress_state(cfg, n, 7 + rank))
+    snap = {k: v.clone() for k, v in sim._buf.items()}
+    acts = torch.zeros((n, p, 2), dtype=torch.int64, device=device)
+    acts[..., 0] = 4
+    gen = torch.Generator(device=device).manual_seed(99 + rank)
+    draws = (torch.rand((n, p), device=device, generator=gen),
+             torch.rand((n, p), device=device, generator=gen))
+    bots = []
+    for pid in range(p):
+        b = AstarBot(sim, mode=False)
+        b.keep_fields = True
+        bots.append(b)
+    noise = torch.rand((p, n, 5), device=device, generator=gen)
+    l2 = torch.empty((64 << 20,), dtype=torch.float32, device=device)
+
+    def restore():
+        for k, v in snap.items():
+            sim._buf[k].copy_(v)
+
+    def tick():
+        sim.step(acts, auto_reset=False, crate_draws=draws, info_planes=False)
+        obs, mm, bm = sim.observe_and_mask(danger=True)
+        for pid, b in enumerate(bots):
+            b.feed(noise=noise[pid])
+            b.act(obs, mm[:, pid], bm[:, pid], pid)
+
+    restore()
+    tick()                                  # first step: records the blast tiers
+
+    def timed_tick(ev):
+        restore()
+        l2.zero_()                          # flush L2 (not timed)
+        ev[0].record()
+        tick()
+        ev[1].record()
+
+    mk = lambda: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))  # noqa: E731
+    for _ in range(args.warmup):
+        timed_tick(mk())
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    evs = [mk() for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        for ev in evs:
+            timed_tick(ev)
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in evs)
+    t_max = torch.tensor([ms], device=device)
+    if dist:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+        dist.destroy_process_group()
+    ms = float(t_max.item())
+    if rank != 0:
+        return None
+    value = n * world * args.steps / (ms / 1e3)
+    cpu_n = args.cpu_envs
+    steps_c, dt_c = _stress_oracle_worker((cpu_n, 0))
+    hbm, _, src = _peaks()
+    alg = ALG_BYTES["step"] + ALG_BYTES["observe"] + 169 * 4 + p * (ALG_BYTES["astar"] + 2 * 169 * 4)
+    return {"metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 sim", "data": "synthetic (seeded bomb-stress states)",
+            "config": {"workload": CFG["workload"], "envs_per_gpu": n,
+                       "l2": "flushed (256 MB write) before each timed step"},
+            "e2e": None, "gpu_launches": (1 + 1 + 2 * p) * args.steps,
+            "roofline": {"kernel": "stress tick", "bound": "hbm",
+                         "achieved": round(alg * value / world / 1e9, 1), "peak": hbm,
+                         "unit": "GB/s", "frac": round(alg * value / world / 1e9 / hbm, 4),
+                         "peak_source": src, "traffic": None},
+            "cpu_baseline": {"value": round(steps_c / dt_c, 1), "unit": UNIT, "cores": 1,
+                             "kind": "port",
+                             "sample": f"oracle, {cpu_n} envs x 1 stress tick"},
+            "clocks": clk.summary()}
+
+
 def _ncu_traffic(kernel):
     """DRAM bytes per launch from the committed ncu summary, if present."""
     path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
@@ -549,6 +715,12 @@ def reference_arm(args):
 
 
 def main():
+    # exactly one line on stdout: libraries (NCCL's version banner, ...) print
+    # to file descriptor 1, so it points at stderr and the JSON line goes to a
+    # saved copy of the original stdout
+    json_fd = os.dup(1)
+    sys.stdout.flush()
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
@@ -574,9 +746,15 @@ def main():
     args.cpu_ticks = args.cpu_ticks or CFG["cpu"][1]
     if TICKS % 16:
         raise SystemExit("--ticks must be a multiple of 16")
-    out = reference_arm(args) if args.impl == "reference" else gpu_bench(args)
+    if args.impl == "reference":
+        out = reference_arm(args)
+    elif args.config == "cfg3":
+        out = stress_bench(args)
+    else:
+        out = gpu_bench(args)
     if out is not None:
-        print(json.dumps(out))
+        os.write(json_fd, (json.dumps(out) + "\n").encode())
+    os.close(json_fd)
 
 
 if __name__ == "__main__":
