@@ -1,207 +1,399 @@
-// CNN policy trunk (train/model.py:77-101, 187-190): conv0 3x3 (14->16, the
-// seat's view permutation folded into its input-channel order) -> LN[16,H,W]
-// -> ReLU -> conv 3x3 16->32 -> LN -> ReLU -> conv 3x3 32->64 -> LN -> ReLU
-// -> conv 1x1 64->8 -> LN -> ReLU -> flatten -> Linear(8HW -> 128).
-// The output (first Linear incl. bias) goes to the same pre-activation buffer
-// as the MLP's first layer; k_mlp_heads then runs the shared tail
-// (LN, ReLU, 128x128, LN, ReLU, heads, masking, sampling) unchanged, because
-// the CNN's `shared` stack after its first Linear is the MLP's.
+// CNN policy (train/model.py:77-101, 187-196) on the 5th-generation tensor
+// cores.
 //
-// One block (256 threads) per (env, seat).  Activations live in shared
-// memory as zero-bordered (H+2)x(W+2) planes; a work item is 4 output
-// channels of one pixel; the LayerNorms are block reductions.  fp32 FMA on
-// the CUDA cores (first version; a tensor-core implicit GEMM is the next
-// step).
+// Trunk: conv0 3x3 (14 -> 16, the seat's view permutation folded into its
+// input-channel order) -> LN[16,H,W] -> ReLU -> conv 3x3 16 -> 32 -> LN ->
+// ReLU -> conv 3x3 32 -> 64 -> LN -> ReLU -> conv 1x1 64 -> 8 -> LN -> ReLU
+// -> flatten (c*HW + y*W + x).
+//
+// k_cnn_trunk (persistent, one CTA of 128 threads per SM, one sample at a
+// time): the sample's activation lives in shared memory as a zero-bordered
+// 15x15 pixel grid, one 128-byte row per pixel (channels K-major, fp16 hi
+// and lo halves, 128-byte swizzle) with 16 margin rows on each side.  A 3x3
+// convolution is then nine GEMMs whose A operands are the same buffer
+// shifted by (ky-1)*15 + (kx-1) rows: the descriptor's start address moves,
+// nothing is copied (the swizzle follows absolute shared-memory address
+// bits, so any row offset is a valid operand start).  Each layer runs
+// M = 2 x 128 padded pixels (225 used, border rows ignored) x N = Cout,
+// K = Cin per tap, with three products per K step (A_hi*W_hi + A_hi*W_lo +
+// A_lo*W_hi; conv0's input is the exact fp16 observation, so two).  All
+// conv weights stay resident in shared memory as pre-swizzled fp16 hi/lo
+// images (one bulk copy per CTA).  The epilogue (thread = TMEM lane = pixel
+// row) adds the bias, computes the sample's LayerNorm statistics with two
+// block reductions (mean, then the centred sum of squares), applies the
+// affine LN and ReLU, splits into fp16 hi/lo and writes the next layer's
+// input into the same buffer; the last layer writes the flattened
+// activation to global memory as fp16 hi and lo rows of 1408 (1352 + zero
+// pad).
+//
+// Linear(1352 -> 128) and the shared tail (LN, ReLU, 128x128, LN, ReLU,
+// heads, masking, sampling) are k_mlp_fused with a split A operand.
+//
+// Geometry: H = W = 13 (the reference's board), P = 2 channel layout (C=14).
 
 #include "qqt_common.cuh"
 
 namespace qqt {
 
-constexpr int kCnnThreads = 256;
+constexpr int kCnnH = 13, kCnnW = 13, kCnnHW = 169, kCnnPW = 15, kCnnPP = 225;
+constexpr int kCnnKIn = 8 * kCnnHW;                  // 1352 flattened features
+constexpr int kCnnKP = 1408;                         // padded to 22 K tiles of 64
+constexpr int kActMargin = 16, kActRows = 288;       // 16 + 256 + 16
+constexpr int kActBytes = kActRows * 128;            // one of hi / lo
+// weight images (bytes, per hi / lo): conv0 16 rows x 3 groups (4 taps of
+// 16 channels per 128-byte row), conv1 32 x 3, conv2 64 x 5 (2 taps of 32),
+// conv3 16 rows (8 real) x 1
+constexpr int kW0 = 3 * 16 * 128, kW1 = 3 * 32 * 128, kW2 = 5 * 64 * 128, kW3 = 16 * 128;
 
-struct CnnPackLayout {
-  // float offsets
-  size_t w0, b0, g0, be0, w1, b1, g1, be1, w2, b2, g2, be2, w3, b3, g3, be3, wl, bl, tail, total;
+struct CnnLayout {
+  size_t c0, c1, c2, c3, wbytes;          // image offsets (bytes); c0 is per seat
+  size_t lnf;                             // float block (bytes offset)
+  size_t mlp, total;                      // embedded MLP pack of the linear + tail
+};
+// float block (floats from lnf): LN gamma/beta [C][HW] per layer, conv biases
+enum {
+  LF_G0 = 0, LF_B0 = LF_G0 + 16 * kCnnHW, LF_G1 = LF_B0 + 16 * kCnnHW,
+  LF_B1 = LF_G1 + 32 * kCnnHW, LF_G2 = LF_B1 + 32 * kCnnHW, LF_B2 = LF_G2 + 64 * kCnnHW,
+  LF_G3 = LF_B2 + 64 * kCnnHW, LF_B3 = LF_G3 + 8 * kCnnHW, LF_CB0 = LF_B3 + 8 * kCnnHW,
+  LF_CB1 = LF_CB0 + 16, LF_CB2 = LF_CB1 + 32, LF_CB3 = LF_CB2 + 64, LF_TOTAL = LF_CB3 + 8
 };
 
-__host__ __device__ inline CnnPackLayout cnn_layout(int c_in, int hw, int n_seats) {
-  CnnPackLayout L;
-  size_t o = 0;
-  auto take = [&](size_t n) {
-    const size_t at = o;
-    o += (n + 63) & ~(size_t)63;
-    return at;
-  };
-  L.w0 = take((size_t)n_seats * 16 * c_in * 9);
-  L.b0 = take(16);
-  L.g0 = take((size_t)16 * hw);
-  L.be0 = take((size_t)16 * hw);
-  L.w1 = take(32 * 16 * 9);
-  L.b1 = take(32);
-  L.g1 = take((size_t)32 * hw);
-  L.be1 = take((size_t)32 * hw);
-  L.w2 = take(64 * 32 * 9);
-  L.b2 = take(64);
-  L.g2 = take((size_t)64 * hw);
-  L.be2 = take((size_t)64 * hw);
-  L.w3 = take(8 * 64);
-  L.b3 = take(8);
-  L.g3 = take((size_t)8 * hw);
-  L.be3 = take((size_t)8 * hw);
-  L.wl = take((size_t)8 * hw * 128);   // transposed [8*hw][128]
-  L.bl = take(128);
-  L.tail = take(F_TOTAL);
-  L.total = o;
+__host__ __device__ inline CnnLayout cnn_layout(int n_seats) {
+  CnnLayout L;
+  L.c0 = 0;
+  L.c1 = (size_t)n_seats * 2 * kW0;
+  L.c2 = L.c1 + 2 * kW1;
+  L.c3 = L.c2 + 2 * kW2;
+  L.wbytes = L.c3 + 2 * kW3;
+  L.lnf = (L.wbytes + 255) / 256 * 256;
+  L.mlp = (L.lnf + (size_t)LF_TOTAL * 4 + 1023) / 1024 * 1024;
+  L.total = L.mlp + mlp_pack_layout(kCnnKIn, 1).total;
   return L;
 }
 
-__device__ __forceinline__ float block_sum(float v, float* red) {
-  v = __fadd_rn(v, 0.f);
+// ------------------------------------------------------------ pack
+
+struct CnnParams {
+  const float* p[16];   // conv stack (qqt_cnn_param_names order)
+};
+
+__device__ __forceinline__ void put_split(uint8_t* img_hi, uint8_t* img_lo, uint32_t off, float v) {
+  const __half hi = __float2half_rn(v);
+  const __half lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
+  *reinterpret_cast<__half*>(img_hi + off) = hi;
+  *reinterpret_cast<__half*>(img_lo + off) = lo;
+}
+
+// Conv weights -> swizzled hi/lo images; LN affine and conv biases -> floats.
+__global__ void k_cnn_pack(CnnParams prm, int n_seats, SeatChannels sc, uint8_t* __restrict__ pk) {
+  const CnnLayout L = cnn_layout(n_seats);
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  // conv0: (seat, group, n, k) -> tap g*4 + k/16, stored channel k%16
+  if (i < n_seats * 3 * 16 * 64) {
+    const int s = i / (3 * 16 * 64), r = i % (3 * 16 * 64);
+    const int g = r / (16 * 64), n = (r / 64) % 16, k = r % 64;
+    const int t = g * 4 + k / 16, ic = k % 16;
+    const float v = (t < 9 && ic < 14) ? prm.p[0][((size_t)n * 14 + sc.src[s][ic]) * 9 + t] : 0.f;
+    uint8_t* base = pk + L.c0 + (size_t)s * 2 * kW0;
+    put_split(base, base + kW0, g * 16 * 128 + sw128_off(n, k, 16), v);
+  }
+  if (i < 3 * 32 * 64) {
+    const int g = i / (32 * 64), n = (i / 64) % 32, k = i % 64;
+    const int t = g * 4 + k / 16, ic = k % 16;
+    const float v = t < 9 ? prm.p[4][((size_t)n * 16 + ic) * 9 + t] : 0.f;
+    put_split(pk + L.c1, pk + L.c1 + kW1, g * 32 * 128 + sw128_off(n, k, 32), v);
+  }
+  if (i < 5 * 64 * 64) {
+    const int g = i / (64 * 64), n = (i / 64) % 64, k = i % 64;
+    const int t = g * 2 + k / 32, ic = k % 32;
+    const float v = t < 9 ? prm.p[8][((size_t)n * 32 + ic) * 9 + t] : 0.f;
+    put_split(pk + L.c2, pk + L.c2 + kW2, g * 64 * 128 + sw128_off(n, k, 64), v);
+  }
+  if (i < 16 * 64) {
+    const int n = i / 64, k = i % 64;
+    const float v = n < 8 ? prm.p[12][(size_t)n * 64 + k] : 0.f;
+    put_split(pk + L.c3, pk + L.c3 + kW3, sw128_off(n, k, 16), v);
+  }
+  float* f = (float*)(pk + L.lnf);
+  if (i < 16 * kCnnHW) { f[LF_G0 + i] = prm.p[2][i]; f[LF_B0 + i] = prm.p[3][i]; }
+  if (i < 32 * kCnnHW) { f[LF_G1 + i] = prm.p[6][i]; f[LF_B1 + i] = prm.p[7][i]; }
+  if (i < 64 * kCnnHW) { f[LF_G2 + i] = prm.p[10][i]; f[LF_B2 + i] = prm.p[11][i]; }
+  if (i < 8 * kCnnHW) { f[LF_G3 + i] = prm.p[14][i]; f[LF_B3 + i] = prm.p[15][i]; }
+  if (i < 16) f[LF_CB0 + i] = prm.p[1][i];
+  if (i < 32) f[LF_CB1 + i] = prm.p[5][i];
+  if (i < 64) f[LF_CB2 + i] = prm.p[9][i];
+  if (i < 8) f[LF_CB3 + i] = prm.p[13][i];
+}
+
+// ------------------------------------------------------------ trunk
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_row(uint32_t taddr, float* v) {
+  if (N == 16) {
+    tmem_ld16(taddr, v);
+  } else {
+#pragma unroll
+    for (int c = 0; c < N; c += 32) tmem_ld32(taddr + c, v + c);
+  }
+}
+
+// Sum over the CTA's 128 threads (every thread gets the total).
+__device__ __forceinline__ float cta_sum(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(QQT_FULL, v, o);
-  __syncthreads();
   if (lane_id() == 0) red[warp_id()] = v;
   __syncthreads();
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < kCnnThreads / 32; ++i) s += red[i];
+  const float s = (red[0] + red[1]) + (red[2] + red[3]);
+  __syncthreads();
   return s;
 }
 
-// out[oc][interior] = bias[oc] + sum_ic sum_taps w[oc][ic][tap] * in[ic][...]
-template <int CIN, int COUT, int KS>
-__device__ __forceinline__ void conv_layer(const float* in, float* out, const float* __restrict__ w,
-                                           const float* __restrict__ b, int h, int wd) {
-  const int pw = wd + 2, pp = (h + 2) * pw, hw = h * wd;
-  const int items = (COUT / 4) * hw;
-  for (int it = threadIdx.x; it < items; it += kCnnThreads) {
-    const int og = it / hw, p = it - og * hw;
-    const int r = p / wd, c = p - r * wd;
-    float acc[4];
+// Padded-grid row r (0..255) -> interior pixel index, or -1.
+__device__ __forceinline__ int interior_pixel(int r) {
+  if (r >= kCnnPP) return -1;
+  const int py = r / kCnnPW, px = r - py * kCnnPW;
+  if (py < 1 || py > kCnnH || px < 1 || px > kCnnW) return -1;
+  return (py - 1) * kCnnW + (px - 1);
+}
+
+// One conv layer's MMAs: two M tiles of 128 padded rows, `taps` taps (3x3:
+// the A operand of tap (ky,kx) starts (ky-1)*15 + (kx-1) rows away), CIN/16
+// K steps per tap; tap t's weights sit in group t / (64 / CIN) at byte
+// (t % (64 / CIN)) * CIN * 2 of each 128-byte row.
+template <int N, int CIN, int TAPS, bool SPLIT>
+__device__ __forceinline__ void conv_mma(uint32_t tmem, const uint8_t* act_hi, const uint8_t* act_lo,
+                                         const uint8_t* w_hi, const uint8_t* w_lo) {
+  constexpr int TPG = 64 / CIN;
+  const uint32_t idesc = idesc_f16(128, N);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[j] = __ldg(b + 4 * og + j);
-    const float* wb = w + (size_t)(4 * og) * CIN * KS * KS;
-    for (int ic = 0; ic < CIN; ++ic) {
-      const float* ip = in + ic * pp + (r + 1 - KS / 2) * pw + (c + 1 - KS / 2);
+  for (int j = 0; j < 2; ++j) {
+    const uint32_t d = tmem + 64 * j;
 #pragma unroll
-      for (int ky = 0; ky < KS; ++ky)
+    for (int t = 0; t < TAPS; ++t) {
+      const int shift = TAPS == 9 ? (t / 3 - 1) * kCnnPW + (t % 3 - 1) : 0;
+      const int arow = kActMargin + j * 128 + shift;
+      const uint32_t wb = (t / TPG) * N * 128 + (t % TPG) * CIN * 2;
+      const uint64_t ah = sw128_desc(act_hi + arow * 128), al = sw128_desc(act_lo + arow * 128);
+      const uint64_t bh = sw128_desc(w_hi + wb), bl = sw128_desc(w_lo + wb);
 #pragma unroll
-        for (int kx = 0; kx < KS; ++kx) {
-          const float x = ip[ky * pw + kx];
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            acc[j] = fmaf(__ldg(wb + ((size_t)j * CIN + ic) * KS * KS + ky * KS + kx), x, acc[j]);
-        }
+      for (int kk = 0; kk < CIN / 16; ++kk) {
+        const uint64_t o = (uint64_t)(kk * 2);       // 32 bytes per K = 16 step
+        umma_f16(d, ah + o, bh + o, idesc, (t > 0 || kk > 0) ? 1u : 0u);
+        umma_f16(d, ah + o, bl + o, idesc, 1u);
+        if (SPLIT) umma_f16(d, al + o, bh + o, idesc, 1u);
+      }
     }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) out[(4 * og + j) * pp + (r + 1) * pw + (c + 1)] = acc[j];
   }
-  __syncthreads();
 }
 
-// LayerNorm over all C*h*w interior values with elementwise affine, then ReLU.
-__device__ __forceinline__ void ln_relu_map(float* buf, int C, const float* __restrict__ g,
-                                            const float* __restrict__ be, int h, int wd,
-                                            float* red) {
-  const int pw = wd + 2, pp = (h + 2) * pw, hw = h * wd, n = C * hw;
+// Epilogue of one layer: rows t and t + 128 of the two M tiles; bias, the
+// sample's LayerNorm over NREAL x HW values, ReLU.  !FINAL: the result goes
+// back into the activation buffer as the next layer's fp16 hi/lo input;
+// FINAL: flattened (c * HW + pixel) into the global hi / lo rows.
+template <int N, int NREAL, bool FINAL>
+__device__ __forceinline__ void conv_epilogue(uint32_t tmem, const float* __restrict__ lnf, int lg,
+                                              int lb, int lcb, uint8_t* act_hi, uint8_t* act_lo,
+                                              float* red, __half* out_hi, __half* out_lo) {
+  const int t = threadIdx.x, w = warp_id();
+  const uint32_t lane_base = tmem + ((uint32_t)(w * 32) << 16);
+  float x0[N], x1[N];
+  tmem_row<N>(lane_base, x0);
+  tmem_row<N>(lane_base + 64, x1);
+  const int p0 = interior_pixel(t), p1 = interior_pixel(t + 128);
   float s = 0.f;
-  for (int i = threadIdx.x; i < n; i += kCnnThreads) {
-    const int c = i / hw, p = i - c * hw, r = p / wd, q = p - r * wd;
-    s += buf[c * pp + (r + 1) * pw + q + 1];
+#pragma unroll
+  for (int c = 0; c < NREAL; ++c) {
+    const float b = __ldg(lnf + lcb + c);
+    x0[c] = __fadd_rn(x0[c], b);
+    x1[c] = __fadd_rn(x1[c], b);
+    if (p0 >= 0) s += x0[c];
+    if (p1 >= 0) s += x1[c];
   }
-  const float mean = block_sum(s, red) / (float)n;
+  constexpr float inv_n = 1.f / (float)(NREAL * kCnnHW);
+  const float mean = cta_sum(s, red) * inv_n;
   float v = 0.f;
-  for (int i = threadIdx.x; i < n; i += kCnnThreads) {
-    const int c = i / hw, p = i - c * hw, r = p / wd, q = p - r * wd;
-    const float d = buf[c * pp + (r + 1) * pw + q + 1] - mean;
-    v = fmaf(d, d, v);
+#pragma unroll
+  for (int c = 0; c < NREAL; ++c) {
+    const float d0 = x0[c] - mean, d1 = x1[c] - mean;
+    if (p0 >= 0) v = fmaf(d0, d0, v);
+    if (p1 >= 0) v = fmaf(d1, d1, v);
   }
-  const float rstd = rsqrtf(block_sum(v, red) / (float)n + 1e-5f);
-  for (int i = threadIdx.x; i < n; i += kCnnThreads) {
-    const int c = i / hw, p = i - c * hw, r = p / wd, q = p - r * wd;
-    float* x = buf + c * pp + (r + 1) * pw + q + 1;
-    *x = fmaxf(fmaf((*x - mean) * rstd, __ldg(g + i), __ldg(be + i)), 0.f);
+  const float rstd = rsqrtf(cta_sum(v, red) * inv_n + 1e-5f);
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int p = half ? p1 : p0;
+    if (p < 0) continue;
+    const float* x = half ? x1 : x0;
+    const int r = kActMargin + (half ? t + 128 : t);
+    if (!FINAL) {
+#pragma unroll
+      for (int c8 = 0; c8 < NREAL / 8; ++c8) {
+        uint32_t hv[4], lv[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float y[2];
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int c = c8 * 8 + 2 * j + q;
+            y[q] = fmaxf(fmaf((x[c] - mean) * rstd, __ldg(lnf + lg + c * kCnnHW + p),
+                              __ldg(lnf + lb + c * kCnnHW + p)), 0.f);
+          }
+          const __half h0 = __float2half_rn(y[0]), h1 = __float2half_rn(y[1]);
+          const __half l0 = __float2half_rn(__fsub_rn(y[0], __half2float(h0)));
+          const __half l1 = __float2half_rn(__fsub_rn(y[1], __half2float(h1)));
+          hv[j] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+          lv[j] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+        }
+        const uint32_t off = r * 128 + ((c8 ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(act_hi + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+        *reinterpret_cast<uint4*>(act_lo + off) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < NREAL; ++c) {
+        const float y = fmaxf(fmaf((x[c] - mean) * rstd, __ldg(lnf + lg + c * kCnnHW + p),
+                                   __ldg(lnf + lb + c * kCnnHW + p)), 0.f);
+        const __half h = __float2half_rn(y);
+        out_hi[c * kCnnHW + p] = h;
+        out_lo[c * kCnnHW + p] = __float2half_rn(__fsub_rn(y, __half2float(h)));
+      }
+    }
   }
-  __syncthreads();
 }
 
-template <int CIN0>
-__global__ void __launch_bounds__(kCnnThreads)
-k_cnn_trunk(const __half* __restrict__ obs, int obs_stride, int n, const float* __restrict__ pk,
-            int n_seats, int h, int wd, float* __restrict__ pre) {
-  extern __shared__ __align__(16) float sm[];
-  __shared__ float red[kCnnThreads / 32];
-  const int e = blockIdx.x, seat = blockIdx.y;
-  const int pw = wd + 2, pp = (h + 2) * pw, hw = h * wd;
-  const CnnPackLayout L = cnn_layout(CIN0, hw, n_seats);
-  float* A = sm;                 // up to 32 planes
-  float* B = sm + 32 * pp;       // up to 64 planes
-  for (int i = threadIdx.x; i < 96 * pp; i += kCnnThreads) sm[i] = 0.f;
-  __syncthreads();
-  const __half* orow = obs + (size_t)e * obs_stride;
-  for (int i = threadIdx.x; i < CIN0 * hw; i += kCnnThreads) {
-    const int c = i / hw, p = i - c * hw, r = p / wd, q = p - r * wd;
-    A[c * pp + (r + 1) * pw + q + 1] = __half2float(orow[i]);
+__global__ void __launch_bounds__(128, 1)
+k_cnn_trunk(const __half* __restrict__ obs, int obs_stride, int n, int n_seats,
+            const uint8_t* __restrict__ pk, __half* __restrict__ out) {
+  const CnnLayout L = cnn_layout(n_seats);
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* act_hi = smem;
+  uint8_t* act_lo = smem + kActBytes;
+  uint8_t* wimg = smem + 2 * kActBytes;
+  uint64_t* wbar = (uint64_t*)(wimg + ((L.wbytes + 15) & ~(size_t)15));
+  uint64_t* dbar = wbar + 1;
+  uint32_t* tmem_slot = (uint32_t*)(dbar + 1);
+  float* red = (float*)(tmem_slot + 4);
+  const float* lnf = (const float*)(pk + L.lnf);
+  const int t = threadIdx.x;
+
+  for (int i = t; i < 2 * kActBytes / 16; i += blockDim.x)
+    reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+  if (t == 0) {
+    mbar_init(wbar, 1);
+    mbar_init(dbar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  __syncthreads();
-  conv_layer<CIN0, 16, 3>(A, B, pk + L.w0 + (size_t)seat * 16 * CIN0 * 9, pk + L.b0, h, wd);
-  ln_relu_map(B, 16, pk + L.g0, pk + L.be0, h, wd, red);
-  // the conv outputs only ever write interiors: borders stay zero
-  conv_layer<16, 32, 3>(B, A, pk + L.w1, pk + L.b1, h, wd);
-  ln_relu_map(A, 32, pk + L.g1, pk + L.be1, h, wd, red);
-  conv_layer<32, 64, 3>(A, B, pk + L.w2, pk + L.b2, h, wd);
-  ln_relu_map(B, 64, pk + L.g2, pk + L.be2, h, wd, red);
-  conv_layer<64, 8, 1>(B, A, pk + L.w3, pk + L.b3, h, wd);
-  ln_relu_map(A, 8, pk + L.g3, pk + L.be3, h, wd, red);
-  // flatten (channel-major) -> Linear(8*hw -> 128): two threads per output
-  float* flat = B;               // compact copy of the 8 planes
-  for (int i = threadIdx.x; i < 8 * hw; i += kCnnThreads) {
-    const int c = i / hw, p = i - c * hw, r = p / wd, q = p - r * wd;
-    flat[i] = A[c * pp + (r + 1) * pw + q + 1];
+  if (warp_id() == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 128;" ::"r"(
+        smem_u32(tmem_slot)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
+  fence_proxy_async();
+  asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
-  const int o = threadIdx.x & 127, half = threadIdx.x >> 7;
-  const int k_in = 8 * hw, k0 = half * (k_in / 2), k1 = half ? k_in : k_in / 2;
-  float acc = 0.f;
-  const float* wl = pk + L.wl;
-  for (int k = k0; k < k1; ++k) acc = fmaf(__ldg(wl + (size_t)k * 128 + o), flat[k], acc);
-  float* part = flat + k_in;
-  if (half) part[o] = acc;
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  const uint32_t tmem = *tmem_slot;
+  if (t == 0) {
+    mbar_expect_tx(wbar, (uint32_t)L.wbytes);
+    for (uint32_t o = 0; o < L.wbytes; o += 16384)
+      bulk_load(wimg + o, pk + o, min((uint32_t)L.wbytes - o, 16384u), wbar);
+  }
+  bool ok = __syncthreads_and(mbar_wait(wbar, 0));
+  uint32_t phase = 0;
+  const int items = n * n_seats;
+  for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
+    const int seat = item / n, e = item - seat * n;
+    // ---- stage the observation: 14 channels (+2 zero) per interior pixel
+    const __half* orow = obs + (size_t)e * obs_stride;
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      const int p = t + 128 * h2;
+      if (p < kCnnHW) {
+        const int r = kActMargin + (p / kCnnW + 1) * kCnnPW + (p % kCnnW + 1);
+        uint32_t v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t a = j * 2 < 14 ? __half_as_ushort(orow[(2 * j) * kCnnHW + p]) : 0u;
+          const uint32_t b = j * 2 + 1 < 14 ? __half_as_ushort(orow[(2 * j + 1) * kCnnHW + p]) : 0u;
+          v[j] = a | (b << 16);
+        }
+        *reinterpret_cast<uint4*>(act_hi + r * 128 + ((0 ^ (r & 7)) << 4)) =
+            make_uint4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<uint4*>(act_hi + r * 128 + ((1 ^ (r & 7)) << 4)) =
+            make_uint4(v[4], v[5], v[6], v[7]);
+      }
+    }
+    __half* ohi = out + ((size_t)seat * 2 * n + e) * kCnnKP;
+    __half* olo = out + ((size_t)seat * 2 * n + n + e) * kCnnKP;
+    if (t < kCnnKP - kCnnKIn) {
+      ohi[kCnnKIn + t] = __float2half_rn(0.f);
+      olo[kCnnKIn + t] = __float2half_rn(0.f);
+    }
+    const uint8_t* w0 = wimg + L.c0 + (size_t)seat * 2 * kW0;
+#pragma unroll 1
+    for (int layer = 0; layer < 4 && ok; ++layer) {
+      fence_proxy_async();
+      asm volatile("tcgen05.fence::before_thread_sync;");
+      __syncthreads();
+      if (t == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        if (layer == 0)
+          conv_mma<16, 16, 9, false>(tmem, act_hi, act_lo, w0, w0 + kW0);
+        else if (layer == 1)
+          conv_mma<32, 16, 9, true>(tmem, act_hi, act_lo, wimg + L.c1, wimg + L.c1 + kW1);
+        else if (layer == 2)
+          conv_mma<64, 32, 9, true>(tmem, act_hi, act_lo, wimg + L.c2, wimg + L.c2 + kW2);
+        else
+          conv_mma<16, 64, 1, true>(tmem, act_hi, act_lo, wimg + L.c3, wimg + L.c3 + kW3);
+        umma_commit(dbar);
+      }
+      ok = __syncthreads_and(mbar_wait(dbar, phase & 1));
+      ++phase;
+      if (!ok) break;
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      if (layer == 0)
+        conv_epilogue<16, 16, false>(tmem, lnf, LF_G0, LF_B0, LF_CB0, act_hi, act_lo, red, ohi, olo);
+      else if (layer == 1)
+        conv_epilogue<32, 32, false>(tmem, lnf, LF_G1, LF_B1, LF_CB1, act_hi, act_lo, red, ohi, olo);
+      else if (layer == 2)
+        conv_epilogue<64, 64, false>(tmem, lnf, LF_G2, LF_B2, LF_CB2, act_hi, act_lo, red, ohi, olo);
+      else
+        conv_epilogue<16, 8, true>(tmem, lnf, LF_G3, LF_B3, LF_CB3, act_hi, act_lo, red, ohi, olo);
+    }
+  }
+  if (!ok && t == 0) {
+    flag_error(QQT_DEV_TIMEOUT);
+    // wait (bounded) for the weight copy and the MMAs of the last commit
+    // before the shared memory and TMEM are given up
+    mbar_wait(wbar, 0);
+    if (phase > 0) mbar_wait(dbar, (phase - 1) & 1);
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
-  if (!half) pre[(size_t)e * (128 * n_seats) + seat * 128 + o] = acc + part[o] + __ldg(pk + L.bl + o);
+  if (warp_id() == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 128;" ::"r"(tmem));
+  }
 }
 
-struct CnnParams {
-  const float* p[18];   // conv stack + shared.0 (see qqt_cnn_param_names)
-};
-
-__global__ void k_cnn_pack(CnnParams prm, int c_in, int hw, int n_seats, SeatChannels sc,
-                           float* __restrict__ pk) {
-  const CnnPackLayout L = cnn_layout(c_in, hw, n_seats);
-  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-  // conv0 with the seat's input-channel gather: stored channel k reads W0[:, inv[k]]
-  if (i < (size_t)n_seats * 16 * c_in * 9) {
-    const int s = (int)(i / (16 * c_in * 9));
-    const int rem = (int)(i % (16 * c_in * 9));
-    const int oc = rem / (c_in * 9), k = (rem / 9) % c_in, tap = rem % 9;
-    pk[L.w0 + i] = prm.p[0][((size_t)oc * c_in + sc.src[s][k]) * 9 + tap];
-  }
-  if (i < 16) pk[L.b0 + i] = prm.p[1][i];
-  if (i < (size_t)16 * hw) { pk[L.g0 + i] = prm.p[2][i]; pk[L.be0 + i] = prm.p[3][i]; }
-  if (i < 32 * 16 * 9) pk[L.w1 + i] = prm.p[4][i];
-  if (i < 32) pk[L.b1 + i] = prm.p[5][i];
-  if (i < (size_t)32 * hw) { pk[L.g1 + i] = prm.p[6][i]; pk[L.be1 + i] = prm.p[7][i]; }
-  if (i < 64 * 32 * 9) pk[L.w2 + i] = prm.p[8][i];
-  if (i < 64) pk[L.b2 + i] = prm.p[9][i];
-  if (i < (size_t)64 * hw) { pk[L.g2 + i] = prm.p[10][i]; pk[L.be2 + i] = prm.p[11][i]; }
-  if (i < 8 * 64) pk[L.w3 + i] = prm.p[12][i];
-  if (i < 8) pk[L.b3 + i] = prm.p[13][i];
-  if (i < (size_t)8 * hw) { pk[L.g3 + i] = prm.p[14][i]; pk[L.be3 + i] = prm.p[15][i]; }
-  if (i < (size_t)128 * 8 * hw) {
-    const int o = (int)(i / (8 * hw)), k = (int)(i % (8 * hw));   // shared.0.weight [128][8hw]
-    pk[L.wl + (size_t)k * 128 + o] = prm.p[16][i];
-  }
-  if (i < 128) pk[L.bl + i] = prm.p[17][i];
+__host__ inline size_t cnn_trunk_smem(int n_seats) {
+  const CnnLayout L = cnn_layout(n_seats);
+  return 1024 + 2 * (size_t)kActBytes + ((L.wbytes + 15) & ~(size_t)15) + 256;
 }
 
 }  // namespace qqt
@@ -220,16 +412,21 @@ static const char* kCnnNames =
 extern "C" const char* qqt_cnn_param_names(void) { return kCnnNames; }
 
 extern "C" uint64_t qqt_cnn_pack_bytes(int32_t channels, int32_t hw, int32_t n_seats) {
-  if (channels != 14 || hw <= 0 || n_seats < 1 || n_seats > 2) return 0;
-  return cnn_layout(channels, hw, n_seats).total * 4;
+  if (channels != 14 || hw != kCnnHW || n_seats < 1 || n_seats > 2) return 0;
+  return cnn_layout(n_seats).total;
 }
 
 extern "C" int qqt_cnn_pack(const float* const* params_dev, int32_t n_players, int32_t channels,
                             int32_t hw, int32_t n_seats, const int32_t* pids, void* pack,
                             qqt_stream_t stream) {
-  if (!params_dev || !pack || !pids || channels != 14 || n_seats < 1 || n_seats > 2)
+  if (!params_dev || !pack || !pids || channels != 14 || hw != kCnnHW || n_seats < 1 ||
+      n_seats > 2)
     return QQT_E_ARG;
-  if (n_players < 2 || n_players > QQT_MAX_P) return QQT_E_ARG;
+  if (n_players != 2) return QQT_E_ARG;
+  if ((uintptr_t)pack & 255) return QQT_E_ALIGN;
+  for (int i = 0; i < 36; ++i)
+    if (!params_dev[i]) return QQT_E_ARG;
+  // stored channel k of seat s reads conv0 input column inv[k] (view permutation)
   SeatChannels sc;
   memset(&sc, 0, sizeof(sc));
   const int base = 2 * n_players + 3;
@@ -249,19 +446,25 @@ extern "C" int qqt_cnn_pack(const float* const* params_dev, int32_t n_players, i
     for (int c = base; c < channels; ++c) perm[j++] = c;
     for (int v = 0; v < channels; ++v) sc.src[s][perm[v]] = v;
   }
-  for (int i = 0; i < 36; ++i)
-    if (!params_dev[i]) return QQT_E_ARG;
-  const CnnPackLayout L = cnn_layout(channels, hw, n_seats);
-  float* pk = (float*)pack;
+  const CnnLayout L = cnn_layout(n_seats);
+  uint8_t* pk = (uint8_t*)pack;
   cudaStream_t st = (cudaStream_t)stream;
   CnnParams cp;
-  for (int i = 0; i < 18; ++i) cp.p[i] = params_dev[i];
-  const size_t n_items = (size_t)128 * 8 * hw;
-  k_cnn_pack<<<(unsigned)((n_items + 255) / 256), 256, 0, st>>>(cp, channels, hw, n_seats, sc, pk);
-  // shared tail (LN, 128x128, LN, heads) in the MLP pack's float layout
+  for (int i = 0; i < 16; ++i) cp.p[i] = params_dev[i];
+  // one thread per element of the largest item: the conv2 image (5 x 64 x 64)
+  const int n_items = max(5 * 64 * 64, max(64 * kCnnHW, n_seats * 3 * 16 * 64));
+  k_cnn_pack<<<(n_items + 255) / 256, 256, 0, st>>>(cp, n_seats, sc, pk);
+  // Linear(1352 -> 128) + tail: an MLP pack with the identity column gather
+  const MlpPack M = mlp_pack_layout(kCnnKIn, 1);
+  SeatChannels id;
+  memset(&id, 0, sizeof(id));
+  for (int c = 0; c < 8; ++c) id.src[0][c] = c;
+  uint8_t* mp = pk + L.mlp;
+  const size_t total = (size_t)M.nt * M.kp;
+  k_mlp_pack_w0<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
+      params_dev[16], kCnnKIn, M.kp, kCnnHW, 8, id, M.nt, (__half*)(mp + M.b_off));
   HeadParams hp;
-  // q[] uses the MLP's parameter order: q[0] = shared.0.weight (index 16),
-  // q[1] = shared.0.bias, q[2] = shared.1.weight, ..., q[19] = critic.2.bias (35)
+  // q[] in the MLP parameter order: q[0] = shared.0.weight (index 16) ... q[19] = critic.2.bias
   const float* const* q = params_dev + 16;
   hp.b0 = q[1];
   hp.ln1g = q[2];
@@ -282,12 +485,25 @@ extern "C" int qqt_cnn_pack(const float* const* params_dev, int32_t n_players, i
   hp.cb0 = q[17];
   hp.cw2 = q[18];
   hp.cb2 = q[19];
-  k_mlp_pack_rest<<<(128 * 128 + 255) / 256, 256, 0, st>>>(hp, n_seats, pk + L.tail);
+  k_mlp_pack_rest<<<(128 * 128 + 255) / 256, 256, 0, st>>>(hp, 1, (float*)(mp + M.f_off));
+  k_mlp_pack_images<<<(192 * 128 + 255) / 256, 256, 0, st>>>(hp, mp + M.img_off);
   return launch_status();
 }
 
+// Flattened trunk outputs: [seat][hi, lo][N][1408] fp16.
 extern "C" uint64_t qqt_cnn_work_bytes(int32_t n_envs, int32_t n_seats) {
-  return (uint64_t)n_envs * 128 * n_seats * 4;
+  return (uint64_t)n_seats * 2 * (uint64_t)n_envs * kCnnKP * 2;
+}
+
+static int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+  }
+  return n;
 }
 
 extern "C" int qqt_cnn_act(const void* pack, const void* obs, int32_t n_envs, int32_t obs_stride,
@@ -297,25 +513,46 @@ extern "C" int qqt_cnn_act(const void* pack, const void* obs, int32_t n_envs, in
                            int32_t act_stride, float* logp, float* value, float* logits,
                            void* work, qqt_stream_t stream) {
   if (!pack || !obs || !mm || !bm || !u || !act || !work || channels != 14) return QQT_E_ARG;
-  if (n_envs <= 0 || n_seats < 1 || n_seats > 2 || height > QQT_MAX_H || width > QQT_MAX_W ||
+  if (n_envs <= 0 || n_seats < 1 || n_seats > 2 || height != kCnnH || width != kCnnW ||
       mm_stride < 5 || bm_stride < 2 || act_stride < 2)
     return QQT_E_ARG;
   if (obs_stride < channels * height * width) return QQT_E_ALIGN;
+  if (((uintptr_t)pack & 255) || ((uintptr_t)work & 15)) return QQT_E_ALIGN;
   for (int s = 0; s < n_seats; ++s)
     if (!mm[s] || !bm[s] || !act[s]) return QQT_E_ARG;
-  const int hw = height * width;
-  const CnnPackLayout L = cnn_layout(channels, hw, n_seats);
-  const float* pk = (const float*)pack;
+  const CnnLayout L = cnn_layout(n_seats);
+  const uint8_t* pk = (const uint8_t*)pack;
   cudaStream_t st = (cudaStream_t)stream;
-  const size_t sm = (size_t)96 * (height + 2) * (width + 2) * 4;
-  cudaFuncSetAttribute(k_cnn_trunk<14>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-  float* pre = (float*)work;
-  k_cnn_trunk<14><<<dim3(n_envs, n_seats), kCnnThreads, sm, st>>>(
-      (const __half*)obs, obs_stride, n_envs, pk, n_seats, height, width, pre);
-  for (int s = 0; s < n_seats; ++s)
-    k_mlp_heads<<<(n_envs + kHR - 1) / kHR, 128, 0, st>>>(pre, 128 * n_seats, s, n_envs,
-                                                           pk + L.tail, mm[s], mm_stride, bm[s],
-                                                           bm_stride, u, act[s], act_stride, logp,
-                                                           value, logits);
+  __half* out = (__half*)work;
+  const size_t sm = cnn_trunk_smem(n_seats);
+  cudaFuncSetAttribute(k_cnn_trunk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  const int items = n_envs * n_seats;
+  k_cnn_trunk<<<min(items, sm_count()), 128, sm, st>>>((const __half*)obs, obs_stride, n_envs,
+                                                       n_seats, pk, out);
+  const MlpPack M = mlp_pack_layout(kCnnKIn, 1);
+  const uint8_t* mp = pk + L.mlp;
+  CUtensorMap mb;
+  if (!make_map(&mb, mp + M.b_off, (uint64_t)M.kp, (uint64_t)2 * M.nt, (uint64_t)M.kp * 2,
+                (uint32_t)M.nt))
+    return QQT_E_ARG;
+  cudaFuncSetAttribute(k_mlp_fused<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       FusedCfg<128, true>::kSmem);
+  for (int s = 0; s < n_seats; ++s) {
+    const __half* ahi = out + (size_t)s * 2 * n_envs * kCnnKP;
+    const __half* alo = ahi + (size_t)n_envs * kCnnKP;
+    CUtensorMap ma, malo;
+    if (!make_map(&ma, ahi, kCnnKP, (uint64_t)n_envs, (uint64_t)kCnnKP * 2, kBM) ||
+        !make_map(&malo, alo, kCnnKP, (uint64_t)n_envs, (uint64_t)kCnnKP * 2, kBM))
+      return QQT_E_ARG;
+    SeatOut io;
+    io.mm[0] = mm[s];
+    io.bm[0] = bm[s];
+    io.act[0] = act[s];
+    io.mm[1] = io.bm[1] = nullptr;
+    io.act[1] = nullptr;
+    k_mlp_fused<128, true><<<(n_envs + kBM - 1) / kBM, 192, FusedCfg<128, true>::kSmem, st>>>(
+        ma, malo, mb, n_envs, M.kp / kBK, (const float*)(mp + M.f_off), mp + M.img_off, io, s,
+        mm_stride, bm_stride, u, act_stride, logp, value, logits);
+  }
   return launch_status();
 }

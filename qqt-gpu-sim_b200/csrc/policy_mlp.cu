@@ -19,8 +19,8 @@
 //            back from TMEM, the output layers (5 move, 2 bomb, 1 value) are
 //            per-thread dot products, then masking with float32's lowest
 //            value, inverse-CDF sampling and the log-probability.
-// k_mlp_heads (4 lanes per row; used by the CNN policy after its trunk)
-//   the same tail on the CUDA cores from a pre-activation buffer.
+// The CNN policy (policy_cnn.cu) reuses this kernel with SPLIT_A for its
+// Linear(1352 -> 128) and the same tail.
 //
 // Every mbarrier wait is bounded; on expiry the CTA raises QQT_DEV_TIMEOUT,
 // waits (bounded) for the copies and MMAs it issued, frees its TMEM and
@@ -284,64 +284,6 @@ __global__ void k_mlp_pack_images(HeadParams hp, uint8_t* __restrict__ img) {
 
 // ---------------------------------------------------------------- heads
 
-// LayerNorm + ReLU over one row held as 32 features per lane by 4 lanes.
-__device__ __forceinline__ void ln_relu_4x32(float* x, const float* g, const float* b, int part) {
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) s += x[i];
-  s += __shfl_xor_sync(QQT_FULL, s, 1);
-  s += __shfl_xor_sync(QQT_FULL, s, 2);
-  const float mean = s * (1.f / 128.f);
-  float v = 0.f;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const float d = x[i] - mean;
-    v = fmaf(d, d, v);
-  }
-  v += __shfl_xor_sync(QQT_FULL, v, 1);
-  v += __shfl_xor_sync(QQT_FULL, v, 2);
-  const float rstd = rsqrtf(v * (1.f / 128.f) + 1e-5f);
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const int k = part * 32 + i;
-    x[i] = fmaxf(fmaf((x[i] - mean) * rstd, __ldg(g + k), __ldg(b + k)), 0.f);
-  }
-}
-
-constexpr int kHR = 32;   // env rows per heads block
-constexpr int kXS = 132;  // padded activation row (16-byte aligned, bank-skewed)
-
-// acc[r][j] += sum_k x[4rg+r][k] * W[k][o0 + j] for k in [0,128): float4
-// activations from shared memory, float4 weights (contiguous outputs).
-template <int NO, int LD>
-__device__ __forceinline__ void tile_matmul(float (*acc)[12], const float (*xs)[kXS], int rg,
-                                            const float* __restrict__ wt, int o0) {
-#pragma unroll 2
-  for (int k = 0; k < 128; k += 4) {
-    float4 a[4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) a[r] = *reinterpret_cast<const float4*>(&xs[4 * rg + r][k]);
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      float wv[NO];
-#pragma unroll
-      for (int j = 0; j < NO; j += 4) {
-        const float4 q = __ldg(reinterpret_cast<const float4*>(wt + (k + kk) * LD + o0 + j));
-        wv[j] = q.x;
-        wv[j + 1] = q.y;
-        wv[j + 2] = q.z;
-        wv[j + 3] = q.w;
-      }
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const float av = kk == 0 ? a[r].x : kk == 1 ? a[r].y : kk == 2 ? a[r].z : a[r].w;
-#pragma unroll
-        for (int j = 0; j < NO; ++j) acc[r][j] = fmaf(wv[j], av, acc[r][j]);
-      }
-    }
-  }
-}
-
 // Logits z (5 move, 2 bomb, value) of one row -> masked categorical samples
 // (inverse CDF: a = #{k : u * S > cs_k} over exp(z - max z)), joint
 // log-prob, value; masked logits take float32's lowest value
@@ -396,118 +338,6 @@ __device__ __forceinline__ void sample_write(const float* z, int row, int seat, 
   if (value_out) value_out[(size_t)seat * n_rows + row] = z[7];
 }
 
-// Register-blocked tail of the MLP: a block of 128 threads owns 32 rows.
-// Row-wise steps (LayerNorm) use 4 threads per row; in the two matrix steps
-// thread t owns rows 4*(t/16)..+3 and a contiguous run of outputs (8 of the
-// 128 layer-2 outputs, 12 of the 192 head units), so per 4 k-steps it issues
-// 4 shared float4 loads and 2-3 float4 weight loads for 128-192 FMAs.
-__global__ void __launch_bounds__(128)
-k_mlp_heads(const float* __restrict__ pre, int nt, int seat, int n_rows,
-            const float* __restrict__ f, const uint8_t* __restrict__ mm, int mm_stride,
-            const uint8_t* __restrict__ bm, int bm_stride, const float* __restrict__ u,
-            int64_t* __restrict__ act, int act_stride, float* __restrict__ logp_out,
-            float* __restrict__ value_out, float* __restrict__ logits_out) {
-  __shared__ __align__(16) float xs[kHR][kXS];
-  const int t = threadIdx.x, lane = lane_id();
-  const int row0 = blockIdx.x * kHR;
-  // ---- LN1 (4 threads per row)
-  {
-    const int r = t >> 2, part = t & 3;
-    const int row = min(row0 + r, n_rows - 1);
-    const float* src = pre + (size_t)row * nt + seat * 128 + part * 32;
-    float x[32];
-#pragma unroll
-    for (int i = 0; i < 32; i += 4) {
-      const float4 q = *reinterpret_cast<const float4*>(src + i);
-      x[i] = q.x;
-      x[i + 1] = q.y;
-      x[i + 2] = q.z;
-      x[i + 3] = q.w;
-    }
-    ln_relu_4x32(x, f + F_LN1G, f + F_LN1B, part);
-#pragma unroll
-    for (int i = 0; i < 32; ++i) xs[r][part * 32 + i] = x[i];
-  }
-  __syncthreads();
-  const int rg = t >> 4, og = t & 15;
-  float acc[4][12];
-  // ---- layer 2: outputs 8*og .. 8*og+7
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float bj = __ldg(f + F_B1 + 8 * og + j);
-#pragma unroll
-    for (int r = 0; r < 4; ++r) acc[r][j] = bj;
-  }
-  tile_matmul<8, 128>(acc, xs, rg, f + F_W1, 8 * og);
-  __syncthreads();
-#pragma unroll
-  for (int r = 0; r < 4; ++r)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) xs[4 * rg + r][8 * og + j] = acc[r][j];
-  __syncthreads();
-  // ---- LN2 (4 threads per row)
-  {
-    const int r = t >> 2, part = t & 3;
-    float x[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) x[i] = xs[r][part * 32 + i];
-    ln_relu_4x32(x, f + F_LN2G, f + F_LN2B, part);
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < 32; ++i) xs[r][part * 32 + i] = x[i];
-  }
-  __syncthreads();
-  // ---- heads hidden layer: units 12*og .. 12*og+11 (0..63 move, 64..127
-  //      bomb, 128..191 critic)
-#pragma unroll
-  for (int j = 0; j < 12; ++j) {
-    const float bj = __ldg(f + F_HB0 + 12 * og + j);
-#pragma unroll
-    for (int r = 0; r < 4; ++r) acc[r][j] = bj;
-  }
-  tile_matmul<12, 192>(acc, xs, rg, f + F_HW0, 12 * og);
-  // ---- output layers: partial sums over this thread's units, then a
-  //      16-lane reduction inside the row group
-  const float* w2 = f + F_HW2;
-  float outp[4][8];
-#pragma unroll
-  for (int r = 0; r < 4; ++r)
-#pragma unroll
-    for (int o = 0; o < 8; ++o) outp[r][o] = 0.f;
-#pragma unroll
-  for (int j = 0; j < 12; ++j) {
-    const int hu = 12 * og + j, head = hu >> 6, hi = hu & 63;
-    const int o_lo = head == 0 ? 0 : (head == 1 ? 5 : 7);
-    const int o_hi = head == 0 ? 5 : (head == 1 ? 7 : 8);
-#pragma unroll
-    for (int o = 0; o < 8; ++o) {
-      if (o < o_lo || o >= o_hi) continue;
-      const float wv = __ldg(w2 + o * 64 + hi);
-#pragma unroll
-      for (int r = 0; r < 4; ++r) outp[r][o] = fmaf(wv, fmaxf(acc[r][j], 0.f), outp[r][o]);
-    }
-  }
-#pragma unroll
-  for (int r = 0; r < 4; ++r)
-#pragma unroll
-    for (int o = 0; o < 8; ++o)
-#pragma unroll
-      for (int m = 1; m < 16; m <<= 1) outp[r][o] += __shfl_xor_sync(QQT_FULL, outp[r][o], m);
-  // ---- masking, sampling, log-prob: thread og < 4 of each row group takes row og
-  float z[8];
-#pragma unroll
-  for (int r = 0; r < 4; ++r)
-    if ((lane & 15) == r)
-#pragma unroll
-      for (int o = 0; o < 8; ++o) z[o] = outp[r][o];
-  const int row = row0 + 4 * rg + og;
-  if (og >= 4 || row >= n_rows) return;
-#pragma unroll
-  for (int o = 0; o < 8; ++o) z[o] += __ldg(f + F_HB2 + o);
-  sample_write(z, row, seat, n_rows, mm, mm_stride, bm, bm_stride, u, act, act_stride, logp_out,
-               value_out, logits_out);
-}
-
 // ------------------------------------------------------------ fused MLP
 
 struct SeatOut {
@@ -516,12 +346,16 @@ struct SeatOut {
   int64_t* act[2];
 };
 
-template <int NT>
+// SPLIT_A: the A operand is an fp32 activation given as fp16 hi and lo
+// halves (two tensor maps); each K step then issues the third product
+// A_lo * W_hi.  Without it A is the exact fp16 observation.
+template <int NT, bool SPLIT_A = false>
 struct FusedCfg {
-  static constexpr int kStages = NT == 128 ? 4 : 2;
-  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kStages = (NT == 128 && !SPLIT_A) ? 4 : (NT == 128 ? 3 : 2);
+  static constexpr int kABytes = kBM * kBK * 2;         // one of hi / lo
+  static constexpr int kAAll = kABytes * (SPLIT_A ? 2 : 1);
   static constexpr int kBBytes = NT * kBK * 2;          // one of hi / lo
-  static constexpr int kStageBytes = kABytes + 2 * kBBytes;
+  static constexpr int kStageBytes = kAAll + 2 * kBBytes;
   static constexpr int kPipeBytes = kStages * kStageBytes;
   // tail layout inside the (reused) pipeline region
   static constexpr int kW1 = 0;                         // shared.3 hi, lo
@@ -534,7 +368,8 @@ struct FusedCfg {
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kColH = NT;                 // head hidden accumulator (192 cols)
 };
-static_assert(FusedCfg<128>::kSmem <= 232448 && FusedCfg<256>::kSmem <= 232448,
+static_assert(FusedCfg<128>::kSmem <= 232448 && FusedCfg<256>::kSmem <= 232448 &&
+                  FusedCfg<128, true>::kSmem <= 232448,
               "fused MLP shared memory over the per-CTA limit");
 static_assert(FusedCfg<256>::kColH + 192 <= FusedCfg<256>::kTmemCols, "TMEM columns");
 
@@ -602,14 +437,15 @@ __device__ __forceinline__ void umma_split_k128(uint32_t d_tmem, const uint8_t* 
   }
 }
 
-template <int NT>
+template <int NT, bool SPLIT_A>
 __global__ void __launch_bounds__(192, 1)
-k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-            int n_rows, int k_tiles, const float* __restrict__ f, const uint8_t* __restrict__ img,
-            SeatOut io, int mm_stride, int bm_stride, const float* __restrict__ u, int act_stride,
+k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_alo,
+            const __grid_constant__ CUtensorMap tm_b, int n_rows, int k_tiles,
+            const float* __restrict__ f, const uint8_t* __restrict__ img, SeatOut io, int seat0,
+            int mm_stride, int bm_stride, const float* __restrict__ u, int act_stride,
             float* __restrict__ logp_out, float* __restrict__ value_out,
             float* __restrict__ logits_out) {
-  using G = FusedCfg<NT>;
+  using G = FusedCfg<NT, SPLIT_A>;
   constexpr int S = NT / 128;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -662,8 +498,9 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
       uint8_t* st = smem + s * G::kStageBytes;
       mbar_expect_tx(&full[s], G::kStageBytes);
       tma_load_2d(&tm_a, &full[s], st, kt * kBK, m0);
-      tma_load_2d(&tm_b, &full[s], st + G::kABytes, kt * kBK, 0);
-      tma_load_2d(&tm_b, &full[s], st + G::kABytes + G::kBBytes, kt * kBK, NT);
+      if (SPLIT_A) tma_load_2d(&tm_alo, &full[s], st + G::kABytes, kt * kBK, m0);
+      tma_load_2d(&tm_b, &full[s], st + G::kAAll, kt * kBK, 0);
+      tma_load_2d(&tm_b, &full[s], st + G::kAAll + G::kBBytes, kt * kBK, NT);
       issued_until = kt + 1;
     }
     // drain: every issued stage must land before the CTA may exit
@@ -683,13 +520,15 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
       asm volatile("tcgen05.fence::after_thread_sync;");
       uint8_t* st = smem + s * G::kStageBytes;
       const uint64_t da = sw128_desc(st);
-      const uint64_t dh = sw128_desc(st + G::kABytes);
-      const uint64_t dl = sw128_desc(st + G::kABytes + G::kBBytes);
+      const uint64_t dal = sw128_desc(st + G::kABytes);
+      const uint64_t dh = sw128_desc(st + G::kAAll);
+      const uint64_t dl = sw128_desc(st + G::kAAll + G::kBBytes);
 #pragma unroll
       for (int kk = 0; kk < kBK / 16; ++kk) {
         const uint64_t off = (uint64_t)((kk * 32) >> 4);   // 32 bytes per K=16 step
         umma_f16(tmem, da + off, dh + off, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
         umma_f16(tmem, da + off, dl + off, idesc, 1u);
+        if (SPLIT_A) umma_f16(tmem, dal + off, dh + off, idesc, 1u);
       }
       umma_commit(&empty[s]);
     }
@@ -790,8 +629,8 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
       if (row < n_rows) {
 #pragma unroll
         for (int o = 0; o < 8; ++o) z[o] += __ldg(f + F_HB2 + o);
-        sample_write(z, row, s, n_rows, io.mm[s], mm_stride, io.bm[s], bm_stride, u, io.act[s],
-                     act_stride, logp_out, value_out, logits_out);
+        sample_write(z, row, seat0 + s, n_rows, io.mm[s], mm_stride, io.bm[s], bm_stride, u,
+                     io.act[s], act_stride, logp_out, value_out, logits_out);
       }
     }
     if (!ok) *abort_flag = 1;
@@ -954,17 +793,17 @@ extern "C" int qqt_mlp_act(const void* pack, const void* obs, int32_t n_envs, in
     io.act[s] = s < n_seats ? act[s] : nullptr;
   }
   if (L.nt == 128) {
-    cudaFuncSetAttribute(k_mlp_fused<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(k_mlp_fused<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          FusedCfg<128>::kSmem);
-    k_mlp_fused<128><<<grid, 192, FusedCfg<128>::kSmem, st>>>(
-        ma, mb, n_envs, k_tiles, fpar, pk + L.img_off, io, mm_stride, bm_stride, u, act_stride,
-        logp, value, logits);
+    k_mlp_fused<128, false><<<grid, 192, FusedCfg<128>::kSmem, st>>>(
+        ma, ma, mb, n_envs, k_tiles, fpar, pk + L.img_off, io, 0, mm_stride, bm_stride, u,
+        act_stride, logp, value, logits);
   } else {
-    cudaFuncSetAttribute(k_mlp_fused<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(k_mlp_fused<256, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          FusedCfg<256>::kSmem);
-    k_mlp_fused<256><<<grid, 192, FusedCfg<256>::kSmem, st>>>(
-        ma, mb, n_envs, k_tiles, fpar, pk + L.img_off, io, mm_stride, bm_stride, u, act_stride,
-        logp, value, logits);
+    k_mlp_fused<256, false><<<grid, 192, FusedCfg<256>::kSmem, st>>>(
+        ma, ma, mb, n_envs, k_tiles, fpar, pk + L.img_off, io, 0, mm_stride, bm_stride, u,
+        act_stride, logp, value, logits);
   }
   return launch_status();
 }
