@@ -6,7 +6,7 @@
 // ReLU -> conv 3x3 32 -> 64 -> LN -> ReLU -> conv 1x1 64 -> 8 -> LN -> ReLU
 // -> flatten (c*HW + y*W + x).
 //
-// k_cnn_trunk (persistent, one CTA of 128 threads per SM, one sample at a
+// k_cnn_trunk (persistent, one CTA of 8 warps per SM, one sample at a
 // time): the sample's activation lives in shared memory as a zero-bordered
 // 15x15 pixel grid, one 128-byte row per pixel (channels K-major, fp16 hi
 // and lo halves, 128-byte swizzle) with 16 margin rows on each side.  A 3x3
@@ -14,13 +14,15 @@
 // shifted by (ky-1)*15 + (kx-1) rows: the descriptor's start address moves,
 // nothing is copied (the swizzle follows absolute shared-memory address
 // bits, so any row offset is a valid operand start).  Each layer runs
-// M = 2 x 128 padded pixels (225 used, border rows ignored) x N = Cout,
-// K = Cin per tap, with three products per K step (A_hi*W_hi + A_hi*W_lo +
-// A_lo*W_hi; conv0's input is the exact fp16 observation, so two).  All
-// conv weights stay resident in shared memory as pre-swizzled fp16 hi/lo
-// images (one bulk copy per CTA).  The epilogue (thread = TMEM lane = pixel
-// row) adds the bias, computes the sample's LayerNorm statistics with two
-// block reductions (mean, then the centred sum of squares), applies the
+// M = 2 x 128 padded pixels (225 used, border rows ignored), K = Cin per
+// tap.  The weights' fp16 hi and lo halves are stacked along N, so one MMA
+// A_hi * [W_hi; W_lo] (N = 2 Cout) gives the hi*hi and hi*lo products in two
+// column halves and a second A_lo * W_hi (N = Cout) accumulates into the
+// first half (conv0's input is the exact fp16 observation: one MMA); the
+// epilogue adds the halves.  All conv weights stay resident in shared
+// memory as pre-swizzled images (one bulk copy per CTA).  The epilogue (thread = TMEM lane = pixel
+// row, two warps per lane quadrant splitting the channels) adds the bias,
+// computes the sample's LayerNorm statistics with two block reductions (mean, then the centred sum of squares), applies the
 // affine LN and ReLU, splits into fp16 hi/lo and writes the next layer's
 // input into the same buffer; the last layer writes the flattened
 // activation to global memory as fp16 hi and lo rows of 1408 (1352 + zero
@@ -40,17 +42,18 @@ constexpr int kCnnKIn = 8 * kCnnHW;                  // 1352 flattened features
 constexpr int kCnnKP = 1408;                         // padded to 22 K tiles of 64
 constexpr int kActMargin = 16, kActRows = 288;       // 16 + 256 + 16
 constexpr int kActBytes = kActRows * 128;            // one of hi / lo
-// weight images (bytes, per hi / lo): conv0 16 rows x 3 groups (4 taps of
-// 16 channels per 128-byte row), conv1 32 x 3, conv2 64 x 5 (2 taps of 32),
-// conv3 16 rows (8 real) x 1
-constexpr int kW0 = 3 * 16 * 128, kW1 = 3 * 32 * 128, kW2 = 5 * 64 * 128, kW3 = 16 * 128;
+// weight images (bytes): per group of taps, 2 x Cout rows of 128 bytes (hi
+// rows, then lo rows); conv0 3 groups (4 taps of 16 channels per row),
+// conv1 3 groups, conv2 5 groups (2 taps of 32), conv3 1 group (Cout padded
+// to 16)
+constexpr int kW0 = 3 * 32 * 128, kW1 = 3 * 64 * 128, kW2 = 5 * 128 * 128, kW3 = 32 * 128;
 
 struct CnnLayout {
   size_t c0, c1, c2, c3, wbytes;          // image offsets (bytes); c0 is per seat
   size_t lnf;                             // float block (bytes offset)
   size_t mlp, total;                      // embedded MLP pack of the linear + tail
 };
-// float block (floats from lnf): LN gamma/beta [C][HW] per layer, conv biases
+// float block (floats from lnf): LN gamma/beta [HW][C] per layer, conv biases
 enum {
   LF_G0 = 0, LF_B0 = LF_G0 + 16 * kCnnHW, LF_G1 = LF_B0 + 16 * kCnnHW,
   LF_B1 = LF_G1 + 32 * kCnnHW, LF_G2 = LF_B1 + 32 * kCnnHW, LF_B2 = LF_G2 + 64 * kCnnHW,
@@ -61,10 +64,10 @@ enum {
 __host__ __device__ inline CnnLayout cnn_layout(int n_seats) {
   CnnLayout L;
   L.c0 = 0;
-  L.c1 = (size_t)n_seats * 2 * kW0;
-  L.c2 = L.c1 + 2 * kW1;
-  L.c3 = L.c2 + 2 * kW2;
-  L.wbytes = L.c3 + 2 * kW3;
+  L.c1 = (size_t)n_seats * kW0;
+  L.c2 = L.c1 + kW1;
+  L.c3 = L.c2 + kW2;
+  L.wbytes = L.c3 + kW3;
   L.lnf = (L.wbytes + 255) / 256 * 256;
   L.mlp = (L.lnf + (size_t)LF_TOTAL * 4 + 1023) / 1024 * 1024;
   L.total = L.mlp + mlp_pack_layout(kCnnKIn, 1).total;
@@ -77,11 +80,13 @@ struct CnnParams {
   const float* p[16];   // conv stack (qqt_cnn_param_names order)
 };
 
-__device__ __forceinline__ void put_split(uint8_t* img_hi, uint8_t* img_lo, uint32_t off, float v) {
+// Weight (n, k) of a group image with C output rows: hi at row n, lo at
+// row C + n (128-byte swizzled K-major rows).
+__device__ __forceinline__ void put_split(uint8_t* group, int C, int n, int k, float v) {
   const __half hi = __float2half_rn(v);
   const __half lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
-  *reinterpret_cast<__half*>(img_hi + off) = hi;
-  *reinterpret_cast<__half*>(img_lo + off) = lo;
+  *reinterpret_cast<__half*>(group + sw128_off(n, k, 2 * C)) = hi;
+  *reinterpret_cast<__half*>(group + sw128_off(C + n, k, 2 * C)) = lo;
 }
 
 // Conv weights -> swizzled hi/lo images; LN affine and conv biases -> floats.
@@ -94,31 +99,38 @@ __global__ void k_cnn_pack(CnnParams prm, int n_seats, SeatChannels sc, uint8_t*
     const int g = r / (16 * 64), n = (r / 64) % 16, k = r % 64;
     const int t = g * 4 + k / 16, ic = k % 16;
     const float v = (t < 9 && ic < 14) ? prm.p[0][((size_t)n * 14 + sc.src[s][ic]) * 9 + t] : 0.f;
-    uint8_t* base = pk + L.c0 + (size_t)s * 2 * kW0;
-    put_split(base, base + kW0, g * 16 * 128 + sw128_off(n, k, 16), v);
+    put_split(pk + L.c0 + (size_t)s * kW0 + g * 32 * 128, 16, n, k, v);
   }
   if (i < 3 * 32 * 64) {
     const int g = i / (32 * 64), n = (i / 64) % 32, k = i % 64;
     const int t = g * 4 + k / 16, ic = k % 16;
     const float v = t < 9 ? prm.p[4][((size_t)n * 16 + ic) * 9 + t] : 0.f;
-    put_split(pk + L.c1, pk + L.c1 + kW1, g * 32 * 128 + sw128_off(n, k, 32), v);
+    put_split(pk + L.c1 + g * 64 * 128, 32, n, k, v);
   }
   if (i < 5 * 64 * 64) {
     const int g = i / (64 * 64), n = (i / 64) % 64, k = i % 64;
     const int t = g * 2 + k / 32, ic = k % 32;
     const float v = t < 9 ? prm.p[8][((size_t)n * 32 + ic) * 9 + t] : 0.f;
-    put_split(pk + L.c2, pk + L.c2 + kW2, g * 64 * 128 + sw128_off(n, k, 64), v);
+    put_split(pk + L.c2 + g * 128 * 128, 64, n, k, v);
   }
   if (i < 16 * 64) {
     const int n = i / 64, k = i % 64;
     const float v = n < 8 ? prm.p[12][(size_t)n * 64 + k] : 0.f;
-    put_split(pk + L.c3, pk + L.c3 + kW3, sw128_off(n, k, 16), v);
+    put_split(pk + L.c3, 16, n, k, v);
   }
+  // LN affine [C][H][W] -> [pixel][C] (a pixel's channels contiguous)
   float* f = (float*)(pk + L.lnf);
-  if (i < 16 * kCnnHW) { f[LF_G0 + i] = prm.p[2][i]; f[LF_B0 + i] = prm.p[3][i]; }
-  if (i < 32 * kCnnHW) { f[LF_G1 + i] = prm.p[6][i]; f[LF_B1 + i] = prm.p[7][i]; }
-  if (i < 64 * kCnnHW) { f[LF_G2 + i] = prm.p[10][i]; f[LF_B2 + i] = prm.p[11][i]; }
-  if (i < 8 * kCnnHW) { f[LF_G3 + i] = prm.p[14][i]; f[LF_B3 + i] = prm.p[15][i]; }
+  auto tr = [&](int C, int off_g, int off_b, const float* g, const float* b) {
+    if (i < C * kCnnHW) {
+      const int c = i / kCnnHW, px = i % kCnnHW;
+      f[off_g + px * C + c] = g[i];
+      f[off_b + px * C + c] = b[i];
+    }
+  };
+  tr(16, LF_G0, LF_B0, prm.p[2], prm.p[3]);
+  tr(32, LF_G1, LF_B1, prm.p[6], prm.p[7]);
+  tr(64, LF_G2, LF_B2, prm.p[10], prm.p[11]);
+  tr(8, LF_G3, LF_B3, prm.p[14], prm.p[15]);
   if (i < 16) f[LF_CB0 + i] = prm.p[1][i];
   if (i < 32) f[LF_CB1 + i] = prm.p[5][i];
   if (i < 64) f[LF_CB2 + i] = prm.p[9][i];
@@ -127,37 +139,44 @@ __global__ void k_cnn_pack(CnnParams prm, int n_seats, SeatChannels sc, uint8_t*
 
 // ------------------------------------------------------------ trunk
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+// tcgen05.ld of NC (4, 8 or 16) consecutive 32-bit columns of this lane.
+template <int NC>
+__device__ __forceinline__ void tmem_ldn(uint32_t taddr, float* v) {
   uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
-      "%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
+  if (NC == 4) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr));
+  } else if (NC == 8) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                   "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+  } else {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+        "%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+  }
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < NC; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-template <int N>
-__device__ __forceinline__ void tmem_row(uint32_t taddr, float* v) {
-  if (N == 16) {
-    tmem_ld16(taddr, v);
-  } else {
-#pragma unroll
-    for (int c = 0; c < N; c += 32) tmem_ld32(taddr + c, v + c);
-  }
-}
+constexpr int kTrunkWarps = 8;    // 2 per TMEM lane quadrant, splitting the columns
 
-// Sum over the CTA's 128 threads (every thread gets the total).
+// Sum over the CTA's threads (every thread gets the total; fixed order).
 __device__ __forceinline__ float cta_sum(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(QQT_FULL, v, o);
   if (lane_id() == 0) red[warp_id()] = v;
   __syncthreads();
-  const float s = (red[0] + red[1]) + (red[2] + red[3]);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kTrunkWarps; ++i) s += red[i];
   __syncthreads();
   return s;
 }
@@ -170,54 +189,89 @@ __device__ __forceinline__ int interior_pixel(int r) {
   return (py - 1) * kCnnW + (px - 1);
 }
 
-// One conv layer's MMAs: two M tiles of 128 padded rows, `taps` taps (3x3:
-// the A operand of tap (ky,kx) starts (ky-1)*15 + (kx-1) rows away), CIN/16
-// K steps per tap; tap t's weights sit in group t / (64 / CIN) at byte
-// (t % (64 / CIN)) * CIN * 2 of each 128-byte row.
-template <int N, int CIN, int TAPS, bool SPLIT>
+// One conv layer's MMAs: two M tiles of 128 padded rows (TMEM columns
+// [128 j, 128 j + 2C)), `taps` taps (3x3: the A operand of tap (ky,kx) starts
+// (ky-1)*15 + (kx-1) rows away), CIN/16 K steps per tap; tap t's weights sit
+// in group t / (64 / CIN) at byte (t % (64 / CIN)) * CIN * 2 of each row.
+template <int C, int CIN, int TAPS, bool SPLIT>
 __device__ __forceinline__ void conv_mma(uint32_t tmem, const uint8_t* act_hi, const uint8_t* act_lo,
-                                         const uint8_t* w_hi, const uint8_t* w_lo) {
+                                         const uint8_t* w) {
   constexpr int TPG = 64 / CIN;
-  const uint32_t idesc = idesc_f16(128, N);
+  const uint32_t id2 = idesc_f16(128, 2 * C), id1 = idesc_f16(128, C);
 #pragma unroll
   for (int j = 0; j < 2; ++j) {
-    const uint32_t d = tmem + 64 * j;
+    const uint32_t d = tmem + 128 * j;
 #pragma unroll
     for (int t = 0; t < TAPS; ++t) {
       const int shift = TAPS == 9 ? (t / 3 - 1) * kCnnPW + (t % 3 - 1) : 0;
       const int arow = kActMargin + j * 128 + shift;
-      const uint32_t wb = (t / TPG) * N * 128 + (t % TPG) * CIN * 2;
+      const uint32_t wb = (t / TPG) * 2 * C * 128 + (t % TPG) * CIN * 2;
       const uint64_t ah = sw128_desc(act_hi + arow * 128), al = sw128_desc(act_lo + arow * 128);
-      const uint64_t bh = sw128_desc(w_hi + wb), bl = sw128_desc(w_lo + wb);
+      const uint64_t bw = sw128_desc(w + wb);
 #pragma unroll
       for (int kk = 0; kk < CIN / 16; ++kk) {
         const uint64_t o = (uint64_t)(kk * 2);       // 32 bytes per K = 16 step
-        umma_f16(d, ah + o, bh + o, idesc, (t > 0 || kk > 0) ? 1u : 0u);
-        umma_f16(d, ah + o, bl + o, idesc, 1u);
-        if (SPLIT) umma_f16(d, al + o, bh + o, idesc, 1u);
+        umma_f16(d, ah + o, bw + o, id2, (t > 0 || kk > 0) ? 1u : 0u);
+        if (SPLIT) umma_f16(d, al + o, bw + o, id1, 1u);
       }
     }
   }
 }
 
-// Epilogue of one layer: rows t and t + 128 of the two M tiles; bias, the
-// sample's LayerNorm over NREAL x HW values, ReLU.  !FINAL: the result goes
-// back into the activation buffer as the next layer's fp16 hi/lo input;
-// FINAL: flattened (c * HW + pixel) into the global hi / lo rows.
+// Epilogue of one layer.  Warp w reads TMEM lane quadrant w % 4 (padded
+// rows q*32 + lane of both M tiles) and column half w / 4 (NC = N / 2
+// channels); bias, the sample's LayerNorm over NREAL x HW values, ReLU.
+// The LN affine parameters of the thread's two pixels are loaded as 16-byte
+// vectors ([pixel][C] layout) before the statistics are reduced.
+// !FINAL: the result goes back into the activation buffer as the next
+// layer's fp16 hi/lo input; FINAL: flattened (c * HW + pixel) into the
+// global hi / lo rows.
 template <int N, int NREAL, bool FINAL>
 __device__ __forceinline__ void conv_epilogue(uint32_t tmem, const float* __restrict__ lnf, int lg,
-                                              int lb, int lcb, uint8_t* act_hi, uint8_t* act_lo,
-                                              float* red, __half* out_hi, __half* out_lo) {
-  const int t = threadIdx.x, w = warp_id();
-  const uint32_t lane_base = tmem + ((uint32_t)(w * 32) << 16);
-  float x0[N], x1[N];
-  tmem_row<N>(lane_base, x0);
-  tmem_row<N>(lane_base + 64, x1);
-  const int p0 = interior_pixel(t), p1 = interior_pixel(t + 128);
+                                              int lb, const float* cb, uint8_t* act_hi,
+                                              uint8_t* act_lo, float* red, __half* out_hi,
+                                              __half* out_lo) {
+  constexpr int NC = N / 2;
+  const int w = warp_id(), q = w & 3, cg = w >> 2, lane = lane_id();
+  const int c0 = cg * NC;
+  const bool real = c0 < NREAL;            // conv3: the second column half is padding
+  const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + c0;
+  float x0[NC], x1[NC], y0[NC], y1[NC];
+  if (NC == 32) {
+    tmem_ld32(taddr, x0);
+    tmem_ld32(taddr + N, y0);
+    tmem_ld32(taddr + 128, x1);
+    tmem_ld32(taddr + 128 + N, y1);
+  } else {
+    tmem_ldn<NC>(taddr, x0);
+    tmem_ldn<NC>(taddr + N, y0);
+    tmem_ldn<NC>(taddr + 128, x1);
+    tmem_ldn<NC>(taddr + 128 + N, y1);
+  }
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {          // (hi*hi + lo*hi) + hi*lo
+    x0[c] = __fadd_rn(x0[c], y0[c]);
+    x1[c] = __fadd_rn(x1[c], y1[c]);
+  }
+  const int r0 = q * 32 + lane, r1 = 128 + r0;
+  const int p0 = real ? interior_pixel(r0) : -1, p1 = real ? interior_pixel(r1) : -1;
+  float g0[NC], b0[NC], g1[NC], b1[NC];
+#pragma unroll
+  for (int c = 0; c < NC; c += 4) {
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 ga = p0 >= 0 ? __ldg(reinterpret_cast<const float4*>(lnf + lg + p0 * NREAL + c0 + c)) : z;
+    const float4 ba = p0 >= 0 ? __ldg(reinterpret_cast<const float4*>(lnf + lb + p0 * NREAL + c0 + c)) : z;
+    const float4 gb = p1 >= 0 ? __ldg(reinterpret_cast<const float4*>(lnf + lg + p1 * NREAL + c0 + c)) : z;
+    const float4 bb = p1 >= 0 ? __ldg(reinterpret_cast<const float4*>(lnf + lb + p1 * NREAL + c0 + c)) : z;
+    g0[c] = ga.x; g0[c + 1] = ga.y; g0[c + 2] = ga.z; g0[c + 3] = ga.w;
+    b0[c] = ba.x; b0[c + 1] = ba.y; b0[c + 2] = ba.z; b0[c + 3] = ba.w;
+    g1[c] = gb.x; g1[c + 1] = gb.y; g1[c + 2] = gb.z; g1[c + 3] = gb.w;
+    b1[c] = bb.x; b1[c + 1] = bb.y; b1[c + 2] = bb.z; b1[c + 3] = bb.w;
+  }
   float s = 0.f;
 #pragma unroll
-  for (int c = 0; c < NREAL; ++c) {
-    const float b = __ldg(lnf + lcb + c);
+  for (int c = 0; c < NC; ++c) {
+    const float b = real ? cb[c0 + c] : 0.f;
     x0[c] = __fadd_rn(x0[c], b);
     x1[c] = __fadd_rn(x1[c], b);
     if (p0 >= 0) s += x0[c];
@@ -227,7 +281,7 @@ __device__ __forceinline__ void conv_epilogue(uint32_t tmem, const float* __rest
   const float mean = cta_sum(s, red) * inv_n;
   float v = 0.f;
 #pragma unroll
-  for (int c = 0; c < NREAL; ++c) {
+  for (int c = 0; c < NC; ++c) {
     const float d0 = x0[c] - mean, d1 = x1[c] - mean;
     if (p0 >= 0) v = fmaf(d0, d0, v);
     if (p1 >= 0) v = fmaf(d1, d1, v);
@@ -238,44 +292,42 @@ __device__ __forceinline__ void conv_epilogue(uint32_t tmem, const float* __rest
     const int p = half ? p1 : p0;
     if (p < 0) continue;
     const float* x = half ? x1 : x0;
-    const int r = kActMargin + (half ? t + 128 : t);
-    if (!FINAL) {
+    const float* g = half ? g1 : g0;
+    const float* bb = half ? b1 : b0;
+    float y[NC];
 #pragma unroll
-      for (int c8 = 0; c8 < NREAL / 8; ++c8) {
+    for (int c = 0; c < NC; ++c) y[c] = fmaxf(fmaf((x[c] - mean) * rstd, g[c], bb[c]), 0.f);
+    if (!FINAL) {
+      const int r = kActMargin + (half ? r1 : r0);
+#pragma unroll
+      for (int k = 0; k < NC / 8; ++k) {
         uint32_t hv[4], lv[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          float y[2];
-#pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const int c = c8 * 8 + 2 * j + q;
-            y[q] = fmaxf(fmaf((x[c] - mean) * rstd, __ldg(lnf + lg + c * kCnnHW + p),
-                              __ldg(lnf + lb + c * kCnnHW + p)), 0.f);
-          }
-          const __half h0 = __float2half_rn(y[0]), h1 = __float2half_rn(y[1]);
-          const __half l0 = __float2half_rn(__fsub_rn(y[0], __half2float(h0)));
-          const __half l1 = __float2half_rn(__fsub_rn(y[1], __half2float(h1)));
+          const float ya = y[8 * k + 2 * j], yb = y[8 * k + 2 * j + 1];
+          const __half h0 = __float2half_rn(ya), h1 = __float2half_rn(yb);
+          const __half l0 = __float2half_rn(__fsub_rn(ya, __half2float(h0)));
+          const __half l1 = __float2half_rn(__fsub_rn(yb, __half2float(h1)));
           hv[j] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
           lv[j] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
         }
+        const int c8 = c0 / 8 + k;
         const uint32_t off = r * 128 + ((c8 ^ (r & 7)) << 4);
         *reinterpret_cast<uint4*>(act_hi + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
         *reinterpret_cast<uint4*>(act_lo + off) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
       }
     } else {
 #pragma unroll
-      for (int c = 0; c < NREAL; ++c) {
-        const float y = fmaxf(fmaf((x[c] - mean) * rstd, __ldg(lnf + lg + c * kCnnHW + p),
-                                   __ldg(lnf + lb + c * kCnnHW + p)), 0.f);
-        const __half h = __float2half_rn(y);
-        out_hi[c * kCnnHW + p] = h;
-        out_lo[c * kCnnHW + p] = __float2half_rn(__fsub_rn(y, __half2float(h)));
+      for (int c = 0; c < NC; ++c) {
+        const __half h = __float2half_rn(y[c]);
+        out_hi[(c0 + c) * kCnnHW + p] = h;
+        out_lo[(c0 + c) * kCnnHW + p] = __float2half_rn(__fsub_rn(y[c], __half2float(h)));
       }
     }
   }
 }
 
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(kTrunkWarps * 32, 1)
 k_cnn_trunk(const __half* __restrict__ obs, int obs_stride, int n, int n_seats,
             const uint8_t* __restrict__ pk, __half* __restrict__ out) {
   const CnnLayout L = cnn_layout(n_seats);
@@ -287,19 +339,21 @@ k_cnn_trunk(const __half* __restrict__ obs, int obs_stride, int n, int n_seats,
   uint64_t* wbar = (uint64_t*)(wimg + ((L.wbytes + 15) & ~(size_t)15));
   uint64_t* dbar = wbar + 1;
   uint32_t* tmem_slot = (uint32_t*)(dbar + 1);
-  float* red = (float*)(tmem_slot + 4);
+  float* red = (float*)(tmem_slot + 4);     // kTrunkWarps floats
+  float* cb = red + kTrunkWarps;            // the 120 conv biases
   const float* lnf = (const float*)(pk + L.lnf);
   const int t = threadIdx.x;
 
   for (int i = t; i < 2 * kActBytes / 16; i += blockDim.x)
     reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+  for (int i = t; i < LF_TOTAL - LF_CB0; i += blockDim.x) cb[i] = lnf[LF_CB0 + i];
   if (t == 0) {
     mbar_init(wbar, 1);
     mbar_init(dbar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp_id() == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 128;" ::"r"(
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(
         smem_u32(tmem_slot)));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
@@ -318,25 +372,22 @@ k_cnn_trunk(const __half* __restrict__ obs, int obs_stride, int n, int n_seats,
   const int items = n * n_seats;
   for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
     const int seat = item / n, e = item - seat * n;
-    // ---- stage the observation: 14 channels (+2 zero) per interior pixel
+    // ---- stage the observation: 14 channels (+2 zero) per interior pixel,
+    //      one (pixel, 8-channel chunk) per thread
     const __half* orow = obs + (size_t)e * obs_stride;
+    for (int i = t; i < 2 * kCnnHW; i += blockDim.x) {
+      const int p = i >> 1, ch = i & 1;
+      const int r = kActMargin + (p / kCnnW + 1) * kCnnPW + (p % kCnnW + 1);
+      uint32_t v[4];
 #pragma unroll
-    for (int h2 = 0; h2 < 2; ++h2) {
-      const int p = t + 128 * h2;
-      if (p < kCnnHW) {
-        const int r = kActMargin + (p / kCnnW + 1) * kCnnPW + (p % kCnnW + 1);
-        uint32_t v[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t a = j * 2 < 14 ? __half_as_ushort(orow[(2 * j) * kCnnHW + p]) : 0u;
-          const uint32_t b = j * 2 + 1 < 14 ? __half_as_ushort(orow[(2 * j + 1) * kCnnHW + p]) : 0u;
-          v[j] = a | (b << 16);
-        }
-        *reinterpret_cast<uint4*>(act_hi + r * 128 + ((0 ^ (r & 7)) << 4)) =
-            make_uint4(v[0], v[1], v[2], v[3]);
-        *reinterpret_cast<uint4*>(act_hi + r * 128 + ((1 ^ (r & 7)) << 4)) =
-            make_uint4(v[4], v[5], v[6], v[7]);
+      for (int j = 0; j < 4; ++j) {
+        const int c = ch * 8 + 2 * j;
+        const uint32_t a = c < 14 ? __half_as_ushort(orow[c * kCnnHW + p]) : 0u;
+        const uint32_t b = c + 1 < 14 ? __half_as_ushort(orow[(c + 1) * kCnnHW + p]) : 0u;
+        v[j] = a | (b << 16);
       }
+      *reinterpret_cast<uint4*>(act_hi + r * 128 + ((ch ^ (r & 7)) << 4)) =
+          make_uint4(v[0], v[1], v[2], v[3]);
     }
     __half* ohi = out + ((size_t)seat * 2 * n + e) * kCnnKP;
     __half* olo = out + ((size_t)seat * 2 * n + n + e) * kCnnKP;
@@ -344,7 +395,7 @@ k_cnn_trunk(const __half* __restrict__ obs, int obs_stride, int n, int n_seats,
       ohi[kCnnKIn + t] = __float2half_rn(0.f);
       olo[kCnnKIn + t] = __float2half_rn(0.f);
     }
-    const uint8_t* w0 = wimg + L.c0 + (size_t)seat * 2 * kW0;
+    const uint8_t* w0 = wimg + L.c0 + (size_t)seat * kW0;
 #pragma unroll 1
     for (int layer = 0; layer < 4 && ok; ++layer) {
       fence_proxy_async();
@@ -353,13 +404,13 @@ k_cnn_trunk(const __half* __restrict__ obs, int obs_stride, int n, int n_seats,
       if (t == 0) {
         asm volatile("tcgen05.fence::after_thread_sync;");
         if (layer == 0)
-          conv_mma<16, 16, 9, false>(tmem, act_hi, act_lo, w0, w0 + kW0);
+          conv_mma<16, 16, 9, false>(tmem, act_hi, act_lo, w0);
         else if (layer == 1)
-          conv_mma<32, 16, 9, true>(tmem, act_hi, act_lo, wimg + L.c1, wimg + L.c1 + kW1);
+          conv_mma<32, 16, 9, true>(tmem, act_hi, act_lo, wimg + L.c1);
         else if (layer == 2)
-          conv_mma<64, 32, 9, true>(tmem, act_hi, act_lo, wimg + L.c2, wimg + L.c2 + kW2);
+          conv_mma<64, 32, 9, true>(tmem, act_hi, act_lo, wimg + L.c2);
         else
-          conv_mma<16, 64, 1, true>(tmem, act_hi, act_lo, wimg + L.c3, wimg + L.c3 + kW3);
+          conv_mma<16, 64, 1, true>(tmem, act_hi, act_lo, wimg + L.c3);
         umma_commit(dbar);
       }
       ok = __syncthreads_and(mbar_wait(dbar, phase & 1));
@@ -367,13 +418,16 @@ k_cnn_trunk(const __half* __restrict__ obs, int obs_stride, int n, int n_seats,
       if (!ok) break;
       asm volatile("tcgen05.fence::after_thread_sync;");
       if (layer == 0)
-        conv_epilogue<16, 16, false>(tmem, lnf, LF_G0, LF_B0, LF_CB0, act_hi, act_lo, red, ohi, olo);
+        conv_epilogue<16, 16, false>(tmem, lnf, LF_G0, LF_B0, cb, act_hi, act_lo, red, ohi, olo);
       else if (layer == 1)
-        conv_epilogue<32, 32, false>(tmem, lnf, LF_G1, LF_B1, LF_CB1, act_hi, act_lo, red, ohi, olo);
+        conv_epilogue<32, 32, false>(tmem, lnf, LF_G1, LF_B1, cb + (LF_CB1 - LF_CB0), act_hi, act_lo,
+                                     red, ohi, olo);
       else if (layer == 2)
-        conv_epilogue<64, 64, false>(tmem, lnf, LF_G2, LF_B2, LF_CB2, act_hi, act_lo, red, ohi, olo);
+        conv_epilogue<64, 64, false>(tmem, lnf, LF_G2, LF_B2, cb + (LF_CB2 - LF_CB0), act_hi, act_lo,
+                                     red, ohi, olo);
       else
-        conv_epilogue<16, 8, true>(tmem, lnf, LF_G3, LF_B3, LF_CB3, act_hi, act_lo, red, ohi, olo);
+        conv_epilogue<16, 8, true>(tmem, lnf, LF_G3, LF_B3, cb + (LF_CB3 - LF_CB0), act_hi, act_lo,
+                                   red, ohi, olo);
     }
   }
   if (!ok && t == 0) {
@@ -387,13 +441,14 @@ k_cnn_trunk(const __half* __restrict__ obs, int obs_stride, int n, int n_seats,
   __syncthreads();
   if (warp_id() == 0) {
     asm volatile("tcgen05.fence::after_thread_sync;");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 128;" ::"r"(tmem));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
   }
 }
 
 __host__ inline size_t cnn_trunk_smem(int n_seats) {
   const CnnLayout L = cnn_layout(n_seats);
-  return 1024 + 2 * (size_t)kActBytes + ((L.wbytes + 15) & ~(size_t)15) + 256;
+  return 1024 + 2 * (size_t)kActBytes + ((L.wbytes + 15) & ~(size_t)15) + 128 +
+         4 * (kTrunkWarps + (LF_TOTAL - LF_CB0));
 }
 
 }  // namespace qqt
@@ -527,7 +582,7 @@ extern "C" int qqt_cnn_act(const void* pack, const void* obs, int32_t n_envs, in
   const size_t sm = cnn_trunk_smem(n_seats);
   cudaFuncSetAttribute(k_cnn_trunk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   const int items = n_envs * n_seats;
-  k_cnn_trunk<<<min(items, sm_count()), 128, sm, st>>>((const __half*)obs, obs_stride, n_envs,
+  k_cnn_trunk<<<min(items, sm_count()), kTrunkWarps * 32, sm, st>>>((const __half*)obs, obs_stride, n_envs,
                                                        n_seats, pk, out);
   const MlpPack M = mlp_pack_layout(kCnnKIn, 1);
   const uint8_t* mp = pk + L.mlp;
