@@ -101,10 +101,69 @@ enum : unsigned {
   PL_OWNER = 16, PL_FUSE = 32, PL_BLAST = 64, PL_ALL = 127
 };
 
+static_assert(QQT_TILE_E == 8, "vectorised tile transfers move 8 envs per access");
+
+// Plane pl (bit 1 << pl of PL_*) of the state / the tile.
+__device__ __forceinline__ uint8_t* state_plane(const QqtState& st, int pl) {
+  switch (pl) {
+    case 0: return st.wall;
+    case 1: return st.brick;
+    case 2: return st.crate;
+    case 3: return st.recycle;
+    case 4: return (uint8_t*)st.owner;
+    case 5: return (uint8_t*)st.fuse;
+    default: return (uint8_t*)st.bomb_blast;
+  }
+}
+__device__ __forceinline__ uint8_t* tile_plane(const Tile& t, int pl) {
+  switch (pl) {
+    case 0: return t.wall;
+    case 1: return t.brick;
+    case 2: return t.crate;
+    case 3: return t.recycle;
+    case 4: return (uint8_t*)t.owner;
+    case 5: return (uint8_t*)t.fuse;
+    default: return (uint8_t*)t.blast;
+  }
+}
+
+// Vector tile transfers need N a multiple of 8, a full tile and 16-byte
+// aligned plane bases.
+__device__ __forceinline__ bool tile_vector_ok(const QqtState& st, int n, int e0) {
+  const uintptr_t a = (uintptr_t)st.wall | (uintptr_t)st.brick | (uintptr_t)st.crate |
+                      (uintptr_t)st.recycle | (uintptr_t)st.owner | (uintptr_t)st.fuse |
+                      (uintptr_t)st.bomb_blast;
+  return (n & 7) == 0 && e0 + QQT_TILE_E <= n && (a & 15) == 0;
+}
+
 // Global [cell][N] -> shared [slot][cell] for envs e0 .. e0+E-1 (block-wide).
+// A full tile with N a multiple of 8 moves each (plane, cell) as one 8-byte
+// (u8 planes) or 16-byte (i16 planes) access; otherwise element by element.
 __device__ inline void load_tile(const Tile& t, const QqtState& st, int n, int e0,
                                  unsigned planes) {
   const int cells = t.cells;
+  if (tile_vector_ok(st, n, e0)) {
+    for (int i = threadIdx.x; i < 7 * cells; i += blockDim.x) {
+      const int pl = i / cells, c = i - pl * cells;
+      if (!(planes & (1u << pl))) continue;
+      const size_t g = (size_t)c * n + e0;
+      uint8_t* dst = tile_plane(t, pl);
+      if (pl < 5) {
+        const uint2 v = *reinterpret_cast<const uint2*>(state_plane(st, pl) + g);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          dst[k * cells + c] = (uint8_t)(((k < 4 ? v.x : v.y) >> (8 * (k & 3))) & 0xff);
+      } else {
+        const uint4 v = *reinterpret_cast<const uint4*>(state_plane(st, pl) + 2 * g);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        int16_t* d16 = reinterpret_cast<int16_t*>(dst);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          d16[k * cells + c] = (int16_t)((w[k >> 1] >> (16 * (k & 1))) & 0xffff);
+      }
+    }
+    return;
+  }
   const int total = cells * QQT_TILE_E;
   for (int i = threadIdx.x; i < total; i += blockDim.x) {
     const int c = i / QQT_TILE_E;
@@ -127,6 +186,31 @@ __device__ inline void load_tile(const Tile& t, const QqtState& st, int n, int e
 __device__ inline void store_tile(const Tile& t, const QqtState& st, int n, int e0,
                                   unsigned planes) {
   const int cells = t.cells;
+  if (tile_vector_ok(st, n, e0)) {
+    for (int i = threadIdx.x; i < 7 * cells; i += blockDim.x) {
+      const int pl = i / cells, c = i - pl * cells;
+      if (!(planes & (1u << pl))) continue;
+      const size_t g = (size_t)c * n + e0;
+      const uint8_t* src = tile_plane(t, pl);
+      if (pl < 5) {
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          lo |= (uint32_t)src[k * cells + c] << (8 * k);
+          hi |= (uint32_t)src[(k + 4) * cells + c] << (8 * k);
+        }
+        *reinterpret_cast<uint2*>(state_plane(st, pl) + g) = make_uint2(lo, hi);
+      } else {
+        const uint16_t* s16 = reinterpret_cast<const uint16_t*>(src);
+        uint32_t w[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          w[k] = (uint32_t)s16[(2 * k) * cells + c] | ((uint32_t)s16[(2 * k + 1) * cells + c] << 16);
+        *reinterpret_cast<uint4*>(state_plane(st, pl) + 2 * g) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+    return;
+  }
   const int total = cells * QQT_TILE_E;
   for (int i = threadIdx.x; i < total; i += blockDim.x) {
     const int c = i / QQT_TILE_E;
@@ -250,6 +334,12 @@ struct DangerScratch {
 
 // Stage A (chain correction among bombs, sim/blast.py:251-289).  Fills
 // s.cur[c] for every bomb cell (0 elsewhere).  Returns the bomb count.
+// Each round is a scatter: lane (front bomb, direction) walks its ray up to
+// its blast and raises the first bomb it meets (walls stop it, bricks end
+// it) with the front value.  That is the reference's per-bomb "nearest front
+// bomb per direction within its blast" gather: a bomb on a wall cell is
+// neither a source nor a target there (the wall test comes first), and it is
+// neither here, so the rounds and the values agree.
 __device__ inline int danger_stage_a(const Env& v, const DangerScratch& s, float fuse_f,
                                      int default_blast, int rounds, int* max_b_out) {
   const int lane = lane_id();
@@ -265,9 +355,26 @@ __device__ inline int danger_stage_a(const Env& v, const DangerScratch& s, float
   *max_b_out = mb;
   __syncwarp();
   for (int r = 0; r < rounds && nb > 0; ++r) {
-    for (int i = lane; i < nb; i += 32) {
-      const int c = s.bombs[i];
-      s.spread[c] = reach_max(v, c, s.front, default_blast, mb);
+    for (int i = lane; i < nb; i += 32) s.spread[s.bombs[i]] = 0.f;
+    __syncwarp();
+    for (int i = lane; i < 4 * nb; i += 32) {
+      const int f = s.bombs[i >> 2], d = i & 3;
+      const float fv = s.front[f];
+      if (!(fv > 0.f) || v.wall[f]) continue;
+      const int bl = blast_of(v, f, default_blast);
+      int rr = f / v.w, cc = f - rr * v.w;
+      for (int k = 1; k <= bl; ++k) {
+        rr += kDR[d];
+        cc += kDC[d];
+        if (rr < 0 || rr >= v.h || cc < 0 || cc >= v.w) break;
+        const int c = rr * v.w + cc;
+        if (v.wall[c]) break;
+        if (v.fuse[c] > 0) {
+          atomicMax(reinterpret_cast<int*>(s.spread + c), __float_as_int(fv));
+          break;
+        }
+        if (v.brick[c]) break;
+      }
     }
     __syncwarp();
     // each bomb is updated by one lane and reads only its own entries here
@@ -293,6 +400,42 @@ __device__ __forceinline__ float danger_at(const Env& v, const DangerScratch& s,
   if (v.wall[c]) return 0.f;
   const float own = v.fuse[c] > 0 ? s.cur[c] : 0.f;
   return fmaxf(own, reach_max(v, c, s.cur, default_blast, max_b));
+}
+
+// Stage B for a whole env (sim/blast.py:291-317), scatter form: out[c] =
+// the cell's own bomb weight (0 elsewhere, walls 0), raised by every bomb's
+// corrected weight along its four rays.  Lane (bomb, direction) walks
+// k = 1..blast(bomb) cells outwards: a wall stops the ray before it, any
+// other cell is raised (shared-memory atomicMax on the bits of the
+// non-negative float), and a bomb or brick stops the ray after it.  A cell
+// thus receives exactly the bombs it would find as the first solid cell
+// within their blast when looking along each direction: the same set, and
+// max is exact, so the values are identical to the gather form.  A bomb on
+// a wall cell is never found by the gather (the wall test comes first), so
+// it casts no rays here, and wall cells stay 0.
+__device__ inline void danger_paint(const Env& v, const DangerScratch& s, int nb,
+                                    int default_blast, float* out) {
+  const int lane = lane_id();
+  for (int c = lane; c < v.cells; c += 32)
+    out[c] = (v.fuse[c] > 0 && !v.wall[c]) ? s.cur[c] : 0.f;
+  __syncwarp();
+  for (int i = lane; i < 4 * nb; i += 32) {
+    const int q = s.bombs[i >> 2], d = i & 3;
+    const float val = s.cur[q];
+    if (!(val > 0.f) || v.wall[q]) continue;
+    const int bl = blast_of(v, q, default_blast);
+    int r = q / v.w, cc = q - r * v.w;
+    for (int k = 1; k <= bl; ++k) {
+      r += kDR[d];
+      cc += kDC[d];
+      if (r < 0 || r >= v.h || cc < 0 || cc >= v.w) break;
+      const int c = r * v.w + cc;
+      if (v.wall[c]) break;
+      atomicMax(reinterpret_cast<int*>(out + c), __float_as_int(val));
+      if (v.fuse[c] > 0 || v.brick[c]) break;
+    }
+  }
+  __syncwarp();
 }
 
 // ------------------------------------------------------------ movement

@@ -35,7 +35,7 @@ struct PInfo {
 // observation row staged in shared memory (the stage-A front/spread arrays
 // are dead by then and share its space), then the per-player values.
 struct ObsLayout {
-  size_t cur, bombs, row, pinfo, total;
+  size_t cur, bombs, row, pinfo, dng, total;
 };
 
 __host__ __device__ inline size_t a16(size_t x) { return (x + 15) & ~(size_t)15; }
@@ -48,7 +48,8 @@ __host__ __device__ inline ObsLayout obs_layout(int cells, int stride, int elem_
   const size_t row_bytes = (size_t)stride * elem_bytes;
   const size_t ab = (size_t)cells * 8;                  // front + spread
   L.pinfo = a16(L.row + (row_bytes > ab ? row_bytes : ab));
-  L.total = a16(L.pinfo + QQT_MAX_P * sizeof(PInfo));
+  L.dng = a16(L.pinfo + QQT_MAX_P * sizeof(PInfo));
+  L.total = a16(L.dng + (size_t)cells * 4);
   return L;
 }
 
@@ -88,6 +89,7 @@ k_observe(QqtCfg cfg, QqtState st, void* obs, float* danger_out, uint8_t* mm, ui
   ds.spread = ds.front + C;
   T* row = (T*)(wb + L.row);
   PInfo* pi = (PInfo*)(wb + L.pinfo);
+  float* dng = (float*)(wb + L.dng);
   const int lane = lane_id();
   const int nch = cfg.obs_channels;
 
@@ -95,8 +97,22 @@ k_observe(QqtCfg cfg, QqtState st, void* obs, float* danger_out, uint8_t* mm, ui
     const int e = e0 + s;
     if (e >= N) break;
     const Env v = env_view(tile, s, h, w);
+    // per-player and per-env scalars: the global loads are issued first so
+    // their latency overlaps the danger map
+    float g_py = 0.f, g_px = 0.f;
+    int g_alive = 0;
+    int64_t g_inv = 0, g_bcap = 0;
+    if (lane < P) {
+      g_py = st.pos[((size_t)lane * 2 + 0) * N + e];
+      g_px = st.pos[((size_t)lane * 2 + 1) * N + e];
+      g_alive = st.alive[(size_t)lane * N + e] != 0;
+      g_inv = st.invuln[(size_t)lane * N + e];
+      g_bcap = st.bombs_cap[(size_t)lane * N + e];
+    }
+    const int64_t g_t = st.t[e];
     int max_b = 0;
-    danger_stage_a(v, ds, cfg.fuse_f, cfg.blast, cfg.danger_rounds, &max_b);
+    const int nb = danger_stage_a(v, ds, cfg.fuse_f, cfg.blast, cfg.danger_rounds, &max_b);
+    danger_paint(v, ds, nb, cfg.blast, dng);
     int cnt[QQT_MAX_P] = {0, 0, 0, 0};
     for (int c = lane; c < C; c += 32) {
       const int o = v.owner[c];
@@ -108,9 +124,9 @@ k_observe(QqtCfg cfg, QqtState st, void* obs, float* danger_out, uint8_t* mm, ui
     if (lane < P) {
       const int p = lane;
       PInfo q;
-      q.y = st.pos[((size_t)p * 2 + 0) * N + e];
-      q.x = st.pos[((size_t)p * 2 + 1) * N + e];
-      q.alive = st.alive[(size_t)p * N + e] != 0;
+      q.y = g_py;
+      q.x = g_px;
+      q.alive = g_alive;
       q.live = live[p];
       const float g = q.alive ? 1.f : 0.f;
       const float fy = fminf(fmaxf(__fsub_rn(q.y, 0.5f), 0.f), (float)(h - 1));
@@ -129,9 +145,8 @@ k_observe(QqtCfg cfg, QqtState st, void* obs, float* danger_out, uint8_t* mm, ui
           q.sw[a2 * 2 + b2] = __fmul_rn(__fmul_rn(wys[a2], wxs[b2]), g);
         }
       q.flat = center_cell(q.y, q.x, h, w);
-      const int64_t inv = st.invuln[(size_t)p * N + e];
-      q.inv = (inv > 0 && q.alive) ? 1.f : 0.f;
-      q.bombs_cap = st.bombs_cap[(size_t)p * N + e];
+      q.inv = (g_inv > 0 && q.alive) ? 1.f : 0.f;
+      q.bombs_cap = g_bcap;
       const float cap = fmaxf((float)q.bombs_cap, 1.f);
       const float avail = fmaxf((float)(q.bombs_cap - (int64_t)q.live), 0.f);
       q.avail = __fmul_rn(__fdiv_rn(avail, cap), g);
@@ -140,10 +155,10 @@ k_observe(QqtCfg cfg, QqtState st, void* obs, float* danger_out, uint8_t* mm, ui
     }
     __syncwarp();   // stage A done (front/spread dead), PInfo visible
 
-    const float tv = __fdiv_rn((float)st.t[e], cfg.max_steps_f);
+    const float tv = __fdiv_rn((float)g_t, cfg.max_steps_f);
     if (obs || danger_out) {
       for (int c = lane; c < C; c += 32) {
-        const float d = danger_at(v, ds, c, cfg.blast, max_b);
+        const float d = dng[c];
         if (danger_out) danger_out[(size_t)e * C + c] = d;
         if (!obs) continue;
         const int f = v.fuse[c], o = v.owner[c];
@@ -275,6 +290,112 @@ __device__ inline bool relax_two(volatile float* d0, volatile float* d1, const f
   return false;
 }
 
+// The same fixed point with the fields in registers, for boards of H x W
+// <= 16 x 16: lane (f, r) = (lane / 16, lane % 16) holds row r of field f
+// (f = 0: d0, f = 1: d1) for the row sweeps (left-to-right then
+// right-to-left, vertical neighbours by shuffles within the 16-lane half),
+// then the rows are transposed through d0 / d1 so that lane (f, c) holds
+// column c for the column sweeps.  Every sweep phase relaxes each cell
+// against all four neighbours, so a phase that changes nothing is the
+// fixed point; the loop stops there.  Returns false if max_phases ran out.
+template <int H, int W>
+__device__ bool relax_two_reg(float* d0, float* d1, const float* cost, int max_phases) {
+  static_assert(H <= 16 && W <= 16, "one row or column per lane of a 16-lane half");
+  const int lane = lane_id(), f = lane >> 4, i = lane & 15;
+  const float INF = __int_as_float(0x7f800000);
+  float* dd = f ? d1 : d0;
+  const bool row_lane = i < H, col_lane = i < W;
+  float v[W > H ? W : H];                // a row (row phases) or a column (column phases)
+  float cr[W], cc[H];
+#pragma unroll
+  for (int c = 0; c < W; ++c) {
+    v[c] = row_lane ? dd[i * W + c] : INF;
+    cr[c] = row_lane ? cost[i * W + c] : INF;
+  }
+#pragma unroll
+  for (int r = 0; r < H; ++r) cc[r] = col_lane ? cost[r * W + i] : INF;
+  bool rows = true, done = false;
+  for (int ph = 0; ph < max_phases; ++ph) {
+    bool ch = false;
+    if (rows) {
+      float up[W], dn[W];
+#pragma unroll
+      for (int c = 0; c < W; ++c) {
+        up[c] = __shfl_up_sync(QQT_FULL, v[c], 1, 16);
+        dn[c] = __shfl_down_sync(QQT_FULL, v[c], 1, 16);
+        if (i == 0) up[c] = INF;
+        if (i >= H - 1) dn[c] = INF;
+        up[c] = fminf(up[c], dn[c]);
+      }
+#pragma unroll
+      for (int c = 0; c < W; ++c) {
+        float m = up[c];
+        if (c > 0) m = fminf(m, v[c - 1]);
+        if (c < W - 1) m = fminf(m, v[c + 1]);
+        const float nd = __fadd_rn(m, cr[c]);
+        if (nd < v[c]) { v[c] = nd; ch = true; }
+      }
+#pragma unroll
+      for (int c = W - 1; c >= 0; --c) {
+        float m = up[c];
+        if (c > 0) m = fminf(m, v[c - 1]);
+        if (c < W - 1) m = fminf(m, v[c + 1]);
+        const float nd = __fadd_rn(m, cr[c]);
+        if (nd < v[c]) { v[c] = nd; ch = true; }
+      }
+    } else {
+      float lf[H], rt[H];
+#pragma unroll
+      for (int r = 0; r < H; ++r) {
+        lf[r] = __shfl_up_sync(QQT_FULL, v[r], 1, 16);
+        rt[r] = __shfl_down_sync(QQT_FULL, v[r], 1, 16);
+        if (i == 0) lf[r] = INF;
+        if (i >= W - 1) rt[r] = INF;
+        lf[r] = fminf(lf[r], rt[r]);
+      }
+#pragma unroll
+      for (int r = 0; r < H; ++r) {
+        float m = lf[r];
+        if (r > 0) m = fminf(m, v[r - 1]);
+        if (r < H - 1) m = fminf(m, v[r + 1]);
+        const float nd = __fadd_rn(m, cc[r]);
+        if (nd < v[r]) { v[r] = nd; ch = true; }
+      }
+#pragma unroll
+      for (int r = H - 1; r >= 0; --r) {
+        float m = lf[r];
+        if (r > 0) m = fminf(m, v[r - 1]);
+        if (r < H - 1) m = fminf(m, v[r + 1]);
+        const float nd = __fadd_rn(m, cc[r]);
+        if (nd < v[r]) { v[r] = nd; ch = true; }
+      }
+    }
+    done = !__any_sync(QQT_FULL, ch);
+    // transpose through the field arrays (also the final write-back)
+    if (rows) {
+      if (row_lane)
+#pragma unroll
+        for (int c = 0; c < W; ++c) dd[i * W + c] = v[c];
+    } else {
+      if (col_lane)
+#pragma unroll
+        for (int r = 0; r < H; ++r) dd[r * W + i] = v[r];
+    }
+    __syncwarp();
+    if (done) break;
+    rows = !rows;
+    if (rows) {
+#pragma unroll
+      for (int c = 0; c < W; ++c) v[c] = row_lane ? dd[i * W + c] : INF;
+    } else {
+#pragma unroll
+      for (int r = 0; r < H; ++r) v[r] = col_lane ? dd[r * W + i] : INF;
+    }
+    __syncwarp();
+  }
+  return done;
+}
+
 __device__ __forceinline__ int argmin5(const float* s) {
   int best = 0;
   for (int k = 1; k < 5; ++k)
@@ -338,7 +459,9 @@ k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const fl
       }
     }
     __syncwarp();
-    if (!relax_two(vs, vo, cost, h, w, C + 1) && lane == 0) flag_error(QQT_DEV_NOT_CONVERGED);
+    const bool conv = (h == 13 && w == 13) ? relax_two_reg<13, 13>(vs, vo, cost, 2 * (C + 1))
+                                           : relax_two(vs, vo, cost, h, w, C + 1);
+    if (!conv && lane == 0) flag_error(QQT_DEV_NOT_CONVERGED);
     if (vsafe_out)
       for (int c = lane; c < C; c += 32) vsafe_out[(size_t)e * C + c] = vs[c];
     if (vopp_out)

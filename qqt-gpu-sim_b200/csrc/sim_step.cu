@@ -16,6 +16,7 @@ namespace qqt {
 
 struct PlayerState {
   float y, x, spd, lo_spd;
+  float rb_hit, rb_grow;   // crate pickup draws of this tick
   int alive0, hp, move, bomb, flat0, placed;
   int32_t since;
   int64_t bombs_cap, blast_cap, invuln, pending, combo, last_hit, lo_b, lo_z;
@@ -123,7 +124,12 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
       me.bomb = bo == 1 ? 1 : 0;
       me.flat0 = center_cell(me.y, me.x, h, w);
       me.placed = 0;
+      // the rewards' per-tick draws, loaded with the rest of the player state
+      me.rb_hit = cfg.corridor ? a.rb_hit[(size_t)e * P + p] : 0.f;
+      me.rb_grow = cfg.corridor ? a.rb_grow[(size_t)e * P + p] : 0.f;
     }
+    const float env_crate_prob = cfg.corridor ? st.crate_prob[e] : 0.f;
+    const bool env_hazard = cfg.crate_speed_only && st.hazard[e];
 
     // ---- 1-2. countdown and sequential placement
     if (a.phase != PHASE_AFTER_PLACE) {
@@ -386,11 +392,10 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
         stood = v.crate[flat1] != 0;
         reward = __fadd_rn(reward, __fmul_rn(__fmul_rn(cfg.brick_reward, stood ? 1.f : 0.f), a0f));
         const bool rec = v.recycle[flat1] != 0;
-        const float prob = rec ? cfg.recycle_crate_prob : st.crate_prob[e];
-        const size_t ri = (size_t)e * P + p;
-        const bool hits = stood && a.rb_hit[ri] < prob && me.alive0;
-        int attr = (int)floorf(__fmul_rn(a.rb_grow[ri], 3.f));
-        if (cfg.crate_speed_only && st.hazard[e]) attr = 2;
+        const float prob = rec ? cfg.recycle_crate_prob : env_crate_prob;
+        const bool hits = stood && me.rb_hit < prob && me.alive0;
+        int attr = (int)floorf(__fmul_rn(me.rb_grow, 3.f));
+        if (env_hazard) attr = 2;
         const int64_t add_b = (hits && attr == 0) ? 1 : 0;
         const int64_t add_z = (hits && attr == 1) ? 1 : 0;
         const float add_s = (hits && attr == 2) ? 1.f : 0.f;
