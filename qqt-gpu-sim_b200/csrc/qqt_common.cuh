@@ -289,6 +289,36 @@ __device__ inline void emit_flame(const Env& v, int src, int blast, int tier_cap
   }
 }
 
+// emit_flame that also queues every live, not yet triggered bomb its flame
+// covers (once: bit in qmask) into next[*qcount] for the next chain round.
+__device__ inline void emit_flame_queue(const Env& v, int src, int blast, int tier_cap,
+                                        volatile uint8_t* cov, const volatile uint8_t* trig,
+                                        uint32_t* qmask, int* qcount, uint16_t* next) {
+  if (v.wall[src] || v.brick[src]) return;
+  cov[src] = 1;
+  if (blast > tier_cap) return;
+  const int r0 = src / v.w, c0 = src - r0 * v.w;
+  for (int d = 0; d < 4; ++d) {
+    int r = r0, c = c0;
+    for (int k = 1; k <= blast; ++k) {
+      r += kDR[d];
+      c += kDC[d];
+      if (r < 0 || r >= v.h || c < 0 || c >= v.w) break;
+      const int q = r * v.w + c;
+      if (v.wall[q]) break;
+      cov[q] = 1;
+      if (v.fuse[q] > 0) {
+        if (!trig[q]) {
+          const uint32_t bit = 1u << (q & 31);
+          if (!(atomicOr(qmask + (q >> 5), bit) & bit)) next[atomicAdd(qcount, 1)] = (uint16_t)q;
+        }
+        break;
+      }
+      if (v.brick[q]) break;
+    }
+  }
+}
+
 // ------------------------------------------------------------- danger map
 
 // Bomb weight clamp(1 - (f-1)/FUSE, 0)^2 in float32 (sim/blast.py:218-220).
@@ -333,23 +363,30 @@ struct DangerScratch {
 };
 
 // Stage A (chain correction among bombs, sim/blast.py:251-289).  Fills
-// s.cur[c] for every bomb cell (0 elsewhere).  Returns the bomb count.
+// s.cur[c] for every bomb cell (other entries are not written).  Returns the
+// bomb count.
 // Each round is a scatter: lane (front bomb, direction) walks its ray up to
 // its blast and raises the first bomb it meets (walls stop it, bricks end
 // it) with the front value.  That is the reference's per-bomb "nearest front
 // bomb per direction within its blast" gather: a bomb on a wall cell is
 // neither a source nor a target there (the wall test comes first), and it is
 // neither here, so the rounds and the values agree.
+// nb_known >= 0: s.bombs already holds the nb_known bomb cells.
 __device__ inline int danger_stage_a(const Env& v, const DangerScratch& s, float fuse_f,
-                                     int default_blast, int rounds, int* max_b_out) {
+                                     int default_blast, int rounds, int* max_b_out,
+                                     int nb_known = -1) {
   const int lane = lane_id();
-  const int nb = warp_compact(v.cells, s.bombs, [&](int c) { return v.fuse[c] > 0; });
+  const int nb = nb_known >= 0 ? nb_known
+                               : warp_compact(v.cells, s.bombs, [&](int c) { return v.fuse[c] > 0; });
+  // only bomb entries of cur / front are ever read (here, by the paint and
+  // by danger_at), so the weights are computed for the bombs alone
   int mb = 0;
-  for (int c = lane; c < v.cells; c += 32) {
+  for (int i = lane; i < nb; i += 32) {
+    const int c = s.bombs[i];
     const float w = fuse_weight(v.fuse[c], fuse_f);
     s.cur[c] = w;
     s.front[c] = w;
-    if (v.fuse[c] > 0) mb = max(mb, blast_of(v, c, default_blast));
+    mb = max(mb, blast_of(v, c, default_blast));
   }
   mb = warp_max(mb);
   *max_b_out = mb;

@@ -29,7 +29,7 @@ struct PShared {
 
 // Per-warp scratch layout (byte offsets, 16-byte aligned sections).
 struct StepLayout {
-  size_t cov, trig, list, cur, bombs, ps, total;
+  size_t cov, trig, list, list2, qmask, cur, bombs, ps, total;
 };
 
 __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
@@ -39,7 +39,9 @@ __host__ __device__ inline StepLayout step_layout(int cells) {
   L.cov = 0;
   L.trig = align16(L.cov + cells);
   L.list = align16(L.trig + cells);
-  L.cur = align16(L.list + (size_t)cells * 2);
+  L.list2 = align16(L.list + (size_t)cells * 2);
+  L.qmask = align16(L.list2 + (size_t)cells * 2);        // queued bits + a counter
+  L.cur = align16(L.qmask + ((size_t)(cells + 31) / 32 + 1) * 4);
   L.bombs = align16(L.cur + (size_t)cells * 12);   // cur, front, spread
   L.ps = align16(L.bombs + (size_t)cells * 2);
   L.total = align16(L.ps + QQT_MAX_P * sizeof(PShared));
@@ -86,6 +88,9 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
   uint8_t* cov = wb + L.cov;
   uint8_t* trig = wb + L.trig;
   uint16_t* list = (uint16_t*)(wb + L.list);
+  uint16_t* list2 = (uint16_t*)(wb + L.list2);
+  uint32_t* qmask = (uint32_t*)(wb + L.qmask);            // bomb queued for the next round
+  int* qcount = (int*)(qmask + (C + 31) / 32);
   DangerScratch ds;
   ds.cur = (float*)(wb + L.cur);
   ds.front = ds.cur + C;
@@ -132,17 +137,29 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
     const bool env_hazard = cfg.crate_speed_only && st.hazard[e];
 
     // ---- 1-2. countdown and sequential placement
+    int ns0 = -1;                     // explosion sources in `list` (-1: not yet)
     if (a.phase != PHASE_AFTER_PLACE) {
-      for (int c = lane; c < C; c += 32) {
-        const int16_t f = v.fuse[c];
-        if (f > 0) v.fuse[c] = f - 1;
-      }
-      __syncwarp();
+      // one pass: countdown, live bombs per owner, this tick's explosion
+      // sources (fuse reached 0, owner set) compacted into `list`
       int cnt[QQT_MAX_P] = {0, 0, 0, 0};
-      for (int c = lane; c < C; c += 32) {
-        const int o = v.owner[c];
-        if (v.fuse[c] > 0 && o >= 0 && o < P) cnt[o]++;
+      ns0 = 0;
+      for (int base = 0; base < C; base += 32) {
+        const int c = base + lane;
+        bool src = false;
+        if (c < C) {
+          int f = v.fuse[c];
+          if (f > 0) v.fuse[c] = (int16_t)(--f);
+          const int o = v.owner[c];
+          if (f > 0 && o >= 0 && o < P) cnt[o]++;
+          src = f == 0 && o >= 0;
+          cov[c] = 0;
+          trig[c] = src ? 1 : 0;
+        }
+        const unsigned m = __ballot_sync(QQT_FULL, src);
+        if (src) list[ns0 + __popc(m & ((1u << lane) - 1u))] = (uint16_t)c;
+        ns0 += __popc(m);
       }
+      if (lane < (C + 31) / 32 + 1) qmask[lane] = 0;   // queue bits and counter
       int live[QQT_MAX_P];
 #pragma unroll
       for (int q = 0; q < QQT_MAX_P; ++q) live[q] = warp_sum(cnt[q]);
@@ -164,6 +181,11 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
             v.fuse[idx] = (int16_t)cfg.fuse;
             v.owner[idx] = (int8_t)q;
             v.blast[idx] = (int16_t)ps[q].blast_cap;
+            if (trig[idx]) {          // it replaced a bomb exploding now: no source
+              trig[idx] = 0;
+              for (int i = 0; i < ns0; ++i)
+                if (list[i] == idx) list[i] = 0xffff;
+            }
           }
         }
       }
@@ -178,6 +200,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
         continue;
       }
     } else {
+      ns0 = -1;                       // sources are compacted below
       if (p < P) {
         me.placed = a.placed_buf[(size_t)p * N + e];
         ps[p].flat0 = me.flat0;
@@ -274,29 +297,44 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
       me.x = fminf(fmaxf(ox, cfg.radius), cfg.w_minus_rad);
     }
 
-    // ---- 6. chain explosion (sim/blast.py:101-155)
-    for (int c = lane; c < C; c += 32) {
-      cov[c] = 0;
-      trig[c] = (v.fuse[c] == 0 && v.owner[c] >= 0) ? 1 : 0;
-    }
-    __syncwarp();
+    // ---- 6. chain explosion (sim/blast.py:101-155).  Round r triggers the
+    //      live bombs covered by the flames so far; a flame that covers a
+    //      live untriggered bomb queues it (once) for the next round, so a
+    //      round reads the queue instead of scanning the board.
     {
-      int ns = warp_compact(C, list, [&](int c) { return trig[c] != 0; });
-      for (int i = lane; i < ns; i += 32) {
-        const int c = list[i];
-        emit_flame(v, c, blast_of(v, c, cfg.blast), tiers, cov);
+      int ns = ns0;
+      if (ns < 0) {
+        for (int c = lane; c < C; c += 32) {
+          cov[c] = 0;
+          trig[c] = (v.fuse[c] == 0 && v.owner[c] >= 0) ? 1 : 0;
+        }
+        if (lane < (C + 31) / 32 + 1) qmask[lane] = 0;
+        __syncwarp();
+        ns = warp_compact(C, list, [&](int c) { return trig[c] != 0; });
       }
       __syncwarp();
-      for (int r = 0; r < cfg.resolve_rounds; ++r) {
-        ns = warp_compact(C, list, [&](int c) { return v.fuse[c] > 0 && cov[c] && !trig[c]; });
-        if (ns == 0) break;
-        for (int i = lane; i < ns; i += 32) trig[list[i]] = 1;
-        __syncwarp();
+      uint16_t* cur_list = list;
+      uint16_t* next_list = list2;
+      for (int r = 0; r <= cfg.resolve_rounds; ++r) {
+        // round 0 emits the sources; round r >= 1 triggers the queue first
+        if (r > 0) {
+          ns = *qcount;
+          __syncwarp();
+          if (ns == 0) break;
+          for (int i = lane; i < ns; i += 32) trig[cur_list[i]] = 1;
+          if (lane == 0) *qcount = 0;
+          __syncwarp();
+        }
         for (int i = lane; i < ns; i += 32) {
-          const int c = list[i];
-          emit_flame(v, c, blast_of(v, c, cfg.blast), tiers, cov);
+          const int c = cur_list[i];
+          if (c == 0xffff) continue;
+          emit_flame_queue(v, c, blast_of(v, c, cfg.blast), tiers, cov, trig, qmask, qcount,
+                           next_list);
         }
         __syncwarp();
+        uint16_t* tmp = cur_list;
+        cur_list = next_list;
+        next_list = tmp;
       }
     }
 
@@ -320,13 +358,8 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
       }
     }
 
-    // ---- 8. bricks burnt: crates on corridor maps
-    for (int c = lane; c < C; c += 32) {
-      if (cov[c]) {
-        if (cfg.corridor && v.brick[c]) v.crate[c] = 1;
-        v.brick[c] = 0;
-      }
-    }
+    // ---- 8. (bricks burnt: in the clearing pass below; damage reads only
+    //      the flame plane)
 
     // ---- 9. damage and invulnerability
     int flat1 = 0, hp_new = 0, alive = 0, died = 0, lost_hp = 0;
@@ -342,13 +375,28 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
       if (hit_eff) me.invuln = cfg.invuln_ticks;
     }
     __syncwarp();
-    // ---- 10. clear exploded bombs
-    for (int c = lane; c < C; c += 32) {
-      if (trig[c]) {
-        v.fuse[c] = 0;
-        v.owner[c] = -1;
-        v.blast[c] = 0;
+    // ---- 8 + 10. one pass: burnt bricks become crates on corridor maps,
+    //      exploded bombs are cleared, and the bombs left are compacted for
+    //      the danger-standing penalty below
+    int nb_post = 0;
+    for (int base = 0; base < C; base += 32) {
+      const int c = base + lane;
+      bool bomb = false;
+      if (c < C) {
+        if (cov[c]) {
+          if (cfg.corridor && v.brick[c]) v.crate[c] = 1;
+          v.brick[c] = 0;
+        }
+        if (trig[c]) {
+          v.fuse[c] = 0;
+          v.owner[c] = -1;
+          v.blast[c] = 0;
+        }
+        bomb = v.fuse[c] > 0;
       }
+      const unsigned m = __ballot_sync(QQT_FULL, bomb);
+      if (bomb) ds.bombs[nb_post + __popc(m & ((1u << lane) - 1u))] = (uint16_t)c;
+      nb_post += __popc(m);
     }
     // ---- 11. t and done
     const int64_t t1 = st.t[e] + 1;
@@ -413,7 +461,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
     // danger standing penalty on the post-step state (sim/torch_sim.py:1163-1182)
     {
       int max_b = 0;
-      danger_stage_a(v, ds, cfg.fuse_f, cfg.blast, cfg.danger_rounds, &max_b);
+      danger_stage_a(v, ds, cfg.fuse_f, cfg.blast, cfg.danger_rounds, &max_b, nb_post);
       if (p < P) {
         const float standing = danger_at(v, ds, flat1, cfg.blast, max_b);
         reward = __fsub_rn(reward, __fmul_rn(__fmul_rn(cfg.danger_penalty, standing), a0f));
