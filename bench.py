@@ -66,6 +66,8 @@ OBS_ROW = 2368 * 2
 ALG_BYTES = {
     "step": 169 * (1 + 1 + 1 + 1 + 2 + 1 + 2) * 2 - 169 + 280 + 32 + 8 + 1,
     "observe": 169 * (1 + 1 + 1 + 1 + 2 + 2) + 56 + OBS_ROW + 14,
+    # the step with the next observation: the step's bytes + the row and masks
+    "step+observe": 169 * (1 + 1 + 1 + 1 + 2 + 1 + 2) * 2 - 169 + 280 + 32 + 8 + 1 + OBS_ROW + 14,
     "astar": 169 * (1 + 1 + 1 + 2) + 169 * 2 + 10 + 20 + 16,
     "greedy": 169 * (1 + 1 + 1 + 2) + 169 * 2 + 10 + 20 + 16,
     "policy": OBS_ROW,           # + per seat: masks, uniforms, actions, log-prob, value
@@ -256,7 +258,7 @@ def instrumented_kernel_times(ro):
     import torch
     sim, buf, dr = ro.sim, ro.buf, ro.draws
     bot_name = CFG["opponent"] or "bot"
-    times = {k: [] for k in ("observe", "policy", bot_name, "step", "flush")}
+    times = {k: [] for k in ("observe", "policy", bot_name, "step+observe", "step", "flush")}
 
     def timed(name, fn):
         a = torch.cuda.Event(enable_timing=True)
@@ -267,12 +269,16 @@ def instrumented_kernel_times(ro):
         times[name].append((a, b))
 
     bot, seats = ro.opponent, ro.seats
+    ready = -1
     for t in range(ro.T):
         holder = {}
         b = t % ro.slots
-        timed("observe", lambda: holder.update(zip(("obs", "mm", "bm"), sim.observe_and_mask(
-            buf.obs_rows[b], buf.mm[b], buf.bm[b], danger=False))))
-        obs, mm, bm = holder["obs"], holder["mm"], holder["bm"]
+        if ready == t:
+            obs, mm, bm = buf.obs(b), buf.mm[b], buf.bm[b]
+        else:
+            timed("observe", lambda: holder.update(zip(("obs", "mm", "bm"), sim.observe_and_mask(
+                buf.obs_rows[b], buf.mm[b], buf.bm[b], danger=False))))
+            obs, mm, bm = holder["obs"], holder["mm"], holder["bm"]
         acts = buf.act[b]
         timed("policy", lambda: ro.learner.act_seats(
             obs, [mm[:, s] for s in seats], [bm[:, s] for s in seats], dr.u_net[t],
@@ -281,23 +287,32 @@ def instrumented_kernel_times(ro):
             o = ro.opp_seat
             ro.feed_opponent(t)
             timed(bot_name, lambda: bot.act(obs, mm[:, o], bm[:, o], o, out=acts[:, o]))
-        timed("step", lambda: sim.step(acts, auto_reset=True,
-                                       crate_draws=(dr.crate[t, 0], dr.crate[t, 1]),
-                                       reward_out=buf.rew[b], done_out=buf.done[b],
-                                       hit_out=buf.dmg[b], info_planes=False))
-        if t % 16 == 15:
+        flush = t % 16 == 15
+        nxt = None
+        if ro.fuse_observe and not flush and t + 1 < ro.T:
+            b1 = (t + 1) % ro.slots
+            nxt = (buf.obs_rows[b1], buf.mm[b1], buf.bm[b1])
+        timed("step+observe" if nxt is not None else "step",
+              lambda: sim.step(acts, auto_reset=True, crate_draws=(dr.crate[t, 0], dr.crate[t, 1]),
+                               reward_out=buf.rew[b], done_out=buf.done[b], hit_out=buf.dmg[b],
+                               info_planes=False, next_obs=nxt))
+        ready = t + 1 if nxt is not None else -1
+        if flush:
             timed("flush", lambda: sim.flush_recycle())
     torch.cuda.synchronize()
     return {k: (len(v), sum(a.elapsed_time(b) for a, b in v) / max(1, len(v)))
             for k, v in times.items()}
 
 
-def _launches_per_tick():
-    """Kernels per tick of one env group: observe, policy (fused MLP: 1;
-    CNN: trunk + heads per seat), bot (astar: cap + field; greedy: 1), step."""
+def _launches_per_rollout():
+    """Kernels per rollout of one env group: per tick policy (fused MLP: 1;
+    CNN: trunk + linear/tail per seat), bot (astar: cap + field; greedy: 1)
+    and the step (which also writes the next observation); a separate observe
+    on the first tick and after each crate recycling; the recycling itself."""
     pol = 1 if CFG["learner"] == "mlp" else 1 + len(CFG["seats"])
     bot = {"astar": 2, "greedy": 1, None: 0}[CFG["opponent"]]
-    return 1 + pol + bot + 1
+    flushes = TICKS // 16
+    return TICKS * (pol + bot + 1) + 1 + (flushes - 1 if TICKS % 16 == 0 else flushes) + flushes
 
 
 def ppo_leg(grp, device):
@@ -475,8 +490,7 @@ def gpu_bench(args):
                        "cuda_graph": True},
             "e2e": {"value": round(e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            # per tick and group: observe, policy, bot, step; recycling every 16 ticks
-            "gpu_launches": (TICKS * _launches_per_tick() + TICKS // 16) * groups * args.steps,
+            "gpu_launches": _launches_per_rollout() * groups * args.steps,
             "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1),
                          "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                          "peak_source": src, "traffic": traffic,

@@ -152,6 +152,20 @@ int qqt_step(const QqtCfg *cfg, const QqtState *st, const int64_t *actions,
              void *scratch, qqt_stream_t stream);
 uint64_t qqt_step_scratch_bytes(const QqtCfg *cfg);
 
+/* qqt_step fused with the next tick's observation: after the step (and the
+ * device auto-reset) the same kernel writes the observation row and legal
+ * masks of the resulting state, exactly what qqt_observe would produce for
+ * it (the danger map reuses the step's danger-standing computation).
+ * Replaces BatchedSim.step followed by the next tick's observe() +
+ * legal_mask() in SelfPlayRunner.collect (train/ppo.py:215-249).
+ *   obs  [N][obs_stride] fp16 rows (cfg->obs_fp32 must be 0), 16-byte
+ *        aligned, obs_stride % 8 == 0;  mm [N][P][5], bm [N][P][2] uint8.
+ * Other arguments as qqt_step. */
+int qqt_step_observe(const QqtCfg *cfg, const QqtState *st, const int64_t *actions,
+                     const float *rb_hit, const float *rb_grow, int32_t *tiers,
+                     int32_t first_step, const QqtStepOut *out, const QqtTemplate *tmpl,
+                     void *scratch, void *obs, uint8_t *mm, uint8_t *bm, qqt_stream_t stream);
+
 /* qqt_step for callers that cannot allocate device memory (for example code
  * running inside another runtime's stream capture, or an embedding that only
  * hands this library pre-placed buffers).  No counterpart in the reference:

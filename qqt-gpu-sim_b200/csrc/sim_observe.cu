@@ -1,10 +1,9 @@
 // Danger map + shared fp16 observation + legal masks, and the rule bots.
 //
-// k_observe: one block per tile of 32 envs, one warp per env at a time.
-//   danger: stage A (chain correction among bombs, gather over the nearest
-//   bomb per direction) then stage B per cell; observation rows are written
-//   straight from registers in 16-byte chunks (lane j writes chunk j of the
-//   env's padded row), so every store is a coalesced 128-bit store.
+// k_observe: one block per tile of 8 envs, one warp per env.
+//   danger: stage A (chain correction among bombs) and stage B, both as
+//   scatters along each bomb's rays; the observation row is written straight
+//   to global memory (consecutive lanes, consecutive cells of a channel).
 // k_astar: warp per env; the two path fields share one warp (row / column
 //   sweeps to a fixed point, exactly the reference's Bellman-Ford limit).
 
@@ -35,19 +34,20 @@ struct PInfo {
 // observation row staged in shared memory (the stage-A front/spread arrays
 // are dead by then and share its space), then the per-player values.
 struct ObsLayout {
-  size_t cur, bombs, row, pinfo, dng, total;
+  size_t cur, bombs, fs, pinfo, dng, total;
 };
 
 __host__ __device__ inline size_t a16(size_t x) { return (x + 15) & ~(size_t)15; }
 
-__host__ __device__ inline ObsLayout obs_layout(int cells, int stride, int elem_bytes) {
+// Per-warp scratch of k_observe: stage-A weights, bomb list, front + spread,
+// player info, the danger map.  The observation row itself is written
+// straight to global memory.
+__host__ __device__ inline ObsLayout obs_layout(int cells) {
   ObsLayout L;
   L.cur = 0;
   L.bombs = a16((size_t)cells * 4);
-  L.row = a16(L.bombs + (size_t)cells * 2);
-  const size_t row_bytes = (size_t)stride * elem_bytes;
-  const size_t ab = (size_t)cells * 8;                  // front + spread
-  L.pinfo = a16(L.row + (row_bytes > ab ? row_bytes : ab));
+  L.fs = a16(L.bombs + (size_t)cells * 2);
+  L.pinfo = a16(L.fs + (size_t)cells * 8);
   L.dng = a16(L.pinfo + QQT_MAX_P * sizeof(PInfo));
   L.total = a16(L.dng + (size_t)cells * 4);
   return L;
@@ -65,6 +65,141 @@ struct FuseTables {
   float weight[32], norm[32];
 };
 
+// One env's observation row, masks and (optionally) danger map from its
+// staged planes (sim/obs.py:25-229), for the warp that owns the env.  Inputs:
+// dng = the env's danger map (sim/blast.py:158-317), live[p] = live bombs of
+// player p, and for lanes < P that player's position, alive flag,
+// invulnerability and bomb cap.  The row goes straight to global memory:
+// lane l writes cell l, l+32, ... of every channel (consecutive lanes,
+// consecutive fp16 elements).
+template <class T>
+__device__ inline void observe_env(const QqtCfg& cfg, const Env& v, int e, PInfo* pi,
+                                   const float* dng, const int* live, float py, float px,
+                                   bool alive_p, int64_t inv_p, int64_t bcap_p, int64_t t_e,
+                                   const FuseTables& ft, void* obs, float* danger_out,
+                                   uint8_t* mm, uint8_t* bm) {
+  const int h = cfg.height, w = cfg.width, C = h * w, P = cfg.n_players;
+  const int lane = lane_id();
+  const int nch = cfg.obs_channels;
+  if (lane < P) {
+    const int p = lane;
+    PInfo q;
+    q.y = py;
+    q.x = px;
+    q.alive = alive_p;
+    q.live = live[p];
+    const float g = q.alive ? 1.f : 0.f;
+    const float fy = fminf(fmaxf(__fsub_rn(q.y, 0.5f), 0.f), (float)(h - 1));
+    const float fx = fminf(fmaxf(__fsub_rn(q.x, 0.5f), 0.f), (float)(w - 1));
+    const int y0 = min(max((int)floorf(fy), 0), h - 1), x0 = min(max((int)floorf(fx), 0), w - 1);
+    const int y1 = min(y0 + 1, h - 1), x1 = min(x0 + 1, w - 1);
+    const float wy = fminf(fmaxf(__fsub_rn(fy, (float)y0), 0.f), 1.f);
+    const float wx = fminf(fmaxf(__fsub_rn(fx, (float)x0), 0.f), 1.f);
+    const float wys[2] = {__fsub_rn(1.f, wy), wy}, wxs[2] = {__fsub_rn(1.f, wx), wx};
+    const int ys[2] = {y0, y1}, xs[2] = {x0, x1};
+#pragma unroll
+    for (int a2 = 0; a2 < 2; ++a2)
+#pragma unroll
+      for (int b2 = 0; b2 < 2; ++b2) {
+        q.sc[a2 * 2 + b2] = ys[a2] * w + xs[b2];
+        q.sw[a2 * 2 + b2] = __fmul_rn(__fmul_rn(wys[a2], wxs[b2]), g);
+      }
+    q.flat = center_cell(q.y, q.x, h, w);
+    q.inv = (inv_p > 0 && q.alive) ? 1.f : 0.f;
+    q.bombs_cap = bcap_p;
+    const float cap = fmaxf((float)q.bombs_cap, 1.f);
+    const float avail = fmaxf((float)(q.bombs_cap - (int64_t)q.live), 0.f);
+    q.avail = __fmul_rn(__fdiv_rn(avail, cap), g);
+    q.capv = __fmul_rn(__fdiv_rn(cap, cfg.obs_growth_bombs_max), g);
+    pi[p] = q;
+  }
+  __syncwarp();   // PInfo visible
+
+  const float tv = __fdiv_rn((float)t_e, cfg.max_steps_f);
+  T* row = obs ? (T*)obs + (size_t)e * cfg.obs_stride : nullptr;
+  if (obs || danger_out) {
+    for (int c = lane; c < C; c += 32) {
+      const float d = dng[c];
+      if (danger_out) danger_out[(size_t)e * C + c] = d;
+      if (!obs) continue;
+      const int f = v.fuse[c], o = v.owner[c];
+      const float fn = f > 0 ? (f < 32 ? ft.norm[f] : __fdiv_rn((float)f, cfg.fuse_f)) : 0.f;
+      for (int p = 0; p < P; ++p) {
+        const PInfo& q = pi[p];
+        float sv = 0.f;
+#pragma unroll
+        for (int m = 0; m < 4; ++m)
+          if (q.sc[m] == c) sv = __fadd_rn(sv, q.sw[m]);
+        row[p * C + c] = to_obs<T>(sv);
+        row[(P + p) * C + c] = to_obs<T>((o == p && f > 0) ? fn : 0.f);
+      }
+      row[2 * P * C + c] = to_obs<T>((v.wall[c] | v.brick[c]) ? 1.f : 0.f);
+      row[(2 * P + 1) * C + c] = to_obs<T>(d);
+      row[(2 * P + 2) * C + c] = to_obs<T>(tv);
+      if (nch > 2 * P + 3) {
+        row[(2 * P + 3) * C + c] = to_obs<T>(v.crate[c] ? 1.f : 0.f);
+        // invulnerability flag, available / cap bombs: at each player's cell
+        for (int p = 0; p < P; ++p) {
+          const PInfo& q = pi[p];
+          const bool at = q.flat == c;
+          row[(2 * P + 4 + p) * C + c] = to_obs<T>(at ? q.inv : 0.f);
+          row[(3 * P + 4 + p) * C + c] = to_obs<T>(at ? q.avail : 0.f);
+          row[(4 * P + 4 + p) * C + c] = to_obs<T>(at ? q.capv : 0.f);
+        }
+        for (int ch = 5 * P + 4; ch < nch; ++ch) row[ch * C + c] = to_obs<T>(0.f);
+      }
+    }
+  }
+  if (obs)
+    for (int i = nch * C + lane; i < cfg.obs_stride; i += 32) row[i] = to_obs<T>(0.f);
+
+  if (mm) {
+    if (lane < 4 * P) {
+      const int p = lane >> 2, d = lane & 3;
+      const PInfo& q = pi[p];
+      const float dv = (d & 1) ? cfg.step_len : -cfg.step_len;
+      bool moved;
+      if (d < 2) {
+        const float ny = resolve_axis(v, __fadd_rn(q.y, dv), dv, q.x, q.y, q.x, cfg.radius, true);
+        moved = fabsf(__fsub_rn(ny, q.y)) > cfg.move_eps2;
+      } else {
+        const float nx = resolve_axis(v, __fadd_rn(q.x, dv), dv, q.y, q.y, q.x, cfg.radius, false);
+        moved = fabsf(__fsub_rn(nx, q.x)) > cfg.move_eps2;
+      }
+      mm[((size_t)e * P + p) * 5 + d] = q.alive ? (moved ? 1 : 0) : 1;
+    } else if (lane < 5 * P) {
+      mm[((size_t)e * P + (lane - 4 * P)) * 5 + 4] = 1;
+    }
+  }
+  if (bm && lane < P) {
+    const PInfo& q = pi[lane];
+    const bool under = v.fuse[q.flat] > 0;
+    const bool under_b = under || v.brick[q.flat];
+    const bool ok = !under && !under_b && (int64_t)q.live < q.bombs_cap;
+    bm[((size_t)e * P + lane) * 2 + 0] = 1;
+    bm[((size_t)e * P + lane) * 2 + 1] = q.alive ? (ok ? 1 : 0) : 1;
+  }
+  __syncwarp();
+}
+
+// Live bombs per owner (fuse > 0, owner in [0, P)), warp-wide.
+__device__ inline void live_counts(const Env& v, int P, int* live) {
+  int cnt[QQT_MAX_P] = {0, 0, 0, 0};
+  for (int c = lane_id(); c < v.cells; c += 32) {
+    const int o = v.owner[c];
+    if (v.fuse[c] > 0 && o >= 0 && o < P) cnt[o]++;
+  }
+#pragma unroll
+  for (int p = 0; p < QQT_MAX_P; ++p) live[p] = warp_sum(cnt[p]);
+}
+
+__device__ inline void fuse_tables(FuseTables& ft, float fuse_f) {
+  if (threadIdx.x < 32) {
+    ft.weight[threadIdx.x] = fuse_weight(threadIdx.x, fuse_f);
+    ft.norm[threadIdx.x] = __fdiv_rn((float)threadIdx.x, fuse_f);
+  }
+}
+
 template <bool F32OUT>
 __global__ void __launch_bounds__(QQT_NWARP * 32)
 k_observe(QqtCfg cfg, QqtState st, void* obs, float* danger_out, uint8_t* mm, uint8_t* bm) {
@@ -73,25 +208,20 @@ k_observe(QqtCfg cfg, QqtState st, void* obs, float* danger_out, uint8_t* mm, ui
   __shared__ FuseTables ft;
   const int h = cfg.height, w = cfg.width, C = h * w, N = cfg.n_envs, P = cfg.n_players;
   const int e0 = blockIdx.x * QQT_TILE_E;
-  if (threadIdx.x < 32) {
-    ft.weight[threadIdx.x] = fuse_weight(threadIdx.x, cfg.fuse_f);
-    ft.norm[threadIdx.x] = __fdiv_rn((float)threadIdx.x, cfg.fuse_f);
-  }
+  fuse_tables(ft, cfg.fuse_f);
   Tile tile = carve_tile(smem, C);
   load_tile(tile, st, N, e0, PL_WALL | PL_BRICK | PL_CRATE | PL_OWNER | PL_FUSE | PL_BLAST);
   __syncthreads();
-  const ObsLayout L = obs_layout(C, cfg.obs_stride, (int)sizeof(T));
+  const ObsLayout L = obs_layout(C);
   uint8_t* wb = smem + tile_bytes(C) + (size_t)warp_id() * L.total;
   DangerScratch ds;
   ds.cur = (float*)(wb + L.cur);
   ds.bombs = (uint16_t*)(wb + L.bombs);
-  ds.front = (float*)(wb + L.row);
+  ds.front = (float*)(wb + L.fs);
   ds.spread = ds.front + C;
-  T* row = (T*)(wb + L.row);
   PInfo* pi = (PInfo*)(wb + L.pinfo);
   float* dng = (float*)(wb + L.dng);
   const int lane = lane_id();
-  const int nch = cfg.obs_channels;
 
   for (int s = warp_id(); s < QQT_TILE_E; s += QQT_NWARP) {
     const int e = e0 + s;
@@ -113,117 +243,10 @@ k_observe(QqtCfg cfg, QqtState st, void* obs, float* danger_out, uint8_t* mm, ui
     int max_b = 0;
     const int nb = danger_stage_a(v, ds, cfg.fuse_f, cfg.blast, cfg.danger_rounds, &max_b);
     danger_paint(v, ds, nb, cfg.blast, dng);
-    int cnt[QQT_MAX_P] = {0, 0, 0, 0};
-    for (int c = lane; c < C; c += 32) {
-      const int o = v.owner[c];
-      if (v.fuse[c] > 0 && o >= 0 && o < P) cnt[o]++;
-    }
     int live[QQT_MAX_P];
-#pragma unroll
-    for (int p = 0; p < QQT_MAX_P; ++p) live[p] = warp_sum(cnt[p]);
-    if (lane < P) {
-      const int p = lane;
-      PInfo q;
-      q.y = g_py;
-      q.x = g_px;
-      q.alive = g_alive;
-      q.live = live[p];
-      const float g = q.alive ? 1.f : 0.f;
-      const float fy = fminf(fmaxf(__fsub_rn(q.y, 0.5f), 0.f), (float)(h - 1));
-      const float fx = fminf(fmaxf(__fsub_rn(q.x, 0.5f), 0.f), (float)(w - 1));
-      const int y0 = min(max((int)floorf(fy), 0), h - 1), x0 = min(max((int)floorf(fx), 0), w - 1);
-      const int y1 = min(y0 + 1, h - 1), x1 = min(x0 + 1, w - 1);
-      const float wy = fminf(fmaxf(__fsub_rn(fy, (float)y0), 0.f), 1.f);
-      const float wx = fminf(fmaxf(__fsub_rn(fx, (float)x0), 0.f), 1.f);
-      const float wys[2] = {__fsub_rn(1.f, wy), wy}, wxs[2] = {__fsub_rn(1.f, wx), wx};
-      const int ys[2] = {y0, y1}, xs[2] = {x0, x1};
-#pragma unroll
-      for (int a2 = 0; a2 < 2; ++a2)
-#pragma unroll
-        for (int b2 = 0; b2 < 2; ++b2) {
-          q.sc[a2 * 2 + b2] = ys[a2] * w + xs[b2];
-          q.sw[a2 * 2 + b2] = __fmul_rn(__fmul_rn(wys[a2], wxs[b2]), g);
-        }
-      q.flat = center_cell(q.y, q.x, h, w);
-      q.inv = (g_inv > 0 && q.alive) ? 1.f : 0.f;
-      q.bombs_cap = g_bcap;
-      const float cap = fmaxf((float)q.bombs_cap, 1.f);
-      const float avail = fmaxf((float)(q.bombs_cap - (int64_t)q.live), 0.f);
-      q.avail = __fmul_rn(__fdiv_rn(avail, cap), g);
-      q.capv = __fmul_rn(__fdiv_rn(cap, cfg.obs_growth_bombs_max), g);
-      pi[p] = q;
-    }
-    __syncwarp();   // stage A done (front/spread dead), PInfo visible
-
-    const float tv = __fdiv_rn((float)g_t, cfg.max_steps_f);
-    if (obs || danger_out) {
-      for (int c = lane; c < C; c += 32) {
-        const float d = dng[c];
-        if (danger_out) danger_out[(size_t)e * C + c] = d;
-        if (!obs) continue;
-        const int f = v.fuse[c], o = v.owner[c];
-        const float fn = f > 0 ? (f < 32 ? ft.norm[f] : __fdiv_rn((float)f, cfg.fuse_f)) : 0.f;
-        for (int p = 0; p < P; ++p) {
-          const PInfo& q = pi[p];
-          float sv = 0.f;
-#pragma unroll
-          for (int m = 0; m < 4; ++m)
-            if (q.sc[m] == c) sv = __fadd_rn(sv, q.sw[m]);
-          row[p * C + c] = to_obs<T>(sv);
-          row[(P + p) * C + c] = to_obs<T>((o == p && f > 0) ? fn : 0.f);
-        }
-        row[2 * P * C + c] = to_obs<T>((v.wall[c] | v.brick[c]) ? 1.f : 0.f);
-        row[(2 * P + 1) * C + c] = to_obs<T>(d);
-        row[(2 * P + 2) * C + c] = to_obs<T>(tv);
-        if (nch > 2 * P + 3) {
-          row[(2 * P + 3) * C + c] = to_obs<T>(v.crate[c] ? 1.f : 0.f);
-          for (int ch = 2 * P + 4; ch < nch; ++ch) row[ch * C + c] = to_obs<T>(0.f);
-        }
-      }
-    }
-    if (obs) {
-      for (int i = nch * C + lane; i < cfg.obs_stride; i += 32) row[i] = to_obs<T>(0.f);
-      __syncwarp();
-      if (lane < P && nch > 2 * P + 3) {
-        const PInfo& q = pi[lane];
-        row[(2 * P + 4 + lane) * C + q.flat] = to_obs<T>(q.inv);
-        row[(3 * P + 4 + lane) * C + q.flat] = to_obs<T>(q.avail);
-        row[(4 * P + 4 + lane) * C + q.flat] = to_obs<T>(q.capv);
-      }
-      __syncwarp();
-      const int nchunk = cfg.obs_stride * (int)sizeof(T) / 16;
-      const uint4* src = reinterpret_cast<const uint4*>(row);
-      uint4* dst = reinterpret_cast<uint4*>((uint8_t*)obs + (size_t)e * cfg.obs_stride * sizeof(T));
-      for (int j = lane; j < nchunk; j += 32) dst[j] = src[j];
-    }
-
-    if (mm) {
-      if (lane < 4 * P) {
-        const int p = lane >> 2, d = lane & 3;
-        const PInfo& q = pi[p];
-        const float dv = (d & 1) ? cfg.step_len : -cfg.step_len;
-        bool moved;
-        if (d < 2) {
-          const float ny = resolve_axis(v, __fadd_rn(q.y, dv), dv, q.x, q.y, q.x, cfg.radius, true);
-          moved = fabsf(__fsub_rn(ny, q.y)) > cfg.move_eps2;
-        } else {
-          const float nx = resolve_axis(v, __fadd_rn(q.x, dv), dv, q.y, q.y, q.x, cfg.radius, false);
-          moved = fabsf(__fsub_rn(nx, q.x)) > cfg.move_eps2;
-        }
-        mm[((size_t)e * P + p) * 5 + d] = q.alive ? (moved ? 1 : 0) : 1;
-      } else if (lane < 5 * P) {
-        mm[((size_t)e * P + (lane - 4 * P)) * 5 + 4] = 1;
-      }
-    }
-    if (bm && lane < P) {
-      const PInfo& q = pi[lane];
-      const bool under = v.fuse[q.flat] > 0;
-      const bool under_b = under || v.brick[q.flat];
-      const bool ok = !under && !under_b && (int64_t)q.live < q.bombs_cap;
-      bm[((size_t)e * P + lane) * 2 + 0] = 1;
-      bm[((size_t)e * P + lane) * 2 + 1] = q.alive ? (ok ? 1 : 0) : 1;
-    }
-    __syncwarp();
+    live_counts(v, P, live);
+    observe_env<T>(cfg, v, e, pi, dng, live, g_py, g_px, g_alive != 0, g_inv, g_bcap, g_t, ft,
+                   obs, danger_out, mm, bm);
   }
 }
 
@@ -673,8 +696,7 @@ extern "C" int qqt_observe(const QqtCfg* cfg, const QqtState* st, void* obs, flo
     if (cfg->obs_stride % epc || cfg->obs_stride < cfg->obs_channels * C) return QQT_E_ALIGN;
     if (((uintptr_t)obs) & 15) return QQT_E_ALIGN;
   }
-  const size_t sm = tile_bytes(C) +
-                   QQT_NWARP * obs_layout(C, cfg->obs_stride, cfg->obs_fp32 ? 4 : 2).total;
+  const size_t sm = tile_bytes(C) + QQT_NWARP * obs_layout(C).total;
   const int blocks = (cfg->n_envs + QQT_TILE_E - 1) / QQT_TILE_E;
   if (cfg->obs_fp32) {
     cudaFuncSetAttribute(k_observe<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);

@@ -29,7 +29,7 @@ struct PShared {
 
 // Per-warp scratch layout (byte offsets, 16-byte aligned sections).
 struct StepLayout {
-  size_t cov, trig, list, list2, qmask, cur, bombs, ps, total;
+  size_t cov, trig, list, list2, qmask, cur, bombs, ps, pinfo, dng, total;
 };
 
 __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
@@ -44,7 +44,9 @@ __host__ __device__ inline StepLayout step_layout(int cells) {
   L.cur = align16(L.qmask + ((size_t)(cells + 31) / 32 + 1) * 4);
   L.bombs = align16(L.cur + (size_t)cells * 12);   // cur, front, spread
   L.ps = align16(L.bombs + (size_t)cells * 2);
-  L.total = align16(L.ps + QQT_MAX_P * sizeof(PShared));
+  L.pinfo = align16(L.ps + QQT_MAX_P * sizeof(PShared));
+  L.dng = align16(L.pinfo + QQT_MAX_P * sizeof(PInfo));
+  L.total = align16(L.dng + (size_t)cells * 4);
   return L;
 }
 
@@ -64,6 +66,11 @@ struct StepParams {
   int has_tmpl;
   int phase;
   uint8_t* placed_buf;   // [P][N]
+  // optional fused observation of the post-step state (the next tick's
+  // input): fp16 rows [N][obs_stride], masks [N][P][5] / [N][P][2]
+  __half* obs;
+  uint8_t* mm;
+  uint8_t* bm;
 };
 
 __device__ __forceinline__ bool placed_map_at(const PShared* ps, int P, int cell) {
@@ -75,6 +82,7 @@ __device__ __forceinline__ bool placed_map_at(const PShared* ps, int P, int cell
 
 __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
   extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ FuseTables ft;
   const QqtCfg& cfg = a.cfg;
   const QqtState& st = a.st;
   const int h = cfg.height, w = cfg.width, C = h * w, N = cfg.n_envs, P = cfg.n_players;
@@ -97,6 +105,9 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
   ds.spread = ds.front + C;
   ds.bombs = (uint16_t*)(wb + L.bombs);
   PShared* ps = (PShared*)(wb + L.ps);
+  PInfo* pinfo = (PInfo*)(wb + L.pinfo);
+  float* dng = (float*)(wb + L.dng);
+  if (a.obs) fuse_tables(ft, a.cfg.fuse_f);
   const int tiers = a.phase == PHASE_PLACE ? 0 : *a.tiers;
   const float INF = __int_as_float(0x7f800000);
 
@@ -379,6 +390,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
     //      exploded bombs are cleared, and the bombs left are compacted for
     //      the danger-standing penalty below
     int nb_post = 0;
+    int post_cnt[QQT_MAX_P] = {0, 0, 0, 0};
     for (int base = 0; base < C; base += 32) {
       const int c = base + lane;
       bool bomb = false;
@@ -393,6 +405,8 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
           v.blast[c] = 0;
         }
         bomb = v.fuse[c] > 0;
+        const int o = v.owner[c];
+        if (bomb && o >= 0 && o < P) post_cnt[o]++;
       }
       const unsigned m = __ballot_sync(QQT_FULL, bomb);
       if (bomb) ds.bombs[nb_post + __popc(m & ((1u << lane) - 1u))] = (uint16_t)c;
@@ -568,6 +582,19 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
       }
       t_out = 0;
     }
+    // ---- fused observation of the post-step (or reset) state: the next
+    //      tick's observation row and legal masks (sim/obs.py:25-229).  The
+    //      danger map reuses the danger-standing stage A (same planes); an
+    //      env reset to its template has no bombs.
+    if (a.obs) {
+      const bool reset = done && a.has_tmpl;
+      danger_paint(v, ds, reset ? 0 : nb_post, cfg.blast, dng);
+      int live[QQT_MAX_P];
+#pragma unroll
+      for (int q = 0; q < QQT_MAX_P; ++q) live[q] = reset ? 0 : warp_sum(post_cnt[q]);
+      observe_env<__half>(cfg, v, e, pinfo, dng, live, me.y, me.x, alive != 0, me.invuln,
+                          me.bombs_cap, t_out, ft, a.obs, nullptr, a.mm, a.bm);
+    }
     if (p < P) {
       const size_t i = (size_t)p * N + e;
       st.pos[((size_t)p * 2) * N + e] = me.y;
@@ -692,16 +719,19 @@ extern "C" uint64_t qqt_step_scratch_bytes(const QqtCfg* cfg) {
   return ((uint64_t)cfg->n_players * cfg->n_envs + 255) / 256 * 256;
 }
 
-extern "C" int qqt_step(const QqtCfg* cfg, const QqtState* st, const int64_t* actions,
-                        const float* rb_hit, const float* rb_grow, int32_t* tiers,
-                        int32_t first_step, const QqtStepOut* out, const QqtTemplate* tmpl,
-                        void* scratch, qqt_stream_t stream) {
+static int launch_step(const QqtCfg* cfg, const QqtState* st, const int64_t* actions,
+                       const float* rb_hit, const float* rb_grow, int32_t* tiers,
+                       int32_t first_step, const QqtStepOut* out, const QqtTemplate* tmpl,
+                       void* scratch, void* obs, uint8_t* mm, uint8_t* bm, qqt_stream_t stream) {
   int rc = check_cfg(cfg);
   if (rc) return rc;
   if (!st || !actions || !tiers || !scratch) return QQT_E_ARG;
   if (cfg->corridor && (!rb_hit || !rb_grow)) return QQT_E_ARG;
   if (tmpl && (!tmpl->wall || !tmpl->brick || !tmpl->spawn || !tmpl->bombs_cap ||
                !tmpl->blast_cap || !tmpl->spd || !tmpl->crate_prob || !tmpl->episode))
+    return QQT_E_ARG;
+  if (obs && (!mm || !bm || cfg->obs_fp32 || cfg->obs_stride < cfg->obs_channels * cfg->height *
+                                                                   cfg->width))
     return QQT_E_ARG;
   StepParams p;
   p.cfg = *cfg;
@@ -723,6 +753,9 @@ extern "C" int qqt_step(const QqtCfg* cfg, const QqtState* st, const int64_t* ac
     p.has_tmpl = 0;
   }
   p.placed_buf = (uint8_t*)scratch;
+  p.obs = (__half*)obs;
+  p.mm = mm;
+  p.bm = bm;
   const int C = cfg->height * cfg->width;
   const size_t sm = tile_bytes(C) + QQT_NWARP * step_warp_bytes(C);
   cudaFuncSetAttribute(k_step, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
@@ -739,6 +772,25 @@ extern "C" int qqt_step(const QqtCfg* cfg, const QqtState* st, const int64_t* ac
     k_step<<<blocks, QQT_NWARP * 32, sm, s>>>(p);
   }
   return launch_status();
+}
+
+extern "C" int qqt_step(const QqtCfg* cfg, const QqtState* st, const int64_t* actions,
+                        const float* rb_hit, const float* rb_grow, int32_t* tiers,
+                        int32_t first_step, const QqtStepOut* out, const QqtTemplate* tmpl,
+                        void* scratch, qqt_stream_t stream) {
+  return launch_step(cfg, st, actions, rb_hit, rb_grow, tiers, first_step, out, tmpl, scratch,
+                     nullptr, nullptr, nullptr, stream);
+}
+
+extern "C" int qqt_step_observe(const QqtCfg* cfg, const QqtState* st, const int64_t* actions,
+                                const float* rb_hit, const float* rb_grow, int32_t* tiers,
+                                int32_t first_step, const QqtStepOut* out, const QqtTemplate* tmpl,
+                                void* scratch, void* obs, uint8_t* mm, uint8_t* bm,
+                                qqt_stream_t stream) {
+  if (!obs || !mm || !bm) return QQT_E_ARG;
+  if (((uintptr_t)obs & 15) || (cfg && (cfg->obs_stride % 8))) return QQT_E_ALIGN;
+  return launch_step(cfg, st, actions, rb_hit, rb_grow, tiers, first_step, out, tmpl, scratch,
+                     obs, mm, bm, stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -72,6 +72,8 @@ def lib():
         sig = {
             "qqt_step": (c_i32, [P(QqtCfg), P(QqtState), c_p, c_p, c_p, c_p, c_i32,
                                  P(QqtStepOut), P(QqtTemplate), c_p, c_p]),
+            "qqt_step_observe": (c_i32, [P(QqtCfg), P(QqtState), c_p, c_p, c_p, c_p, c_i32,
+                                 P(QqtStepOut), P(QqtTemplate), c_p, c_p, c_p, c_p, c_p]),
             "qqt_step_scratch_bytes": (c_u64, [P(QqtCfg)]),
             "qqt_step_noalloc": (c_i32, [P(QqtCfg), P(QqtState), c_p, c_p, c_p, c_p, c_i32,
                                          P(QqtStepOut), P(QqtTemplate), c_p]),

@@ -6,7 +6,10 @@ opponent act -> step(auto_reset) -> crate recycling every 16 ticks.  Every
 kernel writes straight into its row of a device-resident rollout buffer
 (observation rows, masks, actions, log-probs, values, rewards, done flags),
 so a tick moves no data besides what the kernels themselves read and write,
-and the whole T-tick rollout can be captured into one CUDA graph.
+and the whole T-tick rollout can be captured into one CUDA graph.  The step
+kernel also writes the next tick's observation and masks (qqt_step_observe),
+except before a crate recycling, which changes the board after the step:
+the tick after it (and the first tick of a rollout) observes on its own.
 
 Random draws for a rollout (learner sampling uniforms, bot noise, the astar
 mode-ticker integers, crate-pickup uniforms) are inputs in `RolloutDraws`;
@@ -102,11 +105,17 @@ class Rollout:
         self.side = torch.cuda.Stream(sim.device) if opponent is not None else None
         self.draws = RolloutDraws.empty(T, sim.num_envs, self.p, len(self.seats), sim.device)
         self.graph = None
+        # the fused observation writes fp16 rows with the engine's stride
+        self.fuse_observe = bool(sim.cfg.obs_fp16) and sim.obs_stride % 8 == 0
+        self._ready = -1      # tick whose observation the last step already wrote
 
     def tick(self, t: int) -> None:
         sim, buf, dr = self.sim, self.buf, self.draws
         b = t % self.slots
-        obs, mm, bm = sim.observe_and_mask(buf.obs_rows[b], buf.mm[b], buf.bm[b], danger=False)
+        if self._ready == t:
+            obs, mm, bm = buf.obs(b), buf.mm[b], buf.bm[b]
+        else:
+            obs, mm, bm = sim.observe_and_mask(buf.obs_rows[b], buf.mm[b], buf.bm[b], danger=False)
         acts = buf.act[b]
         main = torch.cuda.current_stream(sim.device)
         if self.side is not None:
@@ -125,10 +134,16 @@ class Rollout:
             self.feed_opponent(t)
             bot.act(obs, mm[:, o], bm[:, o], o, out=acts[:, o])
             main.wait_stream(self.side)
+        flush = bool(self.flush_every) and t % self.flush_every == self.flush_every - 1
+        nxt = None
+        if self.fuse_observe and not flush and t + 1 < self.T:
+            b1 = (t + 1) % self.slots
+            nxt = (buf.obs_rows[b1], buf.mm[b1], buf.bm[b1])
         sim.step(acts, auto_reset=True, crate_draws=(dr.crate[t, 0], dr.crate[t, 1]),
                  reward_out=buf.rew[b], done_out=buf.done[b], hit_out=buf.dmg[b],
-                 info_planes=False)
-        if self.flush_every and t % self.flush_every == self.flush_every - 1:
+                 info_planes=False, next_obs=nxt)
+        self._ready = t + 1 if nxt is not None else -1
+        if flush:
             sim.flush_recycle()
 
     def feed_opponent(self, t: int) -> None:

@@ -477,7 +477,7 @@ class B200Sim:
         return r[:, 0, :].t().contiguous(), r[:, 1, :].t().contiguous()
 
     def step(self, actions: torch.Tensor, auto_reset: bool = True, crate_draws=None,
-             hit_out: torch.Tensor | None = None,
+             hit_out: torch.Tensor | None = None, next_obs=None,
              reward_out: torch.Tensor | None = None, done_out: torch.Tensor | None = None,
              info_planes: bool = True):
         """One tick (sim/torch_sim.py:895-1261) -> (reward (N,P), done (N,), info).
@@ -518,13 +518,30 @@ class B200Sim:
             rb_hit = rb_hit.to(self.device, torch.float32).contiguous()
             rb_grow = rb_grow.to(self.device, torch.float32).contiguous()
         dev_reset = auto_reset and self._tmpl is not None
-        rc = capi.lib().qqt_step(ctypes.byref(self._ccfg), ctypes.byref(self._cstate),
-                                 acts.data_ptr(), capi.ptr(rb_hit), capi.ptr(rb_grow),
-                                 self._tiers.data_ptr(), int(self._first_step),
-                                 ctypes.byref(cout),
-                                 ctypes.byref(self._tmpl) if dev_reset else None,
-                                 self._step_scratch.data_ptr(), self._stream())
-        capi.check(rc, "qqt_step")
+        if next_obs is not None:
+            if auto_reset and not dev_reset:
+                raise ValueError("next_obs needs the device auto-reset (a template) or no reset")
+            rows, nmm, nbm = next_obs
+            if rows.dtype != torch.float16 or rows.stride(1) != 1 or rows.stride(0) != self.obs_stride:
+                raise ValueError("next_obs rows must be fp16 with the engine's row stride")
+            for m in (nmm, nbm):
+                if m.dtype != torch.bool or not m.is_contiguous():
+                    raise ValueError("next_obs masks must be contiguous bool tensors")
+            rc = capi.lib().qqt_step_observe(
+                ctypes.byref(self._ccfg), ctypes.byref(self._cstate), acts.data_ptr(),
+                capi.ptr(rb_hit), capi.ptr(rb_grow), self._tiers.data_ptr(), int(self._first_step),
+                ctypes.byref(cout), ctypes.byref(self._tmpl) if dev_reset else None,
+                self._step_scratch.data_ptr(), rows.data_ptr(), nmm.data_ptr(), nbm.data_ptr(),
+                self._stream())
+            capi.check(rc, "qqt_step_observe")
+        else:
+            rc = capi.lib().qqt_step(ctypes.byref(self._ccfg), ctypes.byref(self._cstate),
+                                     acts.data_ptr(), capi.ptr(rb_hit), capi.ptr(rb_grow),
+                                     self._tiers.data_ptr(), int(self._first_step),
+                                     ctypes.byref(cout),
+                                     ctypes.byref(self._tmpl) if dev_reset else None,
+                                     self._step_scratch.data_ptr(), self._stream())
+            capi.check(rc, "qqt_step")
         self._first_step = False
         n, h, w = self.num_envs, self.cfg.height, self.cfg.width
         info = {"n_alive": self._n_alive, "died": self._died, "winner": self._winner, "hit": hit,

@@ -190,3 +190,37 @@ def test_groups_equal_sequential_groups():
         got = _buffers(m[4])
         for k in got:
             assert torch.equal(seq[g][k], got[k]), f"group {g}: {k}"
+
+
+def test_step_observe_equals_step_then_observe():
+    """qqt_step_observe's rows and masks equal observe_and_mask of the
+    post-step state, for envs that continue and envs that time out and are
+    reset to their template on the device."""
+    n, T = 96, 40
+    cfg, sim, pol, bot, ro = _make(n, T, seed=31)
+    for t in range(24):                       # mid-game: bombs, flames, crates
+        ro.tick(t)
+    st = sim.numpy_state()
+    st["t"][::2] = cfg.max_steps - 1          # every other env ends on this step
+    sim.load_numpy_state({"t": st["t"]})
+    acts = ro.buf.act[23].clone()
+    draws = (ro.draws.crate[23, 0], ro.draws.crate[23, 1])
+    snap = _snapshot(sim, bot)
+    rows = torch.zeros_like(ro.buf.obs_rows[0])
+    mm = torch.zeros_like(ro.buf.mm[0])
+    bm = torch.zeros_like(ro.buf.bm[0])
+    _, done_f, _ = sim.step(acts, auto_reset=True, crate_draws=draws, next_obs=(rows, mm, bm))
+    fused_state = sim.numpy_state()
+    done_f = done_f.clone()
+    _restore(sim, bot, snap)
+    _, done_s, _ = sim.step(acts, auto_reset=True, crate_draws=draws)
+    ref_rows = torch.zeros_like(rows)
+    ref_mm, ref_bm = torch.zeros_like(mm), torch.zeros_like(bm)
+    sim.observe_and_mask(ref_rows, ref_mm, ref_bm, danger=False)
+    torch.cuda.synchronize()
+    assert bool(done_f[::2].all()) and torch.equal(done_f, done_s)
+    got = sim.numpy_state()
+    for k in fused_state:
+        assert np.array_equal(fused_state[k], got[k]), f"state {k}"
+    assert torch.equal(rows.view(torch.int16), ref_rows.view(torch.int16)), "observation rows"
+    assert torch.equal(mm, ref_mm) and torch.equal(bm, ref_bm), "legal masks"
