@@ -329,14 +329,12 @@ __device__ bool relax_two_reg(float* d0, float* d1, const float* cost, int max_p
   float* dd = f ? d1 : d0;
   const bool row_lane = i < H, col_lane = i < W;
   float v[W > H ? W : H];                // a row (row phases) or a column (column phases)
-  float cr[W], cc[H];
+  float cr[W];                           // this lane's cost row; columns come from shared memory
 #pragma unroll
   for (int c = 0; c < W; ++c) {
     v[c] = row_lane ? dd[i * W + c] : INF;
     cr[c] = row_lane ? cost[i * W + c] : INF;
   }
-#pragma unroll
-  for (int r = 0; r < H; ++r) cc[r] = col_lane ? cost[r * W + i] : INF;
   bool rows = true, done = false;
   for (int ph = 0; ph < max_phases; ++ph) {
     bool ch = false;
@@ -376,12 +374,13 @@ __device__ bool relax_two_reg(float* d0, float* d1, const float* cost, int max_p
         if (i >= W - 1) rt[r] = INF;
         lf[r] = fminf(lf[r], rt[r]);
       }
+      const float* ccol = cost + (col_lane ? i : 0);
 #pragma unroll
       for (int r = 0; r < H; ++r) {
         float m = lf[r];
         if (r > 0) m = fminf(m, v[r - 1]);
         if (r < H - 1) m = fminf(m, v[r + 1]);
-        const float nd = __fadd_rn(m, cc[r]);
+        const float nd = __fadd_rn(m, col_lane ? ccol[r * W] : INF);
         if (nd < v[r]) { v[r] = nd; ch = true; }
       }
 #pragma unroll
@@ -389,7 +388,7 @@ __device__ bool relax_two_reg(float* d0, float* d1, const float* cost, int max_p
         float m = lf[r];
         if (r > 0) m = fminf(m, v[r - 1]);
         if (r < H - 1) m = fminf(m, v[r + 1]);
-        const float nd = __fadd_rn(m, cc[r]);
+        const float nd = __fadd_rn(m, col_lane ? ccol[r * W] : INF);
         if (nd < v[r]) { v[r] = nd; ch = true; }
       }
     }
@@ -426,7 +425,7 @@ __device__ __forceinline__ int argmin5(const float* s) {
   return best;
 }
 
-__global__ void __launch_bounds__(QQT_NWARP * 32)
+__global__ void __launch_bounds__(QQT_NWARP * 32, 3)
 k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const float* noise,
         int64_t* mode_arr, int64_t* timer_arr, int tick16, const int64_t* new_mode,
         const int64_t* new_timer, float* vsafe_out, float* vopp_out, const int* cap_max_ptr) {
