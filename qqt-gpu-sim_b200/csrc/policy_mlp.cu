@@ -380,25 +380,41 @@ __device__ __forceinline__ void tmem_row128(uint32_t taddr, float* x) {
 }
 
 // x += bias; LayerNorm(128) with affine; ReLU (train/model.py:121-153).
+// Parameters come in as float4 vectors; the sums use four independent
+// accumulators (combined in a fixed order).
 __device__ __forceinline__ void bias_ln_relu_row(float* x, const float* __restrict__ bias,
                                                  const float* __restrict__ g,
                                                  const float* __restrict__ b) {
-  float s = 0.f;
+  float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int i = 0; i < 128; ++i) {
-    x[i] = __fadd_rn(x[i], __ldg(bias + i));
-    s += x[i];
+  for (int i = 0; i < 128; i += 4) {
+    const float4 bb = __ldg(reinterpret_cast<const float4*>(bias + i));
+    x[i] = __fadd_rn(x[i], bb.x);
+    x[i + 1] = __fadd_rn(x[i + 1], bb.y);
+    x[i + 2] = __fadd_rn(x[i + 2], bb.z);
+    x[i + 3] = __fadd_rn(x[i + 3], bb.w);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s4[j] += x[i + j];
   }
-  const float mean = s * (1.f / 128.f);
-  float v = 0.f;
+  const float mean = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * (1.f / 128.f);
+  float v4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int i = 0; i < 128; ++i) {
-    const float d = x[i] - mean;
-    v = fmaf(d, d, v);
+  for (int i = 0; i < 128; i += 4)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float d = x[i + j] - mean;
+      v4[j] = fmaf(d, d, v4[j]);
+    }
+  const float rstd = rsqrtf(((v4[0] + v4[1]) + (v4[2] + v4[3])) * (1.f / 128.f) + 1e-5f);
+#pragma unroll
+  for (int i = 0; i < 128; i += 4) {
+    const float4 gg = __ldg(reinterpret_cast<const float4*>(g + i));
+    const float4 be = __ldg(reinterpret_cast<const float4*>(b + i));
+    x[i] = fmaxf(fmaf((x[i] - mean) * rstd, gg.x, be.x), 0.f);
+    x[i + 1] = fmaxf(fmaf((x[i + 1] - mean) * rstd, gg.y, be.y), 0.f);
+    x[i + 2] = fmaxf(fmaf((x[i + 2] - mean) * rstd, gg.z, be.z), 0.f);
+    x[i + 3] = fmaxf(fmaf((x[i + 3] - mean) * rstd, gg.w, be.w), 0.f);
   }
-  const float rstd = rsqrtf(v * (1.f / 128.f) + 1e-5f);
-#pragma unroll
-  for (int i = 0; i < 128; ++i) x[i] = fmaxf(fmaf((x[i] - mean) * rstd, __ldg(g + i), __ldg(b + i)), 0.f);
 }
 
 // Row r of the activation operand: fp16 hi and lo images, 16-byte stores.
@@ -486,6 +502,9 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer (layer 1)
     int issued_until = 0;
+    // CTAs start at different K tiles so that at any time they read
+    // different lines of the shared weight stream from L2
+    const int k0 = (int)(((unsigned)blockIdx.x * 7u) % (unsigned)k_tiles);
     for (int kt = 0; kt < k_tiles; ++kt) {
       const int s = kt % G::kStages;
       if (kt >= G::kStages) {
@@ -496,11 +515,12 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
       }
       if (*abort_flag) break;
       uint8_t* st = smem + s * G::kStageBytes;
+      const int kx = ((kt + k0) % k_tiles) * kBK;
       mbar_expect_tx(&full[s], G::kStageBytes);
-      tma_load_2d(&tm_a, &full[s], st, kt * kBK, m0);
-      if (SPLIT_A) tma_load_2d(&tm_alo, &full[s], st + G::kABytes, kt * kBK, m0);
-      tma_load_2d(&tm_b, &full[s], st + G::kAAll, kt * kBK, 0);
-      tma_load_2d(&tm_b, &full[s], st + G::kAAll + G::kBBytes, kt * kBK, NT);
+      tma_load_2d(&tm_a, &full[s], st, kx, m0);
+      if (SPLIT_A) tma_load_2d(&tm_alo, &full[s], st + G::kABytes, kx, m0);
+      tma_load_2d(&tm_b, &full[s], st + G::kAAll, kx, 0);
+      tma_load_2d(&tm_b, &full[s], st + G::kAAll + G::kBBytes, kx, NT);
       issued_until = kt + 1;
     }
     // drain: every issued stage must land before the CTA may exit
@@ -615,14 +635,26 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         tmem_ld32(lane_base + G::kColH + 32 * c, h);
         const int head = c >> 1, u0 = (c & 1) * 32;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) h[i] = fmaxf(__fadd_rn(h[i], __ldg(f + F_HB0 + 32 * c + i)), 0.f);
+        for (int i = 0; i < 32; i += 4) {
+          const float4 hb = __ldg(reinterpret_cast<const float4*>(f + F_HB0 + 32 * c + i));
+          h[i] = fmaxf(__fadd_rn(h[i], hb.x), 0.f);
+          h[i + 1] = fmaxf(__fadd_rn(h[i + 1], hb.y), 0.f);
+          h[i + 2] = fmaxf(__fadd_rn(h[i + 2], hb.z), 0.f);
+          h[i + 3] = fmaxf(__fadd_rn(h[i + 3], hb.w), 0.f);
+        }
         const int o_lo = head == 0 ? 0 : (head == 1 ? 5 : 7);
         const int o_hi = head == 0 ? 5 : (head == 1 ? 7 : 8);
 #pragma unroll
         for (int o = 0; o < 8; ++o) {
           if (o < o_lo || o >= o_hi) continue;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) z[o] = fmaf(__ldg(f + F_HW2 + o * 64 + u0 + i), h[i], z[o]);
+          for (int i = 0; i < 32; i += 4) {
+            const float4 wv = __ldg(reinterpret_cast<const float4*>(f + F_HW2 + o * 64 + u0 + i));
+            z[o] = fmaf(wv.x, h[i], z[o]);
+            z[o] = fmaf(wv.y, h[i + 1], z[o]);
+            z[o] = fmaf(wv.z, h[i + 2], z[o]);
+            z[o] = fmaf(wv.w, h[i + 3], z[o]);
+          }
         }
       }
       asm volatile("tcgen05.fence::before_thread_sync;");
