@@ -22,6 +22,8 @@ Outputs (compressed npz, all env-major like the reference tensors):
   traj_cfg4.npz    pillar corridor, self-play MLP (both seats), 64 ticks
   traj_cfg5.npz    pillar corridor, CNN learner vs greedy, 48 ticks
   stress_cfg3.npz  bomb stress: one idle step, danger/obs/masks, V fields
+  ckpt_adapt.npz   adapt_first_conv on seeded models (2 <-> 3 players), and
+  ref_ckpt_mlp.pt  a checkpoint written by the reference's save_ckpt
 """
 
 from __future__ import annotations
@@ -498,6 +500,53 @@ def ppo_golden(R):
     return out
 
 
+def ckpt_golden(R):
+    """Checkpoint format and first-layer migration (train/train.py:92-158,
+    243-260, 307-331): the reference's adapt_first_conv on seeded random
+    models (3x3 grid, 2 <-> 3 players, mlp and cnn), and one checkpoint
+    written by the reference's own save_ckpt (saved beside this file as
+    ref_ckpt_mlp.pt)."""
+    import argparse as _ap
+    import torch
+    from sim.config import n_obs_channels
+    from train.curriculum import CurriculumState
+    from train.model_pool import ModelPool
+    from train.train import adapt_first_conv, save_ckpt
+    AC = R["ActorCritic"]
+    out = {}
+    seed = 0
+    for arch in ("mlp", "cnn"):
+        for p_old, p_new in ((2, 3), (3, 2)):
+            torch.manual_seed(100 + seed)
+            seed += 1
+            old_shape = (n_obs_channels(p_old), 3, 3)
+            new_shape = (n_obs_channels(p_new), 3, 3)
+            m = AC(old_shape, arch=arch, n_players=p_old)
+            with torch.no_grad():
+                for prm in m.parameters():
+                    prm.normal_(0.0, 0.1)
+            nm = adapt_first_conv(m, new_shape, arch=arch, n_players=p_new)
+            tag = f"{arch}_{p_old}to{p_new}"
+            first = "conv0.weight" if arch == "cnn" else "shared.0.weight"
+            out[f"{tag}__old"] = m.state_dict()[first].numpy().copy()
+            out[f"{tag}__new"] = nm.state_dict()[first].numpy().copy()
+            # every other key is copied through unchanged (same shapes)
+            out[f"{tag}__keys"] = np.array(sorted(nm.state_dict().keys()))
+    # a checkpoint written by the reference itself
+    torch.manual_seed(7)
+    m = AC((14, 3, 3), arch="mlp", n_players=2)
+    with torch.no_grad():
+        for prm in m.parameters():
+            prm.normal_(0.0, 0.1)
+    opt = torch.optim.Adam(m.parameters(), lr=1e-4, eps=1e-5)
+    cs = CurriculumState(stage_idx=2, episodes_in_stage=37, recent_wins=[1.0, 0.0, 0.5])
+    args = _ap.Namespace(num_envs=64, arch="mlp", lr=1e-4)
+    path = os.path.join(HERE, "ref_ckpt_mlp.pt")
+    save_ckpt(path, learner=m, opt=opt, pool=ModelPool(), cstate=cs, global_step=12345,
+              elo=1012.5, args=args, fixed_elo={"astar": 990.0})
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("QQT_REFERENCE_ROOT", "/root/reference"))
@@ -518,6 +567,7 @@ def main():
         "stress_cfg3": lambda: stress(R, SC(**scenarios.CFG1), 48, 5),
         "reset_modes": lambda: reset_modes(R),
         "ppo_update": lambda: ppo_golden(R),
+        "ckpt_adapt": lambda: ckpt_golden(R),
     }
     for name, fn in jobs.items():
         if args.only and name not in args.only.split(","):
