@@ -87,49 +87,64 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle samples every 50 ms while running."""
+    """SM clock and clock-event (throttle) reasons every 10 ms while running,
+    through NVML (nvidia-smi's library); the GPU is found by its PCI bus id,
+    so CUDA_VISIBLE_DEVICES remapping does not matter."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # nvmlClocksEventReason* bits
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+            "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, index):
-        self.index = index
+    def __init__(self, device_index):
+        self.device_index = device_index
         self.rows = []
         self._stop = threading.Event()
         self._t = None
+        self._err = None
+
+    def _handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        try:
+            pr = torch.cuda.get_device_properties(self.device_index)
+            bus = "%08x:%02x:%02x.0" % (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.device_index)
 
     def __enter__(self):
+        try:
+            nv, h = self._handle()
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        except Exception as e:          # no NVML: the line says "unsampled"
+            self._err = repr(e)
+            return self
+
         def run():
             while not self._stop.is_set():
                 try:
-                    out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits"], capture_output=True,
-                                         text=True, timeout=5).stdout.strip()
-                    if out:
-                        self.rows.append([x.strip() for x in out.split(",")])
-                except Exception:
-                    pass
-                self._stop.wait(0.05)
+                    self.rows.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                      nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
+                except Exception as e:
+                    self._err = repr(e)
+                self._stop.wait(0.01)
         self._t = threading.Thread(target=run, daemon=True)
         self._t.start()
         return self
 
     def __exit__(self, *a):
         self._stop.set()
-        self._t.join(timeout=10)
+        if self._t is not None:
+            self._t.join(timeout=10)
 
     def summary(self):
         if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4)
-                          if len(r) > 5 + i and r[5 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(self.rows)}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"],
+                    "error": self._err}
+        reasons = sorted({k for _, r in self.rows for k, bit in self.BITS.items() if r & bit})
+        return {"sm_mhz": statistics.median(m for m, _ in self.rows), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.rows), "source": "nvml, 10 ms"}
 
 
 def _template(cfg, n, seed):
@@ -252,56 +267,40 @@ def build_engine(device, rank, slots=None, groups=1):
     return RolloutGroups(ros), gen
 
 
-def instrumented_kernel_times(ro):
-    """One eager rollout with CUDA events around every library call:
-    per-call launches and mean device duration (ms)."""
+def graph_kernel_times(grp):
+    """Per-call device durations inside the captured rollout: a second graph
+    of the same T-tick rollout (same streams and concurrency) with a pair of
+    external timing events around every engine call, replayed once after the
+    timed region.  Returns name -> (launches per rollout of one group, mean
+    ms per call)."""
     import torch
-    sim, buf, dr = ro.sim, ro.buf, ro.draws
     bot_name = CFG["opponent"] or "bot"
-    times = {k: [] for k in ("observe", "policy", bot_name, "step+observe", "step", "flush")}
+    marks = []
 
-    def timed(name, fn):
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
+    def probe(name, fn):
+        a = torch.cuda.Event(enable_timing=True, external=True)
+        b = torch.cuda.Event(enable_timing=True, external=True)
         a.record()
-        fn()
+        out = fn()
         b.record()
-        times[name].append((a, b))
+        marks.append((bot_name if name == "bot" else name, a, b))
+        return out
 
-    bot, seats = ro.opponent, ro.seats
-    ready = -1
-    for t in range(ro.T):
-        holder = {}
-        b = t % ro.slots
-        if ready == t:
-            obs, mm, bm = buf.obs(b), buf.mm[b], buf.bm[b]
-        else:
-            timed("observe", lambda: holder.update(zip(("obs", "mm", "bm"), sim.observe_and_mask(
-                buf.obs_rows[b], buf.mm[b], buf.bm[b], danger=False))))
-            obs, mm, bm = holder["obs"], holder["mm"], holder["bm"]
-        acts = buf.act[b]
-        timed("policy", lambda: ro.learner.act_seats(
-            obs, [mm[:, s] for s in seats], [bm[:, s] for s in seats], dr.u_net[t],
-            [acts[:, s] for s in seats], buf.logp[b], buf.val[b]))
-        if bot is not None:
-            o = ro.opp_seat
-            ro.feed_opponent(t)
-            timed(bot_name, lambda: bot.act(obs, mm[:, o], bm[:, o], o, out=acts[:, o]))
-        flush = t % 16 == 15
-        nxt = None
-        if ro.fuse_observe and not flush and t + 1 < ro.T:
-            b1 = (t + 1) % ro.slots
-            nxt = (buf.obs_rows[b1], buf.mm[b1], buf.bm[b1])
-        timed("step+observe" if nxt is not None else "step",
-              lambda: sim.step(acts, auto_reset=True, crate_draws=(dr.crate[t, 0], dr.crate[t, 1]),
-                               reward_out=buf.rew[b], done_out=buf.done[b], hit_out=buf.dmg[b],
-                               info_planes=False, next_obs=nxt))
-        ready = t + 1 if nxt is not None else -1
-        if flush:
-            timed("flush", lambda: sim.flush_recycle())
+    for ro in grp.ros:
+        ro.probe = probe
+    try:
+        grp.capture()
+    finally:
+        for ro in grp.ros:
+            ro.probe = None
+    grp.replay()
     torch.cuda.synchronize()
-    return {k: (len(v), sum(a.elapsed_time(b) for a, b in v) / max(1, len(v)))
-            for k, v in times.items()}
+    grp.graph = None
+    times = {}
+    for name, a, b in marks:
+        times.setdefault(name, []).append(a.elapsed_time(b))
+    g = len(grp.ros)
+    return {k: (len(v) // g, sum(v) / len(v)) for k, v in times.items()}
 
 
 def _launches_per_rollout():
@@ -378,7 +377,6 @@ def gpu_bench(args):
         ro.draws.generate(gen)
         ro.tick(0)
     grp.collect()                    # finish a full eager rollout for a warm state
-    kt = instrumented_kernel_times(grp.ros[0])
     n_inst = grp.ros[0].sim.num_envs
     grp.capture()
     pool = [[RolloutDrawsPool.make(ro.draws, gen) for ro in grp.ros]
@@ -444,6 +442,9 @@ def gpu_bench(args):
     e_value = N_ENVS * TICKS * world * args.steps / (float(t_e.item()) / 1e3)
     grp.graph = None
     torch.cuda.synchronize()
+    # per-kernel durations for the roofline: the same rollout graph with
+    # timing events around each call (after the timed regions)
+    kt = graph_kernel_times(grp)
 
     ppo = None
     if CFG["ppo"]:
@@ -472,7 +473,8 @@ def gpu_bench(args):
         dom = max((k for k in per if k != "flush"), key=lambda k: per[k]["share"])
         d = per[dom]
         achieved = d["alg_bytes_per_launch"] / (d["mean_ms"] / 1e3) / 1e9
-        traffic = _ncu_traffic(dom) if args.config == "cfg2" else None
+        # ncu traffic was captured for the default cfg2 shard (2 groups of 2816 envs)
+        traffic = _ncu_traffic(dom) if args.config == "cfg2" and n_inst == 2816 else None
         cores = args.cpu_procs
         cpu_v, cpu_steps, cpu_dt = cpu_leg(args.cpu_envs, args.cpu_ticks, cores, conf=args.config)
         out = {
@@ -737,7 +739,7 @@ def main():
     os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))

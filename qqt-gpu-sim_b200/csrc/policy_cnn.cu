@@ -550,16 +550,6 @@ extern "C" uint64_t qqt_cnn_work_bytes(int32_t n_envs, int32_t n_seats) {
   return (uint64_t)n_seats * 2 * (uint64_t)n_envs * kCnnKP * 2;
 }
 
-static int sm_count() {
-  static int n = 0;
-  if (!n) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
-      n = 148;
-  }
-  return n;
-}
 
 extern "C" int qqt_cnn_act(const void* pack, const void* obs, int32_t n_envs, int32_t obs_stride,
                            int32_t height, int32_t width, int32_t channels, int32_t n_seats,
@@ -590,8 +580,6 @@ extern "C" int qqt_cnn_act(const void* pack, const void* obs, int32_t n_envs, in
   if (!make_map(&mb, mp + M.b_off, (uint64_t)M.kp, (uint64_t)2 * M.nt, (uint64_t)M.kp * 2,
                 (uint32_t)M.nt))
     return QQT_E_ARG;
-  cudaFuncSetAttribute(k_mlp_fused<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       FusedCfg<128, true>::kSmem);
   for (int s = 0; s < n_seats; ++s) {
     const __half* ahi = out + (size_t)s * 2 * n_envs * kCnnKP;
     const __half* alo = ahi + (size_t)n_envs * kCnnKP;
@@ -605,9 +593,11 @@ extern "C" int qqt_cnn_act(const void* pack, const void* obs, int32_t n_envs, in
     io.act[0] = act[s];
     io.mm[1] = io.bm[1] = nullptr;
     io.act[1] = nullptr;
-    k_mlp_fused<128, true><<<(n_envs + kBM - 1) / kBM, 192, FusedCfg<128, true>::kSmem, st>>>(
-        ma, malo, mb, n_envs, M.kp / kBK, (const float*)(mp + M.f_off), mp + M.img_off, io, s,
-        mm_stride, bm_stride, u, act_stride, logp, value, logits);
+    const int rc = launch_mlp_fused<128, true>(ma, malo, mb, n_envs, M.kp / kBK,
+                                               (const float*)(mp + M.f_off), mp + M.img_off, io,
+                                               s, mm_stride, bm_stride, u, act_stride, logp,
+                                               value, logits, st);
+    if (rc != QQT_OK) return rc;
   }
   return launch_status();
 }

@@ -1,30 +1,43 @@
 // MLP policy on the 5th-generation tensor cores, one fused kernel per 128
 // env rows (train/model.py:121-153, 167-245).
 //
-// k_mlp_fused<NT>  (one CTA per 128 envs, 192 threads, NT = 128 x seats)
-//   layer 1  warp 0 lane 0 streams K tiles with TMA: A = obs tile [128 x 64]
-//            fp16, B = packed W0 (fp16 hi and lo halves of the seat-permuted
-//            fp32 weights) [NT x 64]; warp 1 lane 0 issues tcgen05.mma
-//            kind::f16 M=128 N=NT, two per K=16 step (A*Bhi + A*Blo) into an
-//            fp32 TMEM accumulator; obs values are exact in fp16 and the
-//            hi/lo split keeps W0's float32 precision.
-//   tail     the pipeline's shared memory is reused: one bulk copy brings
-//            the pre-swizzled fp16 hi/lo images of shared.3 (128x128) and the
-//            three head hidden layers (192x128).  Warps 2-5 own one row per
-//            thread: tcgen05.ld the row, +bias, LayerNorm, ReLU, split the
-//            row into fp16 hi/lo and store it as the next MMA's A operand
-//            (128-byte swizzled K-major).  Each of the two remaining layers
-//            is 8 K steps x 3 MMAs (Ahi*Whi + Ahi*Wlo + Alo*Whi), which keeps
-//            the products at float32 accuracy.  The 192 head units come
-//            back from TMEM, the output layers (5 move, 2 bomb, 1 value) are
-//            per-thread dot products, then masking with float32's lowest
-//            value, inverse-CDF sampling and the log-probability.
+// k_mlp_fused<NT>  (a cluster of ks CTAs per 128 envs, 576 threads each,
+//                   NT = 128 x seats)
+//   layer 1  split along K over the cluster: in CTA rank c, warp 0 lane 0
+//            streams that rank's K tiles with TMA (no multicast): A = obs
+//            tile [128 x 64] fp16, B = packed W0 (fp16 hi and lo halves of
+//            the seat-permuted fp32 weights) [NT x 64]; warp 1 lane 0 issues
+//            tcgen05.mma kind::f16 M=128 N=NT, two per K=16 step (A*Bhi +
+//            A*Blo) into an fp32 TMEM accumulator; obs values are exact in
+//            fp16 and the hi/lo split keeps W0's float32 precision.  Ranks
+//            1..ks-1 copy their partial sums into their own shared memory
+//            and arrive on an mbarrier of rank 0, whose epilogue adds them
+//            in rank order (distributed shared memory reads).  The per-SM
+//            TMA stream is what bounds layer 1, so the split divides it.
+//   tail     (rank 0) the pipeline's shared memory is reused: one bulk copy
+//            brings the pre-swizzled fp16 hi/lo images of shared.3
+//            (128x128) and the three head hidden layers (192x128).  16
+//            epilogue warps give each row four threads (TMEM lane quadrant
+//            x column quarter): tcgen05.ld the quarter, +bias, LayerNorm
+//            (the row sums cross the four threads through scratch columns
+//            of the row's own TMEM lane), ReLU, split into fp16 hi/lo and
+//            store it as the next MMA's A operand (128-byte swizzled
+//            K-major).  Each of the two remaining layers is 8 K steps x 3
+//            MMAs (Ahi*Whi + Ahi*Wlo + Alo*Whi), which keeps the products at
+//            float32 accuracy.  Each thread takes 48 of the 192 head units
+//            and forms partial output logits (5 move, 2 bomb, 1 value); the
+//            first quarter's thread sums the four, masks with float32's
+//            lowest value, samples by inverse CDF and writes the
+//            log-probability and value.
 // The CNN policy (policy_cnn.cu) reuses this kernel with SPLIT_A for its
 // Linear(1352 -> 128) and the same tail.
 //
 // Every mbarrier wait is bounded; on expiry the CTA raises QQT_DEV_TIMEOUT,
 // waits (bounded) for the copies and MMAs it issued, frees its TMEM and
-// returns.
+// returns.  Branch decisions after a wait are made uniform over the epilogue
+// warps (barrier with an AND reduction), and every thread reaches the
+// closing cluster barrier, so no CTA leaves while another reads its shared
+// memory.
 
 #include <cuda.h>
 
@@ -365,30 +378,174 @@ struct FusedCfg {
   static constexpr int kTailBytes = kAct + 2 * kActBytes;
   static constexpr int kRegion = kPipeBytes > kTailBytes ? kPipeBytes : kTailBytes;
   static constexpr int kSmem = kRegion + 1024 /*align*/ + 256 /*barriers*/;
-  static constexpr uint32_t kTmemCols = 512;
+  // split-K partial sums of a non-leader CTA: [seat][128 rows][128] fp32 at
+  // the start of its (drained) pipeline region
+  static constexpr int kPartBytes = (NT / 128) * kBM * 128 * 4;
+  static constexpr uint32_t kTmemCols = 512;            // leader
   static constexpr uint32_t kColH = NT;                 // head hidden accumulator (192 cols)
+  static constexpr uint32_t kColScr = NT + 192;         // row-exchange scratch (48 cols)
 };
 static_assert(FusedCfg<128>::kSmem <= 232448 && FusedCfg<256>::kSmem <= 232448 &&
                   FusedCfg<128, true>::kSmem <= 232448,
               "fused MLP shared memory over the per-CTA limit");
-static_assert(FusedCfg<256>::kColH + 192 <= FusedCfg<256>::kTmemCols, "TMEM columns");
+static_assert(FusedCfg<256>::kColScr + 48 <= FusedCfg<256>::kTmemCols &&
+                  FusedCfg<128>::kColScr + 48 <= FusedCfg<128>::kTmemCols,
+              "TMEM columns");
+static_assert(FusedCfg<128>::kPartBytes <= FusedCfg<128>::kPipeBytes &&
+                  FusedCfg<256>::kPartBytes <= FusedCfg<256>::kPipeBytes &&
+                  FusedCfg<128, true>::kPartBytes <= FusedCfg<128, true>::kPipeBytes,
+              "split-K partials fit the pipeline region");
 
-// One epilogue thread's row: TMEM columns [col, col + 128) -> x.
-__device__ __forceinline__ void tmem_row128(uint32_t taddr, float* x) {
+// Block: warp 0 TMA producer, warp 1 MMA issuer, 16 epilogue warps.  Epilogue
+// warp e = warp - 2 owns TMEM lane quadrant warp % 4 (32 rows) and column
+// quarter e / 4 (32 of a layer's 128 columns): four threads per row.
+constexpr int kEpiWarps = 16;
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kMlpThreads = 64 + kEpiThreads;
+constexpr int kMaxSplitK = 8;
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-  for (int c = 0; c < 4; ++c) tmem_ld32(taddr + 32 * c, x + 32 * c);
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// x += bias; LayerNorm(128) with affine; ReLU (train/model.py:121-153).
-// Parameters come in as float4 vectors; the sums use four independent
-// accumulators (combined in a fixed order).
-__device__ __forceinline__ void bias_ln_relu_row(float* x, const float* __restrict__ bias,
-                                                 const float* __restrict__ g,
-                                                 const float* __restrict__ b) {
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, float* v) {
+  uint32_t r[4];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st1(uint32_t taddr, float v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr),
+               "r"(__float_as_uint(v))
+               : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const float* v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(
+                   taddr),
+               "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+               "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+               "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
+               : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Barrier of the 16 epilogue warps (named barrier 1).
+__device__ __forceinline__ void epi_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+}
+
+// Barrier of the 16 epilogue warps that also ANDs a flag over them, so that
+// every epilogue warp takes the same branch after a bounded wait.
+__device__ __forceinline__ bool epi_and(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "n"(kEpiThreads)
+      : "memory");
+  return r != 0;
+}
+
+// The four values of a row (one per column quarter, four warps) through the
+// row's TMEM lane: each thread writes its value into column scr + quarter,
+// then, after the epilogue barrier, reads all four.
+__device__ __forceinline__ void row_exchange4(uint32_t scr, int quarter, float v, float* p) {
+  tmem_st1(scr + quarter, v);
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  epi_sync();
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  tmem_ld4(scr, p);
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_size() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
+// Address of the same shared-memory offset in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t dsmem_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar)
+               : "memory");
+}
+// Bounded wait with cluster-scope acquire (arrivals from other CTAs).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  flag_error(QQT_DEV_TIMEOUT);
+  return false;
+}
+
+// Byte offset of float4 chunk c (of 32) of row r in a [128][128] fp32
+// partial-sum block; the chunk index is XOR-swizzled by the row so that a
+// warp's 32 rows hit distinct bank groups.
+__device__ __forceinline__ uint32_t part_off(int r, int c) {
+  return (uint32_t)(r * 512 + ((c ^ (r & 31)) << 4));
+}
+
+// x[32] (+bias) -> LayerNorm over the row's 128 columns (this thread holds
+// columns 32q..32q+31; the sums go through the TMEM row exchange) -> affine
+// -> ReLU (train/model.py:121-153).
+__device__ __forceinline__ void bias_ln_relu_quarter(float* x, int q, uint32_t scr,
+                                                     const float* __restrict__ bias,
+                                                     const float* __restrict__ g,
+                                                     const float* __restrict__ b) {
+  const int c0 = 32 * q;
   float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int i = 0; i < 128; i += 4) {
-    const float4 bb = __ldg(reinterpret_cast<const float4*>(bias + i));
+  for (int i = 0; i < 32; i += 4) {
+    const float4 bb = __ldg(reinterpret_cast<const float4*>(bias + c0 + i));
     x[i] = __fadd_rn(x[i], bb.x);
     x[i + 1] = __fadd_rn(x[i + 1], bb.y);
     x[i + 2] = __fadd_rn(x[i + 2], bb.z);
@@ -396,20 +553,23 @@ __device__ __forceinline__ void bias_ln_relu_row(float* x, const float* __restri
 #pragma unroll
     for (int j = 0; j < 4; ++j) s4[j] += x[i + j];
   }
-  const float mean = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * (1.f / 128.f);
+  float p[4];
+  row_exchange4(scr, q, (s4[0] + s4[1]) + (s4[2] + s4[3]), p);
+  const float mean = ((p[0] + p[1]) + (p[2] + p[3])) * (1.f / 128.f);
   float v4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int i = 0; i < 128; i += 4)
+  for (int i = 0; i < 32; i += 4)
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float d = x[i + j] - mean;
       v4[j] = fmaf(d, d, v4[j]);
     }
-  const float rstd = rsqrtf(((v4[0] + v4[1]) + (v4[2] + v4[3])) * (1.f / 128.f) + 1e-5f);
+  row_exchange4(scr + 4, q, (v4[0] + v4[1]) + (v4[2] + v4[3]), p);
+  const float rstd = rsqrtf(((p[0] + p[1]) + (p[2] + p[3])) * (1.f / 128.f) + 1e-5f);
 #pragma unroll
-  for (int i = 0; i < 128; i += 4) {
-    const float4 gg = __ldg(reinterpret_cast<const float4*>(g + i));
-    const float4 be = __ldg(reinterpret_cast<const float4*>(b + i));
+  for (int i = 0; i < 32; i += 4) {
+    const float4 gg = __ldg(reinterpret_cast<const float4*>(g + c0 + i));
+    const float4 be = __ldg(reinterpret_cast<const float4*>(b + c0 + i));
     x[i] = fmaxf(fmaf((x[i] - mean) * rstd, gg.x, be.x), 0.f);
     x[i + 1] = fmaxf(fmaf((x[i + 1] - mean) * rstd, gg.y, be.y), 0.f);
     x[i + 2] = fmaxf(fmaf((x[i + 2] - mean) * rstd, gg.z, be.z), 0.f);
@@ -417,10 +577,12 @@ __device__ __forceinline__ void bias_ln_relu_row(float* x, const float* __restri
   }
 }
 
-// Row r of the activation operand: fp16 hi and lo images, 16-byte stores.
-__device__ __forceinline__ void store_split_row(const float* x, uint8_t* a_hi, uint8_t* a_lo, int r) {
+// Columns 32q..32q+31 of row r of the activation operand: fp16 hi and lo
+// images, 16-byte stores.
+__device__ __forceinline__ void store_split_quarter(const float* x, uint8_t* a_hi, uint8_t* a_lo,
+                                                    int r, int q) {
 #pragma unroll
-  for (int c = 0; c < 16; ++c) {
+  for (int c = 0; c < 4; ++c) {
     uint32_t hv[4], lv[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -431,7 +593,7 @@ __device__ __forceinline__ void store_split_row(const float* x, uint8_t* a_hi, u
       hv[j] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
       lv[j] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
     }
-    const uint32_t off = sw128_off(r, 8 * c, kBM);
+    const uint32_t off = sw128_off(r, 32 * q + 8 * c, kBM);
     *reinterpret_cast<uint4*>(a_hi + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
     *reinterpret_cast<uint4*>(a_lo + off) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
   }
@@ -453,8 +615,14 @@ __device__ __forceinline__ void umma_split_k128(uint32_t d_tmem, const uint8_t* 
   }
 }
 
+// One cluster of ks CTAs (launched with cluster dimension ks, 1 <= ks <= 8)
+// serves 128 env rows.  Layer 1 is split along K: CTA rank c accumulates K
+// tiles [c*kt/ks, (c+1)*kt/ks) into its own TMEM; the other ranks copy their
+// partial sums into their own shared memory and signal the rank-0 CTA, whose
+// epilogue adds them (rank order) to its own while applying LN1, then runs
+// the rest of the network alone.  ks = 1 is a plain one-CTA launch.
 template <int NT, bool SPLIT_A>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kMlpThreads, 1)
 k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_alo,
             const __grid_constant__ CUtensorMap tm_b, int n_rows, int k_tiles,
             const float* __restrict__ f, const uint8_t* __restrict__ img, SeatOut io, int seat0,
@@ -469,12 +637,20 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
   uint64_t* empty = full + G::kStages;
   uint64_t* accb = empty + G::kStages;    // layer-1 accumulator complete
   uint64_t* wbar = accb + 1;              // tail weight images landed
-  uint64_t* abar = wbar + 1;              // activation operand written (128 arrivals)
+  uint64_t* abar = wbar + 1;              // activation operand written (512 arrivals)
   uint64_t* dbar = abar + 1;              // tail MMA group complete
-  uint32_t* tmem_slot = (uint32_t*)(dbar + 1);
+  uint64_t* pready = dbar + 1;            // split-K partials of the other ranks written
+  uint32_t* tmem_slot = (uint32_t*)(pready + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
   const int warp = warp_id(), lane = lane_id();
-  const int m0 = blockIdx.x * kBM;
+  const int ks = (int)cluster_size();
+  const int rank = (int)cluster_rank();
+  const bool leader = rank == 0;
+  const int tile = blockIdx.x / ks;
+  const int m0 = tile * kBM;
+  const int kt0 = rank * k_tiles / ks, kt1 = (rank + 1) * k_tiles / ks;
+  const int n_kt = kt1 - kt0;
+  const uint32_t tmem_cols = leader ? G::kTmemCols : (uint32_t)NT;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < G::kStages; ++s) {
@@ -483,197 +659,311 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
     }
     mbar_init(accb, 1);
     mbar_init(wbar, 1);
-    mbar_init(abar, 128);
+    mbar_init(abar, kEpiThreads);
     mbar_init(dbar, 1);
+    mbar_init(pready, ks > 1 ? ks - 1 : 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
-                 "r"(G::kTmemCols));
+                 "r"(tmem_cols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;");
+  // every CTA's barriers are initialised before any remote arrival
+  if (ks > 1) {
+    cluster_arrive();
+    cluster_wait();
+  }
   const uint32_t tmem = *tmem_slot;
+  bool arrived = false;   // this thread's arrival on the closing cluster barrier
 
-  if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer (layer 1)
-    int issued_until = 0;
-    // CTAs start at different K tiles so that at any time they read
-    // different lines of the shared weight stream from L2
-    const int k0 = (int)(((unsigned)blockIdx.x * 7u) % (unsigned)k_tiles);
-    for (int kt = 0; kt < k_tiles; ++kt) {
-      const int s = kt % G::kStages;
-      if (kt >= G::kStages) {
-        if (!mbar_wait(&empty[s], ((kt / G::kStages) - 1) & 1)) {
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (layer 1, this rank's K tiles)
+      int issued_until = 0;
+      // clusters start at different K tiles so that at any time they read
+      // different lines of the shared weight stream from L2
+      const int k0 = (int)(((unsigned)tile * 7u) % (unsigned)n_kt);
+      for (int kt = 0; kt < n_kt; ++kt) {
+        const int s = kt % G::kStages;
+        if (kt >= G::kStages) {
+          if (!mbar_wait(&empty[s], ((kt / G::kStages) - 1) & 1)) {
+            *abort_flag = 1;
+            break;
+          }
+        }
+        if (*abort_flag) break;
+        uint8_t* st = smem + s * G::kStageBytes;
+        const int kx = (kt0 + (kt + k0) % n_kt) * kBK;
+        mbar_expect_tx(&full[s], G::kStageBytes);
+        tma_load_2d(&tm_a, &full[s], st, kx, m0);
+        if (SPLIT_A) tma_load_2d(&tm_alo, &full[s], st + G::kABytes, kx, m0);
+        tma_load_2d(&tm_b, &full[s], st + G::kAAll, kx, 0);
+        tma_load_2d(&tm_b, &full[s], st + G::kAAll + G::kBBytes, kx, NT);
+        issued_until = kt + 1;
+      }
+      // drain: every issued stage must land before the CTA may exit
+      for (int kt = max(0, issued_until - G::kStages); kt < issued_until; ++kt)
+        mbar_wait(&full[kt % G::kStages], (kt / G::kStages) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      const uint32_t idesc = idesc_f16(kBM, NT);
+      bool ok = true;
+      for (int kt = 0; kt < n_kt && ok; ++kt) {
+        const int s = kt % G::kStages;
+        if (!mbar_wait(&full[s], (kt / G::kStages) & 1) || *abort_flag) {
           *abort_flag = 1;
+          ok = false;
           break;
         }
-      }
-      if (*abort_flag) break;
-      uint8_t* st = smem + s * G::kStageBytes;
-      const int kx = ((kt + k0) % k_tiles) * kBK;
-      mbar_expect_tx(&full[s], G::kStageBytes);
-      tma_load_2d(&tm_a, &full[s], st, kx, m0);
-      if (SPLIT_A) tma_load_2d(&tm_alo, &full[s], st + G::kABytes, kx, m0);
-      tma_load_2d(&tm_b, &full[s], st + G::kAAll, kx, 0);
-      tma_load_2d(&tm_b, &full[s], st + G::kAAll + G::kBBytes, kx, NT);
-      issued_until = kt + 1;
-    }
-    // drain: every issued stage must land before the CTA may exit
-    for (int kt = max(0, issued_until - G::kStages); kt < issued_until; ++kt)
-      mbar_wait(&full[kt % G::kStages], (kt / G::kStages) & 1);
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer
-    const uint32_t idesc = idesc_f16(kBM, NT);
-    bool ok = true;
-    for (int kt = 0; kt < k_tiles && ok; ++kt) {
-      const int s = kt % G::kStages;
-      if (!mbar_wait(&full[s], (kt / G::kStages) & 1) || *abort_flag) {
-        *abort_flag = 1;
-        ok = false;
-        break;
-      }
-      asm volatile("tcgen05.fence::after_thread_sync;");
-      uint8_t* st = smem + s * G::kStageBytes;
-      const uint64_t da = sw128_desc(st);
-      const uint64_t dal = sw128_desc(st + G::kABytes);
-      const uint64_t dh = sw128_desc(st + G::kAAll);
-      const uint64_t dl = sw128_desc(st + G::kAAll + G::kBBytes);
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        uint8_t* st = smem + s * G::kStageBytes;
+        const uint64_t da = sw128_desc(st);
+        const uint64_t dal = sw128_desc(st + G::kABytes);
+        const uint64_t dh = sw128_desc(st + G::kAAll);
+        const uint64_t dl = sw128_desc(st + G::kAAll + G::kBBytes);
 #pragma unroll
-      for (int kk = 0; kk < kBK / 16; ++kk) {
-        const uint64_t off = (uint64_t)((kk * 32) >> 4);   // 32 bytes per K=16 step
-        umma_f16(tmem, da + off, dh + off, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
-        umma_f16(tmem, da + off, dl + off, idesc, 1u);
-        if (SPLIT_A) umma_f16(tmem, dal + off, dh + off, idesc, 1u);
-      }
-      umma_commit(&empty[s]);
-    }
-    umma_commit(accb);   // fires once every issued MMA has completed
-    // the pipeline region is free once layer 1's MMAs are done: bring in the
-    // tail weight images (all CTAs read the same 160 KB, an L2 hit)
-    bool loaded = false;
-    if (mbar_wait(accb, 0) && ok) {
-      mbar_expect_tx(wbar, kImgBytes);
-      for (uint32_t o = 0; o < kImgBytes; o += 16384) bulk_load(smem + o, img + o, 16384, wbar);
-      loaded = true;
-    } else {
-      *abort_flag = 1;
-    }
-    const uint32_t id2 = idesc_f16(kBM, 128), id3 = idesc_f16(kBM, 192);
-    uint8_t* a_hi = smem + G::kAct;
-    uint8_t* a_lo = a_hi + G::kActBytes;
-    int committed = 0;
-    if (loaded && !mbar_wait(wbar, 0)) *abort_flag = 1;
-    for (int s = 0; s < S && !*abort_flag; ++s) {
-      // layer 2: D2 overwrites this seat's layer-1 columns (already read)
-      if (!mbar_wait(abar, (2 * s) & 1)) { *abort_flag = 1; break; }
-      asm volatile("tcgen05.fence::after_thread_sync;");
-      umma_split_k128(tmem + 128 * s, a_hi, a_lo, smem + G::kW1, smem + G::kW1 + kImgW1Bytes, 128,
-                      id2);
-      umma_commit(dbar);
-      ++committed;
-      // head hidden layer
-      if (!mbar_wait(abar, (2 * s + 1) & 1)) { *abort_flag = 1; break; }
-      asm volatile("tcgen05.fence::after_thread_sync;");
-      umma_split_k128(tmem + G::kColH, a_hi, a_lo, smem + G::kH0, smem + G::kH0 + kImgH0Bytes, 192,
-                      id3);
-      umma_commit(dbar);
-      ++committed;
-    }
-    // the epilogue consumes every commit; on abort wait here for the last one
-    if (*abort_flag && committed > 0) mbar_wait(dbar, (committed - 1) & 1);
-    if (loaded && *abort_flag) mbar_wait(wbar, 0);
-  } else if (warp >= 2) {
-    // ---------------- epilogue: one row per thread (TMEM lane quadrant warp % 4)
-    const int q = warp & 3;
-    const int r = q * 32 + lane;
-    const int row = m0 + r;
-    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
-    uint8_t* a_hi = smem + G::kAct;
-    uint8_t* a_lo = a_hi + G::kActBytes;
-    // tcgen05.ld is warp-collective: every branch around it is warp-uniform
-    auto wait_all = [&](uint64_t* bar, uint32_t parity) {
-      const bool got = mbar_wait(bar, parity);
-      return __all_sync(QQT_FULL, got) && __shfl_sync(QQT_FULL, *abort_flag, 0) == 0;
-    };
-    bool ok = wait_all(accb, 0);
-    asm volatile("tcgen05.fence::after_thread_sync;");
-    // the activation operand overlays pipeline stages: wait for the weight
-    // images (issued after every layer-1 MMA completed) before writing it
-    ok = ok && wait_all(wbar, 0);
-    for (int s = 0; s < S && ok; ++s) {
-      float x[128];
-      // LN1 over the layer-1 pre-activations
-      tmem_row128(lane_base + 128 * s, x);
-      bias_ln_relu_row(x, f + F_B0 + 128 * s, f + F_LN1G, f + F_LN1B);
-      store_split_row(x, a_hi, a_lo, r);
-      fence_proxy_async();
-      asm volatile("tcgen05.fence::before_thread_sync;");
-      mbar_arrive(abar);
-      // LN2 over layer 2
-      if (!wait_all(dbar, (2 * s) & 1)) { ok = false; break; }
-      asm volatile("tcgen05.fence::after_thread_sync;");
-      tmem_row128(lane_base + 128 * s, x);
-      bias_ln_relu_row(x, f + F_B1, f + F_LN2G, f + F_LN2B);
-      store_split_row(x, a_hi, a_lo, r);
-      fence_proxy_async();
-      asm volatile("tcgen05.fence::before_thread_sync;");
-      mbar_arrive(abar);
-      // head hidden units -> output layers
-      if (!wait_all(dbar, (2 * s + 1) & 1)) { ok = false; break; }
-      asm volatile("tcgen05.fence::after_thread_sync;");
-      float z[8];
-#pragma unroll
-      for (int o = 0; o < 8; ++o) z[o] = 0.f;
-#pragma unroll
-      for (int c = 0; c < 6; ++c) {
-        float h[32];
-        tmem_ld32(lane_base + G::kColH + 32 * c, h);
-        const int head = c >> 1, u0 = (c & 1) * 32;
-#pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          const float4 hb = __ldg(reinterpret_cast<const float4*>(f + F_HB0 + 32 * c + i));
-          h[i] = fmaxf(__fadd_rn(h[i], hb.x), 0.f);
-          h[i + 1] = fmaxf(__fadd_rn(h[i + 1], hb.y), 0.f);
-          h[i + 2] = fmaxf(__fadd_rn(h[i + 2], hb.z), 0.f);
-          h[i + 3] = fmaxf(__fadd_rn(h[i + 3], hb.w), 0.f);
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          const uint64_t off = (uint64_t)((kk * 32) >> 4);   // 32 bytes per K=16 step
+          umma_f16(tmem, da + off, dh + off, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+          umma_f16(tmem, da + off, dl + off, idesc, 1u);
+          if (SPLIT_A) umma_f16(tmem, dal + off, dh + off, idesc, 1u);
         }
-        const int o_lo = head == 0 ? 0 : (head == 1 ? 5 : 7);
-        const int o_hi = head == 0 ? 5 : (head == 1 ? 7 : 8);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(accb);   // fires once every issued MMA has completed
+      if (leader) {
+        // the pipeline region is free once layer 1's MMAs are done: bring in
+        // the tail weight images (all CTAs read the same 160 KB, an L2 hit)
+        bool loaded = false;
+        if (mbar_wait(accb, 0) && ok) {
+          mbar_expect_tx(wbar, kImgBytes);
+          for (uint32_t o = 0; o < kImgBytes; o += 16384) bulk_load(smem + o, img + o, 16384, wbar);
+          loaded = true;
+        } else {
+          *abort_flag = 1;
+        }
+        const uint32_t id2 = idesc_f16(kBM, 128), id3 = idesc_f16(kBM, 192);
+        uint8_t* a_hi = smem + G::kAct;
+        uint8_t* a_lo = a_hi + G::kActBytes;
+        int committed = 0;
+        if (loaded && !mbar_wait(wbar, 0)) *abort_flag = 1;
+        for (int s = 0; s < S && !*abort_flag; ++s) {
+          // layer 2: D2 overwrites this seat's layer-1 columns (already read)
+          if (!mbar_wait(abar, (2 * s) & 1)) { *abort_flag = 1; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;");
+          umma_split_k128(tmem + 128 * s, a_hi, a_lo, smem + G::kW1, smem + G::kW1 + kImgW1Bytes,
+                          128, id2);
+          umma_commit(dbar);
+          ++committed;
+          // head hidden layer
+          if (!mbar_wait(abar, (2 * s + 1) & 1)) { *abort_flag = 1; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;");
+          umma_split_k128(tmem + G::kColH, a_hi, a_lo, smem + G::kH0,
+                          smem + G::kH0 + kImgH0Bytes, 192, id3);
+          umma_commit(dbar);
+          ++committed;
+        }
+        // the epilogue consumes every commit; on abort wait here for the last one
+        if (*abort_flag && committed > 0) mbar_wait(dbar, (committed - 1) & 1);
+        if (loaded && *abort_flag) mbar_wait(wbar, 0);
+      } else {
+        mbar_wait(accb, 0);   // this rank's MMAs are done before it may exit
+      }
+    }
+  } else {
+    // ---------------- epilogue: row r = 32 * (warp % 4) + lane, columns
+    // 32 * quarter .. + 31 of each 128-wide layer
+    const int qd = warp & 3;
+    const int quarter = (warp - 2) >> 2;
+    const int r = qd * 32 + lane;
+    const int row = m0 + r;
+    const uint32_t lane_base = tmem + ((uint32_t)(qd * 32) << 16);
+    const uint32_t scr = lane_base + G::kColScr;
+    uint8_t* a_hi = smem + G::kAct;
+    uint8_t* a_lo = a_hi + G::kActBytes;
+    bool ok = epi_and(mbar_wait(accb, 0) && *abort_flag == 0);
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    if (!leader) {
+      // split-K partials -> own shared memory (the drained pipeline region)
+      if (ok) {
+#pragma unroll 1
+        for (int s = 0; s < S; ++s) {
+          float x[32];
+          tmem_ld32(lane_base + 128 * s + 32 * quarter, x);
+          uint8_t* part = smem + s * (kBM * 512);
 #pragma unroll
-        for (int o = 0; o < 8; ++o) {
-          if (o < o_lo || o >= o_hi) continue;
+          for (int t = 0; t < 8; ++t)
+            *reinterpret_cast<float4*>(part + part_off(r, 8 * quarter + t)) =
+                make_float4(x[4 * t], x[4 * t + 1], x[4 * t + 2], x[4 * t + 3]);
+        }
+      }
+      asm volatile("fence.acq_rel.cluster;" ::: "memory");
+      epi_sync();
+      // one arrival per rank (also on failure: the error word is already set)
+      if (warp == 2 && lane == 0) mbar_arrive_remote(dsmem_addr(pready, 0));
+      // stays resident (closing cluster barrier) until rank 0 has read the partials
+      cluster_arrive();
+      arrived = true;
+    } else {
+      if (ks > 1) ok = epi_and(ok && mbar_wait_cluster(pready, 0));
+#pragma unroll 1
+      for (int s = 0; s < S && ok; ++s) {
+        float x[32];
+        // LN1 over the layer-1 pre-activations (rank-ordered split-K sum)
+        tmem_ld32(lane_base + 128 * s + 32 * quarter, x);
+#pragma unroll 1
+        for (int c = 1; c < ks; ++c) {
+          const uint32_t base = dsmem_addr(smem + s * (kBM * 512), (uint32_t)c);
 #pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            const float4 wv = __ldg(reinterpret_cast<const float4*>(f + F_HW2 + o * 64 + u0 + i));
-            z[o] = fmaf(wv.x, h[i], z[o]);
-            z[o] = fmaf(wv.y, h[i + 1], z[o]);
-            z[o] = fmaf(wv.z, h[i + 2], z[o]);
-            z[o] = fmaf(wv.w, h[i + 3], z[o]);
+          for (int t = 0; t < 8; ++t) {
+            const float4 v = ld_dsmem_f4(base + part_off(r, 8 * quarter + t));
+            x[4 * t] = __fadd_rn(x[4 * t], v.x);
+            x[4 * t + 1] = __fadd_rn(x[4 * t + 1], v.y);
+            x[4 * t + 2] = __fadd_rn(x[4 * t + 2], v.z);
+            x[4 * t + 3] = __fadd_rn(x[4 * t + 3], v.w);
+          }
+        }
+        if (ks > 1 && s == S - 1) {
+          cluster_arrive();   // done reading the other ranks' shared memory
+          arrived = true;
+        }
+        bias_ln_relu_quarter(x, quarter, scr, f + F_B0 + 128 * s, f + F_LN1G, f + F_LN1B);
+        store_split_quarter(x, a_hi, a_lo, r, quarter);
+        fence_proxy_async();
+        asm volatile("tcgen05.fence::before_thread_sync;");
+        mbar_arrive(abar);
+        // LN2 over layer 2
+        ok = epi_and(mbar_wait(dbar, (2 * s) & 1) && *abort_flag == 0);
+        if (!ok) break;
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        tmem_ld32(lane_base + 128 * s + 32 * quarter, x);
+        bias_ln_relu_quarter(x, quarter, scr + 8, f + F_B1, f + F_LN2G, f + F_LN2B);
+        store_split_quarter(x, a_hi, a_lo, r, quarter);
+        fence_proxy_async();
+        asm volatile("tcgen05.fence::before_thread_sync;");
+        mbar_arrive(abar);
+        // head hidden units 48*quarter .. +47 -> partial output logits
+        ok = epi_and(mbar_wait(dbar, (2 * s + 1) & 1) && *abort_flag == 0);
+        if (!ok) break;
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        float z[8];
+#pragma unroll
+        for (int o = 0; o < 8; ++o) z[o] = 0.f;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+          const int u0 = 48 * quarter + 16 * c;   // 16 units inside one head
+          float h[16];
+          tmem_ld16(lane_base + G::kColH + u0, h);
+#pragma unroll
+          for (int i = 0; i < 16; i += 4) {
+            const float4 hb = __ldg(reinterpret_cast<const float4*>(f + F_HB0 + u0 + i));
+            h[i] = fmaxf(__fadd_rn(h[i], hb.x), 0.f);
+            h[i + 1] = fmaxf(__fadd_rn(h[i + 1], hb.y), 0.f);
+            h[i + 2] = fmaxf(__fadd_rn(h[i + 2], hb.z), 0.f);
+            h[i + 3] = fmaxf(__fadd_rn(h[i + 3], hb.w), 0.f);
+          }
+          const int head = u0 >> 6, uu = u0 & 63;
+          const int o_lo = head == 0 ? 0 : (head == 1 ? 5 : 7);
+          const int o_hi = head == 0 ? 5 : (head == 1 ? 7 : 8);
+#pragma unroll
+          for (int o = 0; o < 8; ++o) {
+            if (o < o_lo || o >= o_hi) continue;
+#pragma unroll
+            for (int i = 0; i < 16; i += 4) {
+              const float4 wv = __ldg(reinterpret_cast<const float4*>(f + F_HW2 + o * 64 + uu + i));
+              z[o] = fmaf(wv.x, h[i], z[o]);
+              z[o] = fmaf(wv.y, h[i + 1], z[o]);
+              z[o] = fmaf(wv.z, h[i + 2], z[o]);
+              z[o] = fmaf(wv.w, h[i + 3], z[o]);
+            }
+          }
+        }
+        // the four quarters' partial logits through the row's TMEM lane
+        tmem_st8(scr + 16 + 8 * quarter, z);
+        asm volatile("tcgen05.fence::before_thread_sync;");
+        epi_sync();
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        if (quarter == 0) {
+          float zz[32];
+          tmem_ld32(scr + 16, zz);
+          if (row < n_rows) {
+#pragma unroll
+            for (int o = 0; o < 8; ++o)
+              z[o] = ((zz[o] + zz[8 + o]) + (zz[16 + o] + zz[24 + o])) + __ldg(f + F_HB2 + o);
+            sample_write(z, row, seat0 + s, n_rows, io.mm[s], mm_stride, io.bm[s], bm_stride, u,
+                         io.act[s], act_stride, logp_out, value_out, logits_out);
           }
         }
       }
-      asm volatile("tcgen05.fence::before_thread_sync;");
-      if (row < n_rows) {
-#pragma unroll
-        for (int o = 0; o < 8; ++o) z[o] += __ldg(f + F_HB2 + o);
-        sample_write(z, row, seat0 + s, n_rows, io.mm[s], mm_stride, io.bm[s], bm_stride, u,
-                     io.act[s], act_stride, logp_out, value_out, logits_out);
-      }
+      if (!ok) *abort_flag = 1;
     }
-    if (!ok) *abort_flag = 1;
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
+  if (ks > 1) {
+    if (!arrived) cluster_arrive();
+    cluster_wait();
+  }
   __syncthreads();
   if (warp == 0) {
     asm volatile("tcgen05.fence::after_thread_sync;");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(G::kTmemCols));
+                 "r"(tmem_cols));
   }
+}
+
+// Split-K factor for a launch of m_tiles row tiles over k_tiles K tiles:
+// QQT_MLP_SPLIT_K (1..8) if set, else 4 for launches of up to 8 row tiles
+// (up to 1024 envs: a small batch is latency-bound, and the split divides
+// the per-SM TMA stream), 2 up to 16 tiles, and no split above that (a
+// rollout's policy runs beside the simulator kernels, and extra CTAs only
+// take SMs from them).
+static int mlp_split_k(int m_tiles, int k_tiles) {
+  static int env = -1;
+  if (env < 0) {
+    const char* e = getenv("QQT_MLP_SPLIT_K");
+    env = e ? atoi(e) : 0;
+    if (env < 0 || env > kMaxSplitK) env = 0;
+  }
+  int ks = env;
+  if (ks == 0) ks = m_tiles <= 8 ? 4 : (m_tiles <= 16 ? 2 : 1);
+  return min(ks, max(1, k_tiles / 2));
+}
+
+template <int NT, bool SPLIT_A>
+static int launch_mlp_fused(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap& mb,
+                            int n_rows, int k_tiles, const float* f, const uint8_t* img,
+                            const SeatOut& io, int seat0, int mm_stride, int bm_stride,
+                            const float* u, int act_stride, float* logp, float* value,
+                            float* logits, cudaStream_t st) {
+  using G = FusedCfg<NT, SPLIT_A>;
+  auto kern = k_mlp_fused<NT, SPLIT_A>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
+  const int m_tiles = (n_rows + kBM - 1) / kBM;
+  const int ks = mlp_split_k(m_tiles, k_tiles);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(m_tiles * ks), 1, 1);
+  cfg.blockDim = dim3(kMlpThreads, 1, 1);
+  cfg.dynamicSmemBytes = G::kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)ks;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = ks > 1 ? 1 : 0;
+  if (cudaLaunchKernelEx(&cfg, kern, ma, malo, mb, n_rows, k_tiles, f, img, io, seat0, mm_stride,
+                         bm_stride, u, act_stride, logp, value, logits) != cudaSuccess)
+    return QQT_E_LAUNCH;
+  return launch_status();
 }
 
 }  // namespace qqt
@@ -817,25 +1107,16 @@ extern "C" int qqt_mlp_act(const void* pack, const void* obs, int32_t n_envs, in
   cudaStream_t st = (cudaStream_t)stream;
   const float* fpar = (const float*)(pk + L.f_off);
   const int k_tiles = L.kp / kBK;
-  const int grid = (n_envs + kBM - 1) / kBM;
   SeatOut io;
   for (int s = 0; s < 2; ++s) {
     io.mm[s] = s < n_seats ? mm[s] : nullptr;
     io.bm[s] = s < n_seats ? bm[s] : nullptr;
     io.act[s] = s < n_seats ? act[s] : nullptr;
   }
-  if (L.nt == 128) {
-    cudaFuncSetAttribute(k_mlp_fused<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         FusedCfg<128>::kSmem);
-    k_mlp_fused<128, false><<<grid, 192, FusedCfg<128>::kSmem, st>>>(
-        ma, ma, mb, n_envs, k_tiles, fpar, pk + L.img_off, io, 0, mm_stride, bm_stride, u,
-        act_stride, logp, value, logits);
-  } else {
-    cudaFuncSetAttribute(k_mlp_fused<256, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         FusedCfg<256>::kSmem);
-    k_mlp_fused<256, false><<<grid, 192, FusedCfg<256>::kSmem, st>>>(
-        ma, ma, mb, n_envs, k_tiles, fpar, pk + L.img_off, io, 0, mm_stride, bm_stride, u,
-        act_stride, logp, value, logits);
-  }
-  return launch_status();
+  if (L.nt == 128)
+    return launch_mlp_fused<128, false>(ma, ma, mb, n_envs, k_tiles, fpar, pk + L.img_off, io, 0,
+                                        mm_stride, bm_stride, u, act_stride, logp, value, logits,
+                                        st);
+  return launch_mlp_fused<256, false>(ma, ma, mb, n_envs, k_tiles, fpar, pk + L.img_off, io, 0,
+                                      mm_stride, bm_stride, u, act_stride, logp, value, logits, st);
 }

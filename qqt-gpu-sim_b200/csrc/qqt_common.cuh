@@ -17,6 +17,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include "../../include/qqt_b200.h"
 
@@ -553,6 +554,21 @@ static inline int check_cfg(const QqtCfg* cfg) {
       cfg->n_players > QQT_MAX_P)
     return QQT_E_LIMIT;
   return QQT_OK;
+}
+
+// SM count of the current device (cached per device).
+static inline int sm_count() {
+  static int n[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!n[dev]) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
+      v = 148;
+    n[dev] = v;
+  }
+  return n[dev];
 }
 
 static inline int launch_status() {

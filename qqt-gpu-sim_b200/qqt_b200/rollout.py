@@ -108,6 +108,12 @@ class Rollout:
         # the fused observation writes fp16 rows with the engine's stride
         self.fuse_observe = bool(sim.cfg.obs_fp16) and sim.obs_stride % 8 == 0
         self._ready = -1      # tick whose observation the last step already wrote
+        # probe(name, fn) wraps each engine call of a tick (e.g. timing events
+        # around it); None runs the calls directly
+        self.probe = None
+
+    def _run(self, name, fn):
+        return fn() if self.probe is None else self.probe(name, fn)
 
     def tick(self, t: int) -> None:
         sim, buf, dr = self.sim, self.buf, self.draws
@@ -115,36 +121,39 @@ class Rollout:
         if self._ready == t:
             obs, mm, bm = buf.obs(b), buf.mm[b], buf.bm[b]
         else:
-            obs, mm, bm = sim.observe_and_mask(buf.obs_rows[b], buf.mm[b], buf.bm[b], danger=False)
+            obs, mm, bm = self._run("observe", lambda: sim.observe_and_mask(
+                buf.obs_rows[b], buf.mm[b], buf.bm[b], danger=False))
         acts = buf.act[b]
         main = torch.cuda.current_stream(sim.device)
+
+        def learner():
+            self.learner.act_seats(obs, [mm[:, s] for s in self.seats],
+                                   [bm[:, s] for s in self.seats], dr.u_net[t],
+                                   [acts[:, s] for s in self.seats], buf.logp[b], buf.val[b])
         if self.side is not None:
             self.side.wait_stream(main)
             with torch.cuda.stream(self.side):
-                self.learner.act_seats(obs, [mm[:, s] for s in self.seats],
-                                       [bm[:, s] for s in self.seats], dr.u_net[t],
-                                       [acts[:, s] for s in self.seats], buf.logp[b], buf.val[b])
+                self._run("policy", learner)
         else:
-            self.learner.act_seats(obs, [mm[:, s] for s in self.seats], [bm[:, s] for s in self.seats],
-                                   dr.u_net[t], [acts[:, s] for s in self.seats], buf.logp[b],
-                                   buf.val[b])
+            self._run("policy", learner)
         if self.opponent is not None:
             o = self.opp_seat
             bot = self.opponent
             self.feed_opponent(t)
-            bot.act(obs, mm[:, o], bm[:, o], o, out=acts[:, o])
+            self._run("bot", lambda: bot.act(obs, mm[:, o], bm[:, o], o, out=acts[:, o]))
             main.wait_stream(self.side)
         flush = bool(self.flush_every) and t % self.flush_every == self.flush_every - 1
         nxt = None
         if self.fuse_observe and not flush and t + 1 < self.T:
             b1 = (t + 1) % self.slots
             nxt = (buf.obs_rows[b1], buf.mm[b1], buf.bm[b1])
-        sim.step(acts, auto_reset=True, crate_draws=(dr.crate[t, 0], dr.crate[t, 1]),
-                 reward_out=buf.rew[b], done_out=buf.done[b], hit_out=buf.dmg[b],
-                 info_planes=False, next_obs=nxt)
+        self._run("step+observe" if nxt is not None else "step", lambda: sim.step(
+            acts, auto_reset=True, crate_draws=(dr.crate[t, 0], dr.crate[t, 1]),
+            reward_out=buf.rew[b], done_out=buf.done[b], hit_out=buf.dmg[b],
+            info_planes=False, next_obs=nxt))
         self._ready = t + 1 if nxt is not None else -1
         if flush:
-            sim.flush_recycle()
+            self._run("flush", sim.flush_recycle)
 
     def feed_opponent(self, t: int) -> None:
         """Hand the opponent bot its draws for tick t (noise; the astar mode
