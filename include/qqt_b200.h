@@ -16,9 +16,10 @@
  *     positions, relaxation not converged) are OR-ed into a device error
  *     word that qqt_get_error() reads and clears.
  *
- * Layout (N envs, C = H*W cells, P players; env index innermost):
- *   plane   [C][N]       wall/brick/crate/recycle (uint8 0/1), fuse (int16),
- *                        owner (int8), bomb_blast (int16)
+ * Layout (N envs, C = H*W cells, P players):
+ *   plane   [N][C]       wall/brick/crate/recycle (uint8 0/1), fuse (int16),
+ *                        owner (int8), bomb_blast (int16); env-major, the
+ *                        reference's (N, H, W) tensors as they are
  *   player  [P][N]       alive/hp (uint8), since_bomb (int32),
  *                        bombs_cap/blast_cap/invuln/pending_lost/combo/
  *                        last_hit/lo_bombs/lo_blast (int64),
@@ -100,7 +101,7 @@ typedef struct QqtState {
 
 /* Per-env reset template used by the device-side auto-reset (the
  * benchmark configurations reset every env to its own template map; see
- * qqt_step).  Planes [C][N]; caps [P][N]; spawn [P][2][N]. */
+ * qqt_step).  Planes [N][C]; caps [P][N]; spawn [P][2][N]. */
 typedef struct QqtTemplate {
   const uint8_t *wall, *brick, *crate;
   const float *spawn;
@@ -119,7 +120,7 @@ typedef struct QqtStepOut {
   uint8_t *done;            /* [N]                                            */
   uint8_t *died, *winner;   /* [N][P]                                         */
   int64_t *n_alive;         /* [N]                                            */
-  uint8_t *covered, *triggered; /* [C][N]                                     */
+  uint8_t *covered, *triggered; /* [N][C]                                     */
   uint8_t *reset_mask;      /* [N] envs reset by the device auto-reset        */
   uint8_t *hit;             /* [N][P] lost hp this tick in an env that did not
                                end: the rollout's damage flag, (hp before the

@@ -1,12 +1,12 @@
 // Shared device code of the B200 rollout engine.
 //
 // Work decomposition: one thread block owns a tile of QQT_TILE_E consecutive
-// envs.  The block stages the tile's planes from the SoA global layout
-// ([cell][env], env innermost, so consecutive threads read consecutive envs)
-// into shared memory transposed to [env][cell], then each warp simulates one
-// env at a time with its 32 lanes spread over cells / bombs / players.  With
-// per-env contiguous planes, lanes walking consecutive cells hit distinct
-// banks.
+// envs.  Planes are env-major in global memory ([env][cell]), so the block
+// stages each plane of its tile as one contiguous run (coalesced 8- and
+// 16-byte accesses) into shared memory with the same [env][cell] layout,
+// then each warp simulates one env with its 32 lanes spread over cells /
+// bombs / players.  With per-env contiguous planes, lanes walking
+// consecutive cells hit distinct banks.
 //
 // Float arithmetic on the parity path uses the _rn intrinsics in the exact
 // operation order of the reference (the library is also built with
@@ -102,7 +102,7 @@ enum : unsigned {
   PL_OWNER = 16, PL_FUSE = 32, PL_BLAST = 64, PL_ALL = 127
 };
 
-static_assert(QQT_TILE_E == 8, "vectorised tile transfers move 8 envs per access");
+static_assert(QQT_TILE_E == 8, "vectorised tile transfers move 8-byte / 16-byte chunks");
 
 // Plane pl (bit 1 << pl of PL_*) of the state / the tile.
 __device__ __forceinline__ uint8_t* state_plane(const QqtState& st, int pl) {
@@ -128,106 +128,105 @@ __device__ __forceinline__ uint8_t* tile_plane(const Tile& t, int pl) {
   }
 }
 
-// Vector tile transfers need N a multiple of 8, a full tile and 16-byte
-// aligned plane bases.
+// Planes are env-major ([N][C]), so a tile (envs e0 .. e0+7) is one
+// contiguous run of 8 * C elements per plane, laid out in shared memory
+// exactly as in global memory ([slot][cell]).  A full tile with 16-byte
+// aligned plane bases moves in 8-byte (u8 planes: 8 * C bytes = C chunks)
+// and 16-byte (i16 planes: 16 * C bytes = C chunks) accesses, consecutive
+// threads on consecutive chunks; a partial tile element by element.
 __device__ __forceinline__ bool tile_vector_ok(const QqtState& st, int n, int e0) {
   const uintptr_t a = (uintptr_t)st.wall | (uintptr_t)st.brick | (uintptr_t)st.crate |
                       (uintptr_t)st.recycle | (uintptr_t)st.owner | (uintptr_t)st.fuse |
                       (uintptr_t)st.bomb_blast;
-  return (n & 7) == 0 && e0 + QQT_TILE_E <= n && (a & 15) == 0;
+  return e0 + QQT_TILE_E <= n && (a & 15) == 0;
 }
 
-// Global [cell][N] -> shared [slot][cell] for envs e0 .. e0+E-1 (block-wide).
-// A full tile with N a multiple of 8 moves each (plane, cell) as one 8-byte
-// (u8 planes) or 16-byte (i16 planes) access; otherwise element by element.
+// Global [N][C] -> shared [slot][cell] for envs e0 .. e0+E-1 (block-wide).
 __device__ inline void load_tile(const Tile& t, const QqtState& st, int n, int e0,
                                  unsigned planes) {
   const int cells = t.cells;
   if (tile_vector_ok(st, n, e0)) {
-    for (int i = threadIdx.x; i < 7 * cells; i += blockDim.x) {
-      const int pl = i / cells, c = i - pl * cells;
-      if (!(planes & (1u << pl))) continue;
-      const size_t g = (size_t)c * n + e0;
-      uint8_t* dst = tile_plane(t, pl);
-      if (pl < 5) {
-        const uint2 v = *reinterpret_cast<const uint2*>(state_plane(st, pl) + g);
+    // kTileBatch accesses per thread are issued before any is consumed, so
+    // their latencies overlap (7 planes x 169 chunks over 256 threads is 4.6)
+    constexpr int kTileBatch = 5;
+    const int total = 7 * cells;
+    for (int i0 = threadIdx.x; i0 < total; i0 += kTileBatch * blockDim.x) {
+      uint4 v[kTileBatch];
+      int it[kTileBatch];
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          dst[k * cells + c] = (uint8_t)(((k < 4 ? v.x : v.y) >> (8 * (k & 3))) & 0xff);
-      } else {
-        const uint4 v = *reinterpret_cast<const uint4*>(state_plane(st, pl) + 2 * g);
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-        int16_t* d16 = reinterpret_cast<int16_t*>(dst);
+      for (int b = 0; b < kTileBatch; ++b) {
+        const int i = i0 + b * blockDim.x;
+        it[b] = -1;
+        v[b] = make_uint4(0, 0, 0, 0);
+        if (i < total) {
+          const int pl = i / cells, k = i - pl * cells;
+          if (planes & (1u << pl)) {
+            it[b] = i;
+            if (pl < 5) {
+              const uint2 u = reinterpret_cast<const uint2*>(
+                  state_plane(st, pl) + (size_t)e0 * cells)[k];
+              v[b] = make_uint4(u.x, u.y, 0, 0);
+            } else {
+              v[b] = reinterpret_cast<const uint4*>(
+                  state_plane(st, pl) + (size_t)e0 * cells * 2)[k];
+            }
+          }
+        }
+      }
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          d16[k * cells + c] = (int16_t)((w[k >> 1] >> (16 * (k & 1))) & 0xffff);
+      for (int b = 0; b < kTileBatch; ++b) {
+        if (it[b] < 0) continue;
+        const int pl = it[b] / cells, k = it[b] - pl * cells;
+        if (pl < 5)
+          reinterpret_cast<uint2*>(tile_plane(t, pl))[k] = make_uint2(v[b].x, v[b].y);
+        else
+          reinterpret_cast<uint4*>(tile_plane(t, pl))[k] = v[b];
       }
     }
     return;
   }
-  const int total = cells * QQT_TILE_E;
+  const int total = cells * min(QQT_TILE_E, n - e0);
+  const size_t g0 = (size_t)e0 * cells;
   for (int i = threadIdx.x; i < total; i += blockDim.x) {
-    const int c = i / QQT_TILE_E;
-    const int s = i - c * QQT_TILE_E;
-    const int e = e0 + s;
-    const int so = s * cells + c;
-    if (e < n) {
-      const size_t g = (size_t)c * n + e;
-      if (planes & PL_WALL) t.wall[so] = st.wall[g];
-      if (planes & PL_BRICK) t.brick[so] = st.brick[g];
-      if (planes & PL_CRATE) t.crate[so] = st.crate[g];
-      if (planes & PL_RECYCLE) t.recycle[so] = st.recycle[g];
-      if (planes & PL_OWNER) t.owner[so] = st.owner[g];
-      if (planes & PL_FUSE) t.fuse[so] = st.fuse[g];
-      if (planes & PL_BLAST) t.blast[so] = st.bomb_blast[g];
-    }
+    const size_t g = g0 + i;
+    if (planes & PL_WALL) t.wall[i] = st.wall[g];
+    if (planes & PL_BRICK) t.brick[i] = st.brick[g];
+    if (planes & PL_CRATE) t.crate[i] = st.crate[g];
+    if (planes & PL_RECYCLE) t.recycle[i] = st.recycle[g];
+    if (planes & PL_OWNER) t.owner[i] = st.owner[g];
+    if (planes & PL_FUSE) t.fuse[i] = st.fuse[g];
+    if (planes & PL_BLAST) t.blast[i] = st.bomb_blast[g];
   }
 }
 
+// Shared [slot][cell] -> global [N][C] (block-wide; after a __syncthreads()).
 __device__ inline void store_tile(const Tile& t, const QqtState& st, int n, int e0,
                                   unsigned planes) {
   const int cells = t.cells;
   if (tile_vector_ok(st, n, e0)) {
     for (int i = threadIdx.x; i < 7 * cells; i += blockDim.x) {
-      const int pl = i / cells, c = i - pl * cells;
+      const int pl = i / cells, k = i - pl * cells;
       if (!(planes & (1u << pl))) continue;
-      const size_t g = (size_t)c * n + e0;
-      const uint8_t* src = tile_plane(t, pl);
-      if (pl < 5) {
-        uint32_t lo = 0, hi = 0;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          lo |= (uint32_t)src[k * cells + c] << (8 * k);
-          hi |= (uint32_t)src[(k + 4) * cells + c] << (8 * k);
-        }
-        *reinterpret_cast<uint2*>(state_plane(st, pl) + g) = make_uint2(lo, hi);
-      } else {
-        const uint16_t* s16 = reinterpret_cast<const uint16_t*>(src);
-        uint32_t w[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          w[k] = (uint32_t)s16[(2 * k) * cells + c] | ((uint32_t)s16[(2 * k + 1) * cells + c] << 16);
-        *reinterpret_cast<uint4*>(state_plane(st, pl) + 2 * g) = make_uint4(w[0], w[1], w[2], w[3]);
-      }
+      if (pl < 5)
+        reinterpret_cast<uint2*>(state_plane(st, pl) + (size_t)e0 * cells)[k] =
+            reinterpret_cast<const uint2*>(tile_plane(t, pl))[k];
+      else
+        reinterpret_cast<uint4*>(state_plane(st, pl) + (size_t)e0 * cells * 2)[k] =
+            reinterpret_cast<const uint4*>(tile_plane(t, pl))[k];
     }
     return;
   }
-  const int total = cells * QQT_TILE_E;
+  const int total = cells * min(QQT_TILE_E, n - e0);
+  const size_t g0 = (size_t)e0 * cells;
   for (int i = threadIdx.x; i < total; i += blockDim.x) {
-    const int c = i / QQT_TILE_E;
-    const int s = i - c * QQT_TILE_E;
-    const int e = e0 + s;
-    const int so = s * cells + c;
-    if (e < n) {
-      const size_t g = (size_t)c * n + e;
-      if (planes & PL_WALL) st.wall[g] = t.wall[so];
-      if (planes & PL_BRICK) st.brick[g] = t.brick[so];
-      if (planes & PL_CRATE) st.crate[g] = t.crate[so];
-      if (planes & PL_RECYCLE) st.recycle[g] = t.recycle[so];
-      if (planes & PL_OWNER) st.owner[g] = t.owner[so];
-      if (planes & PL_FUSE) st.fuse[g] = t.fuse[so];
-      if (planes & PL_BLAST) st.bomb_blast[g] = t.blast[so];
-    }
+    const size_t g = g0 + i;
+    if (planes & PL_WALL) st.wall[g] = t.wall[i];
+    if (planes & PL_BRICK) st.brick[g] = t.brick[i];
+    if (planes & PL_CRATE) st.crate[g] = t.crate[i];
+    if (planes & PL_RECYCLE) st.recycle[g] = t.recycle[i];
+    if (planes & PL_OWNER) st.owner[g] = t.owner[i];
+    if (planes & PL_FUSE) st.fuse[g] = t.fuse[i];
+    if (planes & PL_BLAST) st.bomb_blast[g] = t.blast[i];
   }
 }
 

@@ -69,18 +69,20 @@ struct FuseTables {
 // staged planes (sim/obs.py:25-229), for the warp that owns the env.  Inputs:
 // dng = the env's danger map (sim/blast.py:158-317), live[p] = live bombs of
 // player p, and for lanes < P that player's position, alive flag,
-// invulnerability and bomb cap.  The row goes straight to global memory:
-// lane l writes cell l, l+32, ... of every channel (consecutive lanes,
-// consecutive fp16 elements).
+// invulnerability and bomb cap.  Lane l computes cell l, l+32, ... of every
+// channel (consecutive lanes, consecutive elements); the row goes straight to
+// global memory, or, given a 16-byte aligned per-warp `stage` of obs_stride
+// elements, into shared memory first and out as 16-byte stores.
 template <class T>
 __device__ inline void observe_env(const QqtCfg& cfg, const Env& v, int e, PInfo* pi,
                                    const float* dng, const int* live, float py, float px,
                                    bool alive_p, int64_t inv_p, int64_t bcap_p, int64_t t_e,
                                    const FuseTables& ft, void* obs, float* danger_out,
-                                   uint8_t* mm, uint8_t* bm) {
+                                   uint8_t* mm, uint8_t* bm, T* stage = nullptr) {
   const int h = cfg.height, w = cfg.width, C = h * w, P = cfg.n_players;
   const int lane = lane_id();
   const int nch = cfg.obs_channels;
+  if (stage) __syncwarp();   // the staging area reuses scratch read just before
   if (lane < P) {
     const int p = lane;
     PInfo q;
@@ -116,8 +118,56 @@ __device__ inline void observe_env(const QqtCfg& cfg, const Env& v, int e, PInfo
   __syncwarp();   // PInfo visible
 
   const float tv = __fdiv_rn((float)t_e, cfg.max_steps_f);
-  T* row = obs ? (T*)obs + (size_t)e * cfg.obs_stride : nullptr;
-  if (obs || danger_out) {
+  T* const grow = obs ? (T*)obs + (size_t)e * cfg.obs_stride : nullptr;
+  if (obs && stage) {
+    // staged row: zero it, write the dense channels cell by cell and the
+    // sparse ones (position splats, values at each player's cell) at their
+    // cells, then move it out as 16-byte stores (row stride and base are
+    // 16-byte aligned: checked by the entry points)
+    const int n16 = (int)((size_t)cfg.obs_stride * sizeof(T) / 16);
+    uint4* s4 = reinterpret_cast<uint4*>(stage);
+    for (int k = lane; k < n16; k += 32) s4[k] = make_uint4(0, 0, 0, 0);
+    __syncwarp();
+    const T tvh = to_obs<T>(tv);
+    const bool extra = nch > 2 * P + 3;
+    for (int c = lane; c < C; c += 32) {
+      const float d = dng[c];
+      if (danger_out) danger_out[(size_t)e * C + c] = d;
+      const int f = v.fuse[c], o = v.owner[c];
+      if (f > 0 && o >= 0 && o < P)     // own-bomb fuse channel of the owner
+        stage[(P + o) * C + c] = to_obs<T>(f < 32 ? ft.norm[f] : __fdiv_rn((float)f, cfg.fuse_f));
+      if (v.wall[c] | v.brick[c]) stage[2 * P * C + c] = to_obs<T>(1.f);
+      stage[(2 * P + 1) * C + c] = to_obs<T>(d);
+      stage[(2 * P + 2) * C + c] = tvh;
+      if (extra && v.crate[c]) stage[(2 * P + 3) * C + c] = to_obs<T>(1.f);
+    }
+    if (lane < P) {
+      const PInfo& q = pi[lane];
+      // splat cell sc[m]: the sum over the corners that land on it, in corner
+      // order from 0 (the reference's four scatter_add calls)
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        bool first = true;
+#pragma unroll
+        for (int m2 = 0; m2 < m; ++m2) first = first && q.sc[m2] != q.sc[m];
+        if (!first) continue;
+        float sv = 0.f;
+#pragma unroll
+        for (int m2 = m; m2 < 4; ++m2)
+          if (q.sc[m2] == q.sc[m]) sv = __fadd_rn(sv, q.sw[m2]);
+        stage[lane * C + q.sc[m]] = to_obs<T>(sv);
+      }
+      if (extra) {
+        stage[(2 * P + 4 + lane) * C + q.flat] = to_obs<T>(q.inv);
+        stage[(3 * P + 4 + lane) * C + q.flat] = to_obs<T>(q.avail);
+        stage[(4 * P + 4 + lane) * C + q.flat] = to_obs<T>(q.capv);
+      }
+    }
+    __syncwarp();
+    uint4* dst = reinterpret_cast<uint4*>(grow);
+    for (int k = lane; k < n16; k += 32) dst[k] = s4[k];
+  } else if (obs || danger_out) {
+    T* row = grow;
     for (int c = lane; c < C; c += 32) {
       const float d = dng[c];
       if (danger_out) danger_out[(size_t)e * C + c] = d;
@@ -149,9 +199,9 @@ __device__ inline void observe_env(const QqtCfg& cfg, const Env& v, int e, PInfo
         for (int ch = 5 * P + 4; ch < nch; ++ch) row[ch * C + c] = to_obs<T>(0.f);
       }
     }
+    if (obs)
+      for (int i = nch * C + lane; i < cfg.obs_stride; i += 32) row[i] = to_obs<T>(0.f);
   }
-  if (obs)
-    for (int i = nch * C + lane; i < cfg.obs_stride; i += 32) row[i] = to_obs<T>(0.f);
 
   if (mm) {
     if (lane < 4 * P) {
@@ -252,9 +302,23 @@ k_observe(QqtCfg cfg, QqtState st, void* obs, float* danger_out, uint8_t* mm, ui
 
 // ------------------------------------------------------------------ astar
 
-__host__ __device__ inline size_t astar_warp_bytes(int cells) {
+// Per-warp scratch of k_astar: danger, cost, the two fields, threat, own
+// bombs, then 32 prefetched per-env scalars (8 bytes each).
+__host__ __device__ inline size_t astar_pre_off(int cells) {
   return ((size_t)cells * (4 * 4 + 1 + 2) + 15) / 16 * 16 + 64;
 }
+__host__ __device__ inline size_t astar_warp_bytes(int cells) {
+  return astar_pre_off(cells) + 32 * 8;
+}
+
+// Prefetch slots of k_astar (one global load per lane, issued before the
+// tile staging): the scoring that follows the relaxation is serial on lane
+// 0, and without this every scalar it reads would expose a load latency.
+enum {
+  AP_TIMER = 0, AP_MODE = 1, AP_NEW_MODE = 2, AP_NEW_TIMER = 3,
+  AP_PY = 4, AP_PX = 8, AP_ALIVE = 12,              // + player (QQT_MAX_P slots each)
+  AP_CAP = 16, AP_NOISE = 17, AP_MM = 22, AP_BM = 27
+};
 
 // Two multi-source path fields to their common fixed point: row sweeps
 // (left->right, right->left) then column sweeps, repeated until no value
@@ -433,10 +497,46 @@ k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const fl
   const int h = cfg.height, w = cfg.width, C = h * w, N = cfg.n_envs, P = cfg.n_players;
   const int e0 = blockIdx.x * QQT_TILE_E;
   const float INF = __int_as_float(0x7f800000);
+  static_assert(QQT_TILE_E == QQT_NWARP, "one env per warp");
+  const int dch = 2 * P + 1;
+  // the env's danger channel (fp16 obs row), cells lane + 32 k
+  constexpr int kDK = (QQT_MAX_CELLS + 31) / 32;
+  float dpre[kDK];
+  const bool dpre_ok = C <= 32 * 6;
+#pragma unroll
+  for (int k = 0; k < kDK; ++k) dpre[k] = 0.f;
+  if (dpre_ok && e0 + warp_id() < N) {
+    const __half* orow = obs + (size_t)(e0 + warp_id()) * cfg.obs_stride + (size_t)dch * C;
+#pragma unroll
+    for (int k = 0; k < 6; ++k) {
+      const int c = lane_id() + 32 * k;
+      if (c < C) dpre[k] = __half2float(orow[c]);
+    }
+  }
+  uint64_t pre_v = 0;
+  {
+    const int e = e0 + warp_id(), l = lane_id();
+    if (e < N) {
+      if (l == AP_TIMER && mode_arr) pre_v = (uint64_t)timer_arr[e];
+      else if (l == AP_MODE && mode_arr) pre_v = (uint64_t)mode_arr[e];
+      else if (l == AP_NEW_MODE && mode_arr && tick16) pre_v = (uint64_t)new_mode[e];
+      else if (l == AP_NEW_TIMER && mode_arr && tick16) pre_v = (uint64_t)new_timer[e];
+      else if (l >= AP_PY && l < AP_PY + P) pre_v = __float_as_uint(st.pos[((size_t)(l - AP_PY) * 2) * N + e]);
+      else if (l >= AP_PX && l < AP_PX + P) pre_v = __float_as_uint(st.pos[((size_t)(l - AP_PX) * 2 + 1) * N + e]);
+      else if (l >= AP_ALIVE && l < AP_ALIVE + P) pre_v = st.alive[(size_t)(l - AP_ALIVE) * N + e];
+      else if (l == AP_CAP) pre_v = (uint64_t)st.blast_cap[(size_t)pid * N + e];
+      else if (l >= AP_NOISE && l < AP_NOISE + 5) pre_v = __float_as_uint(noise[(size_t)e * 5 + (l - AP_NOISE)]);
+      else if (l >= AP_MM && l < AP_MM + 5) pre_v = io.mm[(size_t)e * io.mm_stride + (l - AP_MM)];
+      else if (l == AP_BM) pre_v = io.bm[(size_t)e * io.bm_stride + 1];
+    }
+  }
   Tile tile = carve_tile(smem, C);
   load_tile(tile, st, N, e0, PL_WALL | PL_BRICK | PL_OWNER | PL_FUSE);
   __syncthreads();
   uint8_t* wb = smem + tile_bytes(C) + (size_t)warp_id() * astar_warp_bytes(C);
+  uint64_t* pre = (uint64_t*)(wb + astar_pre_off(C));
+  pre[lane_id()] = pre_v;
+  __syncwarp();
   float* d16 = (float*)wb;
   float* cost = d16 + C;
   float* vs = cost + C;
@@ -446,15 +546,17 @@ k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const fl
   const int lane = lane_id();
   const int cap_max = *cap_max_ptr;
   const int G = cfg.growth_blast_max;
-  const int dch = 2 * P + 1;
 
   for (int s = warp_id(); s < QQT_TILE_E; s += QQT_NWARP) {
     const int e = e0 + s;
     if (e >= N) break;
     const Env v = env_view(tile, s, h, w);
     const __half* orow = obs + (size_t)e * cfg.obs_stride + (size_t)dch * C;
-    for (int c = lane; c < C; c += 32) {
-      const float d = __half2float(orow[c]);
+#pragma unroll
+    for (int k = 0; k < kDK; ++k) {
+      const int c = lane + 32 * k;
+      if (c >= C) break;
+      const float d = dpre_ok ? dpre[k] : __half2float(orow[c]);
       d16[c] = d;
       const bool blk = v.wall[c] || v.brick[c] || v.fuse[c] > 0;
       cost[c] = blk ? INF : __fadd_rn(1.f, __fmul_rn(2.f, d));
@@ -474,9 +576,9 @@ k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const fl
     __syncwarp();
     if (lane == 0) {
       for (int o = 0; o < P; ++o) {
-        if (o == pid || !st.alive[(size_t)o * N + e]) continue;
-        const int ro = min(max((int)floorf(st.pos[((size_t)o * 2) * N + e]), 0), h - 1);
-        const int co = min(max((int)floorf(st.pos[((size_t)o * 2 + 1) * N + e]), 0), w - 1);
+        if (o == pid || !pre[AP_ALIVE + o]) continue;
+        const int ro = min(max((int)floorf(__uint_as_float((uint32_t)pre[AP_PY + o])), 0), h - 1);
+        const int co = min(max((int)floorf(__uint_as_float((uint32_t)pre[AP_PX + o])), 0), w - 1);
         vo[ro * w + co] = 0.f;
       }
     }
@@ -493,32 +595,32 @@ k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const fl
       int mode = 0;
       bool has_mode = mode_arr != nullptr;
       if (has_mode) {
-        int64_t tm = timer_arr[e] - 1;
-        int64_t md = mode_arr[e];
+        int64_t tm = (int64_t)pre[AP_TIMER] - 1;
+        int64_t md = (int64_t)pre[AP_MODE];
         if (tick16 && tm <= 0) {
-          md = new_mode[e];
-          tm = new_timer[e];
+          md = (int64_t)pre[AP_NEW_MODE];
+          tm = (int64_t)pre[AP_NEW_TIMER];
         }
         timer_arr[e] = tm;
         mode_arr[e] = md;
         mode = (int)md;
       }
-      const float py = st.pos[((size_t)pid * 2) * N + e], px = st.pos[((size_t)pid * 2 + 1) * N + e];
+      const float py = __uint_as_float((uint32_t)pre[AP_PY + pid]);
+      const float px = __uint_as_float((uint32_t)pre[AP_PX + pid]);
       const int r = min(max((int)floorf(py), 0), h - 1), c = min(max((int)floorf(px), 0), w - 1);
       const float own_dng = d16[r * w + c];
       const int cr[5] = {max(r - 1, 0), min(r + 1, h - 1), r, r, r};
       const int ccs[5] = {c, c, max(c - 1, 0), min(c + 1, w - 1), c};
       float vopp_c[5], vsafe_c[5], dng_c[5], thr_c[5], nz[5];
       bool legal[5];
-      const uint8_t* mrow = io.mm + (size_t)e * io.mm_stride;
       for (int k = 0; k < 5; ++k) {
         const int q = cr[k] * w + ccs[k];
         vopp_c[k] = vo[q];
         vsafe_c[k] = vs[q];
         dng_c[k] = d16[q];
         thr_c[k] = threat[q] ? 1.f : 0.f;
-        legal[k] = mrow[k] && !(v.wall[q] || v.brick[q]);
-        nz[k] = __fmul_rn(0.05f, noise[(size_t)e * 5 + k]);
+        legal[k] = pre[AP_MM + k] && !(v.wall[q] || v.brick[q]);
+        nz[k] = __fmul_rn(0.05f, __uint_as_float((uint32_t)pre[AP_NOISE + k]));
       }
       float app[5], esc[5], score[5];
       bool app_ok = false;
@@ -557,12 +659,12 @@ k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const fl
         const int fm = argmin5(dmv);
         move = dmv[fm] < INF ? fm : argmin5(dl);
       }
-      const int64_t cap = st.blast_cap[(size_t)pid * N + e];
+      const int64_t cap = (int64_t)pre[AP_CAP];
       long long dr_o = 1000000000LL, dc_o = 1000000000LL;
       for (int o = 0; o < P; ++o) {
-        if (o == pid || !st.alive[(size_t)o * N + e]) continue;
-        const int ro = min(max((int)floorf(st.pos[((size_t)o * 2) * N + e]), 0), h - 1);
-        const int co = min(max((int)floorf(st.pos[((size_t)o * 2 + 1) * N + e]), 0), w - 1);
+        if (o == pid || !pre[AP_ALIVE + o]) continue;
+        const int ro = min(max((int)floorf(__uint_as_float((uint32_t)pre[AP_PY + o])), 0), h - 1);
+        const int co = min(max((int)floorf(__uint_as_float((uint32_t)pre[AP_PX + o])), 0), w - 1);
         dr_o = llabs((long long)(r - ro));
         dc_o = llabs((long long)(c - co));
       }
@@ -577,12 +679,12 @@ k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const fl
           const int f = v.fuse[rr * w + c2];
           if (f > 0 && f <= 10) chain = true;
         }
-      const bool can = io.bm[(size_t)e * io.bm_stride + 1] != 0;
+      const bool can = pre[AP_BM] != 0;
       bool can_escape = false;
       for (int k = 0; k < 5; ++k) can_escape |= legal[k] && dng_c[k] < 0.35f && thr_c[k] == 0.f;
       bool place = can && (aligned || near || chain) && own_dng < 0.2f && can_escape;
       if (has_mode && mode == 1) place = can && (aligned || near) && own_dng < 0.2f && can_escape;
-      const bool alive = st.alive[(size_t)pid * N + e] != 0;
+      const bool alive = pre[AP_ALIVE + pid] != 0;
       io.act[(size_t)e * io.act_stride + 0] = alive ? move : 4;
       io.act[(size_t)e * io.act_stride + 1] = alive ? (place ? 1 : 0) : 0;
     }
@@ -641,7 +743,7 @@ __global__ void k_greedy(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, 
   for (int k = 0; k < 5; ++k) {
     const int q = cr[k] * w + ccs[k];
     dng[k] = __half2float(drow[q]);
-    blk[k] = st.wall[(size_t)q * N + e] || st.brick[(size_t)q * N + e];
+    blk[k] = st.wall[(size_t)e * C + q] || st.brick[(size_t)e * C + q];
     dist[k] = 1e9f;
   }
   for (int o = 0; o < P; ++o) {

@@ -27,14 +27,18 @@ struct PShared {
   int64_t bombs_cap, blast_cap;
 };
 
-// Per-warp scratch layout (byte offsets, 16-byte aligned sections).
+// Per-warp scratch layout (byte offsets, 16-byte aligned sections).  When
+// the step writes the next observation, the row is staged at offset 0 over
+// the sections that are dead by then (flames, chain lists, danger stage-A
+// arrays, the placement records), so that it leaves the warp as 16-byte
+// stores; the player info and the danger map it reads sit after it.
 struct StepLayout {
-  size_t cov, trig, list, list2, qmask, cur, bombs, ps, pinfo, dng, total;
+  size_t cov, trig, list, list2, qmask, cur, bombs, ps, row, pinfo, dng, total;
 };
 
 __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
 
-__host__ __device__ inline StepLayout step_layout(int cells) {
+__host__ __device__ inline StepLayout step_layout(int cells, size_t row_bytes) {
   StepLayout L;
   L.cov = 0;
   L.trig = align16(L.cov + cells);
@@ -44,13 +48,22 @@ __host__ __device__ inline StepLayout step_layout(int cells) {
   L.cur = align16(L.qmask + ((size_t)(cells + 31) / 32 + 1) * 4);
   L.bombs = align16(L.cur + (size_t)cells * 12);   // cur, front, spread
   L.ps = align16(L.bombs + (size_t)cells * 2);
-  L.pinfo = align16(L.ps + QQT_MAX_P * sizeof(PShared));
+  const size_t dead_end = align16(L.ps + QQT_MAX_P * sizeof(PShared));
+  L.row = 0;
+  L.pinfo = align16(dead_end > row_bytes ? dead_end : row_bytes);
   L.dng = align16(L.pinfo + QQT_MAX_P * sizeof(PInfo));
   L.total = align16(L.dng + (size_t)cells * 4);
   return L;
 }
 
-__host__ __device__ inline size_t step_warp_bytes(int cells) { return step_layout(cells).total; }
+// Observation row bytes staged per warp (0 without the fused observation).
+__host__ __device__ inline size_t step_row_bytes(const QqtCfg& cfg, bool fused_obs) {
+  return fused_obs ? (size_t)cfg.obs_stride * 2 : 0;
+}
+
+__host__ __device__ inline size_t step_warp_bytes(int cells, size_t row_bytes) {
+  return step_layout(cells, row_bytes).total;
+}
 
 enum { PHASE_FULL = 0, PHASE_PLACE = 1, PHASE_AFTER_PLACE = 2 };
 
@@ -80,18 +93,60 @@ __device__ __forceinline__ bool placed_map_at(const PShared* ps, int P, int cell
   return v;
 }
 
-__global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
+__global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ FuseTables ft;
+  // u8 planes (PL_WALL .. PL_RECYCLE) some env of the block changed; only
+  // those are written back (fuse, owner and blast always are)
+  __shared__ unsigned dirty;
   const QqtCfg& cfg = a.cfg;
   const QqtState& st = a.st;
   const int h = cfg.height, w = cfg.width, C = h * w, N = cfg.n_envs, P = cfg.n_players;
   const int e0 = blockIdx.x * QQT_TILE_E;
   const int lane = lane_id();
   Tile tile = carve_tile(smem, C);
+  if (threadIdx.x == 0) dirty = 0;
+  // the warp's env (one per warp): its per-player state and draws are loaded
+  // before the tile so that their latency overlaps the staging
+  static_assert(QQT_TILE_E == QQT_NWARP, "one env per warp");
+  PlayerState me;
+  float env_crate_prob = 0.f;
+  bool env_hazard = false;
+  int64_t act_mv = 0, act_bo = 0;
+  {
+    const int e = e0 + warp_id();
+    const int p = lane;
+    if (e < N) {
+      if (p < P) {
+        const size_t i = (size_t)p * N + e;
+        me.y = st.pos[((size_t)p * 2) * N + e];
+        me.x = st.pos[((size_t)p * 2 + 1) * N + e];
+        me.spd = st.spd_g[i];
+        me.lo_spd = st.lo_spd[i];
+        me.alive0 = st.alive[i];
+        me.hp = st.hp[i];
+        me.since = st.since_bomb[i];
+        me.bombs_cap = st.bombs_cap[i];
+        me.blast_cap = st.blast_cap[i];
+        me.invuln = st.invuln[i];
+        me.pending = st.pending_lost[i];
+        me.combo = st.combo[i];
+        me.last_hit = st.last_hit[i];
+        me.lo_b = st.lo_bombs[i];
+        me.lo_z = st.lo_blast[i];
+        act_mv = a.actions[((size_t)e * P + p) * 2];
+        act_bo = a.actions[((size_t)e * P + p) * 2 + 1];
+        // the rewards' per-tick draws, loaded with the rest of the player state
+        me.rb_hit = cfg.corridor ? a.rb_hit[(size_t)e * P + p] : 0.f;
+        me.rb_grow = cfg.corridor ? a.rb_grow[(size_t)e * P + p] : 0.f;
+      }
+      env_crate_prob = cfg.corridor ? st.crate_prob[e] : 0.f;
+      env_hazard = cfg.crate_speed_only && st.hazard[e];
+    }
+  }
   load_tile(tile, st, N, e0, PL_ALL);
   __syncthreads();
-  const StepLayout L = step_layout(C);
+  const StepLayout L = step_layout(C, step_row_bytes(cfg, a.obs != nullptr));
   uint8_t* wb = smem + tile_bytes(C) + (size_t)warp_id() * L.total;
   uint8_t* cov = wb + L.cov;
   uint8_t* trig = wb + L.trig;
@@ -115,38 +170,14 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
     const int e = e0 + s;
     if (e >= N) break;
     const Env v = env_view(tile, s, h, w);
-    PlayerState me;
     const int p = lane;
     if (p < P) {
-      const size_t i = (size_t)p * N + e;
-      me.y = st.pos[((size_t)p * 2) * N + e];
-      me.x = st.pos[((size_t)p * 2 + 1) * N + e];
-      me.spd = st.spd_g[i];
-      me.lo_spd = st.lo_spd[i];
-      me.alive0 = st.alive[i] != 0;
-      me.hp = st.hp[i];
-      me.since = st.since_bomb[i];
-      me.bombs_cap = st.bombs_cap[i];
-      me.blast_cap = st.blast_cap[i];
-      me.invuln = st.invuln[i];
-      me.pending = st.pending_lost[i];
-      me.combo = st.combo[i];
-      me.last_hit = st.last_hit[i];
-      me.lo_b = st.lo_bombs[i];
-      me.lo_z = st.lo_blast[i];
-      const int64_t mv = a.actions[((size_t)e * P + p) * 2];
-      const int64_t bo = a.actions[((size_t)e * P + p) * 2 + 1];
-      me.move = (int)max(min(mv, (int64_t)1 << 20), -((int64_t)1 << 20));
-      me.bomb = bo == 1 ? 1 : 0;
+      me.alive0 = me.alive0 != 0;
+      me.move = (int)max(min(act_mv, (int64_t)1 << 20), -((int64_t)1 << 20));
+      me.bomb = act_bo == 1 ? 1 : 0;
       me.flat0 = center_cell(me.y, me.x, h, w);
       me.placed = 0;
-      // the rewards' per-tick draws, loaded with the rest of the player state
-      me.rb_hit = cfg.corridor ? a.rb_hit[(size_t)e * P + p] : 0.f;
-      me.rb_grow = cfg.corridor ? a.rb_grow[(size_t)e * P + p] : 0.f;
     }
-    const float env_crate_prob = cfg.corridor ? st.crate_prob[e] : 0.f;
-    const bool env_hazard = cfg.crate_speed_only && st.hazard[e];
-
     // ---- 1-2. countdown and sequential placement
     int ns0 = -1;                     // explosion sources in `list` (-1: not yet)
     if (a.phase != PHASE_AFTER_PLACE) {
@@ -394,9 +425,11 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
     for (int base = 0; base < C; base += 32) {
       const int c = base + lane;
       bool bomb = false;
+      bool burnt = false;
       if (c < C) {
         if (cov[c]) {
-          if (cfg.corridor && v.brick[c]) v.crate[c] = 1;
+          burnt = v.brick[c] != 0;
+          if (cfg.corridor && burnt) v.crate[c] = 1;
           v.brick[c] = 0;
         }
         if (trig[c]) {
@@ -408,6 +441,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
         const int o = v.owner[c];
         if (bomb && o >= 0 && o < P) post_cnt[o]++;
       }
+      if (__any_sync(QQT_FULL, burnt) && lane == 0) atomicOr(&dirty, PL_BRICK | PL_CRATE);
       const unsigned m = __ballot_sync(QQT_FULL, bomb);
       if (bomb) ds.bombs[nb_post + __popc(m & ((1u << lane) - 1u))] = (uint16_t)c;
       nb_post += __popc(m);
@@ -467,9 +501,10 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
       }
     }
     __syncwarp();
-    if (cfg.corridor && p < P) {
+    if (cfg.corridor && p < P && (v.crate[flat1] || v.recycle[flat1])) {
       v.crate[flat1] = 0;
       v.recycle[flat1] = 0;
+      atomicOr(&dirty, PL_CRATE | PL_RECYCLE);
     }
     __syncwarp();
     // danger standing penalty on the post-step state (sim/torch_sim.py:1163-1182)
@@ -534,8 +569,8 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
     }
     if (a.out.covered || a.out.triggered) {
       for (int c = lane; c < C; c += 32) {
-        if (a.out.covered) a.out.covered[(size_t)c * N + e] = cov[c];
-        if (a.out.triggered) a.out.triggered[(size_t)c * N + e] = trig[c];
+        if (a.out.covered) a.out.covered[(size_t)e * C + c] = cov[c];
+        if (a.out.triggered) a.out.triggered[(size_t)e * C + c] = trig[c];
       }
     }
 
@@ -543,8 +578,9 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
     int64_t t_out = t1;
     if (done && a.has_tmpl) {
       const QqtTemplate& tp = a.tmpl;
+      if (lane == 0) atomicOr(&dirty, PL_ALL);
       for (int c = lane; c < C; c += 32) {
-        const size_t g = (size_t)c * N + e;
+        const size_t g = (size_t)e * C + c;
         v.wall[c] = tp.wall[g];
         v.brick[c] = tp.brick[g];
         v.crate[c] = tp.crate ? tp.crate[g] : 0;
@@ -593,7 +629,8 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
 #pragma unroll
       for (int q = 0; q < QQT_MAX_P; ++q) live[q] = reset ? 0 : warp_sum(post_cnt[q]);
       observe_env<__half>(cfg, v, e, pinfo, dng, live, me.y, me.x, alive != 0, me.invuln,
-                          me.bombs_cap, t_out, ft, a.obs, nullptr, a.mm, a.bm);
+                          me.bombs_cap, t_out, ft, a.obs, nullptr, a.mm, a.bm,
+                          (__half*)(wb + L.row));
     }
     if (p < P) {
       const size_t i = (size_t)p * N + e;
@@ -619,8 +656,8 @@ __global__ void __launch_bounds__(QQT_NWARP * 32) k_step(StepParams a) {
     __syncwarp();
   }
   __syncthreads();
-  const unsigned planes = a.phase == PHASE_PLACE ? (PL_FUSE | PL_OWNER | PL_BLAST)
-                                                  : (a.has_tmpl ? PL_ALL : (PL_ALL & ~PL_WALL));
+  const unsigned planes = (PL_FUSE | PL_OWNER | PL_BLAST) |
+                          (a.phase == PHASE_PLACE ? 0u : dirty);
   store_tile(tile, st, N, e0, planes);
 }
 
@@ -653,7 +690,7 @@ __global__ void k_flush_recycle(QqtCfg cfg, QqtState st, ExclBits ex, uint64_t s
       const int c = lane + 32 * i;
       float k = 2.f;                                    // 2 = not available
       if (c < C) {
-        const size_t g = (size_t)c * N + e;
+        const size_t g = (size_t)e * C + c;
         if (!st.wall[g] && !st.brick[g] && !((ex.w[c >> 5] >> (c & 31)) & 1u)) {
           k = hash_uniform(key + (uint64_t)c);
           ++nav;
@@ -683,7 +720,7 @@ __global__ void k_flush_recycle(QqtCfg cfg, QqtState st, ExclBits ex, uint64_t s
         }
       }
       if ((bc & 31) == lane) {
-        const size_t g = (size_t)bc * N + e;
+        const size_t g = (size_t)e * C + bc;
         st.crate[g] = 1;
         st.recycle[g] = 1;
 #pragma unroll
@@ -757,7 +794,7 @@ static int launch_step(const QqtCfg* cfg, const QqtState* st, const int64_t* act
   p.mm = mm;
   p.bm = bm;
   const int C = cfg->height * cfg->width;
-  const size_t sm = tile_bytes(C) + QQT_NWARP * step_warp_bytes(C);
+  const size_t sm = tile_bytes(C) + QQT_NWARP * step_warp_bytes(C, step_row_bytes(*cfg, obs != nullptr));
   cudaFuncSetAttribute(k_step, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   const int blocks = (cfg->n_envs + QQT_TILE_E - 1) / QQT_TILE_E;
   cudaStream_t s = (cudaStream_t)stream;

@@ -1,11 +1,13 @@
 """B200Sim: the reference `BatchedSim` API on the B200 kernels.
 
-State lives on the device in structure-of-arrays layout with the env index
-innermost: planes are [H*W][N], per-player arrays [P][N], positions
-[P][2][N].  The public attributes (`sim.fuse`, `sim.pos`, ...) are strided
-torch views with the reference's shapes ((N,H,W), (N,P), (N,P,2)), so bots,
-tests and callers that index or poke them work unchanged and without copies;
-assigning to an attribute copies into the device buffer.
+State lives on the device with env-major planes [N][H*W] (a warp simulates
+one env and reads its planes as one contiguous run; a block of 8 envs
+stages 8 consecutive rows), per-player arrays [P][N] and positions
+[P][2][N].  The public attributes (`sim.fuse`, `sim.pos`, ...) are torch
+views with the reference's shapes ((N,H,W), (N,P), (N,P,2)) -- the planes
+plain contiguous tensors -- so bots, tests and callers that index or poke
+them work unchanged and without copies; assigning to an attribute copies
+into the device buffer.
 
 Per tick the engine runs three library calls (observe, one step, plus the
 policy and bot calls made by the caller); nothing in `observe`, `legal_mask`
@@ -115,7 +117,7 @@ class B200Sim:
         d = self.device
         self._buf = {}
         for k, dt in _PLANES.items():
-            self._buf[k] = torch.zeros((hw, n), dtype=dt, device=d)
+            self._buf[k] = torch.zeros((n, hw), dtype=dt, device=d)
         self._buf["owner"].fill_(-1)
         for k, dt in _PLAYER.items():
             self._buf[k] = torch.zeros((p, n), dtype=dt, device=d)
@@ -146,8 +148,8 @@ class B200Sim:
         self._winner = torch.zeros((n, p), dtype=torch.bool, device=d)
         self._hit = torch.zeros((n, p), dtype=torch.bool, device=d)
         self._n_alive = torch.zeros((n,), dtype=torch.int64, device=d)
-        self._covered = torch.zeros((hw, n), dtype=torch.bool, device=d)
-        self._triggered = torch.zeros((hw, n), dtype=torch.bool, device=d)
+        self._covered = torch.zeros((n, hw), dtype=torch.bool, device=d)
+        self._triggered = torch.zeros((n, hw), dtype=torch.bool, device=d)
         self._reset_mask = torch.zeros((n,), dtype=torch.bool, device=d)
         self._tiers = torch.full((1,), -1, dtype=torch.int32, device=d)
         self._first_step = True
@@ -166,7 +168,7 @@ class B200Sim:
         b = self._buf[key]
         n, cfg = self.num_envs, self.cfg
         if key in _PLANES:
-            return b.t().view(n, cfg.height, cfg.width)
+            return b.view(n, cfg.height, cfg.width)
         if key in _PLAYER:
             return b.t()
         if key == "pos":
@@ -210,10 +212,10 @@ class B200Sim:
         d = self.device
         T = lambda a, dt: torch.as_tensor(np.asarray(a)).to(d, dt)  # noqa: E731
         tm = {
-            "wall": T(template["wall"], torch.bool).reshape(n, hw).t().contiguous(),
-            "brick": T(template["brick"], torch.bool).reshape(n, hw).t().contiguous(),
+            "wall": T(template["wall"], torch.bool).reshape(n, hw).contiguous(),
+            "brick": T(template["brick"], torch.bool).reshape(n, hw).contiguous(),
             "crate": T(template.get("crate", np.zeros((n, hw), bool)), torch.bool)
-            .reshape(n, hw).t().contiguous(),
+            .reshape(n, hw).contiguous(),
             "spawn": T(template["spawn"], torch.float32).permute(1, 2, 0).contiguous(),
             "bombs_cap": T(template["bombs_cap"], torch.int64).t().contiguous(),
             "blast_cap": T(template["blast_cap"], torch.int64).t().contiguous(),
@@ -239,12 +241,12 @@ class B200Sim:
         if idx.numel() == 0:
             return
         for k in ("wall", "brick"):
-            b[k][:, idx] = tm[k][:, idx]
-        b["crate"][:, idx] = tm["crate"][:, idx]
-        b["_recycle_crate"][:, idx] = False
-        b["fuse"][:, idx] = 0
-        b["owner"][:, idx] = -1
-        b["bomb_blast"][:, idx] = 0
+            b[k][idx] = tm[k][idx]
+        b["crate"][idx] = tm["crate"][idx]
+        b["_recycle_crate"][idx] = False
+        b["fuse"][idx] = 0
+        b["owner"][idx] = -1
+        b["bomb_blast"][idx] = 0
         b["pos"][:, :, idx] = tm["spawn"][:, :, idx]
         b["bombs_cap"][:, idx] = tm["bombs_cap"][:, idx]
         b["blast_cap"][:, idx] = tm["blast_cap"][:, idx]
@@ -257,13 +259,13 @@ class B200Sim:
 
     def _reset_common(self, idx) -> None:
         b, cfg = self._buf, self.cfg
-        b["_recycle_crate"][:, idx] = False
+        b["_recycle_crate"][idx] = False
         b["_pending_lost"][:, idx] = 0
         b["_combo"][:, idx] = 0
         b["_last_hit"][:, idx] = -10 ** 9
-        b["fuse"][:, idx] = 0
-        b["owner"][:, idx] = -1
-        b["bomb_blast"][:, idx] = 0
+        b["fuse"][idx] = 0
+        b["owner"][idx] = -1
+        b["bomb_blast"][idx] = 0
         b["alive"][:, idx] = True
         b["hp"][:, idx] = cfg.max_hp
         b["since_bomb"][:, idx] = cfg.place_dist_cooldown
@@ -302,10 +304,10 @@ class B200Sim:
         idx = idx_cpu.to(d)
         hw, p, gen = cfg.n_cells, cfg.n_players, self.gen
         b["_is_open"][idx] = False
-        put = lambda key, rows, val: b[key].__setitem__((slice(None), rows), val)  # noqa: E731
+        put = lambda key, rows, val: b[key].__setitem__(rows, val)  # noqa: E731
         if cfg.map_mode != "corridor":
             wall = mapgen.open_obstacles(cfg, count, gen)
-            put("wall", idx, wall.reshape(count, hw).t().to(d))
+            put("wall", idx, wall.reshape(count, hw).to(d))
             put("brick", idx, False)
             b0 = torch.full((count,), float(cfg.max_bombs))
             z0 = torch.full((count,), float(cfg.blast))
@@ -358,8 +360,8 @@ class B200Sim:
                 self._fill_caps(bcap, zcap, scap, is_corr, idx, cfg.growth_bombs_start,
                                 cfg.growth_blast_start, cfg.growth_speed_start)
                 cprob[is_corr] = cfg.growth_crate_prob
-            put("wall", idx, wall.reshape(count, hw).t().to(d))
-            put("brick", idx, brick.reshape(count, hw).t().to(d))
+            put("wall", idx, wall.reshape(count, hw).to(d))
+            put("brick", idx, brick.reshape(count, hw).to(d))
             b["bombs_cap"][:, idx] = bcap.t().to(d)
             b["blast_cap"][:, idx] = zcap.t().to(d)
             b["spd_g"][:, idx] = scap.t().to(d)
@@ -382,14 +384,14 @@ class B200Sim:
             pos[sw, 0] = pos[sw, 1]
             pos[sw, 1] = tmp
         b["pos"][:, :, idx] = pos.permute(1, 2, 0).to(d)
-        b["crate"][:, idx] = False
+        b["crate"][idx] = False
         self._reset_common(idx)
         if cfg.open_crate_cross and cfg.map_mode == "corridor":
             open_idx = idx[b["_is_open"][idx]]
             if open_idx.numel():
                 cells = torch.tensor([r * cfg.width + c for r, c in mapgen.open_cross_cells(cfg)],
                                      dtype=torch.long, device=d)
-                b["crate"][cells.unsqueeze(1), open_idx.unsqueeze(0)] = True
+                b["crate"][open_idx.unsqueeze(1), cells.unsqueeze(0)] = True
         if cfg.hazard_fraction > 0:
             hz = torch.rand(count, generator=gen) < cfg.hazard_fraction
             b["_hazard"][idx] = hz.to(d)
@@ -545,8 +547,8 @@ class B200Sim:
         self._first_step = False
         n, h, w = self.num_envs, self.cfg.height, self.cfg.width
         info = {"n_alive": self._n_alive, "died": self._died, "winner": self._winner, "hit": hit,
-                "blast": self._covered.t().view(n, h, w),
-                "trig": self._triggered.t().view(n, h, w)}
+                "blast": self._covered.view(n, h, w),
+                "trig": self._triggered.view(n, h, w)}
         if auto_reset and not dev_reset:
             if bool(done.any()):
                 info = {k: v.clone() for k, v in info.items()}
@@ -585,7 +587,7 @@ class B200Sim:
             if idx.numel() == 0:
                 continue
             idx_d = idx.to(self.device)
-            avail = (~self._buf["wall"][:, idx_d] & ~self._buf["brick"][:, idx_d]).t().cpu()
+            avail = (~self._buf["wall"][idx_d] & ~self._buf["brick"][idx_d]).cpu()
             avail[:, excl] = False
             rows, cols = [], []
             for i, e in enumerate(idx.tolist()):
@@ -599,8 +601,8 @@ class B200Sim:
             if rows:
                 r = torch.cat(rows).to(self.device)
                 c = torch.cat(cols).to(self.device)
-                self._buf["crate"][r, c] = True
-                self._buf["_recycle_crate"][r, c] = True
+                self._buf["crate"][c, r] = True
+                self._buf["_recycle_crate"][c, r] = True
         lost.zero_()
 
     def _excl_words(self):
