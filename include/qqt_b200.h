@@ -235,6 +235,19 @@ int qqt_astar_act(const QqtCfg *cfg, const QqtState *st, const void *obs,
                   const int64_t *new_timer, int64_t *act, int32_t act_stride,
                   float *vsafe, float *vopp, void *scratch, qqt_stream_t stream);
 
+/* hunter bot: the astar bot with the crate layer and no mode ticker
+ * (make_bot "hunter" = astar_attack(eat_crates=True), sim/bots.py:557-561,
+ * crate layer sim/bots.py:376-431).  With >= 2 of the seat's bomb / blast /
+ * speed attributes under 70 % of their growth caps, a crate on the board
+ * and the seat alive, it descends a third field V_crate (sources = crate
+ * cells, the same cost and obstacles) unless escaping or no crate is
+ * reachable.  Arguments as qqt_astar_act; vcrate [N][C] may be NULL. */
+int qqt_hunter_act(const QqtCfg *cfg, const QqtState *st, const void *obs,
+                   const uint8_t *mm, int32_t mm_stride, const uint8_t *bm,
+                   int32_t bm_stride, int32_t pid, const float *noise, int64_t *act,
+                   int32_t act_stride, float *vsafe, float *vopp, float *vcrate,
+                   void *scratch, qqt_stream_t stream);
+
 /* random bot (sim/bots.py:36-58): uniform legal move from u_move [N]
  * (inverse CDF over legal entries), bomb when u_bomb [N] < bomb_rate and
  * the bomb mask allows it. */

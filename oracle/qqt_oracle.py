@@ -746,11 +746,15 @@ class ModeTicker:
 
 
 def astar_attack(cfg, st, danger_obs, mm, bm, pid, noise, mode=None, cap_max=None,
-                 return_fields=False):
-    """Danger-aware path-field bot (sim/bots.py:267-508), eat_crates off.
+                 return_fields=False, eat_crates=False):
+    """Danger-aware path-field bot (sim/bots.py:267-508).
 
     cap_max: batch max of blast_cap[:, pid] (the reference's chain scan
-    length, sim/bots.py:484); computed here when None.
+    length, sim/bots.py:484); computed here when None.  eat_crates: the
+    `hunter` bot's crate layer (sim/bots.py:376-431, make_bot "hunter" at
+    sim/bots.py:557-561): with >= 2 of the bomb / blast / speed attributes
+    under 70 % of their growth caps and a crate on the board, descend the
+    crate field (sources = crate cells) instead of approaching.
     """
     n, p = st["alive"].shape
     h, w = cfg.height, cfg.width
@@ -799,6 +803,23 @@ def astar_attack(cfg, st, danger_obs, mm, bm, pid, noise, mode=None, cap_max=Non
     idle_col = np.arange(5) == 4
     esc = np.where(use_esc[:, None] & idle_col[None], inf, esc)
     esc = np.where(legal, esc, inf)
+    v_crate = None
+    if eat_crates:
+        fr = np.stack([st["bombs_cap"][:, pid].astype(F32) / F32(cfg.growth_bombs_max),
+                       st["blast_cap"][:, pid].astype(F32) / F32(cfg.growth_blast_max),
+                       st["spd_g"][:, pid].astype(F32) / F32(cfg.growth_speed_max)], 0)
+        hungry = (fr < F32(0.7)).sum(0) >= 2
+        has_crate = st["crate"].reshape(n, -1).any(1)
+        eat_on = hungry & has_crate & st["alive"][:, pid]
+        v_crate = dijkstra_field(st["crate"], dng2, block_all)
+        vcrate = np.take_along_axis(v_crate, cflat, 1)
+        eat = (vcrate * F32(100.0) + two * dng) + nz
+        eat = np.where(dng >= F32(0.5), inf, eat)
+        eat = np.where(legal, eat, inf)
+        no_idle = np.where(~idle_col[None], eat, inf).min(1)
+        eat = np.where(idle_col[None] & (no_idle[:, None] < eat[:, 4:5]), inf, eat)
+        eat_on = eat_on & np.isfinite(eat.min(1))
+        app = np.where(eat_on[:, None], eat, app)
     score = np.where(use_esc[:, None], esc, app)
     if mode is not None:
         vf = np.minimum(vopp, F32(1e3))
@@ -846,7 +867,7 @@ def astar_attack(cfg, st, danger_obs, mm, bm, pid, noise, mode=None, cap_max=Non
     out = np.stack([np.where(dead, MOVE_IDLE, move),
                     np.where(dead, 0, place.astype(np.int64))], -1)
     if return_fields:
-        return out, v_safe, v_opp
+        return (out, v_safe, v_opp, v_crate) if eat_crates else (out, v_safe, v_opp)
     return out
 
 

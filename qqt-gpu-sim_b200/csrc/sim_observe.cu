@@ -73,7 +73,7 @@ struct FuseTables {
 // channel (consecutive lanes, consecutive elements); the row goes straight to
 // global memory, or, given a 16-byte aligned per-warp `stage` of obs_stride
 // elements, into shared memory first and out as 16-byte stores.
-template <class T>
+template <class T, bool STAGED = false>
 __device__ inline void observe_env(const QqtCfg& cfg, const Env& v, int e, PInfo* pi,
                                    const float* dng, const int* live, float py, float px,
                                    bool alive_p, int64_t inv_p, int64_t bcap_p, int64_t t_e,
@@ -82,7 +82,7 @@ __device__ inline void observe_env(const QqtCfg& cfg, const Env& v, int e, PInfo
   const int h = cfg.height, w = cfg.width, C = h * w, P = cfg.n_players;
   const int lane = lane_id();
   const int nch = cfg.obs_channels;
-  if (stage) __syncwarp();   // the staging area reuses scratch read just before
+  if (STAGED) __syncwarp();   // the staging area reuses scratch read just before
   if (lane < P) {
     const int p = lane;
     PInfo q;
@@ -119,7 +119,7 @@ __device__ inline void observe_env(const QqtCfg& cfg, const Env& v, int e, PInfo
 
   const float tv = __fdiv_rn((float)t_e, cfg.max_steps_f);
   T* const grow = obs ? (T*)obs + (size_t)e * cfg.obs_stride : nullptr;
-  if (obs && stage) {
+  if (STAGED) {
     // staged row: zero it, write the dense channels cell by cell and the
     // sparse ones (position splats, values at each player's cell) at their
     // cells, then move it out as 16-byte stores (row stride and base are
@@ -308,16 +308,19 @@ __host__ __device__ inline size_t astar_pre_off(int cells) {
   return ((size_t)cells * (4 * 4 + 1 + 2) + 15) / 16 * 16 + 64;
 }
 __host__ __device__ inline size_t astar_warp_bytes(int cells) {
-  return astar_pre_off(cells) + 32 * 8;
+  return astar_pre_off(cells) + 48 * 8;
 }
 
 // Prefetch slots of k_astar (one global load per lane, issued before the
 // tile staging): the scoring that follows the relaxation is serial on lane
 // 0, and without this every scalar it reads would expose a load latency.
+// Slots 32..41 keep the candidates' V_opp / V_safe while the hunter's crate
+// field reuses the field arrays.
 enum {
   AP_TIMER = 0, AP_MODE = 1, AP_NEW_MODE = 2, AP_NEW_TIMER = 3,
   AP_PY = 4, AP_PX = 8, AP_ALIVE = 12,              // + player (QQT_MAX_P slots each)
-  AP_CAP = 16, AP_NOISE = 17, AP_MM = 22, AP_BM = 27
+  AP_CAP = 16, AP_NOISE = 17, AP_MM = 22, AP_BM = 27, AP_BCAP = 28, AP_SPD = 29,
+  AP_CAND_OPP = 32, AP_CAND_SAFE = 37
 };
 
 // Two multi-source path fields to their common fixed point: row sweeps
@@ -489,10 +492,14 @@ __device__ __forceinline__ int argmin5(const float* s) {
   return best;
 }
 
+// EAT: the hunter bot (sim/bots.py:557-561): astar with the crate layer
+// (sim/bots.py:376-431) and no mode ticker.
+template <bool EAT>
 __global__ void __launch_bounds__(QQT_NWARP * 32, 3)
 k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const float* noise,
         int64_t* mode_arr, int64_t* timer_arr, int tick16, const int64_t* new_mode,
-        const int64_t* new_timer, float* vsafe_out, float* vopp_out, const int* cap_max_ptr) {
+        const int64_t* new_timer, float* vsafe_out, float* vopp_out, float* vcrate_out,
+        const int* cap_max_ptr) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int h = cfg.height, w = cfg.width, C = h * w, N = cfg.n_envs, P = cfg.n_players;
   const int e0 = blockIdx.x * QQT_TILE_E;
@@ -528,10 +535,12 @@ k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const fl
       else if (l >= AP_NOISE && l < AP_NOISE + 5) pre_v = __float_as_uint(noise[(size_t)e * 5 + (l - AP_NOISE)]);
       else if (l >= AP_MM && l < AP_MM + 5) pre_v = io.mm[(size_t)e * io.mm_stride + (l - AP_MM)];
       else if (l == AP_BM) pre_v = io.bm[(size_t)e * io.bm_stride + 1];
+      else if (EAT && l == AP_BCAP) pre_v = (uint64_t)st.bombs_cap[(size_t)pid * N + e];
+      else if (EAT && l == AP_SPD) pre_v = __float_as_uint(st.spd_g[(size_t)pid * N + e]);
     }
   }
   Tile tile = carve_tile(smem, C);
-  load_tile(tile, st, N, e0, PL_WALL | PL_BRICK | PL_OWNER | PL_FUSE);
+  load_tile(tile, st, N, e0, PL_WALL | PL_BRICK | PL_OWNER | PL_FUSE | (EAT ? PL_CRATE : 0u));
   __syncthreads();
   uint8_t* wb = smem + tile_bytes(C) + (size_t)warp_id() * astar_warp_bytes(C);
   uint64_t* pre = (uint64_t*)(wb + astar_pre_off(C));
@@ -590,6 +599,34 @@ k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const fl
       for (int c = lane; c < C; c += 32) vsafe_out[(size_t)e * C + c] = vs[c];
     if (vopp_out)
       for (int c = lane; c < C; c += 32) vopp_out[(size_t)e * C + c] = vo[c];
+    bool any_crate = false;
+    if (EAT) {
+      // keep the candidates' V_opp / V_safe, then relax V_crate (sources =
+      // crate cells, same cost and obstacles) in the field arrays
+      if (lane < 5) {
+        const int r = min(max((int)floorf(__uint_as_float((uint32_t)pre[AP_PY + pid])), 0), h - 1);
+        const int c = min(max((int)floorf(__uint_as_float((uint32_t)pre[AP_PX + pid])), 0), w - 1);
+        const int rr = lane == 0 ? max(r - 1, 0) : (lane == 1 ? min(r + 1, h - 1) : r);
+        const int cc = lane == 2 ? max(c - 1, 0) : (lane == 3 ? min(c + 1, w - 1) : c);
+        pre[AP_CAND_OPP + lane] = __float_as_uint(vo[rr * w + cc]);
+        pre[AP_CAND_SAFE + lane] = __float_as_uint(vs[rr * w + cc]);
+      }
+      bool mine = false;
+      __syncwarp();
+      for (int c = lane; c < C; c += 32) {
+        const bool cr = v.crate[c] != 0;
+        mine |= cr;
+        vs[c] = cr ? 0.f : INF;
+        vo[c] = INF;
+      }
+      any_crate = __any_sync(QQT_FULL, mine);
+      __syncwarp();
+      const bool conv2 = (h == 13 && w == 13) ? relax_two_reg<13, 13>(vs, vo, cost, 2 * (C + 1))
+                                              : relax_two(vs, vo, cost, h, w, C + 1);
+      if (!conv2 && lane == 0) flag_error(QQT_DEV_NOT_CONVERGED);
+      if (vcrate_out)
+        for (int c = lane; c < C; c += 32) vcrate_out[(size_t)e * C + c] = vs[c];
+    }
 
     if (lane == 0) {
       int mode = 0;
@@ -613,10 +650,18 @@ k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const fl
       const int ccs[5] = {c, c, max(c - 1, 0), min(c + 1, w - 1), c};
       float vopp_c[5], vsafe_c[5], dng_c[5], thr_c[5], nz[5];
       bool legal[5];
+      float vcrate_c[5];
       for (int k = 0; k < 5; ++k) {
         const int q = cr[k] * w + ccs[k];
-        vopp_c[k] = vo[q];
-        vsafe_c[k] = vs[q];
+        if (EAT) {
+          vopp_c[k] = __uint_as_float((uint32_t)pre[AP_CAND_OPP + k]);
+          vsafe_c[k] = __uint_as_float((uint32_t)pre[AP_CAND_SAFE + k]);
+          vcrate_c[k] = vs[q];
+        } else {
+          vopp_c[k] = vo[q];
+          vsafe_c[k] = vs[q];
+          vcrate_c[k] = INF;
+        }
         dng_c[k] = d16[q];
         thr_c[k] = threat[q] ? 1.f : 0.f;
         legal[k] = pre[AP_MM + k] && !(v.wall[q] || v.brick[q]);
@@ -636,8 +681,29 @@ k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const fl
         float x = __fadd_rn(__fadd_rn(__fmul_rn(vsafe_c[k], 100.f), __fmul_rn(2.f, thr_c[k])), nz[k]);
         if ((use_esc && k == 4) || !legal[k]) x = INF;
         esc[k] = x;
-        score[k] = use_esc ? esc[k] : app[k];
       }
+      if (EAT) {
+        // crate layer: >= 2 of the growth attributes under 70 % of their
+        // caps, a crate on the board, alive -> descend V_crate (no idling
+        // when a move is better), unless no crate is reachable
+        const float fb = __fdiv_rn((float)(int64_t)pre[AP_BCAP], (float)cfg.growth_bombs_max);
+        const float fz = __fdiv_rn((float)(int64_t)pre[AP_CAP], (float)cfg.growth_blast_max);
+        const float fs = __fdiv_rn(__uint_as_float((uint32_t)pre[AP_SPD]), cfg.growth_speed_max);
+        const int low = (fb < 0.7f) + (fz < 0.7f) + (fs < 0.7f);
+        bool eat_on = low >= 2 && any_crate && pre[AP_ALIVE + pid] != 0;
+        float eat[5];
+        for (int k = 0; k < 5; ++k) {
+          float x = __fadd_rn(__fadd_rn(__fmul_rn(vcrate_c[k], 100.f), __fmul_rn(2.f, dng_c[k])), nz[k]);
+          if (dng_c[k] >= 0.5f || !legal[k]) x = INF;
+          eat[k] = x;
+        }
+        const float no_idle = fminf(fminf(eat[0], eat[1]), fminf(eat[2], eat[3]));
+        if (no_idle < eat[4]) eat[4] = INF;
+        eat_on = eat_on && fminf(no_idle, eat[4]) < INF;
+        if (eat_on)
+          for (int k = 0; k < 5; ++k) app[k] = eat[k];
+      }
+      for (int k = 0; k < 5; ++k) score[k] = use_esc ? esc[k] : app[k];
       if (has_mode && mode == 1) {
         for (int k = 0; k < 5; ++k) {
           float f = __fadd_rn(__fadd_rn(__fadd_rn(-fminf(vopp_c[k], 1e3f), __fmul_rn(2.f, dng_c[k])),
@@ -827,12 +893,14 @@ static int seat_io(const uint8_t* mm, int32_t mm_stride, const uint8_t* bm, int3
   return QQT_OK;
 }
 
-extern "C" int qqt_astar_act(const QqtCfg* cfg, const QqtState* st, const void* obs,
-                             const uint8_t* mm, int32_t mm_stride, const uint8_t* bm,
-                             int32_t bm_stride, int32_t pid, const float* noise, int64_t* mode,
-                             int64_t* timer, int32_t tick16, const int64_t* new_mode,
-                             const int64_t* new_timer, int64_t* act, int32_t act_stride,
-                             float* vsafe, float* vopp, void* scratch, qqt_stream_t stream) {
+template <bool EAT>
+static int launch_astar(const QqtCfg* cfg, const QqtState* st, const void* obs,
+                        const uint8_t* mm, int32_t mm_stride, const uint8_t* bm,
+                        int32_t bm_stride, int32_t pid, const float* noise, int64_t* mode,
+                        int64_t* timer, int32_t tick16, const int64_t* new_mode,
+                        const int64_t* new_timer, int64_t* act, int32_t act_stride,
+                        float* vsafe, float* vopp, float* vcrate, void* scratch,
+                        qqt_stream_t stream) {
   int rc = check_cfg(cfg);
   if (rc) return rc;
   SeatIO io;
@@ -847,11 +915,32 @@ extern "C" int qqt_astar_act(const QqtCfg* cfg, const QqtState* st, const void* 
   cudaMemsetAsync(capmax, 0, sizeof(int), s);
   k_cap_max<<<min((N + 255) / 256, 148), 256, 0, s>>>(st->blast_cap + (size_t)pid * N, N, capmax);
   const size_t sm = tile_bytes(C) + QQT_NWARP * astar_warp_bytes(C);
-  cudaFuncSetAttribute(k_astar, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-  k_astar<<<(N + QQT_TILE_E - 1) / QQT_TILE_E, QQT_NWARP * 32, sm, s>>>(
+  cudaFuncSetAttribute(k_astar<EAT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  k_astar<EAT><<<(N + QQT_TILE_E - 1) / QQT_TILE_E, QQT_NWARP * 32, sm, s>>>(
       *cfg, *st, (const __half*)obs, io, pid, noise, mode, timer, tick16, new_mode, new_timer,
-      vsafe, vopp, capmax);
+      vsafe, vopp, vcrate, capmax);
   return launch_status();
+}
+
+extern "C" int qqt_astar_act(const QqtCfg* cfg, const QqtState* st, const void* obs,
+                             const uint8_t* mm, int32_t mm_stride, const uint8_t* bm,
+                             int32_t bm_stride, int32_t pid, const float* noise, int64_t* mode,
+                             int64_t* timer, int32_t tick16, const int64_t* new_mode,
+                             const int64_t* new_timer, int64_t* act, int32_t act_stride,
+                             float* vsafe, float* vopp, void* scratch, qqt_stream_t stream) {
+  return launch_astar<false>(cfg, st, obs, mm, mm_stride, bm, bm_stride, pid, noise, mode, timer,
+                             tick16, new_mode, new_timer, act, act_stride, vsafe, vopp, nullptr,
+                             scratch, stream);
+}
+
+extern "C" int qqt_hunter_act(const QqtCfg* cfg, const QqtState* st, const void* obs,
+                              const uint8_t* mm, int32_t mm_stride, const uint8_t* bm,
+                              int32_t bm_stride, int32_t pid, const float* noise, int64_t* act,
+                              int32_t act_stride, float* vsafe, float* vopp, float* vcrate,
+                              void* scratch, qqt_stream_t stream) {
+  return launch_astar<true>(cfg, st, obs, mm, mm_stride, bm, bm_stride, pid, noise, nullptr,
+                            nullptr, 0, nullptr, nullptr, act, act_stride, vsafe, vopp, vcrate,
+                            scratch, stream);
 }
 
 extern "C" int qqt_random_act(const QqtCfg* cfg, const QqtState* st, const uint8_t* mm,

@@ -93,6 +93,9 @@ __device__ __forceinline__ bool placed_map_at(const PShared* ps, int P, int cell
   return v;
 }
 
+// PHASE and OBS (a.obs set: the fused next observation) are compile-time so
+// that each instance carries only its own code.
+template <int PHASE, bool OBS>
 __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ FuseTables ft;
@@ -146,7 +149,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
   }
   load_tile(tile, st, N, e0, PL_ALL);
   __syncthreads();
-  const StepLayout L = step_layout(C, step_row_bytes(cfg, a.obs != nullptr));
+  const StepLayout L = step_layout(C, step_row_bytes(cfg, OBS));
   uint8_t* wb = smem + tile_bytes(C) + (size_t)warp_id() * L.total;
   uint8_t* cov = wb + L.cov;
   uint8_t* trig = wb + L.trig;
@@ -162,8 +165,8 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
   PShared* ps = (PShared*)(wb + L.ps);
   PInfo* pinfo = (PInfo*)(wb + L.pinfo);
   float* dng = (float*)(wb + L.dng);
-  if (a.obs) fuse_tables(ft, a.cfg.fuse_f);
-  const int tiers = a.phase == PHASE_PLACE ? 0 : *a.tiers;
+  if (OBS) fuse_tables(ft, a.cfg.fuse_f);
+  const int tiers = PHASE == PHASE_PLACE ? 0 : *a.tiers;
   const float INF = __int_as_float(0x7f800000);
 
   for (int s = warp_id(); s < QQT_TILE_E; s += QQT_NWARP) {
@@ -180,7 +183,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
     }
     // ---- 1-2. countdown and sequential placement
     int ns0 = -1;                     // explosion sources in `list` (-1: not yet)
-    if (a.phase != PHASE_AFTER_PLACE) {
+    if (PHASE != PHASE_AFTER_PLACE) {
       // one pass: countdown, live bombs per owner, this tick's explosion
       // sources (fuse reached 0, owner set) compacted into `list`
       int cnt[QQT_MAX_P] = {0, 0, 0, 0};
@@ -233,7 +236,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
       }
       __syncwarp();
       if (p < P) me.placed = ps[p].placed;
-      if (a.phase == PHASE_PLACE) {
+      if (PHASE == PHASE_PLACE) {
         if (p < P) a.placed_buf[(size_t)p * N + e] = (uint8_t)me.placed;
         int mb = cfg.blast;
         for (int c = lane; c < C; c += 32) mb = max(mb, (int)v.blast[c]);
@@ -622,13 +625,13 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
     //      tick's observation row and legal masks (sim/obs.py:25-229).  The
     //      danger map reuses the danger-standing stage A (same planes); an
     //      env reset to its template has no bombs.
-    if (a.obs) {
+    if (OBS) {
       const bool reset = done && a.has_tmpl;
       danger_paint(v, ds, reset ? 0 : nb_post, cfg.blast, dng);
       int live[QQT_MAX_P];
 #pragma unroll
       for (int q = 0; q < QQT_MAX_P; ++q) live[q] = reset ? 0 : warp_sum(post_cnt[q]);
-      observe_env<__half>(cfg, v, e, pinfo, dng, live, me.y, me.x, alive != 0, me.invuln,
+      observe_env<__half, true>(cfg, v, e, pinfo, dng, live, me.y, me.x, alive != 0, me.invuln,
                           me.bombs_cap, t_out, ft, a.obs, nullptr, a.mm, a.bm,
                           (__half*)(wb + L.row));
     }
@@ -657,7 +660,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
   }
   __syncthreads();
   const unsigned planes = (PL_FUSE | PL_OWNER | PL_BLAST) |
-                          (a.phase == PHASE_PLACE ? 0u : dirty);
+                          (PHASE == PHASE_PLACE ? 0u : dirty);
   store_tile(tile, st, N, e0, planes);
 }
 
@@ -795,18 +798,22 @@ static int launch_step(const QqtCfg* cfg, const QqtState* st, const int64_t* act
   p.bm = bm;
   const int C = cfg->height * cfg->width;
   const size_t sm = tile_bytes(C) + QQT_NWARP * step_warp_bytes(C, step_row_bytes(*cfg, obs != nullptr));
-  cudaFuncSetAttribute(k_step, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   const int blocks = (cfg->n_envs + QQT_TILE_E - 1) / QQT_TILE_E;
   cudaStream_t s = (cudaStream_t)stream;
+  auto launch = [&](auto kern, int phase) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    p.phase = phase;
+    kern<<<blocks, QQT_NWARP * 32, sm, s>>>(p);
+  };
+  const bool fused = obs != nullptr;
   if (first_step) {
     cudaMemsetAsync(tiers, 0xff, sizeof(int32_t), s);   // -1
-    p.phase = PHASE_PLACE;
-    k_step<<<blocks, QQT_NWARP * 32, sm, s>>>(p);
-    p.phase = PHASE_AFTER_PLACE;
-    k_step<<<blocks, QQT_NWARP * 32, sm, s>>>(p);
+    launch(k_step<PHASE_PLACE, false>, PHASE_PLACE);
+    if (fused) launch(k_step<PHASE_AFTER_PLACE, true>, PHASE_AFTER_PLACE);
+    else launch(k_step<PHASE_AFTER_PLACE, false>, PHASE_AFTER_PLACE);
   } else {
-    p.phase = PHASE_FULL;
-    k_step<<<blocks, QQT_NWARP * 32, sm, s>>>(p);
+    if (fused) launch(k_step<PHASE_FULL, true>, PHASE_FULL);
+    else launch(k_step<PHASE_FULL, false>, PHASE_FULL);
   }
   return launch_status();
 }

@@ -82,6 +82,8 @@ def lib():
             "qqt_astar_act": (c_i32, [P(QqtCfg), P(QqtState), c_p, c_p, c_i32, c_p, c_i32,
                                       c_i32, c_p, c_p, c_p, c_i32, c_p, c_p, c_p, c_i32,
                                       c_p, c_p, c_p, c_p]),
+            "qqt_hunter_act": (c_i32, [P(QqtCfg), P(QqtState), c_p, c_p, c_i32, c_p, c_i32,
+                                       c_i32, c_p, c_p, c_i32, c_p, c_p, c_p, c_p, c_p]),
             "qqt_random_act": (c_i32, [P(QqtCfg), P(QqtState), c_p, c_i32, c_p, c_i32, c_i32,
                                        c_p, c_p, c_f32, c_p, c_i32, c_p]),
             "qqt_greedy_act": (c_i32, [P(QqtCfg), P(QqtState), c_p, c_p, c_i32, c_p, c_i32,

@@ -150,6 +150,40 @@ class AstarBot(_Bot):
         return act
 
 
+class HunterBot(_Bot):
+    """The hunter: astar with the crate layer and no mode ticker
+    (make_bot "hunter", sim/bots.py:557-561; crate layer sim/bots.py:376-431).
+
+    keep_fields=True keeps V_safe, V_opp and V_crate of the last call in
+    .vsafe / .vopp / .vcrate."""
+
+    def __init__(self, sim):
+        super().__init__(sim, "hunter")
+        self._scratch = torch.zeros(64, dtype=torch.uint8, device=sim.device)
+        self.vsafe = self.vopp = self.vcrate = None
+        self.keep_fields = False
+
+    def act(self, obs, mmask, bmask, pid: int, out=None):
+        s = self.sim
+        n, hw = s.num_envs, s.cfg.n_cells
+        keep, mp, ms, bp, bs, act = self._io(mmask, bmask, out)
+        noise = self._take("noise", (n, 5))
+        self._fed = None
+        vs = vo = vc = None
+        if self.keep_fields:
+            if self.vsafe is None:
+                self.vsafe, self.vopp, self.vcrate = (
+                    torch.empty((n, hw), dtype=torch.float32, device=s.device) for _ in range(3))
+            vs, vo, vc = self.vsafe.data_ptr(), self.vopp.data_ptr(), self.vcrate.data_ptr()
+        o = _obs_ptr(s, obs)
+        rc = capi.lib().qqt_hunter_act(ctypes.byref(s._ccfg), ctypes.byref(s._cstate), o, mp, ms,
+                                       bp, bs, pid, noise.data_ptr(), act.data_ptr(),
+                                       act.stride(0), vs, vo, vc, self._scratch.data_ptr(),
+                                       s._stream())
+        capi.check(rc, "qqt_hunter_act")
+        return act
+
+
 def _obs_ptr(sim, obs) -> int:
     """Pointer to a row-padded fp16 observation with the engine's stride."""
     if obs.dtype != torch.float16:
@@ -164,13 +198,15 @@ def _obs_ptr(sim, obs) -> int:
 
 
 def make_bot(sim, kind: str, mode: bool = True, bomb_rate: float = 0.10):
-    """kind in {"random", "greedy", "astar", "idle"} (sim/bots.py:538-562)."""
+    """kind in {"random", "greedy", "astar", "hunter", "idle"} (sim/bots.py:538-562)."""
     if kind == "random":
         return RandomBot(sim, bomb_rate)
     if kind == "greedy":
         return GreedyBot(sim)
     if kind == "astar":
         return AstarBot(sim, mode=mode)
+    if kind == "hunter":
+        return HunterBot(sim)
     if kind == "idle":
         return IdleBot(sim)
     raise ValueError(f"unknown bot kind: {kind}")

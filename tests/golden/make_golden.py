@@ -21,6 +21,9 @@ Outputs (compressed npz, all env-major like the reference tensors):
   traj_cfg2.npz    pillar corridor, MLP learner vs astar, 128 ticks
   traj_cfg4.npz    pillar corridor, self-play MLP (both seats), 64 ticks
   traj_cfg5.npz    pillar corridor, CNN learner vs greedy, 48 ticks
+  traj_hunter.npz  pillar corridor with bricks p=0.3 and crates on 12 % of the
+                   free cells, MLP learner vs the hunter bot (astar with the
+                   crate layer), 128 ticks, with V_crate fields
   stress_cfg3.npz  bomb stress: one idle step, danger/obs/masks, V fields
   ckpt_adapt.npz   adapt_first_conv on seeded models (2 <-> 3 players), and
   ref_ckpt_mlp.pt  a checkpoint written by the reference's save_ckpt
@@ -148,9 +151,19 @@ def rollout(R, cfg, n, ticks, seed, template, learner_arch, opp_kind, rng_seed,
             torch.from_numpy(np.broadcast_to(border, (count, h, w)).copy())
     try:
         sim = ts.BatchedSim(cfg, n, device="cpu", seed=seed)
-        if template == "corridor":
-            wall, brick = scenarios.pillar_corridor(n, h, w, seed=seed)
-            set_state(sim, {"wall": wall, "brick": brick})
+        if template in ("corridor", "sparse_crates"):
+            bp = 0.7 if template == "corridor" else 0.3
+            wall, brick = scenarios.pillar_corridor(n, h, w, seed=seed, brick_p=bp)
+            st0 = {"wall": wall, "brick": brick}
+            if template == "sparse_crates":
+                # crates on 12 % of the free cells (corner L cells kept clear),
+                # so that the hunter's crate layer has targets it can reach
+                keep = np.zeros((h, w), bool)
+                for r, c in scenarios.corner_l_cells(h, w):
+                    keep[r, c] = True
+                crng = np.random.default_rng(seed + 100)
+                st0["crate"] = ~wall & ~brick & ~keep[None] & (crng.random(wall.shape) < 0.12)
+            set_state(sim, st0)
             sp = np.array(scenarios.corner_spawns(cfg), dtype=np.float32)
             sim.pos.copy_(torch.from_numpy(np.broadcast_to(sp, (n, p, 2)).copy()))
         init = state_np(sim)
@@ -185,6 +198,7 @@ def rollout(R, cfg, n, ticks, seed, template, learner_arch, opp_kind, rng_seed,
         obs_ticks, obs_rec, dng_rec = [], [], []
         reset_rec, flush_rec = [], []
         fields_rec = []
+        vcrate_rec = []
         bot_draws = []
         for t in range(ticks):
             obs = sim.observe()
@@ -219,7 +233,7 @@ def rollout(R, cfg, n, ticks, seed, template, learner_arch, opp_kind, rng_seed,
                     acts[:, pid] = a
                     tick_draws[pid] = list(fed.log)
             bot_draws.append(tick_draws)
-            if opp_kind == "astar" and t % 8 == 0:
+            if opp_kind in ("astar", "hunter") and t % 8 == 0:
                 dng = obs.float()[:, 2 * p + 1]
                 blk = sim.wall | sim.brick | (sim.fuse > 0)
                 vs = rbots._dijkstra_field(sim, dng < 0.35, dng, blocked=blk)
@@ -229,6 +243,9 @@ def rollout(R, cfg, n, ticks, seed, template, learner_arch, opp_kind, rng_seed,
                 src.view(n, -1)[torch.arange(n), r0 * w + c0] = sim.alive[:, 0]
                 vo = rbots._dijkstra_field(sim, src, dng, blocked=blk)
                 fields_rec.append((t, vs.numpy().copy(), vo.numpy().copy()))
+                if opp_kind == "hunter":
+                    vc = rbots._dijkstra_field(sim, sim.crate, dng, blocked=blk)
+                    vcrate_rec.append(vc.numpy().copy())
             rb = rng.random((2, n, p)).astype(np.float32)
             buf = np.zeros(n * (2 * p + 1), dtype=np.float32)
             buf[: n * p] = rb[0].reshape(-1)
@@ -283,6 +300,8 @@ def rollout(R, cfg, n, ticks, seed, template, learner_arch, opp_kind, rng_seed,
         out["field_ticks"] = np.array([t for t, _, _ in fields_rec])
         out["vsafe"] = np.stack([a for _, a, _ in fields_rec])
         out["vopp"] = np.stack([b for _, _, b in fields_rec])
+    if vcrate_rec:
+        out["vcrate"] = np.stack(vcrate_rec)
     # bot draws per tick and seat, flattened in call order
     for pid in (0, 1):
         kinds = []
@@ -564,6 +583,8 @@ def main():
                                      "mlp", "self", rng_seed=14, obs_every=8),
         "traj_cfg5": lambda: rollout(R, SC(**scenarios.CFG2), 8, 48, 3, "corridor",
                                      "cnn", "greedy", rng_seed=13, obs_every=8),
+        "traj_hunter": lambda: rollout(R, SC(**scenarios.CFG2), 24, 128, 2, "sparse_crates",
+                                       "mlp", "hunter", rng_seed=15, obs_every=8),
         "stress_cfg3": lambda: stress(R, SC(**scenarios.CFG1), 48, 5),
         "reset_modes": lambda: reset_modes(R),
         "ppo_update": lambda: ppo_golden(R),

@@ -20,7 +20,7 @@ pytestmark = pytest.mark.gpu
 
 if torch.cuda.is_available():
     from qqt_b200 import scenarios
-    from qqt_b200.bots import AstarBot, GreedyBot, RandomBot
+    from qqt_b200.bots import AstarBot, GreedyBot, HunterBot, RandomBot
     from qqt_b200.config import SimConfig
     from qqt_b200.sim import B200Sim
     from qqt_b200 import _capi
@@ -80,8 +80,9 @@ def _replay(name, cfg, learner, opp, bomb_rate=0.05, field_check=False):
             continue
         kind = "random" if (pid == 0 or opp == "random") else opp
         bots[pid] = {"random": lambda: RandomBot(sim, bomb_rate), "greedy": lambda: GreedyBot(sim),
-                     "astar": lambda: AstarBot(sim, mode=True)}[kind]()
-        if kind == "astar":
+                     "astar": lambda: AstarBot(sim, mode=True),
+                     "hunter": lambda: HunterBot(sim)}[kind]()
+        if kind in ("astar", "hunter"):
             bots[pid].keep_fields = field_check
     for t in range(T):
         obs, mm, bm = sim.observe_and_mask()
@@ -93,8 +94,8 @@ def _replay(name, cfg, learner, opp, bomb_rate=0.05, field_check=False):
             draws = G.bot_draws(g, pid, t)
             if isinstance(bot, RandomBot):
                 bot.feed(u_move=draws[0][1][:, 0], u_bomb=draws[1][1])
-            elif isinstance(bot, GreedyBot):
-                bot.feed(noise=draws[0][1])
+            elif isinstance(bot, (GreedyBot, HunterBot)):
+                bot.feed(noise=[v for k, v in draws if k == "rand"][0])
             else:
                 ints = [v for k, v in draws if k == "randint"]
                 noise = [v for k, v in draws if k == "rand"][0]
@@ -114,6 +115,8 @@ def _replay(name, cfg, learner, opp, bomb_rate=0.05, field_check=False):
                 i = field_ticks.index(t)
                 assert np.array_equal(_np(bot.vsafe), g["vsafe"][i]), f"{name} t={t}: V_safe"
                 assert np.array_equal(_np(bot.vopp), g["vopp"][i]), f"{name} t={t}: V_opp"
+                if "vcrate" in g:
+                    assert np.array_equal(_np(bot.vcrate), g["vcrate"][i]), f"{name} t={t}: V_crate"
         acts = torch.from_numpy(g["actions"][t]).cuda()
         rb = (torch.from_numpy(g["rb_hit"][t]).cuda(), torch.from_numpy(g["rb_grow"][t]).cuda())
         r, d, info = sim.step(acts, auto_reset=False, crate_draws=rb)
@@ -143,6 +146,10 @@ def test_traj_cfg1_random_bots_gpu():
 
 def test_traj_cfg2_astar_gpu():
     _replay("traj_cfg2", SimConfig(**scenarios.CFG2), "mlp", "astar", field_check=True)
+
+
+def test_traj_hunter_gpu():
+    _replay("traj_hunter", SimConfig(**scenarios.CFG2), "mlp", "hunter", field_check=True)
 
 
 def test_traj_cfg5_greedy_gpu():

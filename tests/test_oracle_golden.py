@@ -54,6 +54,10 @@ def _bot_act(kind, cfg, st, obs16, mm, bm, pid, draws, ticker, bomb_rate):
                                u_move, u_bomb, bomb_rate)
     if kind == "greedy":
         return O.greedy_attack(cfg, st, dng, mm[:, pid], bm[:, pid], pid, draws[0][1])
+    if kind == "hunter":
+        noise = [v for k, v in draws if k == "rand"][0]
+        return O.astar_attack(cfg, st, dng, mm[:, pid], bm[:, pid], pid, noise, mode=None,
+                              eat_crates=True)
     if kind == "astar":
         ints = [v for k, v in draws if k == "randint"]
         noise = [v for k, v in draws if k == "rand"][0]
@@ -133,7 +137,7 @@ def replay(name, cfg, learner, opp, bomb_rate=0.05, check_every_state=True):
 
 
 def _seed_of(name):
-    return {"traj_cfg2": 1, "traj_cfg4": 4, "traj_cfg5": 3}.get(name, 0)
+    return {"traj_cfg2": 1, "traj_cfg4": 4, "traj_cfg5": 3, "traj_hunter": 2}.get(name, 0)
 
 
 def test_traj_cfg1_random_bots():
@@ -199,3 +203,40 @@ def test_traj_cfg2_dijkstra_fields():
         src[np.arange(n), r0 * w + c0] = st["alive"][:, 0]
         vo = O.dijkstra_field(src.reshape(n, h, w), d16, blk)
         assert np.array_equal(vs, g["vsafe"][i]) and np.array_equal(vo, g["vopp"][i])
+
+
+def test_traj_hunter_mlp_vs_hunter():
+    """The hunter bot (astar with the crate layer, sim/bots.py:376-431,
+    557-561) replayed tick by tick against the reference's trajectory."""
+    stats = replay("traj_hunter", SimConfig(**scenarios.CFG2), "mlp", "hunter")
+    assert stats["logit_err"] < 1e-4
+    assert stats["act_mismatch"] == 0
+
+
+def test_traj_hunter_crate_fields_and_eat_branch():
+    """V_crate (sources = crate cells) bit-exact at the recorded ticks, and
+    the crate branch decides some of the hunter's moves in this trajectory."""
+    g = G.load("traj_hunter")
+    cfg = SimConfig(**scenarios.CFG2)
+    wall = g["init_wall"]
+    eat_moves = 0
+    for i, t in enumerate(g["field_ticks"]):
+        st = G.init_state(g) if t == 0 else G.state_at(g, t - 1, wall)
+        if t > 0 and (t - 1) in list(g["reset_ticks"]):
+            continue
+        if t > 0 and (t - 1) in list(g["flush_ticks"]):      # crates recycled after the step
+            j = list(g["flush_ticks"]).index(t - 1)
+            for k in ("crate", "recycle", "pending_lost"):
+                st[k] = g[f"flush{j}_{k}"].copy()
+        obs, _ = O.observe(cfg, st)
+        d16 = obs.astype(np.float16)[:, 2 * cfg.n_players + 1].astype(np.float32)
+        blk = st["wall"] | st["brick"] | (st["fuse"] > 0)
+        vc = O.dijkstra_field(st["crate"], d16, blk)
+        assert np.array_equal(vc, g["vcrate"][i])
+        mm, bm = O.legal_mask(cfg, st)
+        noise = [v for k, v in G.bot_draws(g, 1, t) if k == "rand"][0]
+        a_eat = O.astar_attack(cfg, st, d16, mm[:, 1], bm[:, 1], 1, noise, eat_crates=True)
+        a_plain = O.astar_attack(cfg, st, d16, mm[:, 1], bm[:, 1], 1, noise)
+        assert np.array_equal(a_eat, g["actions"][t][:, 1])
+        eat_moves += int((a_eat[:, 0] != a_plain[:, 0]).sum())
+    assert eat_moves > 0
