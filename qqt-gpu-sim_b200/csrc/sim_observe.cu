@@ -67,7 +67,7 @@ struct FuseTables {
 
 // One env's observation row, masks and (optionally) danger map from its
 // staged planes (sim/obs.py:25-229), for the warp that owns the env.  Inputs:
-// dng = the env's danger map (sim/blast.py:158-317), live[p] = live bombs of
+// dng = the env's danger map (sim/blast.py:158-317), live_p = live bombs of
 // player p, and for lanes < P that player's position, alive flag,
 // invulnerability and bomb cap.  Lane l computes cell l, l+32, ... of every
 // channel (consecutive lanes, consecutive elements); the row goes straight to
@@ -75,7 +75,7 @@ struct FuseTables {
 // elements, into shared memory first and out as 16-byte stores.
 template <class T, bool STAGED = false>
 __device__ inline void observe_env(const QqtCfg& cfg, const Env& v, int e, PInfo* pi,
-                                   const float* dng, const int* live, float py, float px,
+                                   const float* dng, int live_p, float py, float px,
                                    bool alive_p, int64_t inv_p, int64_t bcap_p, int64_t t_e,
                                    const FuseTables& ft, void* obs, float* danger_out,
                                    uint8_t* mm, uint8_t* bm, T* stage = nullptr) {
@@ -89,7 +89,7 @@ __device__ inline void observe_env(const QqtCfg& cfg, const Env& v, int e, PInfo
     q.y = py;
     q.x = px;
     q.alive = alive_p;
-    q.live = live[p];
+    q.live = live_p;
     const float g = q.alive ? 1.f : 0.f;
     const float fy = fminf(fmaxf(__fsub_rn(q.y, 0.5f), 0.f), (float)(h - 1));
     const float fx = fminf(fmaxf(__fsub_rn(q.x, 0.5f), 0.f), (float)(w - 1));
@@ -232,15 +232,22 @@ __device__ inline void observe_env(const QqtCfg& cfg, const Env& v, int e, PInfo
   __syncwarp();
 }
 
-// Live bombs per owner (fuse > 0, owner in [0, P)), warp-wide.
-__device__ inline void live_counts(const Env& v, int P, int* live) {
-  int cnt[QQT_MAX_P] = {0, 0, 0, 0};
-  for (int c = lane_id(); c < v.cells; c += 32) {
-    const int o = v.owner[c];
-    if (v.fuse[c] > 0 && o >= 0 && o < P) cnt[o]++;
-  }
+// Live bombs (fuse > 0) of player `lane` for lanes < P (0 elsewhere),
+// warp-wide: one ballot per player and 32 cells.
+__device__ inline int live_count_of_lane(const Env& v, int P) {
+  int live[QQT_MAX_P] = {0, 0, 0, 0};
+  for (int base = 0; base < v.cells; base += 32) {
+    const int c = base + lane_id();
+    const int f = c < v.cells ? v.fuse[c] : 0, o = c < v.cells ? v.owner[c] : -1;
 #pragma unroll
-  for (int p = 0; p < QQT_MAX_P; ++p) live[p] = warp_sum(cnt[p]);
+    for (int q = 0; q < QQT_MAX_P; ++q)
+      if (q < P) live[q] += __popc(__ballot_sync(QQT_FULL, f > 0 && o == q));
+  }
+  int mine = 0;
+#pragma unroll
+  for (int q = 0; q < QQT_MAX_P; ++q)
+    if (lane_id() == q) mine = live[q];
+  return mine;
 }
 
 __device__ inline void fuse_tables(FuseTables& ft, float fuse_f) {
@@ -293,8 +300,7 @@ k_observe(QqtCfg cfg, QqtState st, void* obs, float* danger_out, uint8_t* mm, ui
     int max_b = 0;
     const int nb = danger_stage_a(v, ds, cfg.fuse_f, cfg.blast, cfg.danger_rounds, &max_b);
     danger_paint(v, ds, nb, cfg.blast, dng);
-    int live[QQT_MAX_P];
-    live_counts(v, P, live);
+    const int live = live_count_of_lane(v, P);
     observe_env<T>(cfg, v, e, pi, dng, live, g_py, g_px, g_alive != 0, g_inv, g_bcap, g_t, ft,
                    obs, danger_out, mm, bm);
   }

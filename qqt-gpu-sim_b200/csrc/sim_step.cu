@@ -186,28 +186,29 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
     if (PHASE != PHASE_AFTER_PLACE) {
       // one pass: countdown, live bombs per owner, this tick's explosion
       // sources (fuse reached 0, owner set) compacted into `list`
-      int cnt[QQT_MAX_P] = {0, 0, 0, 0};
+      // live bombs per owner: one ballot per player and 32 cells
+      int live[QQT_MAX_P] = {0, 0, 0, 0};
       ns0 = 0;
       for (int base = 0; base < C; base += 32) {
         const int c = base + lane;
         bool src = false;
+        int f = 0, o = -1;
         if (c < C) {
-          int f = v.fuse[c];
+          f = v.fuse[c];
           if (f > 0) v.fuse[c] = (int16_t)(--f);
-          const int o = v.owner[c];
-          if (f > 0 && o >= 0 && o < P) cnt[o]++;
+          o = v.owner[c];
           src = f == 0 && o >= 0;
           cov[c] = 0;
           trig[c] = src ? 1 : 0;
         }
+#pragma unroll
+        for (int q = 0; q < QQT_MAX_P; ++q)
+          if (q < P) live[q] += __popc(__ballot_sync(QQT_FULL, f > 0 && o == q));
         const unsigned m = __ballot_sync(QQT_FULL, src);
         if (src) list[ns0 + __popc(m & ((1u << lane) - 1u))] = (uint16_t)c;
         ns0 += __popc(m);
       }
       if (lane < (C + 31) / 32 + 1) qmask[lane] = 0;   // queue bits and counter
-      int live[QQT_MAX_P];
-#pragma unroll
-      for (int q = 0; q < QQT_MAX_P; ++q) live[q] = warp_sum(cnt[q]);
       if (p < P) {
         ps[p].flat0 = me.flat0;
         ps[p].alive0 = me.alive0;
@@ -217,7 +218,9 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
       }
       __syncwarp();
       if (lane == 0) {
-        for (int q = 0; q < P; ++q) {
+#pragma unroll
+        for (int q = 0; q < QQT_MAX_P; ++q) {
+          if (q >= P) break;
           const int idx = ps[q].flat0;
           const bool ok = ps[q].alive0 && ps[q].bomb && v.fuse[idx] <= 0 && !v.brick[idx] &&
                           (int64_t)live[q] < ps[q].bombs_cap;
@@ -424,11 +427,12 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
     //      exploded bombs are cleared, and the bombs left are compacted for
     //      the danger-standing penalty below
     int nb_post = 0;
-    int post_cnt[QQT_MAX_P] = {0, 0, 0, 0};
+    int post_live[QQT_MAX_P] = {0, 0, 0, 0};
     for (int base = 0; base < C; base += 32) {
       const int c = base + lane;
       bool bomb = false;
       bool burnt = false;
+      int o = -1;
       if (c < C) {
         if (cov[c]) {
           burnt = v.brick[c] != 0;
@@ -441,9 +445,11 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
           v.blast[c] = 0;
         }
         bomb = v.fuse[c] > 0;
-        const int o = v.owner[c];
-        if (bomb && o >= 0 && o < P) post_cnt[o]++;
+        o = v.owner[c];
       }
+#pragma unroll
+      for (int q = 0; q < QQT_MAX_P; ++q)
+        if (q < P) post_live[q] += __popc(__ballot_sync(QQT_FULL, bomb && o == q));
       if (__any_sync(QQT_FULL, burnt) && lane == 0) atomicOr(&dirty, PL_BRICK | PL_CRATE);
       const unsigned m = __ballot_sync(QQT_FULL, bomb);
       if (bomb) ds.bombs[nb_post + __popc(m & ((1u << lane) - 1u))] = (uint16_t)c;
@@ -628,10 +634,11 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
     if (OBS) {
       const bool reset = done && a.has_tmpl;
       danger_paint(v, ds, reset ? 0 : nb_post, cfg.blast, dng);
-      int live[QQT_MAX_P];
+      int my_live = 0;    // live bombs of this lane's player (lanes < P)
 #pragma unroll
-      for (int q = 0; q < QQT_MAX_P; ++q) live[q] = reset ? 0 : warp_sum(post_cnt[q]);
-      observe_env<__half, true>(cfg, v, e, pinfo, dng, live, me.y, me.x, alive != 0, me.invuln,
+      for (int q = 0; q < QQT_MAX_P; ++q)
+        if (lane == q && !reset) my_live = post_live[q];
+      observe_env<__half, true>(cfg, v, e, pinfo, dng, my_live, me.y, me.x, alive != 0, me.invuln,
                           me.bombs_cap, t_out, ft, a.obs, nullptr, a.mm, a.bm,
                           (__half*)(wb + L.row));
     }
