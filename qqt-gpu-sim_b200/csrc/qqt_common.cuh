@@ -505,14 +505,15 @@ __device__ inline float resolve_axis(const Env& v, float coord, float delta, flo
   const int span1 = (int)floorf(__fadd_rn(other, rad));
   const int ra = (int)floorf(__fsub_rn(y, rad)), rb = (int)floorf(__fadd_rn(y, rad));
   const int ca = (int)floorf(__fsub_rn(x, rad)), cb = (int)floorf(__fadd_rn(x, rad));
-  bool hit_lo, hit_hi;
-  if (vertical) {
-    hit_lo = impassable_pair(v, lo, span0, lo, span1, ra, rb, ca, cb);
-    hit_hi = impassable_pair(v, hi, span0, hi, span1, ra, rb, ca, cb);
-  } else {
-    hit_lo = impassable_pair(v, span0, lo, span1, lo, ra, rb, ca, cb);
-    hit_hi = impassable_pair(v, span0, hi, span1, hi, ra, rb, ca, cb);
-  }
+  // the two cells of each probed line: (lead, span0) / (lead, span1) moving
+  // vertically, (span0, lead) / (span1, lead) horizontally; selected rather
+  // than branched, so lanes probing different axes do not diverge
+  const int lo_r0 = vertical ? lo : span0, lo_c0 = vertical ? span0 : lo;
+  const int lo_r1 = vertical ? lo : span1, lo_c1 = vertical ? span1 : lo;
+  const int hi_r0 = vertical ? hi : span0, hi_c0 = vertical ? span0 : hi;
+  const int hi_r1 = vertical ? hi : span1, hi_c1 = vertical ? span1 : hi;
+  const bool hit_lo = impassable_pair(v, lo_r0, lo_c0, lo_r1, lo_c1, ra, rb, ca, cb);
+  const bool hit_hi = impassable_pair(v, hi_r0, hi_c0, hi_r1, hi_c1, ra, rb, ca, cb);
   const bool pos = sgn > 0.f;
   const int first_lead = pos ? hi : lo, second_lead = pos ? lo : hi;
   const bool first_hit = pos ? hit_hi : hit_lo, second_hit = pos ? hit_lo : hit_hi;

@@ -208,14 +208,11 @@ __device__ inline void observe_env(const QqtCfg& cfg, const Env& v, int e, PInfo
       const int p = lane >> 2, d = lane & 3;
       const PInfo& q = pi[p];
       const float dv = (d & 1) ? cfg.step_len : -cfg.step_len;
-      bool moved;
-      if (d < 2) {
-        const float ny = resolve_axis(v, __fadd_rn(q.y, dv), dv, q.x, q.y, q.x, cfg.radius, true);
-        moved = fabsf(__fsub_rn(ny, q.y)) > cfg.move_eps2;
-      } else {
-        const float nx = resolve_axis(v, __fadd_rn(q.x, dv), dv, q.y, q.y, q.x, cfg.radius, false);
-        moved = fabsf(__fsub_rn(nx, q.x)) > cfg.move_eps2;
-      }
+      // one probe per lane: d < 2 moves along the rows, else along the columns
+      const bool vert = d < 2;
+      const float cq = vert ? q.y : q.x, oq = vert ? q.x : q.y;
+      const float nc = resolve_axis(v, __fadd_rn(cq, dv), dv, oq, q.y, q.x, cfg.radius, vert);
+      const bool moved = fabsf(__fsub_rn(nc, cq)) > cfg.move_eps2;
       mm[((size_t)e * P + p) * 5 + d] = q.alive ? (moved ? 1 : 0) : 1;
     } else if (lane < 5 * P) {
       mm[((size_t)e * P + (lane - 4 * P)) * 5 + 4] = 1;

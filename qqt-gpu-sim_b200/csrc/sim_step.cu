@@ -327,22 +327,39 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
                         a0f);
       // ---- 4. passivity counter
       me.since = me.placed ? 0 : me.since + 1;
-      // ---- 5. movement (sim/move.py:234-279)
-      const int mv = min(max(me.move, 0), 4);
+    }
+    // ---- 5. movement (sim/move.py:234-279).  Both axes slide from the old
+    //      position, so lane p resolves player p along the rows and lane
+    //      P + p along the columns at the same time.
+    {
+      const int pl = lane < P ? lane : (lane < 2 * P ? lane - P : 0);
+      const float y0 = __shfl_sync(QQT_FULL, me.y, pl), x0 = __shfl_sync(QQT_FULL, me.x, pl);
+      const float spd = __shfl_sync(QQT_FULL, me.spd, pl);
+      const int move = __shfl_sync(QQT_FULL, me.move, pl);
+      const int alive0 = __shfl_sync(QQT_FULL, me.alive0, pl);
+      const int mv = min(max(move, 0), 4);
       float ty = 0.f, tx = 0.f;
       if (mv == 0) ty = -cfg.step_len;
       if (mv == 1) ty = cfg.step_len;
       if (mv == 2) tx = -cfg.step_len;
       if (mv == 3) tx = cfg.step_len;
-      const bool moving = me.alive0 && me.move != 4;
-      const float dy = moving ? __fmul_rn(ty, me.spd) : 0.f;
-      const float dx = moving ? __fmul_rn(tx, me.spd) : 0.f;
-      const float ny = resolve_axis(v, __fadd_rn(me.y, dy), dy, me.x, me.y, me.x, cfg.radius, true);
-      const float nx = resolve_axis(v, __fadd_rn(me.x, dx), dx, me.y, me.y, me.x, cfg.radius, false);
-      const float oy = dy != 0.f ? ny : me.y;
-      const float ox = dx != 0.f ? nx : me.x;
-      me.y = fminf(fmaxf(oy, cfg.radius), cfg.h_minus_rad);
-      me.x = fminf(fmaxf(ox, cfg.radius), cfg.w_minus_rad);
+      const bool moving = alive0 && move != 4;
+      const float dy = moving ? __fmul_rn(ty, spd) : 0.f;
+      const float dx = moving ? __fmul_rn(tx, spd) : 0.f;
+      float res = 0.f;
+      if (lane < 2 * P) {
+        const bool vert = lane < P;
+        const float d = vert ? dy : dx;
+        res = resolve_axis(v, __fadd_rn(vert ? y0 : x0, d), d, vert ? x0 : y0, y0, x0, cfg.radius,
+                           vert);
+      }
+      const float nx = __shfl_sync(QQT_FULL, res, (lane + P) & 31);
+      if (p < P) {
+        const float oy = dy != 0.f ? res : me.y;
+        const float ox = dx != 0.f ? nx : me.x;
+        me.y = fminf(fmaxf(oy, cfg.radius), cfg.h_minus_rad);
+        me.x = fminf(fmaxf(ox, cfg.radius), cfg.w_minus_rad);
+      }
     }
 
     // ---- 6. chain explosion (sim/blast.py:101-155).  Round r triggers the
