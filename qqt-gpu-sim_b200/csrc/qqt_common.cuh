@@ -142,6 +142,17 @@ __device__ __forceinline__ bool tile_vector_ok(const QqtState& st, int n, int e0
 }
 
 // Global [N][C] -> shared [slot][cell] for envs e0 .. e0+E-1 (block-wide).
+// Chunk i of the 7 x C chunks is chunk k = i mod C of plane i / C; a
+// thread's chunks are i0, i0 + blockDim, ..., so (plane, k) advance by one
+// subtraction loop instead of a division per chunk.
+__device__ __forceinline__ void tile_chunk_next(int& pl, int& k, int step, int cells) {
+  k += step;
+  while (k >= cells) {
+    k -= cells;
+    ++pl;
+  }
+}
+
 __device__ inline void load_tile(const Tile& t, const QqtState& st, int n, int e0,
                                  unsigned planes) {
   const int cells = t.cells;
@@ -149,38 +160,36 @@ __device__ inline void load_tile(const Tile& t, const QqtState& st, int n, int e
     // kTileBatch accesses per thread are issued before any is consumed, so
     // their latencies overlap (7 planes x 169 chunks over 256 threads is 4.6)
     constexpr int kTileBatch = 5;
-    const int total = 7 * cells;
-    for (int i0 = threadIdx.x; i0 < total; i0 += kTileBatch * blockDim.x) {
+    const int step = blockDim.x;
+    int pl = threadIdx.x / cells, k = threadIdx.x - pl * cells;
+    while (pl < 7) {
       uint4 v[kTileBatch];
-      int it[kTileBatch];
+      int bpl[kTileBatch], bk[kTileBatch];
 #pragma unroll
       for (int b = 0; b < kTileBatch; ++b) {
-        const int i = i0 + b * blockDim.x;
-        it[b] = -1;
+        bpl[b] = pl;
+        bk[b] = k;
         v[b] = make_uint4(0, 0, 0, 0);
-        if (i < total) {
-          const int pl = i / cells, k = i - pl * cells;
-          if (planes & (1u << pl)) {
-            it[b] = i;
-            if (pl < 5) {
-              const uint2 u = reinterpret_cast<const uint2*>(
-                  state_plane(st, pl) + (size_t)e0 * cells)[k];
-              v[b] = make_uint4(u.x, u.y, 0, 0);
-            } else {
-              v[b] = reinterpret_cast<const uint4*>(
-                  state_plane(st, pl) + (size_t)e0 * cells * 2)[k];
-            }
+        if (pl < 7 && (planes & (1u << pl))) {
+          if (pl < 5) {
+            const uint2 u = reinterpret_cast<const uint2*>(
+                state_plane(st, pl) + (size_t)e0 * cells)[k];
+            v[b] = make_uint4(u.x, u.y, 0, 0);
+          } else {
+            v[b] = reinterpret_cast<const uint4*>(
+                state_plane(st, pl) + (size_t)e0 * cells * 2)[k];
           }
         }
+        if (pl < 7) tile_chunk_next(pl, k, step, cells);
       }
 #pragma unroll
       for (int b = 0; b < kTileBatch; ++b) {
-        if (it[b] < 0) continue;
-        const int pl = it[b] / cells, k = it[b] - pl * cells;
-        if (pl < 5)
-          reinterpret_cast<uint2*>(tile_plane(t, pl))[k] = make_uint2(v[b].x, v[b].y);
+        const int q = bpl[b];
+        if (q >= 7 || !(planes & (1u << q))) continue;
+        if (q < 5)
+          reinterpret_cast<uint2*>(tile_plane(t, q))[bk[b]] = make_uint2(v[b].x, v[b].y);
         else
-          reinterpret_cast<uint4*>(tile_plane(t, pl))[k] = v[b];
+          reinterpret_cast<uint4*>(tile_plane(t, q))[bk[b]] = v[b];
       }
     }
     return;
@@ -204,8 +213,9 @@ __device__ inline void store_tile(const Tile& t, const QqtState& st, int n, int 
                                   unsigned planes) {
   const int cells = t.cells;
   if (tile_vector_ok(st, n, e0)) {
-    for (int i = threadIdx.x; i < 7 * cells; i += blockDim.x) {
-      const int pl = i / cells, k = i - pl * cells;
+    const int step = blockDim.x;
+    for (int pl = threadIdx.x / cells, k = threadIdx.x - pl * cells; pl < 7;
+         tile_chunk_next(pl, k, step, cells)) {
       if (!(planes & (1u << pl))) continue;
       if (pl < 5)
         reinterpret_cast<uint2*>(state_plane(st, pl) + (size_t)e0 * cells)[k] =
