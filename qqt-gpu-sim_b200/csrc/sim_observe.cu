@@ -255,7 +255,7 @@ __device__ inline void fuse_tables(FuseTables& ft, float fuse_f) {
 }
 
 template <bool F32OUT>
-__global__ void __launch_bounds__(QQT_NWARP * 32)
+__global__ void __launch_bounds__(QQT_NWARP * 32, 4)
 k_observe(QqtCfg cfg, QqtState st, void* obs, float* danger_out, uint8_t* mm, uint8_t* bm) {
   using T = typename std::conditional<F32OUT, float, __half>::type;
   extern __shared__ __align__(16) uint8_t smem[];
