@@ -81,6 +81,16 @@ typedef struct QqtCfg {
   float recycle_crate_prob, combo_reward, combo_gap_factor, win_bonus;
   float win_bonus_per_hp, chain_blast_bonus, obs_growth_bombs_max;
   float fuse_f, max_steps_f, h_minus_rad, w_minus_rad;
+  /* hazard waves (sim/torch_sim.py:1404-1466): in envs with state hazard
+   * set, every hazard_wave_ticks ticks (t > 0, t counted after the step's
+   * increment) hazard_bombs_min..max bombs land on free cells with blast
+   * drawn from hazard_blast_min..max, biased upwards as t approaches
+   * hazard_ramp_ticks (= ramp seconds x tick_hz).  Draws are counter-based
+   * hashes of (hazard_seed, env, t), not the reference's torch generator. */
+  int32_t hazard_on, hazard_wave_ticks, hazard_bombs_min, hazard_bombs_max;
+  int32_t hazard_blast_min, hazard_blast_max;
+  float hazard_ramp_ticks;
+  uint32_t hazard_seed_lo, hazard_seed_hi;
 } QqtCfg;
 
 typedef struct QqtState {

@@ -413,12 +413,14 @@ def place_predict_reward(cfg, st, placed, alive0):
     return (bonus * alive0.astype(F32)).astype(F32)
 
 
-def step(cfg, st, actions, rb_hit, rb_grow, explore_coef=1.0):
+def step(cfg, st, actions, rb_hit, rb_grow, explore_coef=1.0, hazard_seed=None):
     """One tick, in place on `st` (sim/torch_sim.py:895-1261), no auto-reset.
 
     rb_hit / rb_grow: (N, P) float32 uniforms for crate pickup (the
-    reference's `_rand_buf` layout).  Returns (reward (N,P) f32, done (N,),
-    info dict with covered/triggered/died/winner/n_alive).
+    reference's `_rand_buf` layout).  hazard_seed: with cfg.hazard_fraction
+    > 0, the hazard wave after the tick count (sim/torch_sim.py:1042-1049)
+    with the engine's keyed draws (`hazard_draws_keyed`).  Returns (reward
+    (N,P) f32, done (N,), info dict with covered/triggered/died/winner/n_alive).
     """
     n, p = st["alive"].shape
     h, w = cfg.height, cfg.width
@@ -474,6 +476,8 @@ def step(cfg, st, actions, rb_hit, rb_grow, explore_coef=1.0):
     st["owner"][triggered] = -1
     st["bomb_blast"][triggered] = 0
     st["t"] += 1
+    if cfg.hazard_fraction > 0 and hazard_seed is not None:
+        hazard_wave(cfg, st, hazard_draws_keyed(cfg, st, hazard_seed))
     n_alive = st["alive"].sum(1)
     done = (n_alive <= 1) | (st["t"] >= cfg.max_steps)
 
@@ -724,6 +728,104 @@ def flush_recycle_keyed(cfg, st, excl, seed, counter):
                 st["crate"][e].reshape(-1)[order] = True
                 st["recycle"][e].reshape(-1)[order] = True
                 st["pending_lost"][e, pl] = 0
+    return st
+
+
+def _u24(x):
+    """SplitMix64 finaliser -> the top 24 bits as an integer (the device's
+    counter-based draw before scaling)."""
+    x = np.asarray(x, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        x = x + np.uint64(0x9E3779B97F4A7C15)
+        x = (x ^ (x >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        x = (x ^ (x >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+    x = x ^ (x >> np.uint64(31))
+    return (x >> np.uint64(40)).astype(np.int64)
+
+
+def hazard_key(seed, e, t, j):
+    """Key of draw family j (0: count, 1: cell order, 2: blast) for env e at
+    tick t (after the step's increment)."""
+    with np.errstate(over="ignore"):
+        return (np.uint64(seed) ^ (np.uint64(e) << np.uint64(20))
+                ^ (np.uint64(t) * np.uint64(0xD1B54A32D192ED03)) ^ (np.uint64(j) << np.uint64(56)))
+
+
+def hazard_wave_envs(cfg, st):
+    """Envs whose wave lands this tick (sim/torch_sim.py:1428)."""
+    return st["hazard"] & (st["t"] > 0) & (st["t"] % cfg.hazard_wave_ticks == 0)
+
+
+def hazard_free_cells(cfg, st, e):
+    """Free cells of env e for the wave (sim/torch_sim.py:1431-1437): no wall,
+    brick or live bomb; each player's centre cell (in player order) is then
+    set to "not alive" (a dead player's cell becomes free even if blocked)."""
+    h, w = cfg.height, cfg.width
+    free = (~st["wall"][e] & ~st["brick"][e] & (st["fuse"][e] <= 0)).reshape(-1).copy()
+    flat = center_flat(st["pos"][e:e + 1], w, h)[0]
+    for pl in range(st["alive"].shape[1]):
+        free[flat[pl]] = not st["alive"][e, pl]
+    return free
+
+
+def hazard_draws_keyed(cfg, st, seed):
+    """The engine's draws for this tick's waves: per wave env e (ascending)
+    a bomb count, an order of the free cells and one uniform per bomb, all
+    counter-based (SplitMix64 of hazard_key(seed, e, t, family) + index).
+    Returned in the reference's shapes: cnt (W,), u (sum cnt,), and per env
+    the permutation of its free-cell list that randperm would give."""
+    envs = np.nonzero(hazard_wave_envs(cfg, st))[0]
+    span = cfg.hazard_bombs_max - cfg.hazard_bombs_min + 1
+    cnt, us, perms = [], [], []
+    hw = cfg.height * cfg.width
+    for e in envs:
+        t = int(st["t"][e])
+        c = cfg.hazard_bombs_min + int((_u24(hazard_key(seed, e, t, 0)) * span) >> 24)
+        cnt.append(c)
+        pool = np.nonzero(hazard_free_cells(cfg, st, e))[0]
+        keys = _u24(hazard_key(seed, e, t, 1) + np.arange(hw, dtype=np.uint64))[pool]
+        perms.append(np.lexsort((pool, keys)))          # ascending key, ties -> lower cell
+        u = (_u24(hazard_key(seed, e, t, 2) + np.arange(c, dtype=np.uint64)).astype(np.float32)
+             * np.float32(1.0 / 16777216.0))
+        us.append(u)
+    return {"envs": envs, "cnt": np.array(cnt, np.int64),
+            "u": np.concatenate(us) if us else np.zeros(0, np.float32), "perm": perms}
+
+
+def hazard_wave(cfg, st, draws):
+    """Place this tick's wave bombs (sim/torch_sim.py:1404-1466) from explicit
+    draws: per wave env, min(cnt, #free) cells pool[perm[:c]] get fuse =
+    cfg.fuse, owner = P (no player), and blast = min + floor(u^x * (max - min
+    + 1)) clamped, x = 1 - 0.8 * clamp(t / ramp_ticks, 0, 1); the blasts are
+    computed over all the wave's bombs in order and handed out with an
+    offset that advances by the clamped count (as the reference does)."""
+    envs = draws["envs"]
+    if len(envs) == 0:
+        return st
+    p = st["alive"].shape[1]
+    cnt = draws["cnt"]
+    ramp = F32(cfg.hazard_ramp_seconds * cfg.tick_hz)
+    frac = np.clip(st["t"][envs].astype(F32) / ramp, F32(0.0), F32(1.0))
+    ex = (F32(1.0) - F32(0.8) * frac).astype(F32)
+    ex_b = np.repeat(ex, cnt)
+    u = draws["u"].astype(F32)
+    v = np.power(u.astype(np.float64), ex_b.astype(np.float64)).astype(F32)
+    lo, hi = cfg.hazard_blast_min, cfg.hazard_blast_max
+    blast = (F32(lo) + np.floor(v * F32(hi - lo + 1))).astype(F32)
+    blast = np.clip(blast, F32(lo), F32(hi)).astype(np.int16)
+    w = cfg.width
+    off = 0
+    for i, e in enumerate(envs):
+        pool = np.nonzero(hazard_free_cells(cfg, st, e))[0]
+        c = min(int(cnt[i]), pool.size)
+        if c <= 0:
+            continue
+        pick = pool[draws["perm"][i][:c]]
+        y, x = pick // w, pick % w
+        st["fuse"][e, y, x] = cfg.fuse
+        st["owner"][e, y, x] = p
+        st["bomb_blast"][e, y, x] = blast[off:off + c]
+        off += c
     return st
 
 

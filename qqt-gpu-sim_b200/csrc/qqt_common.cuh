@@ -555,6 +555,15 @@ __host__ __device__ __forceinline__ float hash_uniform(uint64_t x) {
   return (float)(x >> 40) * (1.0f / 16777216.0f);
 }
 
+// The top 24 bits of the same finaliser, as an integer.
+__host__ __device__ __forceinline__ uint32_t hash_u24(uint64_t x) {
+  x += 0x9E3779B97F4A7C15ull;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  x ^= x >> 31;
+  return (uint32_t)(x >> 40);
+}
+
 }  // namespace qqt
 
 static inline int check_cfg(const QqtCfg* cfg) {

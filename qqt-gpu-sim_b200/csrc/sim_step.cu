@@ -86,6 +86,88 @@ struct StepParams {
   uint8_t* bm;
 };
 
+// Key of hazard draw family j (0: bomb count, 1: cell order, 2: blast) of
+// env e at tick t (counted after the step's increment).
+__device__ __forceinline__ uint64_t hazard_key(uint64_t seed, int e, int64_t t, int j) {
+  return seed ^ ((uint64_t)e << 20) ^ ((uint64_t)t * 0xD1B54A32D192ED03ull) ^ ((uint64_t)j << 56);
+}
+__device__ __forceinline__ uint64_t hazard_seed(const QqtCfg& cfg) {
+  return ((uint64_t)cfg.hazard_seed_hi << 32) | cfg.hazard_seed_lo;
+}
+
+// Hazard wave of one env (sim/torch_sim.py:1404-1466), warp-wide: after
+// the tick count, before the termination test.  min(count, #free) free
+// cells (no wall / brick / live bomb; a player's centre cell is free
+// exactly when the player is dead, later players overriding) with the
+// smallest keys get a fuse-full bomb of owner P; the r-th of them takes
+// blast min + floor(u_r^x * span), x = 1 - 0.8 clamp(t / ramp).  Draws:
+// hash_u24 of hazard_key(seed, env, t, family).  Returns the new length of the post-step bomb list.
+__device__ __forceinline__ int hazard_wave_env(const QqtCfg& cfg, const Env& v,
+                                               const DangerScratch& ds, int e, int t1, int flat1,
+                                               int alive, int nb_post) {
+  const int lane = lane_id(), P = cfg.n_players, C = v.cells;
+  // cell keys in the stage-A weight array (not used until the danger stage
+  // A that follows); 0xffffffff = not free / taken
+  uint32_t* hkey = reinterpret_cast<uint32_t*>(ds.cur);
+  int nfree = 0;
+  for (int base = 0; base < C; base += 32) {
+    const int c = base + lane;
+    bool fr = c < C && !v.wall[c] && !v.brick[c] && v.fuse[c] <= 0;
+    for (int q = 0; q < P; ++q) {
+      const int fq = __shfl_sync(QQT_FULL, flat1, q);
+      const int aq = __shfl_sync(QQT_FULL, alive, q);
+      if (c < C && fq == c) fr = aq == 0;
+    }
+    if (c < C) hkey[c] = fr ? hash_u24(hazard_key(hazard_seed(cfg), e, t1, 1) + (uint64_t)c) : 0xFFFFFFFFu;
+    nfree += __popc(__ballot_sync(QQT_FULL, fr));
+  }
+  __syncwarp();
+  const int span = cfg.hazard_bombs_max - cfg.hazard_bombs_min + 1;
+  const int cnt = cfg.hazard_bombs_min +
+                  (int)(((uint64_t)hash_u24(hazard_key(hazard_seed(cfg), e, t1, 0)) * (uint64_t)span) >> 24);
+  const int n_place = min(cnt, nfree);
+  for (int r = 0; r < n_place; ++r) {
+    uint32_t best = 0xFFFFFFFFu;
+    int bc = 0x7fffffff;
+    for (int c = lane; c < C; c += 32)
+      if (hkey[c] < best) {
+        best = hkey[c];
+        bc = c;
+      }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {   // warp argmin, ties -> lower cell
+      const uint32_t ob = __shfl_xor_sync(QQT_FULL, best, o);
+      const int oc = __shfl_xor_sync(QQT_FULL, bc, o);
+      if (ob < best || (ob == best && oc < bc)) {
+        best = ob;
+        bc = oc;
+      }
+    }
+    // a dead player's cell can hold a live bomb (already in the list): it
+    // is overwritten but listed once
+    const bool listed = v.fuse[bc] > 0;
+    __syncwarp();
+    if (lane == 0) {
+      const float frac = fminf(fmaxf(__fdiv_rn((float)t1, cfg.hazard_ramp_ticks), 0.f), 1.f);
+      const float ex = __fsub_rn(1.f, __fmul_rn(0.8f, frac));
+      const float u = (float)hash_u24(hazard_key(hazard_seed(cfg), e, t1, 2) + (uint64_t)r) *
+                      (1.f / 16777216.f);
+      const float vv = (float)pow((double)u, (double)ex);
+      const float bspan = (float)(cfg.hazard_blast_max - cfg.hazard_blast_min + 1);
+      float bl = __fadd_rn((float)cfg.hazard_blast_min, floorf(__fmul_rn(vv, bspan)));
+      bl = fminf(fmaxf(bl, (float)cfg.hazard_blast_min), (float)cfg.hazard_blast_max);
+      v.fuse[bc] = (int16_t)cfg.fuse;
+      v.owner[bc] = (int8_t)P;
+      v.blast[bc] = (int16_t)bl;
+      hkey[bc] = 0xFFFFFFFFu;
+      if (!listed) ds.bombs[nb_post] = (uint16_t)bc;
+    }
+    if (!listed) ++nb_post;
+    __syncwarp();
+  }
+  return nb_post;
+}
+
 __device__ __forceinline__ bool placed_map_at(const PShared* ps, int P, int cell) {
   bool v = false;
   for (int i = 0; i < P; ++i)
@@ -93,9 +175,10 @@ __device__ __forceinline__ bool placed_map_at(const PShared* ps, int P, int cell
   return v;
 }
 
-// PHASE and OBS (a.obs set: the fused next observation) are compile-time so
-// that each instance carries only its own code.
-template <int PHASE, bool OBS>
+// PHASE, OBS (a.obs set: the fused next observation) and HZ (hazard waves
+// configured) are compile-time so that each instance carries only its own
+// code and registers.
+template <int PHASE, bool OBS, bool HZ>
 __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ FuseTables ft;
@@ -115,6 +198,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
   PlayerState me;
   float env_crate_prob = 0.f;
   bool env_hazard = false;
+  bool env_hz = false;              // hazard-wave env (sim/torch_sim.py:1428)
   int64_t act_mv = 0, act_bo = 0;
   {
     const int e = e0 + warp_id();
@@ -145,6 +229,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
       }
       env_crate_prob = cfg.corridor ? st.crate_prob[e] : 0.f;
       env_hazard = cfg.crate_speed_only && st.hazard[e];
+      env_hz = HZ && st.hazard[e];
     }
   }
   load_tile(tile, st, N, e0, PL_ALL);
@@ -474,6 +559,9 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
     }
     // ---- 11. t and done
     const int64_t t1 = st.t[e] + 1;
+    // ---- hazard wave (sim/torch_sim.py:1404-1466)
+    if (HZ && env_hz && t1 > 0 && t1 % cfg.hazard_wave_ticks == 0)
+      nb_post = hazard_wave_env(cfg, v, ds, e, (int)t1, flat1, alive, nb_post);
     const unsigned amask = __ballot_sync(QQT_FULL, p < P && alive);
     const int n_alive = __popc(amask);
     const bool done = n_alive <= 1 || t1 >= cfg.max_steps;
@@ -830,14 +918,23 @@ static int launch_step(const QqtCfg* cfg, const QqtState* st, const int64_t* act
     kern<<<blocks, QQT_NWARP * 32, sm, s>>>(p);
   };
   const bool fused = obs != nullptr;
+  const bool hz = cfg->hazard_on != 0;
   if (first_step) {
     cudaMemsetAsync(tiers, 0xff, sizeof(int32_t), s);   // -1
-    launch(k_step<PHASE_PLACE, false>, PHASE_PLACE);
-    if (fused) launch(k_step<PHASE_AFTER_PLACE, true>, PHASE_AFTER_PLACE);
-    else launch(k_step<PHASE_AFTER_PLACE, false>, PHASE_AFTER_PLACE);
+    launch(k_step<PHASE_PLACE, false, false>, PHASE_PLACE);
+    if (fused) {
+      if (hz) launch(k_step<PHASE_AFTER_PLACE, true, true>, PHASE_AFTER_PLACE);
+      else launch(k_step<PHASE_AFTER_PLACE, true, false>, PHASE_AFTER_PLACE);
+    } else {
+      if (hz) launch(k_step<PHASE_AFTER_PLACE, false, true>, PHASE_AFTER_PLACE);
+      else launch(k_step<PHASE_AFTER_PLACE, false, false>, PHASE_AFTER_PLACE);
+    }
+  } else if (fused) {
+    if (hz) launch(k_step<PHASE_FULL, true, true>, PHASE_FULL);
+    else launch(k_step<PHASE_FULL, true, false>, PHASE_FULL);
   } else {
-    if (fused) launch(k_step<PHASE_FULL, true>, PHASE_FULL);
-    else launch(k_step<PHASE_FULL, false>, PHASE_FULL);
+    if (hz) launch(k_step<PHASE_FULL, false, true>, PHASE_FULL);
+    else launch(k_step<PHASE_FULL, false, false>, PHASE_FULL);
   }
   return launch_status();
 }

@@ -29,8 +29,15 @@ _CFG_FLOATS = ("radius step_len move_eps2 step_penalty hit_reward brick_reward "
                "obs_growth_bombs_max fuse_f max_steps_f h_minus_rad w_minus_rad").split()
 
 
+_CFG_HAZARD = ([(n, c_i32) for n in ("hazard_on hazard_wave_ticks hazard_bombs_min "
+                                       "hazard_bombs_max hazard_blast_min "
+                                       "hazard_blast_max").split()]
+               + [("hazard_ramp_ticks", c_f32), ("hazard_seed_lo", ctypes.c_uint32),
+                  ("hazard_seed_hi", ctypes.c_uint32)])
+
+
 class QqtCfg(ctypes.Structure):
-    _fields_ = [(n, c_i32) for n in _CFG_INTS] + [(n, c_f32) for n in _CFG_FLOATS]
+    _fields_ = [(n, c_i32) for n in _CFG_INTS] + [(n, c_f32) for n in _CFG_FLOATS] + _CFG_HAZARD
 
 
 STATE_FIELDS = ("wall brick crate recycle fuse owner bomb_blast pos alive hp since_bomb t "

@@ -96,6 +96,12 @@ def make_ccfg(cfg: SimConfig, n_envs: int, explore_coef: float = 1.0,
         setattr(c, k, int(v))
     for k, v in floats.items():
         setattr(c, k, float(v))
+    # hazard waves (sim/torch_sim.py:1404-1466); the seed is set per step
+    c.hazard_on = int(cfg.hazard_fraction > 0)
+    c.hazard_wave_ticks = int(cfg.hazard_wave_ticks)
+    c.hazard_bombs_min, c.hazard_bombs_max = int(cfg.hazard_bombs_min), int(cfg.hazard_bombs_max)
+    c.hazard_blast_min, c.hazard_blast_max = int(cfg.hazard_blast_min), int(cfg.hazard_blast_max)
+    c.hazard_ramp_ticks = float(cfg.hazard_ramp_seconds * cfg.tick_hz)
     return c
 
 
@@ -133,6 +139,11 @@ class B200Sim:
         self._buf["_lo_spd"].fill_(cfg.growth_speed_start)
         self._buf["spd_g"].fill_(1.0)
         self._explore_coef = 1.0
+        # hazard-wave draws: keyed by (seed, env, tick); None derives a new
+        # seed for every step call, an int fixes it (parity checks)
+        self.hazard_seed: int | None = None
+        self._hazard_calls = 0
+        self._hazard_base = (int(seed) * 0x9E3779B97F4A7C15 + 0x5851F42D4C957F2D) & ((1 << 64) - 1)
         self.speed_mult = None
         self._rand_buf: torch.Tensor | None = None
         self._ccfg = make_ccfg(cfg, n, 1.0)
@@ -520,6 +531,14 @@ class B200Sim:
             rb_hit = rb_hit.to(self.device, torch.float32).contiguous()
             rb_grow = rb_grow.to(self.device, torch.float32).contiguous()
         dev_reset = auto_reset and self._tmpl is not None
+        if self.cfg.hazard_fraction > 0:
+            if self.hazard_seed is not None:
+                hs = int(self.hazard_seed)
+            else:
+                self._hazard_calls += 1
+                hs = (self._hazard_base ^ (self._hazard_calls * 0xD1B54A32D192ED03)) & ((1 << 64) - 1)
+            self._ccfg.hazard_seed_lo = hs & 0xFFFFFFFF
+            self._ccfg.hazard_seed_hi = (hs >> 32) & 0xFFFFFFFF
         if next_obs is not None:
             if auto_reset and not dev_reset:
                 raise ValueError("next_obs needs the device auto-reset (a template) or no reset")

@@ -25,6 +25,8 @@ Outputs (compressed npz, all env-major like the reference tensors):
                    free cells, MLP learner vs the hunter bot (astar with the
                    crate layer), 128 ticks, with V_crate fields
   stress_cfg3.npz  bomb stress: one idle step, danger/obs/masks, V fields
+  hazard_wave.npz  the reference's hazard-wave placement on seeded states,
+                   its draws fed from the engine's keyed generator
   ckpt_adapt.npz   adapt_first_conv on seeded models (2 <-> 3 players), and
   ref_ckpt_mlp.pt  a checkpoint written by the reference's save_ckpt
 """
@@ -566,6 +568,74 @@ def ckpt_golden(R):
     return out
 
 
+def hazard_golden(R):
+    """Hazard wave placement (sim/torch_sim.py:1404-1466) run by the
+    reference itself on seeded states, with its randint / rand / randperm
+    fed the engine's keyed draws (oracle.hazard_draws_keyed), so that the
+    placement rules (free cells, the dead-player cell rule, blast formula,
+    offsets) are pinned independently of the random source."""
+    import torch
+    sys.path.insert(0, REPO)
+    from oracle import qqt_oracle as O
+    from qqt_b200.config import SimConfig as BSC
+    rts = R["ts"]
+    kw = dict(map_mode="open", hazard_fraction=1.0, speed=3.0)
+    cfg_r, cfg_b = R["SimConfig"](**kw), BSC(**kw)
+    n, h, w, p = 32, cfg_b.height, cfg_b.width, cfg_b.n_players
+    rng = np.random.default_rng(21)
+    wall = np.broadcast_to(scenarios.border_walls(h, w), (n, h, w)).copy()
+    wall |= (rng.random((n, h, w)) < 0.08)
+    brick = (rng.random((n, h, w)) < 0.2) & ~wall
+    fuse = np.where(rng.random((n, h, w)) < 0.1, rng.integers(1, 30, (n, h, w)), 0).astype(np.int16)
+    fuse[wall] = 0
+    owner = np.where(fuse > 0, rng.integers(0, p + 1, (n, h, w)), -1).astype(np.int8)
+    blast = np.where(fuse > 0, rng.integers(1, 8, (n, h, w)), 0).astype(np.int16)
+    pos = (rng.integers(1, h - 1, (n, p, 2)) + 0.5).astype(np.float32)
+    alive = rng.random((n, p)) < 0.8
+    hazard = rng.random(n) < 0.7
+    t = rng.choice([50, 100, 600, 1200, 49], n).astype(np.int64)
+    st = {"wall": wall, "brick": brick, "fuse": fuse, "owner": owner, "bomb_blast": blast,
+          "pos": pos, "alive": alive, "hazard": hazard, "t": t}
+    seed = 0x1234ABCD5678
+    draws = O.hazard_draws_keyed(cfg_b, st, seed)
+
+    class Fed:
+        def __init__(self):
+            self.perm = list(draws["perm"])
+
+        def randint(self, low, high, size, device=None, **k):
+            return torch.from_numpy(draws["cnt"].copy())
+
+        def rand(self, *size, device=None, **k):
+            return torch.from_numpy(draws["u"].copy())
+
+        def randperm(self, m, device=None, **k):
+            pr = self.perm.pop(0)
+            assert pr.size == m
+            return torch.from_numpy(pr.astype(np.int64))
+
+        def __getattr__(self, name):
+            return getattr(torch, name)
+
+    sim = rts.BatchedSim(cfg_r, n, device="cpu", seed=0)
+    set_state(sim, st)
+    sim.alive.copy_(torch.from_numpy(alive))
+    sim._hazard.copy_(torch.from_numpy(hazard))
+    sim.t.copy_(torch.from_numpy(t))
+    real = rts.torch
+    rts.torch = Fed()
+    try:
+        sim._hazard_wave()
+    finally:
+        rts.torch = real
+    out = {"pre_" + k: np.asarray(v) for k, v in st.items()}
+    out["seed"] = np.array(seed, np.uint64)
+    out["n_wave_envs"] = np.array(len(draws["envs"]))
+    for k in ("fuse", "owner", "bomb_blast"):
+        out["post_" + k] = getattr(sim, k).numpy().copy()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("QQT_REFERENCE_ROOT", "/root/reference"))
@@ -589,6 +659,7 @@ def main():
         "reset_modes": lambda: reset_modes(R),
         "ppo_update": lambda: ppo_golden(R),
         "ckpt_adapt": lambda: ckpt_golden(R),
+        "hazard_wave": lambda: hazard_golden(R),
     }
     for name, fn in jobs.items():
         if args.only and name not in args.only.split(","):

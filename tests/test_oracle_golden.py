@@ -240,3 +240,17 @@ def test_traj_hunter_crate_fields_and_eat_branch():
         assert np.array_equal(a_eat, g["actions"][t][:, 1])
         eat_moves += int((a_eat[:, 0] != a_plain[:, 0]).sum())
     assert eat_moves > 0
+
+
+def test_hazard_wave_matches_reference():
+    """Hazard-wave placement (sim/torch_sim.py:1404-1466): the restatement
+    with the engine's keyed draws equals the reference fed the same draws."""
+    g = G.load("hazard_wave")
+    cfg = SimConfig(map_mode="open", hazard_fraction=1.0, speed=3.0)
+    st = {k[4:]: v.copy() for k, v in g.items() if k.startswith("pre_")}
+    draws = O.hazard_draws_keyed(cfg, st, int(g["seed"]))
+    assert len(draws["envs"]) == int(g["n_wave_envs"]) > 0
+    O.hazard_wave(cfg, st, draws)
+    for k in ("fuse", "owner", "bomb_blast"):
+        assert np.array_equal(st[k], g["post_" + k]), k
+    assert (g["post_owner"] == cfg.n_players).sum() > (g["pre_owner"] == cfg.n_players).sum()
