@@ -57,7 +57,8 @@ enum {
   QQT_DEV_POS_RANGE = 1u << 0,   /* a centre cell fell outside the grid     */
   QQT_DEV_NOT_CONVERGED = 1u << 1, /* path-field relaxation hit its cap     */
   QQT_DEV_BAD_ACTION = 1u << 2,  /* action index outside its head's range   */
-  QQT_DEV_TIMEOUT = 1u << 3      /* a bounded mbarrier wait expired         */
+  QQT_DEV_TIMEOUT = 1u << 3,     /* a bounded mbarrier wait expired         */
+  QQT_DEV_BAD_INDEX = 1u << 4    /* a gather index outside its source rows  */
 };
 
 /* Scalar configuration.  Float fields hold the float32 values the reference
@@ -343,6 +344,41 @@ const char *qqt_cnn_param_names(void);
 int qqt_gae(const float *rew, int32_t rew_stride, const uint8_t *done, const float *val,
             int32_t val_stride, const float *last_val, int32_t T, int32_t N, double gamma,
             double lam, float *adv, float *ret, qqt_stream_t stream);
+
+/* ---- PPO update of the MLP policy: its first layer (train/ppo.py:364-437
+ * via ActorCritic(mlp).evaluate, train/model.py:121-153 and 247-256).  The
+ * reference runs `obs[sel]` (index gather), `.float()`, F.linear(x, W0[:,
+ * inv_cols[pid]], b0) and autograd's weight gradient in float32 for every
+ * minibatch; these entry points do the same from the float16 rows. */
+
+/* dst row i = src row idx[i] (row_bytes of each; strides in bytes; all
+ * 16-byte multiples).  An index outside [0, n_src) zero-fills its row and
+ * raises QQT_DEV_BAD_INDEX. */
+int qqt_gather_rows(const void *src, int64_t n_src, int64_t src_stride_bytes, const int64_t *idx,
+                    int64_t n, void *dst, int64_t dst_stride_bytes, int64_t row_bytes,
+                    qqt_stream_t stream);
+
+/* W0 [128][k_in] float32 with seat pid's view permutation folded into its
+ * column order (train/model.py:127-138), as fp16 hi then lo halves [2][128][kp]
+ * (kp = k_in rounded up to 64); pack = qqt_l1_pack_bytes(k_in) bytes,
+ * 256-byte aligned. */
+int qqt_l1_pack(const float *w0, int32_t k_in, int32_t n_players, int32_t channels, int32_t hw,
+                int32_t pid, void *pack, qqt_stream_t stream);
+uint64_t qqt_l1_pack_bytes(int32_t k_in);
+
+/* h1 [n_rows][128] float32 = x W0p^T + b0 for fp16 rows x [n_rows][x_stride]
+ * (x_stride >= k_in, a multiple of 8; columns >= k_in are not read). */
+int qqt_l1_forward(const void *pack, const void *x, int64_t n_rows, int32_t x_stride,
+                   int32_t k_in, const float *b0, float *h1, qqt_stream_t stream);
+
+/* dw0 [128][k_in] float32 = dL/dW0 of the layer above for dL/dh1 = dh1
+ * [n_rows][128] float32, in W0's own column order (seat pid's permutation
+ * undone).  work = qqt_l1_wgrad_work_bytes(n_rows, k_in) bytes, 1024-byte
+ * aligned. */
+int qqt_l1_wgrad(const void *x, int64_t n_rows, int32_t x_stride, int32_t k_in, const float *dh1,
+                 int32_t n_players, int32_t channels, int32_t hw, int32_t pid, float *dw0,
+                 void *work, qqt_stream_t stream);
+uint64_t qqt_l1_wgrad_work_bytes(int64_t n_rows, int32_t k_in);
 
 /* Device error word: returns the accumulated QQT_DEV_* bits and clears
  * them (synchronises the device). */

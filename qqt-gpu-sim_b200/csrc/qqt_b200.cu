@@ -5,3 +5,4 @@
 #include "policy_mlp.cu"
 #include "policy_cnn.cu"
 #include "train_gae.cu"
+#include "train_mlp.cu"

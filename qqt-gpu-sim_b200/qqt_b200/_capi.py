@@ -98,6 +98,13 @@ def lib():
             "qqt_flush_recycle": (c_i32, [P(QqtCfg), P(QqtState), c_p, c_u64, c_u64, c_p]),
             "qqt_gae": (c_i32, [c_p, c_i32, c_p, c_p, c_i32, c_p, c_i32, c_i32, ctypes.c_double,
                                 ctypes.c_double, c_p, c_p, c_p]),
+            "qqt_gather_rows": (c_i32, [c_p, c_i64, c_i64, c_p, c_i64, c_p, c_i64, c_i64, c_p]),
+            "qqt_l1_pack": (c_i32, [c_p, c_i32, c_i32, c_i32, c_i32, c_i32, c_p, c_p]),
+            "qqt_l1_pack_bytes": (c_u64, [c_i32]),
+            "qqt_l1_forward": (c_i32, [c_p, c_p, c_i64, c_i32, c_i32, c_p, c_p, c_p]),
+            "qqt_l1_wgrad": (c_i32, [c_p, c_i64, c_i32, c_i32, c_p, c_i32, c_i32, c_i32, c_i32,
+                                     c_p, c_p, c_p]),
+            "qqt_l1_wgrad_work_bytes": (c_u64, [c_i64, c_i32]),
             "qqt_get_error": (c_i32, [P(ctypes.c_uint32)]),
             "qqt_version": (ctypes.c_char_p, []),
         }

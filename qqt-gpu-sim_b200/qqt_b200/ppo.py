@@ -6,9 +6,18 @@ the update step: GAE on the device (`qqt_gae` kernel), global advantage
 normalisation, the reference's oversampling of damage / terminal frames,
 clipped policy and value losses with an entropy bonus, a gradient all-reduce
 across ranks (`torch.distributed`, NCCL on GPUs, gloo on CPU), gradient-norm
-clipping and Adam.  The network is a torch restatement of ActorCritic(mlp)
-with the reference's parameter names, so its parameters feed B200Policy's
-packed weights directly (`B200Policy.repack()` after each update).
+clipping and Adam.  The network is ActorCritic(mlp) with the reference's
+parameter names, so its parameters feed B200Policy's packed weights directly
+(`B200Policy.repack()` after each update).
+
+On the GPU the first layer, Linear(2366 -> 128), the one real contraction of
+the update, runs on the tensor-core kernels of csrc/train_mlp.cu from the
+rollout's float16 observation rows: the minibatch's rows are gathered by a
+kernel (the reference's `obs[sel]`), the forward product and the weight
+gradient are tcgen05 GEMMs with float32-accurate hi/lo operand splits, and no
+float32 copy of the observations is made.  The 128-wide layers above it run
+through torch autograd.  CPU tensors (the gloo tests) take the torch
+restatement of the same layer.
 """
 
 from __future__ import annotations
@@ -51,6 +60,91 @@ def inv_cols(n_players: int, c: int, h: int, w: int, pid: int) -> torch.Tensor:
     return torch.from_numpy(np.concatenate([np.arange(hw) + int(inv[k]) * hw for k in range(c)]))
 
 
+def _aligned(buf: torch.Tensor, align: int) -> int:
+    base = buf.data_ptr()
+    return base + (-base) % align
+
+
+def obs_rows(obs: torch.Tensor, k_in: int) -> torch.Tensor:
+    """2-D float16 observation rows the kernels read: (n, stride) with stride
+    >= k_in a multiple of 8 and 16-byte aligned rows.  The rollout buffer's
+    row-padded observations qualify as they are; anything else (an (n, C, H,
+    W) float16 batch) is copied once into zero-padded rows."""
+    n = obs.shape[0]
+    if obs.dtype != torch.float16:
+        raise TypeError(f"observations must be float16 (the rollout's storage), got {obs.dtype}")
+    if (obs.dim() == 2 and obs.stride(1) == 1 and obs.shape[1] >= k_in and obs.stride(0) % 8 == 0
+            and obs.data_ptr() % 16 == 0):
+        return obs
+    flat = obs.reshape(n, -1)[:, :k_in]
+    rows = torch.zeros((n, (k_in + 7) // 8 * 8), dtype=torch.float16, device=obs.device)
+    rows[:, :k_in] = flat
+    return rows
+
+
+def gather_rows(rows: torch.Tensor, idx: torch.Tensor, out: torch.Tensor | None = None):
+    """out[i] = rows[idx[i]] on the device (`qqt_gather_rows`); rows as
+    obs_rows returns them, idx int64 on the same device."""
+    from . import _capi as capi
+    n = idx.numel()
+    if out is None:
+        out = torch.empty((n, rows.shape[1]), dtype=rows.dtype, device=rows.device)
+    idx = idx.to(torch.int64).contiguous()
+    rb = rows.shape[1] * rows.element_size()
+    rb16 = (rb + 15) // 16 * 16
+    if rb16 > rows.stride(0) * rows.element_size():
+        raise ValueError("rows must be padded to a 16-byte multiple")
+    capi.check(capi.lib().qqt_gather_rows(rows.data_ptr(), rows.shape[0],
+                                          rows.stride(0) * rows.element_size(), idx.data_ptr(),
+                                          n, out.data_ptr(), out.stride(0) * out.element_size(),
+                                          rb16, capi.stream_ptr(rows.device)),
+               "qqt_gather_rows")
+    return out
+
+
+class _Layer1(torch.autograd.Function):
+    """Linear(k_in -> 128) with seat pid's view permutation folded into W0's
+    column order (train/model.py:127-138, 149-150) on the B200 kernels.
+    Forward: h1 = x W0p^T + b0 (qqt_l1_forward); backward: dW0
+    (qqt_l1_wgrad, in W0's own column order) and db0 = sum of dL/dh1.  The
+    observations are data, so no input gradient is formed."""
+
+    @staticmethod
+    def forward(ctx, rows, w0, b0, k_in, geom):
+        from . import _capi as capi
+        n_players, channels, hw, pid = geom
+        L, dev = capi.lib(), rows.device
+        st = capi.stream_ptr(dev)
+        w0c, b0c = w0.detach().contiguous(), b0.detach().contiguous()
+        pack = torch.empty(int(L.qqt_l1_pack_bytes(k_in)) + 256, dtype=torch.uint8, device=dev)
+        pk = _aligned(pack, 256)
+        capi.check(L.qqt_l1_pack(w0c.data_ptr(), k_in, n_players, channels, hw, pid, pk, st),
+                   "qqt_l1_pack")
+        n = rows.shape[0]
+        h1 = torch.empty((n, w0.shape[0]), dtype=torch.float32, device=dev)
+        capi.check(L.qqt_l1_forward(pk, rows.data_ptr(), n, rows.stride(0), k_in,
+                                    b0c.data_ptr(), h1.data_ptr(), st), "qqt_l1_forward")
+        ctx.save_for_backward(rows)
+        ctx.k_in, ctx.geom = k_in, geom
+        return h1
+
+    @staticmethod
+    def backward(ctx, dh1):
+        from . import _capi as capi
+        (rows,) = ctx.saved_tensors
+        n_players, channels, hw, pid = ctx.geom
+        L, dev = capi.lib(), rows.device
+        dh1 = dh1.contiguous()
+        n = rows.shape[0]
+        dw0 = torch.empty((dh1.shape[1], ctx.k_in), dtype=torch.float32, device=dev)
+        work = torch.empty(int(L.qqt_l1_wgrad_work_bytes(n, ctx.k_in)) + 1024, dtype=torch.uint8,
+                           device=dev)
+        capi.check(L.qqt_l1_wgrad(rows.data_ptr(), n, rows.stride(0), ctx.k_in, dh1.data_ptr(),
+                                  n_players, channels, hw, pid, dw0.data_ptr(),
+                                  _aligned(work, 1024), capi.stream_ptr(dev)), "qqt_l1_wgrad")
+        return None, dw0, dh1.sum(0), None, None
+
+
 class MLPActorCritic(nn.Module):
     """ActorCritic(arch="mlp") for training (same parameter names)."""
 
@@ -72,9 +166,14 @@ class MLPActorCritic(nn.Module):
     def forward(self, obs: torch.Tensor, pid: int = 0):
         n = obs.shape[0]
         # (N, C, H, W) or the engine's row-padded (N, stride >= C*H*W) rows
-        x = obs.reshape(n, -1)[:, : self.k_in].to(self.shared[0].weight.dtype)
-        w0 = self.shared[0].weight[:, getattr(self, f"inv_cols_{pid}")]
-        x = F.linear(x, w0, self.shared[0].bias)
+        if obs.is_cuda:
+            c, h, w = self.obs_shape
+            x = _Layer1.apply(obs_rows(obs, self.k_in), self.shared[0].weight,
+                              self.shared[0].bias, self.k_in, (self.n_players, c, h * w, pid))
+        else:
+            x = obs.reshape(n, -1)[:, : self.k_in].to(self.shared[0].weight.dtype)
+            w0 = self.shared[0].weight[:, getattr(self, f"inv_cols_{pid}")]
+            x = F.linear(x, w0, self.shared[0].bias)
         x = self.shared[1:](x)
         return self.move_head(x), self.bomb_head(x), self.critic(x).squeeze(-1)
 
@@ -146,6 +245,8 @@ def ppo_update(model: MLPActorCritic, opt, data: dict, last_val, cfg: PPOConfig,
     total = T * n
     flat = lambda x: x.reshape(total, *x.shape[2:])  # noqa: E731
     obs = flat(data["obs"])
+    if obs.is_cuda:
+        obs = obs_rows(obs, model.k_in)
     mm, bm, act = flat(data["mm"]), flat(data["bm"]), flat(data["act"])
     old_logp, old_val = flat(data["logp"]), flat(data["val"])
     adv, ret = flat(adv), flat(ret)
@@ -172,12 +273,21 @@ def ppo_update(model: MLPActorCritic, opt, data: dict, last_val, cfg: PPOConfig,
     # statistics stay on the device; one host read at the end
     out = {k: torch.zeros((), device=dev) for k in ("pg", "vf", "ent", "kl", "clipfrac")}
     updates = 0
+    xg = None
     params = [p for p in model.parameters()]
     for _ in range(cfg.epochs):
         perm = pool[perm_fn(pool.numel())][:total]
         for start in range(0, total, mb):
             sel = perm[start:start + mb]
-            logp, ent, value = model.evaluate(obs[sel], mm[sel], bm[sel], act[sel], pid)
+            if obs.is_cuda:
+                # the minibatch's rows, gathered into one reused block; the
+                # previous minibatch's backward has finished reading it
+                if xg is None or xg.shape[0] < sel.numel():
+                    xg = torch.empty((sel.numel(), obs.shape[1]), dtype=obs.dtype, device=dev)
+                x = gather_rows(obs, sel, xg[:sel.numel()])
+            else:
+                x = obs[sel]
+            logp, ent, value = model.evaluate(x, mm[sel], bm[sel], act[sel], pid)
             ratio = (logp - old_logp[sel]).exp()
             a = adv[sel]
             pg = -torch.min(ratio * a, ratio.clamp(1 - cfg.clip_eps, 1 + cfg.clip_eps) * a).mean()

@@ -1,0 +1,154 @@
+"""The PPO update's first-layer kernels (csrc/train_mlp.cu) against float64
+references of the same products (train/model.py:121-153, train/ppo.py:364-437).
+
+qqt_gather_rows is compared bit for bit with torch indexing; qqt_l1_forward
+and qqt_l1_wgrad (through the autograd function the update uses) with the
+float64 product of the same float16 rows and float32 weights, for both seats'
+view permutations, ragged row counts (a partial last tile, several tiles per
+persistent CTA) and gradients spread over twelve decades.  The whole
+MLPActorCritic.evaluate on the device is compared with its CPU restatement.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from qqt_b200.ppo import MLPActorCritic, _Layer1, gather_rows, inv_cols, obs_rows
+
+pytestmark = pytest.mark.gpu
+
+SHAPE = (14, 13, 13)
+K_IN = 14 * 169
+
+
+def _need_cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+
+
+def _rows(n, seed, stride=2368):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.rand((n, K_IN), generator=g)
+    x = torch.where(torch.rand((n, K_IN), generator=g) < 0.3, x, torch.zeros(()))
+    rows = torch.zeros((n, stride), dtype=torch.float16)
+    rows[:, :K_IN] = x.half()
+    return rows.cuda()
+
+
+def _weights(seed):
+    g = torch.Generator().manual_seed(seed)
+    w0 = (torch.randn((128, K_IN), generator=g) * 0.02).cuda()
+    b0 = (torch.randn(128, generator=g) * 0.1).cuda()
+    return w0, b0
+
+
+def test_gather_rows_bit_exact():
+    _need_cuda()
+    from qqt_b200 import _capi
+    src = _rows(1000, 1)
+    idx = torch.randint(0, 1000, (777,), device="cuda")
+    idx[5] = 999
+    idx[6] = 0
+    out = gather_rows(src, idx)
+    torch.cuda.synchronize()
+    assert torch.equal(out, src[idx])
+    assert _capi.device_error() == 0
+
+
+def test_gather_rows_bad_index_flags_and_zero_fills():
+    _need_cuda()
+    from qqt_b200 import _capi
+    src = _rows(64, 2)
+    idx = torch.tensor([3, 64, -1, 7], device="cuda")
+    out = gather_rows(src, idx)
+    torch.cuda.synchronize()
+    assert _capi.device_error() == 1 << 4   # QQT_DEV_BAD_INDEX
+    assert torch.equal(out[0], src[3]) and torch.equal(out[3], src[7])
+    assert not out[1].any() and not out[2].any()
+
+
+@pytest.mark.parametrize("n", [1, 300, 37965])
+@pytest.mark.parametrize("pid", [0, 1])
+def test_l1_forward_and_wgrad_match_float64(n, pid):
+    _need_cuda()
+    from qqt_b200 import _capi
+    rows = _rows(n, 10 + n)
+    w0, b0 = _weights(3 + pid)
+    w0p = w0[:, inv_cols(2, 14, 13, 13, pid).cuda()]
+    w0.requires_grad_(True)
+    b0.requires_grad_(True)
+    h1 = _Layer1.apply(rows, w0, b0, K_IN, (2, 14, 169, pid))
+    x64 = rows[:, :K_IN].double()
+    ref = x64 @ w0p.detach().double().T + b0.detach().double()
+    err = (h1.double() - ref).abs().max().item()
+    assert err <= 1e-5 * max(1.0, ref.abs().max().item()), err
+    # gradients over twelve decades of magnitude
+    g = torch.Generator().manual_seed(7 + n)
+    dh = torch.randn((n, 128), generator=g) * torch.pow(10.0, -12 * torch.rand((n, 128), generator=g))
+    dh = (dh * 1e-3).cuda()
+    h1.backward(dh)
+    torch.cuda.synchronize()
+    assert _capi.device_error() == 0
+    gp = dh.double().T @ x64                                   # gradient of the permuted W0
+    ref_w = torch.zeros_like(gp)
+    ref_w[:, inv_cols(2, 14, 13, 13, pid).cuda()] = gp
+    scale = ref_w.abs().max().item()
+    err_w = (w0.grad.double() - ref_w).abs().max().item()
+    assert err_w <= 1e-5 * scale, (err_w, scale)
+    # db0 is torch's float32 column sum (as in the reference's autograd)
+    db_err = (b0.grad.double() - dh.double().sum(0)).abs().max().item()
+    assert db_err <= 1e-5 * dh.double().abs().sum(0).max().item()
+
+
+def test_zero_gradient_is_exact_zero():
+    _need_cuda()
+    rows = _rows(200, 4)
+    w0, b0 = _weights(5)
+    w0.requires_grad_(True)
+    h1 = _Layer1.apply(rows, w0, b0, K_IN, (2, 14, 169, 0))
+    h1.backward(torch.zeros_like(h1))
+    torch.cuda.synchronize()
+    assert not w0.grad.any()
+
+
+def test_evaluate_on_device_matches_cpu_restatement():
+    _need_cuda()
+    torch.manual_seed(0)
+    m_cpu = MLPActorCritic(SHAPE, 2)
+    m_gpu = MLPActorCritic(SHAPE, 2).cuda()
+    m_gpu.load_state_dict(m_cpu.state_dict())
+    n = 520
+    rows = _rows(n, 11)
+    obs4 = rows[:, :K_IN].cpu().view(n, *SHAPE)
+    mm = torch.rand((n, 5)) < 0.8
+    mm[:, 4] = True
+    bm = torch.rand((n, 2)) < 0.7
+    bm[:, 0] = True
+    act = torch.stack([torch.multinomial(mm.float(), 1)[:, 0],
+                       torch.multinomial(bm.float(), 1)[:, 0]], -1)
+    for pid in (0, 1):
+        outs = []
+        for m, dev, ob in ((m_cpu, "cpu", obs4), (m_gpu, "cuda", rows)):
+            m.zero_grad()
+            logp, ent, v = m.evaluate(ob, mm.to(dev), bm.to(dev), act.to(dev), pid)
+            loss = -(logp * torch.linspace(-1, 1, n, device=dev)).mean() + 0.5 * (v * v).mean() \
+                - 0.03 * ent.mean()
+            loss.backward()
+            outs.append({"logp": logp.detach().cpu(), "v": v.detach().cpu(),
+                         **{k: p.grad.detach().cpu() for k, p in m.named_parameters()}})
+        for k in outs[0]:
+            a, b = outs[0][k].double(), outs[1][k].double()
+            # outputs to 1e-5; gradients (float32 sums over the batch, in
+            # different orders on the two devices) to 5e-5 of their largest entry
+            tol = (1e-5 if k in ("logp", "v") else 5e-5) * max(1e-30, a.abs().max().item())
+            assert (a - b).abs().max().item() <= max(tol, 1e-12), k
+
+
+def test_obs_rows_pads_four_dimensional_batches():
+    x = (torch.rand((3,) + SHAPE) < 0.5).half()
+    r = obs_rows(x, K_IN)
+    assert r.shape == (3, 2368) and torch.equal(r[:, :K_IN], x.reshape(3, -1))
+    assert not r[:, K_IN:].any()
+    with pytest.raises(TypeError):
+        obs_rows(x.float(), K_IN)
