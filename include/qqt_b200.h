@@ -380,6 +380,29 @@ int qqt_l1_wgrad(const void *x, int64_t n_rows, int32_t x_stride, int32_t k_in, 
                  void *work, qqt_stream_t stream);
 uint64_t qqt_l1_wgrad_work_bytes(int64_t n_rows, int32_t k_in);
 
+/* Training forward of ActorCritic(mlp) for one seat (train/model.py:121-153,
+ * 247-256): obs rows [n_rows][obs_stride] fp16, legal masks, recorded actions
+ * [n_rows][act_stride] int64 -> logp (of the actions), entropy, value [n_rows]
+ * and the pre-LayerNorm activations h1, h2 [n_rows][128] that the backward
+ * reads.  pack = qqt_mlp_pack(..., n_seats = 1, pids = {pid}, ...). */
+int qqt_mlp_train_forward(const void *pack, const void *obs, int32_t n_rows, int32_t obs_stride,
+                          int32_t k_in, const uint8_t *mm, int32_t mm_stride, const uint8_t *bm,
+                          int32_t bm_stride, const int64_t *act, int32_t act_stride, float *logp,
+                          float *ent, float *value, float *h1, float *h2, qqt_stream_t stream);
+
+/* Backward of the layers above the first: g [3][n_rows] = dL/dlogp,
+ * dL/dentropy, dL/dvalue per row -> grads[1..19] (device pointers in
+ * qqt_mlp_param_names() order, reference shapes; grads[0], the first
+ * layer's weight, comes from qqt_l1_wgrad on dh1) and dh1 = dL/dh1
+ * [n_rows][128].  work = qqt_mlp_train_work_bytes(n_rows) bytes, 1024-byte
+ * aligned. */
+int qqt_mlp_train_backward(const void *pack, int32_t n_rows, int32_t k_in, const float *h1,
+                           const float *h2, const uint8_t *mm, int32_t mm_stride,
+                           const uint8_t *bm, int32_t bm_stride, const int64_t *act,
+                           int32_t act_stride, const float *g, float *const *grads, float *dh1,
+                           void *work, qqt_stream_t stream);
+uint64_t qqt_mlp_train_work_bytes(int32_t n_rows);
+
 /* Device error word: returns the accumulated QQT_DEV_* bits and clears
  * them (synchronises the device). */
 int qqt_get_error(uint32_t *code_out);

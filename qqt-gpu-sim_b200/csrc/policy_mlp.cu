@@ -351,6 +351,67 @@ __device__ __forceinline__ void sample_write(const float* z, int row, int seat, 
   if (value_out) value_out[(size_t)seat * n_rows + row] = z[7];
 }
 
+// Logits z of one row scored against the row's recorded actions (the
+// reference's evaluate, train/model.py:247-256): each head's masked logits
+// (illegal entries at float32's lowest value) minus their logsumexp
+// (max + log of the shifted sum), logp = lz_move[a_move] + lz_bomb[a_bomb],
+// entropy = -sum(max(lz, lowest) * exp(lz)) over both heads, value.
+__device__ __forceinline__ void score_write(const float* z, int row,
+                                            const uint8_t* __restrict__ mm, int mm_stride,
+                                            const uint8_t* __restrict__ bm, int bm_stride,
+                                            const int64_t* __restrict__ act, int act_stride,
+                                            float* __restrict__ logp_out,
+                                            float* __restrict__ ent_out,
+                                            float* __restrict__ value_out) {
+  const float lowest = -3.402823466e38f;
+  const uint8_t* mrow = mm + (size_t)row * mm_stride;
+  const uint8_t* brow = bm + (size_t)row * bm_stride;
+  float zm[5], mx = lowest;
+#pragma unroll
+  for (int k = 0; k < 5; ++k) {
+    zm[k] = mrow[k] ? z[k] : lowest;
+    mx = fmaxf(mx, zm[k]);
+  }
+  float tot = 0.f;
+#pragma unroll
+  for (int k = 0; k < 5; ++k) tot += expf(zm[k] - mx);
+  const float lse_m = logf(tot) + mx;
+  const float zb[2] = {brow[0] ? z[5] : lowest, brow[1] ? z[6] : lowest};
+  const float mb = fmaxf(zb[0], zb[1]);
+  const float lse_b = logf(expf(zb[0] - mb) + expf(zb[1] - mb)) + mb;
+  long long am = act[(size_t)row * act_stride], ab = act[(size_t)row * act_stride + 1];
+  if (am < 0 || am > 4 || ab < 0 || ab > 1) {
+    flag_error(QQT_DEV_BAD_ACTION);
+    am = 0;
+    ab = 0;
+  }
+  float lpm = 0.f, ent = 0.f;
+#pragma unroll
+  for (int k = 0; k < 5; ++k) {
+    const float lz = zm[k] - lse_m;
+    lpm = am == k ? lz : lpm;
+    ent += fmaxf(lz, lowest) * expf(lz);
+  }
+  float lpb = 0.f, entb = 0.f;
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const float lz = zb[k] - lse_b;
+    lpb = ab == k ? lz : lpb;
+    entb += fmaxf(lz, lowest) * expf(lz);
+  }
+  logp_out[row] = lpm + lpb;
+  ent_out[row] = -ent - entb;
+  value_out[row] = z[7];
+}
+
+// Training forward outputs (k_mlp_fused<128, false, true>): the pre-LN
+// activations of both trunk layers [n_rows][128] and the entropy per row.
+struct TrainOut {
+  float* h1;
+  float* h2;
+  float* ent;
+};
+
 // ------------------------------------------------------------ fused MLP
 
 struct SeatOut {
@@ -537,10 +598,13 @@ __device__ __forceinline__ uint32_t part_off(int r, int c) {
 // x[32] (+bias) -> LayerNorm over the row's 128 columns (this thread holds
 // columns 32q..32q+31; the sums go through the TMEM row exchange) -> affine
 // -> ReLU (train/model.py:121-153).
+// pre (optional): the thread's 32 pre-LayerNorm values (bias included) are
+// also written there (the training forward keeps them for the backward).
 __device__ __forceinline__ void bias_ln_relu_quarter(float* x, int q, uint32_t scr,
                                                      const float* __restrict__ bias,
                                                      const float* __restrict__ g,
-                                                     const float* __restrict__ b) {
+                                                     const float* __restrict__ b,
+                                                     float* __restrict__ pre = nullptr) {
   const int c0 = 32 * q;
   float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -550,6 +614,7 @@ __device__ __forceinline__ void bias_ln_relu_quarter(float* x, int q, uint32_t s
     x[i + 1] = __fadd_rn(x[i + 1], bb.y);
     x[i + 2] = __fadd_rn(x[i + 2], bb.z);
     x[i + 3] = __fadd_rn(x[i + 3], bb.w);
+    if (pre) *reinterpret_cast<float4*>(pre + i) = make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]);
 #pragma unroll
     for (int j = 0; j < 4; ++j) s4[j] += x[i + j];
   }
@@ -621,14 +686,15 @@ __device__ __forceinline__ void umma_split_k128(uint32_t d_tmem, const uint8_t* 
 // partial sums into their own shared memory and signal the rank-0 CTA, whose
 // epilogue adds them (rank order) to its own while applying LN1, then runs
 // the rest of the network alone.  ks = 1 is a plain one-CTA launch.
-template <int NT, bool SPLIT_A>
+template <int NT, bool SPLIT_A, bool TRAIN>
 __global__ void __launch_bounds__(kMlpThreads, 1)
 k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_alo,
             const __grid_constant__ CUtensorMap tm_b, int n_rows, int k_tiles,
             const float* __restrict__ f, const uint8_t* __restrict__ img, SeatOut io, int seat0,
             int mm_stride, int bm_stride, const float* __restrict__ u, int act_stride,
             float* __restrict__ logp_out, float* __restrict__ value_out,
-            float* __restrict__ logits_out) {
+            float* __restrict__ logits_out, TrainOut tr) {
+  static_assert(!TRAIN || (NT == 128 && !SPLIT_A), "training forward: one seat, fp16 rows");
   using G = FusedCfg<NT, SPLIT_A>;
   constexpr int S = NT / 128;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -835,7 +901,9 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
           cluster_arrive();   // done reading the other ranks' shared memory
           arrived = true;
         }
-        bias_ln_relu_quarter(x, quarter, scr, f + F_B0 + 128 * s, f + F_LN1G, f + F_LN1B);
+        bias_ln_relu_quarter(x, quarter, scr, f + F_B0 + 128 * s, f + F_LN1G, f + F_LN1B,
+                             TRAIN && row < n_rows ? tr.h1 + (size_t)row * 128 + 32 * quarter
+                                                   : nullptr);
         store_split_quarter(x, a_hi, a_lo, r, quarter);
         fence_proxy_async();
         asm volatile("tcgen05.fence::before_thread_sync;");
@@ -845,7 +913,9 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         if (!ok) break;
         asm volatile("tcgen05.fence::after_thread_sync;");
         tmem_ld32(lane_base + 128 * s + 32 * quarter, x);
-        bias_ln_relu_quarter(x, quarter, scr + 8, f + F_B1, f + F_LN2G, f + F_LN2B);
+        bias_ln_relu_quarter(x, quarter, scr + 8, f + F_B1, f + F_LN2G, f + F_LN2B,
+                             TRAIN && row < n_rows ? tr.h2 + (size_t)row * 128 + 32 * quarter
+                                                   : nullptr);
         store_split_quarter(x, a_hi, a_lo, r, quarter);
         fence_proxy_async();
         asm volatile("tcgen05.fence::before_thread_sync;");
@@ -898,8 +968,12 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
 #pragma unroll
             for (int o = 0; o < 8; ++o)
               z[o] = ((zz[o] + zz[8 + o]) + (zz[16 + o] + zz[24 + o])) + __ldg(f + F_HB2 + o);
-            sample_write(z, row, seat0 + s, n_rows, io.mm[s], mm_stride, io.bm[s], bm_stride, u,
-                         io.act[s], act_stride, logp_out, value_out, logits_out);
+            if (TRAIN)
+              score_write(z, row, io.mm[s], mm_stride, io.bm[s], bm_stride, io.act[s],
+                          act_stride, logp_out, tr.ent, value_out);
+            else
+              sample_write(z, row, seat0 + s, n_rows, io.mm[s], mm_stride, io.bm[s], bm_stride,
+                           u, io.act[s], act_stride, logp_out, value_out, logits_out);
           }
         }
       }
@@ -937,14 +1011,14 @@ static int mlp_split_k(int m_tiles, int k_tiles) {
   return min(ks, max(1, k_tiles / 2));
 }
 
-template <int NT, bool SPLIT_A>
+template <int NT, bool SPLIT_A, bool TRAIN = false>
 static int launch_mlp_fused(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap& mb,
                             int n_rows, int k_tiles, const float* f, const uint8_t* img,
                             const SeatOut& io, int seat0, int mm_stride, int bm_stride,
                             const float* u, int act_stride, float* logp, float* value,
-                            float* logits, cudaStream_t st) {
+                            float* logits, cudaStream_t st, TrainOut tr = TrainOut{}) {
   using G = FusedCfg<NT, SPLIT_A>;
-  auto kern = k_mlp_fused<NT, SPLIT_A>;
+  auto kern = k_mlp_fused<NT, SPLIT_A, TRAIN>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
   const int m_tiles = (n_rows + kBM - 1) / kBM;
   const int ks = mlp_split_k(m_tiles, k_tiles);
@@ -961,7 +1035,7 @@ static int launch_mlp_fused(const CUtensorMap& ma, const CUtensorMap& malo, cons
   cfg.attrs = attr;
   cfg.numAttrs = ks > 1 ? 1 : 0;
   if (cudaLaunchKernelEx(&cfg, kern, ma, malo, mb, n_rows, k_tiles, f, img, io, seat0, mm_stride,
-                         bm_stride, u, act_stride, logp, value, logits) != cudaSuccess)
+                         bm_stride, u, act_stride, logp, value, logits, tr) != cudaSuccess)
     return QQT_E_LAUNCH;
   return launch_status();
 }

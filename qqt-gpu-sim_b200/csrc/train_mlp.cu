@@ -248,6 +248,15 @@ __global__ void k_absmax(const float4* __restrict__ x, int64_t n4, uint32_t* __r
   if (lane_id() == 0 && w != 0u) atomicMax(out, w);
 }
 
+__global__ void k_absmax_n(const float* __restrict__ x, int64_t n, uint32_t* __restrict__ out) {
+  float m = 0.f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    m = fmaxf(m, fabsf(__ldg(x + i)));
+  const uint32_t w = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
+  if (lane_id() == 0 && w != 0u) atomicMax(out, w);
+}
+
 __global__ void k_dh_split(const float4* __restrict__ dh, int64_t n4,
                            const uint32_t* __restrict__ amax_bits, uint2* __restrict__ hi,
                            uint2* __restrict__ lo) {
@@ -485,6 +494,841 @@ static WgradWork wgrad_work_layout(int64_t n_rows, int kp) {
   return w;
 }
 
+// ---------------------------------------------------------------- tail backward
+//
+// The layers above the first, backward, for every row of a minibatch
+// (train/model.py:121-153 through autograd).  Two persistent kernels with
+// the block layout of k_mlp_fused (warp 0 loads, warp 1 issues MMAs, 16
+// epilogue warps with four threads per row: TMEM lane quadrant x column
+// quarter):
+//
+// k_tail_heads_bwd  per 128-row tile: LN2 of the saved h2 -> r2 (the same
+//   operations as the forward, so the values agree bit for bit) -> fp16 hi/lo
+//   operand; u = r2 Wh0^T on the tensor cores (the three head hidden layers,
+//   N = 192); per row the head outputs, the masked log-softmax of each head
+//   and, from the incoming dL/dlogp, dL/dentropy, dL/dvalue, the gradient of
+//   every logit; back through the output layers and the ReLUs to dL/du,
+//   scaled by a power of two bounded from the incoming gradients and split
+//   into fp16 hi / lo.  Then dr2 = du Wh0 (Wh0's operand image read MN-major)
+//   and dWh0^T += r2^T du (both operands MN-major views of the K-major
+//   images), accumulated in TMEM over all the CTA's tiles; LN2 backward to
+//   dL/dh2 (written out, float32).
+// k_tail_trunk_bwd  per tile: LN1 of the saved h1 -> r1 operand; dL/dh2
+//   scaled by the power of two from its maximum -> hi/lo operand;
+//   dr1 = dh2 W1 and dW1^T += r1^T dh2 in TMEM; LN1 backward to dL/dh1.
+//
+// Small gradients (biases, LayerNorm affine, the head output layers) are
+// summed over each warp's 32 rows by a shuffle reduce-scatter (lane l keeps
+// element l of a 32-vector) into per-thread registers; the per-CTA partial
+// sums are combined in a fixed order by k_tail_reduce.
+
+constexpr uint32_t kTbScr = 384;                   // TMEM row-exchange scratch columns
+constexpr int kActB = kBM * 128 * 2;               // one fp16 [128 x 128] operand image
+constexpr int kThWh = 0;                           // heads kernel: Wh0 image hi, lo
+constexpr int kThR = 2 * (int)kImgH0Bytes;         //   r2 operand hi, lo
+constexpr int kThD = kThR + 2 * kActB;             //   du operand hi, lo (two heads at a time)
+constexpr int kThBytes = kThD + 2 * kActB;
+constexpr int kThSmem = kThBytes + 1024 + 256;
+constexpr int kTtW = 0;                            // trunk kernel: W1 image hi, lo
+constexpr int kTtR = 2 * (int)kImgW1Bytes;         //   r1 operand hi, lo
+constexpr int kTtD = kTtR + 2 * kActB;             //   dh2 operand hi, lo
+constexpr int kTtBytes = kTtD + 2 * kActB;
+constexpr int kTtSmem = kTtBytes + 1024 + 256;
+constexpr int kThAcc = 10;                         // per-thread small-gradient accumulators
+constexpr int kTtAcc = 3;
+static_assert(kThSmem <= 232448 && kTtSmem <= 232448, "tail backward shared memory");
+
+__device__ __forceinline__ void tmem_st2(uint32_t taddr, float a, float b) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1, %2};" ::"r"(taddr),
+               "r"(__float_as_uint(a)), "r"(__float_as_uint(b))
+               : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Sum of a[32] over the warp's 32 lanes, element `lane` kept by each lane
+// (five halving exchanges; a is clobbered).
+__device__ __forceinline__ float reduce_scatter32(float* a) {
+  const int lane = lane_id();
+#pragma unroll
+  for (int st = 0; st < 5; ++st) {
+    const int s = 16 >> st;
+    const bool up = (lane & s) != 0;
+#pragma unroll
+    for (int i = 0; i < (16 >> st); ++i) {
+      const float send = up ? a[i] : a[i + (16 >> st)];
+      const float keep = up ? a[i + (16 >> st)] : a[i];
+      a[i] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+    }
+  }
+  return a[0];
+}
+
+// Mean and 1/sqrt(var + 1e-5) of the row (this thread holds 32 of its 128
+// values) in bias_ln_relu_quarter's operation order.
+__device__ __forceinline__ void ln_stats_quarter(const float* x, int q, uint32_t scr, float& mean,
+                                                 float& rstd) {
+  float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < 32; i += 4)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s4[j] += x[i + j];
+  float p[4];
+  row_exchange4(scr, q, (s4[0] + s4[1]) + (s4[2] + s4[3]), p);
+  mean = ((p[0] + p[1]) + (p[2] + p[3])) * (1.f / 128.f);
+  float v4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < 32; i += 4)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float d = x[i + j] - mean;
+      v4[j] = fmaf(d, d, v4[j]);
+    }
+  row_exchange4(scr + 4, q, (v4[0] + v4[1]) + (v4[2] + v4[3]), p);
+  rstd = rsqrtf(((p[0] + p[1]) + (p[2] + p[3])) * (1.f / 128.f) + 1e-5f);
+}
+
+// 32 floats of row `row` (columns 32q..) or zeros past the last row.
+__device__ __forceinline__ void load_quarter(const float* __restrict__ src, int row, int n_rows,
+                                             int q, float* x) {
+  if (row < n_rows) {
+    const float4* p = reinterpret_cast<const float4*>(src + (size_t)row * 128 + 32 * q);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 v = __ldg(p + i);
+      x[4 * i] = v.x;
+      x[4 * i + 1] = v.y;
+      x[4 * i + 2] = v.z;
+      x[4 * i + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) x[i] = 0.f;
+  }
+}
+
+// n (8 or 16) values times 2^s as fp16 hi / lo at K columns k0.. of row r of
+// a K-major [128 x K] operand image pair.
+template <int N>
+__device__ __forceinline__ void store_split_scaled(const float* x, float scale, uint8_t* a_hi,
+                                                   uint8_t* a_lo, int r, int k0) {
+#pragma unroll
+  for (int c = 0; c < N / 8; ++c) {
+    uint32_t hv[4], lv[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float v0 = x[8 * c + 2 * j] * scale, v1 = x[8 * c + 2 * j + 1] * scale;
+      const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+      const __half l0 = __float2half_rn(__fsub_rn(v0, __half2float(h0)));
+      const __half l1 = __float2half_rn(__fsub_rn(v1, __half2float(h1)));
+      hv[j] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+      lv[j] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+    }
+    const uint32_t off = sw128_off(r, k0 + 8 * c, kBM);
+    *reinterpret_cast<uint4*>(a_hi + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+    *reinterpret_cast<uint4*>(a_lo + off) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+  }
+}
+
+// kind::f16 descriptor: A K-major, B MN-major.
+__host__ __device__ constexpr uint32_t idesc_f16_kmn(int m, int n) {
+  return (1u << 4) | (1u << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// Gradient of the head logits of one row (train/model.py:247-256 through
+// autograd): lz = z - logsumexp(z) per head over the legal entries,
+// logp = lz_m[a_m] + lz_b[a_b], entropy = -sum(max(lz, lowest) exp(lz)).
+//   dL/dlz_k = gl [k == a] - ge exp(lz_k) ([lz_k >= lowest] + max(lz_k, lowest))
+//   dL/dz_j  = legal_j * (dL/dlz_j - softmax_j * sum_k dL/dlz_k)
+// and dL/dvalue = gv.
+__device__ __forceinline__ void head_grad(const float* z, bool live, const uint8_t* mrow,
+                                          const uint8_t* brow, int am, int ab, float gl, float ge,
+                                          float gv, float* dz) {
+  const float lowest = -3.402823466e38f;
+#pragma unroll
+  for (int o = 0; o < 8; ++o) dz[o] = 0.f;
+  if (!live) return;
+  float zm[5], mx = lowest;
+  bool lg[5];
+#pragma unroll
+  for (int k = 0; k < 5; ++k) {
+    lg[k] = mrow[k] != 0;
+    zm[k] = lg[k] ? z[k] : lowest;
+    mx = fmaxf(mx, zm[k]);
+  }
+  float tot = 0.f;
+#pragma unroll
+  for (int k = 0; k < 5; ++k) tot += expf(zm[k] - mx);
+  const float lse = logf(tot) + mx;
+  float G[5], p[5], sg = 0.f;
+#pragma unroll
+  for (int k = 0; k < 5; ++k) {
+    const float lz = zm[k] - lse;
+    p[k] = expf(lz);
+    const float cl = fmaxf(lz, lowest);
+    G[k] = (k == am ? gl : 0.f) - ge * (p[k] * ((lz >= lowest ? 1.f : 0.f) + cl));
+    sg += G[k];
+  }
+#pragma unroll
+  for (int k = 0; k < 5; ++k) dz[k] = lg[k] ? G[k] - p[k] * sg : 0.f;
+  const bool b0 = brow[0] != 0, b1 = brow[1] != 0;
+  const float zb0 = b0 ? z[5] : lowest, zb1 = b1 ? z[6] : lowest;
+  const float mb = fmaxf(zb0, zb1);
+  const float lseb = logf(expf(zb0 - mb) + expf(zb1 - mb)) + mb;
+  const float l0 = zb0 - lseb, l1 = zb1 - lseb;
+  const float p0 = expf(l0), p1 = expf(l1);
+  const float G0 = (ab == 0 ? gl : 0.f) - ge * (p0 * ((l0 >= lowest ? 1.f : 0.f) + fmaxf(l0, lowest)));
+  const float G1 = (ab == 1 ? gl : 0.f) - ge * (p1 * ((l1 >= lowest ? 1.f : 0.f) + fmaxf(l1, lowest)));
+  const float sb = G0 + G1;
+  dz[5] = b0 ? G0 - p0 * sb : 0.f;
+  dz[6] = b1 ? G1 - p1 * sb : 0.f;
+  dz[7] = gv;
+}
+
+struct TailArgs {
+  const float* h;          // saved pre-LN activations [n][128]: h2 (heads) / h1 (trunk)
+  const float* dh_in;      // trunk: dL/dh2 [n][128]
+  const uint8_t* mm;       // heads: legal moves [n][mm_stride], bomb [n][bm_stride]
+  const uint8_t* bm;
+  const int64_t* act;      // heads: recorded actions [n][act_stride]
+  const float* g;          // heads: [3][n] dL/dlogp, dL/dentropy, dL/dvalue
+  const uint32_t* amax;    // heads: max |g|; trunk: max |dL/dh2|
+  float* dh_out;           // dL/dh2 (heads) / dL/dh1 (trunk) [n][128]
+  float* wpart;            // [grid][out rows][128] per-CTA weight-gradient sums
+  float* apart;            // [grid][16 warps][32 lanes][acc] per-thread small sums
+  int mm_stride, bm_stride, act_stride;
+};
+
+// Closing sequence shared by both kernels: every tcgen05 operation of the
+// CTA has completed before warp 0 frees the TMEM.
+__device__ __forceinline__ void tail_teardown(uint32_t tmem) {
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  if (warp_id() == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+  }
+}
+
+__global__ void __launch_bounds__(kMlpThreads, 1)
+k_tail_heads_bwd(TailArgs a, const float* __restrict__ f, const uint8_t* __restrict__ img,
+                 int n_rows) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* wbar = (uint64_t*)(smem + kThBytes);
+  uint64_t* abar = wbar + 1;     // r2 operand written (512 arrivals)
+  uint64_t* ubar = abar + 1;     // u complete
+  uint64_t* d1bar = ubar + 1;    // du of heads 0, 1 written (512)
+  uint64_t* m2bar = d1bar + 1;   // MMAs on heads 0, 1 complete
+  uint64_t* d2bar = m2bar + 1;   // du of head 2 written (512)
+  uint64_t* m3bar = d2bar + 1;   // MMAs on head 2 complete
+  uint32_t* tmem_slot = (uint32_t*)(m3bar + 1);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  int* du_exp = (int*)(tmem_slot + 2);
+  const int warp = warp_id(), lane = lane_id();
+  const int n_tiles = (n_rows + kBM - 1) / kBM;
+  uint8_t* wh_hi = smem + kThWh;
+  uint8_t* wh_lo = wh_hi + kImgH0Bytes;
+  uint8_t* r_hi = smem + kThR;
+  uint8_t* r_lo = r_hi + kActB;
+  uint8_t* d_hi = smem + kThD;
+  uint8_t* d_lo = d_hi + kActB;
+
+  if (threadIdx.x == 0) {
+    mbar_init(wbar, 1);
+    mbar_init(abar, kEpiThreads);
+    mbar_init(ubar, 1);
+    mbar_init(d1bar, kEpiThreads);
+    mbar_init(m2bar, 1);
+    mbar_init(d2bar, kEpiThreads);
+    mbar_init(m3bar, 1);
+    *abort_flag = 0;
+    // |dL/du| <= 8 max|g| max_u sum_o |Wk2[o][u]| (the logit gradients are at
+    // most 2|dL/dlogp| + 4|dL/dentropy|, the value's |dL/dvalue|)
+    float colmax = 0.f;
+    for (int u = 0; u < 64; ++u) {
+      float s0 = 0.f, s1 = 0.f;
+      for (int o = 0; o < 5; ++o) s0 += fabsf(f[F_HW2 + o * 64 + u]);
+      for (int o = 5; o < 7; ++o) s1 += fabsf(f[F_HW2 + o * 64 + u]);
+      colmax = fmaxf(colmax, fmaxf(fmaxf(s0, s1), fabsf(f[F_HW2 + 7 * 64 + u])));
+    }
+    const float bound = 8.f * __uint_as_float(*a.amax) * colmax;
+    const uint32_t bb = __float_as_uint(bound);
+    *du_exp = dh_scale_exp(&bb);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t c_u = 192;                    // u (N = 192), then dr2 (N = 128)
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_expect_tx(wbar, 2 * kImgH0Bytes);
+      for (uint32_t o = 0; o < 2 * kImgH0Bytes; o += 16384)
+        bulk_load(wh_hi + o, img + kImgH0 + o, 16384, wbar);
+      mbar_wait(wbar, 0);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id_u = idesc_f16(kBM, 192);
+      const uint32_t id_dr = idesc_f16_kmn(kBM, 128);
+      const uint32_t id_w2 = idesc_f16_mn(kBM, 128), id_w1 = idesc_f16_mn(kBM, 64);
+      int committed = 0;
+      bool ok = mbar_wait(wbar, 0);
+      for (int tile = blockIdx.x, lt = 0; tile < n_tiles && ok; tile += gridDim.x, ++lt) {
+        const uint32_t par = (uint32_t)(lt & 1);
+        if (!mbar_wait(abar, par) || *abort_flag) { ok = false; break; }
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        umma_split_k128(tmem + c_u, r_hi, r_lo, wh_hi, wh_lo, 192, id_u);
+        umma_commit(ubar);
+        ++committed;
+        if (!mbar_wait(d1bar, par) || *abort_flag) { ok = false; break; }
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        // dr2 = du(heads 0, 1) Wh0[rows 0..127]: A K-major (K = hidden units),
+        // B = Wh0's image read MN-major (N = 128 inputs, K = its rows)
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t ao = (uint32_t)(kb * 16384 + kk * 32);
+            const uint32_t bo = (uint32_t)((64 * kb + 16 * kk) * 128);
+            const uint64_t ah = sw128_desc(d_hi + ao), al = sw128_desc(d_lo + ao);
+            const uint64_t bh = sw128_mn_desc(wh_hi + bo, 192 * 128);
+            const uint64_t bl = sw128_mn_desc(wh_lo + bo, 192 * 128);
+            umma_f16(tmem + c_u, ah, bh, id_dr, (kb | kk) ? 1u : 0u);
+            umma_f16(tmem + c_u, ah, bl, id_dr, 1u);
+            umma_f16(tmem + c_u, al, bh, id_dr, 1u);
+          }
+        // dWh0^T[:, 0..127] += r2^T du(heads 0, 1): both operands MN-major
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t o = (uint32_t)(kk * 2048);
+          const uint64_t ah = sw128_mn_desc(r_hi + o, 16384), al = sw128_mn_desc(r_lo + o, 16384);
+          const uint64_t bh = sw128_mn_desc(d_hi + o, 16384), bl = sw128_mn_desc(d_lo + o, 16384);
+          umma_f16(tmem, ah, bh, id_w2, (lt > 0 || kk > 0) ? 1u : 0u);
+          umma_f16(tmem, ah, bl, id_w2, 1u);
+          umma_f16(tmem, al, bh, id_w2, 1u);
+        }
+        umma_commit(m2bar);
+        ++committed;
+        if (!mbar_wait(d2bar, par) || *abort_flag) { ok = false; break; }
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        // head 2 (its du in the first K block)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t ao = (uint32_t)(kk * 32);
+          const uint32_t bo = (uint32_t)((128 + 16 * kk) * 128);
+          const uint64_t ah = sw128_desc(d_hi + ao), al = sw128_desc(d_lo + ao);
+          const uint64_t bh = sw128_mn_desc(wh_hi + bo, 192 * 128);
+          const uint64_t bl = sw128_mn_desc(wh_lo + bo, 192 * 128);
+          umma_f16(tmem + c_u, ah, bh, id_dr, 1u);
+          umma_f16(tmem + c_u, ah, bl, id_dr, 1u);
+          umma_f16(tmem + c_u, al, bh, id_dr, 1u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t o = (uint32_t)(kk * 2048);
+          const uint64_t ah = sw128_mn_desc(r_hi + o, 16384), al = sw128_mn_desc(r_lo + o, 16384);
+          const uint64_t bh = sw128_mn_desc(d_hi + o, 16384), bl = sw128_mn_desc(d_lo + o, 16384);
+          umma_f16(tmem + 128, ah, bh, id_w1, (lt > 0 || kk > 0) ? 1u : 0u);
+          umma_f16(tmem + 128, ah, bl, id_w1, 1u);
+          umma_f16(tmem + 128, al, bh, id_w1, 1u);
+        }
+        umma_commit(m3bar);
+        ++committed;
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        // the last commit must land before the CTA may exit
+        if (committed > 0) {
+          uint64_t* lastb = (committed % 3 == 1) ? ubar : (committed % 3 == 2 ? m2bar : m3bar);
+          mbar_wait(lastb, (uint32_t)(((committed - 1) / 3) & 1));
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue: row r = 32 * (warp % 4) + lane, quarter q
+    const int qd = warp & 3;
+    const int q = (warp - 2) >> 2;
+    const int r = qd * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(qd * 32) << 16);
+    const uint32_t scr = lane_base + kTbScr;
+    const float dscale = pow2f(*du_exp), undo = pow2f(-*du_exp);
+    float acc[kThAcc];
+#pragma unroll
+    for (int i = 0; i < kThAcc; ++i) acc[i] = 0.f;
+    bool ok = true;
+    for (int tile = blockIdx.x, lt = 0; tile < n_tiles; tile += gridDim.x, ++lt) {
+      const uint32_t par = (uint32_t)(lt & 1);
+      const int row = tile * kBM + r;
+      // E1: LN2 of h2 -> r2 operand
+      float x[32], mean, rstd;
+      load_quarter(a.h, row, n_rows, q, x);
+      ln_stats_quarter(x, q, scr, mean, rstd);
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        const float4 gg = __ldg(reinterpret_cast<const float4*>(f + F_LN2G + 32 * q + i));
+        const float4 be = __ldg(reinterpret_cast<const float4*>(f + F_LN2B + 32 * q + i));
+        x[i] = fmaxf(fmaf((x[i] - mean) * rstd, gg.x, be.x), 0.f);
+        x[i + 1] = fmaxf(fmaf((x[i + 1] - mean) * rstd, gg.y, be.y), 0.f);
+        x[i + 2] = fmaxf(fmaf((x[i + 2] - mean) * rstd, gg.z, be.z), 0.f);
+        x[i + 3] = fmaxf(fmaf((x[i + 3] - mean) * rstd, gg.w, be.w), 0.f);
+      }
+      store_split_quarter(x, r_hi, r_lo, r, q);
+      fence_proxy_async();
+      asm volatile("tcgen05.fence::before_thread_sync;");
+      mbar_arrive(abar);
+      // E2: head outputs and their gradients
+      ok = epi_and(mbar_wait(ubar, par) && *abort_flag == 0);
+      if (!ok) break;
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      float z[8];
+#pragma unroll
+      for (int o = 0; o < 8; ++o) z[o] = 0.f;
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        const int u0 = 64 * k + 16 * q;        // this thread's 16 units of head k
+        float h[16];
+        tmem_ld16(lane_base + c_u + u0, h);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) h[i] = fmaxf(__fadd_rn(h[i], __ldg(f + F_HB0 + u0 + i)), 0.f);
+        const int o_lo = k == 0 ? 0 : (k == 1 ? 5 : 7), o_hi = k == 0 ? 5 : (k == 1 ? 7 : 8);
+#pragma unroll
+        for (int o = 0; o < 8; ++o) {
+          if (o < o_lo || o >= o_hi) continue;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) z[o] = fmaf(__ldg(f + F_HW2 + o * 64 + 16 * q + i), h[i], z[o]);
+        }
+      }
+      tmem_st8(scr + 16 + 8 * q, z);
+      asm volatile("tcgen05.fence::before_thread_sync;");
+      epi_sync();
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      float dz[8];
+      {
+        float zz[32];
+        tmem_ld32(scr + 16, zz);
+#pragma unroll
+        for (int o = 0; o < 8; ++o)
+          z[o] = ((zz[o] + zz[8 + o]) + (zz[16 + o] + zz[24 + o])) + __ldg(f + F_HB2 + o);
+        const bool live = row < n_rows;
+        const size_t rw = live ? (size_t)row : 0;
+        const int64_t am = live ? a.act[rw * a.act_stride] : 0;
+        const int64_t ab = live ? a.act[rw * a.act_stride + 1] : 0;
+        head_grad(z, live, a.mm + rw * a.mm_stride, a.bm + rw * a.bm_stride,
+                  (am >= 0 && am < 5) ? (int)am : -1, (ab >= 0 && ab < 2) ? (int)ab : -1,
+                  live ? a.g[rw] : 0.f, live ? a.g[(size_t)n_rows + rw] : 0.f,
+                  live ? a.g[2 * (size_t)n_rows + rw] : 0.f, dz);
+      }
+      // heads 0 and 1: dL/du, the output-layer and hidden-bias sums, du operand
+      float dub[32];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int u0 = 64 * k + 16 * q;
+        float h[16], du[16];
+        tmem_ld16(lane_base + c_u + u0, h);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float g = __fadd_rn(h[i], __ldg(f + F_HB0 + u0 + i));
+          h[i] = fmaxf(g, 0.f);
+          float d = 0.f;
+          if (k == 0) {
+#pragma unroll
+            for (int o = 0; o < 5; ++o) d = fmaf(dz[o], __ldg(f + F_HW2 + o * 64 + 16 * q + i), d);
+          } else {
+#pragma unroll
+            for (int o = 5; o < 7; ++o) d = fmaf(dz[o], __ldg(f + F_HW2 + o * 64 + 16 * q + i), d);
+          }
+          du[i] = g > 0.f ? d : 0.f;
+          dub[16 * k + i] = du[i];
+        }
+        if (k == 0) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) { v[i] = h[i] * dz[0]; v[16 + i] = h[i] * dz[1]; }
+          acc[0] += reduce_scatter32(v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) { v[i] = h[i] * dz[2]; v[16 + i] = h[i] * dz[3]; }
+          acc[1] += reduce_scatter32(v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) { v[i] = h[i] * dz[4]; v[16 + i] = 0.f; }
+          acc[2] += reduce_scatter32(v);
+        } else {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) { v[i] = h[i] * dz[5]; v[16 + i] = h[i] * dz[6]; }
+          acc[3] += reduce_scatter32(v);
+        }
+        store_split_scaled<16>(du, dscale, d_hi, d_lo, r, 64 * k + 16 * q);
+      }
+      acc[5] += reduce_scatter32(dub);
+      fence_proxy_async();
+      asm volatile("tcgen05.fence::before_thread_sync;");
+      mbar_arrive(d1bar);
+      // head 2 once the MMAs have released the du operand
+      ok = epi_and(mbar_wait(m2bar, par) && *abort_flag == 0);
+      if (!ok) break;
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      {
+        const int u0 = 128 + 16 * q;
+        float h[16], du[16], v[32];
+        tmem_ld16(lane_base + c_u + u0, h);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float g = __fadd_rn(h[i], __ldg(f + F_HB0 + u0 + i));
+          h[i] = fmaxf(g, 0.f);
+          du[i] = g > 0.f ? dz[7] * __ldg(f + F_HW2 + 7 * 64 + 16 * q + i) : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) { v[i] = h[i] * dz[7]; v[16 + i] = 0.f; }
+        acc[4] += reduce_scatter32(v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = du[i];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) { v[16 + i] = q == 0 ? dz[i] : 0.f; v[24 + i] = 0.f; }
+        acc[6] += reduce_scatter32(v);
+        store_split_scaled<16>(du, dscale, d_hi, d_lo, r, 16 * q);
+      }
+      fence_proxy_async();
+      asm volatile("tcgen05.fence::before_thread_sync;");
+      mbar_arrive(d2bar);
+      // E3: LN2 backward
+      ok = epi_and(mbar_wait(m3bar, par) && *abort_flag == 0);
+      if (!ok) break;
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      float dr[32];
+      tmem_ld32(lane_base + c_u + 32 * q, dr);
+      load_quarter(a.h, row, n_rows, q, x);
+      float s1 = 0.f, s2 = 0.f;
+      {
+        float vg[32], vb[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float xh = (x[i] - mean) * rstd;
+          const float gm = __ldg(f + F_LN2G + 32 * q + i);
+          const float av = fmaf(xh, gm, __ldg(f + F_LN2B + 32 * q + i));
+          const float da = av > 0.f ? dr[i] * undo : 0.f;
+          vb[i] = da;
+          vg[i] = da * xh;
+          const float dxh = da * gm;
+          dr[i] = dxh;
+          x[i] = xh;
+          s1 += dxh;
+          s2 = fmaf(dxh, xh, s2);
+        }
+        acc[7] += reduce_scatter32(vg);
+        acc[8] += reduce_scatter32(vb);
+      }
+      tmem_st2(scr + 8 + 2 * q, s1, s2);
+      asm volatile("tcgen05.fence::before_thread_sync;");
+      epi_sync();
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      float ss[8];
+      tmem_ld8(scr + 8, ss);
+      const float m1 = ((ss[0] + ss[2]) + (ss[4] + ss[6])) * (1.f / 128.f);
+      const float m2 = ((ss[1] + ss[3]) + (ss[5] + ss[7])) * (1.f / 128.f);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) dr[i] = (dr[i] - m1 - x[i] * m2) * rstd;
+      if (row < n_rows) {
+        float4* out = reinterpret_cast<float4*>(a.dh_out + (size_t)row * 128 + 32 * q);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          out[i] = make_float4(dr[4 * i], dr[4 * i + 1], dr[4 * i + 2], dr[4 * i + 3]);
+      }
+      acc[9] += reduce_scatter32(dr);
+    }
+    if (!ok) *abort_flag = 1;
+    // per-thread sums, then the dWh0^T accumulator (lane = input, column = unit)
+    float* ap = a.apart + (((size_t)blockIdx.x * kEpiWarps + (warp - 2)) * 32 + lane) * kThAcc;
+#pragma unroll
+    for (int i = 0; i < kThAcc; ++i) ap[i] = acc[i];
+    if (ok && blockIdx.x < n_tiles) {
+#pragma unroll 1
+      for (int c = 0; c < 3; ++c) {
+        float v[16];
+        tmem_ld16(lane_base + 48 * q + 16 * c, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          a.wpart[((size_t)blockIdx.x * 192 + 48 * q + 16 * c + i) * 128 + r] = v[i] * undo;
+      }
+    }
+  }
+  tail_teardown(tmem);
+}
+
+__global__ void __launch_bounds__(kMlpThreads, 1)
+k_tail_trunk_bwd(TailArgs a, const float* __restrict__ f, const uint8_t* __restrict__ img,
+                 int n_rows) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* wbar = (uint64_t*)(smem + kTtBytes);
+  uint64_t* abar = wbar + 1;     // r1 and dh2 operands written (512 arrivals)
+  uint64_t* m1bar = abar + 1;    // the tile's MMAs complete
+  uint32_t* tmem_slot = (uint32_t*)(m1bar + 1);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  const int warp = warp_id(), lane = lane_id();
+  const int n_tiles = (n_rows + kBM - 1) / kBM;
+  uint8_t* w_hi = smem + kTtW;
+  uint8_t* w_lo = w_hi + kImgW1Bytes;
+  uint8_t* r_hi = smem + kTtR;
+  uint8_t* r_lo = r_hi + kActB;
+  uint8_t* d_hi = smem + kTtD;
+  uint8_t* d_lo = d_hi + kActB;
+
+  if (threadIdx.x == 0) {
+    mbar_init(wbar, 1);
+    mbar_init(abar, kEpiThreads);
+    mbar_init(m1bar, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t c_dr = 128;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_expect_tx(wbar, 2 * kImgW1Bytes);
+      for (uint32_t o = 0; o < 2 * kImgW1Bytes; o += 16384)
+        bulk_load(w_hi + o, img + kImgW1 + o, 16384, wbar);
+      mbar_wait(wbar, 0);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id_dr = idesc_f16_kmn(kBM, 128), id_w = idesc_f16_mn(kBM, 128);
+      int committed = 0;
+      bool ok = mbar_wait(wbar, 0);
+      for (int tile = blockIdx.x, lt = 0; tile < n_tiles && ok; tile += gridDim.x, ++lt) {
+        if (!mbar_wait(abar, (uint32_t)(lt & 1)) || *abort_flag) { ok = false; break; }
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        // dr1 = dh2 W1: A K-major (K = outputs), B = W1's image read MN-major
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t ao = (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32);
+          const uint32_t bo = (uint32_t)(kk * 2048);
+          const uint64_t ah = sw128_desc(d_hi + ao), al = sw128_desc(d_lo + ao);
+          const uint64_t bh = sw128_mn_desc(w_hi + bo, 16384), bl = sw128_mn_desc(w_lo + bo, 16384);
+          umma_f16(tmem + c_dr, ah, bh, id_dr, kk ? 1u : 0u);
+          umma_f16(tmem + c_dr, ah, bl, id_dr, 1u);
+          umma_f16(tmem + c_dr, al, bh, id_dr, 1u);
+        }
+        // dW1^T += r1^T dh2: both MN-major, K = the tile's rows
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t o = (uint32_t)(kk * 2048);
+          const uint64_t ah = sw128_mn_desc(r_hi + o, 16384), al = sw128_mn_desc(r_lo + o, 16384);
+          const uint64_t bh = sw128_mn_desc(d_hi + o, 16384), bl = sw128_mn_desc(d_lo + o, 16384);
+          umma_f16(tmem, ah, bh, id_w, (lt > 0 || kk > 0) ? 1u : 0u);
+          umma_f16(tmem, ah, bl, id_w, 1u);
+          umma_f16(tmem, al, bh, id_w, 1u);
+        }
+        umma_commit(m1bar);
+        ++committed;
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        if (committed > 0) mbar_wait(m1bar, (uint32_t)((committed - 1) & 1));
+      }
+    }
+  } else {
+    const int qd = warp & 3;
+    const int q = (warp - 2) >> 2;
+    const int r = qd * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(qd * 32) << 16);
+    const uint32_t scr = lane_base + kTbScr - 128;   // columns 256..: free in this kernel
+    const int dexp = dh_scale_exp(a.amax);
+    const float dscale = pow2f(dexp), undo = pow2f(-dexp);
+    float acc[kTtAcc] = {0.f, 0.f, 0.f};
+    bool ok = true;
+    for (int tile = blockIdx.x, lt = 0; tile < n_tiles; tile += gridDim.x, ++lt) {
+      const int row = tile * kBM + r;
+      float x[32], mean, rstd;
+      load_quarter(a.h, row, n_rows, q, x);
+      ln_stats_quarter(x, q, scr, mean, rstd);
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        const float4 gg = __ldg(reinterpret_cast<const float4*>(f + F_LN1G + 32 * q + i));
+        const float4 be = __ldg(reinterpret_cast<const float4*>(f + F_LN1B + 32 * q + i));
+        x[i] = fmaxf(fmaf((x[i] - mean) * rstd, gg.x, be.x), 0.f);
+        x[i + 1] = fmaxf(fmaf((x[i + 1] - mean) * rstd, gg.y, be.y), 0.f);
+        x[i + 2] = fmaxf(fmaf((x[i + 2] - mean) * rstd, gg.z, be.z), 0.f);
+        x[i + 3] = fmaxf(fmaf((x[i + 3] - mean) * rstd, gg.w, be.w), 0.f);
+      }
+      store_split_quarter(x, r_hi, r_lo, r, q);
+      load_quarter(a.dh_in, row, n_rows, q, x);
+      store_split_scaled<32>(x, dscale, d_hi, d_lo, r, 32 * q);
+      fence_proxy_async();
+      asm volatile("tcgen05.fence::before_thread_sync;");
+      mbar_arrive(abar);
+      ok = epi_and(mbar_wait(m1bar, (uint32_t)(lt & 1)) && *abort_flag == 0);
+      if (!ok) break;
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      float dr[32];
+      tmem_ld32(lane_base + c_dr + 32 * q, dr);
+      load_quarter(a.h, row, n_rows, q, x);
+      float s1 = 0.f, s2 = 0.f;
+      {
+        float vg[32], vb[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float xh = (x[i] - mean) * rstd;
+          const float gm = __ldg(f + F_LN1G + 32 * q + i);
+          const float av = fmaf(xh, gm, __ldg(f + F_LN1B + 32 * q + i));
+          const float da = av > 0.f ? dr[i] * undo : 0.f;
+          vb[i] = da;
+          vg[i] = da * xh;
+          const float dxh = da * gm;
+          dr[i] = dxh;
+          x[i] = xh;
+          s1 += dxh;
+          s2 = fmaf(dxh, xh, s2);
+        }
+        acc[0] += reduce_scatter32(vg);
+        acc[1] += reduce_scatter32(vb);
+      }
+      tmem_st2(scr + 8 + 2 * q, s1, s2);
+      asm volatile("tcgen05.fence::before_thread_sync;");
+      epi_sync();
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      float ss[8];
+      tmem_ld8(scr + 8, ss);
+      const float m1 = ((ss[0] + ss[2]) + (ss[4] + ss[6])) * (1.f / 128.f);
+      const float m2 = ((ss[1] + ss[3]) + (ss[5] + ss[7])) * (1.f / 128.f);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) dr[i] = (dr[i] - m1 - x[i] * m2) * rstd;
+      if (row < n_rows) {
+        float4* out = reinterpret_cast<float4*>(a.dh_out + (size_t)row * 128 + 32 * q);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          out[i] = make_float4(dr[4 * i], dr[4 * i + 1], dr[4 * i + 2], dr[4 * i + 3]);
+      }
+      acc[2] += reduce_scatter32(dr);
+    }
+    if (!ok) *abort_flag = 1;
+    float* ap = a.apart + (((size_t)blockIdx.x * kEpiWarps + (warp - 2)) * 32 + lane) * kTtAcc;
+#pragma unroll
+    for (int i = 0; i < kTtAcc; ++i) ap[i] = acc[i];
+    if (ok && blockIdx.x < n_tiles) {
+      float v[32];
+      tmem_ld32(lane_base + 32 * q, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        a.wpart[((size_t)blockIdx.x * 128 + 32 * q + i) * 128 + r] = v[i] * undo;
+    }
+  }
+  tail_teardown(tmem);
+}
+
+// Parameter gradients from the per-CTA partial sums, in CTA order (one
+// thread per output element; deterministic).
+//   dWh0: wpart_h [grid][192][128] -> the three head hidden weights
+//   dW1:  wpart_t [grid][128][128]
+//   small sums: thread (warp 2 + 4q + m, lane l) of each CTA holds element l
+//   of the 32-vectors built for quarter q.
+struct TailGrads {
+  float* p[20];            // reference state_dict order (qqt_mlp_param_names)
+};
+
+__device__ __forceinline__ float sum_acc(const float* ap, int grid, int nacc, int q, int lane,
+                                         int slot) {
+  float s = 0.f;
+  for (int c = 0; c < grid; ++c)
+    for (int m = 0; m < 4; ++m)
+      s += ap[(((size_t)c * kEpiWarps + 4 * q + m) * 32 + lane) * nacc + slot];
+  return s;
+}
+
+__global__ void k_tail_reduce(const float* __restrict__ wph, const float* __restrict__ aph,
+                              const float* __restrict__ wpt, const float* __restrict__ apt,
+                              int grid, TailGrads gr) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < 192 * 128) {
+    float s = 0.f;
+    for (int c = 0; c < grid; ++c) s += wph[(size_t)c * 192 * 128 + i];
+    const int u = i >> 7, k = i & 127;
+    gr.p[8 + 4 * (u >> 6)][(u & 63) * 128 + k] = s;      // move/bomb/critic .0.weight
+  }
+  if (i < 128 * 128) {
+    float s = 0.f;
+    for (int c = 0; c < grid; ++c) s += wpt[(size_t)c * 128 * 128 + i];
+    gr.p[4][i] = s;                                       // shared.3.weight [out][in]
+  }
+  if (i < 128) {
+    const int q = i >> 5, l = i & 31;
+    gr.p[6][i] = sum_acc(aph, grid, kThAcc, q, l, 7);     // shared.4.weight (LN2 gamma)
+    gr.p[7][i] = sum_acc(aph, grid, kThAcc, q, l, 8);     // shared.4.bias
+    gr.p[5][i] = sum_acc(aph, grid, kThAcc, q, l, 9);     // shared.3.bias
+    gr.p[2][i] = sum_acc(apt, grid, kTtAcc, q, l, 0);     // shared.1.weight (LN1 gamma)
+    gr.p[3][i] = sum_acc(apt, grid, kTtAcc, q, l, 1);     // shared.1.bias
+    gr.p[1][i] = sum_acc(apt, grid, kTtAcc, q, l, 2);     // shared.0.bias
+  }
+  if (i < 4 * 32) {
+    // head output layers and hidden biases: quarter q, lane l
+    const int q = i >> 5, l = i & 31;
+    const int ul = 16 * q + (l & 15);                     // unit within its head
+    const int hi = l >> 4;
+    gr.p[10][(2 * 0 + hi) * 64 + ul] = sum_acc(aph, grid, kThAcc, q, l, 0);   // move.2 o 0/1
+    gr.p[10][(2 + hi) * 64 + ul] = sum_acc(aph, grid, kThAcc, q, l, 1);       // o 2/3
+    if (!hi) gr.p[10][4 * 64 + ul] = sum_acc(aph, grid, kThAcc, q, l, 2);     // o 4
+    gr.p[14][hi * 64 + ul] = sum_acc(aph, grid, kThAcc, q, l, 3);             // bomb.2 o 0/1
+    if (!hi) gr.p[18][ul] = sum_acc(aph, grid, kThAcc, q, l, 4);              // critic.2
+    gr.p[hi ? 13 : 9][ul] = sum_acc(aph, grid, kThAcc, q, l, 5);              // move/bomb .0.bias
+    if (!hi) gr.p[17][ul] = sum_acc(aph, grid, kThAcc, q, l, 6);              // critic.0.bias
+    if (q == 0 && l >= 16 && l < 24) {
+      const int o = l - 16;
+      const float s = sum_acc(aph, grid, kThAcc, 0, l, 6);
+      if (o < 5) gr.p[11][o] = s;                         // move.2.bias
+      else if (o < 7) gr.p[15][o - 5] = s;                // bomb.2.bias
+      else gr.p[19][0] = s;                               // critic.2.bias
+    }
+  }
+}
+
+struct TrainWork {
+  size_t amax_g, amax_d, dh2, wph, aph, wpt, apt, total;
+};
+
+static TrainWork train_work_layout(int n_rows) {
+  const int grid = max(1, min((n_rows + kBM - 1) / kBM, sm_count()));
+  TrainWork w;
+  auto up = [](size_t v) { return (v + 1023) / 1024 * 1024; };
+  w.amax_g = 0;
+  w.amax_d = 256;
+  w.dh2 = 1024;
+  w.wph = w.dh2 + up((size_t)n_rows * 128 * 4);
+  w.aph = w.wph + up((size_t)grid * 192 * 128 * 4);
+  w.wpt = w.aph + up((size_t)grid * kEpiThreads * kThAcc * 4);
+  w.apt = w.wpt + up((size_t)grid * 128 * 128 * 4);
+  w.total = w.apt + up((size_t)grid * kEpiThreads * kTtAcc * 4);
+  return w;
+}
+
 }  // namespace qqt
 
 extern "C" uint64_t qqt_l1_pack_bytes(int32_t k_in) {
@@ -586,5 +1430,114 @@ extern "C" int qqt_l1_wgrad(const void* x, int64_t n_rows, int32_t x_stride, int
   const int64_t n_out = (int64_t)128 * k_in;
   k_wgrad_reduce<<<(unsigned)((n_out + 255) / 256), 256, 0, st>>>(part, slices, kp, k_in, hw, cs,
                                                                  amax, dw0);
+  return launch_status();
+}
+
+// ---- training forward / tail backward of the MLP (one seat, pack from
+// qqt_mlp_pack with n_seats = 1 and the seat's pid)
+
+extern "C" int qqt_mlp_train_forward(const void* pack, const void* obs, int32_t n_rows,
+                                     int32_t obs_stride, int32_t k_in, const uint8_t* mm,
+                                     int32_t mm_stride, const uint8_t* bm, int32_t bm_stride,
+                                     const int64_t* act, int32_t act_stride, float* logp,
+                                     float* ent, float* value, float* h1, float* h2,
+                                     qqt_stream_t stream) {
+  if (!pack || !obs || !mm || !bm || !act || !logp || !ent || !value || !h1 || !h2)
+    return QQT_E_ARG;
+  if (n_rows <= 0 || k_in <= 0 || obs_stride < k_in || mm_stride < 5 || bm_stride < 2 ||
+      act_stride < 2)
+    return QQT_E_ARG;
+  if ((obs_stride % 8) || ((uintptr_t)obs & 15) || ((uintptr_t)pack & 255) ||
+      ((uintptr_t)h1 & 15) || ((uintptr_t)h2 & 15))
+    return QQT_E_ALIGN;
+  const MlpPack L = mlp_pack_layout(k_in, 1);
+  const uint8_t* pk = (const uint8_t*)pack;
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, obs, (uint64_t)k_in, (uint64_t)n_rows, (uint64_t)obs_stride * 2, kBM))
+    return QQT_E_ARG;
+  if (!make_map(&mb, pk + L.b_off, (uint64_t)L.kp, 256, (uint64_t)L.kp * 2, 128))
+    return QQT_E_ARG;
+  SeatOut io;
+  memset(&io, 0, sizeof(io));
+  io.mm[0] = mm;
+  io.bm[0] = bm;
+  io.act[0] = const_cast<int64_t*>(act);
+  TrainOut tr;
+  tr.h1 = h1;
+  tr.h2 = h2;
+  tr.ent = ent;
+  return launch_mlp_fused<128, false, true>(ma, ma, mb, n_rows, L.kp / kBK,
+                                            (const float*)(pk + L.f_off), pk + L.img_off, io, 0,
+                                            mm_stride, bm_stride, nullptr, act_stride, logp,
+                                            value, nullptr, (cudaStream_t)stream, tr);
+}
+
+extern "C" uint64_t qqt_mlp_train_work_bytes(int32_t n_rows) {
+  if (n_rows <= 0) return 0;
+  return train_work_layout(n_rows).total;
+}
+
+extern "C" int qqt_mlp_train_backward(const void* pack, int32_t n_rows, int32_t k_in,
+                                      const float* h1, const float* h2, const uint8_t* mm,
+                                      int32_t mm_stride, const uint8_t* bm, int32_t bm_stride,
+                                      const int64_t* act, int32_t act_stride, const float* g,
+                                      float* const* grads, float* dh1, void* work,
+                                      qqt_stream_t stream) {
+  if (!pack || !h1 || !h2 || !mm || !bm || !act || !g || !grads || !dh1 || !work)
+    return QQT_E_ARG;
+  if (n_rows <= 0 || k_in <= 0 || mm_stride < 5 || bm_stride < 2 || act_stride < 2)
+    return QQT_E_ARG;
+  for (int i = 1; i < 20; ++i)
+    if (!grads[i]) return QQT_E_ARG;
+  if (((uintptr_t)pack & 255) || ((uintptr_t)h1 & 15) || ((uintptr_t)h2 & 15) ||
+      ((uintptr_t)dh1 & 15) || ((uintptr_t)work & 1023))
+    return QQT_E_ALIGN;
+  const MlpPack L = mlp_pack_layout(k_in, 1);
+  const uint8_t* pk = (const uint8_t*)pack;
+  const float* fpar = (const float*)(pk + L.f_off);
+  const uint8_t* img = pk + L.img_off;
+  const TrainWork W = train_work_layout(n_rows);
+  uint8_t* wk = (uint8_t*)work;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int sms = sm_count();
+  const int grid = max(1, min((n_rows + kBM - 1) / kBM, sms));
+  if (cudaMemsetAsync(wk, 0, 512, st) != cudaSuccess) return QQT_E_LAUNCH;
+  const int64_t ng = 3 * (int64_t)n_rows;
+  k_absmax_n<<<(unsigned)max((int64_t)1, min((ng + 255) / 256, (int64_t)sms * 4)), 256, 0, st>>>(
+      g, ng, (uint32_t*)(wk + W.amax_g));
+  TailArgs a;
+  memset(&a, 0, sizeof(a));
+  a.h = h2;
+  a.mm = mm;
+  a.bm = bm;
+  a.act = act;
+  a.g = g;
+  a.amax = (const uint32_t*)(wk + W.amax_g);
+  a.dh_out = (float*)(wk + W.dh2);
+  a.wpart = (float*)(wk + W.wph);
+  a.apart = (float*)(wk + W.aph);
+  a.mm_stride = mm_stride;
+  a.bm_stride = bm_stride;
+  a.act_stride = act_stride;
+  cudaFuncSetAttribute(k_tail_heads_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, kThSmem);
+  k_tail_heads_bwd<<<grid, kMlpThreads, kThSmem, st>>>(a, fpar, img, n_rows);
+  const int64_t nd = (int64_t)n_rows * 128;
+  k_absmax_n<<<(unsigned)max((int64_t)1, min((nd + 255) / 256, (int64_t)sms * 8)), 256, 0, st>>>(
+      (const float*)(wk + W.dh2), nd, (uint32_t*)(wk + W.amax_d));
+  TailArgs b;
+  memset(&b, 0, sizeof(b));
+  b.h = h1;
+  b.dh_in = (const float*)(wk + W.dh2);
+  b.amax = (const uint32_t*)(wk + W.amax_d);
+  b.dh_out = dh1;
+  b.wpart = (float*)(wk + W.wpt);
+  b.apart = (float*)(wk + W.apt);
+  cudaFuncSetAttribute(k_tail_trunk_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, kTtSmem);
+  k_tail_trunk_bwd<<<grid, kMlpThreads, kTtSmem, st>>>(b, fpar, img, n_rows);
+  TailGrads gr;
+  for (int i = 0; i < 20; ++i) gr.p[i] = grads[i];
+  k_tail_reduce<<<(192 * 128 + 255) / 256, 256, 0, st>>>(
+      (const float*)(wk + W.wph), (const float*)(wk + W.aph), (const float*)(wk + W.wpt),
+      (const float*)(wk + W.apt), grid, gr);
   return launch_status();
 }

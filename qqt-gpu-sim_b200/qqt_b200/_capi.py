@@ -105,6 +105,11 @@ def lib():
             "qqt_l1_wgrad": (c_i32, [c_p, c_i64, c_i32, c_i32, c_p, c_i32, c_i32, c_i32, c_i32,
                                      c_p, c_p, c_p]),
             "qqt_l1_wgrad_work_bytes": (c_u64, [c_i64, c_i32]),
+            "qqt_mlp_train_forward": (c_i32, [c_p, c_p, c_i32, c_i32, c_i32, c_p, c_i32, c_p,
+                                              c_i32, c_p, c_i32, c_p, c_p, c_p, c_p, c_p, c_p]),
+            "qqt_mlp_train_backward": (c_i32, [c_p, c_i32, c_i32, c_p, c_p, c_p, c_i32, c_p,
+                                               c_i32, c_p, c_i32, c_p, c_p, c_p, c_p, c_p]),
+            "qqt_mlp_train_work_bytes": (c_u64, [c_i32]),
             "qqt_get_error": (c_i32, [P(ctypes.c_uint32)]),
             "qqt_version": (ctypes.c_char_p, []),
         }

@@ -10,14 +10,16 @@ clipping and Adam.  The network is ActorCritic(mlp) with the reference's
 parameter names, so its parameters feed B200Policy's packed weights directly
 (`B200Policy.repack()` after each update).
 
-On the GPU the first layer, Linear(2366 -> 128), the one real contraction of
-the update, runs on the tensor-core kernels of csrc/train_mlp.cu from the
+On the GPU every minibatch runs on the kernels of csrc/train_mlp.cu from the
 rollout's float16 observation rows: the minibatch's rows are gathered by a
-kernel (the reference's `obs[sel]`), the forward product and the weight
-gradient are tcgen05 GEMMs with float32-accurate hi/lo operand splits, and no
-float32 copy of the observations is made.  The 128-wide layers above it run
-through torch autograd.  CPU tensors (the gloo tests) take the torch
-restatement of the same layer.
+kernel (the reference's `obs[sel]`); `evaluate` is one fused tcgen05 forward
+(all four layers, the masked log-softmax of both heads, entropy and value,
+keeping the two pre-LayerNorm activations); the PPO loss over the per-row
+(logp, entropy, value) stays in torch autograd; its gradients go back
+through two persistent tcgen05 kernels (heads + LN2, trunk + LN1) and the
+first layer's weight-gradient GEMM.  Products carry float32 accuracy
+through fp16 hi/lo operand splits.  CPU tensors (the gloo tests) take the
+torch restatement of the same network.
 """
 
 from __future__ import annotations
@@ -145,6 +147,74 @@ class _Layer1(torch.autograd.Function):
         return None, dw0, dh1.sum(0), None, None
 
 
+class _MLPTrain(torch.autograd.Function):
+    """ActorCritic(mlp).evaluate (train/model.py:121-153, 247-256) on the B200
+    kernels: returns per-row (logp of the recorded actions, entropy, value);
+    backward gives every parameter's gradient in the reference's layouts.
+    params: the 20 tensors in state_dict order."""
+
+    @staticmethod
+    def forward(ctx, rows, mm, bm, act, geom, *params):
+        from . import _capi as capi
+        n_players, c, hw, pid = geom
+        k_in = c * hw
+        L, dev = capi.lib(), rows.device
+        st = capi.stream_ptr(dev)
+        pc = [p.detach().contiguous() for p in params]
+        pack = torch.empty(int(L.qqt_mlp_pack_bytes(k_in, 1)) + 256, dtype=torch.uint8, device=dev)
+        pk = _aligned(pack, 256)
+        ptrs = (ctypes.c_void_p * 20)(*[p.data_ptr() for p in pc])
+        pids = (ctypes.c_int32 * 2)(pid, 0)
+        capi.check(L.qqt_mlp_pack(ptrs, k_in, n_players, c, hw, 1, pids, pk, st), "qqt_mlp_pack")
+        n = rows.shape[0]
+        mm8 = mm.contiguous().view(torch.uint8)
+        bm8 = bm.contiguous().view(torch.uint8)
+        a64 = act.to(torch.int64).contiguous()
+        logp, ent, v = (torch.empty(n, dtype=torch.float32, device=dev) for _ in range(3))
+        h1, h2 = (torch.empty((n, 128), dtype=torch.float32, device=dev) for _ in range(2))
+        capi.check(L.qqt_mlp_train_forward(pk, rows.data_ptr(), n, rows.stride(0), k_in,
+                                           mm8.data_ptr(), mm8.stride(0), bm8.data_ptr(),
+                                           bm8.stride(0), a64.data_ptr(), a64.stride(0),
+                                           logp.data_ptr(), ent.data_ptr(), v.data_ptr(),
+                                           h1.data_ptr(), h2.data_ptr(), st),
+                   "qqt_mlp_train_forward")
+        ctx.save_for_backward(rows, mm8, bm8, a64, h1, h2)
+        ctx.pack, ctx.pk, ctx.geom = pack, pk, geom
+        ctx.shapes = [p.shape for p in params]
+        return logp, ent, v
+
+    @staticmethod
+    def backward(ctx, gl, ge, gv):
+        from . import _capi as capi
+        rows, mm8, bm8, a64, h1, h2 = ctx.saved_tensors
+        n_players, c, hw, pid = ctx.geom
+        k_in = c * hw
+        L, dev = capi.lib(), rows.device
+        st = capi.stream_ptr(dev)
+        n = rows.shape[0]
+        g = torch.zeros((3, n), dtype=torch.float32, device=dev)
+        for i, gi in enumerate((gl, ge, gv)):
+            if gi is not None:
+                g[i] = gi
+        grads = [torch.empty(s, dtype=torch.float32, device=dev) for s in ctx.shapes]
+        dh1 = torch.empty((n, 128), dtype=torch.float32, device=dev)
+        work = torch.empty(int(L.qqt_mlp_train_work_bytes(n)) + 1024, dtype=torch.uint8,
+                           device=dev)
+        ptrs = (ctypes.c_void_p * 20)(*[t.data_ptr() for t in grads])
+        capi.check(L.qqt_mlp_train_backward(ctx.pk, n, k_in, h1.data_ptr(), h2.data_ptr(),
+                                            mm8.data_ptr(), mm8.stride(0), bm8.data_ptr(),
+                                            bm8.stride(0), a64.data_ptr(), a64.stride(0),
+                                            g.data_ptr(), ptrs, dh1.data_ptr(),
+                                            _aligned(work, 1024), st),
+                   "qqt_mlp_train_backward")
+        wk = torch.empty(int(L.qqt_l1_wgrad_work_bytes(n, k_in)) + 1024, dtype=torch.uint8,
+                         device=dev)
+        capi.check(L.qqt_l1_wgrad(rows.data_ptr(), n, rows.stride(0), k_in, dh1.data_ptr(),
+                                  n_players, c, hw, pid, grads[0].data_ptr(),
+                                  _aligned(wk, 1024), st), "qqt_l1_wgrad")
+        return (None, None, None, None, None, *grads)
+
+
 class MLPActorCritic(nn.Module):
     """ActorCritic(arch="mlp") for training (same parameter names)."""
 
@@ -186,6 +256,10 @@ class MLPActorCritic(nn.Module):
     def evaluate(self, obs, mm, bm, actions, pid: int = 0):
         """(log-prob of `actions`, entropy, value) under the masked heads
         (train/model.py:247-256)."""
+        if obs.is_cuda:
+            c, h, w = self.obs_shape
+            return _MLPTrain.apply(obs_rows(obs, self.k_in), mm, bm, actions,
+                                   (self.n_players, c, h * w, pid), *self.parameters())
         ml, bl, v = self(obs, pid)
         lm = self._masked(ml, mm)
         lb = self._masked(bl, bm)
