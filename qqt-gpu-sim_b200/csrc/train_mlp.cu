@@ -534,7 +534,7 @@ constexpr int kTtR = 2 * (int)kImgW1Bytes;         //   r1 operand hi, lo
 constexpr int kTtD = kTtR + 2 * kActB;             //   dh2 operand hi, lo
 constexpr int kTtBytes = kTtD + 2 * kActB;
 constexpr int kTtSmem = kTtBytes + 1024 + 256;
-constexpr int kThAcc = 10;                         // per-thread small-gradient accumulators
+constexpr int kThAcc = 9;                          // per-thread small-gradient accumulators
 constexpr int kTtAcc = 3;
 static_assert(kThSmem <= 232448 && kTtSmem <= 232448, "tail backward shared memory");
 
@@ -695,6 +695,38 @@ __device__ __forceinline__ void head_grad(const float* z, bool live, const uint8
   dz[7] = gv;
 }
 
+// LayerNorm + affine + ReLU backward for the thread's 32 columns: x holds
+// the pre-LN values (-> x-hat), dr the gradient of the ReLU output times
+// 2^s (-> dL/dx-hat); the gamma and beta sums of the warp's rows go into
+// acc_g, acc_b (reduce-scatter), s1 / s2 are the thread's parts of
+// sum(dx-hat) and sum(dx-hat * x-hat).
+__device__ __forceinline__ void ln_relu_backward(float* x, float* dr, float mean, float rstd,
+                                                 float undo, const float* __restrict__ g,
+                                                 const float* __restrict__ b, float& acc_g,
+                                                 float& acc_b, float& s1, float& s2) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float xh = (x[i] - mean) * rstd;
+    const float av = fmaf(xh, __ldg(g + i), __ldg(b + i));
+    x[i] = xh;
+    dr[i] = av > 0.f ? dr[i] * undo : 0.f;
+  }
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = dr[i];
+  acc_b += reduce_scatter32(v);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = dr[i] * x[i];
+  acc_g += reduce_scatter32(v);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float dxh = dr[i] * __ldg(g + i);
+    dr[i] = dxh;
+    s1 += dxh;
+    s2 = fmaf(dxh, x[i], s2);
+  }
+}
+
 struct TailArgs {
   const float* h;          // saved pre-LN activations [n][128]: h2 (heads) / h1 (trunk)
   const float* dh_in;      // trunk: dL/dh2 [n][128]
@@ -709,9 +741,27 @@ struct TailArgs {
   int mm_stride, bm_stride, act_stride;
 };
 
-// Closing sequence shared by both kernels: every tcgen05 operation of the
-// CTA has completed before warp 0 frees the TMEM.
-__device__ __forceinline__ void tail_teardown(uint32_t tmem) {
+// A read-only load the compiler keeps in place: the per-layer parameters
+// are read again where they are used instead of being held in registers
+// across the whole tile loop.
+__device__ __forceinline__ float ldg_keep(const float* p) {
+  float v;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+
+// Both backward kernels run 16 warps, all of them epilogue warps (row r =
+// 32 * (warp % 4) + lane, column quarter warp / 4); thread 0 also brings in
+// the resident weight image and issues the tile's MMA groups, each after the
+// barrier on which all 512 threads announced the operand it reads.  With no
+// separate producer and MMA warps every thread may hold 128 registers.
+constexpr int kTbThreads = kEpiThreads;
+
+// Wait (bounded) for the last commit thread 0 made, so that no MMA is in
+// flight when the TMEM is freed; then free it.
+__device__ __forceinline__ void tail_teardown(uint32_t tmem, uint64_t* last, uint32_t parity,
+                                              bool pending) {
+  if (threadIdx.x == 0 && pending) mbar_wait(last, parity);
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
   if (warp_id() == 0) {
@@ -720,7 +770,7 @@ __device__ __forceinline__ void tail_teardown(uint32_t tmem) {
   }
 }
 
-__global__ void __launch_bounds__(kMlpThreads, 1)
+__global__ void __launch_bounds__(kTbThreads, 1)
 k_tail_heads_bwd(TailArgs a, const float* __restrict__ f, const uint8_t* __restrict__ img,
                  int n_rows) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -743,14 +793,15 @@ k_tail_heads_bwd(TailArgs a, const float* __restrict__ f, const uint8_t* __restr
   uint8_t* r_lo = r_hi + kActB;
   uint8_t* d_hi = smem + kThD;
   uint8_t* d_lo = d_hi + kActB;
+  const bool issuer = threadIdx.x == 0;
 
-  if (threadIdx.x == 0) {
+  if (issuer) {
     mbar_init(wbar, 1);
-    mbar_init(abar, kEpiThreads);
+    mbar_init(abar, kTbThreads);
     mbar_init(ubar, 1);
-    mbar_init(d1bar, kEpiThreads);
+    mbar_init(d1bar, kTbThreads);
     mbar_init(m2bar, 1);
-    mbar_init(d2bar, kEpiThreads);
+    mbar_init(d2bar, kTbThreads);
     mbar_init(m3bar, 1);
     *abort_flag = 0;
     // |dL/du| <= 8 max|g| max_u sum_o |Wk2[o][u]| (the logit gradients are at
@@ -766,6 +817,9 @@ k_tail_heads_bwd(TailArgs a, const float* __restrict__ f, const uint8_t* __restr
     const uint32_t bb = __float_as_uint(bound);
     *du_exp = dh_scale_exp(&bb);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_expect_tx(wbar, 2 * kImgH0Bytes);
+    for (uint32_t o = 0; o < 2 * kImgH0Bytes; o += 16384)
+      bulk_load(wh_hi + o, img + kImgH0 + o, 16384, wbar);
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -778,29 +832,144 @@ k_tail_heads_bwd(TailArgs a, const float* __restrict__ f, const uint8_t* __restr
   asm volatile("tcgen05.fence::after_thread_sync;");
   const uint32_t tmem = *tmem_slot;
   const uint32_t c_u = 192;                    // u (N = 192), then dr2 (N = 128)
+  const uint32_t id_u = idesc_f16(kBM, 192);
+  const uint32_t id_dr = idesc_f16_kmn(kBM, 128);
+  const uint32_t id_w2 = idesc_f16_mn(kBM, 128), id_w1 = idesc_f16_mn(kBM, 64);
+  int committed = 0;                           // thread 0: commits made (3 per tile)
+  bool wload = issuer ? mbar_wait(wbar, 0) : true;
 
-  if (warp == 0) {
-    if (lane == 0) {
-      mbar_expect_tx(wbar, 2 * kImgH0Bytes);
-      for (uint32_t o = 0; o < 2 * kImgH0Bytes; o += 16384)
-        bulk_load(wh_hi + o, img + kImgH0 + o, 16384, wbar);
-      mbar_wait(wbar, 0);
+  const int qd = warp & 3;
+  const int q = warp >> 2;
+  const int r = qd * 32 + lane;
+  const uint32_t lane_base = tmem + ((uint32_t)(qd * 32) << 16);
+  const uint32_t scr = lane_base + kTbScr;
+  const float dscale = pow2f(*du_exp), undo = pow2f(-*du_exp);
+  float acc[kThAcc];
+#pragma unroll
+  for (int i = 0; i < kThAcc; ++i) acc[i] = 0.f;
+  bool ok = epi_and(wload);
+  for (int tile = blockIdx.x, lt = 0; tile < n_tiles && ok; tile += gridDim.x, ++lt) {
+    const uint32_t par = (uint32_t)(lt & 1);
+    const int row = tile * kBM + r;
+    // E1: LN2 of h2 -> r2 operand
+    float x[32], mean, rstd;
+    load_quarter(a.h, row, n_rows, q, x);
+    ln_stats_quarter(x, q, scr, mean, rstd);
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      const float4 gg = __ldg(reinterpret_cast<const float4*>(f + F_LN2G + 32 * q + i));
+      const float4 be = __ldg(reinterpret_cast<const float4*>(f + F_LN2B + 32 * q + i));
+      x[i] = fmaxf(fmaf((x[i] - mean) * rstd, gg.x, be.x), 0.f);
+      x[i + 1] = fmaxf(fmaf((x[i + 1] - mean) * rstd, gg.y, be.y), 0.f);
+      x[i + 2] = fmaxf(fmaf((x[i + 2] - mean) * rstd, gg.z, be.z), 0.f);
+      x[i + 3] = fmaxf(fmaf((x[i + 3] - mean) * rstd, gg.w, be.w), 0.f);
     }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t id_u = idesc_f16(kBM, 192);
-      const uint32_t id_dr = idesc_f16_kmn(kBM, 128);
-      const uint32_t id_w2 = idesc_f16_mn(kBM, 128), id_w1 = idesc_f16_mn(kBM, 64);
-      int committed = 0;
-      bool ok = mbar_wait(wbar, 0);
-      for (int tile = blockIdx.x, lt = 0; tile < n_tiles && ok; tile += gridDim.x, ++lt) {
-        const uint32_t par = (uint32_t)(lt & 1);
-        if (!mbar_wait(abar, par) || *abort_flag) { ok = false; break; }
+    store_split_quarter(x, r_hi, r_lo, r, q);
+    fence_proxy_async();
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    mbar_arrive(abar);
+    if (issuer) {
+      if (mbar_wait(abar, par) && !*abort_flag) {
         asm volatile("tcgen05.fence::after_thread_sync;");
         umma_split_k128(tmem + c_u, r_hi, r_lo, wh_hi, wh_lo, 192, id_u);
         umma_commit(ubar);
         ++committed;
-        if (!mbar_wait(d1bar, par) || *abort_flag) { ok = false; break; }
+      } else {
+        *abort_flag = 1;
+      }
+    }
+    // E2: head outputs and their gradients
+    ok = epi_and(mbar_wait(ubar, par) && *abort_flag == 0);
+    if (!ok) break;
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    float z[8];
+#pragma unroll
+    for (int o = 0; o < 8; ++o) z[o] = 0.f;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const int u0 = 64 * k + 16 * q;          // this thread's 16 units of head k
+      float h[16];
+      tmem_ld16(lane_base + c_u + u0, h);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) h[i] = fmaxf(__fadd_rn(h[i], ldg_keep(f + F_HB0 + u0 + i)), 0.f);
+      const int o_lo = k == 0 ? 0 : (k == 1 ? 5 : 7), o_hi = k == 0 ? 5 : (k == 1 ? 7 : 8);
+#pragma unroll
+      for (int o = 0; o < 8; ++o) {
+        if (o < o_lo || o >= o_hi) continue;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) z[o] = fmaf(ldg_keep(f + F_HW2 + o * 64 + 16 * q + i), h[i], z[o]);
+      }
+    }
+    tmem_st8(scr + 16 + 8 * q, z);
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    epi_sync();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    float dz[8];
+    {
+      float zz[32];
+      tmem_ld32(scr + 16, zz);
+#pragma unroll
+      for (int o = 0; o < 8; ++o)
+        z[o] = ((zz[o] + zz[8 + o]) + (zz[16 + o] + zz[24 + o])) + __ldg(f + F_HB2 + o);
+      const bool live = row < n_rows;
+      const size_t rw = live ? (size_t)row : 0;
+      const int64_t am = live ? a.act[rw * a.act_stride] : 0;
+      const int64_t ab = live ? a.act[rw * a.act_stride + 1] : 0;
+      head_grad(z, live, a.mm + rw * a.mm_stride, a.bm + rw * a.bm_stride,
+                (am >= 0 && am < 5) ? (int)am : -1, (ab >= 0 && ab < 2) ? (int)ab : -1,
+                live ? a.g[rw] : 0.f, live ? a.g[(size_t)n_rows + rw] : 0.f,
+                live ? a.g[2 * (size_t)n_rows + rw] : 0.f, dz);
+    }
+    // heads 0 and 1: dL/du, the output-layer and hidden-bias sums, du operand.
+    // 32-vectors (lane l keeps element l): acc0 = [q0 dz0 | q0 dz1],
+    // acc1 = [q0 dz2 | q0 dz3], acc2 = [q0 dz4 | du0], acc3 = [q1 dz5 | q1 dz6],
+    // acc4 = [du1 | dz0..7 (quarter 0) | 0], acc5 = [q2 dz7 | du2]
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int u0 = 64 * k + 16 * q;
+      float h[16], du[16], v[32];
+      tmem_ld16(lane_base + c_u + u0, h);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float g = __fadd_rn(h[i], ldg_keep(f + F_HB0 + u0 + i));
+        h[i] = fmaxf(g, 0.f);
+        float d = 0.f;
+        if (k == 0) {
+#pragma unroll
+          for (int o = 0; o < 5; ++o) d = fmaf(dz[o], ldg_keep(f + F_HW2 + o * 64 + 16 * q + i), d);
+        } else {
+#pragma unroll
+          for (int o = 5; o < 7; ++o) d = fmaf(dz[o], ldg_keep(f + F_HW2 + o * 64 + 16 * q + i), d);
+        }
+        du[i] = g > 0.f ? d : 0.f;
+      }
+      if (k == 0) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) { v[i] = h[i] * dz[0]; v[16 + i] = h[i] * dz[1]; }
+        acc[0] += reduce_scatter32(v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) { v[i] = h[i] * dz[2]; v[16 + i] = h[i] * dz[3]; }
+        acc[1] += reduce_scatter32(v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) { v[i] = h[i] * dz[4]; v[16 + i] = du[i]; }
+        acc[2] += reduce_scatter32(v);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) { v[i] = h[i] * dz[5]; v[16 + i] = h[i] * dz[6]; }
+        acc[3] += reduce_scatter32(v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = du[i];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) { v[16 + i] = q == 0 ? dz[i] : 0.f; v[24 + i] = 0.f; }
+        acc[4] += reduce_scatter32(v);
+      }
+      store_split_scaled<16>(du, dscale, d_hi, d_lo, r, 64 * k + 16 * q);
+    }
+    fence_proxy_async();
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    mbar_arrive(d1bar);
+    if (issuer) {
+      if (mbar_wait(d1bar, par) && !*abort_flag) {
         asm volatile("tcgen05.fence::after_thread_sync;");
         // dr2 = du(heads 0, 1) Wh0[rows 0..127]: A K-major (K = hidden units),
         // B = Wh0's image read MN-major (N = 128 inputs, K = its rows)
@@ -829,7 +998,34 @@ k_tail_heads_bwd(TailArgs a, const float* __restrict__ f, const uint8_t* __restr
         }
         umma_commit(m2bar);
         ++committed;
-        if (!mbar_wait(d2bar, par) || *abort_flag) { ok = false; break; }
+      } else {
+        *abort_flag = 1;
+      }
+    }
+    // head 2 once the MMAs have released the du operand
+    ok = epi_and(mbar_wait(m2bar, par) && *abort_flag == 0);
+    if (!ok) break;
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    {
+      const int u0 = 128 + 16 * q;
+      float h[16], du[16], v[32];
+      tmem_ld16(lane_base + c_u + u0, h);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float g = __fadd_rn(h[i], ldg_keep(f + F_HB0 + u0 + i));
+        h[i] = fmaxf(g, 0.f);
+        du[i] = g > 0.f ? dz[7] * ldg_keep(f + F_HW2 + 7 * 64 + 16 * q + i) : 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) { v[i] = h[i] * dz[7]; v[16 + i] = du[i]; }
+      acc[5] += reduce_scatter32(v);
+      store_split_scaled<16>(du, dscale, d_hi, d_lo, r, 16 * q);
+    }
+    fence_proxy_async();
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    mbar_arrive(d2bar);
+    if (issuer) {
+      if (mbar_wait(d2bar, par) && !*abort_flag) {
         asm volatile("tcgen05.fence::after_thread_sync;");
         // head 2 (its du in the first K block)
 #pragma unroll
@@ -854,227 +1050,58 @@ k_tail_heads_bwd(TailArgs a, const float* __restrict__ f, const uint8_t* __restr
         }
         umma_commit(m3bar);
         ++committed;
-      }
-      if (!ok) {
+      } else {
         *abort_flag = 1;
-        // the last commit must land before the CTA may exit
-        if (committed > 0) {
-          uint64_t* lastb = (committed % 3 == 1) ? ubar : (committed % 3 == 2 ? m2bar : m3bar);
-          mbar_wait(lastb, (uint32_t)(((committed - 1) / 3) & 1));
-        }
       }
     }
-  } else {
-    // ---------------- epilogue: row r = 32 * (warp % 4) + lane, quarter q
-    const int qd = warp & 3;
-    const int q = (warp - 2) >> 2;
-    const int r = qd * 32 + lane;
-    const uint32_t lane_base = tmem + ((uint32_t)(qd * 32) << 16);
-    const uint32_t scr = lane_base + kTbScr;
-    const float dscale = pow2f(*du_exp), undo = pow2f(-*du_exp);
-    float acc[kThAcc];
+    // E3: LN2 backward
+    ok = epi_and(mbar_wait(m3bar, par) && *abort_flag == 0);
+    if (!ok) break;
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    float dr[32];
+    tmem_ld32(lane_base + c_u + 32 * q, dr);
+    load_quarter(a.h, row, n_rows, q, x);
+    float s1 = 0.f, s2 = 0.f;
+    ln_relu_backward(x, dr, mean, rstd, undo, f + F_LN2G + 32 * q, f + F_LN2B + 32 * q, acc[6],
+                     acc[7], s1, s2);
+    tmem_st2(scr + 8 + 2 * q, s1, s2);
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    epi_sync();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    float ss[8];
+    tmem_ld8(scr + 8, ss);
+    const float m1 = ((ss[0] + ss[2]) + (ss[4] + ss[6])) * (1.f / 128.f);
+    const float m2 = ((ss[1] + ss[3]) + (ss[5] + ss[7])) * (1.f / 128.f);
 #pragma unroll
-    for (int i = 0; i < kThAcc; ++i) acc[i] = 0.f;
-    bool ok = true;
-    for (int tile = blockIdx.x, lt = 0; tile < n_tiles; tile += gridDim.x, ++lt) {
-      const uint32_t par = (uint32_t)(lt & 1);
-      const int row = tile * kBM + r;
-      // E1: LN2 of h2 -> r2 operand
-      float x[32], mean, rstd;
-      load_quarter(a.h, row, n_rows, q, x);
-      ln_stats_quarter(x, q, scr, mean, rstd);
+    for (int i = 0; i < 32; ++i) dr[i] = (dr[i] - m1 - x[i] * m2) * rstd;
+    if (row < n_rows) {
+      float4* out = reinterpret_cast<float4*>(a.dh_out + (size_t)row * 128 + 32 * q);
 #pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        const float4 gg = __ldg(reinterpret_cast<const float4*>(f + F_LN2G + 32 * q + i));
-        const float4 be = __ldg(reinterpret_cast<const float4*>(f + F_LN2B + 32 * q + i));
-        x[i] = fmaxf(fmaf((x[i] - mean) * rstd, gg.x, be.x), 0.f);
-        x[i + 1] = fmaxf(fmaf((x[i + 1] - mean) * rstd, gg.y, be.y), 0.f);
-        x[i + 2] = fmaxf(fmaf((x[i + 2] - mean) * rstd, gg.z, be.z), 0.f);
-        x[i + 3] = fmaxf(fmaf((x[i + 3] - mean) * rstd, gg.w, be.w), 0.f);
-      }
-      store_split_quarter(x, r_hi, r_lo, r, q);
-      fence_proxy_async();
-      asm volatile("tcgen05.fence::before_thread_sync;");
-      mbar_arrive(abar);
-      // E2: head outputs and their gradients
-      ok = epi_and(mbar_wait(ubar, par) && *abort_flag == 0);
-      if (!ok) break;
-      asm volatile("tcgen05.fence::after_thread_sync;");
-      float z[8];
-#pragma unroll
-      for (int o = 0; o < 8; ++o) z[o] = 0.f;
-#pragma unroll
-      for (int k = 0; k < 3; ++k) {
-        const int u0 = 64 * k + 16 * q;        // this thread's 16 units of head k
-        float h[16];
-        tmem_ld16(lane_base + c_u + u0, h);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) h[i] = fmaxf(__fadd_rn(h[i], __ldg(f + F_HB0 + u0 + i)), 0.f);
-        const int o_lo = k == 0 ? 0 : (k == 1 ? 5 : 7), o_hi = k == 0 ? 5 : (k == 1 ? 7 : 8);
-#pragma unroll
-        for (int o = 0; o < 8; ++o) {
-          if (o < o_lo || o >= o_hi) continue;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) z[o] = fmaf(__ldg(f + F_HW2 + o * 64 + 16 * q + i), h[i], z[o]);
-        }
-      }
-      tmem_st8(scr + 16 + 8 * q, z);
-      asm volatile("tcgen05.fence::before_thread_sync;");
-      epi_sync();
-      asm volatile("tcgen05.fence::after_thread_sync;");
-      float dz[8];
-      {
-        float zz[32];
-        tmem_ld32(scr + 16, zz);
-#pragma unroll
-        for (int o = 0; o < 8; ++o)
-          z[o] = ((zz[o] + zz[8 + o]) + (zz[16 + o] + zz[24 + o])) + __ldg(f + F_HB2 + o);
-        const bool live = row < n_rows;
-        const size_t rw = live ? (size_t)row : 0;
-        const int64_t am = live ? a.act[rw * a.act_stride] : 0;
-        const int64_t ab = live ? a.act[rw * a.act_stride + 1] : 0;
-        head_grad(z, live, a.mm + rw * a.mm_stride, a.bm + rw * a.bm_stride,
-                  (am >= 0 && am < 5) ? (int)am : -1, (ab >= 0 && ab < 2) ? (int)ab : -1,
-                  live ? a.g[rw] : 0.f, live ? a.g[(size_t)n_rows + rw] : 0.f,
-                  live ? a.g[2 * (size_t)n_rows + rw] : 0.f, dz);
-      }
-      // heads 0 and 1: dL/du, the output-layer and hidden-bias sums, du operand
-      float dub[32];
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const int u0 = 64 * k + 16 * q;
-        float h[16], du[16];
-        tmem_ld16(lane_base + c_u + u0, h);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float g = __fadd_rn(h[i], __ldg(f + F_HB0 + u0 + i));
-          h[i] = fmaxf(g, 0.f);
-          float d = 0.f;
-          if (k == 0) {
-#pragma unroll
-            for (int o = 0; o < 5; ++o) d = fmaf(dz[o], __ldg(f + F_HW2 + o * 64 + 16 * q + i), d);
-          } else {
-#pragma unroll
-            for (int o = 5; o < 7; ++o) d = fmaf(dz[o], __ldg(f + F_HW2 + o * 64 + 16 * q + i), d);
-          }
-          du[i] = g > 0.f ? d : 0.f;
-          dub[16 * k + i] = du[i];
-        }
-        if (k == 0) {
-          float v[32];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) { v[i] = h[i] * dz[0]; v[16 + i] = h[i] * dz[1]; }
-          acc[0] += reduce_scatter32(v);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) { v[i] = h[i] * dz[2]; v[16 + i] = h[i] * dz[3]; }
-          acc[1] += reduce_scatter32(v);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) { v[i] = h[i] * dz[4]; v[16 + i] = 0.f; }
-          acc[2] += reduce_scatter32(v);
-        } else {
-          float v[32];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) { v[i] = h[i] * dz[5]; v[16 + i] = h[i] * dz[6]; }
-          acc[3] += reduce_scatter32(v);
-        }
-        store_split_scaled<16>(du, dscale, d_hi, d_lo, r, 64 * k + 16 * q);
-      }
-      acc[5] += reduce_scatter32(dub);
-      fence_proxy_async();
-      asm volatile("tcgen05.fence::before_thread_sync;");
-      mbar_arrive(d1bar);
-      // head 2 once the MMAs have released the du operand
-      ok = epi_and(mbar_wait(m2bar, par) && *abort_flag == 0);
-      if (!ok) break;
-      asm volatile("tcgen05.fence::after_thread_sync;");
-      {
-        const int u0 = 128 + 16 * q;
-        float h[16], du[16], v[32];
-        tmem_ld16(lane_base + c_u + u0, h);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float g = __fadd_rn(h[i], __ldg(f + F_HB0 + u0 + i));
-          h[i] = fmaxf(g, 0.f);
-          du[i] = g > 0.f ? dz[7] * __ldg(f + F_HW2 + 7 * 64 + 16 * q + i) : 0.f;
-        }
-#pragma unroll
-        for (int i = 0; i < 16; ++i) { v[i] = h[i] * dz[7]; v[16 + i] = 0.f; }
-        acc[4] += reduce_scatter32(v);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = du[i];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) { v[16 + i] = q == 0 ? dz[i] : 0.f; v[24 + i] = 0.f; }
-        acc[6] += reduce_scatter32(v);
-        store_split_scaled<16>(du, dscale, d_hi, d_lo, r, 16 * q);
-      }
-      fence_proxy_async();
-      asm volatile("tcgen05.fence::before_thread_sync;");
-      mbar_arrive(d2bar);
-      // E3: LN2 backward
-      ok = epi_and(mbar_wait(m3bar, par) && *abort_flag == 0);
-      if (!ok) break;
-      asm volatile("tcgen05.fence::after_thread_sync;");
-      float dr[32];
-      tmem_ld32(lane_base + c_u + 32 * q, dr);
-      load_quarter(a.h, row, n_rows, q, x);
-      float s1 = 0.f, s2 = 0.f;
-      {
-        float vg[32], vb[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float xh = (x[i] - mean) * rstd;
-          const float gm = __ldg(f + F_LN2G + 32 * q + i);
-          const float av = fmaf(xh, gm, __ldg(f + F_LN2B + 32 * q + i));
-          const float da = av > 0.f ? dr[i] * undo : 0.f;
-          vb[i] = da;
-          vg[i] = da * xh;
-          const float dxh = da * gm;
-          dr[i] = dxh;
-          x[i] = xh;
-          s1 += dxh;
-          s2 = fmaf(dxh, xh, s2);
-        }
-        acc[7] += reduce_scatter32(vg);
-        acc[8] += reduce_scatter32(vb);
-      }
-      tmem_st2(scr + 8 + 2 * q, s1, s2);
-      asm volatile("tcgen05.fence::before_thread_sync;");
-      epi_sync();
-      asm volatile("tcgen05.fence::after_thread_sync;");
-      float ss[8];
-      tmem_ld8(scr + 8, ss);
-      const float m1 = ((ss[0] + ss[2]) + (ss[4] + ss[6])) * (1.f / 128.f);
-      const float m2 = ((ss[1] + ss[3]) + (ss[5] + ss[7])) * (1.f / 128.f);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) dr[i] = (dr[i] - m1 - x[i] * m2) * rstd;
-      if (row < n_rows) {
-        float4* out = reinterpret_cast<float4*>(a.dh_out + (size_t)row * 128 + 32 * q);
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          out[i] = make_float4(dr[4 * i], dr[4 * i + 1], dr[4 * i + 2], dr[4 * i + 3]);
-      }
-      acc[9] += reduce_scatter32(dr);
+      for (int i = 0; i < 8; ++i)
+        out[i] = make_float4(dr[4 * i], dr[4 * i + 1], dr[4 * i + 2], dr[4 * i + 3]);
     }
-    if (!ok) *abort_flag = 1;
-    // per-thread sums, then the dWh0^T accumulator (lane = input, column = unit)
-    float* ap = a.apart + (((size_t)blockIdx.x * kEpiWarps + (warp - 2)) * 32 + lane) * kThAcc;
+    acc[8] += reduce_scatter32(dr);
+  }
+  if (!ok) *abort_flag = 1;
+  // per-thread sums, then the dWh0^T accumulator (lane = input, column = unit)
+  float* ap = a.apart + (((size_t)blockIdx.x * kEpiWarps + warp) * 32 + lane) * kThAcc;
 #pragma unroll
-    for (int i = 0; i < kThAcc; ++i) ap[i] = acc[i];
-    if (ok && blockIdx.x < n_tiles) {
+  for (int i = 0; i < kThAcc; ++i) ap[i] = acc[i];
+  if (ok && blockIdx.x < n_tiles) {
 #pragma unroll 1
-      for (int c = 0; c < 3; ++c) {
-        float v[16];
-        tmem_ld16(lane_base + 48 * q + 16 * c, v);
+    for (int c = 0; c < 3; ++c) {
+      float v[16];
+      tmem_ld16(lane_base + 48 * q + 16 * c, v);
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          a.wpart[((size_t)blockIdx.x * 192 + 48 * q + 16 * c + i) * 128 + r] = v[i] * undo;
-      }
+      for (int i = 0; i < 16; ++i)
+        a.wpart[((size_t)blockIdx.x * 192 + 48 * q + 16 * c + i) * 128 + r] = v[i] * undo;
     }
   }
-  tail_teardown(tmem);
+  uint64_t* lastb = (committed % 3 == 1) ? ubar : (committed % 3 == 2 ? m2bar : m3bar);
+  tail_teardown(tmem, lastb, (uint32_t)(((committed - 1) / 3) & 1), !ok && committed > 0);
 }
 
-__global__ void __launch_bounds__(kMlpThreads, 1)
+__global__ void __launch_bounds__(kTbThreads, 1)
 k_tail_trunk_bwd(TailArgs a, const float* __restrict__ f, const uint8_t* __restrict__ img,
                  int n_rows) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -1092,13 +1119,17 @@ k_tail_trunk_bwd(TailArgs a, const float* __restrict__ f, const uint8_t* __restr
   uint8_t* r_lo = r_hi + kActB;
   uint8_t* d_hi = smem + kTtD;
   uint8_t* d_lo = d_hi + kActB;
+  const bool issuer = threadIdx.x == 0;
 
-  if (threadIdx.x == 0) {
+  if (issuer) {
     mbar_init(wbar, 1);
-    mbar_init(abar, kEpiThreads);
+    mbar_init(abar, kTbThreads);
     mbar_init(m1bar, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_expect_tx(wbar, 2 * kImgW1Bytes);
+    for (uint32_t o = 0; o < 2 * kImgW1Bytes; o += 16384)
+      bulk_load(w_hi + o, img + kImgW1 + o, 16384, wbar);
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -1111,21 +1142,41 @@ k_tail_trunk_bwd(TailArgs a, const float* __restrict__ f, const uint8_t* __restr
   asm volatile("tcgen05.fence::after_thread_sync;");
   const uint32_t tmem = *tmem_slot;
   const uint32_t c_dr = 128;
+  const uint32_t id_dr = idesc_f16_kmn(kBM, 128), id_w = idesc_f16_mn(kBM, 128);
+  int committed = 0;
+  bool wload = issuer ? mbar_wait(wbar, 0) : true;
 
-  if (warp == 0) {
-    if (lane == 0) {
-      mbar_expect_tx(wbar, 2 * kImgW1Bytes);
-      for (uint32_t o = 0; o < 2 * kImgW1Bytes; o += 16384)
-        bulk_load(w_hi + o, img + kImgW1 + o, 16384, wbar);
-      mbar_wait(wbar, 0);
+  const int qd = warp & 3;
+  const int q = warp >> 2;
+  const int r = qd * 32 + lane;
+  const uint32_t lane_base = tmem + ((uint32_t)(qd * 32) << 16);
+  const uint32_t scr = lane_base + 256;        // columns 256..: free in this kernel
+  const int dexp = dh_scale_exp(a.amax);
+  const float dscale = pow2f(dexp), undo = pow2f(-dexp);
+  float acc[kTtAcc] = {0.f, 0.f, 0.f};
+  bool ok = epi_and(wload);
+  for (int tile = blockIdx.x, lt = 0; tile < n_tiles && ok; tile += gridDim.x, ++lt) {
+    const int row = tile * kBM + r;
+    float x[32], mean, rstd;
+    load_quarter(a.h, row, n_rows, q, x);
+    ln_stats_quarter(x, q, scr, mean, rstd);
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      const float4 gg = __ldg(reinterpret_cast<const float4*>(f + F_LN1G + 32 * q + i));
+      const float4 be = __ldg(reinterpret_cast<const float4*>(f + F_LN1B + 32 * q + i));
+      x[i] = fmaxf(fmaf((x[i] - mean) * rstd, gg.x, be.x), 0.f);
+      x[i + 1] = fmaxf(fmaf((x[i + 1] - mean) * rstd, gg.y, be.y), 0.f);
+      x[i + 2] = fmaxf(fmaf((x[i + 2] - mean) * rstd, gg.z, be.z), 0.f);
+      x[i + 3] = fmaxf(fmaf((x[i + 3] - mean) * rstd, gg.w, be.w), 0.f);
     }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t id_dr = idesc_f16_kmn(kBM, 128), id_w = idesc_f16_mn(kBM, 128);
-      int committed = 0;
-      bool ok = mbar_wait(wbar, 0);
-      for (int tile = blockIdx.x, lt = 0; tile < n_tiles && ok; tile += gridDim.x, ++lt) {
-        if (!mbar_wait(abar, (uint32_t)(lt & 1)) || *abort_flag) { ok = false; break; }
+    store_split_quarter(x, r_hi, r_lo, r, q);
+    load_quarter(a.dh_in, row, n_rows, q, x);
+    store_split_scaled<32>(x, dscale, d_hi, d_lo, r, 32 * q);
+    fence_proxy_async();
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    mbar_arrive(abar);
+    if (issuer) {
+      if (mbar_wait(abar, (uint32_t)(lt & 1)) && !*abort_flag) {
         asm volatile("tcgen05.fence::after_thread_sync;");
         // dr1 = dh2 W1: A K-major (K = outputs), B = W1's image read MN-major
 #pragma unroll
@@ -1150,99 +1201,49 @@ k_tail_trunk_bwd(TailArgs a, const float* __restrict__ f, const uint8_t* __restr
         }
         umma_commit(m1bar);
         ++committed;
-      }
-      if (!ok) {
+      } else {
         *abort_flag = 1;
-        if (committed > 0) mbar_wait(m1bar, (uint32_t)((committed - 1) & 1));
       }
     }
-  } else {
-    const int qd = warp & 3;
-    const int q = (warp - 2) >> 2;
-    const int r = qd * 32 + lane;
-    const uint32_t lane_base = tmem + ((uint32_t)(qd * 32) << 16);
-    const uint32_t scr = lane_base + kTbScr - 128;   // columns 256..: free in this kernel
-    const int dexp = dh_scale_exp(a.amax);
-    const float dscale = pow2f(dexp), undo = pow2f(-dexp);
-    float acc[kTtAcc] = {0.f, 0.f, 0.f};
-    bool ok = true;
-    for (int tile = blockIdx.x, lt = 0; tile < n_tiles; tile += gridDim.x, ++lt) {
-      const int row = tile * kBM + r;
-      float x[32], mean, rstd;
-      load_quarter(a.h, row, n_rows, q, x);
-      ln_stats_quarter(x, q, scr, mean, rstd);
+    ok = epi_and(mbar_wait(m1bar, (uint32_t)(lt & 1)) && *abort_flag == 0);
+    if (!ok) break;
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    float dr[32];
+    tmem_ld32(lane_base + c_dr + 32 * q, dr);
+    load_quarter(a.h, row, n_rows, q, x);
+    float s1 = 0.f, s2 = 0.f;
+    ln_relu_backward(x, dr, mean, rstd, undo, f + F_LN1G + 32 * q, f + F_LN1B + 32 * q, acc[0],
+                     acc[1], s1, s2);
+    tmem_st2(scr + 8 + 2 * q, s1, s2);
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    epi_sync();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    float ss[8];
+    tmem_ld8(scr + 8, ss);
+    const float m1 = ((ss[0] + ss[2]) + (ss[4] + ss[6])) * (1.f / 128.f);
+    const float m2 = ((ss[1] + ss[3]) + (ss[5] + ss[7])) * (1.f / 128.f);
 #pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        const float4 gg = __ldg(reinterpret_cast<const float4*>(f + F_LN1G + 32 * q + i));
-        const float4 be = __ldg(reinterpret_cast<const float4*>(f + F_LN1B + 32 * q + i));
-        x[i] = fmaxf(fmaf((x[i] - mean) * rstd, gg.x, be.x), 0.f);
-        x[i + 1] = fmaxf(fmaf((x[i + 1] - mean) * rstd, gg.y, be.y), 0.f);
-        x[i + 2] = fmaxf(fmaf((x[i + 2] - mean) * rstd, gg.z, be.z), 0.f);
-        x[i + 3] = fmaxf(fmaf((x[i + 3] - mean) * rstd, gg.w, be.w), 0.f);
-      }
-      store_split_quarter(x, r_hi, r_lo, r, q);
-      load_quarter(a.dh_in, row, n_rows, q, x);
-      store_split_scaled<32>(x, dscale, d_hi, d_lo, r, 32 * q);
-      fence_proxy_async();
-      asm volatile("tcgen05.fence::before_thread_sync;");
-      mbar_arrive(abar);
-      ok = epi_and(mbar_wait(m1bar, (uint32_t)(lt & 1)) && *abort_flag == 0);
-      if (!ok) break;
-      asm volatile("tcgen05.fence::after_thread_sync;");
-      float dr[32];
-      tmem_ld32(lane_base + c_dr + 32 * q, dr);
-      load_quarter(a.h, row, n_rows, q, x);
-      float s1 = 0.f, s2 = 0.f;
-      {
-        float vg[32], vb[32];
+    for (int i = 0; i < 32; ++i) dr[i] = (dr[i] - m1 - x[i] * m2) * rstd;
+    if (row < n_rows) {
+      float4* out = reinterpret_cast<float4*>(a.dh_out + (size_t)row * 128 + 32 * q);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float xh = (x[i] - mean) * rstd;
-          const float gm = __ldg(f + F_LN1G + 32 * q + i);
-          const float av = fmaf(xh, gm, __ldg(f + F_LN1B + 32 * q + i));
-          const float da = av > 0.f ? dr[i] * undo : 0.f;
-          vb[i] = da;
-          vg[i] = da * xh;
-          const float dxh = da * gm;
-          dr[i] = dxh;
-          x[i] = xh;
-          s1 += dxh;
-          s2 = fmaf(dxh, xh, s2);
-        }
-        acc[0] += reduce_scatter32(vg);
-        acc[1] += reduce_scatter32(vb);
-      }
-      tmem_st2(scr + 8 + 2 * q, s1, s2);
-      asm volatile("tcgen05.fence::before_thread_sync;");
-      epi_sync();
-      asm volatile("tcgen05.fence::after_thread_sync;");
-      float ss[8];
-      tmem_ld8(scr + 8, ss);
-      const float m1 = ((ss[0] + ss[2]) + (ss[4] + ss[6])) * (1.f / 128.f);
-      const float m2 = ((ss[1] + ss[3]) + (ss[5] + ss[7])) * (1.f / 128.f);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) dr[i] = (dr[i] - m1 - x[i] * m2) * rstd;
-      if (row < n_rows) {
-        float4* out = reinterpret_cast<float4*>(a.dh_out + (size_t)row * 128 + 32 * q);
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          out[i] = make_float4(dr[4 * i], dr[4 * i + 1], dr[4 * i + 2], dr[4 * i + 3]);
-      }
-      acc[2] += reduce_scatter32(dr);
+      for (int i = 0; i < 8; ++i)
+        out[i] = make_float4(dr[4 * i], dr[4 * i + 1], dr[4 * i + 2], dr[4 * i + 3]);
     }
-    if (!ok) *abort_flag = 1;
-    float* ap = a.apart + (((size_t)blockIdx.x * kEpiWarps + (warp - 2)) * 32 + lane) * kTtAcc;
-#pragma unroll
-    for (int i = 0; i < kTtAcc; ++i) ap[i] = acc[i];
-    if (ok && blockIdx.x < n_tiles) {
-      float v[32];
-      tmem_ld32(lane_base + 32 * q, v);
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        a.wpart[((size_t)blockIdx.x * 128 + 32 * q + i) * 128 + r] = v[i] * undo;
-    }
+    acc[2] += reduce_scatter32(dr);
   }
-  tail_teardown(tmem);
+  if (!ok) *abort_flag = 1;
+  float* ap = a.apart + (((size_t)blockIdx.x * kEpiWarps + warp) * 32 + lane) * kTtAcc;
+#pragma unroll
+  for (int i = 0; i < kTtAcc; ++i) ap[i] = acc[i];
+  if (ok && blockIdx.x < n_tiles) {
+    float v[32];
+    tmem_ld32(lane_base + 32 * q, v);
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      a.wpart[((size_t)blockIdx.x * 128 + 32 * q + i) * 128 + r] = v[i] * undo;
+  }
+  tail_teardown(tmem, m1bar, (uint32_t)((committed - 1) & 1), !ok && committed > 0);
 }
 
 // Parameter gradients from the per-CTA partial sums, in CTA order (one
@@ -1260,7 +1261,7 @@ __device__ __forceinline__ float sum_acc(const float* ap, int grid, int nacc, in
   float s = 0.f;
   for (int c = 0; c < grid; ++c)
     for (int m = 0; m < 4; ++m)
-      s += ap[(((size_t)c * kEpiWarps + 4 * q + m) * 32 + lane) * nacc + slot];
+      s += ap[(((size_t)c * kEpiWarps + 4 * q + m) * 32 + lane) * nacc + slot];   // warps 4q..4q+3
   return s;
 }
 
@@ -1281,32 +1282,32 @@ __global__ void k_tail_reduce(const float* __restrict__ wph, const float* __rest
   }
   if (i < 128) {
     const int q = i >> 5, l = i & 31;
-    gr.p[6][i] = sum_acc(aph, grid, kThAcc, q, l, 7);     // shared.4.weight (LN2 gamma)
-    gr.p[7][i] = sum_acc(aph, grid, kThAcc, q, l, 8);     // shared.4.bias
-    gr.p[5][i] = sum_acc(aph, grid, kThAcc, q, l, 9);     // shared.3.bias
+    gr.p[6][i] = sum_acc(aph, grid, kThAcc, q, l, 6);     // shared.4.weight (LN2 gamma)
+    gr.p[7][i] = sum_acc(aph, grid, kThAcc, q, l, 7);     // shared.4.bias
+    gr.p[5][i] = sum_acc(aph, grid, kThAcc, q, l, 8);     // shared.3.bias
     gr.p[2][i] = sum_acc(apt, grid, kTtAcc, q, l, 0);     // shared.1.weight (LN1 gamma)
     gr.p[3][i] = sum_acc(apt, grid, kTtAcc, q, l, 1);     // shared.1.bias
     gr.p[1][i] = sum_acc(apt, grid, kTtAcc, q, l, 2);     // shared.0.bias
-  }
-  if (i < 4 * 32) {
-    // head output layers and hidden biases: quarter q, lane l
-    const int q = i >> 5, l = i & 31;
+    // head output layers and hidden biases, 32-vectors of quarter q
     const int ul = 16 * q + (l & 15);                     // unit within its head
-    const int hi = l >> 4;
-    gr.p[10][(2 * 0 + hi) * 64 + ul] = sum_acc(aph, grid, kThAcc, q, l, 0);   // move.2 o 0/1
-    gr.p[10][(2 + hi) * 64 + ul] = sum_acc(aph, grid, kThAcc, q, l, 1);       // o 2/3
-    if (!hi) gr.p[10][4 * 64 + ul] = sum_acc(aph, grid, kThAcc, q, l, 2);     // o 4
-    gr.p[14][hi * 64 + ul] = sum_acc(aph, grid, kThAcc, q, l, 3);             // bomb.2 o 0/1
-    if (!hi) gr.p[18][ul] = sum_acc(aph, grid, kThAcc, q, l, 4);              // critic.2
-    gr.p[hi ? 13 : 9][ul] = sum_acc(aph, grid, kThAcc, q, l, 5);              // move/bomb .0.bias
-    if (!hi) gr.p[17][ul] = sum_acc(aph, grid, kThAcc, q, l, 6);              // critic.0.bias
-    if (q == 0 && l >= 16 && l < 24) {
-      const int o = l - 16;
-      const float s = sum_acc(aph, grid, kThAcc, 0, l, 6);
-      if (o < 5) gr.p[11][o] = s;                         // move.2.bias
-      else if (o < 7) gr.p[15][o - 5] = s;                // bomb.2.bias
-      else gr.p[19][0] = s;                               // critic.2.bias
+    const bool hi = l >= 16;
+    gr.p[10][(hi ? 1 : 0) * 64 + ul] = sum_acc(aph, grid, kThAcc, q, l, 0);   // move.2 o 0 / 1
+    gr.p[10][(hi ? 3 : 2) * 64 + ul] = sum_acc(aph, grid, kThAcc, q, l, 1);   // o 2 / 3
+    const float a2 = sum_acc(aph, grid, kThAcc, q, l, 2);
+    if (hi) gr.p[9][ul] = a2;                             // move.0.bias
+    else gr.p[10][4 * 64 + ul] = a2;                      // move.2 o 4
+    gr.p[14][(hi ? 1 : 0) * 64 + ul] = sum_acc(aph, grid, kThAcc, q, l, 3);   // bomb.2 o 0 / 1
+    const float a4 = sum_acc(aph, grid, kThAcc, q, l, 4);
+    if (!hi) gr.p[13][ul] = a4;                           // bomb.0.bias
+    else if (q == 0 && l < 24) {
+      const int o = l - 16;                               // head output biases
+      if (o < 5) gr.p[11][o] = a4;
+      else if (o < 7) gr.p[15][o - 5] = a4;
+      else gr.p[19][0] = a4;
     }
+    const float a5 = sum_acc(aph, grid, kThAcc, q, l, 5);
+    if (hi) gr.p[17][ul] = a5;                            // critic.0.bias
+    else gr.p[18][ul] = a5;                               // critic.2.weight
   }
 }
 
@@ -1520,7 +1521,7 @@ extern "C" int qqt_mlp_train_backward(const void* pack, int32_t n_rows, int32_t 
   a.bm_stride = bm_stride;
   a.act_stride = act_stride;
   cudaFuncSetAttribute(k_tail_heads_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, kThSmem);
-  k_tail_heads_bwd<<<grid, kMlpThreads, kThSmem, st>>>(a, fpar, img, n_rows);
+  k_tail_heads_bwd<<<grid, kTbThreads, kThSmem, st>>>(a, fpar, img, n_rows);
   const int64_t nd = (int64_t)n_rows * 128;
   k_absmax_n<<<(unsigned)max((int64_t)1, min((nd + 255) / 256, (int64_t)sms * 8)), 256, 0, st>>>(
       (const float*)(wk + W.dh2), nd, (uint32_t*)(wk + W.amax_d));
@@ -1533,7 +1534,7 @@ extern "C" int qqt_mlp_train_backward(const void* pack, int32_t n_rows, int32_t 
   b.wpart = (float*)(wk + W.wpt);
   b.apart = (float*)(wk + W.apt);
   cudaFuncSetAttribute(k_tail_trunk_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, kTtSmem);
-  k_tail_trunk_bwd<<<grid, kMlpThreads, kTtSmem, st>>>(b, fpar, img, n_rows);
+  k_tail_trunk_bwd<<<grid, kTbThreads, kTtSmem, st>>>(b, fpar, img, n_rows);
   TailGrads gr;
   for (int i = 0; i < 20; ++i) gr.p[i] = grads[i];
   k_tail_reduce<<<(192 * 128 + 255) / 256, 256, 0, st>>>(
