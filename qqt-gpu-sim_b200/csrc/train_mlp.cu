@@ -695,6 +695,24 @@ __device__ __forceinline__ void head_grad(const float* z, bool live, const uint8
   dz[7] = gv;
 }
 
+// A read-only load the compiler keeps in place: the per-layer parameters
+// are read again where they are used instead of being held in registers
+// across the whole tile loop.
+__device__ __forceinline__ float ldg_keep(const float* p) {
+  float v;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+
+// 16 consecutive floats (16-byte aligned) as four 16-byte loads.
+__device__ __forceinline__ void ldg16_keep(const float* p, float* v) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v[4 * j]), "=f"(v[4 * j + 1]), "=f"(v[4 * j + 2]), "=f"(v[4 * j + 3])
+                 : "l"(p + 4 * j));
+}
+
 // LayerNorm + affine + ReLU backward for the thread's 32 columns: x holds
 // the pre-LN values (-> x-hat), dr the gradient of the ReLU output times
 // 2^s (-> dL/dx-hat); the gamma and beta sums of the warp's rows go into
@@ -704,14 +722,19 @@ __device__ __forceinline__ void ln_relu_backward(float* x, float* dr, float mean
                                                  float undo, const float* __restrict__ g,
                                                  const float* __restrict__ b, float& acc_g,
                                                  float& acc_b, float& s1, float& s2) {
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const float xh = (x[i] - mean) * rstd;
-    const float av = fmaf(xh, __ldg(g + i), __ldg(b + i));
-    x[i] = xh;
-    dr[i] = av > 0.f ? dr[i] * undo : 0.f;
-  }
   float v[32];
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    ldg16_keep(g + 16 * c, v);
+    ldg16_keep(b + 16 * c, v + 16);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float xh = (x[16 * c + i] - mean) * rstd;
+      const float av = fmaf(xh, v[i], v[16 + i]);
+      x[16 * c + i] = xh;
+      dr[16 * c + i] = av > 0.f ? dr[16 * c + i] * undo : 0.f;
+    }
+  }
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = dr[i];
   acc_b += reduce_scatter32(v);
@@ -719,11 +742,15 @@ __device__ __forceinline__ void ln_relu_backward(float* x, float* dr, float mean
   for (int i = 0; i < 32; ++i) v[i] = dr[i] * x[i];
   acc_g += reduce_scatter32(v);
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const float dxh = dr[i] * __ldg(g + i);
-    dr[i] = dxh;
-    s1 += dxh;
-    s2 = fmaf(dxh, x[i], s2);
+  for (int c = 0; c < 2; ++c) {
+    ldg16_keep(g + 16 * c, v);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float dxh = dr[16 * c + i] * v[i];
+      dr[16 * c + i] = dxh;
+      s1 += dxh;
+      s2 = fmaf(dxh, x[16 * c + i], s2);
+    }
   }
 }
 
@@ -740,15 +767,6 @@ struct TailArgs {
   float* apart;            // [grid][16 warps][32 lanes][acc] per-thread small sums
   int mm_stride, bm_stride, act_stride;
 };
-
-// A read-only load the compiler keeps in place: the per-layer parameters
-// are read again where they are used instead of being held in registers
-// across the whole tile loop.
-__device__ __forceinline__ float ldg_keep(const float* p) {
-  float v;
-  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
-  return v;
-}
 
 // Both backward kernels run 16 warps, all of them epilogue warps (row r =
 // 32 * (warp % 4) + lane, column quarter warp / 4); thread 0 also brings in
@@ -888,16 +906,18 @@ k_tail_heads_bwd(TailArgs a, const float* __restrict__ f, const uint8_t* __restr
 #pragma unroll
     for (int k = 0; k < 3; ++k) {
       const int u0 = 64 * k + 16 * q;          // this thread's 16 units of head k
-      float h[16];
+      float h[16], w[16];
       tmem_ld16(lane_base + c_u + u0, h);
+      ldg16_keep(f + F_HB0 + u0, w);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) h[i] = fmaxf(__fadd_rn(h[i], ldg_keep(f + F_HB0 + u0 + i)), 0.f);
+      for (int i = 0; i < 16; ++i) h[i] = fmaxf(__fadd_rn(h[i], w[i]), 0.f);
       const int o_lo = k == 0 ? 0 : (k == 1 ? 5 : 7), o_hi = k == 0 ? 5 : (k == 1 ? 7 : 8);
 #pragma unroll
       for (int o = 0; o < 8; ++o) {
         if (o < o_lo || o >= o_hi) continue;
+        ldg16_keep(f + F_HW2 + o * 64 + 16 * q, w);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) z[o] = fmaf(ldg_keep(f + F_HW2 + o * 64 + 16 * q + i), h[i], z[o]);
+        for (int i = 0; i < 16; ++i) z[o] = fmaf(w[i], h[i], z[o]);
       }
     }
     tmem_st8(scr + 16 + 8 * q, z);
@@ -929,19 +949,22 @@ k_tail_heads_bwd(TailArgs a, const float* __restrict__ f, const uint8_t* __restr
       const int u0 = 64 * k + 16 * q;
       float h[16], du[16], v[32];
       tmem_ld16(lane_base + c_u + u0, h);
+      ldg16_keep(f + F_HB0 + u0, v);
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const float g = __fadd_rn(h[i], ldg_keep(f + F_HB0 + u0 + i));
-        h[i] = fmaxf(g, 0.f);
-        float d = 0.f;
-        if (k == 0) {
+        h[i] = __fadd_rn(h[i], v[i]);          // pre-ReLU g
+        du[i] = 0.f;
+      }
 #pragma unroll
-          for (int o = 0; o < 5; ++o) d = fmaf(dz[o], ldg_keep(f + F_HW2 + o * 64 + 16 * q + i), d);
-        } else {
+      for (int o = (k == 0 ? 0 : 5); o < (k == 0 ? 5 : 7); ++o) {
+        ldg16_keep(f + F_HW2 + o * 64 + 16 * q, v);
 #pragma unroll
-          for (int o = 5; o < 7; ++o) d = fmaf(dz[o], ldg_keep(f + F_HW2 + o * 64 + 16 * q + i), d);
-        }
-        du[i] = g > 0.f ? d : 0.f;
+        for (int i = 0; i < 16; ++i) du[i] = fmaf(dz[o], v[i], du[i]);
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        du[i] = h[i] > 0.f ? du[i] : 0.f;
+        h[i] = fmaxf(h[i], 0.f);
       }
       if (k == 0) {
 #pragma unroll
@@ -1010,11 +1033,13 @@ k_tail_heads_bwd(TailArgs a, const float* __restrict__ f, const uint8_t* __restr
       const int u0 = 128 + 16 * q;
       float h[16], du[16], v[32];
       tmem_ld16(lane_base + c_u + u0, h);
+      ldg16_keep(f + F_HB0 + u0, v);
+      ldg16_keep(f + F_HW2 + 7 * 64 + 16 * q, v + 16);
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const float g = __fadd_rn(h[i], ldg_keep(f + F_HB0 + u0 + i));
+        const float g = __fadd_rn(h[i], v[i]);
         h[i] = fmaxf(g, 0.f);
-        du[i] = g > 0.f ? dz[7] * ldg_keep(f + F_HW2 + 7 * 64 + 16 * q + i) : 0.f;
+        du[i] = g > 0.f ? dz[7] * v[16 + i] : 0.f;
       }
 #pragma unroll
       for (int i = 0; i < 16; ++i) { v[i] = h[i] * dz[7]; v[16 + i] = du[i]; }
@@ -1246,27 +1271,67 @@ k_tail_trunk_bwd(TailArgs a, const float* __restrict__ f, const uint8_t* __restr
   tail_teardown(tmem, m1bar, (uint32_t)((committed - 1) & 1), !ok && committed > 0);
 }
 
-// Parameter gradients from the per-CTA partial sums, in CTA order (one
-// thread per output element; deterministic).
+// Parameter gradients from the per-CTA partial sums, in CTA order
+// (deterministic).
 //   dWh0: wpart_h [grid][192][128] -> the three head hidden weights
 //   dW1:  wpart_t [grid][128][128]
-//   small sums: thread (warp 2 + 4q + m, lane l) of each CTA holds element l
-//   of the 32-vectors built for quarter q.
+//   small sums: thread (warp 4q + m, lane l) of each CTA holds element l of
+//   the 32-vectors built for quarter q.
 struct TailGrads {
   float* p[20];            // reference state_dict order (qqt_mlp_param_names)
 };
 
-__device__ __forceinline__ float sum_acc(const float* ap, int grid, int nacc, int q, int lane,
-                                         int slot) {
-  float s = 0.f;
-  for (int c = 0; c < grid; ++c)
-    for (int m = 0; m < 4; ++m)
-      s += ap[(((size_t)c * kEpiWarps + 4 * q + m) * 32 + lane) * nacc + slot];   // warps 4q..4q+3
-  return s;
+// Destination of the small sum kept by lane l of quarter q's warps in
+// accumulator `slot` (kind 0: heads kernel, 1: trunk kernel); nullptr for
+// padding.  Heads kernel 32-vectors: slot 0 [q0 dz0 | q0 dz1], 1 [q0 dz2 |
+// q0 dz3], 2 [q0 dz4 | du0], 3 [q1 dz5 | q1 dz6], 4 [du1 | dz0..7 (quarter
+// 0) | 0], 5 [q2 dz7 | du2], 6 LN2 gamma, 7 LN2 beta, 8 shared.3 bias;
+// trunk kernel: 0 LN1 gamma, 1 LN1 beta, 2 shared.0 bias.
+__device__ __forceinline__ float* tail_small_dest(const TailGrads& gr, int kind, int q, int l,
+                                                  int slot) {
+  const int ul = 16 * q + (l & 15);                       // unit within its head
+  const bool hi = l >= 16;
+  if (kind == 1) return gr.p[slot == 0 ? 2 : (slot == 1 ? 3 : 1)] + 32 * q + l;
+  switch (slot) {
+    case 0: return gr.p[10] + (hi ? 1 : 0) * 64 + ul;     // move_head.2.weight
+    case 1: return gr.p[10] + (hi ? 3 : 2) * 64 + ul;
+    case 2: return hi ? gr.p[9] + ul : gr.p[10] + 4 * 64 + ul;   // move_head.0.bias / .2.weight
+    case 3: return gr.p[14] + (hi ? 1 : 0) * 64 + ul;     // bomb_head.2.weight
+    case 4:
+      if (!hi) return gr.p[13] + ul;                      // bomb_head.0.bias
+      if (q != 0 || l >= 24) return nullptr;
+      return l - 16 < 5 ? gr.p[11] + (l - 16) : (l - 16 < 7 ? gr.p[15] + (l - 21) : gr.p[19]);
+    case 5: return hi ? gr.p[17] + ul : gr.p[18] + ul;    // critic.0.bias / critic.2.weight
+    case 6: return gr.p[6] + 32 * q + l;                  // shared.4.weight (LN2 gamma)
+    case 7: return gr.p[7] + 32 * q + l;                  // shared.4.bias
+    default: return gr.p[5] + 32 * q + l;                 // shared.3.bias
+  }
 }
 
-__global__ void k_tail_reduce(const float* __restrict__ wph, const float* __restrict__ aph,
-                              const float* __restrict__ wpt, const float* __restrict__ apt,
+// One warp per small gradient element: lane j sums CTA-warp partials j,
+// j + 32, ... (each CTA's four row-quadrant warps of quarter q) in order,
+// then a fixed shuffle tree.
+__global__ void k_tail_reduce_small(const float* __restrict__ aph, const float* __restrict__ apt,
+                                    int grid, TailGrads gr) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = lane_id();
+  constexpr int kHeads = 128 * kThAcc, kAll = kHeads + 128 * kTtAcc;
+  if (w >= kAll) return;
+  const int kind = w < kHeads ? 0 : 1;
+  const int idx = kind ? w - kHeads : w;
+  const int nacc = kind ? kTtAcc : kThAcc;
+  const int slot = idx % nacc, ql = idx / nacc, q = ql >> 5, l = ql & 31;
+  float* dst = tail_small_dest(gr, kind, q, l, slot);
+  if (!dst) return;
+  const float* ap = kind ? apt : aph;
+  float s = 0.f;
+  for (int j = lane; j < grid * 4; j += 32)
+    s += ap[((((size_t)(j >> 2)) * kEpiWarps + 4 * q + (j & 3)) * 32 + l) * nacc + slot];
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) *dst = s;
+}
+
+__global__ void k_tail_reduce(const float* __restrict__ wph, const float* __restrict__ wpt,
                               int grid, TailGrads gr) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < 192 * 128) {
@@ -1279,35 +1344,6 @@ __global__ void k_tail_reduce(const float* __restrict__ wph, const float* __rest
     float s = 0.f;
     for (int c = 0; c < grid; ++c) s += wpt[(size_t)c * 128 * 128 + i];
     gr.p[4][i] = s;                                       // shared.3.weight [out][in]
-  }
-  if (i < 128) {
-    const int q = i >> 5, l = i & 31;
-    gr.p[6][i] = sum_acc(aph, grid, kThAcc, q, l, 6);     // shared.4.weight (LN2 gamma)
-    gr.p[7][i] = sum_acc(aph, grid, kThAcc, q, l, 7);     // shared.4.bias
-    gr.p[5][i] = sum_acc(aph, grid, kThAcc, q, l, 8);     // shared.3.bias
-    gr.p[2][i] = sum_acc(apt, grid, kTtAcc, q, l, 0);     // shared.1.weight (LN1 gamma)
-    gr.p[3][i] = sum_acc(apt, grid, kTtAcc, q, l, 1);     // shared.1.bias
-    gr.p[1][i] = sum_acc(apt, grid, kTtAcc, q, l, 2);     // shared.0.bias
-    // head output layers and hidden biases, 32-vectors of quarter q
-    const int ul = 16 * q + (l & 15);                     // unit within its head
-    const bool hi = l >= 16;
-    gr.p[10][(hi ? 1 : 0) * 64 + ul] = sum_acc(aph, grid, kThAcc, q, l, 0);   // move.2 o 0 / 1
-    gr.p[10][(hi ? 3 : 2) * 64 + ul] = sum_acc(aph, grid, kThAcc, q, l, 1);   // o 2 / 3
-    const float a2 = sum_acc(aph, grid, kThAcc, q, l, 2);
-    if (hi) gr.p[9][ul] = a2;                             // move.0.bias
-    else gr.p[10][4 * 64 + ul] = a2;                      // move.2 o 4
-    gr.p[14][(hi ? 1 : 0) * 64 + ul] = sum_acc(aph, grid, kThAcc, q, l, 3);   // bomb.2 o 0 / 1
-    const float a4 = sum_acc(aph, grid, kThAcc, q, l, 4);
-    if (!hi) gr.p[13][ul] = a4;                           // bomb.0.bias
-    else if (q == 0 && l < 24) {
-      const int o = l - 16;                               // head output biases
-      if (o < 5) gr.p[11][o] = a4;
-      else if (o < 7) gr.p[15][o - 5] = a4;
-      else gr.p[19][0] = a4;
-    }
-    const float a5 = sum_acc(aph, grid, kThAcc, q, l, 5);
-    if (hi) gr.p[17][ul] = a5;                            // critic.0.bias
-    else gr.p[18][ul] = a5;                               // critic.2.weight
   }
 }
 
@@ -1538,7 +1574,8 @@ extern "C" int qqt_mlp_train_backward(const void* pack, int32_t n_rows, int32_t 
   TailGrads gr;
   for (int i = 0; i < 20; ++i) gr.p[i] = grads[i];
   k_tail_reduce<<<(192 * 128 + 255) / 256, 256, 0, st>>>(
-      (const float*)(wk + W.wph), (const float*)(wk + W.aph), (const float*)(wk + W.wpt),
-      (const float*)(wk + W.apt), grid, gr);
+      (const float*)(wk + W.wph), (const float*)(wk + W.wpt), grid, gr);
+  k_tail_reduce_small<<<(128 * (kThAcc + kTtAcc) * 32 + 255) / 256, 256, 0, st>>>(
+      (const float*)(wk + W.aph), (const float*)(wk + W.apt), grid, gr);
   return launch_status();
 }
