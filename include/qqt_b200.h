@@ -345,6 +345,15 @@ int qqt_gae(const float *rew, int32_t rew_stride, const uint8_t *done, const flo
             int32_t val_stride, const float *last_val, int32_t T, int32_t N, double gamma,
             double lam, float *adv, float *ret, qqt_stream_t stream);
 
+/* Per-player features of the LSTM policy (sim/obs.py:241-340) from the
+ * shared observation rows obs [N][obs_stride] (fp16, or fp32 with
+ * obs_fp32): local [N][Po][C][7][7], rel [N][Po][10][6], glob [N][Po][5] in
+ * the observation's dtype, Po = 1 with only_p0 else P.  max_bombs =
+ * SimConfig.max_bombs.  Equal-distance bomb slots in ascending flat cell
+ * order (the reference leaves that order to torch.topk). */
+int qqt_local_view(const QqtCfg *cfg, const QqtState *st, const void *obs, int32_t max_bombs,
+                   int32_t only_p0, void *local, void *rel, void *glob, qqt_stream_t stream);
+
 /* ---- PPO update of the MLP policy: its first layer (train/ppo.py:364-437
  * via ActorCritic(mlp).evaluate, train/model.py:121-153 and 247-256).  The
  * reference runs `obs[sel]` (index gather), `.float()`, F.linear(x, W0[:,

@@ -581,6 +581,85 @@ def observe(cfg, st):
     return encode_obs(cfg, st, dng), dng
 
 
+# -------------------------------------------------- LSTM local-view features
+
+LV_K = 7          # local window side (sim/obs.py:252)
+LV_MAX_T = 10     # relative-target slots (sim/obs.py:238)
+LV_GLOB = 5       # global scalars (sim/obs.py:239)
+
+
+def local_view_features(cfg, obs, pos, alive, t, fuse, hp, only_p0=False):
+    """Per-player features of the LSTM policy from the shared observation
+    (sim/obs.py:241-340).  obs (N, C, H, W) in its storage dtype; pos (N,P,2)
+    f32, alive (N,P), t (N,), fuse (N,H,W), hp (N,P).  Returns local
+    (N,Po,C,7,7), rel (N,Po,10,6) and glob (N,Po,5) in obs's dtype, Po = 1
+    with only_p0 else P.
+
+      local  the 7x7 window of every channel centred on the player's cell,
+             zero outside the grid (sim/obs.py:257-282)
+      rel    slots 0..P-2: opponent (me + i + 1) % P as [row delta, column
+             delta, alive, 0, 0, 0]; slots P-1..9: cells ordered by L1
+             distance from the player's cell, live bombs first (distance of a
+             non-bomb cell counts as 1e6), as [column delta, row delta, 0,
+             is-bomb, 0, 0] (sim/obs.py:284-322)
+      glob   [t / max_steps, hp / max_hp, danger under the player, bombs /
+             max_bombs, sum(fuse) / (max_bombs * fuse)] (sim/obs.py:324-338)
+
+    Cells at equal distance are taken in ascending flat index; the reference
+    leaves that order to torch.topk (sim/obs.py:306-309), which does not
+    specify it (its CPU and CUDA implementations differ).
+    """
+    n, P, _ = pos.shape
+    c, h, w = obs.shape[1], cfg.height, cfg.width
+    half = LV_K // 2
+    po = 1 if only_p0 else P
+    dt = obs.dtype
+    cell = np.floor(pos).astype(np.int64)
+    pad = np.pad(obs, ((0, 0), (0, 0), (half, half), (half, half)))
+    rows = np.arange(n)
+    local = np.empty((n, po, c, LV_K, LV_K), dt)
+    for m in range(po):
+        for dy in range(LV_K):
+            ys = np.clip(cell[:, m, 0] + dy, 0, h + 2 * half - 1)
+            for dx in range(LV_K):
+                xs = np.clip(cell[:, m, 1] + dx, 0, w + 2 * half - 1)
+                local[:, m, :, dy, dx] = pad[rows, :, ys, xs]
+    rel = np.zeros((n, po, LV_MAX_T, 6), dt)
+    n_opp = P - 1
+    for m in range(po):
+        for i in range(n_opp):
+            opp = (m + i + 1) % P
+            rel[:, m, i, 0] = (pos[:, opp, 0] - pos[:, m, 0]).astype(F32)
+            rel[:, m, i, 1] = (pos[:, opp, 1] - pos[:, m, 1]).astype(F32)
+            rel[:, m, i, 2] = alive[:, opp]
+    k = min(LV_MAX_T - n_opp, h * w)
+    if k > 0:
+        gy = np.arange(h).reshape(1, h, 1)
+        gx = np.arange(w).reshape(1, 1, w)
+        for m in range(po):
+            cy, cx = cell[:, m, 0], cell[:, m, 1]
+            dist = np.abs(gy - cy.reshape(n, 1, 1)) + np.abs(gx - cx.reshape(n, 1, 1))
+            dist = np.where(fuse > 0, dist, 1000000).reshape(n, -1)
+            order = np.argsort(dist, axis=1, kind="stable")[:, :k]
+            vals = np.take_along_axis(dist, order, 1)
+            for j in range(k):
+                gi = order[:, j]
+                rel[:, m, n_opp + j, 0] = (gi % w).astype(F32) - cx.astype(F32)
+                rel[:, m, n_opp + j, 1] = (gi // w).astype(F32) - cy.astype(F32)
+                rel[:, m, n_opp + j, 3] = vals[:, j] < 100000
+    glob = np.zeros((n, po, LV_GLOB), dt)
+    # dtype(t) / max_steps: the division runs in float32 and rounds to dtype
+    glob[..., 0] = (t.astype(dt).astype(F32) / F32(cfg.max_steps)).astype(dt)[:, None]
+    glob[..., 1] = (hp[:, :po].astype(dt).astype(F32) / F32(cfg.max_hp)).astype(dt)
+    danger = obs[:, 2 * cfg.n_players + 1].reshape(n, -1)
+    glob[..., 2] = np.take_along_axis(danger, (cell[:, :po, 0] * w + cell[:, :po, 1]), 1)
+    nb = (fuse > 0).reshape(n, -1).sum(1).astype(F32)
+    glob[..., 3] = (nb / F32(cfg.max_bombs))[:, None]
+    fs = fuse.reshape(n, -1).astype(F32).sum(1, dtype=F32)
+    glob[..., 4] = (fs / F32(cfg.max_bombs * cfg.fuse))[:, None]
+    return local, rel, glob
+
+
 # ------------------------------------------------------------------- bots
 
 def sample_legal(mask, u):

@@ -855,6 +855,126 @@ __global__ void k_greedy(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, 
 
 using namespace qqt;
 
+// ------------------------------------------------ LSTM local-view features
+
+__device__ __forceinline__ float from_obs(float v) { return v; }
+__device__ __forceinline__ float from_obs(__half v) { return __half2float(v); }
+
+// Per-player features of the LSTM policy from the shared observation rows
+// (sim/obs.py:241-340); one warp per (env, output player m):
+//   local [m] the 7x7 window of every channel centred on the player's cell,
+//             the reference's zero padding of 3 and coordinate clamp
+//   rel   [m] opponents (m + i + 1) % P: [row delta, column delta, alive];
+//             then the k = min(10 - (P-1), H*W) cells nearest to the player
+//             (L1, a non-bomb cell counting 1e6) by k warp-argmin rounds
+//             over 64-bit keys (distance, flat cell), written as [column
+//             delta, row delta, 0, is-bomb]
+//   glob  [m] dtype(t) / max_steps, dtype(hp) / max_hp, danger under the
+//             player, live bombs / max_bombs, sum(fuse) / (max_bombs * fuse)
+// The reference orders equal distances by torch.topk, which leaves that
+// order open; here it is ascending flat cell index.
+template <typename T>
+__global__ void k_local_view(QqtCfg cfg, QqtState st, const T* __restrict__ obs, int max_bombs,
+                             int po, T* __restrict__ local, T* __restrict__ rel,
+                             T* __restrict__ glob) {
+  const int gw = (int)((blockIdx.x * (unsigned)blockDim.x + threadIdx.x) >> 5);
+  const int lane = lane_id();
+  const int N = cfg.n_envs, P = cfg.n_players, H = cfg.height, W = cfg.width, C = H * W;
+  const int CH = cfg.obs_channels;
+  if (gw >= N * po) return;
+  const int e = gw / po, m = gw - e * po;
+  const float py = st.pos[(size_t)(2 * m) * N + e], px = st.pos[(size_t)(2 * m + 1) * N + e];
+  const int cy = (int)floorf(py), cx = (int)floorf(px);
+  const T* orow = obs + (size_t)e * cfg.obs_stride;
+  T* lo = local + ((size_t)e * po + m) * CH * 49;
+  for (int i = lane; i < CH * 49; i += 32) {
+    const int ch = i / 49, k = i - ch * 49, dy = k / 7, dx = k - dy * 7;
+    const int ys = min(max(cy + dy, 0), H + 5) - 3, xs = min(max(cx + dx, 0), W + 5) - 3;
+    lo[i] = (ys >= 0 && ys < H && xs >= 0 && xs < W) ? orow[(size_t)ch * C + ys * W + xs]
+                                                     : to_obs<T>(0.f);
+  }
+  T* re = rel + ((size_t)e * po + m) * 60;
+  for (int i = lane; i < 60; i += 32) re[i] = to_obs<T>(0.f);
+  __syncwarp();
+  const int n_opp = P - 1;
+  if (lane < n_opp) {
+    const int opp = (m + lane + 1) % P;
+    re[lane * 6 + 0] = to_obs<T>(__fsub_rn(st.pos[(size_t)(2 * opp) * N + e], py));
+    re[lane * 6 + 1] = to_obs<T>(__fsub_rn(st.pos[(size_t)(2 * opp + 1) * N + e], px));
+    re[lane * 6 + 2] = to_obs<T>(st.alive[(size_t)opp * N + e] ? 1.f : 0.f);
+  }
+  // nearest cells: each lane owns cells lane, lane + 32, ... (at most 14)
+  const int16_t* frow = st.fuse + (size_t)e * C;
+  int nb = 0, fsum = 0;
+  for (int c = lane; c < C; c += 32) {
+    const int f = frow[c];
+    nb += f > 0;
+    fsum += f;
+  }
+  nb = __reduce_add_sync(QQT_FULL, nb);
+  fsum = __reduce_add_sync(QQT_FULL, fsum);
+  const int k = min(10 - n_opp, C);
+  uint32_t taken = 0;
+  for (int j = 0; j < k; ++j) {
+    unsigned long long best = ~0ull;
+    int slot = 0;
+    for (int c = lane; c < C; c += 32, ++slot) {
+      if (taken >> slot & 1u) continue;
+      const int r = c / W, q = c - r * W;
+      const unsigned d = frow[c] > 0 ? (unsigned)(abs(r - cy) + abs(q - cx)) : 1000000u;
+      const unsigned long long key = ((unsigned long long)d << 32) | (unsigned)c;
+      best = key < best ? key : best;
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(QQT_FULL, best, o);
+      best = other < best ? other : best;
+    }
+    const int c = (int)(best & 0xffffffffull);
+    if (lane == (c & 31)) taken |= 1u << (c >> 5);
+    if (lane == 0) {
+      const int r = c / W, q = c - r * W;
+      T* sl = re + (n_opp + j) * 6;
+      sl[0] = to_obs<T>(__fsub_rn((float)q, (float)cx));
+      sl[1] = to_obs<T>(__fsub_rn((float)r, (float)cy));
+      sl[3] = to_obs<T>((best >> 32) < 100000ull ? 1.f : 0.f);
+    }
+  }
+  if (lane == 0) {
+    T* gl = glob + ((size_t)e * po + m) * 5;
+    const float tq = from_obs(to_obs<T>((float)st.t[e]));
+    const float hq = from_obs(to_obs<T>((float)st.hp[(size_t)m * N + e]));
+    gl[0] = to_obs<T>(__fdiv_rn(tq, (float)cfg.max_steps));
+    gl[1] = to_obs<T>(__fdiv_rn(hq, (float)cfg.max_hp));
+    const bool in = cy >= 0 && cy < H && cx >= 0 && cx < W;
+    gl[2] = in ? orow[(size_t)(2 * P + 1) * C + cy * W + cx] : to_obs<T>(0.f);
+    gl[3] = to_obs<T>(__fdiv_rn((float)nb, (float)max_bombs));
+    gl[4] = to_obs<T>(__fdiv_rn((float)fsum, (float)(max_bombs * cfg.fuse)));
+  }
+}
+
+extern "C" int qqt_local_view(const QqtCfg* cfg, const QqtState* st, const void* obs,
+                              int32_t max_bombs, int32_t only_p0, void* local, void* rel,
+                              void* glob, qqt_stream_t stream) {
+  int rc = check_cfg(cfg);
+  if (rc) return rc;
+  if (!st || !obs || !local || !rel || !glob || max_bombs <= 0) return QQT_E_ARG;
+  if (cfg->obs_channels < 2 * cfg->n_players + 2 ||
+      cfg->obs_stride < cfg->obs_channels * cfg->height * cfg->width)
+    return QQT_E_ARG;
+  const int po = only_p0 ? 1 : cfg->n_players;
+  const int64_t warps = (int64_t)cfg->n_envs * po;
+  const unsigned blocks = (unsigned)((warps * 32 + 255) / 256);
+  if (cfg->obs_fp32)
+    k_local_view<float><<<blocks, 256, 0, (cudaStream_t)stream>>>(
+        *cfg, *st, (const float*)obs, max_bombs, po, (float*)local, (float*)rel, (float*)glob);
+  else
+    k_local_view<__half><<<blocks, 256, 0, (cudaStream_t)stream>>>(
+        *cfg, *st, (const __half*)obs, max_bombs, po, (__half*)local, (__half*)rel,
+        (__half*)glob);
+  return launch_status();
+}
+
 extern "C" int qqt_observe(const QqtCfg* cfg, const QqtState* st, void* obs, float* danger,
                            uint8_t* mm, uint8_t* bm, qqt_stream_t stream) {
   int rc = check_cfg(cfg);

@@ -98,6 +98,8 @@ def lib():
             "qqt_flush_recycle": (c_i32, [P(QqtCfg), P(QqtState), c_p, c_u64, c_u64, c_p]),
             "qqt_gae": (c_i32, [c_p, c_i32, c_p, c_p, c_i32, c_p, c_i32, c_i32, ctypes.c_double,
                                 ctypes.c_double, c_p, c_p, c_p]),
+            "qqt_local_view": (c_i32, [P(QqtCfg), P(QqtState), c_p, c_i32, c_i32, c_p, c_p, c_p,
+                                       c_p]),
             "qqt_gather_rows": (c_i32, [c_p, c_i64, c_i64, c_p, c_i64, c_p, c_i64, c_i64, c_p]),
             "qqt_l1_pack": (c_i32, [c_p, c_i32, c_i32, c_i32, c_i32, c_i32, c_p, c_p]),
             "qqt_l1_pack_bytes": (c_u64, [c_i32]),

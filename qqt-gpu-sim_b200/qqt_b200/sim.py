@@ -468,6 +468,34 @@ class B200Sim:
         view = ob[:, :c].view(self.num_envs, cfg.n_channels, cfg.height, cfg.width)
         return view, mm, bm
 
+    def local_view_features(self, obs: torch.Tensor | None = None, only_p0: bool = False):
+        """Per-player LSTM features (sim/obs.py:241-340) -> (local (N,Po,C,7,7),
+        rel (N,Po,10,6), glob (N,Po,5)) in the observation's dtype, Po = 1 with
+        only_p0 else P.  obs: observation rows of this sim's layout ((N,
+        obs_stride) rows, or the (N,C,H,W) view observe() returns); None
+        reads the sim's own buffer (the last observe()).  Bomb slots at equal
+        distance come in ascending cell order (the reference leaves their
+        order to torch.topk)."""
+        rows = self._obs if obs is None else obs
+        if rows.dim() == 4:                      # a view of (N, obs_stride) rows
+            if rows.stride(0) != self.obs_stride:
+                raise ValueError("pass observation rows (N, obs_stride) or observe()'s view")
+            rows = torch.as_strided(rows, (rows.shape[0], self.obs_stride), (self.obs_stride, 1))
+        if tuple(rows.shape) != (self.num_envs, self.obs_stride) or rows.dtype != self._obs.dtype:
+            raise ValueError("observation rows must be (N, obs_stride) of the sim's dtype")
+        cfg = self.cfg
+        po = 1 if only_p0 else cfg.n_players
+        n, c = self.num_envs, cfg.n_channels
+        kw = dict(dtype=rows.dtype, device=self.device)
+        local = torch.empty((n, po, c, 7, 7), **kw)
+        rel = torch.empty((n, po, 10, 6), **kw)
+        glob = torch.empty((n, po, 5), **kw)
+        capi.check(capi.lib().qqt_local_view(ctypes.byref(self._ccfg), ctypes.byref(self._cstate),
+                                             rows.data_ptr(), int(cfg.max_bombs), int(only_p0),
+                                             local.data_ptr(), rel.data_ptr(), glob.data_ptr(),
+                                             self._stream()), "qqt_local_view")
+        return local, rel, glob
+
     def danger(self) -> torch.Tensor:
         """(N, H, W) float32 danger map computed by the last observe()."""
         return self._danger.view(self.num_envs, self.cfg.height, self.cfg.width)

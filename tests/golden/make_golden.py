@@ -63,7 +63,7 @@ def load_reference(ref_root):
     from train.model import ActorCritic
     return dict(bots=rbots, ts=rts, SimConfig=SimConfig, danger_map=danger_map,
                 resolve=resolve_explosions, encode_obs=encode_obs,
-                legal_mask=legal_mask, ActorCritic=ActorCritic)
+                legal_mask=legal_mask, ActorCritic=ActorCritic, root=ref_root)
 
 
 class FedTorch:
@@ -636,6 +636,58 @@ def hazard_golden(R):
     return out
 
 
+def local_view_golden(R):
+    """The reference's local_view_features (sim/obs.py:241-340) on seeded
+    states: P = 2 (corridor) and P = 3 (open) configurations, envs from bomb
+    free to 40 bombs (fewer bombs than slots leaves non-bomb filler slots),
+    players next to the border (clipped windows), fp16 observations from
+    the reference's own observe(); only_p0 both ways."""
+    import torch
+    sys.path.insert(0, R["root"])
+    from sim.obs import local_view_features
+    rts = R["ts"]
+    out = {}
+    for tag, kw, n, seed in (("p2", dict(map_mode="corridor", speed=3.0, max_steps=1800), 40, 31),
+                             ("p3", dict(map_mode="open", n_players=3), 24, 32)):
+        cfg = R["SimConfig"](**kw)
+        h, w, p = cfg.height, cfg.width, cfg.n_players
+        rng = np.random.default_rng(seed)
+        wall = np.broadcast_to(scenarios.border_walls(h, w), (n, h, w)).copy()
+        wall |= (rng.random((n, h, w)) < 0.08)
+        brick = (rng.random((n, h, w)) < 0.2) & ~wall
+        dens = rng.choice([0.0, 0.01, 0.03, 0.1, 0.25], n)[:, None, None]
+        fuse = np.where(rng.random((n, h, w)) < dens, rng.integers(1, 31, (n, h, w)), 0)
+        fuse = fuse.astype(np.int16)
+        fuse[wall] = 0
+        owner = np.where(fuse > 0, rng.integers(0, p, (n, h, w)), -1).astype(np.int8)
+        blast = np.where(fuse > 0, rng.integers(1, 6, (n, h, w)), 0).astype(np.int16)
+        pos = (rng.integers(1, h - 1, (n, p, 2)) + rng.random((n, p, 2)) * 0.98 + 0.01)
+        pos = pos.astype(np.float32)
+        alive = rng.random((n, p)) < 0.8
+        hp = rng.integers(0, cfg.max_hp + 1, (n, p)).astype(np.uint8)
+        t = rng.integers(0, cfg.max_steps, n).astype(np.int64)
+        sim = rts.BatchedSim(cfg, n, device="cpu", seed=0)
+        set_state(sim, {"wall": wall, "brick": brick, "fuse": fuse, "owner": owner,
+                        "bomb_blast": blast, "pos": pos})
+        sim.alive.copy_(torch.from_numpy(alive))
+        sim.hp.copy_(torch.from_numpy(hp).to(sim.hp.dtype))
+        sim.t.copy_(torch.from_numpy(t))
+        obs = sim.observe()
+        st = {"wall": wall, "brick": brick, "fuse": fuse, "owner": owner, "bomb_blast": blast,
+              "pos": pos, "alive": alive, "hp": hp, "t": t}
+        for k, v in st.items():
+            out[f"{tag}__{k}"] = np.asarray(v)
+        out[f"{tag}__obs"] = obs.numpy().copy()
+        for only in (False, True):
+            loc, rel, glob = local_view_features(sim.cfg, obs, sim.pos, sim.alive, sim.t,
+                                                 sim.fuse, sim.hp, only_p0=only)
+            sfx = "p0" if only else "all"
+            out[f"{tag}__{sfx}__local"] = loc.numpy().copy()
+            out[f"{tag}__{sfx}__rel"] = rel.numpy().copy()
+            out[f"{tag}__{sfx}__glob"] = glob.numpy().copy()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("QQT_REFERENCE_ROOT", "/root/reference"))
@@ -660,6 +712,7 @@ def main():
         "ppo_update": lambda: ppo_golden(R),
         "ckpt_adapt": lambda: ckpt_golden(R),
         "hazard_wave": lambda: hazard_golden(R),
+        "local_view": lambda: local_view_golden(R),
     }
     for name, fn in jobs.items():
         if args.only and name not in args.only.split(","):
