@@ -60,7 +60,7 @@ def _grad_worker(rank, world, port, q):
         dev = f"cuda:{rank}"
         g = G.load("ppo_update")
         model = _model(dev)
-        obs = torch.from_numpy(g["obs"][0].astype(np.float32)).to(dev)
+        obs = torch.from_numpy(g["obs"][0]).to(dev)
         half = obs.shape[0] // world
         sl = slice(rank * half, (rank + 1) * half)
         act = torch.from_numpy(g["act"][0]).to(dev)
@@ -136,7 +136,7 @@ def test_nccl_gradient_average_two_gpus():
     got = _spawn(_grad_worker)
     g = G.load("ppo_update")
     model = _model("cuda:0")
-    obs = torch.from_numpy(g["obs"][0].astype(np.float32)).cuda()
+    obs = torch.from_numpy(g["obs"][0]).cuda()
     logp, ent, v = model.evaluate(obs, torch.from_numpy(g["mm"][0]).cuda(),
                                   torch.from_numpy(g["bm"][0]).cuda(),
                                   torch.from_numpy(g["act"][0]).cuda())
