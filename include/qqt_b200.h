@@ -382,20 +382,25 @@ int qqt_l1_forward(const void *pack, const void *x, int64_t n_rows, int32_t x_st
 
 /* dw0 [128][k_in] float32 = dL/dW0 of the layer above for dL/dh1 = dh1
  * [n_rows][128] float32, in W0's own column order (seat pid's permutation
- * undone).  work = qqt_l1_wgrad_work_bytes(n_rows, k_in) bytes, 1024-byte
- * aligned. */
-int qqt_l1_wgrad(const void *x, int64_t n_rows, int32_t x_stride, int32_t k_in, const float *dh1,
-                 int32_t n_players, int32_t channels, int32_t hw, int32_t pid, float *dw0,
-                 void *work, qqt_stream_t stream);
+ * undone).  Row r of the input is x row r, or, with idx (n_rows int64 row
+ * ids into x's n_src rows), x row idx[r] read in place (TMA gather4; an id
+ * outside [0, n_src) reads row 0 and raises QQT_DEV_BAD_INDEX).  work =
+ * qqt_l1_wgrad_work_bytes(n_rows, k_in) bytes, 1024-byte aligned. */
+int qqt_l1_wgrad(const void *x, int64_t n_rows, int32_t x_stride, int32_t k_in,
+                 const int64_t *idx, int64_t n_src, const float *dh1, int32_t n_players,
+                 int32_t channels, int32_t hw, int32_t pid, float *dw0, void *work,
+                 qqt_stream_t stream);
 uint64_t qqt_l1_wgrad_work_bytes(int64_t n_rows, int32_t k_in);
 
 /* Training forward of ActorCritic(mlp) for one seat (train/model.py:121-153,
- * 247-256): obs rows [n_rows][obs_stride] fp16, legal masks, recorded actions
- * [n_rows][act_stride] int64 -> logp (of the actions), entropy, value [n_rows]
- * and the pre-LayerNorm activations h1, h2 [n_rows][128] that the backward
- * reads.  pack = qqt_mlp_pack(..., n_seats = 1, pids = {pid}, ...). */
+ * 247-256): obs rows [n_rows][obs_stride] fp16 (or, with idx, row idx[r] of
+ * obs's n_src rows, read in place by TMA gather4), legal masks, recorded
+ * actions [n_rows][act_stride] int64 -> logp (of the actions), entropy, value
+ * [n_rows] and the pre-LayerNorm activations h1, h2 [n_rows][128] that the
+ * backward reads.  pack = qqt_mlp_pack(..., n_seats = 1, pids = {pid}, ...). */
 int qqt_mlp_train_forward(const void *pack, const void *obs, int32_t n_rows, int32_t obs_stride,
-                          int32_t k_in, const uint8_t *mm, int32_t mm_stride, const uint8_t *bm,
+                          int32_t k_in, const int64_t *idx, int64_t n_src, const uint8_t *mm,
+                          int32_t mm_stride, const uint8_t *bm,
                           int32_t bm_stride, const int64_t *act, int32_t act_stride, float *logp,
                           float *ent, float *value, float *h1, float *h2, qqt_stream_t stream);
 

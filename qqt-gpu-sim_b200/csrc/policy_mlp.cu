@@ -92,6 +92,17 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
       : "memory");
 }
 
+// Four rows (y0..y3) of columns x..x+63 of a tensor map whose box is one
+// row high, landing as a four-row box at dst (TMA tile::gather4).
+__device__ __forceinline__ void tma_gather4(const CUtensorMap* map, uint64_t* bar, void* dst,
+                                            int x, int y0, int y1, int y2, int y3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+      "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3)
+      : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -410,6 +421,8 @@ struct TrainOut {
   float* h1;
   float* h2;
   float* ent;
+  const int64_t* idx;    // optional: row r of the minibatch is row idx[r] of the A map
+  int n_src;             // rows of the A map (idx bounds)
 };
 
 // ------------------------------------------------------------ fused MLP
@@ -438,7 +451,7 @@ struct FusedCfg {
   static constexpr int kActBytes = kBM * 128 * 2;       // one of hi / lo
   static constexpr int kTailBytes = kAct + 2 * kActBytes;
   static constexpr int kRegion = kPipeBytes > kTailBytes ? kPipeBytes : kTailBytes;
-  static constexpr int kSmem = kRegion + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kSmem = kRegion + 1024 /*align*/ + 256 /*barriers*/ + 512 /*row ids*/;
   // split-K partial sums of a non-leader CTA: [seat][128 rows][128] fp32 at
   // the start of its (drained) pipeline region
   static constexpr int kPartBytes = (NT / 128) * kBM * 128 * 4;
@@ -749,6 +762,23 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
   bool arrived = false;   // this thread's arrival on the closing cluster barrier
 
   if (warp == 0) {
+    // training forward over minibatch rows of a larger buffer: the tile's
+    // 128 row ids (rows past the end and invalid ids read row 0; invalid ids
+    // raise QQT_DEV_BAD_INDEX), fetched by TMA tile::gather4, four rows each
+    int32_t* row_id = (int32_t*)(smem + G::kRegion + 256);
+    const bool gather = TRAIN && tr.idx != nullptr;
+    if (gather) {
+      for (int i = lane; i < kBM; i += 32) {
+        const int r = m0 + i;
+        int64_t v = r < n_rows ? tr.idx[r] : 0;
+        if (v < 0 || v >= tr.n_src) {
+          flag_error(QQT_DEV_BAD_INDEX);
+          v = 0;
+        }
+        row_id[i] = (int32_t)v;
+      }
+      __syncwarp();
+    }
     if (lane == 0) {
       // ---------------- TMA producer (layer 1, this rank's K tiles)
       int issued_until = 0;
@@ -767,7 +797,14 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         uint8_t* st = smem + s * G::kStageBytes;
         const int kx = (kt0 + (kt + k0) % n_kt) * kBK;
         mbar_expect_tx(&full[s], G::kStageBytes);
-        tma_load_2d(&tm_a, &full[s], st, kx, m0);
+        if (gather) {
+#pragma unroll 4
+          for (int g = 0; g < kBM / 4; ++g)
+            tma_gather4(&tm_a, &full[s], st + g * 512, kx, row_id[4 * g], row_id[4 * g + 1],
+                        row_id[4 * g + 2], row_id[4 * g + 3]);
+        } else {
+          tma_load_2d(&tm_a, &full[s], st, kx, m0);
+        }
         if (SPLIT_A) tma_load_2d(&tm_alo, &full[s], st + G::kABytes, kx, m0);
         tma_load_2d(&tm_b, &full[s], st + G::kAAll, kx, 0);
         tma_load_2d(&tm_b, &full[s], st + G::kAAll + G::kBBytes, kx, NT);

@@ -290,7 +290,7 @@ constexpr int kWgA = 2 * kWgBox;                          // 128 hidden units (h
 constexpr int kWgN = 256;                                 // observation columns per CTA
 constexpr int kWgStageBytes = 2 * kWgA + (kWgN / 64) * kWgBox;   // 64 KB
 constexpr int kWgThreads = 192;
-constexpr int kWgSmem = kWgStages * kWgStageBytes + 1024 + 256;
+constexpr int kWgSmem = kWgStages * kWgStageBytes + 1024 + 256 + 256 /*row ids*/;
 static_assert(kWgSmem <= 232448, "weight-gradient shared memory");
 
 // MN-major operand tile with the 128-byte swizzle: rows of 64 elements (128
@@ -315,7 +315,8 @@ __host__ __device__ constexpr uint32_t idesc_f16_mn(int m, int n) {
 
 __global__ void __launch_bounds__(kWgThreads, 1)
 k_l1_wgrad(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo,
-           const __grid_constant__ CUtensorMap tm_x, int n_rows, int kp, float* __restrict__ part) {
+           const __grid_constant__ CUtensorMap tm_x, int n_rows, int kp, float* __restrict__ part,
+           const int64_t* __restrict__ idx, int n_src) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* full = (uint64_t*)(smem + kWgStages * kWgStageBytes);
@@ -354,29 +355,61 @@ k_l1_wgrad(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CU
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {
-      int issued = 0;
-      for (int i = 0; i < n_st; ++i) {
-        const int s = i % kWgStages;
+    // the whole warp stages a minibatch's row ids (gathered x rows: row r of
+    // the minibatch is row idx[r] of the x map; rows past the end and
+    // invalid ids read row 0, invalid ids raise QQT_DEV_BAD_INDEX); lane 0
+    // waits on the barriers and issues the copies
+    int32_t* row_id = (int32_t*)(smem + kWgStages * kWgStageBytes + 256);
+    const bool gather = idx != nullptr;
+    int issued = 0;
+    for (int i = 0; i < n_st; ++i) {
+      const int s = i % kWgStages;
+      const int y = (s0 + i) * kWgBK;
+      bool go = true;
+      if (lane == 0) {
         if (i >= kWgStages && !mbar_wait(&empty[s], ((i / kWgStages) - 1) & 1)) {
           *abort_flag = 1;
-          break;
+          go = false;
         }
-        if (*abort_flag) break;
+        if (*abort_flag) go = false;
+      }
+      if (!__shfl_sync(0xffffffffu, go, 0)) break;
+      if (gather) {
+        for (int j = lane; j < kWgBK; j += 32) {
+          const int r = y + j;
+          int64_t v = r < n_rows ? idx[r] : 0;
+          if (v < 0 || v >= n_src) {
+            flag_error(QQT_DEV_BAD_INDEX);
+            v = 0;
+          }
+          row_id[j] = (int32_t)v;
+        }
+        __syncwarp();
+      }
+      if (lane == 0) {
         uint8_t* st = smem + s * kWgStageBytes;
-        const int y = (s0 + i) * kWgBK;
         mbar_expect_tx(&full[s], stage_tx);
         tma_load_2d(&tm_hi, &full[s], st, 0, y);
         tma_load_2d(&tm_hi, &full[s], st + kWgBox, 64, y);
         tma_load_2d(&tm_lo, &full[s], st + kWgA, 0, y);
         tma_load_2d(&tm_lo, &full[s], st + kWgA + kWgBox, 64, y);
-        for (int q = 0; q < n_blk; ++q)
-          tma_load_2d(&tm_x, &full[s], st + 2 * kWgA + q * kWgBox, n0 + 64 * q, y);
+        for (int q = 0; q < n_blk; ++q) {
+          uint8_t* dst = st + 2 * kWgA + q * kWgBox;
+          if (gather) {
+            for (int g = 0; g < kWgBK / 4; ++g)
+              tma_gather4(&tm_x, &full[s], dst + g * 512, n0 + 64 * q, row_id[4 * g],
+                          row_id[4 * g + 1], row_id[4 * g + 2], row_id[4 * g + 3]);
+          } else {
+            tma_load_2d(&tm_x, &full[s], dst, n0 + 64 * q, y);
+          }
+        }
         issued = i + 1;
       }
+      __syncwarp();   // lane 0 has read this stage's row ids before they are replaced
+    }
+    if (lane == 0)
       for (int j = max(0, issued - kWgStages); j < issued; ++j)
         mbar_wait(&full[j % kWgStages], (j / kWgStages) & 1);
-    }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = idesc_f16_mn(128, nw);
@@ -1431,12 +1464,14 @@ extern "C" uint64_t qqt_l1_wgrad_work_bytes(int64_t n_rows, int32_t k_in) {
 }
 
 extern "C" int qqt_l1_wgrad(const void* x, int64_t n_rows, int32_t x_stride, int32_t k_in,
-                            const float* dh1, int32_t n_players, int32_t channels, int32_t hw,
-                            int32_t pid, float* dw0, void* work, qqt_stream_t stream) {
+                            const int64_t* idx, int64_t n_src, const float* dh1,
+                            int32_t n_players, int32_t channels, int32_t hw, int32_t pid,
+                            float* dw0, void* work, qqt_stream_t stream) {
   if (!x || !dh1 || !dw0 || !work || n_rows <= 0 || k_in <= 0 || x_stride < k_in ||
       k_in != channels * hw)
     return QQT_E_ARG;
-  if (n_rows > (int64_t)0x7fffff00) return QQT_E_LIMIT;
+  if (n_rows > (int64_t)0x7fffff00 || (idx && (n_src <= 0 || n_src > (int64_t)0x7fffff00)))
+    return QQT_E_LIMIT;
   if ((x_stride % 8) || ((uintptr_t)x & 15) || ((uintptr_t)dh1 & 15) || ((uintptr_t)work & 1023))
     return QQT_E_ALIGN;
   ColumnSource cs;
@@ -1457,13 +1492,15 @@ extern "C" int qqt_l1_wgrad(const void* x, int64_t n_rows, int32_t x_stride, int
   CUtensorMap mh, ml, mx;
   if (!make_map(&mh, wk + L.hi, 128, (uint64_t)n_rows, 256, kWgBK) ||
       !make_map(&ml, wk + L.lo, 128, (uint64_t)n_rows, 256, kWgBK) ||
-      !make_map(&mx, x, (uint64_t)k_in, (uint64_t)n_rows, (uint64_t)x_stride * 2, kWgBK))
+      !make_map(&mx, x, (uint64_t)k_in, (uint64_t)(idx ? n_src : n_rows), (uint64_t)x_stride * 2,
+                idx ? 1u : (uint32_t)kWgBK))
     return QQT_E_ARG;
   cudaFuncSetAttribute(k_l1_wgrad, cudaFuncAttributeMaxDynamicSharedMemorySize, kWgSmem);
   const int slices = wgrad_slices((int)n_rows, kp);
   const dim3 grid((unsigned)((kp + kWgN - 1) / kWgN), (unsigned)slices);
   float* part = (float*)(wk + L.part);
-  k_l1_wgrad<<<grid, kWgThreads, kWgSmem, st>>>(mh, ml, mx, (int)n_rows, kp, part);
+  k_l1_wgrad<<<grid, kWgThreads, kWgSmem, st>>>(mh, ml, mx, (int)n_rows, kp, part, idx,
+                                                 (int)n_src);
   const int64_t n_out = (int64_t)128 * k_in;
   k_wgrad_reduce<<<(unsigned)((n_out + 255) / 256), 256, 0, st>>>(part, slices, kp, k_in, hw, cs,
                                                                  amax, dw0);
@@ -1474,7 +1511,8 @@ extern "C" int qqt_l1_wgrad(const void* x, int64_t n_rows, int32_t x_stride, int
 // qqt_mlp_pack with n_seats = 1 and the seat's pid)
 
 extern "C" int qqt_mlp_train_forward(const void* pack, const void* obs, int32_t n_rows,
-                                     int32_t obs_stride, int32_t k_in, const uint8_t* mm,
+                                     int32_t obs_stride, int32_t k_in, const int64_t* idx,
+                                     int64_t n_src, const uint8_t* mm,
                                      int32_t mm_stride, const uint8_t* bm, int32_t bm_stride,
                                      const int64_t* act, int32_t act_stride, float* logp,
                                      float* ent, float* value, float* h1, float* h2,
@@ -1487,10 +1525,12 @@ extern "C" int qqt_mlp_train_forward(const void* pack, const void* obs, int32_t 
   if ((obs_stride % 8) || ((uintptr_t)obs & 15) || ((uintptr_t)pack & 255) ||
       ((uintptr_t)h1 & 15) || ((uintptr_t)h2 & 15))
     return QQT_E_ALIGN;
+  if (idx && (n_src <= 0 || n_src > (int64_t)0x7fffff00)) return QQT_E_LIMIT;
   const MlpPack L = mlp_pack_layout(k_in, 1);
   const uint8_t* pk = (const uint8_t*)pack;
   CUtensorMap ma, mb;
-  if (!make_map(&ma, obs, (uint64_t)k_in, (uint64_t)n_rows, (uint64_t)obs_stride * 2, kBM))
+  if (!make_map(&ma, obs, (uint64_t)k_in, (uint64_t)(idx ? n_src : n_rows),
+                (uint64_t)obs_stride * 2, idx ? 1u : (uint32_t)kBM))
     return QQT_E_ARG;
   if (!make_map(&mb, pk + L.b_off, (uint64_t)L.kp, 256, (uint64_t)L.kp * 2, 128))
     return QQT_E_ARG;
@@ -1503,6 +1543,8 @@ extern "C" int qqt_mlp_train_forward(const void* pack, const void* obs, int32_t 
   tr.h1 = h1;
   tr.h2 = h2;
   tr.ent = ent;
+  tr.idx = idx;
+  tr.n_src = (int)n_src;
   return launch_mlp_fused<128, false, true>(ma, ma, mb, n_rows, L.kp / kBK,
                                             (const float*)(pk + L.f_off), pk + L.img_off, io, 0,
                                             mm_stride, bm_stride, nullptr, act_stride, logp,

@@ -104,11 +104,12 @@ def lib():
             "qqt_l1_pack": (c_i32, [c_p, c_i32, c_i32, c_i32, c_i32, c_i32, c_p, c_p]),
             "qqt_l1_pack_bytes": (c_u64, [c_i32]),
             "qqt_l1_forward": (c_i32, [c_p, c_p, c_i64, c_i32, c_i32, c_p, c_p, c_p]),
-            "qqt_l1_wgrad": (c_i32, [c_p, c_i64, c_i32, c_i32, c_p, c_i32, c_i32, c_i32, c_i32,
-                                     c_p, c_p, c_p]),
+            "qqt_l1_wgrad": (c_i32, [c_p, c_i64, c_i32, c_i32, c_p, c_i64, c_p, c_i32, c_i32,
+                                     c_i32, c_i32, c_p, c_p, c_p]),
             "qqt_l1_wgrad_work_bytes": (c_u64, [c_i64, c_i32]),
-            "qqt_mlp_train_forward": (c_i32, [c_p, c_p, c_i32, c_i32, c_i32, c_p, c_i32, c_p,
-                                              c_i32, c_p, c_i32, c_p, c_p, c_p, c_p, c_p, c_p]),
+            "qqt_mlp_train_forward": (c_i32, [c_p, c_p, c_i32, c_i32, c_i32, c_p, c_i64, c_p,
+                                              c_i32, c_p, c_i32, c_p, c_i32, c_p, c_p, c_p, c_p,
+                                              c_p, c_p]),
             "qqt_mlp_train_backward": (c_i32, [c_p, c_i32, c_i32, c_p, c_p, c_p, c_i32, c_p,
                                                c_i32, c_p, c_i32, c_p, c_p, c_p, c_p, c_p]),
             "qqt_mlp_train_work_bytes": (c_u64, [c_i32]),

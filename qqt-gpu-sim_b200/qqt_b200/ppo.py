@@ -141,8 +141,8 @@ class _Layer1(torch.autograd.Function):
         dw0 = torch.empty((dh1.shape[1], ctx.k_in), dtype=torch.float32, device=dev)
         work = torch.empty(int(L.qqt_l1_wgrad_work_bytes(n, ctx.k_in)) + 1024, dtype=torch.uint8,
                            device=dev)
-        capi.check(L.qqt_l1_wgrad(rows.data_ptr(), n, rows.stride(0), ctx.k_in, dh1.data_ptr(),
-                                  n_players, channels, hw, pid, dw0.data_ptr(),
+        capi.check(L.qqt_l1_wgrad(rows.data_ptr(), n, rows.stride(0), ctx.k_in, None, 0,
+                                  dh1.data_ptr(), n_players, channels, hw, pid, dw0.data_ptr(),
                                   _aligned(work, 1024), capi.stream_ptr(dev)), "qqt_l1_wgrad")
         return None, dw0, dh1.sum(0), None, None
 
@@ -151,10 +151,12 @@ class _MLPTrain(torch.autograd.Function):
     """ActorCritic(mlp).evaluate (train/model.py:121-153, 247-256) on the B200
     kernels: returns per-row (logp of the recorded actions, entropy, value);
     backward gives every parameter's gradient in the reference's layouts.
+    rows: the batch's observation rows, or, with idx (int64 row ids), a
+    larger row buffer whose rows idx the batch reads in place (TMA gather).
     params: the 20 tensors in state_dict order."""
 
     @staticmethod
-    def forward(ctx, rows, mm, bm, act, geom, *params):
+    def forward(ctx, rows, idx, mm, bm, act, geom, *params):
         from . import _capi as capi
         n_players, c, hw, pid = geom
         k_in = c * hw
@@ -166,19 +168,23 @@ class _MLPTrain(torch.autograd.Function):
         ptrs = (ctypes.c_void_p * 20)(*[p.data_ptr() for p in pc])
         pids = (ctypes.c_int32 * 2)(pid, 0)
         capi.check(L.qqt_mlp_pack(ptrs, k_in, n_players, c, hw, 1, pids, pk, st), "qqt_mlp_pack")
-        n = rows.shape[0]
+        idx = None if idx is None else idx.to(torch.int64).contiguous()
+        n = rows.shape[0] if idx is None else idx.numel()
         mm8 = mm.contiguous().view(torch.uint8)
         bm8 = bm.contiguous().view(torch.uint8)
         a64 = act.to(torch.int64).contiguous()
         logp, ent, v = (torch.empty(n, dtype=torch.float32, device=dev) for _ in range(3))
         h1, h2 = (torch.empty((n, 128), dtype=torch.float32, device=dev) for _ in range(2))
         capi.check(L.qqt_mlp_train_forward(pk, rows.data_ptr(), n, rows.stride(0), k_in,
+                                           None if idx is None else idx.data_ptr(),
+                                           0 if idx is None else rows.shape[0],
                                            mm8.data_ptr(), mm8.stride(0), bm8.data_ptr(),
                                            bm8.stride(0), a64.data_ptr(), a64.stride(0),
                                            logp.data_ptr(), ent.data_ptr(), v.data_ptr(),
                                            h1.data_ptr(), h2.data_ptr(), st),
                    "qqt_mlp_train_forward")
         ctx.save_for_backward(rows, mm8, bm8, a64, h1, h2)
+        ctx.idx = idx
         ctx.pack, ctx.pk, ctx.geom = pack, pk, geom
         ctx.shapes = [p.shape for p in params]
         return logp, ent, v
@@ -187,11 +193,12 @@ class _MLPTrain(torch.autograd.Function):
     def backward(ctx, gl, ge, gv):
         from . import _capi as capi
         rows, mm8, bm8, a64, h1, h2 = ctx.saved_tensors
+        idx = ctx.idx
         n_players, c, hw, pid = ctx.geom
         k_in = c * hw
         L, dev = capi.lib(), rows.device
         st = capi.stream_ptr(dev)
-        n = rows.shape[0]
+        n = h1.shape[0]
         g = torch.zeros((3, n), dtype=torch.float32, device=dev)
         for i, gi in enumerate((gl, ge, gv)):
             if gi is not None:
@@ -209,10 +216,12 @@ class _MLPTrain(torch.autograd.Function):
                    "qqt_mlp_train_backward")
         wk = torch.empty(int(L.qqt_l1_wgrad_work_bytes(n, k_in)) + 1024, dtype=torch.uint8,
                          device=dev)
-        capi.check(L.qqt_l1_wgrad(rows.data_ptr(), n, rows.stride(0), k_in, dh1.data_ptr(),
+        capi.check(L.qqt_l1_wgrad(rows.data_ptr(), n, rows.stride(0), k_in,
+                                  None if idx is None else idx.data_ptr(),
+                                  0 if idx is None else rows.shape[0], dh1.data_ptr(),
                                   n_players, c, hw, pid, grads[0].data_ptr(),
                                   _aligned(wk, 1024), st), "qqt_l1_wgrad")
-        return (None, None, None, None, None, *grads)
+        return (None, None, None, None, None, None, *grads)
 
 
 class MLPActorCritic(nn.Module):
@@ -253,13 +262,19 @@ class MLPActorCritic(nn.Module):
         logz = z - torch.logsumexp(z, -1, keepdim=True)
         return logz
 
-    def evaluate(self, obs, mm, bm, actions, pid: int = 0):
+    def evaluate(self, obs, mm, bm, actions, pid: int = 0, rows_idx=None):
         """(log-prob of `actions`, entropy, value) under the masked heads
-        (train/model.py:247-256)."""
+        (train/model.py:247-256).  rows_idx (CUDA only): the batch is rows
+        rows_idx of the row buffer `obs` (the reference's obs[sel]), read in
+        place by the kernels' TMA gathers -- no copy of the batch, for callers
+        short of memory; on a rollout buffer far larger than L2 a
+        `gather_rows` copy first is about 4x faster."""
         if obs.is_cuda:
             c, h, w = self.obs_shape
-            return _MLPTrain.apply(obs_rows(obs, self.k_in), mm, bm, actions,
+            return _MLPTrain.apply(obs_rows(obs, self.k_in), rows_idx, mm, bm, actions,
                                    (self.n_players, c, h * w, pid), *self.parameters())
+        if rows_idx is not None:
+            obs = obs[rows_idx]
         ml, bl, v = self(obs, pid)
         lm = self._masked(ml, mm)
         lb = self._masked(bl, bm)
@@ -354,8 +369,11 @@ def ppo_update(model: MLPActorCritic, opt, data: dict, last_val, cfg: PPOConfig,
         for start in range(0, total, mb):
             sel = perm[start:start + mb]
             if obs.is_cuda:
-                # the minibatch's rows, gathered into one reused block; the
-                # previous minibatch's backward has finished reading it
+                # the minibatch's rows copied whole into one reused block (whole
+                # 4.7 KB rows stream at HBM speed; reading them in place with
+                # TMA gathers, evaluate(rows_idx=sel), fetches 128-byte pieces
+                # of random rows and measured 4x slower); the previous
+                # minibatch's backward has finished reading the block
                 if xg is None or xg.shape[0] < sel.numel():
                     xg = torch.empty((sel.numel(), obs.shape[1]), dtype=obs.dtype, device=dev)
                 x = gather_rows(obs, sel, xg[:sel.numel()])

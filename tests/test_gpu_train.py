@@ -187,3 +187,47 @@ def test_obs_rows_pads_four_dimensional_batches():
     assert not r[:, K_IN:].any()
     with pytest.raises(TypeError):
         obs_rows(x.float(), K_IN)
+
+
+@pytest.mark.parametrize("n", [77, 3000])
+def test_gathered_rows_read_in_place_equal_pre_gathered(n):
+    """rows_idx: the training forward and the weight-gradient GEMM read the
+    minibatch's rows of the row buffer in place (TMA gather4); outputs and
+    every gradient equal the pre-gathered path bit for bit.  Invalid ids read
+    row 0 and raise QQT_DEV_BAD_INDEX."""
+    _need_cuda()
+    from qqt_b200 import _capi
+    torch.manual_seed(1)
+    m = MLPActorCritic(SHAPE, 2).cuda()
+    src = _rows(5000, 21)
+    idx = torch.randint(0, 5000, (n,), device="cuda")
+    mm = torch.rand((n, 5), device="cuda") < 0.8
+    mm[:, 4] = True
+    bm = torch.rand((n, 2), device="cuda") < 0.7
+    bm[:, 0] = True
+    act = torch.stack([torch.multinomial(mm.float(), 1)[:, 0],
+                       torch.multinomial(bm.float(), 1)[:, 0]], -1)
+    w = torch.linspace(-1, 1, n, device="cuda")
+
+    def run(x, rows_idx):
+        m.zero_grad()
+        logp, ent, v = m.evaluate(x, mm, bm, act, 1, rows_idx=rows_idx)
+        (-(logp * w).mean() + 0.5 * (v * v).mean() - 0.03 * ent.mean()).backward()
+        return [logp.detach(), ent.detach(), v.detach()] + [p.grad.clone() for p in m.parameters()]
+
+    ref = run(src[idx], None)
+    got = run(src, idx)
+    torch.cuda.synchronize()
+    assert _capi.device_error() == 0
+    for a, b in zip(ref, got):
+        assert torch.equal(a, b)
+    bad = idx.clone()
+    bad[0], bad[-1] = -1, 5000
+    fixed = bad.clamp(0, 4999)
+    fixed[0] = fixed[-1] = 0
+    ref = run(src[fixed], None)
+    got = run(src, bad)
+    torch.cuda.synchronize()
+    assert _capi.device_error() == 1 << 4
+    for a, b in zip(ref, got):
+        assert torch.equal(a, b)
