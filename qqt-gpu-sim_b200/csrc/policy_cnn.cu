@@ -226,11 +226,37 @@ __device__ __forceinline__ void conv_mma(uint32_t tmem, const uint8_t* act_hi, c
 // !FINAL: the result goes back into the activation buffer as the next
 // layer's fp16 hi/lo input; FINAL: flattened (c * HW + pixel) into the
 // global hi / lo rows.
+// The LN affine parameters of the thread's two pixels ([pixel][C] layout,
+// 16-byte loads; the caller issues this before waiting for the layer's MMAs,
+// so the loads overlap them).
+template <int N, int NREAL>
+__device__ __forceinline__ void ln_params(const float* __restrict__ lnf, int lg, int lb, float* g0,
+                                          float* b0, float* g1, float* b1) {
+  constexpr int NC = N / 2;
+  const int w = warp_id(), q = w & 3, cg = w >> 2, lane = lane_id();
+  const int c0 = cg * NC;
+  const bool real = c0 < NREAL;
+  const int r0 = q * 32 + lane, r1 = 128 + r0;
+  const int p0 = real ? interior_pixel(r0) : -1, p1 = real ? interior_pixel(r1) : -1;
+#pragma unroll
+  for (int c = 0; c < NC; c += 4) {
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 ga = p0 >= 0 ? __ldg(reinterpret_cast<const float4*>(lnf + lg + p0 * NREAL + c0 + c)) : z;
+    const float4 ba = p0 >= 0 ? __ldg(reinterpret_cast<const float4*>(lnf + lb + p0 * NREAL + c0 + c)) : z;
+    const float4 gb = p1 >= 0 ? __ldg(reinterpret_cast<const float4*>(lnf + lg + p1 * NREAL + c0 + c)) : z;
+    const float4 bb = p1 >= 0 ? __ldg(reinterpret_cast<const float4*>(lnf + lb + p1 * NREAL + c0 + c)) : z;
+    g0[c] = ga.x; g0[c + 1] = ga.y; g0[c + 2] = ga.z; g0[c + 3] = ga.w;
+    b0[c] = ba.x; b0[c + 1] = ba.y; b0[c + 2] = ba.z; b0[c + 3] = ba.w;
+    g1[c] = gb.x; g1[c + 1] = gb.y; g1[c + 2] = gb.z; g1[c + 3] = gb.w;
+    b1[c] = bb.x; b1[c + 1] = bb.y; b1[c + 2] = bb.z; b1[c + 3] = bb.w;
+  }
+}
+
 template <int N, int NREAL, bool FINAL>
-__device__ __forceinline__ void conv_epilogue(uint32_t tmem, const float* __restrict__ lnf, int lg,
-                                              int lb, const float* cb, uint8_t* act_hi,
-                                              uint8_t* act_lo, float* red, __half* out_hi,
-                                              __half* out_lo) {
+__device__ __forceinline__ void conv_epilogue(uint32_t tmem, const float* g0, const float* b0,
+                                              const float* g1, const float* b1, const float* cb,
+                                              uint8_t* act_hi, uint8_t* act_lo, float* red,
+                                              __half* out_hi, __half* out_lo) {
   constexpr int NC = N / 2;
   const int w = warp_id(), q = w & 3, cg = w >> 2, lane = lane_id();
   const int c0 = cg * NC;
@@ -255,19 +281,6 @@ __device__ __forceinline__ void conv_epilogue(uint32_t tmem, const float* __rest
   }
   const int r0 = q * 32 + lane, r1 = 128 + r0;
   const int p0 = real ? interior_pixel(r0) : -1, p1 = real ? interior_pixel(r1) : -1;
-  float g0[NC], b0[NC], g1[NC], b1[NC];
-#pragma unroll
-  for (int c = 0; c < NC; c += 4) {
-    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-    const float4 ga = p0 >= 0 ? __ldg(reinterpret_cast<const float4*>(lnf + lg + p0 * NREAL + c0 + c)) : z;
-    const float4 ba = p0 >= 0 ? __ldg(reinterpret_cast<const float4*>(lnf + lb + p0 * NREAL + c0 + c)) : z;
-    const float4 gb = p1 >= 0 ? __ldg(reinterpret_cast<const float4*>(lnf + lg + p1 * NREAL + c0 + c)) : z;
-    const float4 bb = p1 >= 0 ? __ldg(reinterpret_cast<const float4*>(lnf + lb + p1 * NREAL + c0 + c)) : z;
-    g0[c] = ga.x; g0[c + 1] = ga.y; g0[c + 2] = ga.z; g0[c + 3] = ga.w;
-    b0[c] = ba.x; b0[c + 1] = ba.y; b0[c + 2] = ba.z; b0[c + 3] = ba.w;
-    g1[c] = gb.x; g1[c + 1] = gb.y; g1[c + 2] = gb.z; g1[c + 3] = gb.w;
-    b1[c] = bb.x; b1[c + 1] = bb.y; b1[c + 2] = bb.z; b1[c + 3] = bb.w;
-  }
   float s = 0.f;
 #pragma unroll
   for (int c = 0; c < NC; ++c) {
@@ -327,6 +340,65 @@ __device__ __forceinline__ void conv_epilogue(uint32_t tmem, const float* __rest
   }
 }
 
+// One conv layer of the sample in the activation buffer: the MMAs (thread
+// 0), the LN parameters fetched while they run, then the epilogue.
+template <int C, int CIN, int TAPS, bool SPLIT, int NREAL, bool FINAL>
+__device__ __forceinline__ bool conv_layer(uint32_t tmem, uint8_t* act_hi, uint8_t* act_lo,
+                                           const uint8_t* w, uint64_t* dbar, uint32_t& phase,
+                                           const float* __restrict__ lnf, int lg, int lb,
+                                           const float* cb, float* red, __half* ohi,
+                                           __half* olo) {
+  constexpr int NC = C / 2;
+  fence_proxy_async();
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    conv_mma<C, CIN, TAPS, SPLIT>(tmem, act_hi, act_lo, w);
+    umma_commit(dbar);
+  }
+  float g0[NC], b0[NC], g1[NC], b1[NC];
+  ln_params<C, NREAL>(lnf, lg, lb, g0, b0, g1, b1);
+  const bool ok = __syncthreads_and(mbar_wait(dbar, phase & 1));
+  ++phase;
+  if (!ok) return false;
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  conv_epilogue<C, NREAL, FINAL>(tmem, g0, b0, g1, b1, cb, act_hi, act_lo, red, ohi, olo);
+  return true;
+}
+
+// The observation of one env (14 channels + 2 zero per interior pixel),
+// one (pixel, 8-channel chunk) item per thread and pass: loaded into
+// registers first, stored into the activation buffer's hi half later.
+constexpr int kObsItems = 2 * kCnnHW;
+__device__ __forceinline__ void obs_load(const __half* __restrict__ orow, uint32_t (*v)[4]) {
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int i = threadIdx.x + k * kTrunkWarps * 32;
+    const int p = i >> 1, ch = i & 1;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = ch * 8 + 2 * j;
+      const bool in = i < kObsItems;
+      const uint32_t a = in && c < 14 ? __half_as_ushort(orow[c * kCnnHW + p]) : 0u;
+      const uint32_t b = in && c + 1 < 14 ? __half_as_ushort(orow[(c + 1) * kCnnHW + p]) : 0u;
+      v[k][j] = a | (b << 16);
+    }
+  }
+}
+
+__device__ __forceinline__ void obs_store(const uint32_t (*v)[4], uint8_t* act_hi) {
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int i = threadIdx.x + k * kTrunkWarps * 32;
+    if (i >= kObsItems) continue;
+    const int p = i >> 1, ch = i & 1;
+    const int r = kActMargin + (p / kCnnW + 1) * kCnnPW + (p % kCnnW + 1);
+    *reinterpret_cast<uint4*>(act_hi + r * 128 + ((ch ^ (r & 7)) << 4)) =
+        make_uint4(v[k][0], v[k][1], v[k][2], v[k][3]);
+  }
+}
+
 __global__ void __launch_bounds__(kTrunkWarps * 32, 1)
 k_cnn_trunk(const __half* __restrict__ obs, int obs_stride, int n, int n_seats,
             const uint8_t* __restrict__ pk, __half* __restrict__ out) {
@@ -370,25 +442,16 @@ k_cnn_trunk(const __half* __restrict__ obs, int obs_stride, int n, int n_seats,
   bool ok = __syncthreads_and(mbar_wait(wbar, 0));
   uint32_t phase = 0;
   const int items = n * n_seats;
+  static_assert(kObsItems <= 2 * kTrunkWarps * 32, "two observation items per thread");
+  uint32_t ov[2][4];
+  if ((int)blockIdx.x < items) {
+    const int e = (int)blockIdx.x % n;
+    obs_load(obs + (size_t)e * obs_stride, ov);
+    obs_store(ov, act_hi);
+  }
   for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
     const int seat = item / n, e = item - seat * n;
-    // ---- stage the observation: 14 channels (+2 zero) per interior pixel,
-    //      one (pixel, 8-channel chunk) per thread
-    const __half* orow = obs + (size_t)e * obs_stride;
-    for (int i = t; i < 2 * kCnnHW; i += blockDim.x) {
-      const int p = i >> 1, ch = i & 1;
-      const int r = kActMargin + (p / kCnnW + 1) * kCnnPW + (p % kCnnW + 1);
-      uint32_t v[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int c = ch * 8 + 2 * j;
-        const uint32_t a = c < 14 ? __half_as_ushort(orow[c * kCnnHW + p]) : 0u;
-        const uint32_t b = c + 1 < 14 ? __half_as_ushort(orow[(c + 1) * kCnnHW + p]) : 0u;
-        v[j] = a | (b << 16);
-      }
-      *reinterpret_cast<uint4*>(act_hi + r * 128 + ((ch ^ (r & 7)) << 4)) =
-          make_uint4(v[0], v[1], v[2], v[3]);
-    }
+    const int next = item + (int)gridDim.x;
     __half* ohi = out + ((size_t)seat * 2 * n + e) * kCnnKP;
     __half* olo = out + ((size_t)seat * 2 * n + n + e) * kCnnKP;
     if (t < kCnnKP - kCnnKIn) {
@@ -396,39 +459,22 @@ k_cnn_trunk(const __half* __restrict__ obs, int obs_stride, int n, int n_seats,
       olo[kCnnKIn + t] = __float2half_rn(0.f);
     }
     const uint8_t* w0 = wimg + L.c0 + (size_t)seat * kW0;
-#pragma unroll 1
-    for (int layer = 0; layer < 4 && ok; ++layer) {
-      fence_proxy_async();
-      asm volatile("tcgen05.fence::before_thread_sync;");
-      __syncthreads();
-      if (t == 0) {
-        asm volatile("tcgen05.fence::after_thread_sync;");
-        if (layer == 0)
-          conv_mma<16, 16, 9, false>(tmem, act_hi, act_lo, w0);
-        else if (layer == 1)
-          conv_mma<32, 16, 9, true>(tmem, act_hi, act_lo, wimg + L.c1);
-        else if (layer == 2)
-          conv_mma<64, 32, 9, true>(tmem, act_hi, act_lo, wimg + L.c2);
-        else
-          conv_mma<16, 64, 1, true>(tmem, act_hi, act_lo, wimg + L.c3);
-        umma_commit(dbar);
-      }
-      ok = __syncthreads_and(mbar_wait(dbar, phase & 1));
-      ++phase;
-      if (!ok) break;
-      asm volatile("tcgen05.fence::after_thread_sync;");
-      if (layer == 0)
-        conv_epilogue<16, 16, false>(tmem, lnf, LF_G0, LF_B0, cb, act_hi, act_lo, red, ohi, olo);
-      else if (layer == 1)
-        conv_epilogue<32, 32, false>(tmem, lnf, LF_G1, LF_B1, cb + (LF_CB1 - LF_CB0), act_hi, act_lo,
-                                     red, ohi, olo);
-      else if (layer == 2)
-        conv_epilogue<64, 64, false>(tmem, lnf, LF_G2, LF_B2, cb + (LF_CB2 - LF_CB0), act_hi, act_lo,
-                                     red, ohi, olo);
-      else
-        conv_epilogue<16, 8, true>(tmem, lnf, LF_G3, LF_B3, cb + (LF_CB3 - LF_CB0), act_hi, act_lo,
-                                   red, ohi, olo);
-    }
+    ok = conv_layer<16, 16, 9, false, 16, false>(tmem, act_hi, act_lo, w0, dbar, phase, lnf,
+                                                 LF_G0, LF_B0, cb, red, ohi, olo) &&
+         conv_layer<32, 16, 9, true, 32, false>(tmem, act_hi, act_lo, wimg + L.c1, dbar, phase,
+                                                lnf, LF_G1, LF_B1, cb + (LF_CB1 - LF_CB0), red,
+                                                ohi, olo) &&
+         conv_layer<64, 32, 9, true, 64, false>(tmem, act_hi, act_lo, wimg + L.c2, dbar, phase,
+                                                lnf, LF_G2, LF_B2, cb + (LF_CB2 - LF_CB0), red,
+                                                ohi, olo);
+    if (!ok) break;
+    // the next env's observation is fetched while the last layer runs and
+    // stored once the layer's MMAs have read the activation buffer
+    if (next < items) obs_load(obs + (size_t)(next % n) * obs_stride, ov);
+    ok = conv_layer<16, 64, 1, true, 8, true>(tmem, act_hi, act_lo, wimg + L.c3, dbar, phase, lnf,
+                                              LF_G3, LF_B3, cb + (LF_CB3 - LF_CB0), red, ohi,
+                                              olo);
+    if (ok && next < items) obs_store(ov, act_hi);
   }
   if (!ok && t == 0) {
     flag_error(QQT_DEV_TIMEOUT);
