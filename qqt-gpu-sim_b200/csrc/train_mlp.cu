@@ -9,8 +9,10 @@
 // themselves:
 //
 // k_gather_rows   the minibatch's rows of the rollout's fp16 observation
-//                 buffer into one contiguous block: one warp per row, 16-byte
-//                 copies, every index checked against the buffer's row count.
+//                 buffer (and of the packed per-row side data) into one
+//                 contiguous block: a warp per observation row, several small
+//                 rows per warp, 16-byte copies, every index checked against
+//                 the buffer's row count.
 // k_l1_fwd        h1 = x W0p^T + b0 (W0p = W0 with the seat's view
 //                 permutation folded into its column order, stored as fp16 hi
 //                 and lo halves by k_mlp_pack_w0): persistent CTAs over
@@ -44,22 +46,28 @@ namespace qqt {
 
 // ---------------------------------------------------------------- gather
 
+// `lanes` lanes (a power of two dividing 32) copy one row, so a warp moves
+// 32 / lanes rows of up to lanes x 16 bytes at once (small side-data rows
+// as well as 4.7 KB observation rows, which take the whole warp).
 __global__ void k_gather_rows(const uint4* __restrict__ src, int64_t src_stride16, int64_t n_src,
                               const int64_t* __restrict__ idx, int64_t n,
-                              uint4* __restrict__ dst, int64_t dst_stride16, int row16) {
-  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+                              uint4* __restrict__ dst, int64_t dst_stride16, int row16,
+                              int lanes) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int lane = lane_id();
+  const int l = lane & (lanes - 1);
+  const int64_t w = (t >> 5) * (32 / lanes) + lane / lanes;
   if (w >= n) return;
   const int64_t r = __ldg(idx + w);
   uint4* d = dst + w * dst_stride16;
   if (r < 0 || r >= n_src) {
-    if (lane == 0) flag_error(QQT_DEV_BAD_INDEX);
-    for (int c = lane; c < row16; c += 32) d[c] = make_uint4(0u, 0u, 0u, 0u);
+    if (l == 0) flag_error(QQT_DEV_BAD_INDEX);
+    for (int c = l; c < row16; c += lanes) d[c] = make_uint4(0u, 0u, 0u, 0u);
     return;
   }
   const uint4* s = src + r * src_stride16;
 #pragma unroll 4
-  for (int c = lane; c < row16; c += 32) d[c] = __ldcs(s + c);
+  for (int c = l; c < row16; c += lanes) d[c] = __ldcs(s + c);
 }
 
 // ---------------------------------------------------------------- forward
@@ -1430,10 +1438,13 @@ extern "C" int qqt_gather_rows(const void* src, int64_t n_src, int64_t src_strid
     return QQT_E_ALIGN;
   if (row_bytes > src_stride_bytes || row_bytes > dst_stride_bytes) return QQT_E_ARG;
   if (n == 0) return QQT_OK;
-  const int64_t threads = n * 32;
+  const int row16 = (int)(row_bytes / 16);
+  int lanes = 1;
+  while (lanes < 32 && lanes < row16) lanes <<= 1;
+  const int64_t threads = (n + 32 / lanes - 1) / (32 / lanes) * 32;
   k_gather_rows<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
       (const uint4*)src, src_stride_bytes / 16, n_src, idx, n, (uint4*)dst, dst_stride_bytes / 16,
-      (int)(row_bytes / 16));
+      row16, lanes);
   return launch_status();
 }
 

@@ -318,6 +318,28 @@ def _all_reduce(t, op=None):
     return 1
 
 
+SIDE_BYTES = 48   # packed per-row side data: act int64 x2 | logp, val, adv, ret f32 | mm u8 x5, bm u8 x2
+
+
+def _pack_side(mm, bm, act, logp, val, adv, ret):
+    """The per-row fields a minibatch reads besides the observation, packed
+    into one 48-byte row each (one gather per minibatch on the device)."""
+    n = act.shape[0]
+    side = torch.zeros((n, SIDE_BYTES), dtype=torch.uint8, device=act.device)
+    side.view(torch.int64)[:, 0:2] = act.to(torch.int64)
+    side.view(torch.float32)[:, 4:8] = torch.stack([logp, val, adv, ret], 1).to(torch.float32)
+    side[:, 32:37] = mm.to(torch.bool).view(torch.uint8)
+    side[:, 37:39] = bm.to(torch.bool).view(torch.uint8)
+    return side
+
+
+def _side_views(sg):
+    """(mm, bm, act, logp, val, adv, ret) views of gathered side rows."""
+    f = sg.view(torch.float32)
+    return (sg[:, 32:37].view(torch.bool), sg[:, 37:39].view(torch.bool),
+            sg.view(torch.int64)[:, 0:2], f[:, 4], f[:, 5], f[:, 6], f[:, 7])
+
+
 def ppo_update(model: MLPActorCritic, opt, data: dict, last_val, cfg: PPOConfig,
                entropy_coef: float, pid: int = 0, perm_fn=None) -> dict:
     """One PPO update over a (T, N) rollout shard (train/ppo.py:364-437).
@@ -362,12 +384,22 @@ def ppo_update(model: MLPActorCritic, opt, data: dict, last_val, cfg: PPOConfig,
     # statistics stay on the device; one host read at the end
     out = {k: torch.zeros((), device=dev) for k in ("pg", "vf", "ent", "kl", "clipfrac")}
     updates = 0
-    xg = None
+    xg = sg = None
+    side = _pack_side(mm, bm, act, old_logp, old_val, adv, ret) if obs.is_cuda else None
     params = [p for p in model.parameters()]
     for _ in range(cfg.epochs):
         perm = pool[perm_fn(pool.numel())][:total]
         for start in range(0, total, mb):
             sel = perm[start:start + mb]
+            if side is not None:
+                # one gather of the packed per-row fields instead of one index op each
+                if sg is None or sg.shape[0] < sel.numel():
+                    sg = torch.empty((sel.numel(), SIDE_BYTES), dtype=torch.uint8, device=dev)
+                s_mm, s_bm, s_act, s_lp, s_val, s_adv, s_ret = _side_views(
+                    gather_rows(side, sel, sg[:sel.numel()]))
+            else:
+                s_mm, s_bm, s_act = mm[sel], bm[sel], act[sel]
+                s_lp, s_val, s_adv, s_ret = old_logp[sel], old_val[sel], adv[sel], ret[sel]
             if obs.is_cuda:
                 # the minibatch's rows copied whole into one reused block (whole
                 # 4.7 KB rows stream at HBM speed; reading them in place with
@@ -379,12 +411,12 @@ def ppo_update(model: MLPActorCritic, opt, data: dict, last_val, cfg: PPOConfig,
                 x = gather_rows(obs, sel, xg[:sel.numel()])
             else:
                 x = obs[sel]
-            logp, ent, value = model.evaluate(x, mm[sel], bm[sel], act[sel], pid)
-            ratio = (logp - old_logp[sel]).exp()
-            a = adv[sel]
+            logp, ent, value = model.evaluate(x, s_mm, s_bm, s_act, pid)
+            ratio = (logp - s_lp).exp()
+            a = s_adv
             pg = -torch.min(ratio * a, ratio.clamp(1 - cfg.clip_eps, 1 + cfg.clip_eps) * a).mean()
-            v_clip = old_val[sel] + (value - old_val[sel]).clamp(-cfg.clip_eps, cfg.clip_eps)
-            vf = 0.5 * torch.max((value - ret[sel]) ** 2, (v_clip - ret[sel]) ** 2).mean()
+            v_clip = s_val + (value - s_val).clamp(-cfg.clip_eps, cfg.clip_eps)
+            vf = 0.5 * torch.max((value - s_ret) ** 2, (v_clip - s_ret) ** 2).mean()
             ent_m = ent.mean()
             loss = pg + cfg.value_coef * vf - entropy_coef * ent_m
             opt.zero_grad(set_to_none=True)
@@ -405,7 +437,7 @@ def ppo_update(model: MLPActorCritic, opt, data: dict, last_val, cfg: PPOConfig,
                 out["pg"] += pg.detach()
                 out["vf"] += vf.detach()
                 out["ent"] += ent_m.detach()
-                out["kl"] += (old_logp[sel] - logp).mean().detach()
+                out["kl"] += (s_lp - logp).mean().detach()
                 out["clipfrac"] += ((ratio - 1).abs() > cfg.clip_eps).float().mean()
             updates += 1
     return {k: float(v) / max(1, updates) for k, v in out.items()}

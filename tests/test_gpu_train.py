@@ -56,6 +56,19 @@ def test_gather_rows_bit_exact():
     assert _capi.device_error() == 0
 
 
+@pytest.mark.parametrize("row_bytes", [16, 48, 112, 4736])
+def test_gather_rows_small_rows_bit_exact(row_bytes):
+    """Several rows per warp for short rows (the packed per-row side data)."""
+    _need_cuda()
+    from qqt_b200 import _capi
+    src = torch.randint(0, 256, (3001, row_bytes), dtype=torch.uint8, device="cuda")
+    idx = torch.randint(0, 3001, (2049,), device="cuda")
+    out = gather_rows(src, idx)
+    torch.cuda.synchronize()
+    assert torch.equal(out, src[idx])
+    assert _capi.device_error() == 0
+
+
 def test_gather_rows_bad_index_flags_and_zero_fills():
     _need_cuda()
     from qqt_b200 import _capi
