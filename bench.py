@@ -75,15 +75,20 @@ ALG_BYTES = {
 }
 POLICY_PER_SEAT = 5 + 2 + 8 + 16 + 4 + 4
 MLP_FLOPS = 2 * (2366 * 128 + 128 * 128 + 3 * 128 * 64 + 64 * 8)
+# CNN policy per sample (train/model.py:77-101): convs 14->16, 16->32, 32->64 (3x3),
+# 64->8 (1x1) on 13x13, Linear(1352->128), the 128x128 layer, heads: 9.07 MFLOP
+CNN_FLOPS = 2 * (169 * 9 * (14 * 16 + 16 * 32 + 32 * 64) + 169 * 64 * 8 + 1352 * 128 +
+                 128 * 128 + 3 * 128 * 64 + 64 * 8)
 
 
 def _peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             m = json.load(f)
-        return float(m["hbm_gbs"]), float(m["bf16_tflops"]), "measured"
+        return (float(m["hbm_gbs"]), float(m.get("bf16_tflops_sustained", m["bf16_tflops"])),
+                "measured")
     except Exception:
-        return 6650.0, 1590.0, "fallback"
+        return 6650.0, 1400.0, "fallback"
 
 
 class ClockSampler:
@@ -484,6 +489,13 @@ def gpu_bench(args):
         dom = max((k for k in per if k != "flush"), key=lambda k: per[k]["share"])
         d = per[dom]
         achieved = d["alg_bytes_per_launch"] / (d["mean_ms"] / 1e3) / 1e9
+        # the CNN policy is a dense contraction (9.07 MFLOP per 4.7 KB row): its
+        # roofline is the tensor pipe (the sustained bf16 peak: it is timed inside
+        # the rollout graph); every other dominant kernel here is bandwidth-bound
+        tensor_bound = dom == "policy" and CFG["learner"] == "cnn"
+        if tensor_bound:
+            d["alg_flops_per_launch"] = CNN_FLOPS * n_inst * n_seats
+            achieved = d["alg_flops_per_launch"] / (d["mean_ms"] / 1e3) / 1e12
         # ncu traffic was captured for the default cfg2 shard (2 groups of 2816 envs)
         traffic = _ncu_traffic(dom) if args.config == "cfg2" and n_inst == 2816 else None
         cores = args.cpu_procs
@@ -504,8 +516,11 @@ def gpu_bench(args):
             "e2e": {"value": round(e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": _launches_per_rollout() * groups * args.steps,
-            "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1),
-                         "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+            "roofline": {"kernel": dom, "bound": "tensor" if tensor_bound else "hbm",
+                         "achieved": round(achieved, 1),
+                         "peak": tflops if tensor_bound else hbm,
+                         "unit": "TFLOP/s" if tensor_bound else "GB/s",
+                         "frac": round(achieved / (tflops if tensor_bound else hbm), 4),
                          "peak_source": src, "traffic": traffic,
                          "per_kernel": per},
             "cpu_baseline": {"value": round(cpu_v, 1), "unit": UNIT, "cores": cores,
