@@ -887,11 +887,24 @@ __global__ void k_local_view(QqtCfg cfg, QqtState st, const T* __restrict__ obs,
   const int cy = (int)floorf(py), cx = (int)floorf(px);
   const T* orow = obs + (size_t)e * cfg.obs_stride;
   T* lo = local + ((size_t)e * po + m) * CH * 49;
-  for (int i = lane; i < CH * 49; i += 32) {
-    const int ch = i / 49, k = i - ch * 49, dy = k / 7, dx = k - dy * 7;
-    const int ys = min(max(cy + dy, 0), H + 5) - 3, xs = min(max(cx + dx, 0), W + 5) - 3;
-    lo[i] = (ys >= 0 && ys < H && xs >= 0 && xs < W) ? orow[(size_t)ch * C + ys * W + xs]
-                                                     : to_obs<T>(0.f);
+  const int total = CH * 49;
+  for (int base = 0; base < total; base += 8 * 32) {
+    T vals[8];                            // eight independent loads in flight per lane
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = base + u * 32 + lane;
+      vals[u] = to_obs<T>(0.f);
+      if (i < total) {
+        const int ch = i / 49, k = i - ch * 49, dy = k / 7, dx = k - dy * 7;
+        const int ys = min(max(cy + dy, 0), H + 5) - 3, xs = min(max(cx + dx, 0), W + 5) - 3;
+        if (ys >= 0 && ys < H && xs >= 0 && xs < W) vals[u] = orow[(size_t)ch * C + ys * W + xs];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = base + u * 32 + lane;
+      if (i < total) lo[i] = vals[u];
+    }
   }
   T* re = rel + ((size_t)e * po + m) * 60;
   for (int i = lane; i < 60; i += 32) re[i] = to_obs<T>(0.f);
@@ -903,26 +916,35 @@ __global__ void k_local_view(QqtCfg cfg, QqtState st, const T* __restrict__ obs,
     re[lane * 6 + 1] = to_obs<T>(__fsub_rn(st.pos[(size_t)(2 * opp + 1) * N + e], px));
     re[lane * 6 + 2] = to_obs<T>(st.alive[(size_t)opp * N + e] ? 1.f : 0.f);
   }
-  // nearest cells: each lane owns cells lane, lane + 32, ... (at most 14)
+  // nearest cells: each lane owns cells lane, lane + 32, ... (at most 14),
+  // their distance keys held in registers (a non-bomb cell counts 1e6; a cell
+  // past the grid or already taken counts 2^32 - 1)
+  constexpr int kOwn = (QQT_MAX_CELLS + 31) / 32;
   const int16_t* frow = st.fuse + (size_t)e * C;
   int nb = 0, fsum = 0;
-  for (int c = lane; c < C; c += 32) {
-    const int f = frow[c];
-    nb += f > 0;
-    fsum += f;
+  unsigned dk[kOwn];
+#pragma unroll
+  for (int j = 0; j < kOwn; ++j) {
+    const int c = lane + 32 * j;
+    unsigned d = 0xffffffffu;
+    if (c < C) {
+      const int f = frow[c];
+      nb += f > 0;
+      fsum += f;
+      const int r = c / W, q = c - r * W;
+      d = f > 0 ? (unsigned)(abs(r - cy) + abs(q - cx)) : 1000000u;
+    }
+    dk[j] = d;
   }
   nb = __reduce_add_sync(QQT_FULL, nb);
   fsum = __reduce_add_sync(QQT_FULL, fsum);
   const int k = min(10 - n_opp, C);
-  uint32_t taken = 0;
   for (int j = 0; j < k; ++j) {
     unsigned long long best = ~0ull;
-    int slot = 0;
-    for (int c = lane; c < C; c += 32, ++slot) {
-      if (taken >> slot & 1u) continue;
-      const int r = c / W, q = c - r * W;
-      const unsigned d = frow[c] > 0 ? (unsigned)(abs(r - cy) + abs(q - cx)) : 1000000u;
-      const unsigned long long key = ((unsigned long long)d << 32) | (unsigned)c;
+#pragma unroll
+    for (int jj = 0; jj < kOwn; ++jj) {
+      const unsigned long long key =
+          ((unsigned long long)dk[jj] << 32) | (unsigned)(lane + 32 * jj);
       best = key < best ? key : best;
     }
 #pragma unroll
@@ -931,7 +953,9 @@ __global__ void k_local_view(QqtCfg cfg, QqtState st, const T* __restrict__ obs,
       best = other < best ? other : best;
     }
     const int c = (int)(best & 0xffffffffull);
-    if (lane == (c & 31)) taken |= 1u << (c >> 5);
+#pragma unroll
+    for (int jj = 0; jj < kOwn; ++jj)
+      if (lane == (c & 31) && jj == (c >> 5)) dk[jj] = 0xffffffffu;
     if (lane == 0) {
       const int r = c / W, q = c - r * W;
       T* sl = re + (n_opp + j) * 6;
