@@ -140,3 +140,24 @@ def test_ppo_update_gpu_tracks_reference():
         ref = g["param__" + k]
         err = np.abs(v.cpu().numpy() - ref).max()
         assert err <= 1e-4 * max(1.0, np.abs(ref).max()), f"{k}: {err}"
+
+
+def test_packed_side_rows_round_trip():
+    """The per-row fields a minibatch reads (actions, old log-prob and value,
+    advantage, return, legal masks) packed into one 48-byte row each: the
+    views of gathered rows equal the fields indexed one by one."""
+    from qqt_b200.ppo import SIDE_BYTES, _pack_side, _side_views
+    g = torch.Generator().manual_seed(3)
+    n = 257
+    mm = torch.rand((n, 5), generator=g) < 0.6
+    bm = torch.rand((n, 2), generator=g) < 0.6
+    act = torch.randint(0, 5, (n, 2), generator=g)
+    f = [torch.randn(n, generator=g) for _ in range(4)]
+    side = _pack_side(mm, bm, act, *f)
+    assert side.shape == (n, SIDE_BYTES) and side.dtype == torch.uint8
+    sel = torch.randint(0, n, (100,), generator=g)
+    s_mm, s_bm, s_act, s_lp, s_val, s_adv, s_ret = _side_views(side[sel])
+    assert torch.equal(s_mm, mm[sel]) and torch.equal(s_bm, bm[sel])
+    assert torch.equal(s_act, act[sel])
+    for got, want in zip((s_lp, s_val, s_adv, s_ret), f):
+        assert torch.equal(got, want[sel])
