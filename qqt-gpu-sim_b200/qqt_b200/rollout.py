@@ -113,7 +113,13 @@ class Rollout:
         self.probe = None
 
     def _run(self, name, fn):
-        return fn() if self.probe is None else self.probe(name, fn)
+        # an NVTX range per engine call (visible to Nsight Systems in eager
+        # ticks and at graph capture; a no-op without a profiler attached)
+        torch.cuda.nvtx.range_push("qqt:" + name)
+        try:
+            return fn() if self.probe is None else self.probe(name, fn)
+        finally:
+            torch.cuda.nvtx.range_pop()
 
     def tick(self, t: int) -> None:
         sim, buf, dr = self.sim, self.buf, self.draws
