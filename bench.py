@@ -312,11 +312,13 @@ def _launches_per_rollout():
     """Kernels per rollout of one env group: per tick policy (fused MLP: 1;
     CNN: trunk + linear/tail per seat), bot (astar: cap + field; greedy: 1)
     and the step (which also writes the next observation); a separate observe
-    on the first tick and after each crate recycling; the recycling itself."""
+    on the first tick; the crate recycling every 16 ticks (which rewrites the
+    crate channel of the step's next-tick rows with one torch copy, not
+    counted here)."""
     pol = 1 if CFG["learner"] == "mlp" else 1 + len(CFG["seats"])
     bot = {"astar": 2, "greedy": 1, None: 0}[CFG["opponent"]]
     flushes = TICKS // 16
-    return TICKS * (pol + bot + 1) + 1 + (flushes - 1 if TICKS % 16 == 0 else flushes) + flushes
+    return TICKS * (pol + bot + 1) + 1 + flushes
 
 
 def ppo_leg(grp, device):

@@ -150,7 +150,9 @@ class Rollout:
             main.wait_stream(self.side)
         flush = bool(self.flush_every) and t % self.flush_every == self.flush_every - 1
         nxt = None
-        if self.fuse_observe and not flush and t + 1 < self.T:
+        if self.fuse_observe and t + 1 < self.T:
+            # after a crate recycle only the crate channel of the next rows
+            # changes; flush_recycle rewrites it (no stand-alone observe)
             b1 = (t + 1) % self.slots
             nxt = (buf.obs_rows[b1], buf.mm[b1], buf.bm[b1])
         self._run("step+observe" if nxt is not None else "step", lambda: sim.step(
@@ -159,7 +161,8 @@ class Rollout:
             info_planes=False, next_obs=nxt))
         self._ready = t + 1 if nxt is not None else -1
         if flush:
-            self._run("flush", sim.flush_recycle)
+            self._run("flush", lambda: sim.flush_recycle(
+                obs_rows=nxt[0] if nxt is not None else None))
 
     def feed_opponent(self, t: int) -> None:
         """Hand the opponent bot its draws for tick t (noise; the astar mode

@@ -603,14 +603,18 @@ class B200Sim:
         return reward, done, info
 
     # ------------------------------------------------------------ recycle
-    def flush_recycle(self, on_device: bool | None = None) -> None:
+    def flush_recycle(self, on_device: bool | None = None, obs_rows: torch.Tensor | None = None):
         """Drop one crate per lost attribute layer on random free cells
         (sim/torch_sim.py:549-596).
 
         on_device=False (default without a template): host generator draws in
         the reference's order, bit-compatible with the reference; True
         (default with a template): one kernel, counter-based draws, no host
-        round trip."""
+        round trip.  obs_rows: observation rows (N, obs_stride) of the current
+        state (e.g. written by the step's fused observe); their crate channel
+        is rewritten from the crate plane, the one channel a recycle changes
+        (crates block neither movement nor flames), so they equal a fresh
+        observe() afterwards."""
         if on_device is None:
             on_device = self._tmpl is not None
         if on_device:
@@ -620,7 +624,19 @@ class B200Sim:
                                               words, int(self._flush_seed), self._flush_count,
                                               self._stream())
             capi.check(rc, "qqt_flush_recycle")
-            return
+        else:
+            self._flush_host()
+        if obs_rows is not None:
+            self._rewrite_crate_channel(obs_rows)
+
+    def _rewrite_crate_channel(self, rows: torch.Tensor) -> None:
+        cfg = self.cfg
+        ch, hw = 2 * cfg.n_players + 3, cfg.n_cells
+        if cfg.n_channels <= ch:
+            return                       # no crate channel in this layout
+        rows[:, ch * hw:(ch + 1) * hw].copy_(self._buf["crate"].reshape(self.num_envs, hw))
+
+    def _flush_host(self) -> None:
         cfg = self.cfg
         lost = self._buf["_pending_lost"]
         if not bool((lost.sum() > 0).item()):

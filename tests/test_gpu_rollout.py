@@ -224,3 +224,33 @@ def test_step_observe_equals_step_then_observe():
         assert np.array_equal(fused_state[k], got[k]), f"state {k}"
     assert torch.equal(rows.view(torch.int16), ref_rows.view(torch.int16)), "observation rows"
     assert torch.equal(mm, ref_mm) and torch.equal(bm, ref_bm), "legal masks"
+
+
+@pytest.mark.parametrize("on_device", [True, False])
+def test_flush_rewrites_the_crate_channel_of_fused_rows(on_device):
+    """A crate recycle changes only the observation's crate channel: the
+    step's fused next-tick rows, after flush_recycle(obs_rows=...) rewrites
+    that channel, equal a fresh observe of the post-recycle state (device
+    and host recycle paths)."""
+    n = 96
+    cfg, sim, pol, bot, ro = _make(n, 40, seed=13)
+    for t in range(20):
+        ro.tick(t)
+    rng = np.random.default_rng(8)
+    lost = rng.integers(0, 4, (n, 2)).astype(np.int64)
+    sim.load_numpy_state({"pending_lost": lost})
+    rows = torch.zeros_like(ro.buf.obs_rows[0])
+    mm = torch.zeros_like(ro.buf.mm[0])
+    bm = torch.zeros_like(ro.buf.bm[0])
+    sim.step(ro.buf.act[19].clone(), auto_reset=True,
+             crate_draws=(ro.draws.crate[19, 0], ro.draws.crate[19, 1]), next_obs=(rows, mm, bm))
+    before = sim.numpy_state()["crate"].copy()
+    sim.flush_recycle(on_device=on_device, obs_rows=rows)
+    ref_rows = torch.zeros_like(rows)
+    ref_mm, ref_bm = torch.zeros_like(mm), torch.zeros_like(bm)
+    sim.observe_and_mask(ref_rows, ref_mm, ref_bm, danger=False)
+    torch.cuda.synchronize()
+    after = sim.numpy_state()["crate"]
+    assert (after.astype(int) - before.astype(int)).sum() > 0, "the recycle dropped crates"
+    assert torch.equal(rows.view(torch.int16), ref_rows.view(torch.int16))
+    assert torch.equal(mm, ref_mm) and torch.equal(bm, ref_bm)
