@@ -564,6 +564,7 @@ static WgradWork wgrad_work_layout(int64_t n_rows, int kp) {
 // sums are combined in a fixed order by k_tail_reduce.
 
 constexpr uint32_t kTbScr = 384;                   // TMEM row-exchange scratch columns
+constexpr uint32_t kTbAcc = 432;                   // heads kernel: per-thread sums (4 x 9)
 constexpr int kActB = kBM * 128 * 2;               // one fp16 [128 x 128] operand image
 constexpr int kThWh = 0;                           // heads kernel: Wh0 image hi, lo
 constexpr int kThR = 2 * (int)kImgH0Bytes;         //   r2 operand hi, lo
@@ -595,6 +596,13 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// TMEM column += v (this thread's lane).
+__device__ __forceinline__ void tmem_acc(uint32_t col, float v) {
+  float o[4];
+  tmem_ld4(col, o);
+  tmem_st1(col, o[0] + v);
 }
 
 // Sum of a[32] over the warp's 32 lanes, element `lane` kept by each lane
@@ -903,9 +911,14 @@ k_tail_heads_bwd(TailArgs a, const float* __restrict__ f, const uint8_t* __restr
   const uint32_t lane_base = tmem + ((uint32_t)(qd * 32) << 16);
   const uint32_t scr = lane_base + kTbScr;
   const float dscale = pow2f(*du_exp), undo = pow2f(-*du_exp);
-  float acc[kThAcc];
-#pragma unroll
-  for (int i = 0; i < kThAcc; ++i) acc[i] = 0.f;
+  // the thread's small-gradient sums live in TMEM columns of its row's lane
+  // (columns kTbAcc + 9q ..), not in registers
+  const uint32_t acol = lane_base + kTbAcc + (uint32_t)(kThAcc * q);
+  {
+    const float z8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    tmem_st8(acol, z8);
+    tmem_st1(acol + 8, 0.f);
+  }
   bool ok = epi_and(wload);
   for (int tile = blockIdx.x, lt = 0; tile < n_tiles && ok; tile += gridDim.x, ++lt) {
     const uint32_t par = (uint32_t)(lt & 1);
@@ -1010,22 +1023,22 @@ k_tail_heads_bwd(TailArgs a, const float* __restrict__ f, const uint8_t* __restr
       if (k == 0) {
 #pragma unroll
         for (int i = 0; i < 16; ++i) { v[i] = h[i] * dz[0]; v[16 + i] = h[i] * dz[1]; }
-        acc[0] += reduce_scatter32(v);
+        tmem_acc(acol + 0, reduce_scatter32(v));
 #pragma unroll
         for (int i = 0; i < 16; ++i) { v[i] = h[i] * dz[2]; v[16 + i] = h[i] * dz[3]; }
-        acc[1] += reduce_scatter32(v);
+        tmem_acc(acol + 1, reduce_scatter32(v));
 #pragma unroll
         for (int i = 0; i < 16; ++i) { v[i] = h[i] * dz[4]; v[16 + i] = du[i]; }
-        acc[2] += reduce_scatter32(v);
+        tmem_acc(acol + 2, reduce_scatter32(v));
       } else {
 #pragma unroll
         for (int i = 0; i < 16; ++i) { v[i] = h[i] * dz[5]; v[16 + i] = h[i] * dz[6]; }
-        acc[3] += reduce_scatter32(v);
+        tmem_acc(acol + 3, reduce_scatter32(v));
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = du[i];
 #pragma unroll
         for (int i = 0; i < 8; ++i) { v[16 + i] = q == 0 ? dz[i] : 0.f; v[24 + i] = 0.f; }
-        acc[4] += reduce_scatter32(v);
+        tmem_acc(acol + 4, reduce_scatter32(v));
       }
       store_split_scaled<16>(du, dscale, d_hi, d_lo, r, 64 * k + 16 * q);
     }
@@ -1084,7 +1097,7 @@ k_tail_heads_bwd(TailArgs a, const float* __restrict__ f, const uint8_t* __restr
       }
 #pragma unroll
       for (int i = 0; i < 16; ++i) { v[i] = h[i] * dz[7]; v[16 + i] = du[i]; }
-      acc[5] += reduce_scatter32(v);
+      tmem_acc(acol + 5, reduce_scatter32(v));
       store_split_scaled<16>(du, dscale, d_hi, d_lo, r, 16 * q);
     }
     fence_proxy_async();
@@ -1127,9 +1140,11 @@ k_tail_heads_bwd(TailArgs a, const float* __restrict__ f, const uint8_t* __restr
     float dr[32];
     tmem_ld32(lane_base + c_u + 32 * q, dr);
     load_quarter(a.h, row, n_rows, q, x);
-    float s1 = 0.f, s2 = 0.f;
-    ln_relu_backward(x, dr, mean, rstd, undo, f + F_LN2G + 32 * q, f + F_LN2B + 32 * q, acc[6],
-                     acc[7], s1, s2);
+    float s1 = 0.f, s2 = 0.f, ag = 0.f, ab = 0.f;
+    ln_relu_backward(x, dr, mean, rstd, undo, f + F_LN2G + 32 * q, f + F_LN2B + 32 * q, ag, ab,
+                     s1, s2);
+    tmem_acc(acol + 6, ag);
+    tmem_acc(acol + 7, ab);
     tmem_st2(scr + 8 + 2 * q, s1, s2);
     asm volatile("tcgen05.fence::before_thread_sync;");
     epi_sync();
@@ -1146,13 +1161,20 @@ k_tail_heads_bwd(TailArgs a, const float* __restrict__ f, const uint8_t* __restr
       for (int i = 0; i < 8; ++i)
         out[i] = make_float4(dr[4 * i], dr[4 * i + 1], dr[4 * i + 2], dr[4 * i + 3]);
     }
-    acc[8] += reduce_scatter32(dr);
+    tmem_acc(acol + 8, reduce_scatter32(dr));
   }
   if (!ok) *abort_flag = 1;
   // per-thread sums, then the dWh0^T accumulator (lane = input, column = unit)
   float* ap = a.apart + (((size_t)blockIdx.x * kEpiWarps + warp) * 32 + lane) * kThAcc;
+  {
+    float accv[kThAcc];
+    tmem_ld8(acol, accv);
+    float a8[4];
+    tmem_ld4(acol + 8, a8);
+    accv[8] = a8[0];
 #pragma unroll
-  for (int i = 0; i < kThAcc; ++i) ap[i] = acc[i];
+    for (int i = 0; i < kThAcc; ++i) ap[i] = accv[i];
+  }
   if (ok && blockIdx.x < n_tiles) {
 #pragma unroll 1
     for (int c = 0; c < 3; ++c) {
