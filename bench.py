@@ -300,7 +300,7 @@ def graph_kernel_times(grp):
             ro.probe = None
     grp.replay()
     torch.cuda.synchronize()
-    grp.graph = None
+    grp.graph, grp.graphs = None, []
     times = {}
     for name, a, b in marks:
         times.setdefault(name, []).append(a.elapsed_time(b))
@@ -433,32 +433,52 @@ def gpu_bench(args):
     ms = float(t_max.item())
     value = N_ENVS * TICKS * world * args.steps / (ms / 1e3)
 
-    # ---- e2e: public API with host-fed draws and a host read of the rewards
-    dev_draws = [t for ro in grp.ros for t in ro.draws.tensors()]
-    host_draws = [t.detach().cpu().pin_memory() for t in dev_draws]
+    # ---- e2e: public API with host-fed draws and a host read of the rewards.
+    # Two graphs read two draw-buffer sets: step i+1's draws are copied from
+    # pinned host memory into one set (copy stream) while step i's graph runs
+    # on the other, as a training loop streams its next rollout's draws.  One
+    # timed region spans every step: the first copy, all replays, all copies,
+    # every reward read and the L2 flushes.
+    grp.capture(double_buffer=True)
+    sets = [[t for d in ds for t in d.tensors()] for ds in grp.draw_sets]
+    host_draws = [t.detach().cpu().pin_memory() for t in sets[0]]
     h2d = sum(t.numel() * t.element_size() for t in host_draws)
     rew_host = [torch.empty((ro.buf.rew.shape[0], ro.sim.num_envs), dtype=torch.float32).pin_memory()
                 for ro in grp.ros]
     d2h = sum(r.numel() * 4 for r in rew_host)
-    e_evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-             for _ in range(args.steps)]
+    main = torch.cuda.current_stream(device)
+    cs = torch.cuda.Stream(device)
+    used = [torch.cuda.Event(), torch.cuda.Event()]       # replay on set k done
+    landed = [torch.cuda.Event(), torch.cuda.Event()]     # copy into set k done
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for dst, src in zip(sets[0], host_draws):
+        dst.copy_(src, non_blocking=True)
     for i in range(args.steps):
-        a, b = e_evs[i]
-        a.record()
-        for dst, src in zip(dev_draws, host_draws):
-            dst.copy_(src, non_blocking=True)
-        grp.replay()
+        k = i % 2
+        if i + 1 < args.steps:
+            with torch.cuda.stream(cs):
+                if i >= 1:
+                    cs.wait_event(used[1 - k])
+                for dst, src in zip(sets[1 - k], host_draws):
+                    dst.copy_(src, non_blocking=True)
+                landed[1 - k].record(cs)
+        if i >= 1:
+            main.wait_event(landed[k])
+        grp.replay(k)
+        used[k].record(main)
         for ro, rh in zip(grp.ros, rew_host):
             rh.copy_(ro.buf.rew[:, :, 0], non_blocking=True)
-        b.record()
-        b.synchronize()
         l2.zero_()
-    e_ms = sum(a.elapsed_time(b) for a, b in e_evs)
+    b.record()
+    b.synchronize()
+    e_ms = a.elapsed_time(b)
     t_e = torch.tensor([e_ms], device=device)
     if dist:
         dist.all_reduce(t_e, op=dist.ReduceOp.MAX)
     e_value = N_ENVS * TICKS * world * args.steps / (float(t_e.item()) / 1e3)
-    grp.graph = None
+    grp.graph, grp.graphs = None, []
     torch.cuda.synchronize()
     # per-kernel durations for the roofline: the same rollout graph with
     # timing events around each call (after the timed regions)

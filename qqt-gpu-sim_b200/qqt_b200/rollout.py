@@ -245,10 +245,7 @@ class RolloutGroups:
             main.wait_stream(s)
         return [r.buf for r in self.ros]
 
-    def capture(self) -> None:
-        for ro in self.ros:
-            if isinstance(ro.opponent, AstarBot) and ro.opponent.mode is None:
-                raise RuntimeError("run one eager tick before capture (ticker init)")
+    def _capture_one(self):
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         g = torch.cuda.CUDAGraph()
@@ -260,10 +257,39 @@ class RolloutGroups:
         for r, c in zip(self.ros, calls0):
             if isinstance(r.opponent, AstarBot):
                 r.opponent.calls = c
-        self.graph = g
+        return g
 
-    def replay(self):
-        self.graph.replay()
+    def capture(self, double_buffer: bool = False) -> None:
+        """Capture the T-tick rollout of every group as one CUDA graph.
+
+        double_buffer: also capture a second graph that reads a second set of
+        draw buffers (`draw_sets[1]`), so a caller can copy the next
+        rollout's host-fed draws into one set while the graph of the other
+        runs (`replay(which)`)."""
+        for ro in self.ros:
+            if isinstance(ro.opponent, AstarBot) and ro.opponent.mode is None:
+                raise RuntimeError("run one eager tick before capture (ticker init)")
+        first = [ro.draws for ro in self.ros]
+        self.graphs = [self._capture_one()]
+        self.draw_sets = [first]
+        if double_buffer:
+            second = []
+            for ro in self.ros:
+                d = ro.draws
+                ro.draws = RolloutDraws(*(torch.empty_like(t) for t in d.tensors()))
+                for a, b in zip(ro.draws.tensors(), d.tensors()):
+                    a.copy_(b)
+                second.append(ro.draws)
+            self.graphs.append(self._capture_one())
+            self.draw_sets.append(second)
+            for ro, d in zip(self.ros, first):
+                ro.draws = d
+        self.graph = self.graphs[0]
+
+    def replay(self, which: int = 0):
+        """Replay the captured rollout; `which` picks the draw-buffer set
+        (double-buffered capture)."""
+        self.graphs[which].replay()
         for r in self.ros:
             if isinstance(r.opponent, AstarBot):
                 r.opponent.calls += r.T

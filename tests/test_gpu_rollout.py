@@ -254,3 +254,41 @@ def test_flush_rewrites_the_crate_channel_of_fused_rows(on_device):
     assert (after.astype(int) - before.astype(int)).sum() > 0, "the recycle dropped crates"
     assert torch.equal(rows.view(torch.int16), ref_rows.view(torch.int16))
     assert torch.equal(mm, ref_mm) and torch.equal(bm, ref_bm)
+
+
+def test_double_buffered_graphs_read_their_own_draws():
+    """capture(double_buffer=True): the second graph reads the second set of
+    draw buffers; with the same draws in both sets the two graphs produce
+    the same rollout, and new draws in the second set change only what the
+    second graph produces."""
+    n, T = 128, 32
+    made = [_make(n, T, seed=41 + g) for g in range(2)]
+    made[1] = _make(n, T, seed=42, pol=made[0][2])
+    for m in made:
+        m[4].tick(0)
+    snaps = [_snapshot(m[1], m[3]) for m in made]
+    grp = RolloutGroups([m[4] for m in made])
+    grp.capture(double_buffer=True)
+    assert len(grp.graphs) == 2 and len(grp.draw_sets) == 2
+
+    def run(which):
+        for m, s in zip(made, snaps):
+            _restore(m[1], m[3], s)
+        grp.replay(which)
+        torch.cuda.synchronize()
+        return [_buffers(m[4]) for m in made]
+
+    a = run(0)
+    b = run(1)
+    for g in range(2):
+        for k in a[g]:
+            assert torch.equal(a[g][k], b[g][k]), f"group {g}: {k}"
+    gen = torch.Generator(device="cuda").manual_seed(99)
+    for d in grp.draw_sets[1]:
+        d.generate(gen)
+    c = run(1)
+    assert any(not torch.equal(a[g]["act"], c[g]["act"]) for g in range(2))
+    again = run(0)
+    for g in range(2):
+        for k in a[g]:
+            assert torch.equal(a[g][k], again[g][k]), f"group {g}: {k} (set 0 untouched)"
