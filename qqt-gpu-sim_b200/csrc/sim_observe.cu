@@ -73,13 +73,14 @@ struct FuseTables {
 // channel (consecutive lanes, consecutive elements); the row goes straight to
 // global memory, or, given a 16-byte aligned per-warp `stage` of obs_stride
 // elements, into shared memory first and out as 16-byte stores.
-template <class T, bool STAGED = false, int NP = 0>
+template <class T, bool STAGED = false, int NP = 0, int G = 0>
 __device__ inline void observe_env(const QqtCfg& cfg, const Env& v, int e, PInfo* pi,
                                    const float* dng, int live_p, float py, float px,
                                    bool alive_p, int64_t inv_p, int64_t bcap_p, int64_t t_e,
                                    const FuseTables& ft, void* obs, float* danger_out,
                                    uint8_t* mm, uint8_t* bm, T* stage = nullptr) {
-  const int h = cfg.height, w = cfg.width, C = h * w, P = NP > 0 ? NP : cfg.n_players;
+  const int h = G > 0 ? G : cfg.height, w = G > 0 ? G : cfg.width, C = h * w;
+  const int P = NP > 0 ? NP : cfg.n_players;
   const int lane = lane_id();
   const int nch = cfg.obs_channels;
   if (STAGED) __syncwarp();   // the staging area reuses scratch read just before
@@ -498,15 +499,16 @@ __device__ __forceinline__ int argmin5(const float* s) {
 // EAT: the hunter bot (sim/bots.py:557-561): astar with the crate layer
 // (sim/bots.py:376-431) and no mode ticker.
 // NP > 0: the player count fixed at compile time; 0: cfg.n_players.
-template <bool EAT, int NP = 0>
+// GS > 0: a GS x GS grid fixed at compile time; 0: the config's grid.
+template <bool EAT, int NP = 0, int GS = 0>
 __global__ void __launch_bounds__(QQT_NWARP * 32, 3)
 k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const float* noise,
         int64_t* mode_arr, int64_t* timer_arr, int tick16, const int64_t* new_mode,
         const int64_t* new_timer, float* vsafe_out, float* vopp_out, float* vcrate_out,
         const int* cap_max_ptr) {
   extern __shared__ __align__(16) uint8_t smem[];
-  const int h = cfg.height, w = cfg.width, C = h * w, N = cfg.n_envs;
-  const int P = NP > 0 ? NP : cfg.n_players;
+  const int h = GS > 0 ? GS : cfg.height, w = GS > 0 ? GS : cfg.width, C = h * w;
+  const int N = cfg.n_envs, P = NP > 0 ? NP : cfg.n_players;
   const int e0 = blockIdx.x * QQT_TILE_E;
   const float INF = __int_as_float(0x7f800000);
   static_assert(QQT_TILE_E == QQT_NWARP, "one env per warp");
@@ -1064,7 +1066,8 @@ static int launch_astar(const QqtCfg* cfg, const QqtState* st, const void* obs,
   cudaMemsetAsync(capmax, 0, sizeof(int), s);
   k_cap_max<<<min((N + 255) / 256, 148), 256, 0, s>>>(st->blast_cap + (size_t)pid * N, N, capmax);
   const size_t sm = tile_bytes(C) + QQT_NWARP * astar_warp_bytes(C);
-  auto kern = cfg->n_players == 2 ? k_astar<EAT, 2> : k_astar<EAT>;
+  const bool two = cfg->n_players == 2, g13 = cfg->height == 13 && cfg->width == 13;
+  auto kern = two ? (g13 ? k_astar<EAT, 2, 13> : k_astar<EAT, 2>) : k_astar<EAT>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   kern<<<(N + QQT_TILE_E - 1) / QQT_TILE_E, QQT_NWARP * 32, sm, s>>>(
       *cfg, *st, (const __half*)obs, io, pid, noise, mode, timer, tick16, new_mode, new_timer,

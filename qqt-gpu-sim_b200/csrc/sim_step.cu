@@ -179,8 +179,9 @@ __device__ __forceinline__ bool placed_map_at(const PShared* ps, int P, int cell
 // configured) are compile-time so that each instance carries only its own
 // code and registers.
 // NP > 0: the player count fixed at compile time (loops over players unroll
-// exactly); 0: cfg.n_players at run time.
-template <int PHASE, bool OBS, bool HZ, int NP = 0>
+// exactly); 0: cfg.n_players at run time.  G > 0: a G x G grid fixed at
+// compile time (cell / row arithmetic by constants); 0: the config's grid.
+template <int PHASE, bool OBS, bool HZ, int NP = 0, int G = 0>
 __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ FuseTables ft;
@@ -189,7 +190,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
   __shared__ unsigned dirty;
   const QqtCfg& cfg = a.cfg;
   const QqtState& st = a.st;
-  const int h = cfg.height, w = cfg.width, C = h * w, N = cfg.n_envs;
+  const int h = G > 0 ? G : cfg.height, w = G > 0 ? G : cfg.width, C = h * w, N = cfg.n_envs;
   const int P = NP > 0 ? NP : cfg.n_players;
   const int e0 = blockIdx.x * QQT_TILE_E;
   const int lane = lane_id();
@@ -746,7 +747,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
 #pragma unroll
       for (int q = 0; q < QQT_MAX_P; ++q)
         if (lane == q && !reset) my_live = post_live[q];
-      observe_env<__half, true, NP>(cfg, v, e, pinfo, dng, my_live, me.y, me.x, alive != 0, me.invuln,
+      observe_env<__half, true, NP, G>(cfg, v, e, pinfo, dng, my_live, me.y, me.x, alive != 0, me.invuln,
                           me.bombs_cap, t_out, ft, a.obs, nullptr, a.mm, a.bm,
                           (__half*)(wb + L.row));
     }
@@ -922,6 +923,9 @@ static int launch_step(const QqtCfg* cfg, const QqtState* st, const int64_t* act
   };
   const bool fused = obs != nullptr;
   const bool hz = cfg->hazard_on != 0;
+  // the steady-state two-player tick on the 13 x 13 board of the
+  // benchmark configs has its own instance
+  const bool two = cfg->n_players == 2, g13 = cfg->height == 13 && cfg->width == 13;
   if (first_step) {
     cudaMemsetAsync(tiers, 0xff, sizeof(int32_t), s);   // -1
     launch(k_step<PHASE_PLACE, false, false>, PHASE_PLACE);
@@ -934,11 +938,13 @@ static int launch_step(const QqtCfg* cfg, const QqtState* st, const int64_t* act
     }
   } else if (fused) {
     if (hz) launch(k_step<PHASE_FULL, true, true>, PHASE_FULL);
-    else if (cfg->n_players == 2) launch(k_step<PHASE_FULL, true, false, 2>, PHASE_FULL);
+    else if (two && g13) launch(k_step<PHASE_FULL, true, false, 2, 13>, PHASE_FULL);
+    else if (two) launch(k_step<PHASE_FULL, true, false, 2>, PHASE_FULL);
     else launch(k_step<PHASE_FULL, true, false>, PHASE_FULL);
   } else {
     if (hz) launch(k_step<PHASE_FULL, false, true>, PHASE_FULL);
-    else if (cfg->n_players == 2) launch(k_step<PHASE_FULL, false, false, 2>, PHASE_FULL);
+    else if (two && g13) launch(k_step<PHASE_FULL, false, false, 2, 13>, PHASE_FULL);
+    else if (two) launch(k_step<PHASE_FULL, false, false, 2>, PHASE_FULL);
     else launch(k_step<PHASE_FULL, false, false>, PHASE_FULL);
   }
   return launch_status();
