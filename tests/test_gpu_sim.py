@@ -227,7 +227,9 @@ def test_step_instances_vs_oracle(shape):
     runtime-shape kernel.  Each against the oracle tick by tick over 50
     ticks (random moves and bombs; the 30-tick fuses go off), with and without
     the fused next-tick observation, which must equal a stand-alone
-    observe of the same state."""
+    observe of the same state.  The astar bot is compiled the same way:
+    every 5th tick each player's astar action (no mode ticker) against the
+    oracle's on the same state and noise."""
     from oracle import qqt_oracle as O
     h, w, p = shape
     cfg = SimConfig(height=h, width=w, n_players=p, map_mode="open", speed=3.0)
@@ -244,6 +246,17 @@ def test_step_instances_vs_oracle(shape):
     zeros = np.zeros((n, p), np.float32)
     exploded = 0
     for t in range(50):
+        if t % 5 == 0:
+            obs, omm, obm = plain.observe_and_mask()
+            d16 = O.observe(cfg, st)[0].astype(np.float16).astype(np.float32)[:, 2 * p + 1]
+            o_mm, o_bm = O.legal_mask(cfg, st)
+            for pid in range(p):
+                noise = rng.random((n, 5), dtype=np.float32)
+                bot = AstarBot(plain, mode=False)
+                bot.feed(noise=torch.from_numpy(noise).cuda())
+                a_gpu = _np(bot.act(obs, omm[:, pid], obm[:, pid], pid))
+                a_ref = O.astar_attack(cfg, st, d16, o_mm[:, pid], o_bm[:, pid], pid, noise)
+                assert np.array_equal(a_gpu, a_ref), f"t={t}: astar actions of player {pid}"
         acts = np.zeros((n, p, 2), np.int64)
         acts[..., 0] = rng.integers(0, 5, (n, p))
         acts[..., 1] = rng.random((n, p)) < 0.3
