@@ -421,6 +421,18 @@ uint64_t qqt_mlp_train_work_bytes(int32_t n_rows);
  * them (synchronises the device). */
 int qqt_get_error(uint32_t *code_out);
 
+/* Failure-path check of the policy kernel (no counterpart in the
+ * reference, whose torch forward has no device-side waits).  With polls >
+ * 0, every following launch of the fused MLP kernel (qqt_mlp_act, the
+ * tail of qqt_cnn_act, qqt_mlp_train_forward) first makes one bounded
+ * mbarrier wait of `polls` polls on a
+ * barrier that nothing completes at that point, before any copy or MMA is
+ * issued; the wait expires like any wait that runs out (QQT_DEV_TIMEOUT in
+ * the error word) and the kernel takes its abort path: no outputs, TMEM
+ * freed, every CTA of a cluster through the closing barrier.  polls = 0
+ * (the default) turns the check off.  Host-global setting. */
+int qqt_test_set_wait_polls(uint32_t polls);
+
 /* Library version string. */
 const char *qqt_version(void);
 

@@ -777,13 +777,15 @@ def _splitmix_unit(x):
     return (x >> np.uint64(40)).astype(np.float32) * np.float32(1.0 / 16777216.0)
 
 
-def flush_recycle_keyed(cfg, st, excl, seed, counter):
+def flush_recycle_keyed(cfg, st, excl, seed, counter, envs=None):
     """Crate recycling with counter-based draws (the engine's device variant of
     sim/torch_sim.py:549-596): for each player p (in order) of each env with
     pending_lost > 0, the min(lost, #available) available cells (not wall,
     not brick, not in `excl`) with the smallest keys u(key + cell) get a
     crate and a recycle mark (ties -> lower cell); key = seed ^ counter*G ^
-    (e << 20) ^ (p << 52) ^ t_e*M.  Checker for k_flush_recycle."""
+    (e << 20) ^ (p << 52) ^ t_e*M.  Checker for k_flush_recycle.  envs:
+    the engine's env index of each row of `st` (a subset of a larger sim);
+    None = 0..N-1."""
     n = st["wall"].shape[0]
     p = st["alive"].shape[1]
     h, w = cfg.height, cfg.width
@@ -798,7 +800,8 @@ def flush_recycle_keyed(cfg, st, excl, seed, counter):
                 lost = int(st["pending_lost"][e, pl])
                 if lost <= 0:
                     continue
-                key = (np.uint64(seed) ^ (np.uint64(counter) * G) ^ (np.uint64(e) << np.uint64(20))
+                ge = e if envs is None else int(envs[e])
+                key = (np.uint64(seed) ^ (np.uint64(counter) * G) ^ (np.uint64(ge) << np.uint64(20))
                        ^ (np.uint64(pl) << np.uint64(52)) ^ (np.uint64(st["t"][e]) * M))
                 avail = ~(st["wall"][e].reshape(-1) | st["brick"][e].reshape(-1) | ex)
                 k = _splitmix_unit(key + cells)
@@ -807,6 +810,77 @@ def flush_recycle_keyed(cfg, st, excl, seed, counter):
                 st["crate"][e].reshape(-1)[order] = True
                 st["recycle"][e].reshape(-1)[order] = True
                 st["pending_lost"][e, pl] = 0
+    return st
+
+
+def template_swap_draws(seed, episode, envs=None):
+    """Spawn-swap decisions of the device auto-reset: env e in its episode
+    `episode[e]` swaps seats 0 and 1 when u(seed ^ (e << 32) ^ episode[e])
+    < 0.5 (the keyed stand-in for the reference's host draw
+    `torch.rand(count, generator=gen) < 0.5`, sim/torch_sim.py:229-240).
+    envs: the engine's env index of each entry (a subset of a larger sim);
+    None = 0..N-1."""
+    ep = np.asarray(episode, dtype=np.int64).astype(np.uint64)
+    e = (np.arange(ep.shape[0]) if envs is None else np.asarray(envs)).astype(np.uint64)
+    return _splitmix_unit(np.uint64(seed) ^ (e << np.uint64(32)) ^ ep) < np.float32(0.5)
+
+
+def template_reset(cfg, st, tmpl, mask, swap=None, episode=None):
+    """Reset the envs in `mask` to their per-env templates, in place.
+
+    Restates the reset branch of the engine's step (the device auto-reset)
+    on the reference's reset_ field list (sim/torch_sim.py:178-420):
+      * map: wall, brick from the template; crate from the template (the
+        reference clears crates, sim/torch_sim.py:385, and lays an open
+        map's cross crates afterwards, :392-396: a template carries the
+        crates an episode starts with); recycle marks cleared (:386);
+      * bombs: fuse 0, owner -1, bomb_blast 0 (:397-399);
+      * players: spawn positions from the template, seats 0 and 1 swapped
+        where `swap` is set (:229-240 / :374-383); bombs_cap, blast_cap,
+        spd_g and the growth floors lo_* from the template's start
+        attributes (:209-224 and the corridor/ring/open branches); alive,
+        hp = max_hp (:400-401), since_bomb = place_dist_cooldown (:404),
+        invuln 0 (:405), pending_lost 0, combo 0, last_hit -10**9
+        (:387-389);
+      * env: t = 0 (:406), crate_prob from the template (:284, :317, :348),
+        hazard off (:420; templates carry no hazard waves).
+    tmpl: dict of wall, brick, crate (N,H,W) bool, spawn (N,P,2) f32,
+    bombs_cap, blast_cap (N,P) int, spd (N,P) f32, crate_prob (N,) f32.
+    swap: (N,) bool or None (no swap).  episode: (N,) int64 counter,
+    incremented for every reset env when given.
+    """
+    idx = np.nonzero(np.asarray(mask, bool))[0]
+    if idx.size == 0:
+        return st
+    p = st["alive"].shape[1]
+    st["wall"][idx] = tmpl["wall"][idx]
+    st["brick"][idx] = tmpl["brick"][idx]
+    st["crate"][idx] = tmpl["crate"][idx] if "crate" in tmpl else False
+    st["recycle"][idx] = False
+    st["fuse"][idx] = 0
+    st["owner"][idx] = -1
+    st["bomb_blast"][idx] = 0
+    pos = np.array(tmpl["spawn"][idx], dtype=F32, copy=True)
+    if swap is not None and p >= 2:
+        sw = np.asarray(swap, bool)[idx]
+        pos[sw, 0], pos[sw, 1] = tmpl["spawn"][idx][sw, 1], tmpl["spawn"][idx][sw, 0]
+    st["pos"][idx] = pos
+    st["alive"][idx] = True
+    st["hp"][idx] = cfg.max_hp
+    st["since_bomb"][idx] = cfg.place_dist_cooldown
+    st["invuln"][idx] = 0
+    st["pending_lost"][idx] = 0
+    st["combo"][idx] = 0
+    st["last_hit"][idx] = -10 ** 9
+    for cap, lo, src in (("bombs_cap", "lo_bombs", "bombs_cap"),
+                         ("blast_cap", "lo_blast", "blast_cap"), ("spd_g", "lo_spd", "spd")):
+        st[cap][idx] = tmpl[src][idx]
+        st[lo][idx] = tmpl[src][idx]
+    st["crate_prob"][idx] = tmpl["crate_prob"][idx]
+    st["hazard"][idx] = False
+    st["t"][idx] = 0
+    if episode is not None:
+        episode[idx] += 1
     return st
 
 

@@ -41,6 +41,8 @@
 
 #include <cuda.h>
 
+#include <atomic>
+
 #include "qqt_common.cuh"
 
 namespace qqt {
@@ -76,8 +78,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait; false (and the timeout flag) when the limit expires.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i)
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          uint32_t limit = kWaitLimit) {
+  for (uint32_t i = 0; i < limit; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   flag_error(QQT_DEV_TIMEOUT);
   return false;
@@ -706,7 +709,7 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
             const float* __restrict__ f, const uint8_t* __restrict__ img, SeatOut io, int seat0,
             int mm_stride, int bm_stride, const float* __restrict__ u, int act_stride,
             float* __restrict__ logp_out, float* __restrict__ value_out,
-            float* __restrict__ logits_out, TrainOut tr) {
+            float* __restrict__ logits_out, TrainOut tr, uint32_t test_wait) {
   static_assert(!TRAIN || (NT == 128 && !SPLIT_A), "training forward: one seat, fp16 rows");
   using G = FusedCfg<NT, SPLIT_A>;
   constexpr int S = NT / 128;
@@ -760,6 +763,15 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
   }
   const uint32_t tmem = *tmem_slot;
   bool arrived = false;   // this thread's arrival on the closing cluster barrier
+  if (test_wait) {
+    // failure-path check (qqt_test_set_wait_polls): before anything is
+    // issued, one bounded wait of test_wait polls on the tail-image barrier,
+    // which nothing completes before layer 1 ends, expires like any wait
+    // that runs out; the CTA then takes the abort path with nothing in
+    // flight
+    if (threadIdx.x == 0 && !mbar_wait(wbar, 0, test_wait)) *abort_flag = 1;
+    __syncthreads();
+  }
 
   if (warp == 0) {
     // training forward over minibatch rows of a larger buffer: the tile's
@@ -821,7 +833,9 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
       bool ok = true;
       for (int kt = 0; kt < n_kt && ok; ++kt) {
         const int s = kt % G::kStages;
-        if (!mbar_wait(&full[s], (kt / G::kStages) & 1) || *abort_flag) {
+        // an abort stops the MMAs before the next stage (the producer
+        // drains every stage it issued before the CTA exits)
+        if (*abort_flag || !mbar_wait(&full[s], (kt / G::kStages) & 1)) {
           *abort_flag = 1;
           ok = false;
           break;
@@ -1048,6 +1062,10 @@ static int mlp_split_k(int m_tiles, int k_tiles) {
   return min(ks, max(1, k_tiles / 2));
 }
 
+// Poll limit of the failure-path check in k_mlp_fused; 0 (the default)
+// leaves it off.  Set only by qqt_test_set_wait_polls.
+static std::atomic<uint32_t> g_test_wait_polls{0};
+
 template <int NT, bool SPLIT_A, bool TRAIN = false>
 static int launch_mlp_fused(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap& mb,
                             int n_rows, int k_tiles, const float* f, const uint8_t* img,
@@ -1071,8 +1089,10 @@ static int launch_mlp_fused(const CUtensorMap& ma, const CUtensorMap& malo, cons
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = ks > 1 ? 1 : 0;
+  const uint32_t test_wait = g_test_wait_polls.load(std::memory_order_relaxed);
   if (cudaLaunchKernelEx(&cfg, kern, ma, malo, mb, n_rows, k_tiles, f, img, io, seat0, mm_stride,
-                         bm_stride, u, act_stride, logp, value, logits, tr) != cudaSuccess)
+                         bm_stride, u, act_stride, logp, value, logits, tr,
+                         test_wait) != cudaSuccess)
     return QQT_E_LAUNCH;
   return launch_status();
 }
@@ -1230,4 +1250,9 @@ extern "C" int qqt_mlp_act(const void* pack, const void* obs, int32_t n_envs, in
                                         st);
   return launch_mlp_fused<256, false>(ma, ma, mb, n_envs, k_tiles, fpar, pk + L.img_off, io, 0,
                                       mm_stride, bm_stride, u, act_stride, logp, value, logits, st);
+}
+
+extern "C" int qqt_test_set_wait_polls(uint32_t polls) {
+  g_test_wait_polls.store(polls, std::memory_order_relaxed);
+  return QQT_OK;
 }

@@ -123,6 +123,7 @@ def lib():
             "qqt_mlp_pack_bytes": (c_u64, [c_i32, c_i32]),
             "qqt_mlp_work_bytes": (c_u64, [c_i32, c_i32]),
             "qqt_mlp_param_names": (ctypes.c_char_p, []),
+            "qqt_test_set_wait_polls": (c_i32, [ctypes.c_uint32]),
             "qqt_cnn_act": (c_i32, [c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_p,
                                     c_i32, c_p, c_i32, c_p, c_p, c_i32, c_p, c_p, c_p, c_p,
                                     c_p]),

@@ -149,6 +149,13 @@ class AstarBot(_Bot):
         capi.check(rc, "qqt_astar_act")
         return act
 
+    def chain_scan_len(self) -> torch.Tensor:
+        """(1,) int32 device view of the last act()'s chain-scan length: the
+        maximum over the batch of the seat's blast_cap (sim/bots.py:484),
+        which the library reduces into the first word of the bot's scratch
+        before the bot kernel reads it."""
+        return self._scratch[:4].view(torch.int32)
+
 
 class HunterBot(_Bot):
     """The hunter: astar with the crate layer and no mode ticker

@@ -111,6 +111,11 @@ class Rollout:
         # probe(name, fn) wraps each engine call of a tick (e.g. timing events
         # around it); None runs the calls directly
         self.probe = None
+        # cap_log: a (T,) int32 device tensor, or None; when set, every tick
+        # also records the astar opponent's chain-scan length (the batch
+        # maximum of its seat's blast_cap, sim/bots.py:484) in cap_log[t],
+        # so a check of a subset of envs can replay the bot's bomb rule
+        self.cap_log = None
 
     def _run(self, name, fn):
         # an NVTX range per engine call (visible to Nsight Systems in eager
@@ -147,6 +152,8 @@ class Rollout:
             bot = self.opponent
             self.feed_opponent(t)
             self._run("bot", lambda: bot.act(obs, mm[:, o], bm[:, o], o, out=acts[:, o]))
+            if self.cap_log is not None and isinstance(bot, AstarBot):
+                self.cap_log[t:t + 1].copy_(bot.chain_scan_len())
             main.wait_stream(self.side)
         flush = bool(self.flush_every) and t % self.flush_every == self.flush_every - 1
         nxt = None

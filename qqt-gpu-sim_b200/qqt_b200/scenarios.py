@@ -87,6 +87,24 @@ CFG1 = dict(height=13, width=13, n_players=2, map_mode="open", speed=3.0, tick_h
 CFG2 = dict(map_mode="corridor", open_fraction=0.0, speed=3.0, max_steps=1800)
 
 
+def open_border_template(cfg, n: int) -> dict:
+    """Per-env template of the cfg1 workload: the open-border map, the
+    reference's open spawns and the start attributes its open-map reset
+    gives both seats at opponent boost 0 (bombs max_bombs, blast `blast`,
+    speed 1.0: sim/torch_sim.py:200-224); crate_prob keeps the construction
+    value (an open-map reset leaves it alone).  With swap_spawns the device
+    reset swaps the two spawns with probability 1/2, as the reference's
+    open-map reset does (sim/torch_sim.py:229-240)."""
+    p, h, w = cfg.n_players, cfg.height, cfg.width
+    wall = np.broadcast_to(border_walls(h, w), (n, h, w)).copy()
+    spawn = np.broadcast_to(np.array(cfg.spawn_pos(), np.float32), (n, p, 2)).copy()
+    return {"wall": wall, "brick": np.zeros_like(wall), "spawn": spawn,
+            "bombs_cap": np.full((n, p), cfg.max_bombs, np.int64),
+            "blast_cap": np.full((n, p), cfg.blast, np.int64),
+            "spd": np.full((n, p), 1.0, np.float32),
+            "crate_prob": np.full((n,), cfg.growth_crate_prob, np.float32)}
+
+
 def corridor_template(cfg, n: int, seed: int) -> dict:
     """Per-env map template of the cfg2 workload: border walls, permanent
     pillars, bricks with p=0.7 (corner L cells kept free), corner spawns and

@@ -254,3 +254,44 @@ def test_hazard_wave_matches_reference():
     for k in ("fuse", "owner", "bomb_blast"):
         assert np.array_equal(st[k], g["post_" + k]), k
     assert (g["post_owner"] == cfg.n_players).sum() > (g["pre_owner"] == cfg.n_players).sum()
+
+
+def test_template_reset_gives_the_reference_reset_state():
+    """oracle.template_reset (the restatement of the engine's device
+    auto-reset) on the cfg1 open-border template reproduces the reference's
+    own post-reset state (sim/torch_sim.py:178-420) for every env that ended
+    in the 256-tick cfg1 trajectory, all state keys, when it is given the
+    spawn swap the reference's generator drew (read from the golden)."""
+    g = G.load("traj_cfg1")
+    cfg = SimConfig(**scenarios.CFG1)
+    wall = g["init_wall"]
+    n = wall.shape[0]
+    tmpl = scenarios.open_border_template(cfg, n)
+    assert np.array_equal(tmpl["wall"], np.broadcast_to(wall, tmpl["wall"].shape))
+    spawn0 = tmpl["spawn"][:, 0]
+    swaps = []
+    for i, t in enumerate(g["reset_ticks"]):
+        st = G.state_at(g, t, wall)
+        done = g["done"][t]
+        rs = G.reset_state(g, i, wall)
+        swap = done & ~np.all(rs["pos"][:, 0] == spawn0, axis=-1)
+        swaps += list(swap[done])
+        episode = np.zeros(n, np.int64)
+        O.template_reset(cfg, st, tmpl, done, swap=swap, episode=episode)
+        bad = G.compare_state(rs, st)
+        assert not bad, f"t={t}: template reset differs from the reference in {bad}"
+        assert np.array_equal(episode, done.astype(np.int64))
+    assert any(swaps) and not all(swaps), "both swap outcomes are exercised"
+
+
+def test_template_swap_draws_are_keyed():
+    """The device reset's spawn-swap draw is a pure function of (seed, env,
+    episode): fixed values, about half swap, and a new episode redraws."""
+    ep = np.zeros(4096, np.int64)
+    a = O.template_swap_draws(7, ep)
+    assert np.array_equal(a, O.template_swap_draws(7, ep))
+    assert 0.45 < a.mean() < 0.55
+    b = O.template_swap_draws(7, ep + 1)
+    assert 0.4 < (a != b).mean() < 0.6
+    c = O.template_swap_draws(8, ep)
+    assert (a != c).any()
