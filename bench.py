@@ -40,20 +40,24 @@ METRIC = "rollout env-steps/sec (sim+obs+policy+sample) at 1/2/4/8 B200 vs ref C
 UNIT = "env-steps/s"
 
 CONFIGS = {
-    "cfg2": dict(envs=5632, learner="mlp", seats=(0,), opponent="astar", ppo=False, cpu=(256, 8),
+    "cfg2": dict(envs=5632, learner="mlp", seats=(0,), opponent="astar", ppo=False, cpu=(352, 16),
+                 ref_per=None,
                  workload="cfg2: 13x13 pillar corridor (bricks p=0.7), P=2, N=5632 envs per "
                           "GPU, random-init MLP learner seat 0 (view_perm) vs astar seat 1, "
                           "128-tick rollout"),
-    "cfg4": dict(envs=65536, learner="mlp", seats=(0, 1), opponent=None, ppo=True, cpu=(256, 8),
+    "cfg4": dict(envs=65536, learner="mlp", seats=(0, 1), opponent=None, ppo=True, cpu=(512, 8),
+                 ref_per=512,
                  workload="cfg4: cfg2 map, N=65536 envs per GPU, self-play (one random-init "
                           "MLP for both seats, one N=256 GEMM), 128-tick rollout; PPO update "
                           "(4 epochs x 8 minibatches, seat-0 buffer) timed separately"),
     "cfg3": dict(envs=16384, learner=None, seats=(), opponent=None, ppo=False, cpu=(64, 1),
+                 ref_per=None,
                  workload="cfg3: chain/danger stress, 13x13 border-wall map, N=16384 envs per GPU, "
                           "20-40 bombs per env (fuse U{1..30}, blast U{1..5}); one step = step "
                           "(IDLE, no reset) + danger map + obs + masks + astar V_safe/V_opp and "
                           "actions for both players, from the same stress state every step"),
-    "cfg5": dict(envs=5632, learner="cnn", seats=(0,), opponent="greedy", ppo=False, cpu=(16, 2),
+    "cfg5": dict(envs=5632, learner="cnn", seats=(0,), opponent="greedy", ppo=False, cpu=(64, 8),
+                 ref_per=64,
                  workload="cfg5: cfg2 map, N=5632 envs per GPU, random-init CNN learner seat 0 "
                           "vs greedy seat 1, 128-tick rollout"),
 }
@@ -159,85 +163,17 @@ def _template(cfg, n, seed):
 
 # --------------------------------------------------------------- CPU legs
 
-def _oracle_rollout_worker(args):
-    """Run the oracle tick protocol of a config on a shard (spawned process)."""
-    n, ticks, seed, conf = args
-    import numpy as np
+def cpu_leg(n_per, ticks, procs, seed=0, conf="cfg2"):
+    """The oracle's rollout tick (oracle/cpu_rollout.py) on `procs` spawned
+    processes of n_per envs each: a 40-tick warm-up into a bomb-rich
+    mid-game state, then `ticks` timed ticks (the slowest shard's time).
+    Returns (env-steps/s, env-steps, seconds)."""
+    from oracle.cpu_rollout import ShardPool
+    pool = ShardPool(conf, n_per, procs, seed=seed, root=ROOT)
     try:
-        from threadpoolctl import threadpool_limits
-        threadpool_limits(1)
-    except Exception:
-        pass
-    from oracle import qqt_oracle as O
-    from qqt_b200 import scenarios
-    from qqt_b200.config import SimConfig
-    from qqt_b200.policy_init import init_params
-    c = CONFIGS[conf]
-    cfg = SimConfig(**scenarios.CFG2)
-    p = cfg.n_players
-    t = _template(cfg, n, seed)
-    st = {"wall": t["wall"], "brick": t["brick"], "crate": np.zeros_like(t["wall"]),
-          "recycle": np.zeros_like(t["wall"]),
-          "fuse": np.zeros(t["wall"].shape, np.int16), "owner": np.full(t["wall"].shape, -1, np.int8),
-          "bomb_blast": np.zeros(t["wall"].shape, np.int16), "pos": t["spawn"].copy(),
-          "alive": np.ones((n, p), bool), "hp": np.full((n, p), cfg.max_hp, np.uint8),
-          "since_bomb": np.full((n, p), cfg.place_dist_cooldown, np.int32),
-          "t": np.zeros(n, np.int64), "bombs_cap": t["bombs_cap"].copy(),
-          "blast_cap": t["blast_cap"].copy(), "spd_g": t["spd"].copy(),
-          "invuln": np.zeros((n, p), np.int64), "pending_lost": np.zeros((n, p), np.int64),
-          "combo": np.zeros((n, p), np.int64), "last_hit": np.full((n, p), -10 ** 9, np.int64),
-          "lo_bombs": t["bombs_cap"].copy(), "lo_blast": t["blast_cap"].copy(),
-          "lo_spd": t["spd"].copy(), "crate_prob": t["crate_prob"].copy(),
-          "hazard": np.zeros(n, bool)}
-    params = init_params(cfg.obs_shape, c["learner"], seed=1)
-    rng = np.random.default_rng(seed)
-    ticker = O.ModeTicker(rng.integers(0, 2, n), rng.integers(60, 240, n))
-    dch = 2 * p + 1
-
-    def learner(obs32, mm, bm, pid):
-        u = rng.random((n, 2))
-        if c["learner"] == "mlp":
-            return O.mlp_act(params, obs32, mm[:, pid], bm[:, pid], pid, p, u[:, 0], u[:, 1])[0]
-        ml, bl, _ = O.cnn_forward(params, obs32, pid, p)
-        am, _ = O.masked_sample(ml, mm[:, pid], u[:, 0])
-        ab, _ = O.masked_sample(bl, bm[:, pid], u[:, 1])
-        return np.stack([am, ab], -1)
-
-    t0 = time.perf_counter()
-    for _ in range(ticks):
-        obs, _ = O.observe(cfg, st)
-        obs32 = obs.astype(np.float16).astype(np.float32)
-        mm, bm = O.legal_mask(cfg, st)
-        a0 = learner(obs32, mm, bm, 0)
-        if c["opponent"] == "astar":
-            mode = ticker.advance(rng.integers(0, 2, n), rng.integers(60, 240, n))
-            a1 = O.astar_attack(cfg, st, obs32[:, dch], mm[:, 1], bm[:, 1], 1,
-                                rng.random((n, 5)).astype(np.float32), mode=mode)
-        elif c["opponent"] == "greedy":
-            a1 = O.greedy_attack(cfg, st, obs32[:, dch], mm[:, 1], bm[:, 1], 1,
-                                 rng.random((n, 5)).astype(np.float32))
-        else:
-            a1 = learner(obs32, mm, bm, 1)
-        acts = np.stack([a0, a1], 1)
-        rb = rng.random((2, n, p)).astype(np.float32)
-        O.step(cfg, st, acts, rb[0], rb[1])
-    return n * ticks, time.perf_counter() - t0
-
-
-def cpu_leg(n_envs, ticks, procs, seed=0, conf="cfg2"):
-    """Bounded oracle sample on `procs` processes (spawned: no GPU state)."""
-    import multiprocessing as mp
-    per = max(1, n_envs // procs)
-    if procs == 1:
-        steps, dt = _oracle_rollout_worker((per, ticks, seed, conf))
-        return steps / dt, steps, dt
-    ctx = mp.get_context("spawn")
-    with ctx.Pool(procs) as pool:
-        res = pool.map(_oracle_rollout_worker,
-                       [(per, ticks, seed + i, conf) for i in range(procs)])
-    # workers run concurrently; each times its own loop (process start-up excluded)
-    dt = max(r[1] for r in res)
-    steps = sum(r[0] for r in res)
+        steps, dt = pool.run(ticks)
+    finally:
+        pool.close()
     return steps / dt, steps, dt
 
 
@@ -521,7 +457,16 @@ def gpu_bench(args):
         # ncu traffic was captured for the default cfg2 shard (2 groups of 2816 envs)
         traffic = _ncu_traffic(dom) if args.config == "cfg2" and n_inst == 2816 else None
         cores = args.cpu_procs
-        cpu_v, cpu_steps, cpu_dt = cpu_leg(args.cpu_envs, args.cpu_ticks, cores, conf=args.config)
+        cpu_base = None
+        if world == 1:
+            cpu_v, cpu_steps, cpu_dt = cpu_leg(args.cpu_envs, args.cpu_ticks, cores,
+                                               conf=args.config)
+            cpu_base = {"value": round(cpu_v, 1), "unit": UNIT, "cores": cores, "kind": "port",
+                        "sample": f"oracle (numpy restatement of the reference tick), "
+                                  f"{cores} process(es) x {args.cpu_envs} envs of the same "
+                                  f"workload: {args.cpu_ticks} mid-game ticks timed after a "
+                                  f"40-tick warm-up into a bomb-rich state ({cpu_steps} "
+                                  f"env-steps in {cpu_dt:.2f} s)"}
         out = {
             "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
@@ -545,10 +490,7 @@ def gpu_bench(args):
                          "frac": round(achieved / (tflops if tensor_bound else hbm), 4),
                          "peak_source": src, "traffic": traffic,
                          "per_kernel": per},
-            "cpu_baseline": {"value": round(cpu_v, 1), "unit": UNIT, "cores": cores,
-                             "kind": "port",
-                             "sample": f"oracle (numpy restatement), {args.cpu_envs} envs x "
-                                       f"{args.cpu_ticks} ticks of the same workload"},
+            "cpu_baseline": cpu_base,
             "clocks": clk.summary(),
         }
         if ppo is not None:
@@ -748,17 +690,58 @@ class RolloutDrawsPool:
 
 
 def reference_arm(args):
-    """Time the CPU restatement of the reference on the host's cores."""
+    """Time the CPU restatement of the reference tick (oracle/cpu_rollout.py)
+    on every host core, on this arm's workload: one spawned process per
+    core, each holding a shard of the GPU's envs (the whole shard for cfg2;
+    512 envs per process for cfg4 and 64 for cfg5, whose full shards would
+    take minutes per tick), warmed up 40 ticks into a bomb-rich mid-game
+    state; every step then plays `--ref-ticks` ticks on all shards at once
+    and is timed by the slowest shard.  cfg3 times the stress tick."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
     procs = args.cpu_procs_ref or max(1, len(os.sched_getaffinity(0)))
+    if args.config == "cfg3":
+        return _reference_stress(args, procs)
+    per = N_ENVS // procs if CFG["ref_per"] is None else min(CFG["ref_per"], N_ENVS // procs)
+    from oracle.cpu_rollout import ShardPool
+    pool = ShardPool(args.config, per, procs, seed=0, root=ROOT)
+    try:
+        for _ in range(args.warmup):
+            pool.run(args.ref_ticks)
+        vals = [pool.run(args.ref_ticks) for _ in range(args.steps)]
+    finally:
+        pool.close()
+    steps = sum(s for s, _ in vals)
+    dt = sum(d for _, d in vals)
+    value = steps / dt
+    sample = (f"oracle restatement of the reference tick, {procs} processes x {per} envs "
+              f"({per * procs} of the {N_ENVS}-env shard), 40-tick warm-up, then "
+              f"{args.warmup} untimed and {args.steps} timed steps of {args.ref_ticks} ticks")
+    return {"impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": UNIT,
+            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 sim, f64 policy (numpy)", "data": "synthetic",
+            "config": {"workload": CFG["workload"], "envs_per_gpu": N_ENVS,
+                       "sample_envs": per * procs, "ticks_per_step": args.ref_ticks,
+                       "warmup_ticks": 40},
+            "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": procs,
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": round(value, 1), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def _reference_stress(args, procs):
+    import multiprocessing as mp
+    per = max(1, N_ENVS // procs)
+    ctx = mp.get_context("spawn")
     vals = []
-    for _ in range(args.warmup):
-        cpu_leg(procs * 8, 2, procs, conf=args.config)
-    for i in range(args.steps):
-        v, steps, dt = cpu_leg(procs * 32, args.ref_ticks, procs, seed=i, conf=args.config)
-        vals.append((steps, dt))
+    with ctx.Pool(procs) as pool:
+        for i in range(args.warmup + args.steps):
+            res = pool.map(_stress_oracle_worker, [(per, 100 * i + j) for j in range(procs)])
+            if i >= args.warmup:
+                vals.append((sum(r[0] for r in res), max(r[1] for r in res)))
     steps = sum(s for s, _ in vals)
     dt = sum(d for _, d in vals)
     value = steps / dt
@@ -766,14 +749,11 @@ def reference_arm(args):
             "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 2),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32 sim, f64 policy (numpy)", "data": "synthetic",
-            "config": {"workload": CFG["workload"], "sample_envs": procs * 32,
-                       "sample_ticks": args.ref_ticks},
+            "dtype": "f32 sim", "data": "synthetic",
+            "config": {"workload": CFG["workload"], "envs_per_gpu": N_ENVS},
             "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": procs,
                              "kind": "port",
-                             "sample": f"oracle restatement of the reference path, "
-                                       f"{procs} processes x 32 envs x {args.ref_ticks} ticks "
-                                       f"per step"},
+                             "sample": f"oracle stress tick, {procs} processes x {per} envs"},
             "e2e": {"value": round(value, 1), "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
 
@@ -791,8 +771,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
-    ap.add_argument("--cpu-envs", type=int, default=0, help="CPU sample envs (0: per config)")
-    ap.add_argument("--cpu-ticks", type=int, default=0, help="CPU sample ticks (0: per config)")
+    ap.add_argument("--cpu-envs", type=int, default=0,
+                    help="CPU baseline envs per process (0: per config)")
+    ap.add_argument("--cpu-ticks", type=int, default=0,
+                    help="CPU baseline timed ticks after the warm-up (0: per config)")
     ap.add_argument("--cpu-procs", type=int, default=1)
     ap.add_argument("--cpu-procs-ref", type=int, default=0)
     ap.add_argument("--ref-ticks", type=int, default=4)
