@@ -340,6 +340,23 @@ def _side_views(sg):
             sg.view(torch.int64)[:, 0:2], f[:, 4], f[:, 5], f[:, 6], f[:, 7])
 
 
+def sampling_pool(total: int, rare: torch.Tensor, copies: int) -> torch.Tensor:
+    """Row indices that every epoch's permutation draws its `total` rows
+    from (oversampling of dying frames, train/ppo.py:377-392): each row
+    once, in order, followed -- when `copies` > 1 and some row is rare (hp
+    lost in an env that continued, or an episode end) -- by the list of
+    rare rows repeated copies - 1 times.  Rare frames are a handful per
+    episode; the extra copies raise their chance of being drawn without
+    changing the number of rows an epoch trains on."""
+    rows = torch.arange(total, device=rare.device)
+    if copies <= 1:
+        return rows
+    rare_rows = torch.nonzero(rare).flatten()
+    if rare_rows.numel() == 0:
+        return rows
+    return torch.cat([rows] + [rare_rows] * (copies - 1))
+
+
 def ppo_update(model: MLPActorCritic, opt, data: dict, last_val, cfg: PPOConfig,
                entropy_coef: float, pid: int = 0, perm_fn=None) -> dict:
     """One PPO update over a (T, N) rollout shard (train/ppo.py:364-437).
@@ -354,13 +371,17 @@ def ppo_update(model: MLPActorCritic, opt, data: dict, last_val, cfg: PPOConfig,
     adv, ret = gae(data["rew"], data["done"], data["val"], last_val, cfg.gamma, cfg.gae_lambda)
     T, n = adv.shape
     total = T * n
-    flat = lambda x: x.reshape(total, *x.shape[2:])  # noqa: E731
-    obs = flat(data["obs"])
+
+    def by_row(x):
+        # (T, N, ...) -> (T*N, ...): one training row per (tick, env)
+        return x.reshape(total, *x.shape[2:])
+
+    obs = by_row(data["obs"])
     if obs.is_cuda:
         obs = obs_rows(obs, model.k_in)
-    mm, bm, act = flat(data["mm"]), flat(data["bm"]), flat(data["act"])
-    old_logp, old_val = flat(data["logp"]), flat(data["val"])
-    adv, ret = flat(adv), flat(ret)
+    mm, bm, act = by_row(data["mm"]), by_row(data["bm"]), by_row(data["act"])
+    old_logp, old_val = by_row(data["logp"]), by_row(data["val"])
+    adv, ret = by_row(adv), by_row(ret)
     # global mean / unbiased std of the advantages over every rank's shard
     stats = torch.stack([adv.sum(), (adv * adv).sum(),
                          torch.tensor(float(total), device=dev)]).to(torch.float64)
@@ -371,14 +392,8 @@ def ppo_update(model: MLPActorCritic, opt, data: dict, last_val, cfg: PPOConfig,
     std = math.sqrt(max(float(var), 0.0)) if world > 1 else float(adv.std())
     adv = (adv - (mean.float() if world > 1 else adv.mean())) / (std + 1e-8)
 
-    base = torch.arange(total, device=dev)
-    over = cfg.oversample_dying
-    pool = base
-    if over > 1:
-        rare = flat(data["dmg"]) | flat(data["done"]).bool()
-        if bool(rare.any()):
-            rare_idx = rare.nonzero(as_tuple=False).squeeze(1)
-            pool = torch.cat([base, rare_idx.repeat(over - 1)])
+    pool = sampling_pool(total, by_row(data["dmg"]) | by_row(data["done"]).bool(),
+                         cfg.oversample_dying)
     mb = max(1, total // cfg.minibatches)
     perm_fn = perm_fn or (lambda k: torch.randperm(k, device=dev))
     # statistics stay on the device; one host read at the end

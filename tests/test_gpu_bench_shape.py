@@ -5,8 +5,8 @@ recycling), captured as the benchmark captures it (two CUDA graphs over two
 draw-buffer sets, `capture(double_buffer=True)`) and replayed from a
 mid-game state, against the oracle on seeded subsets of envs of both groups
 for all 128 ticks of both graphs: observation rows, legal masks, both
-seats' actions, rewards, done and damage flags every tick, and the whole
-state at the end.
+seats' actions, done and damage flags every tick and the whole state at the
+end bit-exact, rewards within 1e-6.
 
 Envs are independent except for one batch-wide value: the astar bot's
 chain scan reaches out to the maximum blast_cap of its seat over the whole
@@ -42,6 +42,12 @@ if torch.cuda.is_available():
 
 N_ENVS, GROUPS, T = 5632, 2, 128
 SUBSET = 192
+
+
+# rewards: within 1e-6 absolute, the bar of the reference goldens: the
+# combo term's gap_factor ** gap is CUDA's powf on the device and the C
+# library's powf in numpy, which may differ in the last bit
+REW_TOL = 1e-6
 
 
 @pytest.fixture(autouse=True)
@@ -139,7 +145,7 @@ def _oracle_group(cfg, params, ro, tmpl, start, sub, calls0, flush0, draws, bufs
         rew, done, _ = O.step(cfg, st, acts, draws["crate"][t, 0][sub], draws["crate"][t, 1][sub])
         dmg = ((hp0 - st["hp"].astype(np.int32)) > 0) & ~done[:, None]
         O.template_reset(cfg, st, tm, done, swap=None, episode=episode)
-        assert np.array_equal(bufs["rew"][t], rew), f"t={t}: reward"
+        assert np.abs(bufs["rew"][t] - rew).max() <= REW_TOL, f"t={t}: reward"
         assert np.array_equal(bufs["done"][t], done), f"t={t}: done"
         assert np.array_equal(bufs["dmg"][t], dmg), f"t={t}: damage flags"
         if t % ro.flush_every == ro.flush_every - 1:

@@ -5,9 +5,9 @@ sim/torch_sim.py:178-420).
 
 * episodes forced to end by timeout (t = max_steps - 1) and by death (hp 1
   with a bomb about to explode underfoot), several times per env, through
-  qqt_step and qqt_step_observe: state (every key), rewards, done, winner,
-  died and damage flags after every tick, and with the fused observation
-  the next tick's rows and legal masks, bit-exact;
+  qqt_step and qqt_step_observe: state (every key), done, winner, died and
+  damage flags after every tick, and with the fused observation the next
+  tick's rows and legal masks, bit-exact; rewards within 1e-6;
 * cfg1 at its benchmark size (N=64, 256 ticks, random bots on both seats)
   with the device reset on, observing and stepping through the public
   B200Sim API, tick by tick against the oracle.
@@ -27,6 +27,12 @@ if torch.cuda.is_available():
     from qqt_b200.bots import RandomBot
     from qqt_b200.config import SimConfig
     from qqt_b200.sim import B200Sim
+
+
+# rewards: within 1e-6 absolute, the bar of the reference goldens: the
+# combo term's gap_factor ** gap is CUDA's powf on the device and the C
+# library's powf in numpy, which may differ in the last bit
+REW_TOL = 1e-6
 
 
 @pytest.fixture(autouse=True)
@@ -104,7 +110,7 @@ def test_device_reset_vs_template_reset(fused):
         O.template_reset(cfg, st, tmpl, o_d, swap=swap, episode=episode)
         resets += o_d
         assert np.array_equal(_np(d), o_d), f"t={t}: done"
-        assert np.array_equal(_np(r), o_r), f"t={t}: reward"
+        assert np.abs(_np(r) - o_r).max() <= REW_TOL, f"t={t}: reward"
         assert np.array_equal(_np(info["winner"]), o_info["winner"]), f"t={t}: winner"
         assert np.array_equal(_np(info["died"]), o_info["died"]), f"t={t}: died"
         assert np.array_equal(_np(info["hit"]), o_hit), f"t={t}: damage flags"
@@ -159,6 +165,6 @@ def test_cfg1_benchmark_size_device_reset_vs_oracle():
                          episode=episode)
         ends += int(o_d.sum())
         assert np.array_equal(_np(d), o_d), f"t={t}: done"
-        assert np.array_equal(_np(r), o_r), f"t={t}: reward"
+        assert np.abs(_np(r) - o_r).max() <= REW_TOL, f"t={t}: reward"
         _cmp_state(sim.numpy_state(), st, f"t={t}")
     assert ends >= 8, f"only {ends} episodes ended in 256 ticks"
