@@ -19,6 +19,8 @@
 #include <stdint.h>
 #include <stdlib.h>
 
+#include <atomic>
+
 #include "../../include/qqt_b200.h"
 
 #define QQT_MAX_H 21
@@ -575,19 +577,20 @@ static inline int check_cfg(const QqtCfg* cfg) {
   return QQT_OK;
 }
 
-// SM count of the current device (cached per device).
+// SM count of the current device (cached per device; host threads may
+// race to fill an entry, and all of them store the same value).
 static inline int sm_count() {
-  static int n[64] = {0};
+  static std::atomic<int> n[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return 148;
-  if (!n[dev]) {
-    int v = 0;
+  int v = n[dev].load(std::memory_order_relaxed);
+  if (v <= 0) {
     if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
       v = 148;
-    n[dev] = v;
+    n[dev].store(v, std::memory_order_relaxed);
   }
-  return n[dev];
+  return v;
 }
 
 static inline int launch_status() {

@@ -25,7 +25,10 @@ import numpy as np
 import torch
 
 FORMAT_VERSION = 2
-FIRST_LAYER = {"cnn": "conv0.weight", "mlp": "shared.0.weight"}
+# the layer whose input channels are the observation's, per architecture
+# (the LSTM's is the first convolution of its local-view CNN)
+FIRST_LAYER = {"cnn": "conv0.weight", "mlp": "shared.0.weight", "lstm": "l_conv1.weight"}
+POLICY_ARCHS = ("mlp", "cnn")     # the architectures B200Policy runs
 
 
 def obs_extra(n_players: int) -> int:
@@ -107,6 +110,8 @@ def adapt_first_layer(state: dict, old_shape, new_shape, arch: str,
     starts at zero.  Keys whose shapes match are copied; `new_state` supplies
     the rest (the new model's initial values), otherwise they are absent.
     """
+    if arch not in FIRST_LAYER:
+        raise ValueError(f"unsupported arch {arch!r} (one of {sorted(FIRST_LAYER)})")
     old_shape, new_shape = tuple(old_shape), tuple(new_shape)
     out = {k: (v.clone() if torch.is_tensor(v) else torch.as_tensor(np.array(v)))
            for k, v in (new_state or {}).items()}
@@ -124,7 +129,8 @@ def adapt_first_layer(state: dict, old_shape, new_shape, arch: str,
                 continue      # dropped, or the new init stays (shape changed, not migrated)
             out[k] = v.clone()
             continue
-        if arch == "cnn":
+        if arch in ("cnn", "lstm"):
+            # a convolution: input channels on dimension 1
             w = torch.zeros((v.shape[0], new_shape[0]) + tuple(v.shape[2:]), dtype=v.dtype)
             w[:, :2] = v[:, :2]
             w[:, 2 * np_:2 * np_ + 3] = v[:, 2 * op:2 * op + 3]
@@ -152,6 +158,10 @@ def load_policy(path: str, device="cuda", target_shape=None, seats=(0,), new_sta
     from .policy import B200Policy
     ck = load_ckpt(path)
     arch = ck.get("arch", "cnn")
+    if arch not in POLICY_ARCHS:
+        raise ValueError(f"B200Policy runs the {' and '.join(POLICY_ARCHS)} architectures, not "
+                         f"{arch!r}; load_ckpt and adapt_first_layer still read and migrate "
+                         "this checkpoint's weights")
     shape = tuple(ck["obs_shape"])
     n_p = ck.get("n_players") or infer_players(shape[0])
     sd = dict(ck["model"])

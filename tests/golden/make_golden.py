@@ -29,6 +29,7 @@ Outputs (compressed npz, all env-major like the reference tensors):
                    its draws fed from the engine's keyed generator
   ckpt_adapt.npz   adapt_first_conv on seeded models (2 <-> 3 players), and
   ref_ckpt_mlp.pt  a checkpoint written by the reference's save_ckpt
+  ckpt_adapt_lstm.npz  adapt_first_conv on the LSTM architecture
 """
 
 from __future__ import annotations
@@ -568,6 +569,30 @@ def ckpt_golden(R):
     return out
 
 
+def ckpt_lstm_golden(R):
+    """adapt_first_conv on the LSTM architecture (train/train.py:140-147: its
+    local CNN's first layer l_conv1 takes the observation's channels in
+    view order), seeded random models, 2 <-> 3 players."""
+    import torch
+    from sim.config import n_obs_channels
+    from train.train import adapt_first_conv
+    AC = R["ActorCritic"]
+    out = {}
+    for i, (p_old, p_new) in enumerate(((2, 3), (3, 2))):
+        torch.manual_seed(200 + i)
+        old_shape = (n_obs_channels(p_old), 13, 13)
+        new_shape = (n_obs_channels(p_new), 13, 13)
+        m = AC(old_shape, arch="lstm", n_players=p_old)
+        with torch.no_grad():
+            for prm in m.parameters():
+                prm.normal_(0.0, 0.1)
+        nm = adapt_first_conv(m, new_shape, arch="lstm", n_players=p_new)
+        tag = f"lstm_{p_old}to{p_new}"
+        out[f"{tag}__old"] = m.state_dict()["l_conv1.weight"].numpy().copy()
+        out[f"{tag}__new"] = nm.state_dict()["l_conv1.weight"].numpy().copy()
+    return out
+
+
 def hazard_golden(R):
     """Hazard wave placement (sim/torch_sim.py:1404-1466) run by the
     reference itself on seeded states, with its randint / rand / randperm
@@ -690,7 +715,7 @@ def local_view_golden(R):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("QQT_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--ref", required=True, help="root of the reference source tree")
     ap.add_argument("--only", default="")
     args = ap.parse_args()
     R = load_reference(args.ref)
@@ -711,6 +736,7 @@ def main():
         "reset_modes": lambda: reset_modes(R),
         "ppo_update": lambda: ppo_golden(R),
         "ckpt_adapt": lambda: ckpt_golden(R),
+        "ckpt_adapt_lstm": lambda: ckpt_lstm_golden(R),
         "hazard_wave": lambda: hazard_golden(R),
         "local_view": lambda: local_view_golden(R),
     }

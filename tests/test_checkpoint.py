@@ -125,3 +125,28 @@ def test_checkpoint_policy_acts_like_oracle(tmp_path):
     lg = logits[0].cpu().numpy()
     for got, want in ((lg[:, :5], ml), (lg[:, 5:7], bl), (lg[:, 7], v)):
         assert np.abs(got - want).max() / np.abs(want).max() <= 2e-3
+
+
+@pytest.mark.parametrize("p_old,p_new", [(2, 3), (3, 2)])
+def test_adapt_first_layer_lstm_matches_reference(p_old, p_new):
+    """The LSTM's local CNN takes the observation channels in view order:
+    l_conv1.weight migrates like conv0 (train/train.py:140-147), bit-exact
+    to the reference's adapt_first_conv (tests/golden/ckpt_adapt_lstm.npz)."""
+    g = np.load(os.path.join(GOLD, "ckpt_adapt_lstm.npz"))
+    tag = f"lstm_{p_old}to{p_new}"
+    old_shape = (2 * p_old + 3 + C.obs_extra(p_old), 13, 13)
+    new_shape = (2 * p_new + 3 + C.obs_extra(p_new), 13, 13)
+    old = {"l_conv1.weight": torch.from_numpy(g[f"{tag}__old"])}
+    out = C.adapt_first_layer(old, old_shape, new_shape, "lstm", p_old, p_new)
+    assert np.array_equal(out["l_conv1.weight"].numpy(), g[f"{tag}__new"])
+
+
+def test_unsupported_arch_errors(tmp_path):
+    with pytest.raises(ValueError, match="unsupported arch"):
+        C.adapt_first_layer({}, (14, 3, 3), (19, 3, 3), "transformer")
+    path = str(tmp_path / "lstm.pt")
+    C.save_ckpt(path, model={"l_conv1.weight": torch.zeros(32, 14, 3, 3)}, obs_shape=(14, 13, 13),
+                n_players=2, arch="lstm")
+    assert C.load_ckpt(path)["arch"] == "lstm"
+    with pytest.raises(ValueError, match="B200Policy runs"):
+        C.load_policy(path, device="cpu")
