@@ -284,7 +284,7 @@ def ppo_leg(grp, device):
         obs, mmv, bmv = sim.observe_and_mask(rows, mm, bm, danger=False)
         pol.act_seats(obs, [mmv[:, s] for s in ro.seats], [bmv[:, s] for s in ro.seats], u,
                       [acts[:, s] for s in ro.seats], None, last)
-        st = ppo_update(model, opt, data, last[0], cfg, cfg.entropy_coef, pid=0)
+        st = ppo_update(model, opt, data, last[0], cfg, cfg.entropy_coef, pid=0, profile=prof)
         pol.load_state_dict({k: p.detach() for k, p in model.state_dict().items()
                              if k in pol.params})
         return st
@@ -292,7 +292,9 @@ def ppo_leg(grp, device):
     # the first update also grows the allocator's pools (multi-GB minibatch
     # blocks) and creates the optimizer state; a training loop pays that once
     times = []
+    prof = {}
     for _ in range(2):
+        prof.clear()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         a.record()
@@ -301,10 +303,14 @@ def ppo_leg(grp, device):
         torch.cuda.synchronize()
         times.append(a.elapsed_time(b))
     ms = times[-1]
+    ar_ms = sum(x.elapsed_time(y) for x, y in prof.get("allreduce_events", []))
     samples = buf.done.numel()
     return {"ms": round(ms, 2), "first_update_ms": round(times[0], 2), "samples": samples,
             "samples_per_s": round(samples / (ms / 1e3), 1),
             "minibatches": cfg.epochs * cfg.minibatches,
+            "grad_allreduce_ms": round(ar_ms, 3),
+            "grad_allreduce_share": round(ar_ms / ms, 5),
+            "grad_allreduce_bytes": 345288 * 4,
             "includes": "bootstrap value, GAE kernel, advantage stats, 32 x (row gather, fused "
                         "forward, backward kernels, gradient all-reduce, clip, Adam), policy "
                         "repack; the second of two updates on the same rollout",

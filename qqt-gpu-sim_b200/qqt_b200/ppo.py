@@ -358,7 +358,8 @@ def sampling_pool(total: int, rare: torch.Tensor, copies: int) -> torch.Tensor:
 
 
 def ppo_update(model: MLPActorCritic, opt, data: dict, last_val, cfg: PPOConfig,
-               entropy_coef: float, pid: int = 0, perm_fn=None) -> dict:
+               entropy_coef: float, pid: int = 0, perm_fn=None,
+               profile: dict | None = None) -> dict:
     """One PPO update over a (T, N) rollout shard (train/ppo.py:364-437).
 
     data: obs (T,N,C,H,W) fp16 (or row-padded view), mm (T,N,5), bm (T,N,2),
@@ -366,6 +367,9 @@ def ppo_update(model: MLPActorCritic, opt, data: dict, last_val, cfg: PPOConfig,
     Advantage statistics and gradients are reduced over all ranks of the
     default process group when one is initialised.  perm_fn(n) -> index
     permutation (defaults to torch.randperm on the data's device).
+    profile: a dict that, on CUDA, receives a list of (start, end) CUDA
+    event pairs around every minibatch's gradient all-reduce under
+    "allreduce_events" (read after a synchronize).
     """
     dev = data["rew"].device
     adv, ret = gae(data["rew"], data["done"], data["val"], last_val, cfg.gamma, cfg.gae_lambda)
@@ -439,7 +443,15 @@ def ppo_update(model: MLPActorCritic, opt, data: dict, last_val, cfg: PPOConfig,
             grads = [p.grad for p in params if p.grad is not None]
             if grads:
                 buf = torch.cat([g.reshape(-1) for g in grads])
+                ev = None
+                if profile is not None and buf.is_cuda:
+                    ev = (torch.cuda.Event(enable_timing=True),
+                          torch.cuda.Event(enable_timing=True))
+                    ev[0].record()
                 w = _all_reduce(buf)
+                if ev is not None:
+                    ev[1].record()
+                    profile.setdefault("allreduce_events", []).append(ev)
                 if w > 1:
                     buf /= w
                     off = 0

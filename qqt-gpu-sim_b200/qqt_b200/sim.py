@@ -602,6 +602,55 @@ class B200Sim:
                 self.reset_(done.clone())
         return reward, done, info
 
+    # --------------------------------------------- CUDA graph of one tick
+    def capture_graph(self, actions: torch.Tensor, obs_buf: torch.Tensor,
+                      mmask_buf: torch.Tensor, bmask_buf: torch.Tensor,
+                      reward_buf: torch.Tensor, done_buf: torch.Tensor,
+                      winner_buf: torch.Tensor) -> None:
+        """Capture observe -> legal_mask -> step(auto_reset=False) writing
+        into fixed buffers as one CUDA graph (BatchedSim.capture_graph,
+        sim/torch_sim.py:649-678); `graph_step()` replays it.  The step reads
+        `actions` in place and its crate-pickup draws from `_rand_buf`
+        (n*(2P+1) floats, the reference's layout), which
+        `graph_refill_rand()` refills between replays.  Like the reference,
+        three eager warm-up ticks run first (they advance the state)."""
+        n, p = self.num_envs, self.cfg.n_players
+        self._g = torch.cuda.CUDAGraph()
+        self._gbufs = (obs_buf, mmask_buf, bmask_buf, reward_buf, done_buf, winner_buf)
+        self._actions = actions
+        self._rand_buf = torch.rand(n * (2 * p + 1), device=self.device)
+        for _ in range(3):
+            self._graph_body()
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.graph(self._g):
+            self._graph_body()
+        torch.cuda.synchronize(self.device)
+
+    def _graph_body(self) -> None:
+        obs_buf, mmask_buf, bmask_buf, reward_buf, done_buf, winner_buf = self._gbufs
+        obs_buf.copy_(self.observe())
+        mm, bm = self.legal_mask()
+        mmask_buf.copy_(mm)
+        bmask_buf.copy_(bm)
+        reward, done, info = self.step(self._actions, auto_reset=False)
+        reward_buf.copy_(reward)
+        done_buf.copy_(done.float())
+        winner_buf.copy_(info["winner"].float())
+
+    def graph_step(self) -> None:
+        """Replay the captured tick (BatchedSim.graph_step)."""
+        self._g.replay()
+
+    def graph_refill_rand(self) -> None:
+        """New uniforms for the captured step's draws, outside the graph
+        (BatchedSim.graph_refill_rand)."""
+        if self._rand_buf is not None:
+            self._rand_buf.uniform_()
+
+    def graph_actions(self) -> torch.Tensor:
+        """The action buffer the captured step reads (BatchedSim.graph_actions)."""
+        return self._actions
+
     # ------------------------------------------------------------ recycle
     def flush_recycle(self, on_device: bool | None = None, obs_rows: torch.Tensor | None = None):
         """Drop one crate per lost attribute layer on random free cells
