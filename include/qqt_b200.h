@@ -125,6 +125,45 @@ typedef struct QqtTemplate {
   int64_t *episode;         /* [N] per-env reset counter (in/out)             */
 } QqtTemplate;
 
+/* Per-episode level generation on the device: the reference's reset_
+ * (sim/torch_sim.py:178-420 with sim/mapgen.py's make_walls, make_bricks,
+ * make_open_obstacles, make_ring_walls, make_ring_bricks).  The geometry
+ * that does not change between episodes comes precomputed from the host
+ * (cell bit sets, spawn positions, thresholds); the random parts are drawn
+ * from a counter-based hash of (seed, env, episode, draw family, index)
+ * instead of the host generator, so an ended episode's next level is built
+ * with no host round trip.  Bit sets: bit c of word c / 32 = cell c. */
+#define QQT_MG_WORDS 14           /* ceil(21 * 21 / 32)                        */
+typedef struct QqtMapGen {
+  uint64_t seed;
+  int64_t *episode;               /* [N] per-env reset counter (in/out)        */
+  const int64_t *opp_boost;       /* [N] opponent start tier 0/1/2 or NULL (0) */
+  uint8_t *is_open;               /* [N] out, or NULL                          */
+  int64_t *map_kind;              /* [N] out (0 corridor, 1 open, 2 ring), or NULL */
+  int32_t corridor_mode;          /* map_mode == "corridor"; else an open map  */
+  float cut_pure, cut_open, cut_ring; /* float32 kind thresholds: pure_open,
+                                     + open_fraction, + ring_fraction          */
+  int32_t obst_max;               /* open_obstacle_max                         */
+  int32_t random_wall_rows, top_wall_rows, corr_c0, corr_c1;
+  int32_t n_edge, edge_cols[4];   /* columns of the vertical brick segments    */
+  float wall_density, ring_density, hazard_fraction;
+  int32_t ring_r0, ring_r1, ring_c0, ring_c1; /* central block [r0,r1)x[c0,c1) */
+  int32_t open_cross;             /* open maps get the cross-band crates       */
+  /* seat-0 start attributes by level kind: [0] corridor / ring (growth
+   * start), [1] open and pure-open maps, [2] open-mode maps */
+  int64_t start_bombs[3], start_blast[3];
+  float start_spd[3];
+  float crate_prob_kind[3];       /* corridor, open, ring                      */
+  int64_t opp_bombs2, opp_blast2; /* opponent tier 2 start                     */
+  float opp_spd2, opp_mult;       /* tier 2 speed; tier 1 multiplier           */
+  int64_t bombs_max, blast_max;   /* growth caps (tier 1 clamp)                */
+  float spd_max;
+  float spawn[3][4][2];           /* [map spawns, open spawns, ring spawns][player][row, col] */
+  uint32_t clear_spawn[QQT_MG_WORDS]; /* map spawn cells + 4-neighbours        */
+  uint32_t clear_ring[QQT_MG_WORDS];  /* ring spawn cells + 4-neighbours       */
+  uint32_t cross[QQT_MG_WORDS];       /* open-map cross-band crate cells       */
+} QqtMapGen;
+
 /* Optional outputs of a step (any may be NULL). */
 typedef struct QqtStepOut {
   float *reward;            /* [N][P]                                         */
@@ -195,6 +234,22 @@ int qqt_step_noalloc(const QqtCfg *cfg, const QqtState *st, const int64_t *actio
                      const float *rb_hit, const float *rb_grow, int32_t *tiers,
                      int32_t first_step, const QqtStepOut *out, const QqtTemplate *tmpl,
                      qqt_stream_t stream);
+
+/* Device auto-reset with per-episode level generation: every env whose
+ * done[e] is set gets a new level and a fresh episode, as the reference's
+ * reset_ gives it (sim/torch_sim.py:178-420; level kind by pure_open /
+ * open / ring fractions, corridor walls with random top/bottom rows, side
+ * bricks and edge segments, open-map obstacles and cross crates, ring
+ * block and band bricks, start attributes with the opponent boost tier,
+ * spawn swap, hazard envs), drawn from a counter-based hash of (seed, env,
+ * episode) rather than the host generator.  Envs with done[e] = 0 are not
+ * touched.  With obs (fp16 rows [N][obs_stride]), mm and bm non-NULL, the
+ * reset envs' observation rows and legal masks are rewritten for the new
+ * episode (after a qqt_step_observe, the rows of the envs that ended).
+ * The per-env counter mg->episode advances for every reset env. */
+int qqt_map_reset(const QqtCfg *cfg, const QqtState *st, const QqtMapGen *mg,
+                  const uint8_t *done, void *obs, uint8_t *mm, uint8_t *bm,
+                  qqt_stream_t stream);
 
 /* Crate recycling on the device: for every player with pending lost
  * attribute layers, drop min(lost, free cells) crates on distinct free cells

@@ -1292,3 +1292,245 @@ def flush_recycle(cfg, st, gen):
             crate[e, cells[perm]] = True
             rec[e, cells[perm]] = True
     st["pending_lost"][...] = 0
+
+
+# ------------------------------------------------ per-episode map generation
+#
+# The reference draws every new episode's level from its host generator
+# (BatchedSim.reset_, sim/torch_sim.py:178-420, with sim/mapgen.py).  The
+# engine's device reset draws the same quantities from a counter-based hash
+# keyed by (seed, env, episode, draw family, index), so that a reset needs
+# no host round trip.  `map_reset` builds the levels from a dict of per-env
+# draws in either form; it is pinned to the reference by feeding it the
+# draws the reference consumed (tests/golden/mapgen_fed.npz), and the device
+# kernel is compared with it on `mapgen_draws_keyed`.
+
+MG_KIND, MG_OBST_N, MG_OBST_KEY, MG_RING, MG_TOP, MG_VSEG, MG_HSEG, MG_HAZARD = range(1, 9)
+
+
+def _mg_hash(seed, envs, episode, fam, index):
+    """SplitMix64 finaliser of (seed ^ e << 32 ^ episode ^ fam << 56) + index
+    -> 24-bit integers, shape (n,) or (n, k) for an index vector."""
+    e = np.asarray(envs, dtype=np.int64).astype(np.uint64)
+    ep = np.asarray(episode, dtype=np.int64).astype(np.uint64)
+    with np.errstate(over="ignore"):
+        key = np.uint64(seed) ^ (e << np.uint64(32)) ^ ep ^ (np.uint64(fam) << np.uint64(56))
+        idx = np.asarray(index, dtype=np.int64).astype(np.uint64)
+        x = key[:, None] + idx[None, :] if idx.ndim else key + idx
+    return _u24(x)
+
+
+def mapgen_draws_keyed(cfg, seed, episode, envs=None):
+    """The device reset's per-env draws for each env's current episode:
+    uniforms u = k / 2^24 of 24-bit keys k, integer draws low + (k * range)
+    >> 24 (the stand-in for the generator's randint)."""
+    episode = np.asarray(episode, dtype=np.int64)
+    n = episode.shape[0]
+    envs = np.arange(n) if envs is None else np.asarray(envs)
+    C = cfg.height * cfg.width
+    unit = np.float32(1.0 / 16777216.0)
+
+    def u(fam, index=0):
+        return _mg_hash(seed, envs, episode, fam, index).astype(np.float32) * unit
+
+    return {
+        "kind_u": u(MG_KIND),
+        "obst_n": (_mg_hash(seed, envs, episode, MG_OBST_N, 0)
+                   * (cfg.open_obstacle_max + 1)) >> 24,
+        "obst_key": _mg_hash(seed, envs, episode, MG_OBST_KEY, np.arange(C)),
+        "ring_u": u(MG_RING, np.arange(C)),
+        "top": (_mg_hash(seed, envs, episode, MG_TOP, 0) * (cfg.top_wall_rows + 1)) >> 24,
+        "vstart_u": u(MG_VSEG, 3 * np.arange(4)),
+        "vlen_u": u(MG_VSEG, 3 * np.arange(4) + 1),
+        "vact_u": u(MG_VSEG, 3 * np.arange(4) + 2),
+        "hstart_u": u(MG_HSEG, 0), "hlen_u": u(MG_HSEG, 1), "hact_u": u(MG_HSEG, 2),
+        "swap_u": template_swap_draws_u(seed, episode, envs),
+        "hazard_u": u(MG_HAZARD),
+    }
+
+
+def template_swap_draws_u(seed, episode, envs=None):
+    """The spawn-swap uniform of template_swap_draws (swap when < 0.5)."""
+    ep = np.asarray(episode, dtype=np.int64).astype(np.uint64)
+    e = (np.arange(ep.shape[0]) if envs is None else np.asarray(envs)).astype(np.uint64)
+    return _splitmix_unit(np.uint64(seed) ^ (e << np.uint64(32)) ^ ep)
+
+
+def _clear4(mask, cells, h, w):
+    for r, c in cells:
+        mask[r, c] = False
+        for dr, dc in DIRS4:
+            if 0 <= r + dr < h and 0 <= c + dc < w:
+                mask[r + dr, c + dc] = False
+
+
+def _open_spawn_pos(cfg):
+    h, w = float(cfg.height), float(cfg.width)
+    row = (h - 1) / 2.0 + 0.5
+    return np.array([(row, (w - 1) * (i + 1) / (cfg.n_players + 1) + 0.5)
+                     for i in range(cfg.n_players)], dtype=F32)
+
+
+def _open_cross(cfg):
+    """Cross-band crate cells of an open map (sim/torch_sim.py:465-506)."""
+    h, w = cfg.height, cfg.width
+    near = set()
+    for y, x in _open_spawn_pos(cfg):
+        r, c = int(y), int(x)
+        near.add((r, c))
+        for dr, dc in DIRS4:
+            if 0 <= r + dr < h and 0 <= c + dc < w:
+                near.add((r + dr, c + dc))
+    cy, cx = (h - 1) // 2, (w - 1) // 2
+    cross = {(r, c) for c in range(w) for r in (cy - 1, cy)} \
+        | {(r, c) for r in range(h) for c in (cx - 1, cx)}
+    return sorted(cross - near)
+
+
+def _opp_start(cfg, boost, b0, z0, s0):
+    """Seat-1 start attributes by opponent boost tier (sim/torch_sim.py:433-453):
+    0 = seat 0's, 1 = x opp_hist_mult rounded (half to even) and capped, 2 =
+    the opp_growth_* constants; float32 arithmetic."""
+    m = F32(cfg.opp_hist_mult)
+    if boost == 2:
+        return int(cfg.opp_growth_bombs), int(cfg.opp_growth_blast), F32(cfg.opp_growth_speed)
+    if boost == 1:
+        b = min(np.rint(F32(b0) * m), F32(cfg.growth_bombs_max))
+        z = min(np.rint(F32(z0) * m), F32(cfg.growth_blast_max))
+        s = min(F32(s0) * m, F32(cfg.growth_speed_max))
+        return int(b), int(z), F32(s)
+    return int(b0), int(z0), F32(s0)
+
+
+def map_reset(cfg, st, mask, dr, opp_boost=None, aux=None):
+    """Reset the envs in `mask` to new levels built from the draws `dr`
+    (mapgen_draws_keyed's keys), in place: the reference's reset_
+    (sim/torch_sim.py:178-420) with sim/mapgen.py's make_walls (:15-62),
+    make_open_obstacles (:65-95), make_bricks (:98-194), make_ring_bricks
+    (:197-227) and make_ring_walls (:230-242).  opp_boost: (N,) tier per env
+    (default 0).  aux: optional dict receiving "is_open" (N,) bool and
+    "map_kind" (N,) int64 (1 open, 2 ring, 0 corridor)."""
+    h, w, p = cfg.height, cfg.width, cfg.n_players
+    corridor = cfg.map_mode == "corridor"
+    rows = np.arange(h)[:, None]
+    cols = np.arange(w)[None, :]
+    c0 = (w - cfg.corridor_width) // 2
+    c1 = c0 + cfg.corridor_width
+    T = cfg.top_wall_rows
+    edge = [c for c in (c0, c0 + 1, c1 - 2, c1 - 1) if c0 <= c < c1]
+    r0 = (h - cfg.ring_center_h) // 2
+    q0 = (w - cfg.ring_center_w) // 2
+    r1, q1 = r0 + cfg.ring_center_h, q0 + cfg.ring_center_w
+    cross = _open_cross(cfg)
+    spawn = {"corr": np.array(cfg.spawn_pos(), F32), "open": _open_spawn_pos(cfg),
+             "ring": np.array(cfg.ring_spawns(), F32)}
+    t_pure = F32(cfg.pure_open_fraction)
+    t_open = F32(cfg.pure_open_fraction + cfg.open_fraction)
+    t_ring = F32(cfg.pure_open_fraction + cfg.open_fraction + cfg.ring_fraction)
+    dens = F32(cfg.wall_density)
+    for e in np.nonzero(np.asarray(mask, bool))[0]:
+        if corridor:
+            r = F32(dr["kind_u"][e])
+            kind = "pure" if r < t_pure else ("open" if r < t_open else
+                                               ("ring" if r < t_ring else "corr"))
+        else:
+            kind = "openmode"
+        wall = np.zeros((h, w), bool)
+        brick = np.zeros((h, w), bool)
+        if kind in ("pure", "open", "openmode"):
+            k = cfg.open_obstacle_max
+            if k > 0:
+                key = np.asarray(dr["obst_key"][e])
+                order = np.argsort(key, kind="stable")[:k]
+                for cell in order[: int(dr["obst_n"][e])]:
+                    wall[min(cell // w, h - 1), min(cell % w, w - 1)] = True
+                _clear4(wall, cfg.spawn_cells(), h, w)
+            if kind == "pure":
+                wall[:] = False
+        elif kind == "ring":
+            wall[r0:r1, q0:q1] = True
+            band = np.zeros((h, w), bool)
+            band[r0 - 1:r1 + 1, q0 - 1:q1 + 1] = True
+            band[r0:r1, q0:q1] = False
+            brick = band & (np.asarray(dr["ring_u"][e], F32).reshape(h, w) < F32(cfg.ring_brick_density))
+            _clear4(brick, cfg.ring_spawn_cells(), h, w)
+        else:
+            top = int(dr["top"][e]) if cfg.random_wall_rows else None
+            if top is not None:
+                bot = T - top
+                wall = np.broadcast_to((rows < top) | (rows >= h - bot), (h, w)).copy()
+                brick = ((cols < c0) | (cols >= c1)) & ~(rows < top)
+            else:
+                wall[:T] = True
+                brick = ((cols < c0) | (cols >= c1)) & ~(rows < T)
+            _clear4(wall, cfg.spawn_cells(), h, w)
+            if cfg.wall_density > 0:
+                if top is None:
+                    span, base = F32(h - T - 4), F32(T)
+                else:
+                    span, base = F32(max(h - (T - top) - 4 - top, 1)), F32(top)
+                for i, col in enumerate(edge):
+                    start = int(F32(F32(dr["vstart_u"][e][i]) * span) + base)
+                    ln = 2 + int(F32(dr["vlen_u"][e][i]) * F32(3.0))
+                    if F32(dr["vact_u"][e][i]) < dens:
+                        brick[max(start, 0):max(start + ln, 0), col] = True
+                if c1 - c0 > 4:
+                    hs = int(F32(F32(dr["hstart_u"][e]) * F32(c1 - c0 - 4)) + F32(c0))
+                    hl = 2 + int(F32(dr["hlen_u"][e]) * F32(3.0))
+                    if F32(dr["hact_u"][e]) < dens:
+                        band_rows = range(T, T + min(2, h - T)) if top is None else (top, top + 1)
+                        seg = (np.arange(c0, c1) >= hs) & (np.arange(c0, c1) < hs + hl)
+                        for rr in band_rows:
+                            brick[rr, c0:c1] |= seg
+            _clear4(brick, cfg.spawn_cells(), h, w)
+        st["wall"][e] = wall
+        st["brick"][e] = brick
+        # start attributes of seats 0 and 1 (other seats keep theirs)
+        if kind == "openmode":
+            b0, z0, s0 = int(cfg.max_bombs), int(cfg.blast), F32(1.0)
+        elif kind in ("pure", "open"):
+            b0, z0, s0 = int(cfg.open_growth_bombs), int(cfg.open_growth_blast), F32(cfg.open_growth_speed)
+        else:
+            b0, z0, s0 = (int(cfg.growth_bombs_start), int(cfg.growth_blast_start),
+                          F32(cfg.growth_speed_start))
+        bo = 0 if opp_boost is None else int(opp_boost[e])
+        caps = [(b0, z0, s0), _opp_start(cfg, bo, b0, z0, s0)]
+        for pl, (bb, zz, ss) in enumerate(caps[:p]):
+            st["bombs_cap"][e, pl] = st["lo_bombs"][e, pl] = bb
+            st["blast_cap"][e, pl] = st["lo_blast"][e, pl] = zz
+            st["spd_g"][e, pl] = st["lo_spd"][e, pl] = ss
+        if corridor:
+            st["crate_prob"][e] = {"pure": F32(1.0), "open": F32(1.0), "ring": F32(cfg.ring_crate_prob),
+                                   "corr": F32(cfg.growth_crate_prob)}[kind]
+        sp = spawn["corr" if kind == "corr" else ("ring" if kind == "ring" else "open")]
+        pos = sp.copy()
+        if F32(dr["swap_u"][e]) < F32(0.5) and p >= 2:
+            pos[[0, 1]] = pos[[1, 0]]
+        st["pos"][e] = pos
+        st["crate"][e] = False
+        if corridor and cfg.open_crate_cross and kind in ("pure", "open"):
+            for rr, cc in cross:
+                st["crate"][e, rr, cc] = True
+        st["recycle"][e] = False
+        st["pending_lost"][e] = 0
+        st["combo"][e] = 0
+        st["last_hit"][e] = -10 ** 9
+        st["fuse"][e] = 0
+        st["owner"][e] = -1
+        st["bomb_blast"][e] = 0
+        st["alive"][e] = True
+        st["hp"][e] = cfg.max_hp
+        st["since_bomb"][e] = cfg.place_dist_cooldown
+        st["invuln"][e] = 0
+        st["t"][e] = 0
+        if cfg.hazard_fraction > 0:
+            hz = F32(dr["hazard_u"][e]) < F32(cfg.hazard_fraction)
+            st["hazard"][e] = hz
+            if hz:
+                st["bombs_cap"][e] = 0
+        else:
+            st["hazard"][e] = False
+        if aux is not None:
+            aux["is_open"][e] = corridor and kind in ("pure", "open")
+            aux["map_kind"][e] = {"openmode": 1, "pure": 1, "open": 1, "ring": 2, "corr": 0}[kind]
+    return st

@@ -2,6 +2,7 @@
 // word and helpers are shared without relocatable device code.
 #include "sim_observe.cu"
 #include "sim_step.cu"
+#include "sim_reset.cu"
 #include "policy_mlp.cu"
 #include "policy_cnn.cu"
 #include "train_gae.cu"

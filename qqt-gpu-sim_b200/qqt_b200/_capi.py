@@ -56,6 +56,27 @@ class QqtTemplate(ctypes.Structure):
                 ("episode", c_p)]
 
 
+MG_WORDS = 14
+
+
+class QqtMapGen(ctypes.Structure):
+    _fields_ = [("seed", c_u64), ("episode", c_p), ("opp_boost", c_p), ("is_open", c_p),
+                ("map_kind", c_p), ("corridor_mode", c_i32), ("cut_pure", c_f32),
+                ("cut_open", c_f32), ("cut_ring", c_f32), ("obst_max", c_i32),
+                ("random_wall_rows", c_i32), ("top_wall_rows", c_i32), ("corr_c0", c_i32),
+                ("corr_c1", c_i32), ("n_edge", c_i32), ("edge_cols", c_i32 * 4),
+                ("wall_density", c_f32), ("ring_density", c_f32), ("hazard_fraction", c_f32),
+                ("ring_r0", c_i32), ("ring_r1", c_i32), ("ring_c0", c_i32), ("ring_c1", c_i32),
+                ("open_cross", c_i32), ("start_bombs", c_i64 * 3), ("start_blast", c_i64 * 3),
+                ("start_spd", c_f32 * 3), ("crate_prob_kind", c_f32 * 3),
+                ("opp_bombs2", c_i64), ("opp_blast2", c_i64), ("opp_spd2", c_f32),
+                ("opp_mult", c_f32), ("bombs_max", c_i64), ("blast_max", c_i64),
+                ("spd_max", c_f32), ("spawn", ((c_f32 * 2) * 4) * 3),
+                ("clear_spawn", ctypes.c_uint32 * MG_WORDS),
+                ("clear_ring", ctypes.c_uint32 * MG_WORDS),
+                ("cross", ctypes.c_uint32 * MG_WORDS)]
+
+
 class QqtStepOut(ctypes.Structure):
     _fields_ = [("reward", c_p), ("done", c_p), ("died", c_p), ("winner", c_p),
                 ("n_alive", c_p), ("covered", c_p), ("triggered", c_p), ("reset_mask", c_p),
@@ -96,6 +117,8 @@ def lib():
             "qqt_greedy_act": (c_i32, [P(QqtCfg), P(QqtState), c_p, c_p, c_i32, c_p, c_i32,
                                        c_i32, c_p, c_p, c_i32, c_p]),
             "qqt_flush_recycle": (c_i32, [P(QqtCfg), P(QqtState), c_p, c_u64, c_u64, c_p]),
+            "qqt_map_reset": (c_i32, [P(QqtCfg), P(QqtState), P(QqtMapGen), c_p, c_p, c_p, c_p,
+                                      c_p]),
             "qqt_gae": (c_i32, [c_p, c_i32, c_p, c_p, c_i32, c_p, c_i32, c_i32, ctypes.c_double,
                                 ctypes.c_double, c_p, c_p, c_p]),
             "qqt_local_view": (c_i32, [P(QqtCfg), P(QqtState), c_p, c_i32, c_i32, c_p, c_p, c_p,

@@ -109,7 +109,13 @@ class B200Sim:
     """Drop-in for `sim.torch_sim.BatchedSim` backed by libqqt_b200.so."""
 
     def __init__(self, cfg: SimConfig, num_envs: int, device: str | torch.device = "cuda",
-                 seed: int = 0, template: dict | None = None) -> None:
+                 seed: int = 0, template: dict | None = None, map_reset: str = "host") -> None:
+        """map_reset: "host" builds every new episode's level on the host
+        generator in the reference's draw order (bit-compatible with a
+        reference BatchedSim of the same seed); "device" builds it on the GPU
+        from counter-based draws (qqt_map_reset), so resets -- the initial one
+        included -- never return to the host.  A template (set_template)
+        replaces both with a fixed per-env level."""
         self.cfg = cfg
         self.num_envs = n = int(num_envs)
         self.device = torch.device(device)
@@ -167,11 +173,16 @@ class B200Sim:
         nb = int(capi.lib().qqt_step_scratch_bytes(ctypes.byref(self._ccfg)))
         self._step_scratch = torch.zeros((max(nb, 256),), dtype=torch.uint8, device=d)
         self._tmpl = None
+        self._mapgen = None
         self._cstate = self._make_cstate()
         self._cout = self._make_cout()
+        if map_reset not in ("host", "device"):
+            raise ValueError("map_reset is 'host' or 'device'")
         if template is not None:
             self.set_template(template, apply=True)
         else:
+            if map_reset == "device":
+                self.enable_device_map_reset(seed)
             self.reset_all()
 
     # ------------------------------------------------------------ views
@@ -246,6 +257,25 @@ class B200Sim:
         if apply:
             self._apply_template(torch.ones(n, dtype=torch.bool, device=d))
 
+    def enable_device_map_reset(self, seed: int = 0) -> None:
+        """Generate each ended episode's next level on the device (the
+        reference's reset_, sim/torch_sim.py:178-420, with counter-based
+        draws keyed by (seed, env, episode)): `reset_`, `reset_all` and
+        `step(auto_reset=True)` then run qqt_map_reset and never synchronise
+        the host.  Installing a template afterwards takes precedence."""
+        cfg, n, d = self.cfg, self.num_envs, self.device
+        if cfg.n_players > 4:
+            raise ValueError("device level generation supports up to 4 players")
+        self._mg_episode = torch.zeros((n,), dtype=torch.int64, device=d)
+        self._mapgen = _make_mapgen(cfg, seed, self._mg_episode, self._buf["_opp_boost"],
+                                    self._buf["_is_open"], self._buf["_map_kind"])
+
+    def _device_map_reset(self, done: torch.Tensor, rows=None, mm=None, bm=None) -> None:
+        capi.check(capi.lib().qqt_map_reset(
+            ctypes.byref(self._ccfg), ctypes.byref(self._cstate), ctypes.byref(self._mapgen),
+            done.data_ptr(), capi.ptr(rows), capi.ptr(mm), capi.ptr(bm), self._stream()),
+            "qqt_map_reset")
+
     def _apply_template(self, mask: torch.Tensor) -> None:
         tm, b = self._tmpl_buf, self._buf
         idx = mask.nonzero(as_tuple=True)[0]
@@ -306,6 +336,10 @@ class B200Sim:
         instead (the benchmark configurations)."""
         if self._tmpl is not None:
             self._apply_template(mask.to(self.device))
+            return
+        if self._mapgen is not None:
+            flags = mask.to(self.device, torch.bool).contiguous().view(torch.uint8)
+            self._device_map_reset(flags)
             return
         cfg, b, d = self.cfg, self._buf, self.device
         idx_cpu = mask.detach().to("cpu").nonzero(as_tuple=True)[0]
@@ -373,12 +407,15 @@ class B200Sim:
                 cprob[is_corr] = cfg.growth_crate_prob
             put("wall", idx, wall.reshape(count, hw).to(d))
             put("brick", idx, brick.reshape(count, hw).to(d))
-            b["bombs_cap"][:, idx] = bcap.t().to(d)
-            b["blast_cap"][:, idx] = zcap.t().to(d)
-            b["spd_g"][:, idx] = scap.t().to(d)
-            b["_lo_bombs"][:, idx] = bcap.t().to(d)
-            b["_lo_blast"][:, idx] = zcap.t().to(d)
-            b["_lo_spd"][:, idx] = scap.t().to(d)
+            # seats 0 and 1 only: the reference's reset_ leaves the start
+            # attributes of any further seat as they were
+            q = min(p, 2)
+            b["bombs_cap"][:q, idx] = bcap[:, :q].t().to(d)
+            b["blast_cap"][:q, idx] = zcap[:, :q].t().to(d)
+            b["spd_g"][:q, idx] = scap[:, :q].t().to(d)
+            b["_lo_bombs"][:q, idx] = bcap[:, :q].t().to(d)
+            b["_lo_blast"][:q, idx] = zcap[:, :q].t().to(d)
+            b["_lo_spd"][:q, idx] = scap[:, :q].t().to(d)
             b["crate_prob"][idx] = cprob.to(d)
             b["_map_kind"][idx] = kind.to(d)
             b["_is_open"][idx] = opn.to(d)
@@ -558,7 +595,8 @@ class B200Sim:
             rb_hit, rb_grow = crate_draws if crate_draws is not None else self._crate_draws()
             rb_hit = rb_hit.to(self.device, torch.float32).contiguous()
             rb_grow = rb_grow.to(self.device, torch.float32).contiguous()
-        dev_reset = auto_reset and self._tmpl is not None
+        dev_reset = auto_reset and (self._tmpl is not None or self._mapgen is not None)
+        map_reset = dev_reset and self._tmpl is None
         if self.cfg.hazard_fraction > 0:
             if self.hazard_seed is not None:
                 hs = int(self.hazard_seed)
@@ -576,21 +614,25 @@ class B200Sim:
             for m in (nmm, nbm):
                 if m.dtype != torch.bool or not m.is_contiguous():
                     raise ValueError("next_obs masks must be contiguous bool tensors")
+            tmpl = ctypes.byref(self._tmpl) if dev_reset and not map_reset else None
             rc = capi.lib().qqt_step_observe(
                 ctypes.byref(self._ccfg), ctypes.byref(self._cstate), acts.data_ptr(),
                 capi.ptr(rb_hit), capi.ptr(rb_grow), self._tiers.data_ptr(), int(self._first_step),
-                ctypes.byref(cout), ctypes.byref(self._tmpl) if dev_reset else None,
-                self._step_scratch.data_ptr(), rows.data_ptr(), nmm.data_ptr(), nbm.data_ptr(),
-                self._stream())
+                ctypes.byref(cout), tmpl, self._step_scratch.data_ptr(), rows.data_ptr(),
+                nmm.data_ptr(), nbm.data_ptr(), self._stream())
             capi.check(rc, "qqt_step_observe")
+            if map_reset:
+                self._device_map_reset(done, rows, nmm, nbm)
         else:
+            tmpl = ctypes.byref(self._tmpl) if dev_reset and not map_reset else None
             rc = capi.lib().qqt_step(ctypes.byref(self._ccfg), ctypes.byref(self._cstate),
                                      acts.data_ptr(), capi.ptr(rb_hit), capi.ptr(rb_grow),
                                      self._tiers.data_ptr(), int(self._first_step),
-                                     ctypes.byref(cout),
-                                     ctypes.byref(self._tmpl) if dev_reset else None,
-                                     self._step_scratch.data_ptr(), self._stream())
+                                     ctypes.byref(cout), tmpl, self._step_scratch.data_ptr(),
+                                     self._stream())
             capi.check(rc, "qqt_step")
+            if map_reset:
+                self._device_map_reset(done)
         self._first_step = False
         n, h, w = self.num_envs, self.cfg.height, self.cfg.width
         info = {"n_alive": self._n_alive, "died": self._died, "winner": self._winner, "hit": hit,
@@ -665,7 +707,7 @@ class B200Sim:
         (crates block neither movement nor flames), so they equal a fresh
         observe() afterwards."""
         if on_device is None:
-            on_device = self._tmpl is not None
+            on_device = self._tmpl is not None or self._mapgen is not None
         if on_device:
             self._flush_count = getattr(self, "_flush_count", 0) + 1
             words = (ctypes.c_uint32 * 14)(*self._excl_words())
@@ -770,6 +812,81 @@ def _make_prop(key):
 
 for _k in list(_PLANES) + list(_PLAYER) + ["pos"] + list(_ENV):
     setattr(B200Sim, _k, _make_prop(_k))
+
+
+def _cell_bits(cells, w: int) -> list[int]:
+    words = [0] * capi.MG_WORDS
+    for r, c in cells:
+        i = r * w + c
+        words[i >> 5] |= 1 << (i & 31)
+    return words
+
+
+def _with_neighbours(cells, h: int, w: int):
+    out = set()
+    for r, c in cells:
+        out.add((r, c))
+        for dr, dc in mapgen.DIRS4:
+            if 0 <= r + dr < h and 0 <= c + dc < w:
+                out.add((r + dr, c + dc))
+    return sorted(out)
+
+
+def _make_mapgen(cfg, seed, episode, opp_boost, is_open, map_kind) -> capi.QqtMapGen:
+    """The level generator's parameters for qqt_map_reset (sim/config.py
+    fields, the reference's reset_ geometry): thresholds as the float32
+    values the reference compares against, spawn positions, and the cell
+    sets that stay fixed between episodes."""
+    g = capi.QqtMapGen()
+    h, w, p = cfg.height, cfg.width, cfg.n_players
+    g.seed = int(seed) & ((1 << 64) - 1)
+    g.episode = episode.data_ptr()
+    g.opp_boost = opp_boost.data_ptr()
+    g.is_open = is_open.data_ptr()
+    g.map_kind = map_kind.data_ptr()
+    g.corridor_mode = int(cfg.map_mode == "corridor")
+    pf, of, rf = cfg.pure_open_fraction, cfg.open_fraction, cfg.ring_fraction
+    g.cut_pure, g.cut_open, g.cut_ring = pf, pf + of, pf + of + rf
+    g.obst_max = int(cfg.open_obstacle_max)
+    g.random_wall_rows = int(cfg.random_wall_rows)
+    g.top_wall_rows = int(cfg.top_wall_rows)
+    c0 = (w - cfg.corridor_width) // 2
+    c1 = c0 + cfg.corridor_width
+    g.corr_c0, g.corr_c1 = c0, c1
+    edge = [c for c in (c0, c0 + 1, c1 - 2, c1 - 1) if c0 <= c < c1]
+    g.n_edge = len(edge)
+    for i, c in enumerate(edge):
+        g.edge_cols[i] = c
+    g.wall_density = cfg.wall_density
+    g.ring_density = cfg.ring_brick_density
+    g.hazard_fraction = cfg.hazard_fraction
+    r0 = (h - cfg.ring_center_h) // 2
+    q0 = (w - cfg.ring_center_w) // 2
+    g.ring_r0, g.ring_r1 = r0, r0 + cfg.ring_center_h
+    g.ring_c0, g.ring_c1 = q0, q0 + cfg.ring_center_w
+    g.open_cross = int(cfg.open_crate_cross)
+    starts = [(cfg.growth_bombs_start, cfg.growth_blast_start, cfg.growth_speed_start),
+              (cfg.open_growth_bombs, cfg.open_growth_blast, cfg.open_growth_speed),
+              (cfg.max_bombs, cfg.blast, 1.0)]
+    for i, (b, z, sp) in enumerate(starts):
+        g.start_bombs[i], g.start_blast[i], g.start_spd[i] = int(b), int(z), float(sp)
+    for i, cp in enumerate((cfg.growth_crate_prob, 1.0, cfg.ring_crate_prob)):
+        g.crate_prob_kind[i] = cp
+    g.opp_bombs2, g.opp_blast2 = int(cfg.opp_growth_bombs), int(cfg.opp_growth_blast)
+    g.opp_spd2, g.opp_mult = cfg.opp_growth_speed, cfg.opp_hist_mult
+    g.bombs_max, g.blast_max = int(cfg.growth_bombs_max), int(cfg.growth_blast_max)
+    g.spd_max = cfg.growth_speed_max
+    for k, pos in enumerate((cfg.spawn_pos(), mapgen.open_spawns(cfg), cfg.ring_spawns())):
+        for i in range(p):
+            g.spawn[k][i][0], g.spawn[k][i][1] = float(pos[i][0]), float(pos[i][1])
+    for name, cells in (("clear_spawn", _with_neighbours(cfg.spawn_cells(), h, w)),
+                        ("clear_ring", _with_neighbours(cfg.ring_spawn_cells(), h, w)),
+                        ("cross", mapgen.open_cross_cells(cfg))):
+        words = _cell_bits(cells, w)
+        arr = getattr(g, name)
+        for i, v in enumerate(words):
+            arr[i] = v
+    return g
 
 
 def _recycle_exclusion(cfg) -> list[int]:

@@ -30,6 +30,7 @@ Outputs (compressed npz, all env-major like the reference tensors):
   ckpt_adapt.npz   adapt_first_conv on seeded models (2 <-> 3 players), and
   ref_ckpt_mlp.pt  a checkpoint written by the reference's save_ckpt
   ckpt_adapt_lstm.npz  adapt_first_conv on the LSTM architecture
+  mapgen_fed.npz   per-episode level generation (reset_) with recorded draws
 """
 
 from __future__ import annotations
@@ -593,6 +594,160 @@ def ckpt_lstm_golden(R):
     return out
 
 
+class FedDraws:
+    """Stand-in for `torch` inside sim/torch_sim.py and sim/mapgen.py during
+    reset_: rand / randint come from recorded 24-bit integer keys k (rand =
+    k / 2^24 as float32; randint = low + (k * (high - low)) >> 24), logged in
+    call order; a (count, H*W) rand (the obstacle permutation keys) gets
+    distinct keys per row, so its argsort has no ties."""
+
+    def __init__(self, real, rng, cells):
+        self._real, self._rng, self._cells = real, rng, cells
+        self.log = []
+
+    def rand(self, *size, generator=None, device=None, dtype=None, **kw):
+        shape = tuple(size[0]) if len(size) == 1 and isinstance(size[0], (tuple, list)) \
+            else tuple(size)
+        if len(shape) == 2 and shape[1] == self._cells:
+            k = np.stack([self._rng.choice(1 << 24, size=shape[1], replace=False)
+                          for _ in range(shape[0])]) if shape[0] else np.zeros(shape, np.int64)
+        else:
+            k = self._rng.integers(0, 1 << 24, size=shape)
+        self.log.append(("rand", k.astype(np.int64)))
+        return self._real.from_numpy(k.astype(np.float32) * np.float32(1.0 / 16777216.0))
+
+    def randint(self, low, high, size, generator=None, device=None, **kw):
+        k = self._rng.integers(0, 1 << 24, size=size).astype(np.int64)
+        self.log.append(("randint", k))
+        return self._real.from_numpy(low + ((k * (high - low)) >> 24))
+
+    def __getattr__(self, name):
+        return getattr(self._real, name)
+
+
+def _route_mapgen_draws(cfg, n, idx, log):
+    """Per-env draw arrays (the oracle's map_reset keys) from the calls the
+    reference's reset_ made, in its call order (sim/torch_sim.py:178-420)."""
+    h, w = cfg.height, cfg.width
+    C = h * w
+    unit = np.float32(1.0 / 16777216.0)
+    d = {"kind_u": np.zeros(n, np.float32), "obst_n": np.zeros(n, np.int64),
+         "obst_key": np.zeros((n, C), np.int64), "ring_u": np.zeros((n, C), np.float32),
+         "top": np.zeros(n, np.int64), "vstart_u": np.zeros((n, 4), np.float32),
+         "vlen_u": np.zeros((n, 4), np.float32), "vact_u": np.zeros((n, 4), np.float32),
+         "hstart_u": np.zeros(n, np.float32), "hlen_u": np.zeros(n, np.float32),
+         "hact_u": np.zeros(n, np.float32), "swap_u": np.zeros(n, np.float32),
+         "hazard_u": np.zeros(n, np.float32)}
+    calls = list(log)
+    pop = lambda: calls.pop(0)  # noqa: E731
+    nmax = cfg.open_obstacle_max
+    if cfg.map_mode == "corridor":
+        r = pop()[1].astype(np.float32) * unit
+        d["kind_u"][idx] = r
+        pf = np.float32(cfg.pure_open_fraction)
+        po = np.float32(cfg.pure_open_fraction + cfg.open_fraction)
+        pr = np.float32(cfg.pure_open_fraction + cfg.open_fraction + cfg.ring_fraction)
+        opn = r < po
+        ring = ~opn & (r < pr)
+        corr = ~(opn | ring)
+        assert (r < pf).sum() <= opn.sum()
+        if opn.any() and nmax > 0:
+            k = pop()[1]
+            d["obst_n"][idx[opn]] = (k * (nmax + 1)) >> 24
+            d["obst_key"][idx[opn]] = pop()[1]
+        if ring.any():
+            d["ring_u"][idx[ring]] = pop()[1].reshape(-1, C).astype(np.float32) * unit
+        if corr.any():
+            ci = idx[corr]
+            if cfg.random_wall_rows:
+                d["top"][ci] = (pop()[1] * (cfg.top_wall_rows + 1)) >> 24
+            if cfg.wall_density > 0:
+                c0 = (w - cfg.corridor_width) // 2
+                c1 = c0 + cfg.corridor_width
+                ne = len([c for c in (c0, c0 + 1, c1 - 2, c1 - 1) if c0 <= c < c1])
+                if ne:
+                    for key in ("vstart_u", "vlen_u", "vact_u"):
+                        d[key][ci, :ne] = pop()[1].astype(np.float32) * unit
+                if c1 - c0 > 4:
+                    for key in ("hstart_u", "hlen_u", "hact_u"):
+                        d[key][ci] = pop()[1].astype(np.float32) * unit
+    elif nmax > 0:
+        k = pop()[1]
+        d["obst_n"][idx] = (k * (nmax + 1)) >> 24
+        d["obst_key"][idx] = pop()[1]
+    d["swap_u"][idx] = pop()[1].astype(np.float32) * unit
+    if cfg.hazard_fraction > 0:
+        d["hazard_u"][idx] = pop()[1].astype(np.float32) * unit
+    assert not calls, f"unrouted draws: {[c[0] for c in calls]}"
+    return d
+
+
+def mapgen_golden(R):
+    """Per-episode level generation (sim/torch_sim.py:178-420, sim/mapgen.py)
+    run by the reference with its generator's draws fed and recorded: for
+    several configurations (mixed pure-open / open / ring / corridor maps,
+    random and fixed wall rows, edge brick segments, open obstacles, cross
+    crates, hazard envs, opponent boost tiers 0-2, two and three players, an
+    open-mode map), the state before and after reset_ of a random subset of
+    envs, and the draws routed per env (tests/test_oracle_golden.py replays
+    them through oracle.map_reset)."""
+    import torch
+    import sim.mapgen as rmg
+    ts = R["ts"]
+    SC = R["SimConfig"]
+    scen = [
+        ("mixed", dict(map_mode="corridor", pure_open_fraction=0.2, open_fraction=0.3,
+                       ring_fraction=0.2, random_wall_rows=True, wall_density=0.45,
+                       open_obstacle_max=6, hazard_fraction=0.3, speed=3.0), 64, 0),
+        ("fixed_rows", dict(map_mode="corridor", open_fraction=0.25, ring_fraction=0.25,
+                            random_wall_rows=False, wall_density=0.25, open_obstacle_max=3,
+                            speed=3.0), 48, 1),
+        ("three_players", dict(map_mode="corridor", n_players=3, open_fraction=0.3,
+                               ring_fraction=0.3, wall_density=0.45, open_obstacle_max=4,
+                               speed=3.0), 48, 2),
+        ("open_mode", dict(map_mode="open", open_obstacle_max=5, hazard_fraction=0.2,
+                           speed=3.0), 40, 1),
+        ("corridor_11", dict(map_mode="corridor", height=11, width=11, corridor_width=5,
+                             top_wall_rows=3, open_fraction=0.2, ring_fraction=0.0,
+                             wall_density=0.45, speed=3.0), 40, 0),
+    ]
+    out = {}
+    names = []
+    for si, (name, kw, n, boost) in enumerate(scen):
+        cfg = SC(**kw)
+        sim = ts.BatchedSim(cfg, n, device="cpu", seed=50 + si)
+        rng = np.random.default_rng(900 + si)
+        boosts = rng.integers(0, 3, n) if boost else np.zeros(n, np.int64)
+        sim._opp_boost.copy_(torch.from_numpy(boosts))
+        mask = rng.random(n) < 0.7
+        pre = state_np(sim)
+        fed = FedDraws(torch, rng, cfg.height * cfg.width)
+        old = (ts.torch, rmg.torch)
+        ts.torch, rmg.torch = fed, fed
+        try:
+            sim.reset_(torch.from_numpy(mask))
+        finally:
+            ts.torch, rmg.torch = old
+        idx = np.nonzero(mask)[0]
+        draws = _route_mapgen_draws(cfg, n, idx, fed.log)
+        post = state_np(sim)
+        tag = f"s{si}"
+        names.append(name)
+        out[f"{tag}__cfg"] = np.array(json.dumps(kw))
+        out[f"{tag}__mask"] = mask
+        out[f"{tag}__boost"] = boosts.astype(np.int64)
+        for k, v in pre.items():
+            out[f"{tag}__pre_{k}"] = v
+        for k, v in post.items():
+            out[f"{tag}__post_{k}"] = v
+        out[f"{tag}__post_is_open"] = sim._is_open.numpy().copy()
+        out[f"{tag}__post_map_kind"] = sim._map_kind.numpy().copy()
+        for k, v in draws.items():
+            out[f"{tag}__draw_{k}"] = v
+    out["scenarios"] = np.array(names)
+    return out
+
+
 def hazard_golden(R):
     """Hazard wave placement (sim/torch_sim.py:1404-1466) run by the
     reference itself on seeded states, with its randint / rand / randperm
@@ -737,6 +892,7 @@ def main():
         "ppo_update": lambda: ppo_golden(R),
         "ckpt_adapt": lambda: ckpt_golden(R),
         "ckpt_adapt_lstm": lambda: ckpt_lstm_golden(R),
+        "mapgen_fed": lambda: mapgen_golden(R),
         "hazard_wave": lambda: hazard_golden(R),
         "local_view": lambda: local_view_golden(R),
     }

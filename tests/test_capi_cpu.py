@@ -49,3 +49,39 @@ def test_config_packing_float32_constants():
     assert np.float32(c.pen_speed) == np.float32(2 * 0.15)
     assert np.float32(c.h_minus_rad) == np.float32(13 - 0.3)
     assert c.corridor == 1 and c.combo_on == 1
+
+
+def test_ctypes_structs_match_the_c_header(tmp_path):
+    """The ctypes mirrors of the header's structs have the C compiler's
+    field offsets and sizes (gcc on include/qqt_b200.h)."""
+    import json
+    import shutil
+    import subprocess
+    from qqt_b200 import _capi
+    if shutil.which("gcc") is None:
+        import pytest
+        pytest.skip("no C compiler")
+    structs = {"QqtCfg": _capi.QqtCfg, "QqtState": _capi.QqtState,
+               "QqtTemplate": _capi.QqtTemplate, "QqtStepOut": _capi.QqtStepOut,
+               "QqtMapGen": _capi.QqtMapGen}
+    lines = ['#include <stddef.h>', '#include <stdio.h>', '#include "qqt_b200.h"',
+             'int main(void) {', 'printf("{");']
+    first = True
+    for name, cls in structs.items():
+        for f in [f[0] for f in cls._fields_] + ["__size__"]:
+            expr = f"sizeof({name})" if f == "__size__" else f"offsetof({name}, {f})"
+            sep = "" if first else ","
+            first = False
+            lines.append(f'printf("{sep}\\"{name}.{f}\\": %zu", (size_t)({expr}));')
+    lines += ['printf("}\\n");', "return 0; }"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)],
+                   check=True)
+    c = json.loads(subprocess.run([str(exe)], check=True, capture_output=True,
+                                  text=True).stdout)
+    for name, cls in structs.items():
+        for f in [f[0] for f in cls._fields_]:
+            assert getattr(cls, f).offset == c[f"{name}.{f}"], f"{name}.{f}"
+        assert ctypes.sizeof(cls) == c[f"{name}.__size__"], name

@@ -295,3 +295,49 @@ def test_template_swap_draws_are_keyed():
     assert 0.4 < (a != b).mean() < 0.6
     c = O.template_swap_draws(8, ep)
     assert (a != c).any()
+
+
+def test_map_reset_matches_the_reference_level_generator():
+    """oracle.map_reset, fed the draws the reference's reset_ consumed (its
+    generator replaced by recorded 24-bit keys), rebuilds exactly the
+    reference's post-reset state (sim/torch_sim.py:178-420, sim/mapgen.py):
+    every state key, is_open and map_kind, for reset and untouched envs, in
+    five configurations (mixed pure-open / open / ring / corridor maps with
+    random or fixed wall rows and edge brick segments, open obstacles, cross
+    crates, hazard envs, opponent boost tiers, three players, an open-mode
+    map, an 11 x 11 board)."""
+    import json
+    g = G.load("mapgen_fed")
+    kinds = set()
+    for si, name in enumerate(g["scenarios"]):
+        tag = f"s{si}"
+        cfg = SimConfig(**json.loads(str(g[f"{tag}__cfg"])))
+        st = {k: np.array(g[f"{tag}__pre_{k}"], copy=True) for k in G.STATE_KEYS}
+        mask = g[f"{tag}__mask"]
+        n = mask.shape[0]
+        dr = {k[len(tag) + 7:]: g[k] for k in g if k.startswith(f"{tag}__draw_")}
+        aux = {"is_open": np.zeros(n, bool), "map_kind": np.zeros(n, np.int64)}
+        pre_open = g[f"{tag}__post_is_open"].copy()
+        pre_kind = g[f"{tag}__post_map_kind"].copy()
+        aux["is_open"][~mask] = pre_open[~mask]
+        aux["map_kind"][~mask] = pre_kind[~mask]
+        O.map_reset(cfg, st, mask, dr, opp_boost=g[f"{tag}__boost"], aux=aux)
+        post = {k: g[f"{tag}__post_{k}"] for k in G.STATE_KEYS}
+        bad = G.compare_state(post, st)
+        assert not bad, f"{name}: state differs in {bad}"
+        assert np.array_equal(aux["is_open"], pre_open), f"{name}: is_open"
+        assert np.array_equal(aux["map_kind"], pre_kind), f"{name}: map_kind"
+        kinds |= set(aux["map_kind"][mask].tolist())
+    assert kinds == {0, 1, 2}, "corridor, open and ring levels all generated"
+
+
+def test_mapgen_keyed_draws_are_in_range():
+    cfg = SimConfig(map_mode="corridor", open_obstacle_max=6, top_wall_rows=4)
+    d = O.mapgen_draws_keyed(cfg, 123, np.arange(500) % 7)
+    assert d["obst_n"].min() >= 0 and d["obst_n"].max() == 6
+    assert d["top"].min() == 0 and d["top"].max() == 4
+    assert d["obst_key"].shape == (500, 169) and d["obst_key"].max() < (1 << 24)
+    for k in ("kind_u", "ring_u", "vstart_u", "hact_u", "swap_u", "hazard_u"):
+        assert 0.0 <= d[k].min() and d[k].max() < 1.0
+    again = O.mapgen_draws_keyed(cfg, 123, np.arange(500) % 7)
+    assert all(np.array_equal(d[k], again[k]) for k in d)
