@@ -147,8 +147,11 @@ def danger_map(fuse, wall, blast, brick, fuse_max: int, rounds_a: int) -> np.nda
         weight = cur
     else:
         weight = w
+    # stage B spreads the weights with walls zeroed (sim/blast.py:297: seed =
+    # weight * passable): a bomb on a wall cell casts no rays here, although
+    # in stage A it still raises the bombs its flame reaches
     seed = np.where(wall, F32(0.0), weight)
-    return np.maximum(seed, reach_max(weight)).astype(F32)
+    return np.maximum(seed, reach_max(seed)).astype(F32)
 
 
 # ------------------------------------------------------------- movement

@@ -379,10 +379,11 @@ struct DangerScratch {
 // bomb count.
 // Each round is a scatter: lane (front bomb, direction) walks its ray up to
 // its blast and raises the first bomb it meets (walls stop it, bricks end
-// it) with the front value.  That is the reference's per-bomb "nearest front
-// bomb per direction within its blast" gather: a bomb on a wall cell is
-// neither a source nor a target there (the wall test comes first), and it is
-// neither here, so the rounds and the values agree.
+// it) with the front value.  That is the reference's front propagation,
+// which shifts each front bomb's value outwards and masks it with the
+// passability of the cell it lands on, never of the cell it starts from: a
+// bomb on a wall cell (a player standing on an obstacle can place one) is a
+// source here as there, and never a target.
 // nb_known >= 0: s.bombs already holds the nb_known bomb cells.
 __device__ inline int danger_stage_a(const Env& v, const DangerScratch& s, float fuse_f,
                                      int default_blast, int rounds, int* max_b_out,
@@ -409,7 +410,7 @@ __device__ inline int danger_stage_a(const Env& v, const DangerScratch& s, float
     for (int i = lane; i < 4 * nb; i += 32) {
       const int f = s.bombs[i >> 2], d = i & 3;
       const float fv = s.front[f];
-      if (!(fv > 0.f) || v.wall[f]) continue;
+      if (!(fv > 0.f)) continue;
       const int bl = blast_of(v, f, default_blast);
       int rr = f / v.w, cc = f - rr * v.w;
       for (int k = 1; k <= bl; ++k) {
@@ -459,9 +460,10 @@ __device__ __forceinline__ float danger_at(const Env& v, const DangerScratch& s,
 // non-negative float), and a bomb or brick stops the ray after it.  A cell
 // thus receives exactly the bombs it would find as the first solid cell
 // within their blast when looking along each direction: the same set, and
-// max is exact, so the values are identical to the gather form.  A bomb on
-// a wall cell is never found by the gather (the wall test comes first), so
-// it casts no rays here, and wall cells stay 0.
+// max is exact, so the values are identical to the gather form.  The
+// reference spreads the weights with walls zeroed (seed = weight *
+// passable), so a bomb on a wall cell casts no rays here, and wall cells
+// stay 0.
 __device__ inline void danger_paint(const Env& v, const DangerScratch& s, int nb,
                                     int default_blast, float* out) {
   const int lane = lane_id();

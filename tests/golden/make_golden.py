@@ -31,6 +31,7 @@ Outputs (compressed npz, all env-major like the reference tensors):
   ref_ckpt_mlp.pt  a checkpoint written by the reference's save_ckpt
   ckpt_adapt_lstm.npz  adapt_first_conv on the LSTM architecture
   mapgen_fed.npz   per-episode level generation (reset_) with recorded draws
+  danger_walls.npz danger map and chain resolution with bombs on wall cells
 """
 
 from __future__ import annotations
@@ -371,6 +372,43 @@ def kat_states(R, ref_root):
         out["covered"].append(cov[0].numpy())
         out["triggered"].append(trig[0].numpy())
     return {k: np.stack([np.asarray(x) for x in v]) for k, v in out.items()}
+
+
+def danger_walls_golden(R):
+    """The reference's danger_map and resolve_explosions (sim/blast.py:43-317)
+    on seeded 13 x 13 states with interior walls and bricks and 10-24 bombs
+    per env placed on any cell, walls included (a player standing on a wall
+    cell can place a bomb there: an open map's obstacle may cover an open
+    spawn), some of them going off this tick (fuse 0, owner set)."""
+    import torch
+    cfg = R["SimConfig"](height=13, width=13, n_players=2, map_mode="corridor", speed=3.0)
+    n, h, w = 48, 13, 13
+    rng = np.random.default_rng(77)
+    wall = rng.random((n, h, w)) < 0.15
+    brick = ~wall & (rng.random((n, h, w)) < 0.15)
+    fuse = np.zeros((n, h, w), np.int16)
+    owner = np.full((n, h, w), -1, np.int8)
+    blast = np.zeros((n, h, w), np.int16)
+    for e in range(n):
+        k = int(rng.integers(10, 25))
+        cells = rng.choice(h * w, size=k, replace=False)
+        walled = np.flatnonzero(wall[e].reshape(-1))
+        if walled.size:                        # at least two bombs on wall cells
+            cells[:2] = rng.choice(walled, size=min(2, walled.size), replace=False)[:2] \
+                if walled.size >= 2 else np.repeat(walled, 2)[:2]
+        cells = np.unique(cells)
+        fuse.reshape(n, -1)[e, cells] = rng.integers(0, 31, size=cells.size)
+        owner.reshape(n, -1)[e, cells] = rng.integers(0, 2, size=cells.size)
+        blast.reshape(n, -1)[e, cells] = rng.integers(1, 6, size=cells.size)
+    T = {k: torch.from_numpy(v) for k, v in
+         dict(wall=wall, brick=brick, fuse=fuse, owner=owner, bomb_blast=blast).items()}
+    bmap = torch.where(T["bomb_blast"] > 0, T["bomb_blast"].long(), cfg.blast)
+    dng = R["danger_map"](T["fuse"], T["wall"], bmap, cfg.fuse, T["brick"], cfg.max_chain)
+    cov, trig = R["resolve"](T["fuse"], T["owner"], T["wall"], bmap, cfg.max_chain, T["brick"])
+    return {"wall": wall, "brick": brick, "fuse": fuse, "owner": owner, "bomb_blast": blast,
+            "danger": dng.numpy(), "covered": cov.numpy(), "triggered": trig.numpy(),
+            "max_chain": np.int64(cfg.max_chain), "fuse_max": np.int64(cfg.fuse),
+            "blast": np.int64(cfg.blast)}
 
 
 def stress(R, cfg, n, seed):
@@ -893,6 +931,7 @@ def main():
         "ckpt_adapt": lambda: ckpt_golden(R),
         "ckpt_adapt_lstm": lambda: ckpt_lstm_golden(R),
         "mapgen_fed": lambda: mapgen_golden(R),
+        "danger_walls": lambda: danger_walls_golden(R),
         "hazard_wave": lambda: hazard_golden(R),
         "local_view": lambda: local_view_golden(R),
     }

@@ -276,3 +276,32 @@ def test_step_instances_vs_oracle(shape):
         assert torch.equal(rows.view(torch.int16), ref_rows.view(torch.int16)), f"t={t}: rows"
         assert torch.equal(mm, ref_mm) and torch.equal(bm, ref_bm), f"t={t}: masks"
     assert exploded > 0
+
+
+def test_danger_and_chains_with_bombs_on_walls_gpu():
+    """Bombs on wall cells (tests/golden/danger_walls.npz, the reference's own
+    danger_map and resolve_explosions): the observe kernel's danger map, and
+    the step's flames and exploded bombs from the state one tick earlier
+    (every bomb's fuse one higher, so that the step's countdown lands on the
+    golden state), bit-exact."""
+    g = G.load("danger_walls")
+    cfg = SimConfig(height=13, width=13, n_players=2, map_mode="corridor", speed=3.0,
+                    chain_cap_rounds=int(g["max_chain"]))
+    n = g["wall"].shape[0]
+    sim = B200Sim(cfg, n, device="cuda", seed=0)
+    st = sim.numpy_state()
+    for k in ("wall", "brick", "fuse", "owner", "bomb_blast"):
+        st[k] = g[k].copy()
+    st["crate"][:] = False
+    sim.load_numpy_state(st)
+    sim.observe_and_mask()
+    assert np.array_equal(_np(sim.danger()), g["danger"])
+    bomb = (g["fuse"] > 0) | ((g["fuse"] == 0) & (g["owner"] >= 0))
+    st["fuse"] = np.where(bomb, g["fuse"] + 1, 0).astype(np.int16)
+    sim.load_numpy_state(st)
+    acts = torch.zeros((n, 2, 2), dtype=torch.int64, device="cuda")
+    acts[..., 0] = 4
+    rb = torch.zeros((n, 2), dtype=torch.float32, device="cuda")
+    _, _, info = sim.step(acts, auto_reset=False, crate_draws=(rb, rb))
+    assert np.array_equal(_np(info["blast"]), g["covered"])
+    assert np.array_equal(_np(info["trig"]), g["triggered"])

@@ -341,3 +341,20 @@ def test_mapgen_keyed_draws_are_in_range():
         assert 0.0 <= d[k].min() and d[k].max() < 1.0
     again = O.mapgen_draws_keyed(cfg, 123, np.arange(500) % 7)
     assert all(np.array_equal(d[k], again[k]) for k in d)
+
+
+def test_danger_and_chains_with_bombs_on_walls():
+    """Bombs on wall cells (a player standing on an obstacle can place one):
+    the reference's danger map spreads stage B from the weights with walls
+    zeroed, while stage A still lets such a bomb raise the bombs its flame
+    reaches; the oracle's danger map and chain resolution equal the
+    reference's on 48 seeded states (tests/golden/danger_walls.npz)."""
+    g = G.load("danger_walls")
+    assert int(((g["fuse"] > 0) & g["wall"]).sum()) > 50
+    bmap = O.blast_map(g["bomb_blast"], int(g["blast"]))
+    dng = O.danger_map(g["fuse"], g["wall"], bmap, g["brick"], int(g["fuse_max"]),
+                       int(g["max_chain"]))
+    assert np.array_equal(dng, g["danger"])
+    cov, trig = O.resolve_explosions(g["fuse"], g["owner"], g["wall"], bmap, g["brick"],
+                                     int(g["max_chain"]) - 1)
+    assert np.array_equal(cov, g["covered"]) and np.array_equal(trig, g["triggered"])
