@@ -485,7 +485,11 @@ def gpu_bench(args):
                        "parallelism": f"env shards x{world}, no rollout collective",
                        "l2": "flushed (256 MB write) between timed steps; each step also "
                              "writes its T x N observation buffer (> L2)",
-                       "cuda_graph": True},
+                       "cuda_graph": True,
+                       "draws": "value: sampling / bot / crate draws generated on the device "
+                                "before the timed region, copied device-to-device into the "
+                                "graph's draw buffers inside it; e2e: copied from pinned host "
+                                "memory inside the timed region"},
             "e2e": {"value": round(e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": _launches_per_rollout() * groups * args.steps,
