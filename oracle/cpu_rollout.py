@@ -155,17 +155,35 @@ class ShardPool:
             pr.start()
             self.conns.append(a)
             self.procs.append(pr)
-        for c in self.conns:
-            tag, _, _ = c.recv()
-            assert tag == "ready"
+        try:
+            for c, pr in zip(self.conns, self.procs):
+                tag, _, _ = self._recv(c, pr)
+                if tag != "ready":
+                    raise RuntimeError(f"oracle shard sent {tag!r} instead of ready")
+        except BaseException:
+            self.close()
+            raise
         self.n = n_per * procs
+
+    @staticmethod
+    def _recv(conn, proc, timeout: float = 900.0):
+        """The shard's next message; raises instead of waiting for good when
+        the process has died or stays silent past `timeout` seconds."""
+        import time as _t
+        end = _t.monotonic() + timeout
+        while not conn.poll(1.0):
+            if not proc.is_alive():
+                raise RuntimeError(f"oracle shard process exited with code {proc.exitcode}")
+            if _t.monotonic() > end:
+                raise RuntimeError("oracle shard process did not answer in time")
+        return conn.recv()
 
     def run(self, ticks: int):
         """Every shard plays `ticks` ticks at once; returns (env-steps,
         seconds of the slowest shard)."""
         for c in self.conns:
             c.send(ticks)
-        res = [c.recv() for c in self.conns]
+        res = [self._recv(c, pr) for c, pr in zip(self.conns, self.procs)]
         return sum(r[1] for r in res), max(r[2] for r in res)
 
     def close(self):
