@@ -184,9 +184,10 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
 // ------------------------------------------------------------ pack layout
 
 // Pack (bytes): [B fp16: 2 x NT x KP] [f32 params] [tail operand images]
+// [the same images as two row halves, for the SM-pair kernel]
 struct MlpPack {
   int kp, nt, n_seats;
-  size_t b_off, f_off, img_off, total;
+  size_t b_off, f_off, img_off, pair_off, total;
 };
 
 // Tail operand images (bytes from img_off), each 128-byte swizzled K-major,
@@ -218,7 +219,8 @@ __host__ __device__ inline MlpPack mlp_pack_layout(int k_in, int n_seats) {
   p.b_off = 0;
   p.f_off = ((size_t)2 * p.nt * p.kp * 2 + 255) / 256 * 256;
   p.img_off = (p.f_off + (size_t)F_TOTAL * 4 + 1023) / 1024 * 1024;
-  p.total = p.img_off + kImgBytes;
+  p.pair_off = p.img_off + kImgBytes;
+  p.total = p.pair_off + kImgBytes;
   return p;
 }
 
@@ -1099,6 +1101,8 @@ static int launch_mlp_fused(const CUtensorMap& ma, const CUtensorMap& malo, cons
 
 }  // namespace qqt
 
+#include "policy_pair.cu"
+
 using namespace qqt;
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -1203,6 +1207,7 @@ extern "C" int qqt_mlp_pack(const float* const* params, int32_t k_in, int32_t n_
   hp.cb2 = params[19];
   k_mlp_pack_rest<<<(128 * 128 + 255) / 256, 256, 0, st>>>(hp, n_seats, (float*)(pk + L.f_off));
   k_mlp_pack_images<<<(192 * 128 + 255) / 256, 256, 0, st>>>(hp, pk + L.img_off);
+  k_mlp_pack_pair_images<<<(192 * 128 + 255) / 256, 256, 0, st>>>(hp, pk + L.pair_off);
   return launch_status();
 }
 
@@ -1243,6 +1248,16 @@ extern "C" int qqt_mlp_act(const void* pack, const void* obs, int32_t n_envs, in
     io.mm[s] = s < n_seats ? mm[s] : nullptr;
     io.bm[s] = s < n_seats ? bm[s] : nullptr;
     io.act[s] = s < n_seats ? act[s] : nullptr;
+  }
+  const int m_tiles = (n_envs + kBM - 1) / kBM;
+  if (L.nt == 256 && mlp_pair_enabled() && mlp_split_k(m_tiles, k_tiles) == 1) {
+    // large two-seat batch: SM pairs, each CTA streaming half of the weights
+    CUtensorMap mbh;
+    if (!make_map(&mbh, pk + L.b_off, (uint64_t)L.kp, (uint64_t)2 * L.nt, (uint64_t)L.kp * 2,
+                  (uint32_t)(L.nt / 2)))
+      return QQT_E_ARG;
+    return launch_mlp_pair<256>(ma, mbh, n_envs, k_tiles, fpar, pk + L.pair_off, io, mm_stride,
+                                bm_stride, u, act_stride, logp, value, logits, st);
   }
   if (L.nt == 128)
     return launch_mlp_fused<128, false>(ma, ma, mb, n_envs, k_tiles, fpar, pk + L.img_off, io, 0,

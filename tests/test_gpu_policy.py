@@ -113,6 +113,37 @@ def test_mlp_ragged_tail_and_small_batch():
         assert _rel(logits[0, :, 7].cpu().numpy(), v) <= REL_TOL
 
 
+@pytest.mark.parametrize("n,seats", [(2100, (0, 1)), (2200, (0, 1)), (2433, (0, 1)),
+                                     (2100, (0,))])
+def test_mlp_pair_batches_with_ragged_pairs(n, seats):
+    # two-seat batches above 16 row tiles run on SM pairs: an odd tile count
+    # leaves the last pair's second CTA past the end, a ragged count cuts a
+    # tile (one seat: the single-CTA kernel at the same sizes)
+    cfg = SimConfig(**scenarios.CFG2)
+    p = 2
+    rng = np.random.default_rng(n)
+    obs16 = (rng.random((n,) + cfg.obs_shape) * (rng.random((n,) + cfg.obs_shape) < 0.3)
+             ).astype(np.float16)
+    mm = rng.random((n, p, 5)) < 0.8
+    mm[..., 4] = True
+    bm = rng.random((n, p, 2)) < 0.7
+    bm[..., 0] = True
+    params = init_params(cfg.obs_shape, "mlp", seed=9)
+    pol = B200Policy(params, cfg.obs_shape, p, seats=seats)
+    u = rng.random((len(seats), n, 2)).astype(np.float32)
+    logits, acts, logp = pol.forward_logits(_padded(obs16), torch.from_numpy(mm).cuda(),
+                                            torch.from_numpy(bm).cuda(), torch.from_numpy(u).cuda())
+    lg = logits.cpu().numpy()
+    for s, pid in enumerate(seats):
+        ml, bl, v = O.mlp_forward(params, obs16.astype(np.float32), pid, p)
+        assert _rel(lg[s, :, :5], ml) <= REL_TOL and _rel(lg[s, :, 5:7], bl) <= REL_TOL
+        assert _rel(lg[s, :, 7], v) <= REL_TOL
+        a, lp, _, _, _ = O.mlp_act(params, obs16.astype(np.float32), mm[:, pid], bm[:, pid], pid,
+                                   p, u[s, :, 0], u[s, :, 1])
+        assert int((acts[s].cpu().numpy() != a).any(-1).sum()) == 0
+        assert np.abs(logp[s].cpu().numpy() - lp).max() <= 1e-3
+
+
 def test_cnn_logits_vs_reference_goldens():
     g = G.load("traj_cfg5")
     cfg = SimConfig(**scenarios.CFG2)
