@@ -461,6 +461,11 @@ struct FusedCfg {
   // the start of its (drained) pipeline region
   static constexpr int kPartBytes = (NT / 128) * kBM * 128 * 4;
   static constexpr uint32_t kTmemCols = 512;            // leader
+  // layer 1: one seat accumulates A W_hi and A W_lo in columns [0, 128) and
+  // [128, 256) (one N = 256 MMA over the stacked hi / lo weight rows, so
+  // the A tile is read once per K step); two seats accumulate both
+  // products into the seat's 128 columns
+  static constexpr uint32_t kL1Cols = NT == 128 ? 256 : NT;
   static constexpr uint32_t kColH = NT;                 // head hidden accumulator (192 cols)
   static constexpr uint32_t kColScr = NT + 192;         // row-exchange scratch (48 cols)
 };
@@ -734,7 +739,7 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
   const int m0 = tile * kBM;
   const int kt0 = rank * k_tiles / ks, kt1 = (rank + 1) * k_tiles / ks;
   const int n_kt = kt1 - kt0;
-  const uint32_t tmem_cols = leader ? G::kTmemCols : (uint32_t)NT;
+  const uint32_t tmem_cols = leader ? G::kTmemCols : G::kL1Cols;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < G::kStages; ++s) {
@@ -832,6 +837,7 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
     if (lane == 0) {
       // ---------------- MMA issuer
       const uint32_t idesc = idesc_f16(kBM, NT);
+      const uint32_t idesc_st = idesc_f16(kBM, 256);   // one seat: hi and lo rows stacked
       bool ok = true;
       for (int kt = 0; kt < n_kt && ok; ++kt) {
         const int s = kt % G::kStages;
@@ -851,8 +857,13 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk) {
           const uint64_t off = (uint64_t)((kk * 32) >> 4);   // 32 bytes per K=16 step
-          umma_f16(tmem, da + off, dh + off, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
-          umma_f16(tmem, da + off, dl + off, idesc, 1u);
+          if (NT == 128) {
+            // W_lo's rows follow W_hi's in the stage (same swizzle phase)
+            umma_f16(tmem, da + off, dh + off, idesc_st, (kt > 0 || kk > 0) ? 1u : 0u);
+          } else {
+            umma_f16(tmem, da + off, dh + off, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+            umma_f16(tmem, da + off, dl + off, idesc, 1u);
+          }
           if (SPLIT_A) umma_f16(tmem, dal + off, dh + off, idesc, 1u);
         }
         umma_commit(&empty[s]);
@@ -910,13 +921,26 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
     uint8_t* a_lo = a_hi + G::kActBytes;
     bool ok = epi_and(mbar_wait(accb, 0) && *abort_flag == 0);
     asm volatile("tcgen05.fence::after_thread_sync;");
+    // this thread's 32 layer-1 sums of seat s (one seat: A W_hi + A W_lo)
+    auto ld_layer1 = [&](int s, float* x) {
+      tmem_ld32(lane_base + 128 * s + 32 * quarter, x);
+      if (NT == 128) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float y[16];
+          tmem_ld16(lane_base + 128 + 32 * quarter + 16 * h, y);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) x[16 * h + i] = __fadd_rn(x[16 * h + i], y[i]);
+        }
+      }
+    };
     if (!leader) {
       // split-K partials -> own shared memory (the drained pipeline region)
       if (ok) {
 #pragma unroll 1
         for (int s = 0; s < S; ++s) {
           float x[32];
-          tmem_ld32(lane_base + 128 * s + 32 * quarter, x);
+          ld_layer1(s, x);
           uint8_t* part = smem + s * (kBM * 512);
 #pragma unroll
           for (int t = 0; t < 8; ++t)
@@ -937,7 +961,7 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
       for (int s = 0; s < S && ok; ++s) {
         float x[32];
         // LN1 over the layer-1 pre-activations (rank-ordered split-K sum)
-        tmem_ld32(lane_base + 128 * s + 32 * quarter, x);
+        ld_layer1(s, x);
 #pragma unroll 1
         for (int c = 1; c < ks; ++c) {
           const uint32_t base = dsmem_addr(smem + s * (kBM * 512), (uint32_t)c);

@@ -187,10 +187,15 @@ def test_evaluate_on_device_matches_cpu_restatement(n):
         assert _capi.device_error() == 0
         for k in outs[0]:
             a, b = outs[0][k].double(), outs[1][k].double()
-            # outputs to 1e-5; gradients (float32 sums over the batch, in
-            # different orders on the two devices) to 5e-5 of their largest entry
-            tol = (1e-5 if k in ("logp", "v", "ent") else 5e-5) * max(1e-30, a.abs().max().item())
-            assert (a - b).abs().max().item() <= max(tol, 1e-12), (k, (a - b).abs().max().item(), tol)
+            # outputs to 1e-5 of their largest entry, but never tighter than
+            # 1e-6 absolute (float32 sums of O(1) terms in different orders:
+            # one row's value can be ~5e-3 itself); gradients (float32 sums
+            # over the batch, in different orders on the two devices) to 5e-5
+            # of their largest entry
+            out = k in ("logp", "v", "ent")
+            tol = (1e-5 if out else 5e-5) * max(1e-30, a.abs().max().item())
+            tol = max(tol, 1e-6 if out else 1e-12)
+            assert (a - b).abs().max().item() <= tol, (k, (a - b).abs().max().item(), tol)
 
 
 def test_obs_rows_pads_four_dimensional_batches():
