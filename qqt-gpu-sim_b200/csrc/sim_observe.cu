@@ -306,10 +306,10 @@ k_observe(QqtCfg cfg, QqtState st, void* obs, float* danger_out, uint8_t* mm, ui
 
 // ------------------------------------------------------------------ astar
 
-// Per-warp scratch of k_astar: danger, cost, the two fields, threat, own
-// bombs, then 32 prefetched per-env scalars (8 bytes each).
+// Per-warp scratch of k_astar: danger, cost, the two fields, own bombs,
+// then 32 prefetched per-env scalars (8 bytes each).
 __host__ __device__ inline size_t astar_pre_off(int cells) {
-  return ((size_t)cells * (4 * 4 + 1 + 2) + 15) / 16 * 16 + 64;
+  return ((size_t)cells * (4 * 4 + 2) + 15) / 16 * 16 + 64;
 }
 __host__ __device__ inline size_t astar_warp_bytes(int cells) {
   return astar_pre_off(cells) + 48 * 8;
@@ -557,8 +557,7 @@ k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const fl
   float* cost = d16 + C;
   float* vs = cost + C;
   float* vo = vs + C;
-  uint8_t* threat = (uint8_t*)(vo + C);
-  uint16_t* own = (uint16_t*)(threat + ((C + 1) & ~1));
+  uint16_t* own = (uint16_t*)(vo + C);
   const int lane = lane_id();
   const int cap_max = *cap_max_ptr;
   const int G = cfg.growth_blast_max;
@@ -579,16 +578,9 @@ k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const fl
       vs[c] = d < 0.35f ? 0.f : INF;
       vo[c] = INF;
     }
+    // own live bombs: the threat term (a cell within Manhattan distance G
+    // of one, sim/bots.py:301-309) is only read at the five candidates
     const int nown = warp_compact(C, own, [&](int c) { return v.owner[c] == pid && v.fuse[c] > 0; });
-    for (int c = lane; c < C; c += 32) {
-      const int r = c / w, cc = c - r * w;
-      uint8_t t = 0;
-      for (int i = 0; i < nown && !t; ++i) {
-        const int b = own[i], br = b / w, bc = b - br * w;
-        if (abs(br - r) + abs(bc - cc) <= G) t = 1;
-      }
-      threat[c] = t;
-    }
     __syncwarp();
     if (lane == 0) {
       for (int o = 0; o < P; ++o) {
@@ -635,104 +627,124 @@ k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const fl
         for (int c = lane; c < C; c += 32) vcrate_out[(size_t)e * C + c] = vs[c];
     }
 
-    if (lane == 0) {
-      int mode = 0;
-      bool has_mode = mode_arr != nullptr;
-      if (has_mode) {
-        int64_t tm = (int64_t)pre[AP_TIMER] - 1;
-        int64_t md = (int64_t)pre[AP_MODE];
-        if (tick16 && tm <= 0) {
-          md = (int64_t)pre[AP_NEW_MODE];
-          tm = (int64_t)pre[AP_NEW_TIMER];
-        }
+    // scoring (sim/bots.py:433-508): candidate k (up, down, left, right,
+    // idle) on lane k, each with the same float operations as a serial
+    // loop; lane 0 combines the five.  Lanes 5..31 repeat the idle
+    // candidate and are left out of every vote.
+    int mode = 0;
+    const bool has_mode = mode_arr != nullptr;
+    if (has_mode) {
+      int64_t tm = (int64_t)pre[AP_TIMER] - 1;
+      int64_t md = (int64_t)pre[AP_MODE];
+      if (tick16 && tm <= 0) {
+        md = (int64_t)pre[AP_NEW_MODE];
+        tm = (int64_t)pre[AP_NEW_TIMER];
+      }
+      if (lane == 0) {
         timer_arr[e] = tm;
         mode_arr[e] = md;
-        mode = (int)md;
       }
-      const float py = __uint_as_float((uint32_t)pre[AP_PY + pid]);
-      const float px = __uint_as_float((uint32_t)pre[AP_PX + pid]);
-      const int r = min(max((int)floorf(py), 0), h - 1), c = min(max((int)floorf(px), 0), w - 1);
-      const float own_dng = d16[r * w + c];
-      const int cr[5] = {max(r - 1, 0), min(r + 1, h - 1), r, r, r};
-      const int ccs[5] = {c, c, max(c - 1, 0), min(c + 1, w - 1), c};
-      float vopp_c[5], vsafe_c[5], dng_c[5], thr_c[5], nz[5];
-      bool legal[5];
-      float vcrate_c[5];
-      for (int k = 0; k < 5; ++k) {
-        const int q = cr[k] * w + ccs[k];
-        if (EAT) {
-          vopp_c[k] = __uint_as_float((uint32_t)pre[AP_CAND_OPP + k]);
-          vsafe_c[k] = __uint_as_float((uint32_t)pre[AP_CAND_SAFE + k]);
-          vcrate_c[k] = vs[q];
-        } else {
-          vopp_c[k] = vo[q];
-          vsafe_c[k] = vs[q];
-          vcrate_c[k] = INF;
+      mode = (int)md;
+    }
+    const float py = __uint_as_float((uint32_t)pre[AP_PY + pid]);
+    const float px = __uint_as_float((uint32_t)pre[AP_PX + pid]);
+    const int r = min(max((int)floorf(py), 0), h - 1), c = min(max((int)floorf(px), 0), w - 1);
+    const float own_dng = d16[r * w + c];
+    const bool cand = lane < 5;
+    const int k = cand ? lane : 4;
+    const int rk = k == 0 ? max(r - 1, 0) : (k == 1 ? min(r + 1, h - 1) : r);
+    const int ck = k == 2 ? max(c - 1, 0) : (k == 3 ? min(c + 1, w - 1) : c);
+    const int q = rk * w + ck;
+    float vopp_k, vsafe_k, vcrate_k;
+    if (EAT) {
+      vopp_k = __uint_as_float((uint32_t)pre[AP_CAND_OPP + k]);
+      vsafe_k = __uint_as_float((uint32_t)pre[AP_CAND_SAFE + k]);
+      vcrate_k = vs[q];
+    } else {
+      vopp_k = vo[q];
+      vsafe_k = vs[q];
+      vcrate_k = INF;
+    }
+    const float dng_k = d16[q];
+    bool thr = false;
+    for (int i = 0; i < nown && !thr; ++i) {
+      const int b = own[i], br = b / w, bc = b - br * w;
+      if (abs(br - rk) + abs(bc - ck) <= G) thr = true;
+    }
+    const float thr_k = thr ? 1.f : 0.f;
+    const bool legal_k = pre[AP_MM + k] && !(v.wall[q] || v.brick[q]);
+    const float nz_k = __fmul_rn(0.05f, __uint_as_float((uint32_t)pre[AP_NOISE + k]));
+    float app = __fadd_rn(__fadd_rn(__fadd_rn(vopp_k, __fmul_rn(2.f, dng_k)), __fmul_rn(2.f, thr_k)),
+                          nz_k);
+    if (dng_k >= 0.5f || !legal_k) app = INF;
+    const bool app_ok = __any_sync(QQT_FULL, cand && app < INF);
+    const bool use_esc = own_dng >= 0.35f || !app_ok;
+    float esc = __fadd_rn(__fadd_rn(__fmul_rn(vsafe_k, 100.f), __fmul_rn(2.f, thr_k)), nz_k);
+    if ((use_esc && k == 4) || !legal_k) esc = INF;
+    if (EAT) {
+      // crate layer: >= 2 of the growth attributes under 70 % of their
+      // caps, a crate on the board, alive -> descend V_crate (no idling
+      // when a move is better), unless no crate is reachable
+      const float fb = __fdiv_rn((float)(int64_t)pre[AP_BCAP], (float)cfg.growth_bombs_max);
+      const float fz = __fdiv_rn((float)(int64_t)pre[AP_CAP], (float)cfg.growth_blast_max);
+      const float fs = __fdiv_rn(__uint_as_float((uint32_t)pre[AP_SPD]), cfg.growth_speed_max);
+      const int low = (fb < 0.7f) + (fz < 0.7f) + (fs < 0.7f);
+      bool eat_on = low >= 2 && any_crate && pre[AP_ALIVE + pid] != 0;
+      float eat = __fadd_rn(__fadd_rn(__fmul_rn(vcrate_k, 100.f), __fmul_rn(2.f, dng_k)), nz_k);
+      if (dng_k >= 0.5f || !legal_k) eat = INF;
+      const float no_idle = fminf(fminf(__shfl_sync(QQT_FULL, eat, 0), __shfl_sync(QQT_FULL, eat, 1)),
+                                  fminf(__shfl_sync(QQT_FULL, eat, 2), __shfl_sync(QQT_FULL, eat, 3)));
+      if (k == 4 && no_idle < eat) eat = INF;
+      eat_on = eat_on && fminf(no_idle, __shfl_sync(QQT_FULL, eat, 4)) < INF;
+      if (eat_on) app = eat;
+    }
+    float score = use_esc ? esc : app;
+    if (has_mode && mode == 1) {
+      float f = __fadd_rn(__fadd_rn(__fadd_rn(-fminf(vopp_k, 1e3f), __fmul_rn(2.f, dng_k)),
+                                    __fmul_rn(2.f, thr_k)), nz_k);
+      if (dng_k >= 0.5f || !legal_k) f = INF;
+      score = use_esc ? esc : f;
+    }
+    const unsigned legal_m = __ballot_sync(QQT_FULL, cand && legal_k);
+    const unsigned safe_m =
+        __ballot_sync(QQT_FULL, cand && legal_k && dng_k < 0.35f && thr_k == 0.f);
+    float sc[5], dl[5];
+#pragma unroll
+    for (int j = 0; j < 5; ++j) {
+      sc[j] = __shfl_sync(QQT_FULL, score, j);
+      dl[j] = __shfl_sync(QQT_FULL, legal_k ? dng_k : INF, j);
+    }
+    // chain term: a live bomb with fuse 1..10 within cap_max cells in a
+    // straight line (the batch's largest blast cap, sim/bots.py:484), one
+    // (distance, direction) probe per lane
+    const int cap = (int)(int64_t)pre[AP_CAP];
+    bool chain = false;
+    for (int base = 0; base < 4 * cap_max && !chain; base += 32) {
+      const int j = base + lane;
+      bool hit = false;
+      if (j < 4 * cap_max) {
+        const int dist = (j >> 2) + 1, d = j & 3;
+        const int r2 = r + (d == 0 ? -dist : (d == 1 ? dist : 0));
+        const int c2 = c + (d == 2 ? -dist : (d == 3 ? dist : 0));
+        if (r2 >= 0 && r2 < h && c2 >= 0 && c2 < w) {
+          const int f = v.fuse[r2 * w + c2];
+          hit = f > 0 && f <= 10;
         }
-        dng_c[k] = d16[q];
-        thr_c[k] = threat[q] ? 1.f : 0.f;
-        legal[k] = pre[AP_MM + k] && !(v.wall[q] || v.brick[q]);
-        nz[k] = __fmul_rn(0.05f, __uint_as_float((uint32_t)pre[AP_NOISE + k]));
       }
-      float app[5], esc[5], score[5];
-      bool app_ok = false;
-      for (int k = 0; k < 5; ++k) {
-        float a = __fadd_rn(__fadd_rn(__fadd_rn(vopp_c[k], __fmul_rn(2.f, dng_c[k])),
-                                      __fmul_rn(2.f, thr_c[k])), nz[k]);
-        if (dng_c[k] >= 0.5f || !legal[k]) a = INF;
-        app[k] = a;
-        app_ok |= a < INF;
+      chain = __any_sync(QQT_FULL, hit);
+    }
+    if (lane == 0) {
+      int move = argmin5(sc);
+      bool finite = false;
+      float dmv[5];
+      for (int j = 0; j < 5; ++j) {
+        finite |= sc[j] < INF;
+        dmv[j] = j < 4 ? dl[j] : INF;
       }
-      const bool use_esc = own_dng >= 0.35f || !app_ok;
-      for (int k = 0; k < 5; ++k) {
-        float x = __fadd_rn(__fadd_rn(__fmul_rn(vsafe_c[k], 100.f), __fmul_rn(2.f, thr_c[k])), nz[k]);
-        if ((use_esc && k == 4) || !legal[k]) x = INF;
-        esc[k] = x;
-      }
-      if (EAT) {
-        // crate layer: >= 2 of the growth attributes under 70 % of their
-        // caps, a crate on the board, alive -> descend V_crate (no idling
-        // when a move is better), unless no crate is reachable
-        const float fb = __fdiv_rn((float)(int64_t)pre[AP_BCAP], (float)cfg.growth_bombs_max);
-        const float fz = __fdiv_rn((float)(int64_t)pre[AP_CAP], (float)cfg.growth_blast_max);
-        const float fs = __fdiv_rn(__uint_as_float((uint32_t)pre[AP_SPD]), cfg.growth_speed_max);
-        const int low = (fb < 0.7f) + (fz < 0.7f) + (fs < 0.7f);
-        bool eat_on = low >= 2 && any_crate && pre[AP_ALIVE + pid] != 0;
-        float eat[5];
-        for (int k = 0; k < 5; ++k) {
-          float x = __fadd_rn(__fadd_rn(__fmul_rn(vcrate_c[k], 100.f), __fmul_rn(2.f, dng_c[k])), nz[k]);
-          if (dng_c[k] >= 0.5f || !legal[k]) x = INF;
-          eat[k] = x;
-        }
-        const float no_idle = fminf(fminf(eat[0], eat[1]), fminf(eat[2], eat[3]));
-        if (no_idle < eat[4]) eat[4] = INF;
-        eat_on = eat_on && fminf(no_idle, eat[4]) < INF;
-        if (eat_on)
-          for (int k = 0; k < 5; ++k) app[k] = eat[k];
-      }
-      for (int k = 0; k < 5; ++k) score[k] = use_esc ? esc[k] : app[k];
-      if (has_mode && mode == 1) {
-        for (int k = 0; k < 5; ++k) {
-          float f = __fadd_rn(__fadd_rn(__fadd_rn(-fminf(vopp_c[k], 1e3f), __fmul_rn(2.f, dng_c[k])),
-                                        __fmul_rn(2.f, thr_c[k])), nz[k]);
-          if (dng_c[k] >= 0.5f || !legal[k]) f = INF;
-          score[k] = use_esc ? esc[k] : f;
-        }
-      }
-      int move = argmin5(score);
-      bool any_legal = false, finite = false;
-      float dl[5], dmv[5];
-      for (int k = 0; k < 5; ++k) {
-        any_legal |= legal[k];
-        finite |= score[k] < INF;
-        dl[k] = legal[k] ? dng_c[k] : INF;
-        dmv[k] = k < 4 ? dl[k] : INF;
-      }
-      if (!finite && any_legal) {
+      if (!finite && legal_m != 0) {
         const int fm = argmin5(dmv);
         move = dmv[fm] < INF ? fm : argmin5(dl);
       }
-      const int64_t cap = (int64_t)pre[AP_CAP];
       long long dr_o = 1000000000LL, dc_o = 1000000000LL;
       for (int o = 0; o < P; ++o) {
         if (o == pid || !pre[AP_ALIVE + o]) continue;
@@ -744,17 +756,8 @@ k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const fl
       const bool aligned = (dr_o == 0 && dc_o <= cap) || (dc_o == 0 && dr_o <= cap);
       const long long manh = min(dr_o + dc_o, 100000000LL);
       const bool near = manh <= max((long long)cap + 1, 1LL);
-      bool chain = false;
-      for (int k = 1; k <= cap_max && !chain; ++k)
-        for (int d = 0; d < 4; ++d) {
-          const int rr = r + kDR[d] * k, c2 = c + kDC[d] * k;
-          if (rr < 0 || rr >= h || c2 < 0 || c2 >= w) continue;
-          const int f = v.fuse[rr * w + c2];
-          if (f > 0 && f <= 10) chain = true;
-        }
       const bool can = pre[AP_BM] != 0;
-      bool can_escape = false;
-      for (int k = 0; k < 5; ++k) can_escape |= legal[k] && dng_c[k] < 0.35f && thr_c[k] == 0.f;
+      const bool can_escape = safe_m != 0;
       bool place = can && (aligned || near || chain) && own_dng < 0.2f && can_escape;
       if (has_mode && mode == 1) place = can && (aligned || near) && own_dng < 0.2f && can_escape;
       const bool alive = pre[AP_ALIVE + pid] != 0;
