@@ -768,12 +768,21 @@ k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const fl
   }
 }
 
-__global__ void k_cap_max(const int64_t* blast_cap, int n, int* out) {
+// One block: the maximum over the seat's blast caps (0 for an empty batch),
+// written once, so no memset precedes it and the bot's first node in a
+// captured tick is a kernel.
+__global__ void __launch_bounds__(1024) k_cap_max(const int64_t* blast_cap, int n, int* out) {
+  __shared__ int wmax[32];
   int m = 0;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
-    m = max(m, (int)blast_cap[i]);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) m = max(m, (int)blast_cap[i]);
   m = warp_max(m);
-  if (lane_id() == 0) atomicMax(out, m);
+  if (lane_id() == 0) wmax[warp_id()] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < (blockDim.x >> 5) ? wmax[threadIdx.x] : 0;
+    m = warp_max(m);
+    if (threadIdx.x == 0) *out = m;
+  }
 }
 
 // ---------------------------------------------------------- random / greedy
@@ -1066,8 +1075,7 @@ static int launch_astar(const QqtCfg* cfg, const QqtState* st, const void* obs,
   cudaStream_t s = (cudaStream_t)stream;
   const int N = cfg->n_envs, C = cfg->height * cfg->width;
   int* capmax = (int*)scratch;
-  cudaMemsetAsync(capmax, 0, sizeof(int), s);
-  k_cap_max<<<min((N + 255) / 256, 148), 256, 0, s>>>(st->blast_cap + (size_t)pid * N, N, capmax);
+  k_cap_max<<<1, 1024, 0, s>>>(st->blast_cap + (size_t)pid * N, N, capmax);
   const size_t sm = tile_bytes(C) + QQT_NWARP * astar_warp_bytes(C);
   const bool two = cfg->n_players == 2, g13 = cfg->height == 13 && cfg->width == 13;
   auto kern = two ? (g13 ? k_astar<EAT, 2, 13> : k_astar<EAT, 2>) : k_astar<EAT>;
