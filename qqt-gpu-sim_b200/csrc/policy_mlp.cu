@@ -24,8 +24,10 @@
 //            store it as the next MMA's A operand (128-byte swizzled
 //            K-major).  Each of the two remaining layers is 8 K steps x 3
 //            MMAs (Ahi*Whi + Ahi*Wlo + Alo*Whi), which keeps the products at
-//            float32 accuracy.  Each thread takes 48 of the 192 head units
-//            and forms partial output logits (5 move, 2 bomb, 1 value); the
+//            float32 accuracy.  Each thread takes a share of the 192 head
+//            units (the four shares hold about equal numbers of output
+//            multiply-adds) and forms partial output logits (5 move, 2
+//            bomb, 1 value); the
 //            first quarter's thread sums the four, masks with float32's
 //            lowest value, samples by inverse CDF and writes the
 //            log-probability and value.
@@ -157,6 +159,24 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+// Two 32-column loads (columns a .. a+31 and b .. b+31 of the warp's lanes)
+// with one wait, so the second load's latency overlaps the first's.
+__device__ __forceinline__ void tmem_ld32x2(uint32_t a, uint32_t b, float* x, float* y) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%65];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(a), "r"(b)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    x[i] = __uint_as_float(r[i]);
+    y[i] = __uint_as_float(r[32 + i]);
+  }
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -313,16 +333,39 @@ __global__ void k_mlp_pack_images(HeadParams hp, uint8_t* __restrict__ img) {
 
 // ---------------------------------------------------------------- heads
 
+// The sampling inputs of one row: legal-move bits (bit k: move k, bits 5
+// and 6: bomb 0 and 1) and the two uniforms.  The epilogue loads them before
+// layer 1 completes, so their latency stays off the tail's critical path.
+struct SampleIn {
+  uint32_t legal;
+  float um, ub;
+};
+
+__device__ __forceinline__ SampleIn sample_load(int row, int seat, int n_rows,
+                                                const uint8_t* __restrict__ mm, int mm_stride,
+                                                const uint8_t* __restrict__ bm, int bm_stride,
+                                                const float* __restrict__ u) {
+  const uint8_t* mrow = mm + (size_t)row * mm_stride;
+  const uint8_t* brow = bm + (size_t)row * bm_stride;
+  SampleIn in;
+  uint32_t b = 0;
+#pragma unroll
+  for (int k = 0; k < 5; ++k) b |= (mrow[k] ? 1u : 0u) << k;
+  b |= (brow[0] ? 1u : 0u) << 5;
+  b |= (brow[1] ? 1u : 0u) << 6;
+  in.legal = b;
+  in.um = u[((size_t)seat * n_rows + row) * 2];
+  in.ub = u[((size_t)seat * n_rows + row) * 2 + 1];
+  return in;
+}
+
 // Logits z (5 move, 2 bomb, value) of one row -> masked categorical samples
 // (inverse CDF: a = #{k : u * S > cs_k} over exp(z - max z)), joint
 // log-prob, value; masked logits take float32's lowest value
 // (train/model.py:204-245).
 __device__ __forceinline__ void sample_write(const float* z, int row, int seat, int n_rows,
-                                             const uint8_t* __restrict__ mm, int mm_stride,
-                                             const uint8_t* __restrict__ bm, int bm_stride,
-                                             const float* __restrict__ u,
-                                             int64_t* __restrict__ act, int act_stride,
-                                             float* __restrict__ logp_out,
+                                             const SampleIn& in, int64_t* __restrict__ act,
+                                             int act_stride, float* __restrict__ logp_out,
                                              float* __restrict__ value_out,
                                              float* __restrict__ logits_out) {
   if (logits_out) {
@@ -331,13 +374,11 @@ __device__ __forceinline__ void sample_write(const float* z, int row, int seat, 
     for (int o = 0; o < 8; ++o) lo[o] = z[o];
   }
   const float lowest = -3.402823466e38f;
-  const uint8_t* mrow = mm + (size_t)row * mm_stride;
-  const uint8_t* brow = bm + (size_t)row * bm_stride;
   float zm[5], cs[5];
   float mx = lowest;
 #pragma unroll
   for (int k = 0; k < 5; ++k) {
-    zm[k] = mrow[k] ? z[k] : lowest;
+    zm[k] = (in.legal >> k) & 1u ? z[k] : lowest;
     mx = fmaxf(mx, zm[k]);
   }
   float tot = 0.f;
@@ -346,7 +387,7 @@ __device__ __forceinline__ void sample_write(const float* z, int row, int seat, 
     tot += expf(zm[k] - mx);
     cs[k] = tot;
   }
-  const float um = u[((size_t)seat * n_rows + row) * 2] * tot;
+  const float um = in.um * tot;
   int am = 0;
 #pragma unroll
   for (int k = 0; k < 5; ++k) am += um > cs[k];
@@ -355,10 +396,11 @@ __device__ __forceinline__ void sample_write(const float* z, int row, int seat, 
 #pragma unroll
   for (int k = 1; k < 5; ++k) zam = am == k ? zm[k] : zam;
   const float lpm = zam - mx - logf(tot);
-  const float zb0 = brow[0] ? z[5] : lowest, zb1 = brow[1] ? z[6] : lowest;
+  const float zb0 = (in.legal >> 5) & 1u ? z[5] : lowest;
+  const float zb1 = (in.legal >> 6) & 1u ? z[6] : lowest;
   const float mb = fmaxf(zb0, zb1);
   const float e0 = expf(zb0 - mb), s2 = e0 + expf(zb1 - mb);
-  const float ub = u[((size_t)seat * n_rows + row) * 2 + 1] * s2;
+  const float ub = in.ub * s2;
   const int ab = ub > e0 ? 1 : 0;
   const float lpb = (ab ? zb1 : zb0) - mb - logf(s2);
   act[(size_t)row * act_stride] = am;
@@ -502,6 +544,17 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tmem_ld4(uint32_t taddr, float* v) {
   uint32_t r[4];
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
@@ -560,6 +613,27 @@ __device__ __forceinline__ void row_exchange4(uint32_t scr, int quarter, float v
   tmem_ld4(scr, p);
 }
 
+// Barrier of the four epilogue warps of k_mlp_fused / k_mlp_pair that share
+// TMEM lane quadrant warp % 4 (one warp per column quarter, so the four
+// threads of each of those 32 rows): named barriers 2..5.
+__device__ __forceinline__ void quad_sync() {
+  switch (warp_id() & 3) {   // constant barrier ids
+    case 0: asm volatile("bar.sync 2, 128;" ::: "memory"); break;
+    case 1: asm volatile("bar.sync 3, 128;" ::: "memory"); break;
+    case 2: asm volatile("bar.sync 4, 128;" ::: "memory"); break;
+    default: asm volatile("bar.sync 5, 128;" ::: "memory"); break;
+  }
+}
+
+// row_exchange4 among the four threads of a row only (quad_sync).
+__device__ __forceinline__ void row_exchange4_quad(uint32_t scr, int quarter, float v, float* p) {
+  tmem_st1(scr + quarter, v);
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  quad_sync();
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  tmem_ld4(scr, p);
+}
+
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -611,6 +685,71 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
   return false;
 }
 
+// Head output layers over head hidden units U0 .. U0+NU-1 (inside one head;
+// TMEM columns hcol + U0 ..): +bias, ReLU, then the head's output rows
+// (train/model.py:167-245: move_head.2 / bomb_head.2 / critic.2) into this
+// thread's partial logits z (5 move, 2 bomb, 1 value).
+template <int U0, int NU>
+__device__ __forceinline__ void head_out_chunk(uint32_t hcol, const float* __restrict__ f,
+                                               float* z) {
+  static_assert(NU == 8 || NU == 16 || NU == 32, "chunk width");
+  static_assert((U0 >> 6) == ((U0 + NU - 1) >> 6), "a chunk lies inside one head");
+  float h[NU];
+  if constexpr (NU == 8) tmem_ld8(hcol + U0, h);
+  else if constexpr (NU == 16) tmem_ld16(hcol + U0, h);
+  else tmem_ld32(hcol + U0, h);
+  constexpr int head = U0 >> 6, uu = U0 & 63;
+  constexpr int o_lo = head == 0 ? 0 : (head == 1 ? 5 : 7);
+  constexpr int o_hi = head == 0 ? 5 : (head == 1 ? 7 : 8);
+#pragma unroll
+  for (int i = 0; i < NU; i += 4) {
+    const float4 hb = __ldg(reinterpret_cast<const float4*>(f + F_HB0 + U0 + i));
+    h[i] = fmaxf(__fadd_rn(h[i], hb.x), 0.f);
+    h[i + 1] = fmaxf(__fadd_rn(h[i + 1], hb.y), 0.f);
+    h[i + 2] = fmaxf(__fadd_rn(h[i + 2], hb.z), 0.f);
+    h[i + 3] = fmaxf(__fadd_rn(h[i + 3], hb.w), 0.f);
+  }
+#pragma unroll
+  for (int o = o_lo; o < o_hi; ++o)
+#pragma unroll
+    for (int i = 0; i < NU; i += 4) {
+      const float4 wv = __ldg(reinterpret_cast<const float4*>(f + F_HW2 + o * 64 + uu + i));
+      z[o] = fmaf(wv.x, h[i], z[o]);
+      z[o] = fmaf(wv.y, h[i + 1], z[o]);
+      z[o] = fmaf(wv.z, h[i + 2], z[o]);
+      z[o] = fmaf(wv.w, h[i + 3], z[o]);
+    }
+}
+
+// The four threads of a row split the 512 output multiply-adds (64 move
+// units x 5 + 64 bomb units x 2 + 64 value units x 1) about evenly: units
+// 0-23 (120), 24-47 (120), 48-87 (128), 88-191 (144).  `quarter` is
+// warp-uniform, so every TMEM load stays warp-collective.
+__device__ __forceinline__ void head_out_quarter(uint32_t hcol, int quarter,
+                                                 const float* __restrict__ f, float* z) {
+  switch (quarter) {
+    case 0:
+      head_out_chunk<0, 16>(hcol, f, z);
+      head_out_chunk<16, 8>(hcol, f, z);
+      break;
+    case 1:
+      head_out_chunk<24, 8>(hcol, f, z);
+      head_out_chunk<32, 16>(hcol, f, z);
+      break;
+    case 2:
+      head_out_chunk<48, 16>(hcol, f, z);
+      head_out_chunk<64, 16>(hcol, f, z);
+      head_out_chunk<80, 8>(hcol, f, z);
+      break;
+    default:
+      head_out_chunk<88, 8>(hcol, f, z);
+      head_out_chunk<96, 32>(hcol, f, z);
+      head_out_chunk<128, 32>(hcol, f, z);
+      head_out_chunk<160, 32>(hcol, f, z);
+      break;
+  }
+}
+
 // Byte offset of float4 chunk c (of 32) of row r in a [128][128] fp32
 // partial-sum block; the chunk index is XOR-swizzled by the row so that a
 // warp's 32 rows hit distinct bank groups.
@@ -642,7 +781,7 @@ __device__ __forceinline__ void bias_ln_relu_quarter(float* x, int q, uint32_t s
     for (int j = 0; j < 4; ++j) s4[j] += x[i + j];
   }
   float p[4];
-  row_exchange4(scr, q, (s4[0] + s4[1]) + (s4[2] + s4[3]), p);
+  row_exchange4_quad(scr, q, (s4[0] + s4[1]) + (s4[2] + s4[3]), p);
   const float mean = ((p[0] + p[1]) + (p[2] + p[3])) * (1.f / 128.f);
   float v4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -652,7 +791,7 @@ __device__ __forceinline__ void bias_ln_relu_quarter(float* x, int q, uint32_t s
       const float d = x[i + j] - mean;
       v4[j] = fmaf(d, d, v4[j]);
     }
-  row_exchange4(scr + 4, q, (v4[0] + v4[1]) + (v4[2] + v4[3]), p);
+  row_exchange4_quad(scr + 4, q, (v4[0] + v4[1]) + (v4[2] + v4[3]), p);
   const float rstd = rsqrtf(((p[0] + p[1]) + (p[2] + p[3])) * (1.f / 128.f) + 1e-5f);
 #pragma unroll
   for (int i = 0; i < 32; i += 4) {
@@ -674,12 +813,13 @@ __device__ __forceinline__ void store_split_quarter(const float* x, uint8_t* a_h
     uint32_t hv[4], lv[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
+      // packed conversions: element 2j in the low half, 2j+1 in the high
       const float v0 = x[8 * c + 2 * j], v1 = x[8 * c + 2 * j + 1];
-      const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
-      const __half l0 = __float2half_rn(__fsub_rn(v0, __half2float(h0)));
-      const __half l1 = __float2half_rn(__fsub_rn(v1, __half2float(h1)));
-      hv[j] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-      lv[j] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+      const __half2 h = __floats2half2_rn(v0, v1);
+      const float2 hf = __half22float2(h);
+      const __half2 l = __floats2half2_rn(__fsub_rn(v0, hf.x), __fsub_rn(v1, hf.y));
+      hv[j] = *reinterpret_cast<const uint32_t*>(&h);
+      lv[j] = *reinterpret_cast<const uint32_t*>(&l);
     }
     const uint32_t off = sw128_off(r, 32 * q + 8 * c, kBM);
     *reinterpret_cast<uint4*>(a_hi + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
@@ -919,19 +1059,25 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
     const uint32_t scr = lane_base + G::kColScr;
     uint8_t* a_hi = smem + G::kAct;
     uint8_t* a_lo = a_hi + G::kActBytes;
+    // sampling inputs of this row (the thread of quarter 0 samples it)
+    SampleIn sin[S];
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+      sin[s] = SampleIn{0u, 0.f, 0.f};
+      if (!TRAIN && leader && quarter == 0 && row < n_rows)
+        sin[s] = sample_load(row, seat0 + s, n_rows, io.mm[s], mm_stride, io.bm[s], bm_stride, u);
+    }
     bool ok = epi_and(mbar_wait(accb, 0) && *abort_flag == 0);
     asm volatile("tcgen05.fence::after_thread_sync;");
     // this thread's 32 layer-1 sums of seat s (one seat: A W_hi + A W_lo)
     auto ld_layer1 = [&](int s, float* x) {
-      tmem_ld32(lane_base + 128 * s + 32 * quarter, x);
       if (NT == 128) {
+        float y[32];
+        tmem_ld32x2(lane_base + 32 * quarter, lane_base + 128 + 32 * quarter, x, y);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          float y[16];
-          tmem_ld16(lane_base + 128 + 32 * quarter + 16 * h, y);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) x[16 * h + i] = __fadd_rn(x[16 * h + i], y[i]);
-        }
+        for (int i = 0; i < 32; ++i) x[i] = __fadd_rn(x[i], y[i]);
+      } else {
+        tmem_ld32(lane_base + 128 * s + 32 * quarter, x);
       }
     };
     if (!leader) {
@@ -997,46 +1143,18 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         fence_proxy_async();
         asm volatile("tcgen05.fence::before_thread_sync;");
         mbar_arrive(abar);
-        // head hidden units 48*quarter .. +47 -> partial output logits
+        // head hidden units -> this quarter's partial output logits
         ok = epi_and(mbar_wait(dbar, (2 * s + 1) & 1) && *abort_flag == 0);
         if (!ok) break;
         asm volatile("tcgen05.fence::after_thread_sync;");
         float z[8];
 #pragma unroll
         for (int o = 0; o < 8; ++o) z[o] = 0.f;
-#pragma unroll
-        for (int c = 0; c < 3; ++c) {
-          const int u0 = 48 * quarter + 16 * c;   // 16 units inside one head
-          float h[16];
-          tmem_ld16(lane_base + G::kColH + u0, h);
-#pragma unroll
-          for (int i = 0; i < 16; i += 4) {
-            const float4 hb = __ldg(reinterpret_cast<const float4*>(f + F_HB0 + u0 + i));
-            h[i] = fmaxf(__fadd_rn(h[i], hb.x), 0.f);
-            h[i + 1] = fmaxf(__fadd_rn(h[i + 1], hb.y), 0.f);
-            h[i + 2] = fmaxf(__fadd_rn(h[i + 2], hb.z), 0.f);
-            h[i + 3] = fmaxf(__fadd_rn(h[i + 3], hb.w), 0.f);
-          }
-          const int head = u0 >> 6, uu = u0 & 63;
-          const int o_lo = head == 0 ? 0 : (head == 1 ? 5 : 7);
-          const int o_hi = head == 0 ? 5 : (head == 1 ? 7 : 8);
-#pragma unroll
-          for (int o = 0; o < 8; ++o) {
-            if (o < o_lo || o >= o_hi) continue;
-#pragma unroll
-            for (int i = 0; i < 16; i += 4) {
-              const float4 wv = __ldg(reinterpret_cast<const float4*>(f + F_HW2 + o * 64 + uu + i));
-              z[o] = fmaf(wv.x, h[i], z[o]);
-              z[o] = fmaf(wv.y, h[i + 1], z[o]);
-              z[o] = fmaf(wv.z, h[i + 2], z[o]);
-              z[o] = fmaf(wv.w, h[i + 3], z[o]);
-            }
-          }
-        }
+        head_out_quarter(lane_base + G::kColH, quarter, f, z);
         // the four quarters' partial logits through the row's TMEM lane
         tmem_st8(scr + 16 + 8 * quarter, z);
         asm volatile("tcgen05.fence::before_thread_sync;");
-        epi_sync();
+        quad_sync();
         asm volatile("tcgen05.fence::after_thread_sync;");
         if (quarter == 0) {
           float zz[32];
@@ -1049,8 +1167,8 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
               score_write(z, row, io.mm[s], mm_stride, io.bm[s], bm_stride, io.act[s],
                           act_stride, logp_out, tr.ent, value_out);
             else
-              sample_write(z, row, seat0 + s, n_rows, io.mm[s], mm_stride, io.bm[s], bm_stride,
-                           u, io.act[s], act_stride, logp_out, value_out, logits_out);
+              sample_write(z, row, seat0 + s, n_rows, sin[s], io.act[s], act_stride, logp_out,
+                           value_out, logits_out);
           }
         }
       }

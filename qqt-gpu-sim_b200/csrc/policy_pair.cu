@@ -306,6 +306,14 @@ k_mlp_pair(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
     uint8_t* a_lo = smem + G::kActBytes;
     const uint32_t abar_lead = dsmem_addr(abar, 0);
     const bool elected = warp == 2 && lane == 0;
+    // sampling inputs of this row (the thread of quarter 0 samples it)
+    SampleIn sin[S];
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+      sin[s] = SampleIn{0u, 0.f, 0.f};
+      if (quarter == 0 && row < n_rows)
+        sin[s] = sample_load(row, s, n_rows, io.mm[s], mm_stride, io.bm[s], bm_stride, u);
+    }
     // the leader always commits accb, also after an abort: waiting for it
     // keeps the CTA resident until that arrival has landed
     bool ok = mbar_wait(accb, 0);
@@ -343,46 +351,18 @@ k_mlp_pair(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
       bias_ln_relu_quarter(x, quarter, scr + 8, f + F_B1, f + F_LN2G, f + F_LN2B);
       store_split_quarter(x, a_hi, a_lo, r, quarter);
       operand_ready(false);
-      // head hidden units 48 * quarter .. + 47 -> partial output logits
+      // head hidden units -> this quarter's partial output logits
       ok = epi_and(mbar_wait(dbar, (2 * s + 1) & 1) && *abort_flag == 0);
       if (!ok) break;
       asm volatile("tcgen05.fence::after_thread_sync;");
       float z[8];
 #pragma unroll
       for (int o = 0; o < 8; ++o) z[o] = 0.f;
-#pragma unroll
-      for (int c = 0; c < 3; ++c) {
-        const int u0 = 48 * quarter + 16 * c;   // 16 units inside one head
-        float h[16];
-        tmem_ld16(lane_base + G::kColH + u0, h);
-#pragma unroll
-        for (int i = 0; i < 16; i += 4) {
-          const float4 hb = __ldg(reinterpret_cast<const float4*>(f + F_HB0 + u0 + i));
-          h[i] = fmaxf(__fadd_rn(h[i], hb.x), 0.f);
-          h[i + 1] = fmaxf(__fadd_rn(h[i + 1], hb.y), 0.f);
-          h[i + 2] = fmaxf(__fadd_rn(h[i + 2], hb.z), 0.f);
-          h[i + 3] = fmaxf(__fadd_rn(h[i + 3], hb.w), 0.f);
-        }
-        const int head = u0 >> 6, uu = u0 & 63;
-        const int o_lo = head == 0 ? 0 : (head == 1 ? 5 : 7);
-        const int o_hi = head == 0 ? 5 : (head == 1 ? 7 : 8);
-#pragma unroll
-        for (int o = 0; o < 8; ++o) {
-          if (o < o_lo || o >= o_hi) continue;
-#pragma unroll
-          for (int i = 0; i < 16; i += 4) {
-            const float4 wv = __ldg(reinterpret_cast<const float4*>(f + F_HW2 + o * 64 + uu + i));
-            z[o] = fmaf(wv.x, h[i], z[o]);
-            z[o] = fmaf(wv.y, h[i + 1], z[o]);
-            z[o] = fmaf(wv.z, h[i + 2], z[o]);
-            z[o] = fmaf(wv.w, h[i + 3], z[o]);
-          }
-        }
-      }
+      head_out_quarter(lane_base + G::kColH, quarter, f, z);
       // the four quarters' partial logits through the row's TMEM lane
       tmem_st8(scr + 16 + 8 * quarter, z);
       asm volatile("tcgen05.fence::before_thread_sync;");
-      epi_sync();
+      quad_sync();
       asm volatile("tcgen05.fence::after_thread_sync;");
       if (quarter == 0) {
         float zz[32];
@@ -391,8 +371,8 @@ k_mlp_pair(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
 #pragma unroll
           for (int o = 0; o < 8; ++o)
             z[o] = ((zz[o] + zz[8 + o]) + (zz[16 + o] + zz[24 + o])) + __ldg(f + F_HB2 + o);
-          sample_write(z, row, s, n_rows, io.mm[s], mm_stride, io.bm[s], bm_stride, u,
-                       io.act[s], act_stride, logp_out, value_out, logits_out);
+          sample_write(z, row, s, n_rows, sin[s], io.act[s], act_stride, logp_out, value_out,
+                       logits_out);
         }
       }
     }

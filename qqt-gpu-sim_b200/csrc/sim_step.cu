@@ -236,6 +236,9 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
       env_hz = HZ && st.hazard[e];
     }
   }
+  // the fused observation's fuse tables (warp 0 writes them) are visible
+  // to every warp after the barrier below
+  if (OBS) fuse_tables(ft, a.cfg.fuse_f);
   load_tile(tile, st, N, e0, PL_ALL);
   __syncthreads();
   const StepLayout L = step_layout(C, step_row_bytes(cfg, OBS));
@@ -254,7 +257,6 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
   PShared* ps = (PShared*)(wb + L.ps);
   PInfo* pinfo = (PInfo*)(wb + L.pinfo);
   float* dng = (float*)(wb + L.dng);
-  if (OBS) fuse_tables(ft, a.cfg.fuse_f);
   const int tiers = PHASE == PHASE_PLACE ? 0 : *a.tiers;
   const float INF = __int_as_float(0x7f800000);
 
