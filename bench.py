@@ -768,6 +768,121 @@ def _reference_stress(args, procs):
                     "d2h_bytes_per_step": 0}}
 
 
+# ------------------------------------------------------- phase stamps
+
+PHASES = {
+    2: ("step (lane 0 of every warp of every 4th block)",
+        [0, 16, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 17],
+        ["tile staging", "per-env set-up", "countdown + placement", "placement bonus",
+         "movement", "chain explosion", "damage", "clearing + bomb list", "t / done",
+         "rewards", "danger standing", "terminal rewards", "outputs", "device reset",
+         "danger paint + observation + masks", "player stores", "barrier + write-back"], True),
+    1: ("MLP policy, epilogue warp 2 (one record per CTA)",
+        [0, 1, 7, 8, 9, 10, 11, 12, 13, 14],
+        ["set-up (barriers, TMEM)", "layer 1 (wait for its MMAs)", "LN1 + operand",
+         "layer-2 MMAs", "LN2 + operand", "head MMAs", "output layers",
+         "logit reduce + sampling", "exit"], False),
+}
+
+
+def phase_table(rec, kid):
+    """Per-phase durations (us) of kernel `kid` from phase-stamp records:
+    the k-th record of a (block[, warp], phase) is that block's k-th launch."""
+    import numpy as np
+    title, order, names, by_warp = PHASES[kid]
+    w0 = rec[:, 0]
+    t = rec[:, 1].astype(np.int64)
+    k = (w0 >> np.uint64(56)).astype(np.int64)
+    ph = ((w0 >> np.uint64(48)) & np.uint64(0xff)).astype(np.int64)
+    blk = ((w0 >> np.uint64(8)) & np.uint64(0xffffff)).astype(np.int64)
+    wp = (w0 & np.uint64(0xff)).astype(np.int64)
+    key = blk * 64 + wp if by_warp else blk
+    cols = []
+    for p in order:
+        m = (k == kid) & (ph == p)
+        kk, tt = key[m], t[m]
+        o = np.lexsort((tt, kk))
+        kk, tt = kk[o], tt[o]
+        start = np.r_[0, np.flatnonzero(kk[1:] != kk[:-1]) + 1]
+        occ = np.arange(len(kk)) - np.repeat(start, np.diff(np.r_[start, len(kk)]))
+        cols.append(dict(zip(zip(kk.tolist(), occ.tolist()), tt.tolist())))
+    common = set(cols[0])
+    for c in cols[1:]:
+        common &= set(c)
+    if not common:
+        return [f"{title}: no records"]
+    keys = sorted(common)
+    T = np.array([[c[x] for c in cols] for x in keys], dtype=np.int64)
+    D = np.diff(T, axis=1) / 1000.0
+    tot = (T[:, -1] - T[:, 0]) / 1000.0
+    out = [f"{title}: {len(keys)} samples, total mean {tot.mean():.2f} us, "
+           f"p50 {np.median(tot):.2f}, p95 {np.percentile(tot, 95):.2f}"]
+    for j, nm in enumerate(names):
+        out.append(f"  {nm:36s} mean {D[:, j].mean():6.2f}  p50 {np.median(D[:, j]):6.2f}"
+                   f"  p95 {np.percentile(D[:, j], 95):6.2f}")
+    return out
+
+
+def phase_stamps_leg(args):
+    """Per-phase durations of the step and policy kernels, from the
+    phase-stamp build of the library (build.py --phase-stamps): one captured
+    rollout of the configured workload after warm-up replays, then 20 policy
+    launches of one env group alone.  Prints tables, no JSON line."""
+    import ctypes
+    import numpy as np
+    import torch
+    from qqt_b200 import _capi
+    _capi.LIB_PATH = os.path.join(os.path.dirname(_capi.LIB_PATH), "libqqt_b200_phase.so")
+    L = _capi.lib()
+    cap = 8_000_000
+
+    def read():
+        buf = np.zeros((cap, 2), np.uint64)
+        n = ctypes.c_uint32(0)
+        _capi.check(L.qqt_phase_read(buf.ctypes.data, cap, ctypes.byref(n)), "qqt_phase_read")
+        return buf[: n.value]
+
+    torch.cuda.set_device(0)
+    grp, gen = build_engine("cuda:0", 0, args.slots, 1 if CFG["ppo"] else args.groups)
+    for ro in grp.ros:
+        ro.draws.generate(gen)
+        ro.tick(0)
+    grp.collect()
+    grp.capture()
+    for _ in range(3):
+        for ro in grp.ros:
+            ro.draws.generate(gen)
+        grp.replay()
+    for ro in grp.ros:
+        ro.draws.generate(gen)
+    torch.cuda.synchronize()
+    _capi.check(L.qqt_phase_reset(), "qqt_phase_reset")
+    grp.replay()
+    torch.cuda.synchronize()
+    rec = read()
+    lines = [f"phase stamps, {args.config}: {N_ENVS} envs per GPU in {len(grp.ros)} group(s), "
+             f"one {TICKS}-tick rollout replay ({len(rec)} records)"]
+    for kid in (2, 1):
+        lines += phase_table(rec, kid)
+    ro = grp.ros[0]
+    b = 5 % ro.slots
+    obs, mm, bm, acts = ro.buf.obs(b), ro.buf.mm[b], ro.buf.bm[b], ro.buf.act[b]
+    seats = list(ro.seats)
+    pol = lambda: ro.learner.act_seats(obs, [mm[:, s] for s in seats], [bm[:, s] for s in seats],
+                                       ro.draws.u_net[b], [acts[:, s] for s in seats],
+                                       ro.buf.logp[b], ro.buf.val[b])
+    for _ in range(5):
+        pol()
+    torch.cuda.synchronize()
+    _capi.check(L.qqt_phase_reset(), "qqt_phase_reset")
+    for _ in range(20):
+        pol()
+        torch.cuda.synchronize()
+    lines.append(f"policy alone: 20 launches over one group's {ro.sim.num_envs} envs")
+    lines += phase_table(read(), 1)
+    print("\n".join(lines), file=sys.stderr)
+
+
 def main():
     # exactly one line on stdout: libraries (NCCL's version banner, ...) print
     # to file descriptor 1, so it points at stderr and the JSON line goes to a
@@ -794,6 +909,9 @@ def main():
                     help="independent env groups per GPU, each on its own stream")
     ap.add_argument("--slots", type=int, default=0,
                     help="rollout-buffer slots (0 = one per tick; fewer = ring, profiling only)")
+    ap.add_argument("--phase-stamps", action="store_true",
+                    help="print per-phase kernel durations from the phase-stamp build "
+                         "(build.py --phase-stamps) instead of the JSON line")
     args = ap.parse_args()
     global CFG, N_ENVS, TICKS
     CFG = CONFIGS[args.config]
@@ -802,7 +920,10 @@ def main():
     args.cpu_ticks = args.cpu_ticks or CFG["cpu"][1]
     if TICKS % 16:
         raise SystemExit("--ticks must be a multiple of 16")
-    if args.impl == "reference":
+    if args.phase_stamps:
+        phase_stamps_leg(args)
+        out = None
+    elif args.impl == "reference":
         out = reference_arm(args)
     elif args.config == "cfg3":
         out = stress_bench(args)

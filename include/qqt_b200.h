@@ -488,6 +488,16 @@ int qqt_get_error(uint32_t *code_out);
  * (the default) turns the check off.  Host-global setting. */
 int qqt_test_set_wait_polls(uint32_t polls);
 
+/* Phase stamps (no counterpart in the reference).  A library built with
+ * `build.py --phase-stamps` (libqqt_b200_phase.so) records, at the phase
+ * boundaries of the step and MLP policy kernels, 16-byte records: word 0 =
+ * kernel id << 56 | phase << 48 | SM << 32 | block << 8 | warp, word 1 =
+ * the globaltimer in ns.  qqt_phase_read copies up to `cap` records to
+ * host memory (n_out = the count) and qqt_phase_reset clears the ring.
+ * The regular library returns QQT_E_ARG from both. */
+int qqt_phase_read(uint64_t *host, uint32_t cap, uint32_t *n_out);
+int qqt_phase_reset(void);
+
 /* Library version string. */
 const char *qqt_version(void);
 

@@ -880,6 +880,7 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
   const int kt0 = rank * k_tiles / ks, kt1 = (rank + 1) * k_tiles / ks;
   const int n_kt = kt1 - kt0;
   const uint32_t tmem_cols = leader ? G::kTmemCols : G::kL1Cols;
+  QQT_PH_START(ph_t0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < G::kStages; ++s) {
@@ -908,6 +909,8 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
     cluster_arrive();
     cluster_wait();
   }
+  QQT_PH_AT(1, 0, ph_t0, threadIdx.x == 0);
+  QQT_PH(1, 1, threadIdx.x == 0);
   const uint32_t tmem = *tmem_slot;
   bool arrived = false;   // this thread's arrival on the closing cluster barrier
   if (test_wait) {
@@ -968,7 +971,9 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         tma_load_2d(&tm_b, &full[s], st + G::kAAll, kx, 0);
         tma_load_2d(&tm_b, &full[s], st + G::kAAll + G::kBBytes, kx, NT);
         issued_until = kt + 1;
+        QQT_PH(1, 2, kt == 0);
       }
+      QQT_PH(1, 3, true);
       // drain: every issued stage must land before the CTA may exit
       for (int kt = max(0, issued_until - G::kStages); kt < issued_until; ++kt)
         mbar_wait(&full[kt % G::kStages], (kt / G::kStages) & 1);
@@ -1009,11 +1014,13 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         umma_commit(&empty[s]);
       }
       umma_commit(accb);   // fires once every issued MMA has completed
+      QQT_PH(1, 4, true);
       if (leader) {
         // the pipeline region is free once layer 1's MMAs are done: bring in
         // the tail weight images (all CTAs read the same 160 KB, an L2 hit)
         bool loaded = false;
         if (mbar_wait(accb, 0) && ok) {
+          QQT_PH(1, 5, true);
           mbar_expect_tx(wbar, kImgBytes);
           for (uint32_t o = 0; o < kImgBytes; o += 16384) bulk_load(smem + o, img + o, 16384, wbar);
           loaded = true;
@@ -1025,6 +1032,7 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         uint8_t* a_lo = a_hi + G::kActBytes;
         int committed = 0;
         if (loaded && !mbar_wait(wbar, 0)) *abort_flag = 1;
+        QQT_PH(1, 6, true);
         for (int s = 0; s < S && !*abort_flag; ++s) {
           // layer 2: D2 overwrites this seat's layer-1 columns (already read)
           if (!mbar_wait(abar, (2 * s) & 1)) { *abort_flag = 1; break; }
@@ -1068,6 +1076,10 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         sin[s] = sample_load(row, seat0 + s, n_rows, io.mm[s], mm_stride, io.bm[s], bm_stride, u);
     }
     bool ok = epi_and(mbar_wait(accb, 0) && *abort_flag == 0);
+    QQT_PH(1, 7, warp == 2 && lane == 0);
+    // layer 1 is done: a kernel launched as this one's programmatic
+    // dependent (the simulator step) may start staging its state now
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("tcgen05.fence::after_thread_sync;");
     // this thread's 32 layer-1 sums of seat s (one seat: A W_hi + A W_lo)
     auto ld_layer1 = [&](int s, float* x) {
@@ -1131,9 +1143,11 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         fence_proxy_async();
         asm volatile("tcgen05.fence::before_thread_sync;");
         mbar_arrive(abar);
+        QQT_PH(1, 8, warp == 2 && lane == 0);
         // LN2 over layer 2
         ok = epi_and(mbar_wait(dbar, (2 * s) & 1) && *abort_flag == 0);
         if (!ok) break;
+        QQT_PH(1, 9, warp == 2 && lane == 0);
         asm volatile("tcgen05.fence::after_thread_sync;");
         tmem_ld32(lane_base + 128 * s + 32 * quarter, x);
         bias_ln_relu_quarter(x, quarter, scr + 8, f + F_B1, f + F_LN2G, f + F_LN2B,
@@ -1143,15 +1157,18 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         fence_proxy_async();
         asm volatile("tcgen05.fence::before_thread_sync;");
         mbar_arrive(abar);
+        QQT_PH(1, 10, warp == 2 && lane == 0);
         // head hidden units -> this quarter's partial output logits
         ok = epi_and(mbar_wait(dbar, (2 * s + 1) & 1) && *abort_flag == 0);
         if (!ok) break;
+        QQT_PH(1, 11, warp == 2 && lane == 0);
         asm volatile("tcgen05.fence::after_thread_sync;");
         float z[8];
 #pragma unroll
         for (int o = 0; o < 8; ++o) z[o] = 0.f;
         head_out_quarter(lane_base + G::kColH, quarter, f, z);
         // the four quarters' partial logits through the row's TMEM lane
+        QQT_PH(1, 12, warp == 2 && lane == 0);
         tmem_st8(scr + 16 + 8 * quarter, z);
         asm volatile("tcgen05.fence::before_thread_sync;");
         quad_sync();
@@ -1173,6 +1190,7 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         }
       }
       if (!ok) *abort_flag = 1;
+      QQT_PH(1, 13, warp == 2 && lane == 0);
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
@@ -1186,6 +1204,7 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(tmem_cols));
   }
+  QQT_PH(1, 14, threadIdx.x == 0);
 }
 
 // Split-K factor for a launch of m_tiles row tiles over k_tiles K tiles:

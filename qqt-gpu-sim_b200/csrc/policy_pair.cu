@@ -318,6 +318,9 @@ k_mlp_pair(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
     // keeps the CTA resident until that arrival has landed
     bool ok = mbar_wait(accb, 0);
     ok = epi_and(ok && *abort_flag == 0);
+    // layer 1 is done: a kernel launched as this one's programmatic
+    // dependent (the simulator step) may start staging its state now
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("tcgen05.fence::after_thread_sync;");
     // this CTA's activation operand is written: the generic-proxy stores
     // are made visible to the tensor cores, the TMEM reads of the columns

@@ -7,3 +7,4 @@
 #include "policy_cnn.cu"
 #include "train_gae.cu"
 #include "train_mlp.cu"
+#include "phase_stamps.cu"

@@ -37,6 +37,52 @@ __device__ unsigned int g_error = 0;   // device error word (qqt_get_error)
 
 __device__ __forceinline__ void flag_error(unsigned bits) { atomicOr(&g_error, bits); }
 
+// Phase stamps (build.py --phase-stamps, QQT_PHASE_STAMPS): kernels append
+// (kernel id, phase, SM, block, warp, globaltimer ns) records at their phase
+// boundaries to a device ring that qqt_phase_read copies out; the regular
+// build compiles every stamp to nothing.  Kernel ids: 1 the MLP policy, 2
+// the simulator step.
+#ifdef QQT_PHASE_STAMPS
+#define QQT_PH_CAP 8000000u
+__device__ unsigned long long g_ph[2 * QQT_PH_CAP];
+__device__ unsigned int g_ph_n;
+__device__ __forceinline__ unsigned long long ph_now() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void ph_rec(unsigned kid, unsigned ph, unsigned long long t) {
+  unsigned smid;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+  const unsigned i = atomicAdd(&g_ph_n, 1u);
+  if (i < QQT_PH_CAP) {
+    g_ph[2 * i] = ((unsigned long long)kid << 56) | ((unsigned long long)ph << 48) |
+                  ((unsigned long long)smid << 32) | ((unsigned long long)blockIdx.x << 8) |
+                  (threadIdx.x >> 5);
+    g_ph[2 * i + 1] = t;
+  }
+}
+#define QQT_PH_START(var) const unsigned long long var = ph_now()
+#define QQT_PH(kid, ph, cond) \
+  do {                        \
+    if (cond) ph_rec((kid), (ph), ph_now()); \
+  } while (0)
+#define QQT_PH_AT(kid, ph, t, cond) \
+  do {                              \
+    if (cond) ph_rec((kid), (ph), (t)); \
+  } while (0)
+#else
+#define QQT_PH_START(var) \
+  do {                    \
+  } while (0)
+#define QQT_PH(kid, ph, cond) \
+  do {                        \
+  } while (0)
+#define QQT_PH_AT(kid, ph, t, cond) \
+  do {                              \
+  } while (0)
+#endif
+
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
 
@@ -271,8 +317,10 @@ __device__ __forceinline__ int blast_of(const Env& v, int c, int default_blast) 
   return b > 0 ? b : default_blast;
 }
 
-__constant__ const int kDR[4] = {-1, 1, 0, 0};
-__constant__ const int kDC[4] = {0, 0, -1, 1};
+// Direction d (0 up, 1 down, 2 left, 3 right) as row / column steps,
+// computed (no table: a per-lane d would serialise constant-cache reads).
+__device__ __forceinline__ int dir_dr(int d) { return d == 0 ? -1 : (d == 1 ? 1 : 0); }
+__device__ __forceinline__ int dir_dc(int d) { return d == 2 ? -1 : (d == 3 ? 1 : 0); }
 
 // ------------------------------------------------------------- fire rays
 
@@ -290,8 +338,8 @@ __device__ inline void emit_flame(const Env& v, int src, int blast, int tier_cap
   for (int d = 0; d < 4; ++d) {
     int r = r0, c = c0;
     for (int k = 1; k <= blast; ++k) {
-      r += kDR[d];
-      c += kDC[d];
+      r += dir_dr(d);
+      c += dir_dc(d);
       if (r < 0 || r >= v.h || c < 0 || c >= v.w) break;
       const int q = r * v.w + c;
       if (v.wall[q]) break;
@@ -313,8 +361,8 @@ __device__ inline void emit_flame_queue(const Env& v, int src, int blast, int ti
   for (int d = 0; d < 4; ++d) {
     int r = r0, c = c0;
     for (int k = 1; k <= blast; ++k) {
-      r += kDR[d];
-      c += kDC[d];
+      r += dir_dr(d);
+      c += dir_dc(d);
       if (r < 0 || r >= v.h || c < 0 || c >= v.w) break;
       const int q = r * v.w + c;
       if (v.wall[q]) break;
@@ -351,8 +399,8 @@ __device__ inline float reach_max(const Env& v, int c, const float* val, int def
   for (int d = 0; d < 4; ++d) {
     int r = r0, cc = c0;
     for (int k = 1; k <= max_b; ++k) {
-      r -= kDR[d];
-      cc -= kDC[d];
+      r -= dir_dr(d);
+      cc -= dir_dc(d);
       if (r < 0 || r >= v.h || cc < 0 || cc >= v.w) break;
       const int q = r * v.w + cc;
       if (v.wall[q]) break;
@@ -414,8 +462,8 @@ __device__ inline int danger_stage_a(const Env& v, const DangerScratch& s, float
       const int bl = blast_of(v, f, default_blast);
       int rr = f / v.w, cc = f - rr * v.w;
       for (int k = 1; k <= bl; ++k) {
-        rr += kDR[d];
-        cc += kDC[d];
+        rr += dir_dr(d);
+        cc += dir_dc(d);
         if (rr < 0 || rr >= v.h || cc < 0 || cc >= v.w) break;
         const int c = rr * v.w + cc;
         if (v.wall[c]) break;
@@ -452,6 +500,40 @@ __device__ __forceinline__ float danger_at(const Env& v, const DangerScratch& s,
   return fmaxf(own, reach_max(v, c, s.cur, default_blast, max_b));
 }
 
+// danger_at for every player at once (warp-wide): lane 4 p + d walks
+// direction d from player p's cell `cell` (lane p's value), the four lanes
+// of a player combine by max (exact, so the same value as danger_at), and
+// lane p (p < P) returns the player's danger; other lanes return 0.
+__device__ inline float danger_at_players(const Env& v, const DangerScratch& s, int cell,
+                                          int default_blast, int max_b, int P) {
+  const int lane = lane_id();
+  const int p = lane >> 2, d = lane & 3;
+  const int c = __shfl_sync(QQT_FULL, cell, p);
+  float best = 0.f;
+  if (p < P) {
+    const int r0 = c / v.w, c0 = c - r0 * v.w;
+    int r = r0, cc = c0;
+    for (int k = 1; k <= max_b; ++k) {
+      r -= dir_dr(d);
+      cc -= dir_dc(d);
+      if (r < 0 || r >= v.h || cc < 0 || cc >= v.w) break;
+      const int q = r * v.w + cc;
+      if (v.wall[q]) break;
+      if (v.fuse[q] > 0) {
+        if (k <= blast_of(v, q, default_blast)) best = s.cur[q];
+        break;
+      }
+      if (v.brick[q]) break;
+    }
+  }
+  best = fmaxf(best, __shfl_xor_sync(QQT_FULL, best, 1));
+  best = fmaxf(best, __shfl_xor_sync(QQT_FULL, best, 2));
+  const float reach = __shfl_sync(QQT_FULL, best, (4 * lane) & 31);
+  if (lane >= P || v.wall[cell]) return 0.f;
+  const float own = v.fuse[cell] > 0 ? s.cur[cell] : 0.f;
+  return fmaxf(own, reach);
+}
+
 // Stage B for a whole env (sim/blast.py:291-317), scatter form: out[c] =
 // the cell's own bomb weight (0 elsewhere, walls 0), raised by every bomb's
 // corrected weight along its four rays.  Lane (bomb, direction) walks
@@ -477,8 +559,8 @@ __device__ inline void danger_paint(const Env& v, const DangerScratch& s, int nb
     const int bl = blast_of(v, q, default_blast);
     int r = q / v.w, cc = q - r * v.w;
     for (int k = 1; k <= bl; ++k) {
-      r += kDR[d];
-      cc += kDC[d];
+      r += dir_dr(d);
+      cc += dir_dc(d);
       if (r < 0 || r >= v.h || cc < 0 || cc >= v.w) break;
       const int c = r * v.w + cc;
       if (v.wall[c]) break;

@@ -194,6 +194,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
   const int P = NP > 0 ? NP : cfg.n_players;
   const int e0 = blockIdx.x * QQT_TILE_E;
   const int lane = lane_id();
+  QQT_PH_START(ph_t0);
   Tile tile = carve_tile(smem, C);
   if (threadIdx.x == 0) dirty = 0;
   // the warp's env (one per warp): its per-player state and draws are loaded
@@ -225,8 +226,6 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
         me.last_hit = st.last_hit[i];
         me.lo_b = st.lo_bombs[i];
         me.lo_z = st.lo_blast[i];
-        act_mv = a.actions[((size_t)e * P + p) * 2];
-        act_bo = a.actions[((size_t)e * P + p) * 2 + 1];
         // the rewards' per-tick draws, loaded with the rest of the player state
         me.rb_hit = cfg.corridor ? a.rb_hit[(size_t)e * P + p] : 0.f;
         me.rb_grow = cfg.corridor ? a.rb_grow[(size_t)e * P + p] : 0.f;
@@ -241,6 +240,21 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
   if (OBS) fuse_tables(ft, a.cfg.fuse_f);
   load_tile(tile, st, N, e0, PL_ALL);
   __syncthreads();
+  QQT_PH_AT(2, 0, ph_t0, (blockIdx.x & 3) == 0 && lane == 0);
+  QQT_PH(2, 16, (blockIdx.x & 3) == 0 && lane == 0);
+  // Launched as a programmatic dependent (launch_step): the state staged
+  // above is no kernel's output but the previous step's, so it may be read
+  // while the kernel before this one (the policy, which triggers its
+  // dependents once its first layer is done) still runs.  The actions it
+  // writes are read only after this wait, and nothing is written before it.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  {
+    const int e = e0 + warp_id();
+    if (e < N && lane < P) {
+      act_mv = a.actions[((size_t)e * P + lane) * 2];
+      act_bo = a.actions[((size_t)e * P + lane) * 2 + 1];
+    }
+  }
   const StepLayout L = step_layout(C, step_row_bytes(cfg, OBS));
   uint8_t* wb = smem + tile_bytes(C) + (size_t)warp_id() * L.total;
   uint8_t* cov = wb + L.cov;
@@ -272,6 +286,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
       me.flat0 = center_cell(me.y, me.x, h, w);
       me.placed = 0;
     }
+    QQT_PH(2, 1, (blockIdx.x & 3) == 0 && lane == 0);
     // ---- 1-2. countdown and sequential placement
     int ns0 = -1;                     // explosion sources in `list` (-1: not yet)
     if (PHASE != PHASE_AFTER_PLACE) {
@@ -353,6 +368,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
     }
     const float a0f = (p < P && me.alive0) ? 1.f : 0.f;
 
+    QQT_PH(2, 2, (blockIdx.x & 3) == 0 && lane == 0);
     // ---- 3. placement bonus (sim/torch_sim.py:1263-1355)
     float bonus = 0.f;
     if (p < P) {
@@ -365,8 +381,8 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
           int r = r0, cc = c0;
           for (int k = (d < 0 ? 0 : 1); k <= (d < 0 ? 0 : b); ++k) {
             if (d >= 0) {
-              r += kDR[d];
-              cc += kDC[d];
+              r += dir_dr(d);
+              cc += dir_dc(d);
               if (r < 0 || r >= h || cc < 0 || cc >= w) break;
             }
             const int q = r * w + cc;
@@ -395,8 +411,8 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
               const int dist_cells = abs(orow - r0) + abs(ocol - c0);
               int r = r0, cc = c0;
               for (int k = 1; k <= b && k <= dist_cells; ++k) {
-                r += kDR[d];
-                cc += kDC[d];
+                r += dir_dr(d);
+                cc += dir_dc(d);
                 const int q = r * w + cc;
                 if (v.wall[q]) break;
                 if (k == dist_cells) under = true;
@@ -419,6 +435,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
       // ---- 4. passivity counter
       me.since = me.placed ? 0 : me.since + 1;
     }
+    QQT_PH(2, 3, (blockIdx.x & 3) == 0 && lane == 0);
     // ---- 5. movement (sim/move.py:234-279).  Both axes slide from the old
     //      position, so lane p resolves player p along the rows and lane
     //      P + p along the columns at the same time.
@@ -453,6 +470,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
       }
     }
 
+    QQT_PH(2, 4, (blockIdx.x & 3) == 0 && lane == 0);
     // ---- 6. chain explosion (sim/blast.py:101-155).  Round r triggers the
     //      live bombs covered by the flames so far; a flame that covers a
     //      live untriggered bomb queues it (once) for the next round, so a
@@ -517,6 +535,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
     // ---- 8. (bricks burnt: in the clearing pass below; damage reads only
     //      the flame plane)
 
+    QQT_PH(2, 5, (blockIdx.x & 3) == 0 && lane == 0);
     // ---- 9. damage and invulnerability
     int flat1 = 0, hp_new = 0, alive = 0, died = 0, lost_hp = 0;
     if (p < P) {
@@ -531,6 +550,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
       if (hit_eff) me.invuln = cfg.invuln_ticks;
     }
     __syncwarp();
+    QQT_PH(2, 6, (blockIdx.x & 3) == 0 && lane == 0);
     // ---- 8 + 10. one pass: burnt bricks become crates on corridor maps,
     //      exploded bombs are cleared, and the bombs left are compacted for
     //      the danger-standing penalty below
@@ -563,6 +583,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
       if (bomb) ds.bombs[nb_post + __popc(m & ((1u << lane) - 1u))] = (uint16_t)c;
       nb_post += __popc(m);
     }
+    QQT_PH(2, 7, (blockIdx.x & 3) == 0 && lane == 0);
     // ---- 11. t and done
     const int64_t t1 = st.t[e] + 1;
     // ---- hazard wave (sim/torch_sim.py:1404-1466)
@@ -572,6 +593,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
     const int n_alive = __popc(amask);
     const bool done = n_alive <= 1 || t1 >= cfg.max_steps;
 
+    QQT_PH(2, 8, (blockIdx.x & 3) == 0 && lane == 0);
     // ---- 12. rewards
     const float dmg = (p < P) ? (float)max(me.hp - hp_new, 0) : 0.f;
     float tot_dmg = 0.f, tot_hp = 0.f;
@@ -627,15 +649,16 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
       atomicOr(&dirty, PL_CRATE | PL_RECYCLE);
     }
     __syncwarp();
+    QQT_PH(2, 9, (blockIdx.x & 3) == 0 && lane == 0);
     // danger standing penalty on the post-step state (sim/torch_sim.py:1163-1182)
     {
       int max_b = 0;
       danger_stage_a(v, ds, cfg.fuse_f, cfg.blast, cfg.danger_rounds, &max_b, nb_post);
-      if (p < P) {
-        const float standing = danger_at(v, ds, flat1, cfg.blast, max_b);
+      const float standing = danger_at_players(v, ds, flat1, cfg.blast, max_b, P);
+      if (p < P)
         reward = __fsub_rn(reward, __fmul_rn(__fmul_rn(cfg.danger_penalty, standing), a0f));
-      }
     }
+    QQT_PH(2, 10, (blockIdx.x & 3) == 0 && lane == 0);
     const bool death_done = done && n_alive == 1;
     const bool all_alive = done && n_alive == P;
     int winner = 0;
@@ -674,6 +697,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
       }
     }
 
+    QQT_PH(2, 11, (blockIdx.x & 3) == 0 && lane == 0);
     // ---- outputs
     if (p < P) {
       const size_t ri = (size_t)e * P + p;
@@ -694,6 +718,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
       }
     }
 
+    QQT_PH(2, 12, (blockIdx.x & 3) == 0 && lane == 0);
     // ---- device reset to the env's template (no host round trip)
     int64_t t_out = t1;
     if (done && a.has_tmpl) {
@@ -738,6 +763,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
       }
       t_out = 0;
     }
+    QQT_PH(2, 13, (blockIdx.x & 3) == 0 && lane == 0);
     // ---- fused observation of the post-step (or reset) state: the next
     //      tick's observation row and legal masks (sim/obs.py:25-229).  The
     //      danger map reuses the danger-standing stage A (same planes); an
@@ -753,6 +779,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
                           me.bombs_cap, t_out, ft, a.obs, nullptr, a.mm, a.bm,
                           (__half*)(wb + L.row));
     }
+    QQT_PH(2, 14, (blockIdx.x & 3) == 0 && lane == 0);
     if (p < P) {
       const size_t i = (size_t)p * N + e;
       st.pos[((size_t)p * 2) * N + e] = me.y;
@@ -773,6 +800,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
         st.lo_spd[i] = me.lo_spd;
       }
     }
+    QQT_PH(2, 15, (blockIdx.x & 3) == 0 && lane == 0);
     if (lane == 0) st.t[e] = t_out;
     __syncwarp();
   }
@@ -780,6 +808,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
   const unsigned planes = (PL_FUSE | PL_OWNER | PL_BLAST) |
                           (PHASE == PHASE_PLACE ? 0u : dirty);
   store_tile(tile, st, N, e0, planes);
+  QQT_PH(2, 17, (blockIdx.x & 3) == 0 && lane == 0);
 }
 
 // Crate recycling on the device (sim/torch_sim.py:549-596 semantics with a
@@ -877,6 +906,17 @@ extern "C" uint64_t qqt_step_scratch_bytes(const QqtCfg* cfg) {
   return ((uint64_t)cfg->n_players * cfg->n_envs + 255) / 256 * 256;
 }
 
+// QQT_STEP_PDL=0 launches the step without programmatic stream
+// serialization (it then starts only once the kernel before it has ended).
+static bool step_pdl_enabled() {
+  static int env = -1;
+  if (env < 0) {
+    const char* e = getenv("QQT_STEP_PDL");
+    env = (e && e[0] == '0') ? 0 : 1;
+  }
+  return env == 1;
+}
+
 static int launch_step(const QqtCfg* cfg, const QqtState* st, const int64_t* actions,
                        const float* rb_hit, const float* rb_grow, int32_t* tiers,
                        int32_t first_step, const QqtStepOut* out, const QqtTemplate* tmpl,
@@ -918,10 +958,24 @@ static int launch_step(const QqtCfg* cfg, const QqtState* st, const int64_t* act
   const size_t sm = tile_bytes(C) + QQT_NWARP * step_warp_bytes(C, step_row_bytes(*cfg, obs != nullptr));
   const int blocks = (cfg->n_envs + QQT_TILE_E - 1) / QQT_TILE_E;
   cudaStream_t s = (cudaStream_t)stream;
+  // programmatic stream serialization: the step may start (stage its tile)
+  // once the kernel before it in the stream has triggered its dependents;
+  // kernels that never trigger (all but the policy) serialise as usual
+  const bool pdl = step_pdl_enabled();
   auto launch = [&](auto kern, int phase) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
     p.phase = phase;
-    kern<<<blocks, QQT_NWARP * 32, sm, s>>>(p);
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)blocks, 1, 1);
+    lc.blockDim = dim3(QQT_NWARP * 32, 1, 1);
+    lc.dynamicSmemBytes = sm;
+    lc.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = at;
+    lc.numAttrs = pdl ? 1 : 0;
+    cudaLaunchKernelEx(&lc, kern, p);
   };
   const bool fused = obs != nullptr;
   const bool hz = cfg->hazard_on != 0;

@@ -137,6 +137,8 @@ def lib():
                                                c_i32, c_p, c_i32, c_p, c_p, c_p, c_p, c_p]),
             "qqt_mlp_train_work_bytes": (c_u64, [c_i32]),
             "qqt_get_error": (c_i32, [P(ctypes.c_uint32)]),
+            "qqt_phase_read": (c_i32, [c_p, ctypes.c_uint32, P(ctypes.c_uint32)]),
+            "qqt_phase_reset": (c_i32, []),
             "qqt_version": (ctypes.c_char_p, []),
         }
         optional = {

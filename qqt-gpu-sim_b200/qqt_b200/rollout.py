@@ -100,7 +100,7 @@ class Rollout:
         self.buf = DeviceRolloutBuffer(self.slots, sim.num_envs, self.p, len(self.seats),
                                        sim.obs_stride, cfg.obs_shape, sim.device)
         # the learner and the opponent both read only this tick's observation
-        # and masks: they run as two concurrent branches (policy on a side
+        # and masks: they run as two concurrent branches (the bot on a side
         # stream) that join before the step
         self.side = torch.cuda.Stream(sim.device) if opponent is not None else None
         self.draws = RolloutDraws.empty(T, sim.num_envs, self.p, len(self.seats), sim.device)
@@ -141,19 +141,21 @@ class Rollout:
             self.learner.act_seats(obs, [mm[:, s] for s in self.seats],
                                    [bm[:, s] for s in self.seats], dr.u_net[t],
                                    [acts[:, s] for s in self.seats], buf.logp[b], buf.val[b])
-        if self.side is not None:
-            self.side.wait_stream(main)
-            with torch.cuda.stream(self.side):
-                self._run("policy", learner)
-        else:
-            self._run("policy", learner)
+        # the opponent bot runs on the side stream and the learner's policy
+        # on the tick's stream right before the step, so the step (launched
+        # as the policy's programmatic dependent) can stage its state while
+        # the policy finishes
         if self.opponent is not None:
             o = self.opp_seat
             bot = self.opponent
             self.feed_opponent(t)
-            self._run("bot", lambda: bot.act(obs, mm[:, o], bm[:, o], o, out=acts[:, o]))
-            if self.cap_log is not None and isinstance(bot, AstarBot):
-                self.cap_log[t:t + 1].copy_(bot.chain_scan_len())
+            self.side.wait_stream(main)
+            with torch.cuda.stream(self.side):
+                self._run("bot", lambda: bot.act(obs, mm[:, o], bm[:, o], o, out=acts[:, o]))
+                if self.cap_log is not None and isinstance(bot, AstarBot):
+                    self.cap_log[t:t + 1].copy_(bot.chain_scan_len())
+        self._run("policy", learner)
+        if self.opponent is not None:
             main.wait_stream(self.side)
         flush = bool(self.flush_every) and t % self.flush_every == self.flush_every - 1
         nxt = None
@@ -226,7 +228,7 @@ class RolloutGroups:
     whole T-tick rollout of every group is still one CUDA graph.
 
     `Rollout.tick` has no cross-group dependency: each group's kernels are
-    ordered only by its own stream (plus its policy side stream)."""
+    ordered only by its own stream (plus its bot side stream)."""
 
     def __init__(self, rollouts):
         self.ros = list(rollouts)
