@@ -772,11 +772,13 @@ def _reference_stress(args, procs):
 
 PHASES = {
     2: ("step (lane 0 of every warp of every 4th block)",
-        [0, 16, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 17],
+        [0, 16, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 18, 19, 20, 21, 22, 14, 15, 17],
         ["tile staging", "per-env set-up", "countdown + placement", "placement bonus",
          "movement", "chain explosion", "damage", "clearing + bomb list", "t / done",
          "rewards", "danger standing", "terminal rewards", "outputs", "device reset",
-         "danger paint + observation + masks", "player stores", "barrier + write-back"], True),
+         "danger paint", "observation: player info", "observation: zero row",
+         "observation: channels", "observation: row out", "legal masks", "player stores",
+         "barrier + write-back"], True),
     1: ("MLP policy, epilogue warp 2 (one record per CTA)",
         [0, 1, 7, 8, 9, 10, 11, 12, 13, 14],
         ["set-up (barriers, TMEM)", "layer 1 (wait for its MMAs)", "LN1 + operand",

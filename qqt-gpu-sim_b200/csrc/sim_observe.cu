@@ -84,6 +84,7 @@ __device__ inline void observe_env(const QqtCfg& cfg, const Env& v, int e, PInfo
   const int lane = lane_id();
   const int nch = cfg.obs_channels;
   if (STAGED) __syncwarp();   // the staging area reuses scratch read just before
+  QQT_PH(2, 18, STAGED && (blockIdx.x & 3) == 0 && lane == 0);
   if (lane < P) {
     const int p = lane;
     PInfo q;
@@ -117,6 +118,7 @@ __device__ inline void observe_env(const QqtCfg& cfg, const Env& v, int e, PInfo
     pi[p] = q;
   }
   __syncwarp();   // PInfo visible
+  QQT_PH(2, 19, STAGED && (blockIdx.x & 3) == 0 && lane == 0);
 
   const float tv = __fdiv_rn((float)t_e, cfg.max_steps_f);
   T* const grow = obs ? (T*)obs + (size_t)e * cfg.obs_stride : nullptr;
@@ -129,6 +131,7 @@ __device__ inline void observe_env(const QqtCfg& cfg, const Env& v, int e, PInfo
     uint4* s4 = reinterpret_cast<uint4*>(stage);
     for (int k = lane; k < n16; k += 32) s4[k] = make_uint4(0, 0, 0, 0);
     __syncwarp();
+    QQT_PH(2, 20, STAGED && (blockIdx.x & 3) == 0 && lane == 0);
     const T tvh = to_obs<T>(tv);
     const bool extra = nch > 2 * P + 3;
     for (int c = lane; c < C; c += 32) {
@@ -165,8 +168,10 @@ __device__ inline void observe_env(const QqtCfg& cfg, const Env& v, int e, PInfo
       }
     }
     __syncwarp();
+    QQT_PH(2, 21, STAGED && (blockIdx.x & 3) == 0 && lane == 0);
     uint4* dst = reinterpret_cast<uint4*>(grow);
     for (int k = lane; k < n16; k += 32) dst[k] = s4[k];
+    QQT_PH(2, 22, STAGED && (blockIdx.x & 3) == 0 && lane == 0);
   } else if (obs || danger_out) {
     T* row = grow;
     for (int c = lane; c < C; c += 32) {
