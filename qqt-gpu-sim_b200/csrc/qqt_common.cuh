@@ -152,30 +152,6 @@ enum : unsigned {
 
 static_assert(QQT_TILE_E == 8, "vectorised tile transfers move 8-byte / 16-byte chunks");
 
-// Plane pl (bit 1 << pl of PL_*) of the state / the tile.
-__device__ __forceinline__ uint8_t* state_plane(const QqtState& st, int pl) {
-  switch (pl) {
-    case 0: return st.wall;
-    case 1: return st.brick;
-    case 2: return st.crate;
-    case 3: return st.recycle;
-    case 4: return (uint8_t*)st.owner;
-    case 5: return (uint8_t*)st.fuse;
-    default: return (uint8_t*)st.bomb_blast;
-  }
-}
-__device__ __forceinline__ uint8_t* tile_plane(const Tile& t, int pl) {
-  switch (pl) {
-    case 0: return t.wall;
-    case 1: return t.brick;
-    case 2: return t.crate;
-    case 3: return t.recycle;
-    case 4: return (uint8_t*)t.owner;
-    case 5: return (uint8_t*)t.fuse;
-    default: return (uint8_t*)t.blast;
-  }
-}
-
 // Planes are env-major ([N][C]), so a tile (envs e0 .. e0+7) is one
 // contiguous run of 8 * C elements per plane, laid out in shared memory
 // exactly as in global memory ([slot][cell]).  A full tile with 16-byte
@@ -190,55 +166,30 @@ __device__ __forceinline__ bool tile_vector_ok(const QqtState& st, int n, int e0
 }
 
 // Global [N][C] -> shared [slot][cell] for envs e0 .. e0+E-1 (block-wide).
-// Chunk i of the 7 x C chunks is chunk k = i mod C of plane i / C; a
-// thread's chunks are i0, i0 + blockDim, ..., so (plane, k) advance by one
-// subtraction loop instead of a division per chunk.
-__device__ __forceinline__ void tile_chunk_next(int& pl, int& k, int step, int cells) {
-  k += step;
-  while (k >= cells) {
-    k -= cells;
-    ++pl;
-  }
-}
-
+// Thread j moves chunk j (and j + blockDim, ...) of every requested plane:
+// its loads are issued together, then stored.
 __device__ inline void load_tile(const Tile& t, const QqtState& st, int n, int e0,
                                  unsigned planes) {
   const int cells = t.cells;
   if (tile_vector_ok(st, n, e0)) {
-    // kTileBatch accesses per thread are issued before any is consumed, so
-    // their latencies overlap (7 planes x 169 chunks over 256 threads is 4.6)
-    constexpr int kTileBatch = 5;
-    const int step = blockDim.x;
-    int pl = threadIdx.x / cells, k = threadIdx.x - pl * cells;
-    while (pl < 7) {
-      uint4 v[kTileBatch];
-      int bpl[kTileBatch], bk[kTileBatch];
-#pragma unroll
-      for (int b = 0; b < kTileBatch; ++b) {
-        bpl[b] = pl;
-        bk[b] = k;
-        v[b] = make_uint4(0, 0, 0, 0);
-        if (pl < 7 && (planes & (1u << pl))) {
-          if (pl < 5) {
-            const uint2 u = reinterpret_cast<const uint2*>(
-                state_plane(st, pl) + (size_t)e0 * cells)[k];
-            v[b] = make_uint4(u.x, u.y, 0, 0);
-          } else {
-            v[b] = reinterpret_cast<const uint4*>(
-                state_plane(st, pl) + (size_t)e0 * cells * 2)[k];
-          }
-        }
-        if (pl < 7) tile_chunk_next(pl, k, step, cells);
-      }
-#pragma unroll
-      for (int b = 0; b < kTileBatch; ++b) {
-        const int q = bpl[b];
-        if (q >= 7 || !(planes & (1u << q))) continue;
-        if (q < 5)
-          reinterpret_cast<uint2*>(tile_plane(t, q))[bk[b]] = make_uint2(v[b].x, v[b].y);
-        else
-          reinterpret_cast<uint4*>(tile_plane(t, q))[bk[b]] = v[b];
-      }
+    const size_t o = (size_t)e0 * cells;   // element offset of the tile in a plane
+    for (int k = threadIdx.x; k < cells; k += blockDim.x) {
+      const uint2 z2 = make_uint2(0, 0);
+      const uint4 z4 = make_uint4(0, 0, 0, 0);
+      const uint2 wl = (planes & PL_WALL) ? reinterpret_cast<const uint2*>(st.wall + o)[k] : z2;
+      const uint2 br = (planes & PL_BRICK) ? reinterpret_cast<const uint2*>(st.brick + o)[k] : z2;
+      const uint2 cr = (planes & PL_CRATE) ? reinterpret_cast<const uint2*>(st.crate + o)[k] : z2;
+      const uint2 rc = (planes & PL_RECYCLE) ? reinterpret_cast<const uint2*>(st.recycle + o)[k] : z2;
+      const uint2 ow = (planes & PL_OWNER) ? reinterpret_cast<const uint2*>(st.owner + o)[k] : z2;
+      const uint4 fu = (planes & PL_FUSE) ? reinterpret_cast<const uint4*>(st.fuse + o)[k] : z4;
+      const uint4 bl = (planes & PL_BLAST) ? reinterpret_cast<const uint4*>(st.bomb_blast + o)[k] : z4;
+      if (planes & PL_WALL) reinterpret_cast<uint2*>(t.wall)[k] = wl;
+      if (planes & PL_BRICK) reinterpret_cast<uint2*>(t.brick)[k] = br;
+      if (planes & PL_CRATE) reinterpret_cast<uint2*>(t.crate)[k] = cr;
+      if (planes & PL_RECYCLE) reinterpret_cast<uint2*>(t.recycle)[k] = rc;
+      if (planes & PL_OWNER) reinterpret_cast<uint2*>(t.owner)[k] = ow;
+      if (planes & PL_FUSE) reinterpret_cast<uint4*>(t.fuse)[k] = fu;
+      if (planes & PL_BLAST) reinterpret_cast<uint4*>(t.blast)[k] = bl;
     }
     return;
   }
@@ -261,16 +212,22 @@ __device__ inline void store_tile(const Tile& t, const QqtState& st, int n, int 
                                   unsigned planes) {
   const int cells = t.cells;
   if (tile_vector_ok(st, n, e0)) {
-    const int step = blockDim.x;
-    for (int pl = threadIdx.x / cells, k = threadIdx.x - pl * cells; pl < 7;
-         tile_chunk_next(pl, k, step, cells)) {
-      if (!(planes & (1u << pl))) continue;
-      if (pl < 5)
-        reinterpret_cast<uint2*>(state_plane(st, pl) + (size_t)e0 * cells)[k] =
-            reinterpret_cast<const uint2*>(tile_plane(t, pl))[k];
-      else
-        reinterpret_cast<uint4*>(state_plane(st, pl) + (size_t)e0 * cells * 2)[k] =
-            reinterpret_cast<const uint4*>(tile_plane(t, pl))[k];
+    const size_t o = (size_t)e0 * cells;
+    for (int k = threadIdx.x; k < cells; k += blockDim.x) {
+      if (planes & PL_WALL)
+        reinterpret_cast<uint2*>(st.wall + o)[k] = reinterpret_cast<const uint2*>(t.wall)[k];
+      if (planes & PL_BRICK)
+        reinterpret_cast<uint2*>(st.brick + o)[k] = reinterpret_cast<const uint2*>(t.brick)[k];
+      if (planes & PL_CRATE)
+        reinterpret_cast<uint2*>(st.crate + o)[k] = reinterpret_cast<const uint2*>(t.crate)[k];
+      if (planes & PL_RECYCLE)
+        reinterpret_cast<uint2*>(st.recycle + o)[k] = reinterpret_cast<const uint2*>(t.recycle)[k];
+      if (planes & PL_OWNER)
+        reinterpret_cast<uint2*>(st.owner + o)[k] = reinterpret_cast<const uint2*>(t.owner)[k];
+      if (planes & PL_FUSE)
+        reinterpret_cast<uint4*>(st.fuse + o)[k] = reinterpret_cast<const uint4*>(t.fuse)[k];
+      if (planes & PL_BLAST)
+        reinterpret_cast<uint4*>(st.bomb_blast + o)[k] = reinterpret_cast<const uint4*>(t.blast)[k];
     }
     return;
   }
