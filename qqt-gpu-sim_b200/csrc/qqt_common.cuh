@@ -102,6 +102,7 @@ template <class F>
 __device__ __forceinline__ int warp_compact(int n, uint16_t* list, F pred) {
   const int lane = lane_id();
   int count = 0;
+#pragma unroll
   for (int base = 0; base < n; base += 32) {
     const int c = base + lane;
     const bool p = c < n && pred(c);
@@ -506,6 +507,7 @@ __device__ inline float danger_at_players(const Env& v, const DangerScratch& s, 
 __device__ inline void danger_paint(const Env& v, const DangerScratch& s, int nb,
                                     int default_blast, float* out) {
   const int lane = lane_id();
+#pragma unroll
   for (int c = lane; c < v.cells; c += 32)
     out[c] = (v.fuse[c] > 0 && !v.wall[c]) ? s.cur[c] : 0.f;
   __syncwarp();

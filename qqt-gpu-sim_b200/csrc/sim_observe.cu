@@ -129,11 +129,13 @@ __device__ inline void observe_env(const QqtCfg& cfg, const Env& v, int e, PInfo
     // 16-byte aligned: checked by the entry points)
     const int n16 = (int)((size_t)cfg.obs_stride * sizeof(T) / 16);
     uint4* s4 = reinterpret_cast<uint4*>(stage);
+#pragma unroll 4
     for (int k = lane; k < n16; k += 32) s4[k] = make_uint4(0, 0, 0, 0);
     __syncwarp();
     QQT_PH(2, 20, STAGED && (blockIdx.x & 3) == 0 && lane == 0);
     const T tvh = to_obs<T>(tv);
     const bool extra = nch > 2 * P + 3;
+#pragma unroll
     for (int c = lane; c < C; c += 32) {
       const float d = dng[c];
       if (danger_out) danger_out[(size_t)e * C + c] = d;
@@ -170,6 +172,7 @@ __device__ inline void observe_env(const QqtCfg& cfg, const Env& v, int e, PInfo
     __syncwarp();
     QQT_PH(2, 21, STAGED && (blockIdx.x & 3) == 0 && lane == 0);
     uint4* dst = reinterpret_cast<uint4*>(grow);
+#pragma unroll 4
     for (int k = lane; k < n16; k += 32) dst[k] = s4[k];
     QQT_PH(2, 22, STAGED && (blockIdx.x & 3) == 0 && lane == 0);
   } else if (obs || danger_out) {

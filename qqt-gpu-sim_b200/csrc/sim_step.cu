@@ -295,6 +295,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
       // live bombs per owner: one ballot per player and 32 cells
       int live[QQT_MAX_P] = {0, 0, 0, 0};
       ns0 = 0;
+#pragma unroll
       for (int base = 0; base < C; base += 32) {
         const int c = base + lane;
         bool src = false;
@@ -556,6 +557,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
     //      the danger-standing penalty below
     int nb_post = 0;
     int post_live[QQT_MAX_P] = {0, 0, 0, 0};
+#pragma unroll
     for (int base = 0; base < C; base += 32) {
       const int c = base + lane;
       bool bomb = false;
