@@ -497,10 +497,19 @@ __device__ bool relax_two_reg(float* d0, float* d1, const float* cost, int max_p
   return done;
 }
 
-__device__ __forceinline__ int argmin5(const float* s) {
+// First index of the smallest of five values; the running minimum stays in
+// a register (and is returned in *min_out), so the caller's array is only
+// indexed by constants and stays in registers too.
+__device__ __forceinline__ int argmin5(const float* s, float* min_out = nullptr) {
   int best = 0;
+  float bv = s[0];
+#pragma unroll
   for (int k = 1; k < 5; ++k)
-    if (s[k] < s[best]) best = k;
+    if (s[k] < bv) {
+      bv = s[k];
+      best = k;
+    }
+  if (min_out) *min_out = bv;
   return best;
 }
 
@@ -745,13 +754,15 @@ k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const fl
       int move = argmin5(sc);
       bool finite = false;
       float dmv[5];
+#pragma unroll
       for (int j = 0; j < 5; ++j) {
         finite |= sc[j] < INF;
         dmv[j] = j < 4 ? dl[j] : INF;
       }
       if (!finite && legal_m != 0) {
-        const int fm = argmin5(dmv);
-        move = dmv[fm] < INF ? fm : argmin5(dl);
+        float fmin;
+        const int fm = argmin5(dmv, &fmin);
+        move = fmin < INF ? fm : argmin5(dl);
       }
       long long dr_o = 1000000000LL, dc_o = 1000000000LL;
       for (int o = 0; o < P; ++o) {
@@ -851,7 +862,9 @@ __global__ void k_greedy(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, 
   }
   const uint8_t* mrow = io.mm + (size_t)e * io.mm_stride;
   int best = 0, esc_d = 0;
-  float best_s = INF, esc_s = INF;
+  // best_dng = dng[best] without a run-time index into dng
+  float best_s = INF, esc_s = INF, best_dng = dng[0];
+#pragma unroll
   for (int k = 0; k < 5; ++k) {
     const bool legal = mrow[k] && !blk[k];
     const float nz = __fmul_rn(0.05f, noise[(size_t)e * 5 + k]);
@@ -859,6 +872,7 @@ __global__ void k_greedy(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, 
     if (sc < best_s) {
       best_s = sc;
       best = k;
+      best_dng = dng[k];
     }
     const float es = legal ? dng[k] : INF;
     if (es < esc_s) {
@@ -866,7 +880,7 @@ __global__ void k_greedy(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, 
       esc_d = k;
     }
   }
-  const bool use_safe = best_s < INF && dng[best] < 0.35f;
+  const bool use_safe = best_s < INF && best_dng < 0.35f;
   const int move = use_safe ? best : esc_d;
   const bool place = io.bm[(size_t)e * io.bm_stride + 1] &&
                      dist[4] < (float)st.blast_cap[(size_t)pid * N + e] && own < 0.2f;
