@@ -391,9 +391,11 @@ struct DangerScratch {
 // bomb on a wall cell (a player standing on an obstacle can place one) is a
 // source here as there, and never a target.
 // nb_known >= 0: s.bombs already holds the nb_known bomb cells.
+// wtab (optional): fuse_weight(f, fuse_f) for f = 0..31, read instead of
+// dividing for fuses below 32 (the same values).
 __device__ inline int danger_stage_a(const Env& v, const DangerScratch& s, float fuse_f,
                                      int default_blast, int rounds, int* max_b_out,
-                                     int nb_known = -1) {
+                                     int nb_known = -1, const float* wtab = nullptr) {
   const int lane = lane_id();
   const int nb = nb_known >= 0 ? nb_known
                                : warp_compact(v.cells, s.bombs, [&](int c) { return v.fuse[c] > 0; });
@@ -402,7 +404,8 @@ __device__ inline int danger_stage_a(const Env& v, const DangerScratch& s, float
   int mb = 0;
   for (int i = lane; i < nb; i += 32) {
     const int c = s.bombs[i];
-    const float w = fuse_weight(v.fuse[c], fuse_f);
+    const int f = v.fuse[c];
+    const float w = (wtab && f >= 0 && f < 32) ? wtab[f] : fuse_weight(f, fuse_f);
     s.cur[c] = w;
     s.front[c] = w;
     mb = max(mb, blast_of(v, c, default_blast));

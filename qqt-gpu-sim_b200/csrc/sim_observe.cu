@@ -63,6 +63,7 @@ __device__ __forceinline__ __half to_obs<__half>(float v) { return __float2half_
 // Fuse tables (bit-identical to computing the IEEE division / weight per cell).
 struct FuseTables {
   float weight[32], norm[32];
+  float capv[32];   // i / obs_growth_bombs_max, the observation's bomb-cap value
 };
 
 // One env's observation row, masks and (optionally) danger map from its
@@ -114,7 +115,8 @@ __device__ inline void observe_env(const QqtCfg& cfg, const Env& v, int e, PInfo
     const float cap = fmaxf((float)q.bombs_cap, 1.f);
     const float avail = fmaxf((float)(q.bombs_cap - (int64_t)q.live), 0.f);
     q.avail = __fmul_rn(__fdiv_rn(avail, cap), g);
-    q.capv = __fmul_rn(__fdiv_rn(cap, cfg.obs_growth_bombs_max), g);
+    const int64_t ci = q.bombs_cap > 1 ? q.bombs_cap : 1;   // cap as an integer
+    q.capv = __fmul_rn(ci < 32 ? ft.capv[ci] : __fdiv_rn(cap, cfg.obs_growth_bombs_max), g);
     pi[p] = q;
   }
   __syncwarp();   // PInfo visible
@@ -256,10 +258,11 @@ __device__ inline int live_count_of_lane(const Env& v, int P) {
   return mine;
 }
 
-__device__ inline void fuse_tables(FuseTables& ft, float fuse_f) {
+__device__ inline void fuse_tables(FuseTables& ft, float fuse_f, float growth_bombs_max) {
   if (threadIdx.x < 32) {
     ft.weight[threadIdx.x] = fuse_weight(threadIdx.x, fuse_f);
     ft.norm[threadIdx.x] = __fdiv_rn((float)threadIdx.x, fuse_f);
+    ft.capv[threadIdx.x] = __fdiv_rn((float)threadIdx.x, growth_bombs_max);
   }
 }
 
@@ -271,7 +274,7 @@ k_observe(QqtCfg cfg, QqtState st, void* obs, float* danger_out, uint8_t* mm, ui
   __shared__ FuseTables ft;
   const int h = cfg.height, w = cfg.width, C = h * w, N = cfg.n_envs, P = cfg.n_players;
   const int e0 = blockIdx.x * QQT_TILE_E;
-  fuse_tables(ft, cfg.fuse_f);
+  fuse_tables(ft, cfg.fuse_f, cfg.obs_growth_bombs_max);
   Tile tile = carve_tile(smem, C);
   load_tile(tile, st, N, e0, PL_WALL | PL_BRICK | PL_CRATE | PL_OWNER | PL_FUSE | PL_BLAST);
   __syncthreads();
@@ -304,7 +307,8 @@ k_observe(QqtCfg cfg, QqtState st, void* obs, float* danger_out, uint8_t* mm, ui
     }
     const int64_t g_t = st.t[e];
     int max_b = 0;
-    const int nb = danger_stage_a(v, ds, cfg.fuse_f, cfg.blast, cfg.danger_rounds, &max_b);
+    const int nb = danger_stage_a(v, ds, cfg.fuse_f, cfg.blast, cfg.danger_rounds, &max_b, -1,
+                                  ft.weight);
     danger_paint(v, ds, nb, cfg.blast, dng);
     const int live = live_count_of_lane(v, P);
     observe_env<T>(cfg, v, e, pi, dng, live, g_py, g_px, g_alive != 0, g_inv, g_bcap, g_t, ft,

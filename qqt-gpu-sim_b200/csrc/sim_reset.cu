@@ -72,6 +72,7 @@ k_map_reset(QqtCfg cfg, QqtState st, QqtMapGen g, const uint8_t* __restrict__ do
     if (lane < 32) {
       ft.weight[lane] = fuse_weight(lane, cfg.fuse_f);
       ft.norm[lane] = __fdiv_rn((float)lane, cfg.fuse_f);
+      ft.capv[lane] = __fdiv_rn((float)lane, cfg.obs_growth_bombs_max);
     }
   }
   uint8_t* wb = smem + (size_t)warp_id() * reset_warp_bytes(C);

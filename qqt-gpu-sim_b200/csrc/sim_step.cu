@@ -237,7 +237,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
   }
   // the fused observation's fuse tables (warp 0 writes them) are visible
   // to every warp after the barrier below
-  if (OBS) fuse_tables(ft, a.cfg.fuse_f);
+  if (OBS) fuse_tables(ft, a.cfg.fuse_f, a.cfg.obs_growth_bombs_max);
   load_tile(tile, st, N, e0, PL_ALL);
   __syncthreads();
   QQT_PH_AT(2, 0, ph_t0, (blockIdx.x & 3) == 0 && lane == 0);
@@ -392,7 +392,9 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
               if (o != p && ps[o].flat0 == q && ps[o].alive0) cover = __fadd_rn(cover, 1.f);
             const int fq = v.fuse[q];
             if (fq > 0 && v.owner[q] >= 0 && !placed_map_at(ps, P, q)) {
-              const float frac = fminf(fmaxf(__fdiv_rn((float)fq, cfg.fuse_f), 0.f), 1.f);
+              // fq / fuse from the fuse table when it was built (same division)
+              const float fdiv = (OBS && fq < 32) ? ft.norm[fq] : __fdiv_rn((float)fq, cfg.fuse_f);
+              const float frac = fminf(fmaxf(fdiv, 0.f), 1.f);
               chain = __fadd_rn(chain, __fadd_rn(cfg.chain_time_factor,
                                                  __fmul_rn(cfg.chain_time_rest, __fsub_rn(1.f, frac))));
             }
@@ -655,7 +657,8 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
     // danger standing penalty on the post-step state (sim/torch_sim.py:1163-1182)
     {
       int max_b = 0;
-      danger_stage_a(v, ds, cfg.fuse_f, cfg.blast, cfg.danger_rounds, &max_b, nb_post);
+      danger_stage_a(v, ds, cfg.fuse_f, cfg.blast, cfg.danger_rounds, &max_b, nb_post,
+                     OBS ? ft.weight : nullptr);
       const float standing = danger_at_players(v, ds, flat1, cfg.blast, max_b, P);
       if (p < P)
         reward = __fsub_rn(reward, __fmul_rn(__fmul_rn(cfg.danger_penalty, standing), a0f));
@@ -684,7 +687,9 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
       winner = death_done && alive && n_alive == 1;
       const int loser = death_done && !alive && n_alive == 1;
       const float hpf = (float)hp_new;
-      const float diff = __fsub_rn(hpf, __fdiv_rn(__fsub_rn(tot_hp, hpf), (float)(P - 1)));
+      // (x / 1 is x exactly: no division for two players)
+      const float others = __fsub_rn(tot_hp, hpf);
+      const float diff = __fsub_rn(hpf, P == 2 ? others : __fdiv_rn(others, (float)(P - 1)));
       const float aa = all_alive ? 1.f : 0.f;
       if (!cfg.win_hp_scaled) {
         reward = __fadd_rn(reward, __fmul_rn(cfg.win_bonus,
