@@ -779,6 +779,10 @@ PHASES = {
          "danger paint", "observation: player info", "observation: zero row",
          "observation: channels", "observation: row out", "legal masks", "player stores",
          "barrier + write-back"], True),
+    3: ("astar bot (lane 0 of every warp of every 4th block)",
+        [0, 1, 2, 3, 4],
+        ["tile staging", "field set-up", "relaxation (V_safe, V_opp)", "scoring + bomb rule"],
+        True),
     1: ("MLP policy, epilogue warp 2 (one record per CTA)",
         [0, 1, 7, 8, 9, 10, 11, 12, 13, 14],
         ["set-up (barriers, TMEM)", "layer 1 (wait for its MMAs)", "LN1 + operand",
@@ -825,6 +829,75 @@ def phase_table(rec, kid):
     return out
 
 
+def launch_spans(rec, kid, p_start, p_end, by_warp):
+    """(first start, last start, last end) in ns of every launch of kernel
+    `kid` from phase-stamp records: the k-th record of a block (or warp) at
+    phase p_start / p_end belongs to that block's k-th launch."""
+    import numpy as np
+    w0 = rec[:, 0]
+    t = rec[:, 1].astype(np.int64)
+    k = (w0 >> np.uint64(56)).astype(np.int64)
+    ph = ((w0 >> np.uint64(48)) & np.uint64(0xff)).astype(np.int64)
+    blk = ((w0 >> np.uint64(8)) & np.uint64(0xffffff)).astype(np.int64)
+    key = blk * 64 + (w0 & np.uint64(0xff)).astype(np.int64) if by_warp else blk
+    occ_t = {}
+    for p in (p_start, p_end):
+        m = (k == kid) & (ph == p)
+        kk, tt = key[m], t[m]
+        o = np.lexsort((tt, kk))
+        kk, tt = kk[o], tt[o]
+        start = np.r_[0, np.flatnonzero(kk[1:] != kk[:-1]) + 1]
+        occ = np.arange(len(kk)) - np.repeat(start, np.diff(np.r_[start, len(kk)]))
+        for oc in np.unique(occ):
+            occ_t.setdefault(int(oc), {})[p] = tt[occ == oc]
+    out = [(v[p_start].min(), v[p_start].max(), v[p_end].max())
+           for _, v in sorted(occ_t.items()) if p_start in v and p_end in v]
+    return np.array(out, dtype=np.int64).reshape(-1, 3)
+
+
+def relax_histogram(rec):
+    """The astar relaxation's sweep-phase counts (stamp ids 40 + n)."""
+    import numpy as np
+    w0 = rec[:, 0]
+    k = (w0 >> np.uint64(56)).astype(np.int64)
+    ph = ((w0 >> np.uint64(48)) & np.uint64(0xff)).astype(np.int64)
+    n = ph[(k == 3) & (ph >= 40)] - 40
+    if len(n) == 0:
+        return []
+    vals, cnt = np.unique(n, return_counts=True)
+    top = ", ".join(f"{v}: {c / len(n):.1%}" for v, c in zip(vals, cnt) if c / len(n) >= 0.01)
+    return [f"astar relaxation sweep phases per env: mean {n.mean():.2f} ({top})"]
+
+
+def chain_summary(rec):
+    """How one tick's policy -> step chain lines up, from the launches'
+    first / last block stamps: the gap from a step's end to the next policy
+    start, how early the step's first blocks start before its policy ends
+    (staging under programmatic launch), the step's end after its policy's,
+    and each kernel's span and block start spread."""
+    import numpy as np
+    S = launch_spans(rec, 2, 0, 17, True)
+    P = launch_spans(rec, 1, 0, 14, False)
+    if len(S) == 0 or len(P) == 0:
+        return ["chain: no step / policy launches recorded"]
+    se = np.sort(S[:, 2])
+    gap_sp = [p[0] - se[se <= p[0]][-1] for p in P if (se <= p[0]).any()]
+    # a step's policy: the latest policy that ended after the step started
+    early, after = [], []
+    for s in S:
+        cand = P[(P[:, 2] >= s[0]) & (P[:, 0] <= s[0])]
+        if len(cand):
+            pe = cand[:, 2].max()
+            early.append(pe - s[0])
+            after.append(s[2] - pe)
+    f = lambda v: f"{np.mean(v) / 1e3:.2f}" if len(v) else "-"
+    return [
+        f"chain: step end -> next policy start {f(gap_sp)} us; step's first block starts "
+        f"{f(early)} us before its policy ends; step ends {f(after)} us after it",
+        f"  step launch span {f(S[:, 2] - S[:, 0])} us (block start spread {f(S[:, 1] - S[:, 0])}); "
+        f"policy span {f(P[:, 2] - P[:, 0])} us (CTA start spread {f(P[:, 1] - P[:, 0])})"]
+
+
 def phase_stamps_leg(args):
     """Per-phase durations of the step and policy kernels, from the
     phase-stamp build of the library (build.py --phase-stamps): one captured
@@ -864,8 +937,10 @@ def phase_stamps_leg(args):
     rec = read()
     lines = [f"phase stamps, {args.config}: {N_ENVS} envs per GPU in {len(grp.ros)} group(s), "
              f"one {TICKS}-tick rollout replay ({len(rec)} records)"]
-    for kid in (2, 1):
+    for kid in (2, 3, 1):
         lines += phase_table(rec, kid)
+    lines += relax_histogram(rec)
+    lines += chain_summary(rec)
     ro = grp.ros[0]
     b = 5 % ro.slots
     obs, mm, bm, acts = ro.buf.obs(b), ro.buf.mm[b], ro.buf.bm[b], ro.buf.act[b]

@@ -405,7 +405,8 @@ __device__ inline bool relax_two(volatile float* d0, volatile float* d1, const f
 // against all four neighbours, so a phase that changes nothing is the
 // fixed point; the loop stops there.  Returns false if max_phases ran out.
 template <int H, int W>
-__device__ bool relax_two_reg(float* d0, float* d1, const float* cost, int max_phases) {
+__device__ bool relax_two_reg(float* d0, float* d1, const float* cost, int max_phases,
+                              int* phases_out = nullptr) {
   static_assert(H <= 16 && W <= 16, "one row or column per lane of a 16-lane half");
   const int lane = lane_id(), f = lane >> 4, i = lane & 15;
   const float INF = __int_as_float(0x7f800000);
@@ -419,8 +420,10 @@ __device__ bool relax_two_reg(float* d0, float* d1, const float* cost, int max_p
     cr[c] = row_lane ? cost[i * W + c] : INF;
   }
   bool rows = true, done = false;
+  int ph_used = 0;
   for (int ph = 0; ph < max_phases; ++ph) {
     bool ch = false;
+    ph_used = ph + 1;
     if (rows) {
       float up[W], dn[W];
 #pragma unroll
@@ -498,6 +501,7 @@ __device__ bool relax_two_reg(float* d0, float* d1, const float* cost, int max_p
     }
     __syncwarp();
   }
+  if (phases_out) *phases_out = ph_used;
   return done;
 }
 
@@ -567,9 +571,12 @@ k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const fl
       else if (EAT && l == AP_SPD) pre_v = __float_as_uint(st.spd_g[(size_t)pid * N + e]);
     }
   }
+  QQT_PH_START(ph_t0);
   Tile tile = carve_tile(smem, C);
   load_tile(tile, st, N, e0, PL_WALL | PL_BRICK | PL_OWNER | PL_FUSE | (EAT ? PL_CRATE : 0u));
   __syncthreads();
+  QQT_PH_AT(3, 0, ph_t0, (blockIdx.x & 3) == 0 && lane_id() == 0);
+  QQT_PH(3, 1, (blockIdx.x & 3) == 0 && lane_id() == 0);
   uint8_t* wb = smem + tile_bytes(C) + (size_t)warp_id() * astar_warp_bytes(C);
   uint64_t* pre = (uint64_t*)(wb + astar_pre_off(C));
   pre[lane_id()] = pre_v;
@@ -580,6 +587,10 @@ k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const fl
   float* vo = vs + C;
   uint16_t* own = (uint16_t*)(vo + C);
   const int lane = lane_id();
+  // k_astar is launched as k_cap_max's programmatic dependent: everything
+  // above reads the step's outputs, complete before k_cap_max started;
+  // only the chain-scan length comes from k_cap_max itself
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int cap_max = *cap_max_ptr;
   const int G = cfg.growth_blast_max;
 
@@ -612,8 +623,14 @@ k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const fl
       }
     }
     __syncwarp();
-    const bool conv = (h == 13 && w == 13) ? relax_two_reg<13, 13>(vs, vo, cost, 2 * (C + 1))
-                                           : relax_two(vs, vo, cost, h, w, C + 1);
+    QQT_PH(3, 2, (blockIdx.x & 3) == 0 && lane_id() == 0);
+    int relax_phases = 0;
+    const bool conv = (h == 13 && w == 13)
+                          ? relax_two_reg<13, 13>(vs, vo, cost, 2 * (C + 1), &relax_phases)
+                          : relax_two(vs, vo, cost, h, w, C + 1);
+    QQT_PH(3, 3, (blockIdx.x & 3) == 0 && lane_id() == 0);
+    // the phase count of the two-field relaxation, as a stamp id 40 + n
+    QQT_PH(3, 40 + min(relax_phases, 200), (blockIdx.x & 3) == 0 && lane_id() == 0);
     if (!conv && lane == 0) flag_error(QQT_DEV_NOT_CONVERGED);
     if (vsafe_out)
       for (int c = lane; c < C; c += 32) vsafe_out[(size_t)e * C + c] = vs[c];
@@ -788,6 +805,7 @@ k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const fl
       io.act[(size_t)e * io.act_stride + 1] = alive ? (place ? 1 : 0) : 0;
     }
     __syncwarp();
+    QQT_PH(3, 4, (blockIdx.x & 3) == 0 && lane_id() == 0);
   }
 }
 
@@ -795,6 +813,9 @@ k_astar(QqtCfg cfg, QqtState st, const __half* obs, SeatIO io, int pid, const fl
 // written once, so no memset precedes it and the bot's first node in a
 // captured tick is a kernel.
 __global__ void __launch_bounds__(1024) k_cap_max(const int64_t* blast_cap, int n, int* out) {
+  // the bot kernel after it may start staging now (it waits for this
+  // kernel's result before reading it)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __shared__ int wmax[32];
   int m = 0;
   for (int i = threadIdx.x; i < n; i += blockDim.x) m = max(m, (int)blast_cap[i]);
@@ -1106,9 +1127,20 @@ static int launch_astar(const QqtCfg* cfg, const QqtState* st, const void* obs,
   const bool two = cfg->n_players == 2, g13 = cfg->height == 13 && cfg->width == 13;
   auto kern = two ? (g13 ? k_astar<EAT, 2, 13> : k_astar<EAT, 2>) : k_astar<EAT>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-  kern<<<(N + QQT_TILE_E - 1) / QQT_TILE_E, QQT_NWARP * 32, sm, s>>>(
-      *cfg, *st, (const __half*)obs, io, pid, noise, mode, timer, tick16, new_mode, new_timer,
-      vsafe, vopp, vcrate, capmax);
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3((unsigned)((N + QQT_TILE_E - 1) / QQT_TILE_E), 1, 1);
+  lc.blockDim = dim3(QQT_NWARP * 32, 1, 1);
+  lc.dynamicSmemBytes = sm;
+  lc.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = at;
+  lc.numAttrs = 1;
+  if (cudaLaunchKernelEx(&lc, kern, *cfg, *st, (const __half*)obs, io, pid, noise, mode, timer,
+                         tick16, new_mode, new_timer, vsafe, vopp, vcrate,
+                         (const int*)capmax) != cudaSuccess)
+    return QQT_E_LAUNCH;
   return launch_status();
 }
 
