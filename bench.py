@@ -788,6 +788,11 @@ PHASES = {
         ["set-up (barriers, TMEM)", "layer 1 (wait for its MMAs)", "LN1 + operand",
          "layer-2 MMAs", "LN2 + operand", "head MMAs", "output layers",
          "logit reduce + sampling", "exit"], False),
+    # the same kernel's producer (thread 0) and MMA-issuer stamps
+    11: ("MLP policy, layer-1 producer / MMA issuer (one record per CTA)",
+         [0, 1, 2, 3, 4, 5],
+         ["set-up (barriers, TMEM, K-tile flags)", "first TMA issued", "rest of the TMAs issued",
+          "last MMAs issued", "last MMAs complete"], False, 1),
 }
 
 
@@ -795,7 +800,8 @@ def phase_table(rec, kid):
     """Per-phase durations (us) of kernel `kid` from phase-stamp records:
     the k-th record of a (block[, warp], phase) is that block's k-th launch."""
     import numpy as np
-    title, order, names, by_warp = PHASES[kid]
+    title, order, names, by_warp = PHASES[kid][:4]
+    kid = PHASES[kid][4] if len(PHASES[kid]) > 4 else kid
     w0 = rec[:, 0]
     t = rec[:, 1].astype(np.int64)
     k = (w0 >> np.uint64(56)).astype(np.int64)
@@ -937,7 +943,7 @@ def phase_stamps_leg(args):
     rec = read()
     lines = [f"phase stamps, {args.config}: {N_ENVS} envs per GPU in {len(grp.ros)} group(s), "
              f"one {TICKS}-tick rollout replay ({len(rec)} records)"]
-    for kid in (2, 3, 1):
+    for kid in (2, 3, 1, 11):
         lines += phase_table(rec, kid)
     lines += relax_histogram(rec)
     lines += chain_summary(rec)
@@ -945,18 +951,23 @@ def phase_stamps_leg(args):
     b = 5 % ro.slots
     obs, mm, bm, acts = ro.buf.obs(b), ro.buf.mm[b], ro.buf.bm[b], ro.buf.act[b]
     seats = list(ro.seats)
-    pol = lambda: ro.learner.act_seats(obs, [mm[:, s] for s in seats], [bm[:, s] for s in seats],
-                                       ro.draws.u_net[b], [acts[:, s] for s in seats],
-                                       ro.buf.logp[b], ro.buf.val[b])
-    for _ in range(5):
-        pol()
-    torch.cuda.synchronize()
-    _capi.check(L.qqt_phase_reset(), "qqt_phase_reset")
-    for _ in range(20):
-        pol()
+    for tiles in (ro.buf.tiles[b], None):
+        pol = lambda: ro.learner.act_seats(obs, [mm[:, s] for s in seats],
+                                           [bm[:, s] for s in seats], ro.draws.u_net[b],
+                                           [acts[:, s] for s in seats], ro.buf.logp[b],
+                                           ro.buf.val[b], obs_tiles=tiles)
+        for _ in range(5):
+            pol()
         torch.cuda.synchronize()
-    lines.append(f"policy alone: 20 launches over one group's {ro.sim.num_envs} envs")
-    lines += phase_table(read(), 1)
+        _capi.check(L.qqt_phase_reset(), "qqt_phase_reset")
+        for _ in range(20):
+            pol()
+            torch.cuda.synchronize()
+        lines.append(f"policy alone: 20 launches over one group's {ro.sim.num_envs} envs, "
+                     + ("with" if tiles is not None else "without") + " the rows' K-tile flags")
+        rec = read()
+        lines += phase_table(rec, 1)
+        lines += phase_table(rec, 11)
     print("\n".join(lines), file=sys.stderr)
 
 

@@ -211,11 +211,15 @@ uint64_t qqt_step_scratch_bytes(const QqtCfg *cfg);
  * legal_mask() in SelfPlayRunner.collect (train/ppo.py:215-249).
  *   obs  [N][obs_stride] fp16 rows (cfg->obs_fp32 must be 0), 16-byte
  *        aligned, obs_stride % 8 == 0;  mm [N][P][5], bm [N][P][2] uint8.
+ *   obs_tiles  NULL, or [N][4] uint32 (16-byte aligned): row e's K-tile
+ *        flags for qqt_mlp_act -- K tile t (row entries [64 t, 64 t + 64))
+ *        holds a nonzero only if bit min(t >> 2, 31) of word t & 3 is set.
  * Other arguments as qqt_step. */
 int qqt_step_observe(const QqtCfg *cfg, const QqtState *st, const int64_t *actions,
                      const float *rb_hit, const float *rb_grow, int32_t *tiers,
                      int32_t first_step, const QqtStepOut *out, const QqtTemplate *tmpl,
-                     void *scratch, void *obs, uint8_t *mm, uint8_t *bm, qqt_stream_t stream);
+                     void *scratch, void *obs, uint8_t *mm, uint8_t *bm, uint32_t *obs_tiles,
+                     qqt_stream_t stream);
 
 /* qqt_step for callers that cannot allocate device memory (for example code
  * running inside another runtime's stream capture, or an embedding that only
@@ -245,11 +249,13 @@ int qqt_step_noalloc(const QqtCfg *cfg, const QqtState *st, const int64_t *actio
  * episode) rather than the host generator.  Envs with done[e] = 0 are not
  * touched.  With obs (fp16 rows [N][obs_stride]), mm and bm non-NULL, the
  * reset envs' observation rows and legal masks are rewritten for the new
- * episode (after a qqt_step_observe, the rows of the envs that ended).
+ * episode (after a qqt_step_observe, the rows of the envs that ended);
+ * obs_tiles (may be NULL, layout of qqt_step_observe) then flags every K
+ * tile of those rows.
  * The per-env counter mg->episode advances for every reset env. */
 int qqt_map_reset(const QqtCfg *cfg, const QqtState *st, const QqtMapGen *mg,
                   const uint8_t *done, void *obs, uint8_t *mm, uint8_t *bm,
-                  qqt_stream_t stream);
+                  uint32_t *obs_tiles, qqt_stream_t stream);
 
 /* Crate recycling on the device: for every player with pending lost
  * attribute layers, drop min(lost, free cells) crates on distinct free cells
@@ -341,6 +347,11 @@ int qqt_greedy_act(const QqtCfg *cfg, const QqtState *st, const void *obs,
  *   pack    weights packed by qqt_mlp_pack (256-byte aligned)
  *   obs     [N][obs_stride] fp16, obs_stride % 8 == 0, 16-byte aligned; the
  *           first k_in = C*H*W entries of each row are the observation
+ *   obs_tiles  NULL (every K tile runs), or [N][4] uint32, 16-byte aligned:
+ *           the rows' nonzero-K-tile flags as qqt_step_observe writes them.
+ *           A K tile (64 entries) flagged in none of a 128-row tile's rows
+ *           is skipped for those rows (it adds exactly zero); flags may
+ *           over-report but must not miss a nonzero entry
  *   n_seats 1 or 2, the seats the pack was built for, in its order
  *   mm, bm  host arrays of n_seats device pointers: seat s's move-mask row e
  *           is at mm[s] + e*mm_stride (5 entries), bomb-mask row at
@@ -351,7 +362,8 @@ int qqt_greedy_act(const QqtCfg *cfg, const QqtState *st, const void *obs,
  *   logp, value [n_seats][N] (may be NULL); logits [n_seats][N][8]
  *           (5 move, 2 bomb, value) or NULL
  *   work    reserved (may be NULL); qqt_mlp_work_bytes gives its size */
-int qqt_mlp_act(const void *pack, const void *obs, int32_t n_envs, int32_t obs_stride,
+int qqt_mlp_act(const void *pack, const void *obs, const uint32_t *obs_tiles,
+                int32_t n_envs, int32_t obs_stride,
                 int32_t k_in, int32_t n_seats, const uint8_t *const *mm, int32_t mm_stride,
                 const uint8_t *const *bm, int32_t bm_stride, const float *u,
                 int64_t *const *act, int32_t act_stride, float *logp, float *value,

@@ -9,7 +9,10 @@
 //            the seat-permuted fp32 weights) [NT x 64]; warp 1 lane 0 issues
 //            tcgen05.mma kind::f16 M=128 N=NT, two per K=16 step (A*Bhi +
 //            A*Blo) into an fp32 TMEM accumulator; obs values are exact in
-//            fp16 and the hi/lo split keeps W0's float32 precision.  Ranks
+//            fp16 and the hi/lo split keeps W0's float32 precision.  Given
+//            the rows' nonzero-tile flags, a K tile that is zero in all
+//            128 rows is neither loaded nor multiplied (it adds exactly
+//            zero).  Ranks
 //            1..ks-1 copy their partial sums into their own shared memory
 //            and arrive on an mbarrier of rank 0, whose epilogue adds them
 //            in rank order (distributed shared memory reads).  The per-SM
@@ -514,6 +517,13 @@ struct FusedCfg {
 static_assert(FusedCfg<128>::kSmem <= 232448 && FusedCfg<256>::kSmem <= 232448 &&
                   FusedCfg<128, true>::kSmem <= 232448,
               "fused MLP shared memory over the per-CTA limit");
+// barriers (full, empty: kStages each; accb, wbar, abar, dbar, pready), TMEM
+// slot and abort flag below byte 192 of the barrier block, the K-tile flags
+// in [192, 256), the gathered row ids after it
+static_assert((2 * FusedCfg<128>::kStages + 5) * 8 + 8 <= 192 &&
+                  (2 * FusedCfg<256>::kStages + 5) * 8 + 8 <= 192 &&
+                  (2 * FusedCfg<128, true>::kStages + 5) * 8 + 8 <= 192,
+              "fused barrier block");
 static_assert(FusedCfg<256>::kColScr + 48 <= FusedCfg<256>::kTmemCols &&
                   FusedCfg<128>::kColScr + 48 <= FusedCfg<128>::kTmemCols,
               "TMEM columns");
@@ -843,6 +853,89 @@ __device__ __forceinline__ void umma_split_k128(uint32_t d_tmem, const uint8_t* 
   }
 }
 
+// ---- layer-1 K tiles that hold a nonzero observation entry
+//
+// The caller may pass, per observation row, four 32-bit words that flag the
+// row's K tiles (64 fp16 entries each) holding a nonzero: tile t is flagged
+// by bit min(t >> 2, 31) of word t & 3 (bit 31 also stands for every tile
+// past 127).  A tile that is zero in every row of a CTA's row tile adds
+// exactly zero to each layer-1 accumulator, so the CTA neither loads it nor
+// issues its MMAs; the tiles that do run keep their order, so the sums are
+// the ones the full pass produces.  The flags may over-report (a flagged
+// zero tile costs time only); they must never miss a nonzero.  Without
+// flags every tile runs.
+// Bring a TMA descriptor (a __grid_constant__ kernel parameter) into the
+// descriptor cache ahead of the first copy that uses it.
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
+}
+
+__device__ __forceinline__ bool ktile_on(const uint4& m, int t) {
+  const int q = t & 3;
+  const uint32_t w = q == 0 ? m.x : (q == 1 ? m.y : (q == 2 ? m.z : m.w));
+  return (w >> min(t >> 2, 31)) & 1u;
+}
+
+// Warps 2..5: warp 2 + q ORs the flags of rows r0 + q*32 + lane (+128, ...)
+// below min(r1, n_rows) into part[q]; no flags: every bit set.
+__device__ __forceinline__ void ktile_flags_part(const uint4* __restrict__ tiles, int r0, int r1,
+                                                 int n_rows, uint4* part) {
+  const int q = warp_id() - 2;
+  uint4 m = make_uint4(~0u, ~0u, ~0u, ~0u);
+  if (tiles) {
+    m = make_uint4(0, 0, 0, 0);
+    const int lim = min(r1, n_rows);
+    for (int r = r0 + q * 32 + lane_id(); r < lim; r += 128) {
+      const uint4 v = tiles[r];
+      m.x |= v.x;
+      m.y |= v.y;
+      m.z |= v.z;
+      m.w |= v.w;
+    }
+    m.x = __reduce_or_sync(QQT_FULL, m.x);
+    m.y = __reduce_or_sync(QQT_FULL, m.y);
+    m.z = __reduce_or_sync(QQT_FULL, m.z);
+    m.w = __reduce_or_sync(QQT_FULL, m.w);
+  }
+  if (lane_id() == 0) part[q] = m;
+}
+
+__device__ __forceinline__ uint4 ktile_flags(const uint4* part) {
+  uint4 m = part[0];
+#pragma unroll
+  for (int q = 1; q < 4; ++q) {
+    m.x |= part[q].x;
+    m.y |= part[q].y;
+    m.z |= part[q].z;
+    m.w |= part[q].w;
+  }
+  return m;
+}
+
+// The flags as a 64-bit mask over the first 64 K tiles, for every lane of
+// the calling warp (two ballots); rows of more than 64 tiles run them all.
+__device__ __forceinline__ uint64_t ktile_mask(const uint4* part, int k_tiles) {
+  const uint4 m = ktile_flags(part);
+  const int l = lane_id();
+  const uint32_t lo = __ballot_sync(QQT_FULL, l < k_tiles && ktile_on(m, l));
+  const uint32_t hi = __ballot_sync(QQT_FULL, l + 32 < k_tiles && ktile_on(m, l + 32));
+  return k_tiles > 64 ? ~0ull : (((uint64_t)hi << 32) | lo);
+}
+
+__device__ __forceinline__ bool ktile_in(uint64_t mask, int t) {
+  return t >= 64 || ((mask >> t) & 1ull);
+}
+
+// Tiles a CTA runs out of [kt0, kt1), visited from tile `first`: that one
+// always (so the accumulators are written even if every flag is clear),
+// then the flagged ones.
+__device__ __forceinline__ int ktile_count(uint64_t mask, int kt0, int kt1, int first) {
+  if (kt1 > 64 || mask == ~0ull) return kt1 - kt0;
+  const int n = kt1 - kt0;
+  const uint64_t range = (n >= 64 ? ~0ull : ((1ull << n) - 1)) << kt0;
+  return __popcll(mask & range) + (ktile_in(mask, first) ? 0 : 1);
+}
+
 // One cluster of ks CTAs (launched with cluster dimension ks, 1 <= ks <= 8)
 // serves 128 env rows.  Layer 1 is split along K: CTA rank c accumulates K
 // tiles [c*kt/ks, (c+1)*kt/ks) into its own TMEM; the other ranks copy their
@@ -856,7 +949,8 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
             const float* __restrict__ f, const uint8_t* __restrict__ img, SeatOut io, int seat0,
             int mm_stride, int bm_stride, const float* __restrict__ u, int act_stride,
             float* __restrict__ logp_out, float* __restrict__ value_out,
-            float* __restrict__ logits_out, TrainOut tr, uint32_t test_wait) {
+            float* __restrict__ logits_out, TrainOut tr, uint32_t test_wait,
+            const uint4* __restrict__ tiles) {
   static_assert(!TRAIN || (NT == 128 && !SPLIT_A), "training forward: one seat, fp16 rows");
   using G = FusedCfg<NT, SPLIT_A>;
   constexpr int S = NT / 128;
@@ -871,6 +965,7 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
   uint64_t* pready = dbar + 1;            // split-K partials of the other ranks written
   uint32_t* tmem_slot = (uint32_t*)(pready + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  uint4* kpart = (uint4*)(smem + G::kRegion + 192);   // K-tile flags, one word set per warp
   const int warp = warp_id(), lane = lane_id();
   const int ks = (int)cluster_size();
   const int rank = (int)cluster_rank();
@@ -883,6 +978,9 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
   QQT_PH_START(ph_t0);
 
   if (threadIdx.x == 0) {
+    prefetch_tmap(&tm_a);
+    if (SPLIT_A) prefetch_tmap(&tm_alo);
+    prefetch_tmap(&tm_b);
     for (int s = 0; s < G::kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -901,6 +999,7 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
                  "r"(tmem_cols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
+  if (warp >= 2 && warp < 6) ktile_flags_part(TRAIN ? nullptr : tiles, m0, m0 + kBM, n_rows, kpart);
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;");
@@ -924,6 +1023,7 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
   }
 
   if (warp == 0) {
+    const uint64_t kmask = ktile_mask(kpart, k_tiles);
     // training forward over minibatch rows of a larger buffer: the tile's
     // 128 row ids (rows past the end and invalid ids read row 0; invalid ids
     // raise QQT_DEV_BAD_INDEX), fetched by TMA tile::gather4, four rows each
@@ -947,7 +1047,9 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
       // clusters start at different K tiles so that at any time they read
       // different lines of the shared weight stream from L2
       const int k0 = (int)(((unsigned)tile * 7u) % (unsigned)n_kt);
-      for (int kt = 0; kt < n_kt; ++kt) {
+      int kt_src = kt0 + k0;
+      for (int j = 0, kt = 0; j < n_kt; ++j, kt_src = kt_src + 1 == kt1 ? kt0 : kt_src + 1) {
+        if (j > 0 && !ktile_in(kmask, kt_src)) continue;   // zero in every row of the tile
         const int s = kt % G::kStages;
         if (kt >= G::kStages) {
           if (!mbar_wait(&empty[s], ((kt / G::kStages) - 1) & 1)) {
@@ -957,7 +1059,7 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         }
         if (*abort_flag) break;
         uint8_t* st = smem + s * G::kStageBytes;
-        const int kx = (kt0 + (kt + k0) % n_kt) * kBK;
+        const int kx = kt_src * kBK;
         mbar_expect_tx(&full[s], G::kStageBytes);
         if (gather) {
 #pragma unroll 4
@@ -970,8 +1072,8 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         if (SPLIT_A) tma_load_2d(&tm_alo, &full[s], st + G::kABytes, kx, m0);
         tma_load_2d(&tm_b, &full[s], st + G::kAAll, kx, 0);
         tma_load_2d(&tm_b, &full[s], st + G::kAAll + G::kBBytes, kx, NT);
-        issued_until = kt + 1;
-        QQT_PH(1, 2, kt == 0);
+        issued_until = ++kt;
+        QQT_PH(1, 2, kt == 1);
       }
       QQT_PH(1, 3, true);
       // drain: every issued stage must land before the CTA may exit
@@ -979,12 +1081,16 @@ k_mlp_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         mbar_wait(&full[kt % G::kStages], (kt / G::kStages) & 1);
     }
   } else if (warp == 1) {
+    const uint64_t kmask = ktile_mask(kpart, k_tiles);
     if (lane == 0) {
       // ---------------- MMA issuer
       const uint32_t idesc = idesc_f16(kBM, NT);
       const uint32_t idesc_st = idesc_f16(kBM, 256);   // one seat: hi and lo rows stacked
+      // the producer's tile sequence: its length is all this loop needs
+      const int n_run =
+          ktile_count(kmask, kt0, kt1, kt0 + (int)(((unsigned)tile * 7u) % (unsigned)n_kt));
       bool ok = true;
-      for (int kt = 0; kt < n_kt && ok; ++kt) {
+      for (int kt = 0; kt < n_run && ok; ++kt) {
         const int s = kt % G::kStages;
         // an abort stops the MMAs before the next stage (the producer
         // drains every stage it issued before the CTA exits)
@@ -1234,7 +1340,8 @@ static int launch_mlp_fused(const CUtensorMap& ma, const CUtensorMap& malo, cons
                             int n_rows, int k_tiles, const float* f, const uint8_t* img,
                             const SeatOut& io, int seat0, int mm_stride, int bm_stride,
                             const float* u, int act_stride, float* logp, float* value,
-                            float* logits, cudaStream_t st, TrainOut tr = TrainOut{}) {
+                            float* logits, cudaStream_t st, TrainOut tr = TrainOut{},
+                            const uint4* tiles = nullptr) {
   using G = FusedCfg<NT, SPLIT_A>;
   auto kern = k_mlp_fused<NT, SPLIT_A, TRAIN>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
@@ -1255,7 +1362,7 @@ static int launch_mlp_fused(const CUtensorMap& ma, const CUtensorMap& malo, cons
   const uint32_t test_wait = g_test_wait_polls.load(std::memory_order_relaxed);
   if (cudaLaunchKernelEx(&cfg, kern, ma, malo, mb, n_rows, k_tiles, f, img, io, seat0, mm_stride,
                          bm_stride, u, act_stride, logp, value, logits, tr,
-                         test_wait) != cudaSuccess)
+                         test_wait, tiles) != cudaSuccess)
     return QQT_E_LAUNCH;
   return launch_status();
 }
@@ -1379,7 +1486,8 @@ extern "C" uint64_t qqt_mlp_work_bytes(int32_t n_envs, int32_t n_seats) {
   return 256;
 }
 
-extern "C" int qqt_mlp_act(const void* pack, const void* obs, int32_t n_envs, int32_t obs_stride,
+extern "C" int qqt_mlp_act(const void* pack, const void* obs, const uint32_t* obs_tiles,
+                           int32_t n_envs, int32_t obs_stride,
                            int32_t k_in, int32_t n_seats, const uint8_t* const* mm,
                            int32_t mm_stride, const uint8_t* const* bm, int32_t bm_stride,
                            const float* u, int64_t* const* act, int32_t act_stride, float* logp,
@@ -1391,8 +1499,10 @@ extern "C" int qqt_mlp_act(const void* pack, const void* obs, int32_t n_envs, in
     return QQT_E_ARG;
   for (int s = 0; s < n_seats; ++s)
     if (!mm[s] || !bm[s] || !act[s]) return QQT_E_ARG;
-  if (obs_stride % 8 || obs_stride < k_in || ((uintptr_t)obs & 15) || ((uintptr_t)pack & 255))
+  if (obs_stride % 8 || obs_stride < k_in || ((uintptr_t)obs & 15) || ((uintptr_t)pack & 255) ||
+      ((uintptr_t)obs_tiles & 15))
     return QQT_E_ALIGN;
+  const uint4* tiles = reinterpret_cast<const uint4*>(obs_tiles);
   const MlpPack L = mlp_pack_layout(k_in, n_seats);
   const uint8_t* pk = (const uint8_t*)pack;
   CUtensorMap ma, mb;
@@ -1418,14 +1528,15 @@ extern "C" int qqt_mlp_act(const void* pack, const void* obs, int32_t n_envs, in
                   (uint32_t)(L.nt / 2)))
       return QQT_E_ARG;
     return launch_mlp_pair<256>(ma, mbh, n_envs, k_tiles, fpar, pk + L.pair_off, io, mm_stride,
-                                bm_stride, u, act_stride, logp, value, logits, st);
+                                bm_stride, u, act_stride, logp, value, logits, st, tiles);
   }
   if (L.nt == 128)
     return launch_mlp_fused<128, false>(ma, ma, mb, n_envs, k_tiles, fpar, pk + L.img_off, io, 0,
                                         mm_stride, bm_stride, u, act_stride, logp, value, logits,
-                                        st);
+                                        st, TrainOut{}, tiles);
   return launch_mlp_fused<256, false>(ma, ma, mb, n_envs, k_tiles, fpar, pk + L.img_off, io, 0,
-                                      mm_stride, bm_stride, u, act_stride, logp, value, logits, st);
+                                      mm_stride, bm_stride, u, act_stride, logp, value, logits, st,
+                                      TrainOut{}, tiles);
 }
 
 extern "C" int qqt_test_set_wait_polls(uint32_t polls) {

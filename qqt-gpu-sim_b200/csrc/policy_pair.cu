@@ -53,6 +53,11 @@ struct PairCfg {
 };
 static_assert(PairCfg<128>::kSmem <= 232448 && PairCfg<256>::kSmem <= 232448,
               "pair MLP shared memory over the per-CTA limit");
+// barriers (full, empty: kStages each; accb, wbar, abar, dbar), TMEM slot and
+// abort flag below byte 192 of the barrier block, the K-tile flags above it
+static_assert((2 * PairCfg<128>::kStages + 4) * 8 + 8 <= 192 &&
+                  (2 * PairCfg<256>::kStages + 4) * 8 + 8 <= 192,
+              "pair barrier block");
 static_assert(2 * PairCfg<128>::kImgHalf == (int)kImgBytes, "two halves = the tail images");
 static_assert(PairCfg<256>::kColScr + 48 <= PairCfg<256>::kTmemCols, "TMEM columns");
 
@@ -142,7 +147,7 @@ k_mlp_pair(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
            int n_rows, int k_tiles, const float* __restrict__ f, const uint8_t* __restrict__ img,
            SeatOut io, int mm_stride, int bm_stride, const float* __restrict__ u, int act_stride,
            float* __restrict__ logp_out, float* __restrict__ value_out,
-           float* __restrict__ logits_out, uint32_t test_wait) {
+           float* __restrict__ logits_out, uint32_t test_wait, const uint4* __restrict__ tiles) {
   using G = PairCfg<NT>;
   constexpr int S = NT / 128;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -155,6 +160,7 @@ k_mlp_pair(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
   uint64_t* dbar = abar + 1;             // tail MMA group complete (commit, both CTAs)
   uint32_t* tmem_slot = (uint32_t*)(dbar + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  uint4* kpart = (uint4*)(smem + G::kBars + 192);   // K-tile flags, one word set per warp
   const int warp = warp_id(), lane = lane_id();
   const int rank = (int)cluster_rank();
   const bool leader = rank == 0;
@@ -165,6 +171,8 @@ k_mlp_pair(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
   const int m_load = min(m0, (n_rows - 1) / kBM * kBM);
 
   if (threadIdx.x == 0) {
+    prefetch_tmap(&tm_a);
+    prefetch_tmap(&tm_b);
     for (int s = 0; s < G::kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -183,6 +191,9 @@ k_mlp_pair(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
                  "r"(G::kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
   }
+  // both CTAs OR the flags of the pair's 256 rows, so both run the same tiles
+  if (warp >= 2 && warp < 6) ktile_flags_part(tiles, 2 * pair * kBM, 2 * pair * kBM + 2 * kBM,
+                                              n_rows, kpart);
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;");
@@ -200,6 +211,7 @@ k_mlp_pair(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
   }
 
   if (warp == 0) {
+    const uint64_t kmask = ktile_mask(kpart, k_tiles);
     if (lane == 0) {
       // ---------------- producer (both CTAs)
       int issued = 0;
@@ -207,7 +219,11 @@ k_mlp_pair(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
       // pairs start at different K tiles so that at any time they read
       // different lines of the shared weight stream from L2
       const int k0 = (int)(((unsigned)pair * 7u) % (unsigned)k_tiles);
-      for (int kt = 0; kt < k_tiles && !*abort_flag; ++kt) {
+      const int n_run = ktile_count(kmask, 0, k_tiles, k0);
+      int kt_src = k0;
+      for (int j = 0, kt = 0; j < k_tiles && !*abort_flag;
+           ++j, kt_src = kt_src + 1 == k_tiles ? 0 : kt_src + 1) {
+        if (j > 0 && !ktile_in(kmask, kt_src)) continue;   // zero in every row of the pair
         const int s = kt % G::kStages;
         if (kt >= G::kStages && !mbar_wait(&empty[s], ((kt / G::kStages) - 1) & 1)) {
           *abort_flag = 1;
@@ -215,19 +231,19 @@ k_mlp_pair(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
         }
         uint8_t* st = smem + s * G::kStageBytes;
         const uint32_t fb = dsmem_addr(&full[s], 0);
-        const int kx = ((kt + k0) % k_tiles) * kBK;
+        const int kx = kt_src * kBK;
         // the leader's stage barrier counts both CTAs' bytes
         if (leader) mbar_expect_tx(&full[s], 2 * G::kStageBytes);
         tma_load_2d_pair(&tm_a, fb, st, kx, m_load);
         tma_load_2d_pair(&tm_b, fb, st + G::kABytes, kx, rank * (NT / 2));
         tma_load_2d_pair(&tm_b, fb, st + G::kABytes + G::kBHalf, kx, NT + rank * (NT / 2));
-        issued = kt + 1;
+        issued = ++kt;
       }
       // every stage this CTA issued is consumed before the CTA may exit
       // (the leader commits each stage's empty barrier in both CTAs)
       for (int kt = max(0, issued - G::kStages); kt < issued; ++kt)
         if (!mbar_wait(&empty[kt % G::kStages], (kt / G::kStages) & 1)) *abort_flag = 1;
-      if (issued == k_tiles && !*abort_flag) {
+      if (issued == n_run && !*abort_flag) {
         // the stages' last MMAs are done (each commit covers every earlier
         // MMA): the drained region takes the images
         mbar_expect_tx(wbar, G::kImgHalf);
@@ -239,11 +255,14 @@ k_mlp_pair(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
       if (img_issued && !mbar_wait(wbar, 0)) *abort_flag = 1;
     }
   } else if (warp == 1) {
+    const uint64_t kmask = ktile_mask(kpart, k_tiles);
     if (lane == 0 && leader) {
       // ---------------- MMA issuer (the leader, for the pair)
       const uint32_t idesc1 = idesc_f16(2 * kBM, NT);
+      // the producers' tile sequence: its length is all this loop needs
+      const int n_run = ktile_count(kmask, 0, k_tiles, (int)(((unsigned)pair * 7u) % (unsigned)k_tiles));
       bool ok = true;
-      for (int kt = 0; kt < k_tiles; ++kt) {
+      for (int kt = 0; kt < n_run; ++kt) {
         const int s = kt % G::kStages;
         if (*abort_flag || !mbar_wait(&full[s], (kt / G::kStages) & 1)) {
           *abort_flag = 1;
@@ -408,7 +427,8 @@ template <int NT>
 static int launch_mlp_pair(const CUtensorMap& ma, const CUtensorMap& mb, int n_rows, int k_tiles,
                            const float* f, const uint8_t* img, const SeatOut& io, int mm_stride,
                            int bm_stride, const float* u, int act_stride, float* logp,
-                           float* value, float* logits, cudaStream_t st) {
+                           float* value, float* logits, cudaStream_t st,
+                           const uint4* tiles = nullptr) {
   using G = PairCfg<NT>;
   auto kern = k_mlp_pair<NT>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
@@ -428,7 +448,7 @@ static int launch_mlp_pair(const CUtensorMap& ma, const CUtensorMap& mb, int n_r
   cfg.numAttrs = 1;
   const uint32_t test_wait = g_test_wait_polls.load(std::memory_order_relaxed);
   if (cudaLaunchKernelEx(&cfg, kern, ma, mb, n_rows, k_tiles, f, img, io, mm_stride, bm_stride, u,
-                         act_stride, logp, value, logits, test_wait) != cudaSuccess)
+                         act_stride, logp, value, logits, test_wait, tiles) != cudaSuccess)
     return QQT_E_LAUNCH;
   return launch_status();
 }

@@ -73,13 +73,17 @@ struct FuseTables {
 // invulnerability and bomb cap.  Lane l computes cell l, l+32, ... of every
 // channel (consecutive lanes, consecutive elements); the row goes straight to
 // global memory, or, given a 16-byte aligned per-warp `stage` of obs_stride
-// elements, into shared memory first and out as 16-byte stores.
+// elements, into shared memory first and out as 16-byte stores.  Staged
+// fp16 rows may also report which of their 64-entry K tiles hold a nonzero
+// (`tiles`, four words per row: tile t is bit min(t >> 2, 31) of word t & 3,
+// the flags the MLP policy uses to skip zero tiles).
 template <class T, bool STAGED = false, int NP = 0, int G = 0>
 __device__ inline void observe_env(const QqtCfg& cfg, const Env& v, int e, PInfo* pi,
                                    const float* dng, int live_p, float py, float px,
                                    bool alive_p, int64_t inv_p, int64_t bcap_p, int64_t t_e,
                                    const FuseTables& ft, void* obs, float* danger_out,
-                                   uint8_t* mm, uint8_t* bm, T* stage = nullptr) {
+                                   uint8_t* mm, uint8_t* bm, T* stage = nullptr,
+                                   uint32_t* tiles = nullptr) {
   const int h = G > 0 ? G : cfg.height, w = G > 0 ? G : cfg.width, C = h * w;
   const int P = NP > 0 ? NP : cfg.n_players;
   const int lane = lane_id();
@@ -174,8 +178,27 @@ __device__ inline void observe_env(const QqtCfg& cfg, const Env& v, int e, PInfo
     __syncwarp();
     QQT_PH(2, 21, STAGED && (blockIdx.x & 3) == 0 && lane == 0);
     uint4* dst = reinterpret_cast<uint4*>(grow);
+    if (sizeof(T) == 2 && tiles) {
+      // chunk k = lane + 32 i (eight entries) lies in K tile k >> 3 =
+      // 4 i + (lane >> 3): lane group g = lane >> 3 sees only the tiles of
+      // word g, tile 4 i + g at bit i (bit 31 from i = 31 on)
+      uint32_t acc = 0, bit = 1;
 #pragma unroll 4
-    for (int k = lane; k < n16; k += 32) dst[k] = s4[k];
+      for (int k = lane; k < n16; k += 32) {
+        const uint4 x = s4[k];
+        dst[k] = x;
+        if ((x.x | x.y) | (x.z | x.w)) acc |= bit;
+        bit = bit == 0x80000000u ? bit : bit << 1;
+      }
+      acc |= __shfl_xor_sync(QQT_FULL, acc, 1);
+      acc |= __shfl_xor_sync(QQT_FULL, acc, 2);
+      acc |= __shfl_xor_sync(QQT_FULL, acc, 4);
+      if ((lane & 7) == 0) tiles[(size_t)e * 4 + (lane >> 3)] = acc;
+    } else {
+#pragma unroll 4
+      for (int k = lane; k < n16; k += 32) dst[k] = s4[k];
+      if (tiles && lane < 4) tiles[(size_t)e * 4 + lane] = ~0u;
+    }
     QQT_PH(2, 22, STAGED && (blockIdx.x & 3) == 0 && lane == 0);
   } else if (obs || danger_out) {
     T* row = grow;

@@ -60,7 +60,7 @@ __host__ __device__ inline size_t reset_warp_bytes(int cells) {
 template <bool OBS>
 __global__ void __launch_bounds__(QQT_NWARP * 32)
 k_map_reset(QqtCfg cfg, QqtState st, QqtMapGen g, const uint8_t* __restrict__ done,
-            __half* obs, uint8_t* mm, uint8_t* bm) {
+            __half* obs, uint8_t* mm, uint8_t* bm, uint32_t* obs_tiles) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ FuseTables ft;
   const int e = blockIdx.x * QQT_NWARP + warp_id();
@@ -270,6 +270,8 @@ k_map_reset(QqtCfg cfg, QqtState st, QqtMapGen g, const uint8_t* __restrict__ do
     __syncwarp();
     observe_env<__half, false>(cfg, v, e, pinfo, dng, 0, py, px, true, 0, bcap_out, 0, ft, obs,
                                nullptr, mm, bm);
+    // the rewritten row's K-tile flags: every tile (flags may over-report)
+    if (obs_tiles && lane < 4) obs_tiles[(size_t)e * 4 + lane] = ~0u;
   }
 }
 
@@ -279,7 +281,7 @@ using namespace qqt;
 
 extern "C" int qqt_map_reset(const QqtCfg* cfg, const QqtState* st, const QqtMapGen* mg,
                              const uint8_t* done, void* obs, uint8_t* mm, uint8_t* bm,
-                             qqt_stream_t stream) {
+                             uint32_t* obs_tiles, qqt_stream_t stream) {
   int rc = check_cfg(cfg);
   if (rc) return rc;
   if (!st || !mg || !done || !mg->episode) return QQT_E_ARG;
@@ -295,11 +297,11 @@ extern "C" int qqt_map_reset(const QqtCfg* cfg, const QqtState* st, const QqtMap
   if (with_obs) {
     cudaFuncSetAttribute(k_map_reset<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
     k_map_reset<true><<<blocks, QQT_NWARP * 32, sm, s>>>(*cfg, *st, *mg, done, (__half*)obs, mm,
-                                                         bm);
+                                                         bm, obs_tiles);
   } else {
     cudaFuncSetAttribute(k_map_reset<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
     k_map_reset<false><<<blocks, QQT_NWARP * 32, sm, s>>>(*cfg, *st, *mg, done, nullptr, nullptr,
-                                                          nullptr);
+                                                          nullptr, nullptr);
   }
   return launch_status();
 }

@@ -84,6 +84,7 @@ struct StepParams {
   __half* obs;
   uint8_t* mm;
   uint8_t* bm;
+  uint32_t* obs_tiles;   // [N][4] nonzero-K-tile flags of the rows, or null
 };
 
 // Key of hazard draw family j (0: bomb count, 1: cell order, 2: blast) of
@@ -784,7 +785,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
         if (lane == q && !reset) my_live = post_live[q];
       observe_env<__half, true, NP, G>(cfg, v, e, pinfo, dng, my_live, me.y, me.x, alive != 0, me.invuln,
                           me.bombs_cap, t_out, ft, a.obs, nullptr, a.mm, a.bm,
-                          (__half*)(wb + L.row));
+                          (__half*)(wb + L.row), a.obs_tiles);
     }
     QQT_PH(2, 14, (blockIdx.x & 3) == 0 && lane == 0);
     if (p < P) {
@@ -927,7 +928,8 @@ static bool step_pdl_enabled() {
 static int launch_step(const QqtCfg* cfg, const QqtState* st, const int64_t* actions,
                        const float* rb_hit, const float* rb_grow, int32_t* tiers,
                        int32_t first_step, const QqtStepOut* out, const QqtTemplate* tmpl,
-                       void* scratch, void* obs, uint8_t* mm, uint8_t* bm, qqt_stream_t stream) {
+                       void* scratch, void* obs, uint8_t* mm, uint8_t* bm,
+                       uint32_t* obs_tiles, qqt_stream_t stream) {
   int rc = check_cfg(cfg);
   if (rc) return rc;
   if (!st || !actions || !tiers || !scratch) return QQT_E_ARG;
@@ -961,6 +963,7 @@ static int launch_step(const QqtCfg* cfg, const QqtState* st, const int64_t* act
   p.obs = (__half*)obs;
   p.mm = mm;
   p.bm = bm;
+  p.obs_tiles = obs ? obs_tiles : nullptr;
   const int C = cfg->height * cfg->width;
   const size_t sm = tile_bytes(C) + QQT_NWARP * step_warp_bytes(C, step_row_bytes(*cfg, obs != nullptr));
   const int blocks = (cfg->n_envs + QQT_TILE_E - 1) / QQT_TILE_E;
@@ -1018,18 +1021,19 @@ extern "C" int qqt_step(const QqtCfg* cfg, const QqtState* st, const int64_t* ac
                         int32_t first_step, const QqtStepOut* out, const QqtTemplate* tmpl,
                         void* scratch, qqt_stream_t stream) {
   return launch_step(cfg, st, actions, rb_hit, rb_grow, tiers, first_step, out, tmpl, scratch,
-                     nullptr, nullptr, nullptr, stream);
+                     nullptr, nullptr, nullptr, nullptr, stream);
 }
 
 extern "C" int qqt_step_observe(const QqtCfg* cfg, const QqtState* st, const int64_t* actions,
                                 const float* rb_hit, const float* rb_grow, int32_t* tiers,
                                 int32_t first_step, const QqtStepOut* out, const QqtTemplate* tmpl,
                                 void* scratch, void* obs, uint8_t* mm, uint8_t* bm,
-                                qqt_stream_t stream) {
+                                uint32_t* obs_tiles, qqt_stream_t stream) {
   if (!obs || !mm || !bm) return QQT_E_ARG;
-  if (((uintptr_t)obs & 15) || (cfg && (cfg->obs_stride % 8))) return QQT_E_ALIGN;
+  if (((uintptr_t)obs & 15) || ((uintptr_t)obs_tiles & 15) || (cfg && (cfg->obs_stride % 8)))
+    return QQT_E_ALIGN;
   return launch_step(cfg, st, actions, rb_hit, rb_grow, tiers, first_step, out, tmpl, scratch,
-                     obs, mm, bm, stream);
+                     obs, mm, bm, obs_tiles, stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -101,7 +101,8 @@ def lib():
             "qqt_step": (c_i32, [P(QqtCfg), P(QqtState), c_p, c_p, c_p, c_p, c_i32,
                                  P(QqtStepOut), P(QqtTemplate), c_p, c_p]),
             "qqt_step_observe": (c_i32, [P(QqtCfg), P(QqtState), c_p, c_p, c_p, c_p, c_i32,
-                                 P(QqtStepOut), P(QqtTemplate), c_p, c_p, c_p, c_p, c_p]),
+                                 P(QqtStepOut), P(QqtTemplate), c_p, c_p, c_p, c_p, c_p,
+                                 c_p]),
             "qqt_step_scratch_bytes": (c_u64, [P(QqtCfg)]),
             "qqt_step_noalloc": (c_i32, [P(QqtCfg), P(QqtState), c_p, c_p, c_p, c_p, c_i32,
                                          P(QqtStepOut), P(QqtTemplate), c_p]),
@@ -118,7 +119,7 @@ def lib():
                                        c_i32, c_p, c_p, c_i32, c_p]),
             "qqt_flush_recycle": (c_i32, [P(QqtCfg), P(QqtState), c_p, c_u64, c_u64, c_p]),
             "qqt_map_reset": (c_i32, [P(QqtCfg), P(QqtState), P(QqtMapGen), c_p, c_p, c_p, c_p,
-                                      c_p]),
+                                      c_p, c_p]),
             "qqt_gae": (c_i32, [c_p, c_i32, c_p, c_p, c_i32, c_p, c_i32, c_i32, ctypes.c_double,
                                 ctypes.c_double, c_p, c_p, c_p]),
             "qqt_local_view": (c_i32, [P(QqtCfg), P(QqtState), c_p, c_i32, c_i32, c_p, c_p, c_p,
@@ -142,7 +143,7 @@ def lib():
             "qqt_version": (ctypes.c_char_p, []),
         }
         optional = {
-            "qqt_mlp_act": (c_i32, [c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_p, c_i32, c_p,
+            "qqt_mlp_act": (c_i32, [c_p, c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_p, c_i32, c_p,
                                     c_i32, c_p, c_p, c_i32, c_p, c_p, c_p, c_p, c_p]),
             "qqt_mlp_pack": (c_i32, [c_p, c_i32, c_i32, c_i32, c_i32, c_i32, c_p, c_p, c_p]),
             "qqt_mlp_pack_bytes": (c_u64, [c_i32, c_i32]),

@@ -15,6 +15,7 @@ import numpy as np
 import torch
 
 from . import _capi as capi
+from .sim import check_tile_flags
 
 PARAM_NAMES = ("shared.0.weight shared.0.bias shared.1.weight shared.1.bias shared.3.weight "
                "shared.3.bias shared.4.weight shared.4.bias move_head.0.weight "
@@ -115,15 +116,23 @@ class B200Policy:
             return buf, pad
         return obs, stride
 
-    def act_seats(self, obs, mmasks, bmasks, u, acts, logp=None, value=None, logits=None):
+    def act_seats(self, obs, mmasks, bmasks, u, acts, logp=None, value=None, logits=None,
+                  obs_tiles=None):
         """Act for every seat of the pack in one call.
 
         obs (N, C, H, W) fp16; mmasks/bmasks: per seat (N,5)/(N,2) views;
         u (S, N, 2) uniforms; acts: per seat (N, 2) int64 views to fill.
+        obs_tiles: optional (N, 4) int32 nonzero-K-tile flags of the obs rows
+        (as the step's fused observation writes them); the MLP then skips the
+        first-layer K tiles that are zero in all rows of a row tile (exact).
+        The CNN ignores them.
         """
         n = obs.shape[0]
         S = len(self.seats)
+        # (a repacked copy keeps every entry at its index, so the flags hold)
         ob, stride = self._obs_rows(obs)
+        if obs_tiles is not None:
+            check_tile_flags(obs_tiles, n)
         mms = [_rows(m, 5) for m in mmasks]
         bms = [_rows(b, 2) for b in bmasks]
         for a in acts:
@@ -138,7 +147,8 @@ class B200Policy:
         bp = (ctypes.c_void_p * 2)(*([b.data_ptr() for b in bms] + [0] * (2 - S)))
         ap = (ctypes.c_void_p * 2)(*([a.data_ptr() for a in acts] + [0] * (2 - S)))
         if self.arch == "mlp":
-            rc = capi.lib().qqt_mlp_act(self.pack.data_ptr(), ob.data_ptr(), n, stride, self.k_in,
+            rc = capi.lib().qqt_mlp_act(self.pack.data_ptr(), ob.data_ptr(), capi.ptr(obs_tiles),
+                                        n, stride, self.k_in,
                                         S, mp, mms[0].stride(0), bp, bms[0].stride(0),
                                         uu.data_ptr(), ap, acts[0].stride(0), capi.ptr(logp),
                                         capi.ptr(value), capi.ptr(logits),
@@ -167,8 +177,9 @@ class B200Policy:
         self.act_seats(obs, [move_mask], [bomb_mask], u.reshape(1, n, 2), [acts], logp, value)
         return acts, logp[0], value[0]
 
-    def forward_logits(self, obs, move_mask, bomb_mask, u=None):
-        """(logits (S,N,8): 5 move, 2 bomb, value; actions per seat; logp (S,N))."""
+    def forward_logits(self, obs, move_mask, bomb_mask, u=None, obs_tiles=None):
+        """(logits (S,N,8): 5 move, 2 bomb, value; actions per seat; logp (S,N)).
+        obs_tiles: optional K-tile flags of the rows (see act_seats)."""
         n = obs.shape[0]
         S = len(self.seats)
         if u is None:
@@ -178,5 +189,5 @@ class B200Policy:
         acts = [torch.empty((n, 2), dtype=torch.int64, device=self.device) for _ in range(S)]
         mm = [move_mask[:, p] for p in self.seats]
         bm = [bomb_mask[:, p] for p in self.seats]
-        self.act_seats(obs, mm, bm, u, acts, logp, None, logits)
+        self.act_seats(obs, mm, bm, u, acts, logp, None, logits, obs_tiles=obs_tiles)
         return logits, acts, logp

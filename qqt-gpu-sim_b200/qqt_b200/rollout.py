@@ -34,6 +34,9 @@ class DeviceRolloutBuffer:
         self.T, self.n, self.p = T, n, p
         self.obs_shape = obs_shape
         self.obs_rows = torch.zeros((T, n, obs_stride), dtype=torch.float16, device=d)
+        # per row, which 64-entry K tiles hold a nonzero (written by the
+        # step's fused observation; the MLP policy skips all-zero tiles)
+        self.tiles = torch.full((T, n, 4), -1, dtype=torch.int32, device=d)
         self.mm = torch.ones((T, n, p, 5), dtype=torch.bool, device=d)
         self.bm = torch.ones((T, n, p, 2), dtype=torch.bool, device=d)
         self.act = torch.zeros((T, n, p, 2), dtype=torch.int64, device=d)
@@ -129,8 +132,10 @@ class Rollout:
     def tick(self, t: int) -> None:
         sim, buf, dr = self.sim, self.buf, self.draws
         b = t % self.slots
+        tiles = None
         if self._ready == t:
             obs, mm, bm = buf.obs(b), buf.mm[b], buf.bm[b]
+            tiles = buf.tiles[b]
         else:
             obs, mm, bm = self._run("observe", lambda: sim.observe_and_mask(
                 buf.obs_rows[b], buf.mm[b], buf.bm[b], danger=False))
@@ -140,7 +145,8 @@ class Rollout:
         def learner():
             self.learner.act_seats(obs, [mm[:, s] for s in self.seats],
                                    [bm[:, s] for s in self.seats], dr.u_net[t],
-                                   [acts[:, s] for s in self.seats], buf.logp[b], buf.val[b])
+                                   [acts[:, s] for s in self.seats], buf.logp[b], buf.val[b],
+                                   obs_tiles=tiles)
         # the opponent bot runs on the side stream and the learner's policy
         # on the tick's stream right before the step, so the step (launched
         # as the policy's programmatic dependent) can stage its state while
@@ -163,7 +169,7 @@ class Rollout:
             # after a crate recycle only the crate channel of the next rows
             # changes; flush_recycle rewrites it (no stand-alone observe)
             b1 = (t + 1) % self.slots
-            nxt = (buf.obs_rows[b1], buf.mm[b1], buf.bm[b1])
+            nxt = (buf.obs_rows[b1], buf.mm[b1], buf.bm[b1], buf.tiles[b1])
         self._run("step+observe" if nxt is not None else "step", lambda: sim.step(
             acts, auto_reset=True, crate_draws=(dr.crate[t, 0], dr.crate[t, 1]),
             reward_out=buf.rew[b], done_out=buf.done[b], hit_out=buf.dmg[b],
@@ -171,7 +177,8 @@ class Rollout:
         self._ready = t + 1 if nxt is not None else -1
         if flush:
             self._run("flush", lambda: sim.flush_recycle(
-                obs_rows=nxt[0] if nxt is not None else None))
+                obs_rows=nxt[0] if nxt is not None else None,
+                obs_tiles=nxt[3] if nxt is not None else None))
 
     def feed_opponent(self, t: int) -> None:
         """Hand the opponent bot its draws for tick t (noise; the astar mode

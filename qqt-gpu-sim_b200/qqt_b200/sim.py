@@ -46,6 +46,44 @@ _CSTATE = {"wall": "wall", "brick": "brick", "crate": "crate", "recycle": "_recy
            "lo_spd": "_lo_spd", "crate_prob": "crate_prob", "hazard": "_hazard"}
 
 
+def check_tile_flags(tiles: torch.Tensor, n: int) -> None:
+    """K-tile flags of n observation rows: a contiguous (n, 4) int32 tensor
+    whose storage starts on a 16-byte boundary."""
+    if (tiles.dtype != torch.int32 or tuple(tiles.shape) != (n, 4) or not tiles.is_contiguous()
+            or tiles.data_ptr() % 16):
+        raise ValueError("K-tile flags must be a contiguous, 16-byte aligned (N, 4) int32 tensor")
+
+
+def tile_flag_words(lo: int, hi: int, device) -> torch.Tensor:
+    """(4,) int32 flag words of every 64-entry K tile that overlaps row
+    entries [lo, hi): tile t is bit min(t >> 2, 31) of word t & 3."""
+    words = [0, 0, 0, 0]
+    for t in range(lo // 64, (hi + 63) // 64):
+        words[t & 3] |= 1 << min(t >> 2, 31)
+    return torch.tensor([w - (1 << 32) if w >= 1 << 31 else w for w in words],
+                        dtype=torch.int32, device=device)
+
+
+def tile_flags(rows: torch.Tensor) -> torch.Tensor:
+    """(N, 4) int32 K-tile flags of fp16 observation rows (N, stride) -- bit
+    min(t >> 2, 31) of word t & 3 set when entries [64 t, 64 t + 64) of the
+    row hold a nonzero bit pattern -- for callers that build rows
+    themselves (the step's fused observation writes the same words)."""
+    n, k = rows.shape
+    kt = (k + 63) // 64
+    bits = rows.contiguous().view(torch.int16) != 0
+    if kt * 64 != k:
+        bits = torch.nn.functional.pad(bits, (0, kt * 64 - k))
+    nz = bits.view(n, kt, 64).any(-1).to(torch.int64)
+    t = torch.arange(kt, device=rows.device)
+    shifted = nz << torch.clamp(t >> 2, max=31)
+    words = torch.zeros((n, 4), dtype=torch.int64, device=rows.device)
+    for t0 in range(kt):
+        words[:, t0 & 3] |= shifted[:, t0]
+    words = torch.where(words >= 1 << 31, words - (1 << 32), words)
+    return words.to(torch.int32)
+
+
 def _round_up(x: int, m: int) -> int:
     return (x + m - 1) // m * m
 
@@ -172,6 +210,11 @@ class B200Sim:
         self._first_step = True
         nb = int(capi.lib().qqt_step_scratch_bytes(ctypes.byref(self._ccfg)))
         self._step_scratch = torch.zeros((max(nb, 256),), dtype=torch.uint8, device=d)
+        # K-tile flag words of the observation's crate channel (a recycle
+        # rewrites it), made here so no later call copies from the host
+        ch = 2 * cfg.n_players + 3
+        self._crate_tile_words = (tile_flag_words(ch * hw, (ch + 1) * hw, d)
+                                  if cfg.n_channels > ch else None)
         self._tmpl = None
         self._mapgen = None
         self._cstate = self._make_cstate()
@@ -270,10 +313,12 @@ class B200Sim:
         self._mapgen = _make_mapgen(cfg, seed, self._mg_episode, self._buf["_opp_boost"],
                                     self._buf["_is_open"], self._buf["_map_kind"])
 
-    def _device_map_reset(self, done: torch.Tensor, rows=None, mm=None, bm=None) -> None:
+    def _device_map_reset(self, done: torch.Tensor, rows=None, mm=None, bm=None,
+                          tiles=None) -> None:
         capi.check(capi.lib().qqt_map_reset(
             ctypes.byref(self._ccfg), ctypes.byref(self._cstate), ctypes.byref(self._mapgen),
-            done.data_ptr(), capi.ptr(rows), capi.ptr(mm), capi.ptr(bm), self._stream()),
+            done.data_ptr(), capi.ptr(rows), capi.ptr(mm), capi.ptr(bm), capi.ptr(tiles),
+            self._stream()),
             "qqt_map_reset")
 
     def _apply_template(self, mask: torch.Tensor) -> None:
@@ -567,6 +612,10 @@ class B200Sim:
         (e.g. rollout-buffer rows) written directly instead of the engine's
         own buffers.  info_planes=False skips writing info["blast"] /
         info["trig"] (the flame and exploded-bomb planes).
+        `next_obs` = (rows, mm, bm) or (rows, mm, bm, tiles): the same kernel
+        also writes the next tick's observation rows (N, obs_stride) fp16 and
+        legal masks, and, given `tiles` (N, 4) int32, each row's
+        nonzero-K-tile flags for the MLP policy (`B200Policy.act_seats`).
         """
         acts = actions
         if acts.device != self.device or acts.dtype != torch.int64 or not acts.is_contiguous():
@@ -608,21 +657,24 @@ class B200Sim:
         if next_obs is not None:
             if auto_reset and not dev_reset:
                 raise ValueError("next_obs needs the device auto-reset (a template) or no reset")
-            rows, nmm, nbm = next_obs
+            rows, nmm, nbm = next_obs[:3]
+            tiles = next_obs[3] if len(next_obs) > 3 else None
             if rows.dtype != torch.float16 or rows.stride(1) != 1 or rows.stride(0) != self.obs_stride:
                 raise ValueError("next_obs rows must be fp16 with the engine's row stride")
             for m in (nmm, nbm):
                 if m.dtype != torch.bool or not m.is_contiguous():
                     raise ValueError("next_obs masks must be contiguous bool tensors")
+            if tiles is not None:
+                check_tile_flags(tiles, self.num_envs)
             tmpl = ctypes.byref(self._tmpl) if dev_reset and not map_reset else None
             rc = capi.lib().qqt_step_observe(
                 ctypes.byref(self._ccfg), ctypes.byref(self._cstate), acts.data_ptr(),
                 capi.ptr(rb_hit), capi.ptr(rb_grow), self._tiers.data_ptr(), int(self._first_step),
                 ctypes.byref(cout), tmpl, self._step_scratch.data_ptr(), rows.data_ptr(),
-                nmm.data_ptr(), nbm.data_ptr(), self._stream())
+                nmm.data_ptr(), nbm.data_ptr(), capi.ptr(tiles), self._stream())
             capi.check(rc, "qqt_step_observe")
             if map_reset:
-                self._device_map_reset(done, rows, nmm, nbm)
+                self._device_map_reset(done, rows, nmm, nbm, tiles)
         else:
             tmpl = ctypes.byref(self._tmpl) if dev_reset and not map_reset else None
             rc = capi.lib().qqt_step(ctypes.byref(self._ccfg), ctypes.byref(self._cstate),
@@ -694,7 +746,8 @@ class B200Sim:
         return self._actions
 
     # ------------------------------------------------------------ recycle
-    def flush_recycle(self, on_device: bool | None = None, obs_rows: torch.Tensor | None = None):
+    def flush_recycle(self, on_device: bool | None = None, obs_rows: torch.Tensor | None = None,
+                      obs_tiles: torch.Tensor | None = None):
         """Drop one crate per lost attribute layer on random free cells
         (sim/torch_sim.py:549-596).
 
@@ -705,7 +758,9 @@ class B200Sim:
         state (e.g. written by the step's fused observe); their crate channel
         is rewritten from the crate plane, the one channel a recycle changes
         (crates block neither movement nor flames), so they equal a fresh
-        observe() afterwards."""
+        observe() afterwards.  obs_tiles: those rows' K-tile flags (N, 4)
+        int32 (see `step`'s next_obs); the crate channel's tiles are flagged
+        in every row."""
         if on_device is None:
             on_device = self._tmpl is not None or self._mapgen is not None
         if on_device:
@@ -718,14 +773,17 @@ class B200Sim:
         else:
             self._flush_host()
         if obs_rows is not None:
-            self._rewrite_crate_channel(obs_rows)
+            self._rewrite_crate_channel(obs_rows, obs_tiles)
 
-    def _rewrite_crate_channel(self, rows: torch.Tensor) -> None:
+    def _rewrite_crate_channel(self, rows: torch.Tensor, tiles=None) -> None:
         cfg = self.cfg
         ch, hw = 2 * cfg.n_players + 3, cfg.n_cells
         if cfg.n_channels <= ch:
             return                       # no crate channel in this layout
         rows[:, ch * hw:(ch + 1) * hw].copy_(self._buf["crate"].reshape(self.num_envs, hw))
+        if tiles is not None:
+            check_tile_flags(tiles, self.num_envs)
+            tiles.bitwise_or_(self._crate_tile_words)
 
     def _flush_host(self) -> None:
         cfg = self.cfg

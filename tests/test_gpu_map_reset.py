@@ -27,7 +27,7 @@ if torch.cuda.is_available():
     from oracle import qqt_oracle as O
     from qqt_b200 import _capi
     from qqt_b200.config import SimConfig
-    from qqt_b200.sim import B200Sim
+    from qqt_b200.sim import B200Sim, tile_flags
 
 CONFIGS = {
     "mixed": dict(map_mode="corridor", pure_open_fraction=0.2, open_fraction=0.3,
@@ -118,6 +118,7 @@ def test_device_map_reset_rollout_with_fused_observation():
     rows = torch.zeros((n, sim.obs_stride), dtype=torch.float16, device="cuda")
     nmm = torch.zeros((n, p, 5), dtype=torch.bool, device="cuda")
     nbm = torch.zeros((n, p, 2), dtype=torch.bool, device="cuda")
+    tiles = torch.zeros((n, 4), dtype=torch.int32, device="cuda")
     k_in = cfg.n_channels * cfg.n_cells
     ends = 0
     for t in range(T):
@@ -131,7 +132,7 @@ def test_device_map_reset_rollout_with_fused_observation():
         r, d, _ = sim.step(torch.from_numpy(acts).cuda(), auto_reset=True,
                            crate_draws=(torch.from_numpy(rb[0]).cuda(),
                                         torch.from_numpy(rb[1]).cuda()),
-                           next_obs=(rows, nmm, nbm))
+                           next_obs=(rows, nmm, nbm, tiles))
         torch.cuda.synchronize()
         o_r, o_d, _ = O.step(cfg, st, acts, rb[0], rb[1], hazard_seed=sim.hazard_seed)
         O.map_reset(cfg, st, o_d, O.mapgen_draws_keyed(cfg, seed, episode),
@@ -146,4 +147,9 @@ def test_device_map_reset_rollout_with_fused_observation():
         assert np.array_equal(got, obs.astype(np.float16).reshape(n, -1).view(np.uint16)), \
             f"t={t}: next observation rows"
         assert np.array_equal(_np(nmm), mm) and np.array_equal(_np(nbm), bm), f"t={t}: masks"
+        # K-tile flags: exact for rows the step wrote, every tile for rows
+        # the level generator rewrote
+        exact = tile_flags(rows)
+        assert torch.equal(tiles[~d], exact[~d]), f"t={t}: K-tile flags"
+        assert bool((tiles[d] == -1).all()), f"t={t}: K-tile flags of reset rows"
     assert ends >= n, f"only {ends} episodes ended"

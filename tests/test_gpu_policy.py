@@ -144,6 +144,67 @@ def test_mlp_pair_batches_with_ragged_pairs(n, seats):
         assert np.abs(logp[s].cpu().numpy() - lp).max() <= 1e-3
 
 
+@pytest.mark.parametrize("n,seats", [(5632, (0,)), (300, (0,)), (2100, (0, 1)), (2433, (0, 1)),
+                                     (1000, (0, 1))])
+def test_mlp_zero_tile_skip_is_bit_identical(n, seats):
+    # rows with whole 64-entry K tiles zero in some 128-row tiles (and in
+    # single rows): with the rows' K-tile flags the first layer skips the
+    # tiles that are zero in every row of a row tile (one CTA, the split-K
+    # cluster at 300 rows and 1000 two-seat rows, SM pairs at 2100 / 2433);
+    # outputs must equal the unflagged pass bit for bit.  Over-reported
+    # flags (all set) change nothing either.
+    from qqt_b200.sim import tile_flags
+    cfg = SimConfig(**scenarios.CFG2)
+    p = 2
+    rng = np.random.default_rng(n + len(seats))
+    c, h, w = cfg.obs_shape
+    k = c * h * w
+    kt = (k + 63) // 64
+    obs16 = (rng.random((n, k)) * (rng.random((n, k)) < 0.3)).astype(np.float16)
+    for r0 in range(0, n, 128):
+        for t in np.flatnonzero(rng.random(kt) < 0.45):
+            obs16[r0:r0 + 128, 64 * t:64 * t + 64] = 0
+    for i in rng.choice(n, size=n // 10, replace=False):
+        obs16[i, 64 * rng.integers(kt):][:64] = 0
+    obs = _padded(obs16.reshape((n,) + cfg.obs_shape))
+    flags = tile_flags(torch.as_strided(obs, (n, obs.stride(0)), (obs.stride(0), 1)))
+    mm = rng.random((n, p, 5)) < 0.8
+    mm[..., 4] = True
+    bm = rng.random((n, p, 2)) < 0.7
+    bm[..., 0] = True
+    mm, bm = torch.from_numpy(mm).cuda(), torch.from_numpy(bm).cuda()
+    params = init_params(cfg.obs_shape, "mlp", seed=13)
+    pol = B200Policy(params, cfg.obs_shape, p, seats=seats)
+    u = torch.from_numpy(rng.random((len(seats), n, 2)).astype(np.float32)).cuda()
+    base = pol.forward_logits(obs, mm, bm, u)
+    for fl in (flags, torch.full_like(flags, -1)):
+        got = pol.forward_logits(obs, mm, bm, u, obs_tiles=fl)
+        assert torch.equal(got[0], base[0]), "logits differ with K-tile flags"
+        for a, b in zip(got[1], base[1]):
+            assert torch.equal(a, b)
+        assert torch.equal(got[2], base[2])
+    ml, _, v = O.mlp_forward(params, obs16.reshape((n,) + cfg.obs_shape).astype(np.float32),
+                             seats[0], p)
+    assert _rel(base[0][0, :, :5].cpu().numpy(), ml) <= REL_TOL
+    assert _rel(base[0][0, :, 7].cpu().numpy(), v) <= REL_TOL
+
+
+def test_mlp_all_zero_rows_with_clear_flags():
+    # every flag clear (rows all zero): the first K tile still runs, so the
+    # layer-1 accumulators are written and the output is the bias path's
+    cfg = SimConfig(**scenarios.CFG2)
+    n, p = 300, 2
+    obs = _padded(np.zeros((n,) + cfg.obs_shape, np.float16))
+    mm = torch.ones((n, p, 5), dtype=torch.bool, device="cuda")
+    bm = torch.ones((n, p, 2), dtype=torch.bool, device="cuda")
+    pol = B200Policy(init_params(cfg.obs_shape, "mlp", seed=4), cfg.obs_shape, p, seats=(0,))
+    u = torch.rand((1, n, 2), device="cuda")
+    base = pol.forward_logits(obs, mm, bm, u)
+    got = pol.forward_logits(obs, mm, bm, u,
+                             obs_tiles=torch.zeros((n, 4), dtype=torch.int32, device="cuda"))
+    assert torch.equal(got[0], base[0]) and torch.equal(got[2], base[2])
+
+
 def test_cnn_logits_vs_reference_goldens():
     g = G.load("traj_cfg5")
     cfg = SimConfig(**scenarios.CFG2)

@@ -29,7 +29,7 @@ if torch.cuda.is_available():
     from qqt_b200.policy import B200Policy
     from qqt_b200.policy_init import init_params
     from qqt_b200.rollout import Rollout, RolloutGroups
-    from qqt_b200.sim import B200Sim, _recycle_exclusion
+    from qqt_b200.sim import B200Sim, _recycle_exclusion, tile_flags
 
 
 @pytest.fixture(autouse=True)
@@ -209,7 +209,9 @@ def test_step_observe_equals_step_then_observe():
     rows = torch.zeros_like(ro.buf.obs_rows[0])
     mm = torch.zeros_like(ro.buf.mm[0])
     bm = torch.zeros_like(ro.buf.bm[0])
-    _, done_f, _ = sim.step(acts, auto_reset=True, crate_draws=draws, next_obs=(rows, mm, bm))
+    tiles = torch.zeros((n, 4), dtype=torch.int32, device="cuda")
+    _, done_f, _ = sim.step(acts, auto_reset=True, crate_draws=draws,
+                            next_obs=(rows, mm, bm, tiles))
     fused_state = sim.numpy_state()
     done_f = done_f.clone()
     _restore(sim, bot, snap)
@@ -224,6 +226,7 @@ def test_step_observe_equals_step_then_observe():
         assert np.array_equal(fused_state[k], got[k]), f"state {k}"
     assert torch.equal(rows.view(torch.int16), ref_rows.view(torch.int16)), "observation rows"
     assert torch.equal(mm, ref_mm) and torch.equal(bm, ref_bm), "legal masks"
+    assert torch.equal(tiles, tile_flags(rows)), "K-tile flags of the written rows"
 
 
 @pytest.mark.parametrize("on_device", [True, False])
@@ -242,10 +245,12 @@ def test_flush_rewrites_the_crate_channel_of_fused_rows(on_device):
     rows = torch.zeros_like(ro.buf.obs_rows[0])
     mm = torch.zeros_like(ro.buf.mm[0])
     bm = torch.zeros_like(ro.buf.bm[0])
+    tiles = torch.zeros((n, 4), dtype=torch.int32, device="cuda")
     sim.step(ro.buf.act[19].clone(), auto_reset=True,
-             crate_draws=(ro.draws.crate[19, 0], ro.draws.crate[19, 1]), next_obs=(rows, mm, bm))
+             crate_draws=(ro.draws.crate[19, 0], ro.draws.crate[19, 1]),
+             next_obs=(rows, mm, bm, tiles))
     before = sim.numpy_state()["crate"].copy()
-    sim.flush_recycle(on_device=on_device, obs_rows=rows)
+    sim.flush_recycle(on_device=on_device, obs_rows=rows, obs_tiles=tiles)
     ref_rows = torch.zeros_like(rows)
     ref_mm, ref_bm = torch.zeros_like(mm), torch.zeros_like(bm)
     sim.observe_and_mask(ref_rows, ref_mm, ref_bm, danger=False)
@@ -254,6 +259,24 @@ def test_flush_rewrites_the_crate_channel_of_fused_rows(on_device):
     assert (after.astype(int) - before.astype(int)).sum() > 0, "the recycle dropped crates"
     assert torch.equal(rows.view(torch.int16), ref_rows.view(torch.int16))
     assert torch.equal(mm, ref_mm) and torch.equal(bm, ref_bm)
+    # the K-tile flags still cover every nonzero tile of the rewritten rows
+    assert not bool((tile_flags(rows) & ~tiles).any()), "a nonzero K tile lost its flag"
+
+
+def test_rollout_tile_flags_cover_the_rows():
+    """Every tick's K-tile flags in a rollout buffer cover the tick's rows
+    (the policy skips unflagged tiles); they are exact for rows the step
+    wrote, and over-report only the crate channel after a crate recycle."""
+    n, T = 256, 40
+    cfg, sim, pol, bot, ro = _make(n, T, seed=17)
+    ro.collect()
+    torch.cuda.synchronize()
+    for t in range(T):
+        exact = tile_flags(ro.buf.obs_rows[t])
+        flags = ro.buf.tiles[t]
+        assert not bool((exact & ~flags).any()), f"t={t}: a nonzero K tile lost its flag"
+        if t % ro.flush_every != 0:
+            assert torch.equal(flags, exact), f"t={t}: K-tile flags"
 
 
 def test_double_buffered_graphs_read_their_own_draws():
