@@ -19,12 +19,16 @@ struct PlayerState {
   float rb_hit, rb_grow;   // crate pickup draws of this tick
   int alive0, hp, move, bomb, flat0, placed;
   int32_t since;
-  int64_t bombs_cap, blast_cap, invuln, pending, combo, last_hit, lo_b, lo_z;
+  // the int64 state counters, held as 32-bit integers for the tick (caps,
+  // invulnerability ticks, lost layers and combo counts are small; last_hit
+  // is a tick index or its -1e9 sentinel): exact for every value below
+  // 2^31 in magnitude, and written back sign-extended
+  int32_t bombs_cap, blast_cap, invuln, pending, combo, last_hit, lo_b, lo_z;
 };
 
 struct PShared {
   int flat0, alive0, bomb, placed;
-  int64_t bombs_cap, blast_cap;
+  int32_t bombs_cap, blast_cap;
 };
 
 // Per-warp scratch layout (byte offsets, 16-byte aligned sections).  When
@@ -219,14 +223,14 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
         me.alive0 = st.alive[i];
         me.hp = st.hp[i];
         me.since = st.since_bomb[i];
-        me.bombs_cap = st.bombs_cap[i];
-        me.blast_cap = st.blast_cap[i];
-        me.invuln = st.invuln[i];
-        me.pending = st.pending_lost[i];
-        me.combo = st.combo[i];
-        me.last_hit = st.last_hit[i];
-        me.lo_b = st.lo_bombs[i];
-        me.lo_z = st.lo_blast[i];
+        me.bombs_cap = (int32_t)st.bombs_cap[i];
+        me.blast_cap = (int32_t)st.blast_cap[i];
+        me.invuln = (int32_t)st.invuln[i];
+        me.pending = (int32_t)st.pending_lost[i];
+        me.combo = (int32_t)st.combo[i];
+        me.last_hit = (int32_t)st.last_hit[i];
+        me.lo_b = (int32_t)st.lo_bombs[i];
+        me.lo_z = (int32_t)st.lo_blast[i];
         // the rewards' per-tick draws, loaded with the rest of the player state
         me.rb_hit = cfg.corridor ? a.rb_hit[(size_t)e * P + p] : 0.f;
         me.rb_grow = cfg.corridor ? a.rb_grow[(size_t)e * P + p] : 0.f;
@@ -331,7 +335,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
           if (q >= P) break;
           const int idx = ps[q].flat0;
           const bool ok = ps[q].alive0 && ps[q].bomb && v.fuse[idx] <= 0 && !v.brick[idx] &&
-                          (int64_t)live[q] < ps[q].bombs_cap;
+                          live[q] < ps[q].bombs_cap;
           ps[q].placed = ok;
           if (ok) {
             v.fuse[idx] = (int16_t)cfg.fuse;
@@ -617,9 +621,9 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
                          __fmul_rn(__fmul_rn(coef, bonus), a0f));
       if (cfg.hit_attr_penalty > 0) {
         const bool hit_any = dmg > 0.f && me.alive0;
-        const int64_t pen = cfg.hit_attr_penalty;
-        const int64_t nb = max(me.bombs_cap - pen, me.lo_b);
-        const int64_t nz = max(me.blast_cap - pen, me.lo_z);
+        const int32_t pen = cfg.hit_attr_penalty;
+        const int32_t nb = max(me.bombs_cap - pen, me.lo_b);
+        const int32_t nz = max(me.blast_cap - pen, me.lo_z);
         const float nsp = fmaxf(__fsub_rn(me.spd, cfg.pen_speed), me.lo_spd);
         const float lostf = __fadd_rn((float)((me.bombs_cap - nb) + (me.blast_cap - nz)),
                                       rintf(__fdiv_rn(__fsub_rn(me.spd, nsp), cfg.growth_speed_step)));
@@ -627,7 +631,7 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
           me.bombs_cap = nb;
           me.blast_cap = nz;
           me.spd = nsp;
-          me.pending += (int64_t)lostf;
+          me.pending += (int32_t)lostf;
         }
       }
       reward = __fadd_rn(reward, __fmul_rn(__fmul_rn(coef, chain_bonus), a0f));
@@ -639,11 +643,11 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
         const bool hits = stood && me.rb_hit < prob && me.alive0;
         int attr = (int)floorf(__fmul_rn(me.rb_grow, 3.f));
         if (env_hazard) attr = 2;
-        const int64_t add_b = (hits && attr == 0) ? 1 : 0;
-        const int64_t add_z = (hits && attr == 1) ? 1 : 0;
+        const int32_t add_b = (hits && attr == 0) ? 1 : 0;
+        const int32_t add_z = (hits && attr == 1) ? 1 : 0;
         const float add_s = (hits && attr == 2) ? 1.f : 0.f;
-        me.bombs_cap = min(me.bombs_cap + add_b, (int64_t)cfg.growth_bombs_max);
-        me.blast_cap = min(me.blast_cap + add_z, (int64_t)cfg.growth_blast_max);
+        me.bombs_cap = min(me.bombs_cap + add_b, cfg.growth_bombs_max);
+        me.blast_cap = min(me.blast_cap + add_z, cfg.growth_blast_max);
         me.spd = fminf(__fadd_rn(me.spd, __fmul_rn(add_s, cfg.growth_speed_step)), cfg.growth_speed_max);
       }
     }
@@ -670,18 +674,18 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
     int winner = 0;
     if (p < P) {
       if (cfg.combo_on) {
-        const int64_t c = me.combo;
+        const int32_t c = me.combo;
         int64_t gap = t1 - me.last_hit;
         if (gap < 0) gap = 0;
         const float factor = powf(cfg.combo_gap_factor, (float)gap);
-        const int64_t inc = dealt > 0.f ? 1 : 0;
-        const int64_t now = (c + inc) * inc;
+        const int32_t inc = dealt > 0.f ? 1 : 0;
+        const int32_t now = (c + inc) * inc;
         const float pts = __fmul_rn(__fmul_rn(__fmul_rn((float)now, cfg.combo_reward), factor),
                                     fminf(dealt, 1.f));
         reward = __fadd_rn(reward, __fmul_rn(pts, a0f));
         if (inc) {
           me.combo = now;
-          me.last_hit = t1;
+          me.last_hit = (int32_t)t1;
         }
         if (dmg > 0.f) me.combo = 0;
       }
@@ -756,9 +760,9 @@ __global__ void __launch_bounds__(QQT_NWARP * 32, 3) k_step(StepParams a) {
         me.invuln = 0;
         me.pending = 0;
         me.combo = 0;
-        me.last_hit = -1000000000LL;
-        me.bombs_cap = tp.bombs_cap[i];
-        me.blast_cap = tp.blast_cap[i];
+        me.last_hit = -1000000000;
+        me.bombs_cap = (int32_t)tp.bombs_cap[i];
+        me.blast_cap = (int32_t)tp.blast_cap[i];
         me.spd = tp.spd[i];
         me.lo_b = me.bombs_cap;
         me.lo_z = me.blast_cap;
