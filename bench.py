@@ -897,11 +897,32 @@ def chain_summary(rec):
             early.append(pe - s[0])
             after.append(s[2] - pe)
     f = lambda v: f"{np.mean(v) / 1e3:.2f}" if len(v) else "-"
+    # what gates a step's start: its policy's layer 1 (the programmatic
+    # trigger, stamp 5 of the last CTA) or the bot of the same tick (the
+    # latest astar launch that ended before the step started)
+    L1 = launch_spans(rec, 1, 0, 5, False)
+    A = launch_spans(rec, 3, 0, 4, True)
+    after_l1, after_bot, bot_vs_pol = [], [], []
+    for s in S:
+        cand = L1[(L1[:, 2] <= s[0])]
+        if len(cand):
+            after_l1.append(s[0] - cand[:, 2].max())
+        ab = A[A[:, 2] <= s[0]]
+        if len(ab):
+            after_bot.append(s[0] - ab[:, 2].max())
+    for a in A:
+        cand = P[np.abs(P[:, 0] - a[0]) < 15000]
+        if len(cand):
+            bot_vs_pol.append(a[2] - cand[np.argmin(np.abs(cand[:, 0] - a[0])), 0])
     return [
         f"chain: step end -> next policy start {f(gap_sp)} us; step's first block starts "
         f"{f(early)} us before its policy ends; step ends {f(after)} us after it",
         f"  step launch span {f(S[:, 2] - S[:, 0])} us (block start spread {f(S[:, 1] - S[:, 0])}); "
-        f"policy span {f(P[:, 2] - P[:, 0])} us (CTA start spread {f(P[:, 1] - P[:, 0])})"]
+        f"policy span {f(P[:, 2] - P[:, 0])} us (CTA start spread {f(P[:, 1] - P[:, 0])})",
+        f"  a step's first block starts {f(after_l1)} us after its policy's layer 1 ends and "
+        f"{f(after_bot)} us after the latest bot launch ended; a bot launch ends "
+        f"{f(bot_vs_pol)} us after the policy launch nearest its start began "
+        f"(bot span {f(A[:, 2] - A[:, 0])} us)"]
 
 
 def phase_stamps_leg(args):
