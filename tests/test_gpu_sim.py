@@ -22,7 +22,7 @@ if torch.cuda.is_available():
     from qqt_b200 import scenarios
     from qqt_b200.bots import AstarBot, GreedyBot, HunterBot, RandomBot
     from qqt_b200.config import SimConfig
-    from qqt_b200.sim import B200Sim
+    from qqt_b200.sim import B200Sim, tile_flags
     from qqt_b200 import _capi
 
 
@@ -227,7 +227,7 @@ def test_step_instances_vs_oracle(shape):
     runtime-shape kernel.  Each against the oracle tick by tick over 50
     ticks (random moves and bombs; the 30-tick fuses go off), with and without
     the fused next-tick observation, which must equal a stand-alone
-    observe of the same state.  The astar bot is compiled the same way:
+    observe of the same state (its K-tile flags those of the rows).  The astar bot is compiled the same way:
     every 5th tick each player's astar action (no mode ticker) against the
     oracle's on the same state and noise."""
     from oracle import qqt_oracle as O
@@ -240,6 +240,7 @@ def test_step_instances_vs_oracle(shape):
     rows = torch.zeros((n, fused.obs_stride), dtype=torch.float16, device="cuda")
     mm = torch.zeros((n, p, 5), dtype=torch.bool, device="cuda")
     bm = torch.zeros((n, p, 2), dtype=torch.bool, device="cuda")
+    tiles = torch.zeros((n, 4), dtype=torch.int32, device="cuda")
     ref_rows = torch.zeros_like(rows)
     ref_mm, ref_bm = torch.zeros_like(mm), torch.zeros_like(bm)
     rng = np.random.default_rng(7)
@@ -261,7 +262,7 @@ def test_step_instances_vs_oracle(shape):
         acts[..., 0] = rng.integers(0, 5, (n, p))
         acts[..., 1] = rng.random((n, p)) < 0.3
         a = torch.from_numpy(acts).cuda()
-        r, d, _ = fused.step(a, auto_reset=False, next_obs=(rows, mm, bm))
+        r, d, _ = fused.step(a, auto_reset=False, next_obs=(rows, mm, bm, tiles))
         r2, d2, _ = plain.step(a, auto_reset=False)
         plain.observe_and_mask(ref_rows, ref_mm, ref_bm, danger=False)
         owned = st["owner"] >= 0
@@ -275,6 +276,7 @@ def test_step_instances_vs_oracle(shape):
         assert np.abs(_np(r) - o_r).max() <= 1e-6 and np.abs(_np(r2) - o_r).max() <= 1e-6
         assert torch.equal(rows.view(torch.int16), ref_rows.view(torch.int16)), f"t={t}: rows"
         assert torch.equal(mm, ref_mm) and torch.equal(bm, ref_bm), f"t={t}: masks"
+        assert torch.equal(tiles, tile_flags(rows)), f"t={t}: K-tile flags"
     assert exploded > 0
 
 
