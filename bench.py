@@ -1,5 +1,6 @@
 #!/usr/bin/env python3
-"""Rollout throughput benchmark (BASELINE.json metric).
+"""Rollout throughput benchmark: the reference's headline metric, rollout
+env-steps per second at 1/2/4/8 B200 against the reference's CPU path.
 
 One "step" = one 128-tick rollout of one GPU's env shard: observe -> masks ->
 learner act -> opponent act -> step (device auto-reset) -> crate recycling
